@@ -1,0 +1,143 @@
+// linear.cuh — decode-shape linear layers (R <= 8 activation rows).
+//
+// Semantics restated from the apus C engine:
+//   FP8 linear (c/gdsa.h:525-534 = c/fp8blk.h dequant + c/bf16.h GEMM):
+//     w[o,k]   = bf16_rne(e4m3(W[o,k]) * ws[o/128][k/128])   (one fp32 mul)
+//     y[m,o]   = bf16_rne( sum_k f32(x[m,k]) * f32(w[o,k]) )  (fp32 acc)
+//   BF16 linear (c/bf16.h:15-60): the same with w = W.
+// The dequantized weight keeps the reference's exact BF16 value; only the
+// fp32 summation ORDER differs (the reference is strictly sequential in k,
+// this kernel reduces 16-wide k groups on the tensor core and combines
+// k-split partials in a fixed order).  The order depends on (O, K) only, so
+// every activation row gets bitwise the same result at any row count R —
+// the batch invariance the speculative verify relies on.
+//
+// Work decomposition.  A warp owns 8 weight rows and a contiguous range of
+// 64-byte k-steps.  Lane (g = lane/4, t = lane%4) streams 16 bytes of weight
+// row g per step (FP8: 16 codes, BF16: 8 values) with one 128-bit
+// non-allocating load, converts them into the B fragment of
+// mma.m16n8k16.bf16 (the weight rows are the n = 8 columns), and loads the
+// matching activation k-values of row g as the A fragment (rows 8..15 of A
+// are padding).  The k-permutation inside a step is the same for A and B,
+// so the dot products are unchanged.  D[m][n] lands in lane (m, n/2).
+#pragma once
+#include "common.cuh"
+
+namespace apus {
+
+APUS_DEV uint4 ld_stream16(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+APUS_DEV uint4 ld_nc16(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+// Two E4M3 codes (low byte = lower k) -> f16x2, exact.
+APUS_DEV uint32_t cvt_e4m3x2_f16x2(uint32_t two_codes) {
+    uint32_t r;
+    uint16_t in = (uint16_t)two_codes;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(in));
+    return r;
+}
+
+// (lo, hi) fp32 -> bf16x2 with RNE; lo goes to the low half.
+APUS_DEV uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// Four E4M3 codes of one 32-bit word times the block scale, each rounded to
+// BF16 exactly like c/fp8blk.h:115-136, packed as two bf16x2 words.
+APUS_DEV void dequant4(uint32_t w, float s, uint32_t &b0, uint32_t &b1) {
+    uint32_t h01 = cvt_e4m3x2_f16x2(w & 0xffffu);
+    uint32_t h23 = cvt_e4m3x2_f16x2(w >> 16);
+    __half2 v01 = *reinterpret_cast<__half2 *>(&h01);
+    __half2 v23 = *reinterpret_cast<__half2 *>(&h23);
+    float2 f01 = __half22float2(v01);
+    float2 f23 = __half22float2(v23);
+    b0 = pack_bf16x2(__fmul_rn(f01.x, s), __fmul_rn(f01.y, s));
+    b1 = pack_bf16x2(__fmul_rn(f23.x, s), __fmul_rn(f23.y, s));
+}
+
+APUS_DEV void mma_bf16_16816(float &d0, float &d1, float &d2, float &d3,
+                             uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One warp: 8 weight rows x k-steps [s0, s1).  Each step is 64 bytes of a
+// weight row (FP8: 64 codes; BF16: 32 values).  wrow_ptr points at this
+// lane's weight row (row g of the group, already clamped to a valid row),
+// offset by 16*t bytes.  xrow points at activation row g offset to this
+// lane's first k (FP8: 16*t elements, BF16: 8*t), or nullptr when g >= R.
+// srow: FP8 scale row of weight row g (ws + (row/128)*nkb), unused for BF16.
+// Returns the partial dot products for (x row g, weight rows 2t, 2t+1).
+template <bool FP8>
+APUS_DEV void warp_rows8(const uint8_t *wrow_ptr, const uint16_t *xrow,
+                         const float *srow, int s0, int s1,
+                         float &out0, float &out1) {
+    constexpr int U = 4;
+    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+    uint4 wb[U];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+        if (s0 + u < s1) wb[u] = ld_stream16(wrow_ptr + (size_t)(s0 + u) * 64);
+    for (int s = s0; s < s1; s += U) {
+        uint4 cur[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) cur[u] = wb[u];
+#pragma unroll
+        for (int u = 0; u < U; u++)
+            if (s + U + u < s1) wb[u] = ld_stream16(wrow_ptr + (size_t)(s + U + u) * 64);
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int st = s + u;
+            if (st < s1) {
+                const uint32_t wv[4] = {cur[u].x, cur[u].y, cur[u].z, cur[u].w};
+                if (FP8) {
+                    uint32_t xw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    if (xrow) {
+                        uint4 xa = ld_nc16(xrow + (size_t)st * 64);
+                        uint4 xb = ld_nc16(xrow + (size_t)st * 64 + 8);
+                        xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
+                        xw[4] = xb.x; xw[5] = xb.y; xw[6] = xb.z; xw[7] = xb.w;
+                    }
+                    const float sc = __ldg(srow + (st >> 1));
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        uint32_t b0, b1;
+                        dequant4(wv[j], sc, b0, b1);
+                        mma_bf16_16816(d0, d1, d2, d3, xw[2 * j], 0u, xw[2 * j + 1], 0u, b0, b1);
+                    }
+                } else {
+                    uint32_t xw[4] = {0, 0, 0, 0};
+                    if (xrow) {
+                        uint4 xa = ld_nc16(xrow + (size_t)st * 32);
+                        xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 2; j++)
+                        mma_bf16_16816(d0, d1, d2, d3, xw[2 * j], 0u, xw[2 * j + 1], 0u,
+                                       wv[2 * j], wv[2 * j + 1]);
+                }
+            }
+        }
+    }
+    (void)d2; (void)d3;
+    out0 = d0;
+    out1 = d1;
+}
+
+}  // namespace apus

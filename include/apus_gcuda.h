@@ -1,0 +1,104 @@
+/*
+ * apus_gcuda.h — C ABI of the B200 (sm_100a) backend for the apus
+ * GLM-5.3-Flash engine: the linear-layer leaf (FP8 128x128 block dequant,
+ * FP8/BF16 decode GEMV) behind the reference's own entry points.
+ *
+ * Drop-in rules:
+ *   - Host-pointer entry points keep the reference signatures exactly, so a C
+ *     engine that stops compiling the CPU implementation of c/fp8blk.h /
+ *     c/bf16.h and links libapus_gcuda.so instead runs unchanged.
+ *   - The hook-table entries have the signatures of ApusGmetalHooks
+ *     (c/backend_gmetal.h:120-126): 0 = handled, nonzero = not handled.
+ *   - `_dev` twins take device pointers plus a cudaStream_t passed as void*.
+ *   - No CPU fallback: when the CUDA path cannot run, entry points return
+ *     nonzero (or, for the void reference signatures, record the error in
+ *     apus_gcuda_last_error() and leave the output untouched).
+ * Numerics: dequant is bitwise c/fp8blk.h; GEMV rows are the reference
+ * dequant->BF16->fp32-accumulate->BF16 composition with a different (fixed,
+ * row-count independent) fp32 summation order.
+ */
+#ifndef APUS_GCUDA_H
+#define APUS_GCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- backend control (mirrors c/backend_gmetal.h:131-156) --------------- */
+
+/* Initialise the CUDA device (must be sm_100). 0 on success, -1 + err. */
+int  apus_gcuda_enable(char *err, size_t errcap);        /* c/backend_gmetal.h:134 */
+void apus_gcuda_disable(void);                           /* c/backend_gmetal.h:136 */
+int  apus_gcuda_is_enabled(void);                        /* c/backend_gmetal.h:137 */
+/* Last error message of the calling thread ("" when none). */
+const char *apus_gcuda_last_error(void);
+
+/* Persistent HBM residency for a model-owned host weight region: the bytes
+ * are uploaded once; hooked ops whose weight pointer lies inside a
+ * registered region read the resident copy (c/backend_gmetal.h:147-148). */
+int  apus_gcuda_register_region(const void *ptr, size_t len);
+void apus_gcuda_unregister_region(const void *ptr);
+uint64_t apus_gcuda_bytes_pinned(void);                  /* c/backend_gmetal.h:154 */
+uint64_t apus_gcuda_dispatches(void);                    /* c/backend_gmetal.h:155 */
+uint64_t apus_gcuda_offload_bf16(void);                  /* c/backend_gmetal.h:156 */
+uint64_t apus_gcuda_offload_fp8blk(void);                /* c/backend_gmetal.h:157 */
+
+/* Hook table with the layout of ApusGmetalHooks (c/backend_gmetal.h:120-126). */
+typedef struct {
+    int (*bf16_gemm)(const uint16_t *w, const uint16_t *x, uint16_t *y,
+                     size_t M, size_t O, size_t K);
+    int (*fp8blk_linear)(const uint8_t *codes, const float *scales,
+                         const uint16_t *x, uint16_t *y,
+                         size_t M, size_t O, size_t K);
+} ApusGcudaHooks;
+void apus_gcuda_fill_hooks(ApusGcudaHooks *out);
+
+/* Direct hook entries (c/backend_gmetal.h:163-167): host pointers, any M. */
+int apus_gcuda_bf16_gemm(const uint16_t *w, const uint16_t *x, uint16_t *y,
+                         size_t M, size_t O, size_t K);
+int apus_gcuda_fp8blk_linear(const uint8_t *codes, const float *scales,
+                             const uint16_t *x, uint16_t *y,
+                             size_t M, size_t O, size_t K);
+
+/* ---- c/fp8blk.h drop-ins ------------------------------------------------- */
+size_t apus_fp8blk_nblocks(size_t n);                    /* c/fp8blk.h:63 */
+void apus_fp8blk_dequant(const uint8_t *w, const float *ws,
+                         uint16_t *out, size_t O, size_t K);   /* c/fp8blk.h:81-82 */
+void apus_fp8blk_dequant_mt(const uint8_t *w, const float *ws,
+                            uint16_t *out, size_t O, size_t K); /* c/fp8blk.h:88-89 */
+
+/* ---- c/bf16.h drop-ins (xf scratch is accepted and unused) --------------- */
+void apus_bf16_gemv_mt(const uint16_t *w, const uint16_t *x, float *xf,
+                       uint16_t *y, size_t O, size_t K);       /* c/bf16.h:146-147 */
+void apus_bf16_gemm_mt(const uint16_t *w, const uint16_t *x, float *xf,
+                       uint16_t *y, size_t M, size_t O, size_t K); /* c/bf16.h:150-151 */
+
+/* ---- device-pointer twins ------------------------------------------------ */
+int apus_fp8blk_dequant_dev(const uint8_t *w, const float *ws, uint16_t *out,
+                            size_t O, size_t K, void *stream);
+/* y [M,O] BF16 codes; M <= 8 per launch (larger M is split into 8-row
+ * launches, each row bitwise independent of the others). */
+int apus_gcuda_fp8blk_linear_dev(const uint8_t *codes, const float *scales,
+                                 const uint16_t *x, uint16_t *y,
+                                 size_t M, size_t O, size_t K, void *stream);
+int apus_gcuda_bf16_gemm_dev(const uint16_t *w, const uint16_t *x, uint16_t *y,
+                             size_t M, size_t O, size_t K, void *stream);
+/* fp32 output, no rounding (router logits c/gmoe.h:168-173, mHC mixes
+ * c/gmhc.h:250-258). */
+int apus_gcuda_bf16_gemm_f32_dev(const uint16_t *w, const uint16_t *x, float *y,
+                                 size_t M, size_t O, size_t K, void *stream);
+/* BF16 GEMV fused with the greedy pick of c/sample.h:76-81 on the
+ * BF16-rounded outputs (lowest index wins ties): ids [M]; y (optional) gets
+ * the BF16 logits. */
+int apus_gcuda_bf16_gemm_argmax_dev(const uint16_t *w, const uint16_t *x, uint16_t *y,
+                                    int32_t *ids, size_t M, size_t O, size_t K,
+                                    void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* APUS_GCUDA_H */

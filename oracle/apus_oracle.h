@@ -1,0 +1,43 @@
+/*
+ * apus_oracle.h — CPU restatement of the apus GLM-5.3-Flash speculative
+ * decode path, used ONLY as the checker for the CUDA path (tests, smoke,
+ * the bench's CPU-baseline leg).  It is not part of the product: nothing in
+ * libapus_gcuda.so calls it.
+ *
+ * Each function restates one reference function (cited file:line, paths
+ * inside the apus repository).  The arithmetic keeps the reference's
+ * rounding points and summation orders, so with an identical libm expf the
+ * outputs are bitwise those of the reference; oracle/ref_glue.c lets the
+ * tests prove that against the reference sources themselves.
+ */
+#ifndef APUS_ORACLE_H
+#define APUS_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- numerics (c/num.h:110-166) ---- */
+float    orc_bf16_f32(uint16_t b);
+uint16_t orc_bf16_bits(float x);
+float    orc_bf16_round(float x);
+float    orc_e4m3_f32(uint8_t c);
+uint8_t  orc_e4m3_quant(float x);
+float    orc_sigmoid(float x);                 /* c/gmhc.h:157-160 */
+float    orc_pw_sum(const float *a, size_t n); /* c/gmhc.h:165-185 */
+
+/* ---- linear leaf ---- */
+void orc_fp8_dequant(const uint8_t *w, const float *ws, uint16_t *out, size_t O, size_t K);
+void orc_bf16_gemm(const uint16_t *w, const uint16_t *x, uint16_t *y, size_t M, size_t O, size_t K);
+void orc_bf16_gemm_f32(const uint16_t *w, const uint16_t *x, float *y, size_t M, size_t O, size_t K);
+void orc_fp8_linear(const uint8_t *codes, const float *scales, const uint16_t *x, uint16_t *y,
+                    size_t M, size_t O, size_t K);
+int  orc_argmax_bf16(const uint16_t *logits, size_t n);   /* c/sample.h:76-81 on widened codes */
+
+#ifdef __cplusplus
+}
+#endif
+#endif
