@@ -32,6 +32,7 @@ apus_gcuda_enable = _fn("apus_gcuda_enable", _i, C.c_char_p, _sz)
 apus_gcuda_disable = _fn("apus_gcuda_disable", None)
 apus_gcuda_is_enabled = _fn("apus_gcuda_is_enabled", _i)
 apus_gcuda_last_error = _fn("apus_gcuda_last_error", C.c_char_p)
+apus_gcuda_kernel_error = _fn("apus_gcuda_kernel_error", _i)
 apus_gcuda_register_region = _fn("apus_gcuda_register_region", _i, _vp, _sz)
 apus_gcuda_unregister_region = _fn("apus_gcuda_unregister_region", None, _vp)
 apus_gcuda_bytes_pinned = _fn("apus_gcuda_bytes_pinned", _u64)
@@ -45,6 +46,7 @@ apus_fp8blk_dequant = _fn("apus_fp8blk_dequant", None, _vp, _vp, _vp, _sz, _sz)
 apus_fp8blk_dequant_mt = _fn("apus_fp8blk_dequant_mt", None, _vp, _vp, _vp, _sz, _sz)
 apus_bf16_gemv_mt = _fn("apus_bf16_gemv_mt", None, _vp, _vp, _vp, _vp, _sz, _sz)
 apus_bf16_gemm_mt = _fn("apus_bf16_gemm_mt", None, _vp, _vp, _vp, _vp, _sz, _sz, _sz)
+apus_gcuda_set_pdl = _fn("apus_gcuda_set_pdl", None, _i)
 apus_fp8blk_dequant_dev = _fn("apus_fp8blk_dequant_dev", _i, _vp, _vp, _vp, _sz, _sz, _vp)
 apus_gcuda_fp8blk_linear_dev = _fn("apus_gcuda_fp8blk_linear_dev", _i, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp)
 apus_gcuda_bf16_gemm_dev = _fn("apus_gcuda_bf16_gemm_dev", _i, _vp, _vp, _vp, _sz, _sz, _sz, _vp)

@@ -52,7 +52,23 @@ struct Scratch {
         return p;
     }
 };
-Scratch g_sw, g_ss, g_sx, g_sy, g_keys;
+Scratch g_sw, g_ss, g_sx, g_sy, g_keys, g_part, g_tick;
+
+// Split-K scratch of the library's own GEMV launches (grow-only; the ticket
+// array is zeroed on growth and every launch leaves it zeroed).
+int splitk_scratch(long O, long K, float **part, int **tick) {
+    size_t pf, nt;
+    gemv_scratch_need(O, K, &pf, &nt);
+    *part = nullptr;
+    *tick = nullptr;
+    if (!pf) return 0;
+    size_t old = g_tick.cap;
+    *part = (float *)g_part.get(pf * sizeof(float));
+    *tick = (int *)g_tick.get(nt * sizeof(int));
+    if (!*part || !*tick) { gcuda_set_error("split-K scratch allocation failed"); return -1; }
+    if (g_tick.cap != old && cudaMemset(*tick, 0, g_tick.cap) != cudaSuccess) return -1;
+    return 0;
+}
 cudaStream_t g_stream = nullptr;
 
 int ensure_enabled() {
@@ -102,12 +118,16 @@ int linear_host(const void *w, size_t wbytes, const float *ws, size_t sbytes, in
     if (!dx || !dy) { gcuda_set_error("scratch allocation failed"); return -1; }
     if (gcuda_check(cudaMemcpyAsync(dx, x, M * K * 2, cudaMemcpyHostToDevice, g_stream), "x upload"))
         return -1;
+    float *part;
+    int *tick;
+    if (splitk_scratch((long)O, (long)K, &part, &tick)) return -1;
     for (size_t m0 = 0; m0 < M; m0 += 8) {
         GemvDesc d{};
         d.W = dw; d.WS = dws; d.nkb = (long)((K + 127) / 128);
         d.x = dx + m0 * K; d.ldx = (long)K;
         d.R = (int)((M - m0) < 8 ? (M - m0) : 8);
         d.O = (long)O; d.K = (long)K; d.fp8 = fp8;
+        d.part = part; d.ticket = tick;
         d.y = dy + m0 * O; d.ldy = (long)O;
         if (gemv_launch(d, g_stream)) { gcuda_check(cudaGetLastError(), "gemv launch"); return -1; }
         g_dispatch++;
@@ -153,7 +173,7 @@ void apus_gcuda_disable(void) {
     for (auto &kv : g_regions) cudaFree(kv.second.dev);
     g_regions.clear();
     g_pinned = 0;
-    for (Scratch *s : {&g_sw, &g_ss, &g_sx, &g_sy, &g_keys}) {
+    for (Scratch *s : {&g_sw, &g_ss, &g_sx, &g_sy, &g_keys, &g_part, &g_tick}) {
         if (s->p) cudaFree(s->p);
         s->p = nullptr;
         s->cap = 0;
@@ -166,6 +186,11 @@ void apus_gcuda_disable(void) {
 int apus_gcuda_is_enabled(void) { return g_enabled ? 1 : 0; }
 
 const char *apus_gcuda_last_error(void) { return g_err; }
+
+int apus_gcuda_kernel_error(void) {
+    cudaDeviceSynchronize();
+    return kernel_error_read_and_clear();
+}
 
 int apus_gcuda_register_region(const void *ptr, size_t len) {
     if (ensure_enabled()) return -1;
@@ -262,9 +287,19 @@ int apus_fp8blk_dequant_dev(const uint8_t *w, const float *ws, uint16_t *out,
                ? gcuda_check(cudaGetLastError(), "dequant launch") : 0;
 }
 
+static int g_pdl = 0;
+
+void apus_gcuda_set_pdl(int on) { g_pdl = on ? 1 : 0; }
+
 static int linear_dev(const void *w, const float *ws, int fp8, const uint16_t *x, uint16_t *y,
                       float *yf, unsigned long long *keys, size_t M, size_t O, size_t K,
                       cudaStream_t st) {
+    float *part;
+    int *tick;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (splitk_scratch((long)O, (long)K, &part, &tick)) return -1;
+    }
     for (size_t m0 = 0; m0 < M; m0 += 8) {
         GemvDesc d{};
         d.W = w; d.WS = ws; d.nkb = (long)((K + 127) / 128);
@@ -274,6 +309,8 @@ static int linear_dev(const void *w, const float *ws, int fp8, const uint16_t *x
         if (y) { d.y = y + m0 * O; d.ldy = (long)O; }
         if (yf) { d.yf = yf + m0 * O; d.ldyf = (long)O; }
         if (keys) d.amax = keys + m0;
+        d.part = part; d.ticket = tick;
+        d.pdl = g_pdl;
         if (gemv_launch(d, st)) return gcuda_check(cudaGetLastError(), "gemv launch") ? -1 : -1;
     }
     return 0;

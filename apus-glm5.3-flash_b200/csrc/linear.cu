@@ -1,5 +1,6 @@
 // linear.cu — FP8 128x128-block dequant and the decode GEMV kernels.
 #include "linear.cuh"
+#include "pipe.cuh"
 #include "gcuda.h"
 
 namespace apus {
@@ -46,54 +47,268 @@ __global__ void k_fp8_dequant(const uint8_t *__restrict__ w, const float *__rest
 }
 
 // ---------------------------------------------------------------------------
-// Fast GEMV: CTA = 8 warps = RG row groups x KS k-splits; 8*RG weight rows.
-template <bool FP8, int RG>
-__global__ void __launch_bounds__(256) k_gemv(GemvDesc d) {
-    constexpr int KS = 8 / RG;
-    __shared__ float part[KS][RG][8][8];
-    __shared__ unsigned long long keys[RG * 64];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rg = warp % RG, ks = warp / RG;
-    const int g = lane >> 2, t = lane & 3;
-    const long row_base = (long)blockIdx.x * (8 * RG) + rg * 8;
-    const long wrow = min(row_base + g, (long)d.O - 1);
-    const int NS = d.K / (FP8 ? 64 : 32);
-    const int s0 = (int)((long)NS * ks / KS), s1 = (int)((long)NS * (ks + 1) / KS);
-    const size_t row_bytes = FP8 ? (size_t)d.K : (size_t)d.K * 2;
-    const uint8_t *wp = (const uint8_t *)d.W + (size_t)wrow * row_bytes + 16 * t;
-    const uint16_t *xp = (g < d.R) ? d.x + (size_t)g * d.ldx + (FP8 ? 16 : 8) * t : nullptr;
-    const float *srow = FP8 ? d.WS + (size_t)(wrow >> 7) * d.nkb : nullptr;
-    float c0, c1;
-    warp_rows8<FP8>(wp, xp, srow, s0, s1, c0, c1);
-    part[ks][rg][g][2 * t] = c0;
-    part[ks][rg][g][2 * t + 1] = c1;
-    __syncthreads();
-    const int tid = threadIdx.x;
-    if (tid < RG * 64) {
-        const int rr = tid / 64, m = (tid / 8) % 8, o = tid % 8;
-        float acc = part[0][rr][m][o];
-#pragma unroll
-        for (int q = 1; q < KS; q++) acc = acc + part[q][rr][m][o];
-        const long row = (long)blockIdx.x * (8 * RG) + rr * 8 + o;
-        const bool ok = (m < d.R) && (row < d.O);
-        if (ok) {
-            if (d.y) d.y[(size_t)m * d.ldy + row] = bf16_bits(acc);
-            if (d.yf) d.yf[(size_t)m * d.ldyf + row] = acc;
-        }
-        if (d.amax) keys[tid] = ok ? argmax_key(bf16_round(acc), (uint32_t)row) : 0ull;
+// Staged GEMV (persistent).  Work item = (tile of 16 weight rows, k-range).
+// K is cut into ranges of KX elements (a rule of K alone, so the summation
+// order never depends on the activation row count R); a CTA keeps one
+// k-range for its whole life and stages that slice of the activations in
+// shared memory once (up to 4 rows; more rows are read through L1).
+// Warp 8 is the producer: lane 0 streams each tile's k-range through a ring
+// of NSTAGE stages with 1-D bulk copies (one per row per 2 KiB chunk,
+// completion counted on the stage's "full" mbarrier).  Warps 0-7 consume:
+// each takes a fixed slice of the 64-byte k-steps of every chunk.  The
+// weight rows are the 16-row A operand of mma.m16n8k16 (lane (g,t) holds rows
+// g and g+8), the activation rows the 8 B columns, so one MMA covers 256
+// weights.  FP8 codes are dequantized in registers to the reference's exact
+// BF16 weight (one fp32 multiply by the block scale, RNE).  Four accumulator
+// sets shorten the MMA dependency chain; at the end of the tile the 8 warp
+// partials are summed in warp order.  With several k-ranges the partial goes
+// to scratch and the last CTA of the tile (atomic ticket) sums the ranges in
+// range order and runs the epilogue.  Row strides are padded so the 8 lanes
+// of every quarter-warp hit distinct 16-byte shared-memory bank groups.
+namespace gemvcfg {
+constexpr int NSTAGE = 2;
+constexpr int TR = 16;                // weight rows per tile
+constexpr int CH = 2048;              // bytes of one weight row per chunk
+constexpr int RS = CH + 64;           // smem row stride of the ring
+constexpr int STAGE_BYTES = TR * RS;
+constexpr long KX = 4096;             // elements of K per work item
+constexpr int XMAX = 4 * (2 * (int)KX + 16);   // staged activations: up to 4 rows
+constexpr int THREADS = 288;          // 8 consumer warps + 1 producer warp
+constexpr int PART = 8 * TR;          // floats of one warp partial: [x col][w row]
+}  // namespace gemvcfg
+
+__device__ int g_apus_kernel_err;
+
+APUS_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+APUS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Epilogue of one finished (x row m, weight row `row`) dot product; the 16
+// threads of an x row are consecutive lanes (one half-warp).
+APUS_DEV void gemv_store(const GemvDesc &d, int m, long row, float a, unsigned long long *best_sh,
+                         bool lead) {
+    const bool ok = (m < d.R) && (row < d.O);
+    if (ok) {
+        if (d.y) d.y[(size_t)m * d.ldy + row] = bf16_bits(a);
+        if (d.yf) d.yf[(size_t)m * d.ldyf + row] = a;
     }
     if (d.amax) {
-        __syncthreads();
-        if (tid < d.R) {
-            unsigned long long best = 0ull;
-            for (int rr = 0; rr < RG; rr++)
-                for (int o = 0; o < 8; o++) {
-                    unsigned long long k = keys[rr * 64 + tid * 8 + o];
-                    best = k > best ? k : best;
-                }
-            atomicMax(d.amax + tid, best);
+        unsigned long long k = ok ? argmax_key(bf16_round(a), (uint32_t)row) : 0ull;
+#pragma unroll
+        for (int off2 = 8; off2; off2 >>= 1) {
+            unsigned long long o2 = __shfl_xor_sync(0xffffffffu, k, off2, 16);
+            k = o2 > k ? o2 : k;
         }
+        if (lead && k > best_sh[m]) best_sh[m] = k;
     }
+}
+
+template <bool FP8, bool XS>
+__global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
+    using namespace gemvcfg;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *ring = smem;
+    uint16_t *xs = (uint16_t *)(smem + NSTAGE * STAGE_BYTES);
+    float *part = (float *)(smem + NSTAGE * STAGE_BYTES + (XS ? XMAX : 0));
+    uint64_t *full = (uint64_t *)(part + 8 * PART);
+    uint64_t *empty = full + NSTAGE;
+    __shared__ unsigned long long best_sh[8];
+    __shared__ int abort_sh, ticket_sh;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long rowbytes = FP8 ? d.K : 2 * d.K;
+    const long ntile = (d.O + TR - 1) / TR;
+    const int nks = (int)((d.K + KX - 1) / KX);
+    const int ks = (int)(blockIdx.x % nks);
+    const long t_first = blockIdx.x / nks, t_step = gridDim.x / nks;
+    const long k0 = ks * KX, klen = min(KX, d.K - k0);          // elements
+    const long kb0 = FP8 ? k0 : 2 * k0, kbytes = FP8 ? klen : 2 * klen;
+    const int nch = (int)((kbytes + CH - 1) / CH);
+    const long xstride = klen + 8;                               // elements
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 8); }
+        fence_barrier_init();
+        abort_sh = 0;
+    }
+    if (threadIdx.x < 8) best_sh[threadIdx.x] = 0ull;
+    __syncthreads();
+    // The next kernel in the stream may start its own weight stream now.
+    pdl_launch_dependents();
+
+    if (warp == 8) {            // ---------------- producer
+        // Lane 0 owns the barriers; lanes 0..TR-1 each issue one row's copy, so
+        // the per-instruction issue cost of the bulk copies is paid in parallel.
+        // Weights never depend on the previous kernel, so the stream starts
+        // before the dependency wait unless the caller says otherwise.
+        if (d.weights_after_wait) pdl_wait();
+        long c = 0;
+        bool ok = true;
+        for (long t = t_first; t < ntile && ok; t += t_step) {
+            const long row0 = t * TR;
+            for (int ch = 0; ch < nch; ch++, c++) {
+                const int s = (int)(c % NSTAGE);
+                const long rnd = c / NSTAGE;
+                const long off = (long)ch * CH;
+                const uint32_t len = (uint32_t)min((long)CH, kbytes - off);
+                if (lane == 0) {
+                    if (rnd > 0 && !mbar_wait(&empty[s], (uint32_t)((rnd - 1) & 1), &abort_sh,
+                                              &g_apus_kernel_err, 1))
+                        ok = false;
+                    else
+                        mbar_arrive_expect_tx(&full[s], TR * len);
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                if (lane < TR) {
+                    const long row = min(row0 + lane, d.O - 1);
+                    bulk_g2s(ring + s * STAGE_BYTES + lane * RS,
+                             (const uint8_t *)d.W + row * rowbytes + kb0 + off, len, &full[s]);
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers: activations come from the previous kernel
+    pdl_wait();
+    if (XS) {   // stage x[:, k0:k0+klen]: row r at xs + r*xstride
+        const int per_row = (int)(klen / 8), total = d.R * per_row;   // <= 8 per thread
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = threadIdx.x + u * 256;
+            if (i < total) v[u] = ld_nc16(d.x + (size_t)(i / per_row) * d.ldx + k0 + (i % per_row) * 8);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = threadIdx.x + u * 256;
+            if (i < total) *(uint4 *)(xs + (i / per_row) * xstride + (i % per_row) * 8) = v[u];
+        }
+        named_bar_sync(1, 256);
+    }
+    const int g = lane >> 2, t4 = lane & 3;
+    const bool xrow_ok = g < d.R;            // lane supplies B column g
+    long c = 0;
+    for (long t = t_first; t < ntile; t += t_step) {
+        const long row0 = t * TR;
+        const float *srA = nullptr, *srB = nullptr;
+        if (FP8) {   // scale rows of weight rows g and g+8
+            srA = d.WS + (size_t)(min(row0 + g, d.O - 1) >> 7) * d.nkb;
+            srB = d.WS + (size_t)(min(row0 + g + 8, d.O - 1) >> 7) * d.nkb;
+        }
+        float acc[4][4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+        for (int ch = 0; ch < nch; ch++, c++) {
+            const int s = (int)(c % NSTAGE);
+            const long off = (long)ch * CH;
+            const int nst = (int)(min((long)CH, kbytes - off) / 64);
+            const int s0 = nst * warp / 8, s1 = nst * (warp + 1) / 8;
+            constexpr int MAXS = CH / 64 / 8 + 1;
+            float scA[MAXS], scB[MAXS];
+            if (FP8) {   // scales first: their latency hides under the barrier wait
+#pragma unroll
+                for (int i = 0; i < MAXS; i++) {
+                    const long kbk = (kb0 + off) / 128 + ((s0 + i) >> 1);
+                    scA[i] = (s0 + i < s1) ? __ldg(srA + kbk) : 0.f;
+                    scB[i] = (s0 + i < s1) ? __ldg(srB + kbk) : 0.f;
+                }
+            }
+            const bool have = mbar_wait(&full[s], (uint32_t)((c / NSTAGE) & 1), &abort_sh,
+                                        &g_apus_kernel_err, 2);
+            const int e1 = have ? s1 : s0;
+            const uint8_t *wA = ring + s * STAGE_BYTES + g * RS + 16 * t4;
+            const uint8_t *wB = wA + 8 * RS;
+#pragma unroll
+            for (int i = 0; i < MAXS; i++) {
+                const int st = s0 + i;
+                if (st >= e1) break;
+                const uint4 va = lds128(wA + st * 64), vb = lds128(wB + st * 64);
+                const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+                const long ls = off / 64 + st;                  // step within the k-range
+                if (FP8) {
+                    uint32_t xw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    if (xrow_ok) {
+                        uint4 xa, xb;
+                        if (XS) {
+                            const uint16_t *xp = xs + g * xstride + ls * 64 + 16 * t4;
+                            xa = lds128(xp); xb = lds128(xp + 8);
+                        } else {
+                            const uint16_t *xp = d.x + (size_t)g * d.ldx + k0 + ls * 64 + 16 * t4;
+                            xa = ld_nc16(xp); xb = ld_nc16(xp + 8);
+                        }
+                        xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
+                        xw[4] = xb.x; xw[5] = xb.y; xw[6] = xb.z; xw[7] = xb.w;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        uint32_t a0, a2, a1, a3;
+                        dequant4(wa[j], scA[i], a0, a2);
+                        dequant4(wb[j], scB[i], a1, a3);
+                        mma_bf16_16816(acc[j][0], acc[j][1], acc[j][2], acc[j][3],
+                                       a0, a1, a2, a3, xw[2 * j], xw[2 * j + 1]);
+                    }
+                } else {
+                    uint32_t xw[4] = {0, 0, 0, 0};
+                    if (xrow_ok) {
+                        uint4 xa;
+                        if (XS) xa = lds128(xs + g * xstride + ls * 32 + 8 * t4);
+                        else xa = ld_nc16(d.x + (size_t)g * d.ldx + k0 + ls * 32 + 8 * t4);
+                        xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        const int q = (i & 1) * 2 + j;
+                        mma_bf16_16816(acc[q][0], acc[q][1], acc[q][2], acc[q][3],
+                                       wa[2 * j], wb[2 * j], wa[2 * j + 1], wb[2 * j + 1],
+                                       xw[2 * j], xw[2 * j + 1]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // D layout: c0 = (w row g, x col 2t), c1 = (g, 2t+1), c2 = (g+8, 2t), c3 = (g+8, 2t+1)
+        float *pw = part + warp * PART;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int xc = 2 * t4 + (e & 1), wr = g + 8 * (e >> 1);
+            pw[xc * TR + wr] = (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+        }
+        named_bar_sync(1, 256);
+        const int tid = threadIdx.x;
+        // thread tid < 128: x col m = tid/16, weight row o = tid%16
+        float a = 0.f;
+        if (tid < 128) {
+            a = part[tid];
+#pragma unroll
+            for (int w = 1; w < 8; w++) a = a + part[w * PART + tid];
+        }
+        if (nks == 1) {
+            if (tid < 128) gemv_store(d, tid >> 4, row0 + (tid & 15), a, best_sh, (tid & 15) == 0);
+        } else {
+            // publish this range's partial; the last range of the tile reduces
+            float *slot = d.part + ((size_t)t * nks + ks) * PART;
+            if (tid < 128) slot[tid] = a;
+            __threadfence();
+            named_bar_sync(1, 256);
+            if (tid == 0) ticket_sh = atomicAdd(d.ticket + t, 1);
+            named_bar_sync(1, 256);
+            if (ticket_sh == nks - 1) {
+                __threadfence();
+                if (tid < 128) {
+                    const float *base = d.part + (size_t)t * nks * PART;
+                    float r = __ldcg(base + tid);
+                    for (int q = 1; q < nks; q++) r = r + __ldcg(base + q * PART + tid);
+                    gemv_store(d, tid >> 4, row0 + (tid & 15), r, best_sh, (tid & 15) == 0);
+                }
+                if (tid == 0) d.ticket[t] = 0;     // ready for the next launch
+            }
+        }
+        named_bar_sync(1, 256);
+    }
+    if (d.amax && threadIdx.x < d.R && best_sh[threadIdx.x])
+        atomicMax(d.amax + threadIdx.x, best_sh[threadIdx.x]);
 }
 
 // Generic GEMV for shapes the fast path cannot stream (K not a multiple of
@@ -146,6 +361,13 @@ __global__ void k_argmax_extract(const unsigned long long *keys, int32_t *ids, i
 
 using namespace apus;
 
+void gemv_scratch_need(long O, long K, size_t *part_floats, size_t *tickets) {
+    const long nks = (K + gemvcfg::KX - 1) / gemvcfg::KX;
+    const long ntile = (O + gemvcfg::TR - 1) / gemvcfg::TR;
+    *part_floats = nks > 1 ? (size_t)(ntile * nks * gemvcfg::PART) : 0;
+    *tickets = nks > 1 ? (size_t)ntile : 0;
+}
+
 bool gemv_fast_ok(const GemvDesc &d) {
     const int kstep = d.fp8 ? 64 : 32;
     if (d.K <= 0 || d.K % kstep) return false;
@@ -154,19 +376,69 @@ bool gemv_fast_ok(const GemvDesc &d) {
     return true;
 }
 
+static int g_num_sms = 0;
+
+static size_t gemv_smem(bool xs) {
+    using namespace gemvcfg;
+    return NSTAGE * STAGE_BYTES + (xs ? XMAX : 0) + 8 * PART * 4 + 2 * NSTAGE * 8;
+}
+
+template <bool FP8, bool XS>
+static int launch_tma(const GemvDesc &d, cudaStream_t st) {
+    static bool attr = false;
+    const size_t sm = gemv_smem(XS);
+    if (!attr) {
+        if (cudaFuncSetAttribute(k_gemv_tma<FP8, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
+            != cudaSuccess) return -1;
+        attr = true;
+    }
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const long ntile = (d.O + gemvcfg::TR - 1) / gemvcfg::TR;
+    const long nks = (d.K + gemvcfg::KX - 1) / gemvcfg::KX;
+    long per_ks = (2L * g_num_sms) / nks;                    // CTAs per k-range
+    if (per_ks < 1) per_ks = 1;
+    if (per_ks > ntile) per_ks = ntile;
+    const long grid = per_ks * nks;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(gemvcfg::THREADS);
+    cfg.dynamicSmemBytes = sm;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = d.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_gemv_tma<FP8, XS>, d) == cudaSuccess ? 0 : -1;
+}
+
 int gemv_launch(const GemvDesc &d, cudaStream_t st) {
     if (d.R < 1 || d.R > 8 || d.O <= 0 || d.K <= 0) return -1;
     if (gemv_fast_ok(d)) {
-        constexpr int RG = 2;
-        const unsigned grid = (unsigned)((d.O + 8 * RG - 1) / (8 * RG));
-        if (d.fp8) k_gemv<true, RG><<<grid, 256, 0, st>>>(d);
-        else k_gemv<false, RG><<<grid, 256, 0, st>>>(d);
+        const long klen = d.K < gemvcfg::KX ? d.K : gemvcfg::KX;
+        const bool xs = (long)d.R * (klen * 2 + 16) <= gemvcfg::XMAX;
+        if (d.K > gemvcfg::KX && (!d.part || !d.ticket)) return -1;
+        int rc;
+        if (d.fp8) rc = xs ? launch_tma<true, true>(d, st) : launch_tma<true, false>(d, st);
+        else rc = xs ? launch_tma<false, true>(d, st) : launch_tma<false, false>(d, st);
+        if (rc) return -1;
     } else {
         const unsigned grid = (unsigned)((d.O + 7) / 8);
         if (d.fp8) k_gemv_generic<true><<<grid, 256, 0, st>>>(d);
         else k_gemv_generic<false><<<grid, 256, 0, st>>>(d);
     }
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int kernel_error_read_and_clear(void) {
+    int v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, g_apus_kernel_err, sizeof v);
+    cudaMemcpyToSymbol(g_apus_kernel_err, &z, sizeof z);
+    return v;
 }
 
 int fp8_dequant_launch(const uint8_t *w, const float *ws, uint16_t *out, size_t O, size_t K,

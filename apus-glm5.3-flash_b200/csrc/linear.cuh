@@ -13,9 +13,9 @@
 // the batch invariance the speculative verify relies on.
 //
 // Work decomposition.  A warp owns 8 weight rows and a contiguous range of
-// 64-byte k-steps.  Lane (g = lane/4, t = lane%4) streams 16 bytes of weight
-// row g per step (FP8: 16 codes, BF16: 8 values) with one 128-bit
-// non-allocating load, converts them into the B fragment of
+// 64-byte k-steps.  Lane (g = lane/4, t = lane%4) reads 16 bytes of weight
+// row g per step (FP8: 16 codes, BF16: 8 values) from the shared-memory
+// stage the bulk copies filled, converts them into the B fragment of
 // mma.m16n8k16.bf16 (the weight rows are the n = 8 columns), and loads the
 // matching activation k-values of row g as the A fragment (rows 8..15 of A
 // are padding).  The k-permutation inside a step is the same for A and B,
@@ -77,67 +77,35 @@ APUS_DEV void mma_bf16_16816(float &d0, float &d1, float &d2, float &d3,
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// One warp: 8 weight rows x k-steps [s0, s1).  Each step is 64 bytes of a
-// weight row (FP8: 64 codes; BF16: 32 values).  wrow_ptr points at this
-// lane's weight row (row g of the group, already clamped to a valid row),
-// offset by 16*t bytes.  xrow points at activation row g offset to this
-// lane's first k (FP8: 16*t elements, BF16: 8*t), or nullptr when g >= R.
-// srow: FP8 scale row of weight row g (ws + (row/128)*nkb), unused for BF16.
-// Returns the partial dot products for (x row g, weight rows 2t, 2t+1).
+APUS_DEV void mma_f16_16816(float &d0, float &d1, float &d2, float &d3,
+                            uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                            uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 64-byte k-step of the staged GEMV for lane (g, t): wv is the lane's
+// 16 weight bytes of row g; xw the activation words of row g covering the
+// same k range (FP8: 8 words = 16 values, BF16: 4 words = 8 values).
 template <bool FP8>
-APUS_DEV void warp_rows8(const uint8_t *wrow_ptr, const uint16_t *xrow,
-                         const float *srow, int s0, int s1,
-                         float &out0, float &out1) {
-    constexpr int U = 4;
-    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-    uint4 wb[U];
+APUS_DEV void gemv_step(const uint4 wv4, const uint32_t *xw, float sc, float &d0, float &d1,
+                        float &d2, float &d3) {
+    const uint32_t wv[4] = {wv4.x, wv4.y, wv4.z, wv4.w};
+    if (FP8) {
 #pragma unroll
-    for (int u = 0; u < U; u++)
-        if (s0 + u < s1) wb[u] = ld_stream16(wrow_ptr + (size_t)(s0 + u) * 64);
-    for (int s = s0; s < s1; s += U) {
-        uint4 cur[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) cur[u] = wb[u];
-#pragma unroll
-        for (int u = 0; u < U; u++)
-            if (s + U + u < s1) wb[u] = ld_stream16(wrow_ptr + (size_t)(s + U + u) * 64);
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int st = s + u;
-            if (st < s1) {
-                const uint32_t wv[4] = {cur[u].x, cur[u].y, cur[u].z, cur[u].w};
-                if (FP8) {
-                    uint32_t xw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    if (xrow) {
-                        uint4 xa = ld_nc16(xrow + (size_t)st * 64);
-                        uint4 xb = ld_nc16(xrow + (size_t)st * 64 + 8);
-                        xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
-                        xw[4] = xb.x; xw[5] = xb.y; xw[6] = xb.z; xw[7] = xb.w;
-                    }
-                    const float sc = __ldg(srow + (st >> 1));
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        uint32_t b0, b1;
-                        dequant4(wv[j], sc, b0, b1);
-                        mma_bf16_16816(d0, d1, d2, d3, xw[2 * j], 0u, xw[2 * j + 1], 0u, b0, b1);
-                    }
-                } else {
-                    uint32_t xw[4] = {0, 0, 0, 0};
-                    if (xrow) {
-                        uint4 xa = ld_nc16(xrow + (size_t)st * 32);
-                        xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
-                    }
-#pragma unroll
-                    for (int j = 0; j < 2; j++)
-                        mma_bf16_16816(d0, d1, d2, d3, xw[2 * j], 0u, xw[2 * j + 1], 0u,
-                                       wv[2 * j], wv[2 * j + 1]);
-                }
-            }
+        for (int j = 0; j < 4; j++) {
+            uint32_t b0, b1;
+            dequant4(wv[j], sc, b0, b1);
+            mma_bf16_16816(d0, d1, d2, d3, xw[2 * j], 0u, xw[2 * j + 1], 0u, b0, b1);
         }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+            mma_bf16_16816(d0, d1, d2, d3, xw[2 * j], 0u, xw[2 * j + 1], 0u, wv[2 * j], wv[2 * j + 1]);
     }
-    (void)d2; (void)d3;
-    out0 = d0;
-    out1 = d1;
 }
 
 }  // namespace apus

@@ -161,6 +161,7 @@ def bench_c0(args, ws, rank):
     dy = torch.empty((M, N), dtype=torch.int16, device="cuda")
     st = torch.cuda.Stream()
     sp = G.C.c_void_p(st.cuda_stream)
+    G.apus_gcuda_set_pdl(1)   # consecutive linears overlap their weight streams
 
     def step(i):
         G.check(G.apus_gcuda_fp8blk_linear_dev(G.ptr(dW[i % nbuf]), G.ptr(dS), G.ptr(dx), G.ptr(dy),

@@ -35,6 +35,10 @@ void apus_gcuda_disable(void);                           /* c/backend_gmetal.h:1
 int  apus_gcuda_is_enabled(void);                        /* c/backend_gmetal.h:137 */
 /* Last error message of the calling thread ("" when none). */
 const char *apus_gcuda_last_error(void);
+/* Device-side error word of the pipelined kernels (0 = none; nonzero = a
+ * bounded wait gave up: 1 producer, 2 consumer), read and cleared.
+ * Synchronises the device. */
+int apus_gcuda_kernel_error(void);
 
 /* Persistent HBM residency for a model-owned host weight region: the bytes
  * are uploaded once; hooked ops whose weight pointer lies inside a
@@ -77,6 +81,11 @@ void apus_bf16_gemm_mt(const uint16_t *w, const uint16_t *x, float *xf,
                        uint16_t *y, size_t M, size_t O, size_t K); /* c/bf16.h:150-151 */
 
 /* ---- device-pointer twins ------------------------------------------------ */
+/* Launch the `_dev` linears as programmatic dependents of the previous kernel
+ * in the stream (their weight stream starts while it drains).  Only safe when
+ * no kernel immediately before a linear writes that linear's weights. Off by
+ * default. */
+void apus_gcuda_set_pdl(int on);
 int apus_fp8blk_dequant_dev(const uint8_t *w, const float *ws, uint16_t *out,
                             size_t O, size_t K, void *stream);
 /* y [M,O] BF16 codes; M <= 8 per launch (larger M is split into 8-row

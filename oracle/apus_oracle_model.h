@@ -1,0 +1,103 @@
+/*
+ * apus_oracle_model.h — CPU restatement (TEST INFRASTRUCTURE ONLY) of the
+ * apus GLM-5.3-Flash decode stack: mHC, MoE, KDA, DSA, the layer loop, the
+ * MTP draft head and the greedy speculative step.  The checker of the CUDA
+ * engine; never linked into it.
+ */
+#ifndef APUS_ORACLE_MODEL_H
+#define APUS_ORACLE_MODEL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORC_MAX_LAYERS 64
+
+/* Field names and meaning of ApusGmodelConfig (c/gmodel.h:88-108); the two
+ * per-layer pattern arrays are inline. */
+typedef struct {
+    int hidden_size, vocab_size, num_hidden_layers;
+    float rms_norm_eps;
+    int hc_mult, hc_sinkhorn_iters;
+    float hc_eps;
+    int first_k_dense_replace;
+    int intermediate_size, moe_intermediate_size;
+    int n_routed_experts, n_shared_experts, num_experts_per_tok;
+    float routed_scaling_factor;
+    int norm_topk_prob;
+    float swiglu_limit;
+    int num_attention_heads, q_lora_rank, kv_lora_rank;
+    int qk_nope_head_dim, v_head_dim;
+    int index_n_heads, index_head_dim, index_topk, index_kpool;
+    int index_kpool_always_select_tail;
+    int linear_num_heads, linear_head_dim, linear_conv_kernel_dim;
+    float linear_lower_bound;
+    int num_nextn_predict_layers;
+    int layer_is_dsa[ORC_MAX_LAYERS];
+    int mlp_is_sparse[ORC_MAX_LAYERS];
+} OrcConfig;
+
+typedef struct OrcModel OrcModel;
+typedef struct OrcState OrcState;
+typedef struct OrcMtpState OrcMtpState;
+typedef struct OrcSpec OrcSpec;
+
+/* model: weights are caller-owned arrays registered by checkpoint name
+ * ("layers.3.self_attn.q_a_proj.weight", "embed_tokens.weight", ...). */
+OrcModel *orc_model_new(const OrcConfig *c, int has_mtp);
+void orc_model_free(OrcModel *m);
+int  orc_model_set(OrcModel *m, const char *name, const void *data);  /* 0 ok, -1 unknown */
+const char *orc_model_missing(const OrcModel *m);   /* first unset tensor or NULL */
+
+OrcState *orc_state_new(const OrcModel *m, size_t cap);
+void orc_state_free(OrcState *st);
+size_t orc_state_pos(const OrcState *st);
+
+/* apus_gmodel_decode_batch (c/gmodel.h:1648-1656): s tokens, RECURRENT KDA,
+ * per-token DSA interleave.  logits [s,V], h_out [s,hc*d], yn_out [s,d]
+ * (BF16 codes; h_out/yn_out may be NULL). */
+int orc_decode_batch(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
+                     uint16_t *logits, uint16_t *h_out, uint16_t *yn_out);
+
+/* Sublayer entry points for unit parity (state passed explicitly). */
+void orc_rmsnorm(const uint16_t *x, const uint16_t *w, uint16_t *y, size_t n, float eps);
+void orc_layernorm(const uint16_t *x, const uint16_t *w, const uint16_t *b, uint16_t *y,
+                   size_t n, float eps);
+void orc_hc_pre(const OrcModel *m, int layer, int ffn, const uint16_t *h4, uint16_t *x,
+                float *post, float *comb);
+void orc_hc_post(const uint16_t *x, const uint16_t *res4, const float *post, const float *comb,
+                 uint16_t *y4, size_t d, size_t n);
+void orc_hc_head(const uint16_t *x4, uint16_t *y, size_t d, size_t n);
+void orc_moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out,
+                     int32_t *idx_out, float *w_out);
+void orc_kda_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,
+                    uint16_t *conv_state, float *rec_state, uint16_t *out);
+void orc_dsa_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,
+                    OrcState *st, uint16_t *out);
+
+/* MTP head (c/gmtp.h:471-541) and its DSA-cache state. */
+OrcMtpState *orc_mtp_state_new(const OrcModel *m, size_t cap);
+void orc_mtp_state_free(OrcMtpState *st);
+int orc_mtp_forward(OrcModel *m, OrcMtpState *mst, const int32_t *ids, const uint16_t *prev_h,
+                    size_t s, uint16_t *logits, uint16_t *out_h);
+
+/* Greedy speculative decode (c/gmtp.h:617-891), depth D = verify rows. */
+typedef void (*OrcDraftHook)(void *ctx, int64_t q, int32_t *drafts, int n);
+OrcSpec *orc_spec_new(OrcModel *m, OrcState *st, OrcMtpState *mst, int depth);
+void orc_spec_free(OrcSpec *sp);
+void orc_spec_set_draft_hook(OrcSpec *sp, OrcDraftHook hook, void *ctx);
+int  orc_spec_prefill(OrcSpec *sp, const int32_t *ids, size_t n);
+int  orc_spec_step(OrcSpec *sp, int *out, int cap);
+/* stats: emitted, batches, refeed, offered, accepted, q, held */
+void orc_spec_stats(const OrcSpec *sp, uint64_t *out7);
+
+/* Non-speculative greedy decode: prefill then n_gen argmax tokens. */
+int orc_greedy(OrcModel *m, OrcState *st, const int32_t *ids, size_t n, int n_gen, int32_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

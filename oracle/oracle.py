@@ -104,3 +104,119 @@ def bf16_of(x):
     nan = (u & 0x7FFFFFFF) > 0x7F800000
     r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF
     return np.where(nan, (u >> 16) & 0xFFFF, r).astype(np.uint16)
+
+
+# ---- model-level restatement (apus_oracle_model.c) -------------------------
+
+MAX_LAYERS = 64
+_CFG_FIELDS = [
+    ("hidden_size", C.c_int), ("vocab_size", C.c_int), ("num_hidden_layers", C.c_int),
+    ("rms_norm_eps", C.c_float), ("hc_mult", C.c_int), ("hc_sinkhorn_iters", C.c_int),
+    ("hc_eps", C.c_float), ("first_k_dense_replace", C.c_int), ("intermediate_size", C.c_int),
+    ("moe_intermediate_size", C.c_int), ("n_routed_experts", C.c_int), ("n_shared_experts", C.c_int),
+    ("num_experts_per_tok", C.c_int), ("routed_scaling_factor", C.c_float), ("norm_topk_prob", C.c_int),
+    ("swiglu_limit", C.c_float), ("num_attention_heads", C.c_int), ("q_lora_rank", C.c_int),
+    ("kv_lora_rank", C.c_int), ("qk_nope_head_dim", C.c_int), ("v_head_dim", C.c_int),
+    ("index_n_heads", C.c_int), ("index_head_dim", C.c_int), ("index_topk", C.c_int),
+    ("index_kpool", C.c_int), ("index_kpool_always_select_tail", C.c_int), ("linear_num_heads", C.c_int),
+    ("linear_head_dim", C.c_int), ("linear_conv_kernel_dim", C.c_int), ("linear_lower_bound", C.c_float),
+    ("num_nextn_predict_layers", C.c_int), ("layer_is_dsa", C.c_int * MAX_LAYERS),
+    ("mlp_is_sparse", C.c_int * MAX_LAYERS),
+]
+
+
+class Config(C.Structure):
+    """Field names of ApusGmodelConfig (c/gmodel.h:88-108); also the layout of
+    OrcConfig and ApusGcudaConfig."""
+    _fields_ = _CFG_FIELDS
+
+
+def make_config(**kw):
+    c = Config()
+    for name, _ in _CFG_FIELDS:
+        if name in ("layer_is_dsa", "mlp_is_sparse"):
+            continue
+        setattr(c, name, kw[name])
+    L = kw["num_hidden_layers"]
+    for i in range(L):
+        c.layer_is_dsa[i] = int(kw["layer_is_dsa"][i])
+        c.mlp_is_sparse[i] = int(kw["mlp_is_sparse"][i])
+    return c
+
+
+_decl(ORC, "orc_model_new", _vp, _vp, _i)
+_decl(ORC, "orc_model_free", None, _vp)
+_decl(ORC, "orc_model_set", _i, _vp, C.c_char_p, _vp)
+_decl(ORC, "orc_state_new", _vp, _vp, _sz)
+_decl(ORC, "orc_state_free", None, _vp)
+_decl(ORC, "orc_state_pos", _sz, _vp)
+_decl(ORC, "orc_decode_batch", _i, _vp, _vp, _vp, _sz, _vp, _vp, _vp)
+_decl(ORC, "orc_mtp_state_new", _vp, _vp, _sz)
+_decl(ORC, "orc_mtp_state_free", None, _vp)
+_decl(ORC, "orc_mtp_forward", _i, _vp, _vp, _vp, _vp, _sz, _vp, _vp)
+_decl(ORC, "orc_spec_new", _vp, _vp, _vp, _vp, _i)
+_decl(ORC, "orc_spec_free", None, _vp)
+_decl(ORC, "orc_spec_set_draft_hook", None, _vp, _vp, _vp)
+_decl(ORC, "orc_spec_prefill", _i, _vp, _vp, _sz)
+_decl(ORC, "orc_spec_step", _i, _vp, _vp, _i)
+_decl(ORC, "orc_spec_stats", None, _vp, _vp)
+_decl(ORC, "orc_greedy", _i, _vp, _vp, _vp, _sz, _i, _vp)
+_decl(ORC, "orc_rmsnorm", None, _vp, _vp, _vp, _sz, _f)
+_decl(ORC, "orc_hc_pre", None, _vp, _i, _i, _vp, _vp, _vp, _vp)
+_decl(ORC, "orc_hc_post", None, _vp, _vp, _vp, _vp, _vp, _sz, _sz)
+_decl(ORC, "orc_hc_head", None, _vp, _vp, _sz, _sz)
+_decl(ORC, "orc_moe_forward", None, _vp, _i, _vp, _sz, _vp, _vp, _vp)
+_decl(ORC, "orc_kda_decode", None, _vp, _i, _vp, _sz, _vp, _vp, _vp)
+_decl(ORC, "orc_dsa_decode", None, _vp, _i, _vp, _sz, _vp, _vp)
+
+DRAFT_HOOK = C.CFUNCTYPE(None, _vp, C.c_int64, C.POINTER(C.c_int32), C.c_int)
+
+if REF is not None:
+    _decl(REF, "ref_model_new", _vp, _vp, _i)
+    _decl(REF, "ref_model_set", _i, _vp, C.c_char_p, _vp)
+    _decl(REF, "ref_model_finalize", None, _vp)
+    _decl(REF, "ref_state_new", _vp, _vp, _sz)
+    _decl(REF, "ref_state_free", None, _vp)
+    _decl(REF, "ref_decode_batch", _i, _vp, _vp, _vp, _sz, _vp, _vp, _vp)
+    _decl(REF, "ref_spec_new", _vp, _vp, _vp, _sz, _i)
+    _decl(REF, "ref_spec_free", None, _vp)
+    _decl(REF, "ref_spec_set_draft_hook", None, _vp, _vp, _vp)
+    _decl(REF, "ref_spec_prefill", _i, _vp, _vp, _sz)
+    _decl(REF, "ref_spec_step", _i, _vp, _vp, _i)
+    _decl(REF, "ref_spec_stats", None, _vp, _vp)
+    _decl(REF, "ref_mtp_forward", _i, _vp, _vp, _vp, _sz, _vp, _vp)
+
+
+class Model:
+    """A weight dict (name -> numpy array, caller-owned) bound to the oracle
+    restatement (kind='orc') or the reference engine (kind='ref')."""
+
+    def __init__(self, cfg, weights, has_mtp, kind="orc"):
+        self.cfg, self.w, self.kind = cfg, weights, kind
+        self.lib = ORC if kind == "orc" else REF
+        if kind == "orc":
+            self.h = ORC.orc_model_new(C.byref(cfg), int(has_mtp))
+            setter = ORC.orc_model_set
+        else:
+            self.h = REF.ref_model_new(C.byref(cfg), int(has_mtp))
+            setter = REF.ref_model_set
+        for name, arr in weights.items():
+            if setter(self.h, name.encode(), p(arr)) != 0:
+                raise KeyError(name)
+        if kind == "ref":
+            REF.ref_model_finalize(self.h)
+
+    def state(self, cap):
+        return (ORC.orc_state_new if self.kind == "orc" else REF.ref_state_new)(self.h, cap)
+
+    def decode_batch(self, st, ids, want_h=False):
+        cfg = self.cfg
+        s = len(ids)
+        ids = np.ascontiguousarray(ids, np.int32)
+        logits = np.empty((s, cfg.vocab_size), np.uint16)
+        h = np.empty((s, cfg.hc_mult * cfg.hidden_size), np.uint16)
+        yn = np.empty((s, cfg.hidden_size), np.uint16)
+        fn = ORC.orc_decode_batch if self.kind == "orc" else REF.ref_decode_batch
+        rc = fn(self.h, st, p(ids), s, p(logits), p(h), p(yn))
+        assert rc == 0
+        return (logits, h, yn) if want_h else logits

@@ -111,11 +111,12 @@ def _dev_linear(gcuda, fp8, W, S, x):
                                             M, O_, W.shape[1], gcuda.stream_of())
     gcuda.check(rc, "linear_dev")
     torch.cuda.synchronize()
+    assert gcuda.apus_gcuda_kernel_error() == 0
     return dy.cpu().numpy().view(np.uint16)
 
 
 @pytest.mark.parametrize("shape", [(4, 4096, 4096), (1, 1536, 4096), (8, 512, 4096), (3, 4096, 1024),
-                                   (4, 300, 1536)])
+                                   (4, 300, 1536), (4, 520, 16384), (6, 256, 12288)])
 def test_fp8_gemv_vs_oracle(gcuda, shape):
     M, O_, K = shape
     rng = np.random.default_rng(hash(shape) & 0xffff)
@@ -125,7 +126,8 @@ def test_fp8_gemv_vs_oracle(gcuda, shape):
     assert_close_rows(got, O.fp8_linear(c, s, x))
 
 
-@pytest.mark.parametrize("shape", [(4, 4096, 4096), (1, 2048, 8192), (5, 288, 4096), (2, 40, 512)])
+@pytest.mark.parametrize("shape", [(4, 4096, 4096), (1, 2048, 8192), (5, 288, 4096), (2, 40, 512),
+                                   (4, 1000, 8192), (8, 64, 6144)])
 def test_bf16_gemv_vs_oracle(gcuda, shape):
     M, O_, K = shape
     rng = np.random.default_rng(hash(shape) & 0xffff)
@@ -135,12 +137,13 @@ def test_bf16_gemv_vs_oracle(gcuda, shape):
     assert_close_rows(got, O.bf16_gemm(w, x))
 
 
-@pytest.mark.parametrize("fp8", [True, False])
-def test_row_count_invariance_bitwise(gcuda, fp8):
+@pytest.mark.parametrize("fp8,K", [(True, 2048), (False, 2048), (True, 12288), (False, 8192)])
+def test_row_count_invariance_bitwise(gcuda, fp8, K):
     """Row m of an R-row call is bitwise the 1-row call on row m (the
-    property speculative verify == sequential decode rests on)."""
+    property speculative verify == sequential decode rests on), with and
+    without the split-K reduction."""
     rng = np.random.default_rng(5)
-    O_, K = 1024, 2048
+    O_ = 1024
     if fp8:
         W, S = fp8_weights(rng, O_, K)
     else:
