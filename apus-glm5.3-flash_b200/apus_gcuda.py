@@ -53,6 +53,17 @@ apus_gcuda_bf16_gemm_dev = _fn("apus_gcuda_bf16_gemm_dev", _i, _vp, _vp, _vp, _s
 apus_gcuda_bf16_gemm_f32_dev = _fn("apus_gcuda_bf16_gemm_f32_dev", _i, _vp, _vp, _vp, _sz, _sz, _sz, _vp)
 apus_gcuda_bf16_gemm_argmax_dev = _fn("apus_gcuda_bf16_gemm_argmax_dev", _i, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp)
 
+_f = C.c_float
+apus_gcuda_moe_new = _fn("apus_gcuda_moe_new", _vp, _i, _i, _sz, _sz, _f, _f, _i)
+apus_gcuda_moe_free = _fn("apus_gcuda_moe_free", None, _vp)
+apus_gcuda_moe_set = _fn("apus_gcuda_moe_set", _i, _vp, C.c_char_p, _vp, _sz)
+apus_gcuda_moe_get = _fn("apus_gcuda_moe_get", _i, _vp, C.c_char_p, _vp, _sz)
+apus_gcuda_moe_init_random = _fn("apus_gcuda_moe_init_random", _i, _vp, C.c_uint64)
+apus_gcuda_moe_forward_dev = _fn("apus_gcuda_moe_forward_dev", _i, _vp, _vp, _sz, _vp, _vp, _vp)
+apus_gcuda_moe_forward2 = _fn("apus_gcuda_moe_forward2", _i, _vp, _vp, _sz, _vp, _vp)
+apus_gcuda_moe_last_routing = _fn("apus_gcuda_moe_last_routing", _i, _vp, _sz, _vp, _vp)
+apus_gcuda_moe_last_bytes = _fn("apus_gcuda_moe_last_bytes", _u64, _vp)
+
 
 class GcudaError(RuntimeError):
     pass

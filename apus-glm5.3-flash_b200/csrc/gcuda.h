@@ -23,6 +23,18 @@ struct GemvDesc {
     int *ticket;            // split-K tile counters [ceil(O/16)], zero between launches
     int pdl;                // launch as a programmatic dependent of the previous kernel
     int weights_after_wait; // weight pointers are produced by the previous kernel
+    // Grouped mode (gexpert != null): problem p of *gcount (<= gmax) uses the
+    // weights of expert gexpert[p] inside packed arrays (W + w_estride bytes per
+    // expert, WS + s_estride floats per expert), activations x + p*x_pstride
+    // and output y + p*y_pstride.  K must fit one k-range (K <= 4096).
+    const int *gexpert;
+    const int *gcount;
+    int gmax;
+    long w_estride, s_estride, x_pstride, y_pstride;
+    // x holds [R][2K] gate|up pairs; the staged activation is the SwiGLU
+    // h = bf16(bf16(silu(min(g, lim))) * clip(u, +-lim)) (c/gmoe.h:216-224).
+    int x_swiglu;
+    float swiglu_limit;
 };
 
 bool gemv_fast_ok(const GemvDesc &d);
@@ -39,3 +51,9 @@ int argmax_extract_launch(const unsigned long long *keys, int32_t *ids, int n, c
 // error plumbing (capi.cu)
 void gcuda_set_error(const char *fmt, ...);
 int gcuda_check(cudaError_t e, const char *what);
+
+// seeded device-side weight fill (init.cu)
+enum { FILL_BF16_NORMAL = 0, FILL_E4M3_NORMAL = 1, FILL_F32_LOGUNIFORM = 2, FILL_F32_NORMAL = 3,
+       FILL_F32_CONST = 4, FILL_BF16_CONST = 5 };
+int fill_launch(int kind, void *dst, size_t n, uint64_t seed, uint64_t stream_id, float a, float b,
+                cudaStream_t st);

@@ -1,0 +1,181 @@
+// gmoe.cu — the GLM-5.3-Flash MoE sublayer on the B200 (c/gmoe.h semantics).
+//
+// Decode shape: R <= 8 token rows, E routed experts (288) + 1 shared expert,
+// top-k (8).  Per layer call, with no host round-trip:
+//   1. router GEMV: fp32 logits [R][E] = x . gate_w (c/gmoe.h:168-173);
+//   2. k_moe_route (one CTA): sigmoid (numpy-stable), +bias for selection,
+//      stable top-k with lower-index ties, weights from the unbiased scores
+//      normalised with the numpy pairwise sum and scaled (c/gmoe.h:191-208);
+//      builds the device work list: the union of selected experts in
+//      ascending order plus the shared expert last;
+//   3. grouped FP8 GEMV over the work list: gate|up rows [2*inter][dim] of
+//      every active expert -> gu [P][R][2*inter];
+//   4. grouped FP8 GEMV down [dim][inter] whose activation staging applies the
+//      SwiGLU with the clamps (c/gmoe.h:216-224) -> yd [P][R][dim];
+//   5. k_moe_combine: per row, ascending expert index, contrib =
+//      bf16(bf16(expert) * w) and y = bf16(y + contrib), shared expert last
+//      (c/gmoe.h:305-336).
+// Expert weights live in HBM packed per layer: codes [E+1][2*inter][dim]
+// (gate rows then up rows; expert E is the shared expert) and
+// [E+1][dim][inter], F32 128x128 block scales packed the same way.
+#include "common.cuh"
+#include "gcuda.h"
+#include "gmoe_dev.h"
+
+namespace apus {
+
+// c/gmhc.h:165-185 for n <= 8 (the router weight sum, n = topk)
+APUS_DEV float pw_sum_small(const float *a, int n) {
+    if (n < 8) {
+        float r = a[0];
+        for (int i = 1; i < n; i++) r += a[i];
+        return r;
+    }
+    return pw_sum_leaf(a, n);
+}
+
+__global__ void k_moe_route(MoeDev m, int R, const float *logits, const int32_t *forced) {
+    __shared__ float sc[MOE_MAX_R][MOE_MAX_E];
+    __shared__ float bi[MOE_MAX_R][MOE_MAX_E];
+    __shared__ int32_t sel[MOE_MAX_R][MOE_MAX_TOPK];
+    __shared__ int flag[MOE_MAX_E + 1];
+    __shared__ int slot_of[MOE_MAX_E + 1];
+    const int E = m.E, K = m.topk;
+    for (int i = threadIdx.x; i < R * E; i += blockDim.x) {
+        const int r = i / E, e = i % E;
+        const float s = sigmoid_np(logits[(size_t)r * E + e]);
+        sc[r][e] = s;
+        bi[r][e] = s + m.gate_bias[e];
+    }
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) flag[e] = 0;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < R) {      // one warp per row: k passes of a lowest-index argmax
+        const int r = warp;
+        for (int j = 0; j < K; j++) {
+            float best = 0.f;
+            int bidx = -1;
+            for (int e = lane; e < E; e += 32) {
+                bool used = false;
+                for (int q = 0; q < j; q++) used |= (sel[r][q] == e);
+                if (used) continue;
+                const float v = bi[r][e];
+                if (bidx < 0 || v > best) { best = v; bidx = e; }
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+                const int oi = __shfl_xor_sync(0xffffffffu, bidx, off);
+                if (oi >= 0 && (bidx < 0 || ov > best || (ov == best && oi < bidx))) { best = ov; bidx = oi; }
+            }
+            if (forced) bidx = forced[r * K + j];
+            if (lane == 0) sel[r][j] = bidx;
+            __syncwarp();
+        }
+        if (lane == 0) {
+            float w[MOE_MAX_TOPK];
+            for (int j = 0; j < K; j++) w[j] = sc[r][sel[r][j]];
+            const float sum = pw_sum_small(w, K);
+            for (int j = 0; j < K; j++) w[j] = w[j] / (sum + 1e-20f) * m.route_scale;
+            // the combine walks the row's experts in ascending index order
+            int32_t id[MOE_MAX_TOPK];
+            for (int j = 0; j < K; j++) id[j] = sel[r][j];
+            for (int a = 1; a < K; a++)
+                for (int b = a; b > 0 && id[b - 1] > id[b]; b--) {
+                    int32_t ti = id[b]; id[b] = id[b - 1]; id[b - 1] = ti;
+                    float tw = w[b]; w[b] = w[b - 1]; w[b - 1] = tw;
+                }
+            for (int j = 0; j < K; j++) {
+                m.row_expert[r * K + j] = id[j];
+                m.row_weight[r * K + j] = w[j];
+                // unsorted selection, for inspection (c/gmoe.h:112-117 router_idx)
+                m.row_sel[r * K + j] = sel[r][j];
+                atomicExch(&flag[id[j]], 1);
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int p = 0;
+        for (int e = 0; e < E; e++) {
+            slot_of[e] = p;
+            if (flag[e]) m.prob_expert[p++] = e;
+        }
+        slot_of[E] = p;
+        m.prob_expert[p++] = E;            // shared expert, always last
+        *m.prob_count = p;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < R * K; i += blockDim.x)
+        m.row_prob[i] = slot_of[m.row_expert[i]];
+    if (threadIdx.x < R) m.row_prob_shared[threadIdx.x] = slot_of[E];
+}
+
+// out[r][i] = bf16(y + shared), y = ascending bf16 accumulation of
+// bf16(bf16(expert) * w) (c/gmoe.h:305-336).
+__global__ void k_moe_combine(MoeDev m, int R, uint16_t *out, long ldo) {
+    const int d = m.dim, K = m.topk;
+    const size_t pstride = (size_t)m.max_r * d;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < (long)R * d;
+         i += (long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / d), c = (int)(i % d);
+        float y = 0.f;
+        for (int j = 0; j < K; j++) {
+            const int p = m.row_prob[r * K + j];
+            const float e = bf16_f32(m.yd[p * pstride + (size_t)r * d + c]);
+            const float contrib = bf16_round(e * m.row_weight[r * K + j]);
+            y = bf16_round(y + contrib);
+        }
+        const int ps = m.row_prob_shared[r];
+        const float sh = bf16_f32(m.yd[ps * pstride + (size_t)r * d + c]);
+        out[(size_t)r * ldo + c] = bf16_bits(y + sh);
+    }
+}
+
+}  // namespace apus
+
+using namespace apus;
+
+int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
+                       const int32_t *forced, cudaStream_t st) {
+    if (R < 1 || R > m.max_r || R > MOE_MAX_R) return -1;
+    // 1. router logits (fp32, no rounding)
+    GemvDesc r{};
+    r.W = m.gate_w; r.x = x; r.ldx = ldx; r.R = R; r.O = m.E; r.K = m.dim; r.fp8 = 0;
+    r.yf = m.logits; r.ldyf = m.E;
+    r.pdl = m.pdl;
+    if (gemv_launch(r, st)) return -1;
+    // 2. routing + work list
+    k_moe_route<<<1, 256, 0, st>>>(m, R, m.logits, forced);
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    // 3. gate|up of every active expert
+    GemvDesc gu{};
+    gu.W = m.gu_codes; gu.WS = m.gu_scales; gu.nkb = (m.dim + 127) / 128;
+    gu.x = x; gu.ldx = ldx; gu.R = R; gu.O = 2L * m.inter; gu.K = m.dim; gu.fp8 = 1;
+    gu.y = m.gu; gu.ldy = 2L * m.inter;
+    gu.gexpert = m.prob_expert; gu.gcount = m.prob_count; gu.gmax = R * m.topk + 1;
+    gu.w_estride = 2L * m.inter * m.dim;
+    gu.s_estride = (2L * m.inter / 128) * ((m.dim + 127) / 128);
+    gu.x_pstride = 0;
+    gu.y_pstride = (long)m.max_r * 2 * m.inter;
+    gu.pdl = m.pdl;
+    if (gemv_launch(gu, st)) return -1;
+    // 4. down with the SwiGLU applied while staging
+    GemvDesc dn{};
+    dn.W = m.d_codes; dn.WS = m.d_scales; dn.nkb = (m.inter + 127) / 128;
+    dn.x = m.gu; dn.ldx = 2L * m.inter; dn.R = R; dn.O = m.dim; dn.K = m.inter; dn.fp8 = 1;
+    dn.y = m.yd; dn.ldy = m.dim;
+    dn.gexpert = m.prob_expert; dn.gcount = m.prob_count; dn.gmax = R * m.topk + 1;
+    dn.w_estride = (long)m.dim * m.inter;
+    dn.s_estride = ((m.dim + 127) / 128) * ((m.inter + 127) / 128);
+    dn.x_pstride = (long)m.max_r * 2 * m.inter;
+    dn.y_pstride = (long)m.max_r * m.dim;
+    dn.x_swiglu = 1;
+    dn.swiglu_limit = m.limit;
+    dn.pdl = m.pdl;
+    if (gemv_launch(dn, st)) return -1;
+    // 5. ordered combine
+    const long n = (long)R * m.dim;
+    k_moe_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(m, R, out, ldo);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}

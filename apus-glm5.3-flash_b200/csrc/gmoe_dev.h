@@ -1,0 +1,37 @@
+// gmoe_dev.h — device-side MoE sublayer descriptor (internal).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define MOE_MAX_R 8
+#define MOE_MAX_E 512
+#define MOE_MAX_TOPK 16
+
+// All pointers are device memory.  Weights: see gmoe.cu for the packed layout.
+struct MoeDev {
+    int E, topk, dim, inter, max_r, pdl;
+    float route_scale, limit;
+    const uint16_t *gate_w;      // [E][dim] BF16 router
+    const float *gate_bias;      // [E] f32 (selection-only bias)
+    const uint8_t *gu_codes;     // [E+1][2*inter][dim] E4M3 (expert E = shared)
+    const float *gu_scales;      // [E+1][2*inter/128][ceil(dim/128)]
+    const uint8_t *d_codes;      // [E+1][dim][inter]
+    const float *d_scales;       // [E+1][ceil(dim/128)][ceil(inter/128)]
+    // per-call scratch
+    float *logits;               // [max_r][E]
+    int32_t *row_expert;         // [max_r][topk] selected experts, ascending
+    float *row_weight;           // [max_r][topk] weights in that order
+    int32_t *row_sel;            // [max_r][topk] selection in top-k order
+    int32_t *row_prob;           // [max_r][topk] problem slot of each selection
+    int32_t *row_prob_shared;    // [max_r] problem slot of the shared expert
+    int32_t *prob_expert;        // [max_r*topk+1] expert of each problem slot
+    int32_t *prob_count;         // [1]
+    uint16_t *gu;                // [max_r*topk+1][max_r][2*inter]
+    uint16_t *yd;                // [max_r*topk+1][max_r][dim]
+};
+
+// x [R][ldx] BF16 device rows -> out [R][ldo] BF16.  forced: optional device
+// [R][topk] selections replacing the computed top-k (the reference's
+// teacher-forcing hook, c/gmoe.h:145-152).
+int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
+                       const int32_t *forced, cudaStream_t st);

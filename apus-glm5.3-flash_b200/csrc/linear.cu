@@ -47,13 +47,17 @@ __global__ void k_fp8_dequant(const uint8_t *__restrict__ w, const float *__rest
 }
 
 // ---------------------------------------------------------------------------
-// Staged GEMV (persistent).  Work item = (tile of 16 weight rows, k-range).
+// Staged GEMV (persistent).  Work item = (problem, tile of 16 weight rows,
+// k-range).  A single GEMV is one problem; grouped mode (MoE experts) runs a
+// device-side table of problems whose size the previous kernel decided.
 // K is cut into ranges of KX elements (a rule of K alone, so the summation
-// order never depends on the activation row count R); a CTA keeps one
-// k-range for its whole life and stages that slice of the activations in
-// shared memory once (up to 4 rows; more rows are read through L1).
-// Warp 8 is the producer: lane 0 streams each tile's k-range through a ring
-// of NSTAGE stages with 1-D bulk copies (one per row per 2 KiB chunk,
+// order never depends on the activation row count R); in single mode a CTA
+// keeps one k-range for its whole life and stages that slice of the
+// activations in shared memory once; in grouped mode each CTA walks a
+// contiguous run of (problem, tile) items and restages when the problem's
+// activations change.
+// Warp 8 is the producer: lanes 0..15 stream each item's k-range through a
+// ring of NSTAGE stages with 1-D bulk copies (one per row per 2 KiB chunk,
 // completion counted on the stage's "full" mbarrier).  Warps 0-7 consume:
 // each takes a fixed slice of the 64-byte k-steps of every chunk.  The
 // weight rows are the 16-row A operand of mma.m16n8k16 (lane (g,t) holds rows
@@ -84,11 +88,11 @@ APUS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Epilogue of one finished (x row m, weight row `row`) dot product; the 16
 // threads of an x row are consecutive lanes (one half-warp).
-APUS_DEV void gemv_store(const GemvDesc &d, int m, long row, float a, unsigned long long *best_sh,
-                         bool lead) {
+APUS_DEV void gemv_store(const GemvDesc &d, uint16_t *y, int m, long row, float a,
+                         unsigned long long *best_sh, bool lead) {
     const bool ok = (m < d.R) && (row < d.O);
     if (ok) {
-        if (d.y) d.y[(size_t)m * d.ldy + row] = bf16_bits(a);
+        if (y) y[(size_t)m * d.ldy + row] = bf16_bits(a);
         if (d.yf) d.yf[(size_t)m * d.ldyf + row] = a;
     }
     if (d.amax) {
@@ -101,6 +105,35 @@ APUS_DEV void gemv_store(const GemvDesc &d, int m, long row, float a, unsigned l
         if (lead && k > best_sh[m]) best_sh[m] = k;
     }
 }
+
+// Work-item enumeration shared by the producer and the consumers.
+struct GemvItems {
+    long ntile, first, step, end;   // single: t = first + j*step < end; grouped: i in [first, end)
+    int nks, ks;
+    bool grouped;
+    APUS_DEV void init(const GemvDesc &d, int count) {
+        ntile = (d.O + gemvcfg::TR - 1) / gemvcfg::TR;
+        grouped = d.gexpert != nullptr;
+        if (grouped) {
+            nks = 1;
+            ks = 0;
+            const long total = (long)count * ntile;
+            first = total * blockIdx.x / gridDim.x;
+            end = total * (blockIdx.x + 1) / gridDim.x;
+            step = 1;
+        } else {
+            nks = (int)((d.K + gemvcfg::KX - 1) / gemvcfg::KX);
+            ks = (int)(blockIdx.x % nks);
+            first = blockIdx.x / nks;
+            step = gridDim.x / nks;
+            end = ntile;
+        }
+    }
+    APUS_DEV void at(long i, int &p, long &t) const {
+        if (grouped) { p = (int)(i / ntile); t = i % ntile; }
+        else { p = 0; t = i; }
+    }
+};
 
 template <bool FP8, bool XS>
 __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
@@ -116,14 +149,6 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long rowbytes = FP8 ? d.K : 2 * d.K;
-    const long ntile = (d.O + TR - 1) / TR;
-    const int nks = (int)((d.K + KX - 1) / KX);
-    const int ks = (int)(blockIdx.x % nks);
-    const long t_first = blockIdx.x / nks, t_step = gridDim.x / nks;
-    const long k0 = ks * KX, klen = min(KX, d.K - k0);          // elements
-    const long kb0 = FP8 ? k0 : 2 * k0, kbytes = FP8 ? klen : 2 * klen;
-    const int nch = (int)((kbytes + CH - 1) / CH);
-    const long xstride = klen + 8;                               // elements
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 8); }
@@ -140,10 +165,20 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
         // the per-instruction issue cost of the bulk copies is paid in parallel.
         // Weights never depend on the previous kernel, so the stream starts
         // before the dependency wait unless the caller says otherwise.
-        if (d.weights_after_wait) pdl_wait();
+        if (d.weights_after_wait || d.gexpert) pdl_wait();
+        GemvItems it;
+        it.init(d, d.gexpert ? min(*d.gcount, d.gmax) : 1);
+        const long k0 = it.ks * KX, klen = min(KX, d.K - k0);
+        const long kb0 = FP8 ? k0 : 2 * k0, kbytes = FP8 ? klen : 2 * klen;
+        const int nch = (int)((kbytes + CH - 1) / CH);
         long c = 0;
         bool ok = true;
-        for (long t = t_first; t < ntile && ok; t += t_step) {
+        for (long i = it.first; i < it.end && ok; i += it.step) {
+            int p;
+            long t;
+            it.at(i, p, t);
+            const uint8_t *W = (const uint8_t *)d.W;
+            if (it.grouped) W += (size_t)d.gexpert[p] * d.w_estride;
             const long row0 = t * TR;
             for (int ch = 0; ch < nch; ch++, c++) {
                 const int s = (int)(c % NSTAGE);
@@ -161,8 +196,8 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
                 if (!ok) break;
                 if (lane < TR) {
                     const long row = min(row0 + lane, d.O - 1);
-                    bulk_g2s(ring + s * STAGE_BYTES + lane * RS,
-                             (const uint8_t *)d.W + row * rowbytes + kb0 + off, len, &full[s]);
+                    bulk_g2s(ring + s * STAGE_BYTES + lane * RS, W + row * rowbytes + kb0 + off, len,
+                             &full[s]);
                 }
             }
         }
@@ -171,30 +206,76 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
 
     // ---------------- consumers: activations come from the previous kernel
     pdl_wait();
-    if (XS) {   // stage x[:, k0:k0+klen]: row r at xs + r*xstride
-        const int per_row = (int)(klen / 8), total = d.R * per_row;   // <= 8 per thread
-        uint4 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int i = threadIdx.x + u * 256;
-            if (i < total) v[u] = ld_nc16(d.x + (size_t)(i / per_row) * d.ldx + k0 + (i % per_row) * 8);
-        }
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int i = threadIdx.x + u * 256;
-            if (i < total) *(uint4 *)(xs + (i / per_row) * xstride + (i % per_row) * 8) = v[u];
-        }
-        named_bar_sync(1, 256);
-    }
+    GemvItems it;
+    it.init(d, d.gexpert ? min(*d.gcount, d.gmax) : 1);
+    const long k0 = it.ks * KX, klen = min(KX, d.K - k0);          // elements
+    const long kb0 = FP8 ? k0 : 2 * k0, kbytes = FP8 ? klen : 2 * klen;
+    const int nch = (int)((kbytes + CH - 1) / CH);
+    const long xstride = klen + 8;                                  // elements
     const int g = lane >> 2, t4 = lane & 3;
     const bool xrow_ok = g < d.R;            // lane supplies B column g
+    const uint16_t *xsrc_staged = nullptr;   // activations currently in smem
     long c = 0;
-    for (long t = t_first; t < ntile; t += t_step) {
+    for (long i = it.first; i < it.end; i += it.step) {
+        int p;
+        long t;
+        it.at(i, p, t);
+        const uint16_t *xsrc = d.x + (size_t)p * d.x_pstride;
+        uint16_t *yout = d.y ? d.y + (size_t)p * d.y_pstride : nullptr;
+        const float *WS = d.WS;
+        if (FP8 && it.grouped) WS += (size_t)d.gexpert[p] * d.s_estride;
+        if (XS && xsrc != xsrc_staged) {   // stage x[:, k0:k0+klen]: row r at xs + r*xstride
+            named_bar_sync(1, 256);          // previous item's readers are done
+            const int per_row = (int)(klen / 8), total = d.R * per_row;   // <= 8 per thread
+            if (!d.x_swiglu) {
+                for (int u0 = 0; u0 < 8; u0 += 4) {    // two batches of 4 loads in flight
+                    uint4 v[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int q = threadIdx.x + (u0 + u) * 256;
+                        if (q < total) v[u] = ld_nc16(xsrc + (size_t)(q / per_row) * d.ldx + k0 + (q % per_row) * 8);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int q = threadIdx.x + (u0 + u) * 256;
+                        if (q < total) *(uint4 *)(xs + (q / per_row) * xstride + (q % per_row) * 8) = v[u];
+                    }
+                }
+            } else {
+                // x row = [g | u] of 2*K values: h = swiglu(g, u), c/gmoe.h:216-224
+                const float lim = d.swiglu_limit;
+                for (int q = threadIdx.x; q < total; q += 256) {
+                    const int r = q / per_row, cc = (q % per_row) * 8;
+                    const uint16_t *xr = xsrc + (size_t)r * d.ldx + k0 + cc;
+                    const uint4 gv = ld_nc16(xr), uv = ld_nc16(xr + d.K);
+                    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        uint16_t hh[2];
+#pragma unroll
+                        for (int hf = 0; hf < 2; hf++) {
+                            float gf = hf ? bf16hi(gw[e]) : bf16lo(gw[e]);
+                            float uf = hf ? bf16hi(uw[e]) : bf16lo(uw[e]);
+                            if (gf > lim) gf = lim;
+                            if (uf > lim) uf = lim;
+                            else if (uf < -lim) uf = -lim;
+                            const float hv = bf16_round(gf * sigmoid_np(gf));
+                            hh[hf] = bf16_bits(hv * uf);
+                        }
+                        o[e] = (uint32_t)hh[0] | ((uint32_t)hh[1] << 16);
+                    }
+                    *(uint4 *)(xs + r * xstride + cc) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            named_bar_sync(1, 256);
+            xsrc_staged = xsrc;
+        }
         const long row0 = t * TR;
         const float *srA = nullptr, *srB = nullptr;
         if (FP8) {   // scale rows of weight rows g and g+8
-            srA = d.WS + (size_t)(min(row0 + g, d.O - 1) >> 7) * d.nkb;
-            srB = d.WS + (size_t)(min(row0 + g + 8, d.O - 1) >> 7) * d.nkb;
+            srA = WS + (size_t)(min(row0 + g, d.O - 1) >> 7) * d.nkb;
+            srB = WS + (size_t)(min(row0 + g + 8, d.O - 1) >> 7) * d.nkb;
         }
         float acc[4][4];
 #pragma unroll
@@ -208,10 +289,10 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
             float scA[MAXS], scB[MAXS];
             if (FP8) {   // scales first: their latency hides under the barrier wait
 #pragma unroll
-                for (int i = 0; i < MAXS; i++) {
-                    const long kbk = (kb0 + off) / 128 + ((s0 + i) >> 1);
-                    scA[i] = (s0 + i < s1) ? __ldg(srA + kbk) : 0.f;
-                    scB[i] = (s0 + i < s1) ? __ldg(srB + kbk) : 0.f;
+                for (int q = 0; q < MAXS; q++) {
+                    const long kbk = (kb0 + off) / 128 + ((s0 + q) >> 1);
+                    scA[q] = (s0 + q < s1) ? __ldg(srA + kbk) : 0.f;
+                    scB[q] = (s0 + q < s1) ? __ldg(srB + kbk) : 0.f;
                 }
             }
             const bool have = mbar_wait(&full[s], (uint32_t)((c / NSTAGE) & 1), &abort_sh,
@@ -220,8 +301,8 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
             const uint8_t *wA = ring + s * STAGE_BYTES + g * RS + 16 * t4;
             const uint8_t *wB = wA + 8 * RS;
 #pragma unroll
-            for (int i = 0; i < MAXS; i++) {
-                const int st = s0 + i;
+            for (int q = 0; q < MAXS; q++) {
+                const int st = s0 + q;
                 if (st >= e1) break;
                 const uint4 va = lds128(wA + st * 64), vb = lds128(wB + st * 64);
                 const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
@@ -234,7 +315,7 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
                             const uint16_t *xp = xs + g * xstride + ls * 64 + 16 * t4;
                             xa = lds128(xp); xb = lds128(xp + 8);
                         } else {
-                            const uint16_t *xp = d.x + (size_t)g * d.ldx + k0 + ls * 64 + 16 * t4;
+                            const uint16_t *xp = xsrc + (size_t)g * d.ldx + k0 + ls * 64 + 16 * t4;
                             xa = ld_nc16(xp); xb = ld_nc16(xp + 8);
                         }
                         xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
@@ -243,8 +324,8 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
                         uint32_t a0, a2, a1, a3;
-                        dequant4(wa[j], scA[i], a0, a2);
-                        dequant4(wb[j], scB[i], a1, a3);
+                        dequant4(wa[j], scA[q], a0, a2);
+                        dequant4(wb[j], scB[q], a1, a3);
                         mma_bf16_16816(acc[j][0], acc[j][1], acc[j][2], acc[j][3],
                                        a0, a1, a2, a3, xw[2 * j], xw[2 * j + 1]);
                     }
@@ -253,13 +334,13 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
                     if (xrow_ok) {
                         uint4 xa;
                         if (XS) xa = lds128(xs + g * xstride + ls * 32 + 8 * t4);
-                        else xa = ld_nc16(d.x + (size_t)g * d.ldx + k0 + ls * 32 + 8 * t4);
+                        else xa = ld_nc16(xsrc + (size_t)g * d.ldx + k0 + ls * 32 + 8 * t4);
                         xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
                     }
 #pragma unroll
                     for (int j = 0; j < 2; j++) {
-                        const int q = (i & 1) * 2 + j;
-                        mma_bf16_16816(acc[q][0], acc[q][1], acc[q][2], acc[q][3],
+                        const int qq = (q & 1) * 2 + j;
+                        mma_bf16_16816(acc[qq][0], acc[qq][1], acc[qq][2], acc[qq][3],
                                        wa[2 * j], wb[2 * j], wa[2 * j + 1], wb[2 * j + 1],
                                        xw[2 * j], xw[2 * j + 1]);
                     }
@@ -284,23 +365,23 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
 #pragma unroll
             for (int w = 1; w < 8; w++) a = a + part[w * PART + tid];
         }
-        if (nks == 1) {
-            if (tid < 128) gemv_store(d, tid >> 4, row0 + (tid & 15), a, best_sh, (tid & 15) == 0);
+        if (it.nks == 1) {
+            if (tid < 128) gemv_store(d, yout, tid >> 4, row0 + (tid & 15), a, best_sh, (tid & 15) == 0);
         } else {
             // publish this range's partial; the last range of the tile reduces
-            float *slot = d.part + ((size_t)t * nks + ks) * PART;
+            float *slot = d.part + ((size_t)t * it.nks + it.ks) * PART;
             if (tid < 128) slot[tid] = a;
             __threadfence();
             named_bar_sync(1, 256);
             if (tid == 0) ticket_sh = atomicAdd(d.ticket + t, 1);
             named_bar_sync(1, 256);
-            if (ticket_sh == nks - 1) {
+            if (ticket_sh == it.nks - 1) {
                 __threadfence();
                 if (tid < 128) {
-                    const float *base = d.part + (size_t)t * nks * PART;
+                    const float *base = d.part + (size_t)t * it.nks * PART;
                     float r = __ldcg(base + tid);
-                    for (int q = 1; q < nks; q++) r = r + __ldcg(base + q * PART + tid);
-                    gemv_store(d, tid >> 4, row0 + (tid & 15), r, best_sh, (tid & 15) == 0);
+                    for (int q = 1; q < it.nks; q++) r = r + __ldcg(base + q * PART + tid);
+                    gemv_store(d, yout, tid >> 4, row0 + (tid & 15), r, best_sh, (tid & 15) == 0);
                 }
                 if (tid == 0) d.ticket[t] = 0;     // ready for the next launch
             }
@@ -398,11 +479,17 @@ static int launch_tma(const GemvDesc &d, cudaStream_t st) {
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     }
     const long ntile = (d.O + gemvcfg::TR - 1) / gemvcfg::TR;
-    const long nks = (d.K + gemvcfg::KX - 1) / gemvcfg::KX;
-    long per_ks = (2L * g_num_sms) / nks;                    // CTAs per k-range
-    if (per_ks < 1) per_ks = 1;
-    if (per_ks > ntile) per_ks = ntile;
-    const long grid = per_ks * nks;
+    long grid;
+    if (d.gexpert) {
+        grid = 2L * g_num_sms;
+        if (grid > (long)d.gmax * ntile) grid = (long)d.gmax * ntile;
+    } else {
+        const long nks = (d.K + gemvcfg::KX - 1) / gemvcfg::KX;
+        long per_ks = (2L * g_num_sms) / nks;                    // CTAs per k-range
+        if (per_ks < 1) per_ks = 1;
+        if (per_ks > ntile) per_ks = ntile;
+        grid = per_ks * nks;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(gemvcfg::THREADS);
@@ -422,6 +509,8 @@ int gemv_launch(const GemvDesc &d, cudaStream_t st) {
         const long klen = d.K < gemvcfg::KX ? d.K : gemvcfg::KX;
         const bool xs = (long)d.R * (klen * 2 + 16) <= gemvcfg::XMAX;
         if (d.K > gemvcfg::KX && (!d.part || !d.ticket)) return -1;
+        if (d.gexpert && (d.K > gemvcfg::KX || !d.gcount || d.gmax < 1)) return -1;
+        if (d.x_swiglu && !xs) return -1;
         int rc;
         if (d.fp8) rc = xs ? launch_tma<true, true>(d, st) : launch_tma<true, false>(d, st);
         else rc = xs ? launch_tma<false, true>(d, st) : launch_tma<false, false>(d, st);

@@ -255,6 +255,155 @@ def cpu_c0(budget_s=10.0):
             "kind": "reference", "sample": f"{n} fp8_linear calls (dequant_mt + bf16_gemm_mt), {dt * 1e3:.2f} ms each"}
 
 
+# --------------------------------------------------------------------------
+# config 1: one MoE verify layer
+C1 = dict(R=4, E=288, topk=8, dim=4096, inter=1024, nx=16)
+
+
+def c1_inputs(seed=1):
+    import numpy as np
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    xs = torch.randn((C1["nx"], C1["R"], C1["dim"]), generator=g).to(torch.bfloat16)
+    return xs.view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def bench_c1(args, ws, rank):
+    """A step = one MoE layer call on 4 rows (router + top-8 of 288 + shared,
+    FP8 experts resident in HBM).  Activations rotate over 16 seeded batches
+    so the routed union changes step to step; the union (~30 experts, ~380 MB)
+    exceeds L2, so every call streams its experts from HBM."""
+    import numpy as np
+    import torch
+    import apus_gcuda as G
+    G.enable()
+    R, d = C1["R"], C1["dim"]
+    h = G.apus_gcuda_moe_new(C1["E"], C1["topk"], d, C1["inter"], 2.5, 10.0, R)
+    assert h, G.apus_gcuda_last_error()
+    G.check(G.apus_gcuda_moe_init_random(h, 1), "init")
+    xs = c1_inputs(1)
+    dx = torch.from_numpy(xs.view(np.int16)).cuda()
+    dy = torch.empty((R, d), dtype=torch.int16, device="cuda")
+    st = torch.cuda.Stream()
+    sp = G.C.c_void_p(st.cuda_stream)
+    # algorithmic bytes per call, from each input batch's realised routing
+    algo = []
+    for i in range(C1["nx"]):
+        G.check(G.apus_gcuda_moe_forward_dev(h, G.ptr(dx[i]), R, G.ptr(dy), None, sp), "moe")
+        st.synchronize()
+        algo.append(G.apus_gcuda_moe_last_bytes(h) + R * d * 4)
+    algo_mean = float(np.mean(algo))
+
+    def step(i):
+        G.check(G.apus_gcuda_moe_forward_dev(h, G.ptr(dx[i % C1["nx"]]), R, G.ptr(dy), None, sp), "moe")
+
+    with torch.cuda.stream(st):
+        for i in range(args.warmup):
+            step(i)
+    st.synchronize()
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        time.sleep(0.3)
+        e0.record(st)
+        for i in range(args.steps):
+            step(i)
+        e1.record(st)
+        st.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), ws)
+    per = ms / args.steps
+    hbm, _, src = peaks()
+    gbs = algo_mean / (per * 1e-3) / 1e9
+    out = {"metric": METRIC, "value": round(1e3 / per * ws, 2), "unit": "MoE layer calls/s (config 1)",
+           "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8e4m3->bf16, f32 acc",
+           "data": "synthetic (BASELINE config 1 distributions, seed 1)",
+           "config": {"workload": "config1: MoE verify layer, 4 rows, 288 experts top-8 + shared, hidden 4096, "
+                                  "inter 1024", "l2": "routed union ~380 MB > L2; 16 rotating input batches",
+                      "parallelism": f"replicas x{ws}"},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": src,
+                        "algo_bytes_per_launch": algo_mean},
+           "gpu_launches": 5 * args.steps, "clocks": clk.summary()}
+    if args.quick:
+        return out
+    # e2e: the host-pointer apus_gmoe_forward2 drop-in
+    yh = np.empty((R, d), np.uint16)
+    for i in range(args.warmup):
+        G.check(G.apus_gcuda_moe_forward2(h, G.ptr(xs[i % C1["nx"]]), R, G.ptr(yh), None), "moe2")
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        G.check(G.apus_gcuda_moe_forward2(h, G.ptr(xs[i % C1["nx"]]), R, G.ptr(yh), None), "moe2")
+    e2e = max_over_ranks((time.perf_counter() - t0) / args.steps, ws)
+    out["e2e"] = {"value": round(ws / e2e, 2), "unit": "MoE layer calls/s through apus_gcuda_moe_forward2",
+                  "h2d_bytes_per_step": R * d * 2, "d2h_bytes_per_step": R * d * 2}
+    out["_moe"] = h
+    return out
+
+
+def cpu_c1(h, budget_s=10.0):
+    """The reference apus_gmoe_forward2 (c/gmoe.h:265-337) on the same weights:
+    the experts routed by the sample batches are read back from HBM and
+    dequantized to BF16 with the reference's apus_fp8blk_dequant_mt, as its
+    engine does at load (c/gmodel.h:1003-1073; not timed)."""
+    import ctypes as C
+    import numpy as np
+    import apus_gcuda as G
+    import oracle as O
+    if O.REF is None:
+        return None
+    R, d, E, inter, K = C1["R"], C1["dim"], C1["E"], C1["inter"], C1["topk"]
+    O._decl(O.REF, "ref_moe_forward", O._i, O._i, O._i, O._sz, O._sz, O._f, O._f, O._vp, O._vp, O._vp, O._vp,
+            O._vp, O._vp, O._vp, O._vp, O._vp, O._sz, O._vp)
+    xs = c1_inputs(1)
+    nb = 2
+    used = set()
+    idx = np.zeros((R, K), np.int32)
+    for i in range(nb):
+        y = np.empty((R, d), np.uint16)
+        G.check(G.apus_gcuda_moe_forward2(h, G.ptr(xs[i]), R, G.ptr(y), None), "moe2")
+        G.check(G.apus_gcuda_moe_last_routing(h, R, O.p(idx), None), "routing")
+        used |= set(idx.ravel().tolist())
+
+    def get(name, shape, dt):
+        a = np.empty(shape, dt)
+        G.check(G.apus_gcuda_moe_get(h, name.encode(), O.p(a), a.nbytes), name)
+        return a
+
+    def deq(name, O_, K_):
+        c = get(name + ".weight", (O_, K_), np.uint8)
+        s = get(name + ".weight_scale_inv", ((O_ + 127) // 128, (K_ + 127) // 128), np.float32)
+        out = np.empty((O_, K_), np.uint16)
+        O.REF.apus_fp8blk_dequant_mt(O.p(c), O.p(s), O.p(out), O_, K_)
+        return out
+
+    gate_w = get("mlp.gate.weight", (E, d), np.uint16)
+    bias = get("mlp.gate.e_score_correction_bias", (E,), np.float32)
+    keep = []
+    PP = C.c_void_p * E
+    eg, eu, ed = PP(), PP(), PP()
+    for e in sorted(used):
+        for arr, p, shp in ((eg, "gate", (inter, d)), (eu, "up", (inter, d)), (ed, "down", (d, inter))):
+            a = deq(f"mlp.experts.{e}.{p}_proj", *shp)
+            keep.append(a)
+            arr[e] = a.ctypes.data
+    sg = deq("mlp.shared_experts.gate_proj", inter, d)
+    su = deq("mlp.shared_experts.up_proj", inter, d)
+    sd = deq("mlp.shared_experts.down_proj", d, inter)
+    out = np.empty((R, d), np.uint16)
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or n < 1:
+        O.REF.ref_moe_forward(E, K, d, inter, 2.5, 10.0, O.p(gate_w), O.p(bias), eg, eu, ed, O.p(sg), O.p(su),
+                              O.p(sd), O.p(xs[n % nb]), R, O.p(out))
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(1.0 / dt, 3), "unit": "MoE layer calls/s", "cores": O.REF.apus_ref_threads(),
+            "kind": "reference",
+            "sample": f"{n} apus_gmoe_forward2 calls (4 rows, 288 experts top-8 + shared, experts pre-dequantized "
+                      f"to BF16 as the reference engine holds them), {dt * 1e3:.1f} ms each"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -284,11 +433,19 @@ def main():
         print(json.dumps(line), flush=True)
         return
     ws, rank, local = dist_init()
-    out = bench_c0(args, ws, rank)
-    if rank == 0:
-        if not args.quick:
-            out["cpu_baseline"] = cpu_c0(budget_s=10.0)
-        print(json.dumps(out), flush=True)
+    if args.config == 1:
+        out = bench_c1(args, ws, rank)
+        h = out.pop("_moe", None)
+        if rank == 0 and not args.quick and h:
+            out["cpu_baseline"] = cpu_c1(h, budget_s=10.0)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    else:
+        out = bench_c0(args, ws, rank)
+        if rank == 0:
+            if not args.quick:
+                out["cpu_baseline"] = cpu_c0(budget_s=10.0)
+            print(json.dumps(out), flush=True)
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -248,7 +248,7 @@ static void expert(Fp8 g, Fp8 u, Fp8 dn, const uint16_t *x, size_t d, size_t int
 
 /* c/gmoe.h:265-337 forward2 (per token, ascending expert, shared last) */
 void orc_moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out,
-                     int32_t *idx_out, float *w_out) {
+                     int32_t *idx_out, float *w_out, const int32_t *forced) {
     const OrcConfig *c = &m->c;
     const OLayer *Ly = &m->L[layer];
     int E = c->n_routed_experts, topk = c->num_experts_per_tok;
@@ -260,6 +260,18 @@ void orc_moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, 
     for (size_t t = 0; t < s; t++) {
         const uint16_t *xt = x + t * d;
         router(m, Ly, xt, idx, wt);
+        if (forced) {   /* c/gmoe.h:287-297: weights re-gathered at the forced indices */
+            float scores_f[64];
+            for (int j = 0; j < topk; j++) {
+                idx[j] = forced[t * topk + j];
+                float acc = 0.0f;
+                for (size_t i = 0; i < d; i++)
+                    acc += orc_bf16_f32(Ly->gate_w[(size_t)idx[j] * d + i]) * orc_bf16_f32(xt[i]);
+                scores_f[j] = orc_sigmoid(acc);
+            }
+            float sum = orc_pw_sum(scores_f, (size_t)topk);
+            for (int j = 0; j < topk; j++) wt[j] = scores_f[j] / (sum + 1e-20f) * c->routed_scaling_factor;
+        }
         if (idx_out) memcpy(idx_out + t * topk, idx, (size_t)topk * 4);
         if (w_out) memcpy(w_out + t * topk, wt, (size_t)topk * 4);
         memset(y, 0, d * 4);
@@ -718,7 +730,7 @@ int orc_decode_batch(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
                     expert(m->L[l].mlp_g, m->L[l].mlp_u, m->L[l].mlp_d, x + t * d, d, inter,
                            c->swiglu_limit, sub + t * d);
             } else {
-                orc_moe_forward(m, l, x, s, sub, NULL, NULL);
+                orc_moe_forward(m, l, x, s, sub, NULL, NULL, NULL);
             }
             for (size_t t = 0; t < s; t++)
                 orc_hc_post(sub + t * d, h + t * hc * d, post + t * hc, comb + t * hc * hc, h2 + t * hc * d, d, hc);
@@ -771,7 +783,7 @@ int orc_mtp_forward(OrcModel *m, OrcMtpState *mst, const int32_t *ids, const uin
     dsa_forward(m, W, xn, s, &mst->dsa, sub);
     for (size_t i = 0; i < s * d; i++) x[i] = orc_bf16_bits(orc_bf16_f32(x[i]) + orc_bf16_f32(sub[i]));
     for (size_t t = 0; t < s; t++) orc_rmsnorm(x + t * d, W->post_norm, xn + t * d, d, eps);
-    orc_moe_forward(m, Lm, xn, s, sub, NULL, NULL);
+    orc_moe_forward(m, Lm, xn, s, sub, NULL, NULL, NULL);
     for (size_t i = 0; i < s * d; i++) x[i] = orc_bf16_bits(orc_bf16_f32(x[i]) + orc_bf16_f32(sub[i]));
     for (size_t t = 0; t < s; t++) orc_rmsnorm(x + t * d, W->shared_norm, out_h + t * d, d, eps);
     gemm(m->head, out_h, logits, s, V, d);

@@ -165,7 +165,7 @@ _decl(ORC, "orc_rmsnorm", None, _vp, _vp, _vp, _sz, _f)
 _decl(ORC, "orc_hc_pre", None, _vp, _i, _i, _vp, _vp, _vp, _vp)
 _decl(ORC, "orc_hc_post", None, _vp, _vp, _vp, _vp, _vp, _sz, _sz)
 _decl(ORC, "orc_hc_head", None, _vp, _vp, _sz, _sz)
-_decl(ORC, "orc_moe_forward", None, _vp, _i, _vp, _sz, _vp, _vp, _vp)
+_decl(ORC, "orc_moe_forward", None, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp)
 _decl(ORC, "orc_kda_decode", None, _vp, _i, _vp, _sz, _vp, _vp, _vp)
 _decl(ORC, "orc_dsa_decode", None, _vp, _i, _vp, _sz, _vp, _vp)
 

@@ -27,6 +27,26 @@
 /* thread count the reference pool will use (c/pool.h APUS_THREADS) */
 int apus_ref_threads(void) { return apus_pool_default_threads(); }
 
+/* The reference MoE sublayer (c/gmoe.h apus_gmoe_forward2) on caller-owned
+ * BF16 (dequantized) expert views; eg/eu/ed are [E] pointer arrays whose
+ * unselected entries are never dereferenced. */
+int ref_moe_forward(int E, int topk, size_t dim, size_t inter, float route_scale, float limit,
+                    const uint16_t *gate_w, const float *gate_bias, const uint16_t *const *eg,
+                    const uint16_t *const *eu, const uint16_t *const *ed, const uint16_t *sg,
+                    const uint16_t *su, const uint16_t *sd, const uint16_t *x, size_t s, uint16_t *out) {
+    ApusGmoeW w;
+    memset(&w, 0, sizeof w);
+    w.router.E = E; w.router.topk = topk; w.router.dim = dim; w.router.route_scale = route_scale;
+    w.router.gate_w = gate_w; w.router.gate_bias = gate_bias;
+    w.inter = inter; w.eg = eg; w.eu = eu; w.ed = ed;
+    w.sg = sg; w.su = su; w.sd = sd; w.sinter = inter; w.limit = limit;
+    ApusGmoeScratch sc;
+    apus_gmoe_scratch_init(&sc, &w, s);
+    apus_gmoe_forward2(&w, x, s, out, NULL, &sc, NULL);
+    apus_gmoe_scratch_free(&sc);
+    return 0;
+}
+
 /* ------------------------------------------------------------------------
  * Building a reference ApusGmodel from caller-owned arrays.  The reference
  * loads weights from its safetensors container (c/gmodel.h:622-1106); the
