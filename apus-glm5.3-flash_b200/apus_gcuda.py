@@ -91,3 +91,163 @@ def stream_of(torch_stream=None):
     import torch
     s = torch_stream if torch_stream is not None else torch.cuda.current_stream()
     return C.c_void_p(s.cuda_stream)
+
+
+# ---- the resident model + speculative step (include/apus_gmtp_gcuda.h) ----
+
+MAX_LAYERS = 64
+_CFG_FIELDS = [
+    ("hidden_size", _i), ("vocab_size", _i), ("num_hidden_layers", _i), ("rms_norm_eps", _f),
+    ("hc_mult", _i), ("hc_sinkhorn_iters", _i), ("hc_eps", _f), ("first_k_dense_replace", _i),
+    ("intermediate_size", _i), ("moe_intermediate_size", _i), ("n_routed_experts", _i),
+    ("n_shared_experts", _i), ("num_experts_per_tok", _i), ("routed_scaling_factor", _f),
+    ("norm_topk_prob", _i), ("swiglu_limit", _f), ("num_attention_heads", _i), ("q_lora_rank", _i),
+    ("kv_lora_rank", _i), ("qk_nope_head_dim", _i), ("v_head_dim", _i), ("index_n_heads", _i),
+    ("index_head_dim", _i), ("index_topk", _i), ("index_kpool", _i), ("index_kpool_always_select_tail", _i),
+    ("linear_num_heads", _i), ("linear_head_dim", _i), ("linear_conv_kernel_dim", _i),
+    ("linear_lower_bound", _f), ("num_nextn_predict_layers", _i),
+    ("layer_is_dsa", _i * MAX_LAYERS), ("mlp_is_sparse", _i * MAX_LAYERS),
+]
+
+
+class GcudaConfig(C.Structure):
+    """ApusGcudaConfig: the field names and meaning of ApusGmodelConfig
+    (c/gmodel.h:88-108) with the per-layer patterns inline."""
+    _fields_ = _CFG_FIELDS
+
+
+def make_config(**kw):
+    c = GcudaConfig()
+    for name, _ in _CFG_FIELDS:
+        if name not in ("layer_is_dsa", "mlp_is_sparse"):
+            setattr(c, name, kw[name])
+    for i in range(kw["num_hidden_layers"]):
+        c.layer_is_dsa[i] = int(kw["layer_is_dsa"][i])
+        c.mlp_is_sparse[i] = int(kw["mlp_is_sparse"][i])
+    return c
+
+
+_cs = C.c_char_p
+apus_gcuda_model_new = _fn("apus_gcuda_model_new", _vp, _vp, _i, _sz, _i)
+apus_gcuda_model_free = _fn("apus_gcuda_model_free", None, _vp)
+apus_gcuda_model_set = _fn("apus_gcuda_model_set", _i, _vp, _cs, _vp, _sz)
+apus_gcuda_model_get = _fn("apus_gcuda_model_get", _i, _vp, _cs, _vp, _sz)
+apus_gcuda_model_init_random = _fn("apus_gcuda_model_init_random", _i, _vp, _u64)
+apus_gcuda_model_reset = _fn("apus_gcuda_model_reset", _i, _vp)
+apus_gcuda_model_pos = _fn("apus_gcuda_model_pos", _sz, _vp)
+apus_gcuda_decode_batch = _fn("apus_gcuda_decode_batch", _i, _vp, _vp, _sz, _vp, _vp, _vp)
+apus_gcuda_mtp_forward = _fn("apus_gcuda_mtp_forward", _i, _vp, _vp, _vp, _sz, _vp, _vp)
+apus_gcuda_gspec_prefill = _fn("apus_gcuda_gspec_prefill", _i, _vp, _vp, _sz)
+apus_gcuda_gspec_step = _fn("apus_gcuda_gspec_step", _i, _vp, _vp, _i)
+apus_gcuda_gspec_step_async = _fn("apus_gcuda_gspec_step_async", _i, _vp)
+apus_gcuda_gspec_emitted = _fn("apus_gcuda_gspec_emitted", _i, _vp, _vp, _sz)
+apus_gcuda_gspec_stats = _fn("apus_gcuda_gspec_stats", _i, _vp, _vp)
+apus_gcuda_gspec_force = _fn("apus_gcuda_gspec_force", _i, _vp, _vp, _sz, _sz, C.c_double, _u64)
+apus_gcuda_greedy = _fn("apus_gcuda_greedy", _i, _vp, _vp, _sz, _i, _vp)
+apus_gcuda_state_digest = _fn("apus_gcuda_state_digest", _u64, _vp)
+apus_gcuda_model_debug_stop = _fn("apus_gcuda_model_debug_stop", _i, _vp, _i, _i)
+apus_gcuda_model_debug_read = _fn("apus_gcuda_model_debug_read", _i, _vp, _cs, _vp, _sz)
+
+
+class GModel:
+    """One resident model + sequence on the current CUDA device (the
+    reference's ApusGmodel/ApusGmodelState/ApusGmtp/ApusGspec bundle,
+    c/gmodel.h:161-320, c/gmtp.h:123-259).  Arrays are numpy (host)."""
+
+    def __init__(self, cfg, has_mtp=True, kv_cap=1024, depth=4):
+        import numpy as np
+        self.np = np
+        enable()
+        self.cfg, self.depth = cfg, depth
+        self.h = apus_gcuda_model_new(C.byref(cfg), int(has_mtp), kv_cap, depth)
+        if not self.h:
+            raise GcudaError(f"model_new: {apus_gcuda_last_error().decode(errors='replace')}")
+
+    def close(self):
+        if self.h:
+            apus_gcuda_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set(self, name, arr):
+        arr = self.np.ascontiguousarray(arr)
+        check(apus_gcuda_model_set(self.h, name.encode(), ptr(arr), arr.nbytes), f"set {name}")
+
+    def load(self, weights):
+        for k, v in weights.items():
+            self.set(k, v)
+
+    def init_random(self, seed):
+        check(apus_gcuda_model_init_random(self.h, seed), "init_random")
+
+    def reset(self):
+        check(apus_gcuda_model_reset(self.h), "reset")
+
+    def pos(self):
+        return apus_gcuda_model_pos(self.h)
+
+    def decode_batch(self, ids, want_h=False):
+        np, cfg = self.np, self.cfg
+        ids = np.ascontiguousarray(ids, np.int32)
+        s = len(ids)
+        logits = np.empty((s, cfg.vocab_size), np.uint16)
+        h = np.empty((s, cfg.hc_mult * cfg.hidden_size), np.uint16)
+        yn = np.empty((s, cfg.hidden_size), np.uint16)
+        check(apus_gcuda_decode_batch(self.h, ptr(ids), s, ptr(logits), ptr(h), ptr(yn)), "decode_batch")
+        return (logits, h, yn) if want_h else logits
+
+    def mtp_forward(self, ids, prev_h):
+        np, cfg = self.np, self.cfg
+        ids = np.ascontiguousarray(ids, np.int32)
+        prev_h = np.ascontiguousarray(prev_h, np.uint16)
+        s = len(ids)
+        logits = np.empty((s, cfg.vocab_size), np.uint16)
+        oh = np.empty((s, cfg.hidden_size), np.uint16)
+        check(apus_gcuda_mtp_forward(self.h, ptr(ids), ptr(prev_h), s, ptr(logits), ptr(oh)), "mtp_forward")
+        return logits, oh
+
+    def spec_prefill(self, ids):
+        ids = self.np.ascontiguousarray(ids, self.np.int32)
+        check(apus_gcuda_gspec_prefill(self.h, ptr(ids), len(ids)), "gspec_prefill")
+
+    def spec_step(self):
+        out = (C.c_int * 16)()
+        n = apus_gcuda_gspec_step(self.h, out, 16)
+        return list(out[:n])
+
+    def spec_step_async(self):
+        check(apus_gcuda_gspec_step_async(self.h), "gspec_step_async")
+
+    def emitted(self, cap=1 << 16):
+        out = self.np.empty(cap, self.np.int32)
+        n = apus_gcuda_gspec_emitted(self.h, ptr(out), cap)
+        if n < 0:
+            raise GcudaError(apus_gcuda_last_error().decode(errors="replace"))
+        return out[:min(n, cap)].tolist()
+
+    def stats(self):
+        o = (C.c_uint64 * 6)()
+        rc = apus_gcuda_gspec_stats(self.h, o)
+        return dict(zip(("emitted", "batches", "offered", "accepted", "pos", "held"), list(o))), rc
+
+    def force(self, truth, base, p=1.0, seed=0):
+        if truth is None:
+            check(apus_gcuda_gspec_force(self.h, None, 0, 0, 0.0, 0), "force off")
+            return
+        t = self.np.ascontiguousarray(truth, self.np.int32)
+        check(apus_gcuda_gspec_force(self.h, ptr(t), len(t), base, float(p), seed), "force")
+
+    def greedy(self, ids, n_gen):
+        np = self.np
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty(n_gen, np.int32)
+        check(apus_gcuda_greedy(self.h, ptr(ids), len(ids), n_gen, ptr(out)), "greedy")
+        return out.tolist()
+
+    def digest(self):
+        return apus_gcuda_state_digest(self.h)

@@ -75,7 +75,7 @@ __global__ void k_moe_route(MoeDev m, int R, const float *logits, const int32_t 
         if (lane == 0) {
             float w[MOE_MAX_TOPK];
             for (int j = 0; j < K; j++) w[j] = sc[r][sel[r][j]];
-            const float sum = pw_sum_small(w, K);
+            const float sum = K ? pw_sum_small(w, K) : 0.f;
             for (int j = 0; j < K; j++) w[j] = w[j] / (sum + 1e-20f) * m.route_scale;
             // the combine walks the row's experts in ascending index order
             int32_t id[MOE_MAX_TOPK];
@@ -127,8 +127,9 @@ __global__ void k_moe_combine(MoeDev m, int R, uint16_t *out, long ldo) {
             y = bf16_round(y + contrib);
         }
         const int ps = m.row_prob_shared[r];
-        const float sh = bf16_f32(m.yd[ps * pstride + (size_t)r * d + c]);
-        out[(size_t)r * ldo + c] = bf16_bits(y + sh);
+        const uint16_t shb = m.yd[ps * pstride + (size_t)r * d + c];
+        // a dense MLP (no routed experts) passes its output through unchanged
+        out[(size_t)r * ldo + c] = K ? bf16_bits(y + bf16_f32(shb)) : shb;
     }
 }
 
@@ -139,12 +140,14 @@ using namespace apus;
 int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
                        const int32_t *forced, cudaStream_t st) {
     if (R < 1 || R > m.max_r || R > MOE_MAX_R) return -1;
-    // 1. router logits (fp32, no rounding)
-    GemvDesc r{};
-    r.W = m.gate_w; r.x = x; r.ldx = ldx; r.R = R; r.O = m.E; r.K = m.dim; r.fp8 = 0;
-    r.yf = m.logits; r.ldyf = m.E;
-    r.pdl = m.pdl;
-    if (gemv_launch(r, st)) return -1;
+    // 1. router logits (fp32, no rounding); a dense MLP has no router
+    if (m.E > 0) {
+        GemvDesc r{};
+        r.W = m.gate_w; r.x = x; r.ldx = ldx; r.R = R; r.O = m.E; r.K = m.dim; r.fp8 = 0;
+        r.yf = m.logits; r.ldyf = m.E;
+        r.pdl = m.pdl;
+        if (gemv_launch(r, st)) return -1;
+    }
     // 2. routing + work list
     k_moe_route<<<1, 256, 0, st>>>(m, R, m.logits, forced);
     if (cudaGetLastError() != cudaSuccess) return -1;

@@ -1,0 +1,677 @@
+// layers.cu — per-layer kernels of the glm5_next decode stack on the B200.
+//
+// Each kernel restates one reference function; rounding points and, where it
+// is cheap, summation orders are kept (numpy pairwise sums for norms, strictly
+// sequential accumulations where the reference is sequential).  Everything is
+// per token row, so a batch of R rows gives every row bitwise the result it
+// gets alone (the verify == sequential decode property); the KDA recurrence
+// and the DSA caches are stepped in row order.
+#include "common.cuh"
+#include "gcuda.h"
+#include "model_dev.h"
+
+namespace apus {
+
+// ---------------------------------------------------------------- helpers
+
+// numpy pairwise sum of a[0..n) held in shared memory by the whole block
+// (thread 0 walks the recursion; fine for the short vectors used here).
+APUS_DEV float pw_sum_shared(const float *a, int n) {
+    // recursion with an explicit stack, leaves via pw_sum_leaf
+    struct Fr { int off, len, state; float left; };
+    Fr st[24];
+    int sp = 0;
+    st[sp++] = {0, n, 0, 0.f};
+    float ret = 0.f;
+    while (sp) {
+        Fr &f = st[sp - 1];
+        if (f.len <= 128) { ret = f.len ? pw_sum_leaf(a + f.off, f.len) : 0.f; sp--; continue; }
+        const int n2 = (f.len / 2) & ~7;
+        if (f.state == 0) { f.state = 1; st[sp++] = {f.off, n2, 0, 0.f}; continue; }
+        if (f.state == 1) { f.left = ret; f.state = 2; st[sp++] = {f.off + n2, f.len - n2, 0, 0.f}; continue; }
+        ret = f.left + ret;
+        sp--;
+    }
+    return ret;
+}
+
+// Block-parallel version: leaves of <= 128 summed by separate threads, the
+// combine tree walked by thread 0.  Bitwise equal to pw_sum_shared.
+APUS_DEV float block_pw(const float *a, int n, float *leaf_buf, float *out_sh) {
+    // leaf k covers the k-th <=128 piece in left-to-right order of the recursion
+    __shared__ int leaf_off[256], leaf_len[256], nleaf;
+    if (threadIdx.x == 0) {
+        int so[24], sl[24], sp = 0, nl = 0;
+        so[sp] = 0; sl[sp] = n; sp++;
+        while (sp) {
+            sp--;
+            const int off = so[sp], len = sl[sp];
+            if (len <= 128) { leaf_off[nl] = off; leaf_len[nl] = len; nl++; continue; }
+            const int n2 = (len / 2) & ~7;
+            so[sp] = off + n2; sl[sp] = len - n2; sp++;
+            so[sp] = off; sl[sp] = n2; sp++;
+        }
+        nleaf = nl;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nleaf; i += blockDim.x)
+        leaf_buf[i] = leaf_len[i] ? pw_sum_leaf(a + leaf_off[i], leaf_len[i]) : 0.f;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        struct Fr { int len, state; float left; };
+        Fr st[24];
+        int sp = 0, cur = 0;
+        st[sp++] = {n, 0, 0.f};
+        float ret = 0.f;
+        while (sp) {
+            Fr &f = st[sp - 1];
+            if (f.len <= 128) { ret = leaf_buf[cur++]; sp--; continue; }
+            const int n2 = (f.len / 2) & ~7;
+            if (f.state == 0) { f.state = 1; st[sp++] = {n2, 0, 0.f}; continue; }
+            if (f.state == 1) { f.left = ret; f.state = 2; st[sp++] = {f.len - n2, 0, 0.f}; continue; }
+            ret = f.left + ret;
+            sp--;
+        }
+        *out_sh = ret;
+    }
+    __syncthreads();
+    const float r = *out_sh;
+    __syncthreads();
+    return r;
+}
+
+// Weighted RMSNorm of one row held as fp32 in smem (c/gdsa.h:258-274):
+// var = pairwise mean of squares; t = bf16(x * (1/sqrt(var+eps))); y = bf16(w*t).
+APUS_DEV void rmsnorm_row_smem(float *xs, float *sq, int n, const uint16_t *w, float eps, uint16_t *y,
+                               float *leaf, float *res) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) sq[i] = xs[i] * xs[i];
+    __syncthreads();
+    const float var = block_pw(sq, n, leaf, res) / (float)n;
+    const float inv = 1.0f / sqrtf(var + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float t = bf16_round(xs[i] * inv);
+        y[i] = bf16_bits(bf16_f32(w[i]) * t);
+    }
+}
+
+// ------------------------------------------------------------------ embed
+
+__global__ void k_embed(const uint16_t *embed, const int32_t *ids, int d, int hc, uint16_t *h4) {
+    const int r = blockIdx.y;
+    const uint16_t *row = embed + (size_t)ids[r] * d;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x) {
+        const uint16_t v = row[i];
+        for (int j = 0; j < hc; j++) h4[((size_t)r * hc + j) * d + i] = v;
+    }
+}
+
+// --------------------------------------------------------------------- mHC
+
+// inverse RMS of the flattened streams (c/gmhc.h:187-195): one CTA per row
+__global__ void k_hc_rms(const uint16_t *h4, int n, float eps, float *rms) {
+    extern __shared__ float sq[];
+    __shared__ float leaf[256], res;
+    const uint16_t *x = h4 + (size_t)blockIdx.x * n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = bf16_f32(x[i]);
+        sq[i] = v * v;
+    }
+    __syncthreads();
+    const float var = block_pw(sq, n, leaf, &res) / (float)n;
+    if (threadIdx.x == 0) rms[blockIdx.x] = 1.0f / sqrtf(var + eps);
+}
+
+// mixes[r][j] = sum_i fn[j][i] * (x4[r][i] * inv[r])  (c/gmhc.h:248-258),
+// fp32, fixed per-thread strides + fixed tree: one CTA per (j, r).
+__global__ void k_hc_mix(const uint16_t *fn, const uint16_t *h4, const float *rms, int n, int nmix,
+                         float *mix) {
+    const int j = blockIdx.x, r = blockIdx.y;
+    const float inv = rms[r];
+    const uint16_t *f = fn + (size_t)j * n, *x = h4 + (size_t)r * n;
+    float acc = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) acc += bf16_f32(f[i]) * (bf16_f32(x[i]) * inv);
+    __shared__ float red[256];
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s; s >>= 1) {
+        if ((int)threadIdx.x < s) red[threadIdx.x] = red[threadIdx.x] + red[threadIdx.x + s];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) mix[(size_t)r * nmix + j] = red[0];
+}
+
+// gates + Sinkhorn (c/gmhc.h:197-265), collapse (:267-276) and the layer's
+// weighted RMSNorm (c/gdsa.h:258-274): one CTA per row.
+__global__ void k_hc_maps(const uint16_t *h4, const float *mix, const float *scale, const float *base,
+                          const uint16_t *norm_w, int d, int hc, int iters, float hc_eps, float eps,
+                          float *post_out, float *comb_out, uint16_t *x_out) {
+    extern __shared__ float ys[];           // [d] collapsed + [d] squares
+    float *sq = ys + d;
+    __shared__ float pre[8], post[8], comb[64], leaf[256], res;
+    const int r = blockIdx.x, nmix = (2 + hc) * hc;
+    const float *m = mix + (size_t)r * nmix;
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < hc; j++) pre[j] = sigmoid_np(m[j] * scale[0] + base[j]) + hc_eps;
+        for (int j = 0; j < hc; j++) post[j] = 2.0f * sigmoid_np(m[hc + j] * scale[1] + base[hc + j]);
+        for (int j = 0; j < hc; j++)
+            for (int k = 0; k < hc; k++) {
+                const int idx = 2 * hc + j * hc + k;
+                comb[j * hc + k] = m[idx] * scale[2] + base[idx];
+            }
+        for (int j = 0; j < hc; j++) {      // row softmax + eps
+            float *rr = comb + j * hc, mx = rr[0];
+            for (int k = 1; k < hc; k++) if (rr[k] > mx) mx = rr[k];
+            for (int k = 0; k < hc; k++) rr[k] = expf(rr[k] - mx);
+            const float sum = pw_sum_leaf(rr, hc);
+            for (int k = 0; k < hc; k++) rr[k] = rr[k] / sum + hc_eps;
+        }
+        for (int it = 0; it < iters; it++) {
+            if (it)
+                for (int j = 0; j < hc; j++) {
+                    float *rr = comb + j * hc;
+                    const float den = pw_sum_leaf(rr, hc) + hc_eps;
+                    for (int k = 0; k < hc; k++) rr[k] /= den;
+                }
+            for (int k = 0; k < hc; k++) {
+                float sum = comb[k];
+                for (int j = 1; j < hc; j++) sum += comb[j * hc + k];
+                const float den = sum + hc_eps;
+                for (int j = 0; j < hc; j++) comb[j * hc + k] /= den;
+            }
+        }
+        for (int j = 0; j < hc; j++) post_out[r * hc + j] = post[j];
+        for (int j = 0; j < hc * hc; j++) comb_out[r * hc * hc + j] = comb[j];
+    }
+    __syncthreads();
+    const uint16_t *x4 = h4 + (size_t)r * hc * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        float acc = pre[0] * bf16_f32(x4[i]);
+        for (int j = 1; j < hc; j++) acc += pre[j] * bf16_f32(x4[(size_t)j * d + i]);
+        ys[i] = bf16_round(acc);
+    }
+    __syncthreads();
+    rmsnorm_row_smem(ys, sq, d, norm_w, eps, x_out + (size_t)r * d, leaf, &res);
+}
+
+// expand (c/gmhc.h:278-294): y[j][i] = bf16(bf16(bf16(post[j]) x[i]) +
+// bf16(sum_k bf16(comb[k][j]) res[k][i]))
+__global__ void k_hc_post(const uint16_t *x, const uint16_t *h4, const float *post, const float *comb,
+                          int d, int hc, uint16_t *out) {
+    const int r = blockIdx.y;
+    for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < hc * d; q += gridDim.x * blockDim.x) {
+        const int j = q / d, i = q % d;
+        const float pb = bf16_round(post[r * hc + j]);
+        const float t1 = bf16_round(pb * bf16_f32(x[(size_t)r * d + i]));
+        float acc = 0.f;
+        for (int k = 0; k < hc; k++)
+            acc += bf16_round(comb[r * hc * hc + k * hc + j]) * bf16_f32(h4[((size_t)r * hc + k) * d + i]);
+        out[((size_t)r * hc + j) * d + i] = bf16_bits(t1 + bf16_round(acc));
+    }
+}
+
+// HyperHead mean (c/gmhc.h:296-304) + final RMSNorm
+__global__ void k_head_norm(const uint16_t *h4, const uint16_t *w, int d, int hc, float eps, uint16_t *yn) {
+    extern __shared__ float ys[];
+    float *sq = ys + d;
+    __shared__ float leaf[256], res;
+    const int r = blockIdx.x;
+    const uint16_t *x4 = h4 + (size_t)r * hc * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        float acc = bf16_f32(x4[i]);
+        for (int j = 1; j < hc; j++) acc += bf16_f32(x4[(size_t)j * d + i]);
+        ys[i] = bf16_round(acc / (float)hc);
+    }
+    __syncthreads();
+    rmsnorm_row_smem(ys, sq, d, w, eps, yn + (size_t)r * d, leaf, &res);
+}
+
+__global__ void k_rmsnorm_rows(const uint16_t *x, long ldx, const uint16_t *w, int n, float eps, uint16_t *y,
+                               long ldy) {
+    extern __shared__ float ys[];
+    float *sq = ys + n;
+    __shared__ float leaf[256], res;
+    const int r = blockIdx.x;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ys[i] = bf16_f32(x[(size_t)r * ldx + i]);
+    __syncthreads();
+    rmsnorm_row_smem(ys, sq, n, w, eps, y + (size_t)r * ldy, leaf, &res);
+}
+
+__global__ void k_residual_add(uint16_t *x, const uint16_t *sub, long n) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        x[i] = bf16_bits(bf16_f32(x[i]) + bf16_f32(sub[i]));
+}
+
+// --------------------------------------------------------------------- KDA
+
+// depthwise causal conv k=K + SiLU over the q|k|v channels, tokens chained
+// (c/gkda.h:227-257).  The conv state after token t goes to checkpoint slot
+// (cur+1+t) % NSLOT; the committed slot is never written.
+__global__ void k_kda_conv(const uint16_t *kp, long ldkp, const uint16_t *conv_w, uint16_t *conv_slots,
+                           const Ctl *ctl, int R, int C, int K, uint16_t *out) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    const int cur = ctl->kda_cur;
+    const size_t slot = (size_t)C * (K - 1);
+    uint16_t st[8];
+    for (int j = 0; j < K - 1; j++) st[j] = conv_slots[cur * slot + (size_t)c * (K - 1) + j];
+    const uint16_t *wc = conv_w + (size_t)c * K;
+    for (int t = 0; t < R; t++) {
+        const uint16_t xc = kp[(size_t)t * ldkp + c];
+        float acc = 0.f;
+        for (int i = 0; i < K - 1; i++) acc += bf16_f32(wc[i]) * bf16_f32(st[i]);
+        acc += bf16_f32(wc[K - 1]) * bf16_f32(xc);
+        out[(size_t)t * C + c] = bf16_bits(acc * sigmoid_np(acc));
+        for (int j = 0; j + 1 < K - 1; j++) st[j] = st[j + 1];
+        st[K - 2] = xc;
+        const int s = (cur + 1 + t) % NSLOT;
+        for (int j = 0; j < K - 1; j++) conv_slots[s * slot + (size_t)c * (K - 1) + j] = st[j];
+    }
+}
+
+// The delta-rule recurrence of one head over R chained tokens
+// (c/gkda.h:279-346) fused with the forget gate (:629-643), beta (:644-647)
+// and the gated o_norm (:543-569).  128 threads; thread j owns column j of the
+// fp32 state S[i][j] (128 registers), so kv[j] = sum_i S[i][j] k[i] and
+// o[j] = sum_i S[i][j] q[i] run in the reference's sequential i order.
+template <int D>
+__global__ void __launch_bounds__(D) k_kda_rec(const uint16_t *qkvc, const uint16_t *kp, long ldkp, int beta_off,
+                                               const uint16_t *fgo, long fg_pstride, const float *A_log,
+                                               const float *dt_bias, const uint16_t *o_norm, float *rec_slots,
+                                               const Ctl *ctl, int R, int H, float lower_bound, float eps,
+                                               float qscale, uint16_t *core_out) {
+    const int h = blockIdx.x, j = threadIdx.x, qkv = H * D;
+    __shared__ float qf[D], kf[D], dec[D], sq[D], red[2];
+    float S[D];
+    const int cur = ctl->kda_cur;
+    const size_t hs = (size_t)D * D;
+    const float *S0 = rec_slots + (size_t)cur * H * hs + (size_t)h * hs;
+#pragma unroll
+    for (int i = 0; i < D; i++) S[i] = S0[(size_t)i * D + j];
+    const float a = expf(A_log[h]);
+    for (int t = 0; t < R; t++) {
+        const uint16_t *q = qkvc + (size_t)t * 3 * qkv + (size_t)h * D;
+        const uint16_t *k = q + qkv, *v = q + 2 * qkv;
+        // l2norm q, k (c/gkda.h:263-273), pairwise sums of squares
+        const float qv = bf16_f32(q[j]), kv_ = bf16_f32(k[j]);
+        sq[j] = qv * qv;
+        __syncthreads();
+        if (j == 0) red[0] = sqrtf(pw_sum_leaf(sq, D) + 1e-6f);
+        __syncthreads();
+        sq[j] = kv_ * kv_;
+        __syncthreads();
+        if (j == 0) red[1] = sqrtf(pw_sum_leaf(sq, D) + 1e-6f);
+        __syncthreads();
+        qf[j] = (qv / red[0]) * qscale;
+        kf[j] = kv_ / red[1];
+        // forget gate: g = lb * sigmoid(exp(A_log) * (fg + dt_bias)); decay exp(g)
+        const float z = bf16_f32(fgo[(size_t)t * qkv + (size_t)h * D + j]) + dt_bias[(size_t)h * D + j];
+        dec[j] = expf(lower_bound * sigmoid_np(a * z));
+        const float beta = bf16_round(sigmoid_np(bf16_f32(kp[(size_t)t * ldkp + beta_off + h])));
+        const float vj = bf16_f32(v[j]);
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < D; i++) S[i] = S[i] * dec[i];
+        float kvm = 0.f;
+#pragma unroll
+        for (int i = 0; i < D; i++) kvm += S[i] * kf[i];
+        const float dl = (vj - kvm) * beta;
+#pragma unroll
+        for (int i = 0; i < D; i++) S[i] = S[i] + kf[i] * dl;
+        float o = 0.f;
+#pragma unroll
+        for (int i = 0; i < D; i++) o += S[i] * qf[i];
+        const float core = bf16_round(o);
+        // checkpoint the state after this token
+        float *Sd = rec_slots + (size_t)((cur + 1 + t) % NSLOT) * H * hs + (size_t)h * hs;
+#pragma unroll
+        for (int i = 0; i < D; i++) Sd[(size_t)i * D + j] = S[i];
+        // gated o_norm, eps = rms_norm_eps
+        __syncthreads();
+        sq[j] = core * core;
+        __syncthreads();
+        if (j == 0) red[0] = 1.0f / sqrtf(pw_sum_leaf(sq, D) / (float)D + eps);
+        __syncthreads();
+        float y = core * red[0];
+        y = bf16_f32(o_norm[j]) * y;
+        y = y * sigmoid_np(bf16_f32(fgo[fg_pstride + (size_t)t * qkv + (size_t)h * D + j]));
+        core_out[(size_t)t * qkv + (size_t)h * D + j] = bf16_bits(y);
+        __syncthreads();
+    }
+}
+
+// --------------------------------------------------------------------- DSA
+
+// Append this call's rows to the caches at base+t (c/gdsa.h:612-626 for K/V,
+// :329-334 for the indexer key LayerNorm and compress gate).
+__global__ void k_dsa_append(const uint16_t *kvb, const uint16_t *ikgw, const uint16_t *knw, const uint16_t *knb,
+                             const int *base_n, int AH, int qd, int vd, int ID, int IH, int cap, DsaState ds) {
+    const int t = blockIdx.x;
+    const int pos = *base_n + t;
+    if (pos >= cap) return;
+    const uint16_t *row = kvb + (size_t)t * AH * (qd + vd);
+    for (int q = threadIdx.x; q < AH * (qd + vd); q += blockDim.x) {
+        const int h = q / (qd + vd), e = q % (qd + vd);
+        if (e < qd) ds.k[((size_t)h * cap + pos) * qd + e] = row[q];
+        else ds.v[((size_t)h * cap + pos) * vd + (e - qd)] = row[q];
+    }
+    // LayerNorm of the indexer key (c/gdsa.h:276-305, eps 1e-6)
+    __shared__ float xs[256], d2[256], leaf[256], res;
+    const uint16_t *ir = ikgw + (size_t)t * (2 * ID + IH);
+    for (int i = threadIdx.x; i < ID; i += blockDim.x) xs[i] = bf16_f32(ir[i]);
+    __syncthreads();
+    const float mu = block_pw(xs, ID, leaf, &res) / (float)ID;
+    for (int i = threadIdx.x; i < ID; i += blockDim.x) { const float dd = xs[i] - mu; d2[i] = dd * dd; }
+    __syncthreads();
+    const float var = block_pw(d2, ID, leaf, &res) / (float)ID;
+    const float inv = 1.0f / sqrtf(var + 1e-6f);
+    for (int i = threadIdx.x; i < ID; i += blockDim.x) {
+        float v = (xs[i] - mu) * inv;
+        v = v * bf16_f32(knw[i]) + bf16_f32(knb[i]);
+        ds.ik[(size_t)pos * ID + i] = bf16_bits(v);
+        ds.ig[(size_t)pos * ID + i] = ir[ID + i];
+    }
+}
+
+// Pool keys of the pools completed by this call (c/gdsa.h:344-372): the
+// softmax(gate + ape) over the kpool members, probs cast to BF16, weighted
+// average rounded to BF16.  A completed pool never changes, so it is
+// computed once when its last member is appended.
+__global__ void k_dsa_pool(const uint16_t *ape, const int *base_n, int R, int ID, int kp, int cap, DsaState ds) {
+    const int base = *base_n;
+    const int t = blockIdx.x, pos = base + t;
+    if (pos >= cap || (pos % kp) != kp - 1) return;
+    const int p = pos / kp;
+    for (int dd = threadIdx.x; dd < ID; dd += blockDim.x) {
+        float lg[16], e[16];
+        for (int c = 0; c < kp; c++)
+            lg[c] = bf16_f32(ds.ig[(size_t)(p * kp + c) * ID + dd]) + bf16_f32(ape[c * ID + dd]);
+        float mx = lg[0];
+        for (int c = 1; c < kp; c++) if (lg[c] > mx) mx = lg[c];
+        float sum = 0.f;
+        for (int c = 0; c < kp; c++) { e[c] = expf(lg[c] - mx); sum += e[c]; }
+        float acc = 0.f;
+        for (int c = 0; c < kp; c++) acc += bf16_round(e[c] / sum) * bf16_f32(ds.ik[(size_t)(p * kp + c) * ID + dd]);
+        ds.pkey[(size_t)p * ID + dd] = bf16_bits(acc);
+    }
+}
+
+// Indexer scores (c/gdsa.h:376-403) for every pool visible to row t:
+// sc = sum_h w_h * relu((idx_q[h] . key[p]) * ID^-0.5), w_h = bf16(wproj x) * IH^-0.5
+__global__ void k_dsa_score(const uint16_t *iq, const uint16_t *ikgw, const int *base_n, int IH, int ID, int kp,
+                            int maxpools, DsaState ds, float *score) {
+    const int t = blockIdx.y;
+    const int qpos = *base_n + t;
+    const int nvalid = (qpos + 1) / kp;
+    const float idx_scale = (float)(1.0 / sqrt((double)ID)), ih_scale = (float)(1.0 / sqrt((double)IH));
+    __shared__ float qs[32 * 128 + 32];
+    for (int i = threadIdx.x; i < IH * ID; i += blockDim.x) qs[i] = bf16_f32(iq[(size_t)t * IH * ID + i]);
+    for (int h = threadIdx.x; h < IH; h += blockDim.x)
+        qs[IH * ID + h] = bf16_f32(ikgw[(size_t)t * (2 * ID + IH) + 2 * ID + h]) * ih_scale;
+    __syncthreads();
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < nvalid && p < maxpools; p += gridDim.x * blockDim.x) {
+        const uint16_t *key = ds.pkey + (size_t)p * ID;
+        float acc = 0.f;
+        for (int h = 0; h < IH; h++) {
+            float dot = 0.f;
+            for (int i = 0; i < ID; i++) dot += qs[h * ID + i] * bf16_f32(key[i]);
+            const float v = dot * idx_scale;
+            acc += qs[IH * ID + h] * (v > 0.f ? v : 0.f);
+        }
+        score[(size_t)t * maxpools + p] = acc;
+    }
+}
+
+// top-(topk/kpool) pools per row, stable with lower-index ties
+// (c/gdsa.h:404-429): a pool is kept iff fewer than K pools beat it.
+__global__ void k_dsa_select(const float *score, const int *base_n, int kp, int ksel, int maxpools, uint8_t *sel) {
+    const int t = blockIdx.x;
+    const int nvalid = min((*base_n + t + 1) / kp, maxpools);
+    const float *s = score + (size_t)t * maxpools;
+    uint8_t *o = sel + (size_t)t * maxpools;
+    if (nvalid <= ksel) {
+        for (int p = threadIdx.x; p < nvalid; p += blockDim.x) o[p] = 1;
+        return;
+    }
+    for (int p = threadIdx.x; p < nvalid; p += blockDim.x) {
+        const unsigned long long kpk = argmax_key(s[p], (uint32_t)p);
+        int beat = 0;
+        for (int q = 0; q < nvalid && beat < ksel; q++) beat += argmax_key(s[q], (uint32_t)q) > kpk;
+        o[p] = beat < ksel;
+    }
+}
+
+// Attention over the selected positions (c/gdsa.h:451-517): one CTA per
+// head handles every row, so each K/V row is read once per call.
+//   sc = bf16(bf16(q.k) * qd^-0.5); p = bf16(softmax(sc)); o = bf16(sum p v)
+// Visibility of position j for row t: j <= base+t and (its pool is
+// selected, or j is in the row's incomplete tail pool).
+__global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd,
+                                                  int vd, int kp, int maxpools, const uint8_t *sel, DsaState ds,
+                                                  float *sbuf, int sstride, uint16_t *out) {
+    const int h = blockIdx.x;
+    const int base = *base_n;
+    const int nmax = base + R;            // positions that exist after this call's append
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const float scale = (float)(1.0 / sqrt((double)qd));
+    float *sc = sbuf + (size_t)h * R * sstride;       // [R][sstride] scores (global scratch)
+    __shared__ float qsh[MAXR][256];
+    for (int i = threadIdx.x; i < R * qd; i += blockDim.x)
+        qsh[i / qd][i % qd] = bf16_f32(q[(size_t)(i / qd) * AH * qd + (size_t)h * qd + i % qd]);
+    __syncthreads();
+    auto visible = [&](int t, int j) -> bool {
+        const int qpos = base + t;
+        if (j > qpos) return false;
+        const int vis = qpos + 1, tc = vis % kp, ts = vis - tc;
+        if (j >= ts) return true;
+        const int p = j / kp;
+        return p < maxpools && sel[(size_t)t * maxpools + p];
+    };
+    // scores: one warp per position, lanes split the qd dims (fixed tree)
+    for (int j = warp; j < nmax; j += nw) {
+        bool any = false;
+        for (int t = 0; t < R; t++) any |= visible(t, j);
+        if (!any) continue;
+        const uint16_t *kr = ds.k + ((size_t)h * ds.cap + j) * qd;
+        float kv[8];
+        for (int e = 0; e < qd / 32; e++) kv[e] = bf16_f32(kr[lane + 32 * e]);
+        for (int t = 0; t < R; t++) {
+            if (!visible(t, j)) continue;
+            float acc = 0.f;
+            for (int e = 0; e < qd / 32; e++) acc += qsh[t][lane + 32 * e] * kv[e];
+#pragma unroll
+            for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+            if (lane == 0) sc[(size_t)t * sstride + j] = bf16_round(bf16_round(acc) * scale);
+        }
+    }
+    __syncthreads();
+    // softmax per row over its visible positions (fixed-order block reductions)
+    __shared__ float red[256], mxs[MAXR], sums[MAXR];
+    for (int t = 0; t < R; t++) {
+        float m = -3.4028234663852886e+38f;
+        for (int j = threadIdx.x; j <= base + t; j += blockDim.x)
+            if (visible(t, j)) m = fmaxf(m, sc[(size_t)t * sstride + j]);
+        red[threadIdx.x] = m;
+        __syncthreads();
+        for (int s = blockDim.x / 2; s; s >>= 1) {
+            if ((int)threadIdx.x < s) red[threadIdx.x] = fmaxf(red[threadIdx.x], red[threadIdx.x + s]);
+            __syncthreads();
+        }
+        const float mx = red[0];
+        __syncthreads();
+        float su = 0.f;
+        for (int j = threadIdx.x; j <= base + t; j += blockDim.x)
+            if (visible(t, j)) {
+                const float e = expf(sc[(size_t)t * sstride + j] - mx);
+                sc[(size_t)t * sstride + j] = e;
+                su += e;
+            }
+        red[threadIdx.x] = su;
+        __syncthreads();
+        for (int s = blockDim.x / 2; s; s >>= 1) {
+            if ((int)threadIdx.x < s) red[threadIdx.x] = red[threadIdx.x] + red[threadIdx.x + s];
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) { mxs[t] = mx; sums[t] = red[0]; }
+        __syncthreads();
+    }
+    // o[t][dv] = bf16(sum_j bf16(e_j / sum) * v_j[dv]), ascending j
+    for (int dv = threadIdx.x; dv < vd; dv += blockDim.x) {
+        float acc[MAXR];
+        for (int t = 0; t < R; t++) acc[t] = 0.f;
+        for (int j = 0; j < nmax; j++) {
+            const float vj = bf16_f32(ds.v[((size_t)h * ds.cap + j) * vd + dv]);
+            for (int t = 0; t < R; t++)
+                if (visible(t, j)) acc[t] += bf16_round(sc[(size_t)t * sstride + j] / sums[t]) * vj;
+        }
+        for (int t = 0; t < R; t++) out[(size_t)t * AH * vd + (size_t)h * vd + dv] = bf16_bits(acc[t]);
+    }
+}
+
+}  // namespace apus
+
+using namespace apus;
+
+static int ok_launch() { return cudaGetLastError() == cudaSuccess ? 0 : -1; }
+
+// Leaves of the numpy pairwise recursion over n (what block_pw's 256-entry
+// leaf table must hold).
+static int pw_leaves(int n) {
+    if (n <= 128) return 1;
+    const int n2 = (n / 2) & ~7;
+    return pw_leaves(n2) + pw_leaves(n - n2);
+}
+
+int layers_prepare(const Dims &D) {
+    const int rows[] = {D.hc * D.d, D.d, D.ql, D.kl, D.ID, D.D};
+    for (int n : rows)
+        if (n > 0 && pw_leaves(n) > 256) return -1;
+    if (D.K < 2 || D.K > 9 || D.kpool > 16 || D.qd > 256 || D.IH * D.ID > 32 * 128) return -1;
+    // row kernels keep one or two fp32 copies of the row in dynamic smem
+    const int maxrow = D.d > D.ql ? (D.d > D.kl ? D.d : D.kl) : (D.ql > D.kl ? D.ql : D.kl);
+    const size_t need_rms = (size_t)D.hc * D.d * 4, need_row = (size_t)2 * maxrow * 4;
+    if (need_rms > 200 * 1024 || need_row > 200 * 1024) return -1;
+    if (cudaFuncSetAttribute(k_hc_rms, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_rms) ||
+        cudaFuncSetAttribute(k_hc_maps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
+        cudaFuncSetAttribute(k_head_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
+        cudaFuncSetAttribute(k_rmsnorm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row))
+        return -1;
+    return 0;
+}
+
+int k_embed_launch(const uint16_t *embed, const int32_t *ids, int R, int d, int hc, uint16_t *h4, cudaStream_t st) {
+    k_embed<<<dim3((d + 255) / 256, R), 256, 0, st>>>(embed, ids, d, hc, h4);
+    return ok_launch();
+}
+
+int hc_pre_launch(const Dims &D, const LayerW &W, int site, const uint16_t *h4, int R, Scratch &S,
+                  cudaStream_t st) {
+    const int n = D.hc * D.d, nmix = (2 + D.hc) * D.hc;
+    k_hc_rms<<<R, 512, n * sizeof(float), st>>>(h4, n, D.eps, S.rms);
+    k_hc_mix<<<dim3(nmix, R), 256, 0, st>>>(W.hc_fn[site], h4, S.rms, n, nmix, S.mix);
+    k_hc_maps<<<R, 512, 2 * D.d * sizeof(float), st>>>(h4, S.mix, W.hc_scale[site], W.hc_base[site],
+                                                       site ? W.post_norm : W.input_norm, D.d, D.hc,
+                                                       D.sinkhorn_iters, D.hc_eps, D.eps, S.post, S.comb, S.x);
+    return ok_launch();
+}
+
+int hc_post_launch(const Dims &D, const uint16_t *x, const uint16_t *h4, int R, const Scratch &S, uint16_t *h4out,
+                   cudaStream_t st) {
+    k_hc_post<<<dim3((D.hc * D.d + 255) / 256, R), 256, 0, st>>>(x, h4, S.post, S.comb, D.d, D.hc, h4out);
+    return ok_launch();
+}
+
+int head_norm_launch(const Dims &D, const uint16_t *h4, const uint16_t *norm_w, int R, uint16_t *yn,
+                     cudaStream_t st) {
+    k_head_norm<<<R, 512, 2 * D.d * sizeof(float), st>>>(h4, norm_w, D.d, D.hc, D.eps, yn);
+    return ok_launch();
+}
+
+int rmsnorm_rows_launch(const uint16_t *x, long ldx, const uint16_t *w, int n, int R, float eps, uint16_t *y,
+                        long ldy, cudaStream_t st) {
+    k_rmsnorm_rows<<<R, 512, 2 * n * sizeof(float), st>>>(x, ldx, w, n, eps, y, ldy);
+    return ok_launch();
+}
+
+int residual_add_launch(uint16_t *x, const uint16_t *sub, long n, cudaStream_t st) {
+    k_residual_add<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, sub, n);
+    return ok_launch();
+}
+
+static const int g_two_problems[2] = {0, 1};
+
+int kda_launch(const Dims &D, const LayerW &W, KdaState &KS, const Ctl *ctl, int R, Scratch &S, float *part,
+               int *tick, cudaStream_t st) {
+    const int qkv = D.qkv, ldkp = kda_ldkp(D);
+    static int *d_probs = nullptr, *d_cnt = nullptr;
+    if (!d_probs) {
+        if (cudaMalloc(&d_probs, 2 * sizeof(int)) != cudaSuccess || cudaMalloc(&d_cnt, sizeof(int)) != cudaSuccess)
+            return -1;
+        const int two = 2;
+        cudaMemcpy(d_probs, g_two_problems, 2 * sizeof(int), cudaMemcpyHostToDevice);
+        cudaMemcpy(d_cnt, &two, sizeof(int), cudaMemcpyHostToDevice);
+    }
+    // q|k|v|f_a|g_a|b share the normed input: one GEMV
+    GemvDesc g{};
+    g.W = W.kda.proj; g.x = S.x; g.ldx = D.d; g.R = R; g.O = kda_nproj(D); g.K = D.d; g.fp8 = 0;
+    g.y = S.kp; g.ldy = ldkp; g.part = part; g.ticket = tick;
+    if (gemv_launch(g, st)) return -1;
+    // conv + SiLU over q|k|v, tokens chained, checkpointed
+    k_kda_conv<<<(3 * qkv + 127) / 128, 128, 0, st>>>(S.kp, ldkp, W.kda.conv, KS.conv, ctl, R, 3 * qkv, D.K, S.qkvc);
+    if (ok_launch()) return -1;
+    // f_b and g_b (low-rank up-projections) as two problems of one launch
+    GemvDesc fg{};
+    fg.W = W.kda.fg_b; fg.x = S.kp + 3 * qkv; fg.ldx = ldkp; fg.R = R; fg.O = qkv; fg.K = D.Dr; fg.fp8 = 0;
+    fg.y = S.fgo; fg.ldy = qkv;
+    fg.gexpert = d_probs; fg.gcount = d_cnt; fg.gmax = 2;
+    fg.w_estride = (long)qkv * D.Dr * 2; fg.x_pstride = D.Dr; fg.y_pstride = (long)MAXR * qkv;
+    if (gemv_launch(fg, st)) return -1;
+    if (D.D != 128) return -1;
+    k_kda_rec<128><<<D.H, 128, 0, st>>>(S.qkvc, S.kp, ldkp, 3 * qkv + 2 * D.Dr, S.fgo, (long)MAXR * qkv,
+                                         W.kda.A_log, W.kda.dt_bias, W.kda.o_norm, KS.rec, ctl, R, D.H,
+                                         D.lower_bound, D.eps, (float)pow((double)D.D, -0.5), S.core);
+    if (ok_launch()) return -1;
+    GemvDesc o{};
+    o.W = W.kda.o_w; o.x = S.core; o.ldx = qkv; o.R = R; o.O = D.d; o.K = qkv; o.fp8 = 0;
+    o.y = S.sub; o.ldy = D.d; o.part = part; o.ticket = tick;
+    return gemv_launch(o, st);
+}
+
+int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, int R, Scratch &S, const uint16_t *x,
+               uint16_t *out, float *part, int *tick, cudaStream_t st) {
+    const int ql = D.ql, kl = D.kl;
+    GemvDesc a{};
+    a.W = W.qkva_c; a.WS = W.qkva_s; a.nkb = (D.d + 127) / 128; a.x = x; a.ldx = D.d; a.R = R;
+    a.O = ql + kl; a.K = D.d; a.fp8 = 1; a.y = S.qkva; a.ldy = ql + kl; a.part = part; a.ticket = tick;
+    if (gemv_launch(a, st)) return -1;
+    if (rmsnorm_rows_launch(S.qkva, ql + kl, W.q_a_norm, ql, R, D.eps, S.qres, ql, st)) return -1;
+    if (rmsnorm_rows_launch(S.qkva + ql, ql + kl, W.kv_a_norm, kl, R, D.eps, S.kpass, kl, st)) return -1;
+    GemvDesc b{};
+    b.W = W.q_b_c; b.WS = W.q_b_s; b.nkb = (ql + 127) / 128; b.x = S.qres; b.ldx = ql; b.R = R;
+    b.O = (long)D.AH * D.qd; b.K = ql; b.fp8 = 1; b.y = S.q; b.ldy = (long)D.AH * D.qd; b.part = part; b.ticket = tick;
+    if (gemv_launch(b, st)) return -1;
+    GemvDesc c{};
+    c.W = W.kv_b; c.x = S.kpass; c.ldx = kl; c.R = R; c.O = (long)D.AH * (D.qd + D.vd); c.K = kl; c.fp8 = 0;
+    c.y = S.kvb; c.ldy = c.O; c.part = part; c.ticket = tick;
+    if (gemv_launch(c, st)) return -1;
+    GemvDesc e{};
+    e.W = W.idx_kgw; e.x = x; e.ldx = D.d; e.R = R; e.O = 2 * D.ID + D.IH; e.K = D.d; e.fp8 = 0;
+    e.y = S.ikgw; e.ldy = e.O; e.part = part; e.ticket = tick;
+    if (gemv_launch(e, st)) return -1;
+    GemvDesc f{};
+    f.W = W.idx_wq_b; f.x = S.qres; f.ldx = ql; f.R = R; f.O = (long)D.IH * D.ID; f.K = ql; f.fp8 = 0;
+    f.y = S.iq; f.ldy = f.O; f.part = part; f.ticket = tick;
+    if (gemv_launch(f, st)) return -1;
+    k_dsa_append<<<R, 256, 0, st>>>(S.kvb, S.ikgw, W.idx_knorm_w, W.idx_knorm_b, base_n, D.AH, D.qd, D.vd, D.ID,
+                                     D.IH, DS.cap, DS);
+    k_dsa_pool<<<R, 128, 0, st>>>(W.idx_ape, base_n, R, D.ID, D.kpool, DS.cap, DS);
+    k_dsa_score<<<dim3(8, R), 256, 0, st>>>(S.iq, S.ikgw, base_n, D.IH, D.ID, D.kpool, S.maxpools, DS, S.iscore);
+    k_dsa_select<<<R, 256, 0, st>>>(S.iscore, base_n, D.kpool, D.topk / D.kpool, S.maxpools, S.isel);
+    if (ok_launch()) return -1;
+    k_dsa_attn<<<D.AH, 256, 0, st>>>(S.q, base_n, R, D.AH, D.qd, D.vd, D.kpool, S.maxpools, S.isel, DS,
+                                      (float *)S.attn_scores, S.attn_sstride, S.attn);
+    if (ok_launch()) return -1;
+    GemvDesc o{};
+    o.W = W.o_c; o.WS = W.o_s; o.nkb = ((long)D.AH * D.vd + 127) / 128; o.x = S.attn; o.ldx = (long)D.AH * D.vd;
+    o.R = R; o.O = D.d; o.K = (long)D.AH * D.vd; o.fp8 = 1; o.y = out; o.ldy = D.d; o.part = part; o.ticket = tick;
+    return gemv_launch(o, st);
+}

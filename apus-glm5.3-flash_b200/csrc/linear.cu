@@ -400,21 +400,47 @@ __global__ void k_gemv_generic(GemvDesc d) {
     const int lane = threadIdx.x & 31;
     const long o = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (o >= d.O) return;
+    // grouped mode: blockIdx.y is the problem (same meaning as the fast path)
+    const int p = blockIdx.y;
+    const uint8_t *Wb = (const uint8_t *)d.W;
+    const float *WS = d.WS;
+    const uint16_t *xs = d.x;
+    uint16_t *yout = d.y;
+    if (d.gexpert) {
+        if (p >= min(*d.gcount, d.gmax)) return;
+        Wb += (size_t)d.gexpert[p] * d.w_estride;
+        if (FP8) WS += (size_t)d.gexpert[p] * d.s_estride;
+        xs += (size_t)p * d.x_pstride;
+        if (yout) yout += (size_t)p * d.y_pstride;
+    }
     float acc[8];
 #pragma unroll
     for (int r = 0; r < 8; r++) acc[r] = 0.f;
     for (long k = lane; k < d.K; k += 32) {
         float w;
         if (FP8) {
-            const uint8_t c = ((const uint8_t *)d.W)[(size_t)o * d.K + k];
-            const float s = d.WS[(size_t)(o >> 7) * d.nkb + (k >> 7)];
+            const uint8_t c = Wb[(size_t)o * d.K + k];
+            const float s = WS[(size_t)(o >> 7) * d.nkb + (k >> 7)];
             w = bf16_round(__fmul_rn(e4m3_f32(c), s));
         } else {
-            w = bf16_f32(((const uint16_t *)d.W)[(size_t)o * d.K + k]);
+            w = bf16_f32(((const uint16_t *)Wb)[(size_t)o * d.K + k]);
         }
 #pragma unroll
         for (int r = 0; r < 8; r++)
-            if (r < d.R) acc[r] = acc[r] + w * bf16_f32(d.x[(size_t)r * d.ldx + k]);
+            if (r < d.R) {
+                float xv;
+                if (d.x_swiglu) {     // x row = [gate | up] of width 2K (c/gmoe.h:216-224)
+                    float ga = bf16_f32(xs[(size_t)r * d.ldx + k]), up = bf16_f32(xs[(size_t)r * d.ldx + d.K + k]);
+                    const float lim = d.swiglu_limit;
+                    ga = ga > lim ? lim : ga;
+                    up = up > lim ? lim : (up < -lim ? -lim : up);
+                    const float hv = bf16_round(ga * sigmoid_np(ga));
+                    xv = bf16_round(hv * up);
+                } else {
+                    xv = bf16_f32(xs[(size_t)r * d.ldx + k]);
+                }
+                acc[r] = acc[r] + w * xv;
+            }
     }
 #pragma unroll
     for (int r = 0; r < 8; r++)
@@ -424,9 +450,9 @@ __global__ void k_gemv_generic(GemvDesc d) {
         float v = acc[0];
 #pragma unroll
         for (int r = 1; r < 8; r++) if (lane == r) v = acc[r];
-        if (d.y) d.y[(size_t)lane * d.ldy + o] = bf16_bits(v);
-        if (d.yf) d.yf[(size_t)lane * d.ldyf + o] = v;
-        if (d.amax) atomicMax(d.amax + lane, argmax_key(bf16_round(v), (uint32_t)o));
+        if (yout) yout[(size_t)lane * d.ldy + o] = bf16_bits(v);
+        if (d.yf && !d.gexpert) d.yf[(size_t)lane * d.ldyf + o] = v;
+        if (d.amax && !d.gexpert) atomicMax(d.amax + lane, argmax_key(bf16_round(v), (uint32_t)o));
     }
 }
 
@@ -516,7 +542,8 @@ int gemv_launch(const GemvDesc &d, cudaStream_t st) {
         else rc = xs ? launch_tma<false, true>(d, st) : launch_tma<false, false>(d, st);
         if (rc) return -1;
     } else {
-        const unsigned grid = (unsigned)((d.O + 7) / 8);
+        if (d.R > 8) return -1;
+        const dim3 grid((unsigned)((d.O + 7) / 8), d.gexpert ? (unsigned)d.gmax : 1u);
         if (d.fp8) k_gemv_generic<true><<<grid, 256, 0, st>>>(d);
         else k_gemv_generic<false><<<grid, 256, 0, st>>>(d);
     }

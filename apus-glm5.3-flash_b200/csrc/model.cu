@@ -1,0 +1,1000 @@
+// model.cu — the resident glm5_next model, its decode forward, the MTP head
+// and the on-device speculative step (include/apus_gmtp_gcuda.h).
+//
+// HBM layout (chosen for one-launch decode GEMVs): per KDA layer the six
+// projections that read the same normed input are one row-concatenated BF16
+// matrix (q|k|v|f_a|g_a|b); per DSA layer q_a|kv_a are one FP8 matrix and
+// the indexer's wk|compress_gate|weights_proj one BF16 matrix; MoE experts
+// are packed per layer (see gmoe.cu); the dense MLP is the "shared expert"
+// of an MoE with no routed experts.
+//
+// Speculative step (c/gmtp.h:776-891, greedy), all launches fixed-shape so no
+// host round-trip happens inside a step:
+//   k_spec_begin   batch = [held, d2..dD]
+//   main forward   D rows at pos..pos+D-1, lm_head GEMV fused with argmax
+//   MTP replay     D pairs (h_prev|yn[0..D-2], batch) at the MTP position;
+//                  rows past the accepted prefix land in dead cache rows
+//   k_spec_walk    accept walk, emit, commit pos/KDA checkpoint/MTP position,
+//                  pick draft 1 and the chaining hidden of the accepted row
+//   chain          D-1 single-row MTP forwards, each argmax -> next draft
+// Rollback is a checkpoint-slot select for KDA (the recurrent kernel wrote
+// the state after every row) and a position rewind for the DSA caches.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gcuda.h"
+#include "model_dev.h"
+#include "../../include/apus_gcuda.h"
+#include "../../include/apus_gmtp_gcuda.h"
+
+// ------------------------------------------------------------ device kernels
+namespace apus {
+
+__global__ void k_commit(Ctl *c, int R) {
+    if (threadIdx.x == 0) {
+        c->pos += R;
+        c->kda_cur = (c->kda_cur + R) % NSLOT;
+    }
+}
+
+__global__ void k_mtp_commit(Ctl *c, int R) {
+    if (threadIdx.x == 0) c->mtp_n += R;
+}
+
+__global__ void k_extract_picks(const unsigned long long *keys, int R, int *dst) {
+    if ((int)threadIdx.x < R) dst[threadIdx.x] = (int)argmax_key_index(keys[threadIdx.x]);
+}
+
+__global__ void k_reset_keys(unsigned long long *keys, int R) {
+    if ((int)threadIdx.x < R) keys[threadIdx.x] = 0ull;
+}
+
+// Step start.  A step whose rows would pass the capacity freezes the
+// sequence (err) instead: the launches still run (into the slack rows past
+// the capacity) but commit nothing.
+__global__ void k_spec_begin(Ctl *c, int D, int cap, int32_t *ids) {
+    if (threadIdx.x == 0) {
+        if (c->pos + D > cap) c->err = 1;
+        c->batch[0] = c->held;
+        for (int j = 1; j < D; j++) c->batch[j] = c->drafts[j];
+        for (int j = 0; j < D; j++) ids[j] = c->batch[j];
+    }
+}
+
+// MTP replay input rows: row 0 pairs the held token with the carried hnorm
+// input of position q-1, row j the draft batch[j] with yn[j-1] (lag 1,
+// postnorm source, c/gmtp.h:855-866).
+__global__ void k_replay_rows(const uint16_t *hprev_carry, const uint16_t *yn, int D, int d, uint16_t *rows) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D * d; i += gridDim.x * blockDim.x) {
+        const int r = i / d, e = i % d;
+        rows[i] = r == 0 ? hprev_carry[e] : yn[(size_t)(r - 1) * d + e];
+    }
+}
+
+// Accept walk (c/gmtp.h:807-831) and state fixup (:833-848, :867-884).
+__global__ void k_spec_walk(Ctl *c, int D, int32_t *log, int log_cap) {
+    if (threadIdx.x != 0) return;
+    if (c->err) { c->n_emitted = 0; return; }
+    int matched = 0, last = -1;
+    c->emitted[0] = c->held;
+    for (int j = 1; j < D; j++) {
+        const int x = c->picks[j - 1];
+        c->stat_offered++;
+        if (c->drafts[j] == x) { matched++; c->stat_accepted++; c->emitted[matched] = x; }
+        else { last = x; break; }
+    }
+    if (last < 0) last = c->picks[D - 1];
+    c->n_emitted = matched + 1;
+    c->matched = matched;
+    for (int i = 0; i <= matched && c->log_n + i < log_cap; i++) log[c->log_n + i] = c->emitted[i];
+    c->log_n += matched + 1;
+    c->stat_emitted += matched + 1;
+    c->stat_batches++;
+    c->pos += matched + 1;
+    c->kda_cur = (c->kda_cur + matched + 1) % NSLOT;
+    c->held = last;
+    // MTP: the replay wrote D rows at mtp_n; keep the accepted prefix
+    c->mtp_n += matched + 1;
+    c->drafts[0] = c->mtp_picks[matched];
+    for (int i = 1; i < MAXR; i++) c->chain_pos[i] = c->mtp_n + i - 1;
+}
+
+__global__ void k_copy_row(const uint16_t *src, long row, int d, uint16_t *dst) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x)
+        dst[i] = src[row * d + i];
+}
+
+// copy row `matched` (device-selected) of a [D][d] block
+__global__ void k_copy_sel_row(const uint16_t *src, const Ctl *c, int d, uint16_t *dst) {
+    const int row = c->matched;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x)
+        dst[i] = src[(size_t)row * d + i];
+}
+
+__global__ void k_chain_first(const Ctl *c, int32_t *ids) {
+    if (threadIdx.x == 0) ids[0] = c->drafts[0];
+}
+
+__global__ void k_chain_next(Ctl *c, int i, int32_t *ids) {
+    if (threadIdx.x == 0) {
+        c->drafts[i] = c->mtp_picks[0];
+        ids[0] = c->drafts[i];
+    }
+}
+
+__device__ unsigned long long sm64(unsigned long long z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void k_force(Ctl *c, const int32_t *truth, int D, int V) {
+    if (threadIdx.x != 0 || !c->force_on) return;
+    for (int i = 0; i < D; i++) {
+        const long pos = (long)c->pos + i - c->force_base;
+        if (pos < 0 || pos >= c->force_n) continue;
+        const double u = (double)(sm64(c->force_seed ^ (unsigned long long)(c->pos + i)) >> 11) * 0x1.0p-53;
+        const int t = truth[pos];
+        c->drafts[i] = u < c->force_p ? t : (t + 1) % V;
+    }
+}
+
+__global__ void k_greedy_prep(Ctl *c, int32_t *ids) {
+    if (threadIdx.x == 0) ids[0] = c->held;
+}
+
+__global__ void k_greedy_post(Ctl *c, int32_t *log, int log_cap) {
+    if (threadIdx.x == 0) {
+        if (c->log_n < log_cap) log[c->log_n] = c->held;
+        c->log_n++;
+        c->held = c->picks[0];
+    }
+}
+
+__global__ void k_set_held_from_pick(Ctl *c, int row) {
+    if (threadIdx.x == 0) c->held = c->picks[row];
+}
+
+}  // namespace apus
+using namespace apus;
+
+// ------------------------------------------------------------------- host
+
+struct ApusGcudaModel {
+    ApusGcudaConfig cfg;
+    Dims D;
+    int has_mtp, depth, cap, nL;
+    std::vector<LayerW> L;
+    uint16_t *embed = nullptr, *norm = nullptr, *head = nullptr;
+    uint16_t *enorm = nullptr, *hnorm = nullptr, *eh_proj = nullptr, *shared_norm = nullptr;
+    std::vector<KdaState> kda;
+    std::vector<DsaState> dsa;
+    DsaState mtp_dsa{};
+    Scratch S{};
+    float *part = nullptr;
+    int *tick = nullptr;
+    Ctl *ctl = nullptr;
+    int32_t *log = nullptr;
+    int log_cap = 0;
+    int32_t *truth = nullptr;
+    Ctl force{};                         // forced-draft settings (survive reset)
+    int dbg_layer = -1, dbg_stage = -1;  // inspection stop inside main_forward
+    uint16_t *yn_prompt = nullptr;       // [cap][d] post-norm rows of the prompt
+    uint16_t *hcarry = nullptr, *hmtp = nullptr, *mtp_rows = nullptr;
+    int32_t *ids = nullptr;
+    cudaStream_t st = nullptr;
+    std::vector<void *> allocs;
+    // shared MoE scratch
+    MoeDev moe_scr{};
+};
+
+static void *dmalloc(ApusGcudaModel *m, size_t n, bool zero = true) {
+    void *p = nullptr;
+    if (cudaMalloc(&p, n ? n : 16) != cudaSuccess) return nullptr;
+    if (zero) cudaMemset(p, 0, n ? n : 16);
+    m->allocs.push_back(p);
+    return p;
+}
+
+static Dims dims_of(const ApusGcudaConfig &c) {
+    Dims D{};
+    D.d = c.hidden_size; D.V = c.vocab_size; D.L = c.num_hidden_layers; D.hc = c.hc_mult;
+    D.eps = c.rms_norm_eps; D.hc_eps = c.hc_eps; D.lower_bound = c.linear_lower_bound;
+    D.route_scale = c.routed_scaling_factor; D.limit = c.swiglu_limit; D.sinkhorn_iters = c.hc_sinkhorn_iters;
+    D.H = c.linear_num_heads; D.D = c.linear_head_dim; D.Dr = c.linear_head_dim; D.K = c.linear_conv_kernel_dim;
+    D.qkv = D.H * D.D;
+    D.AH = c.num_attention_heads; D.qd = c.qk_nope_head_dim; D.vd = c.v_head_dim; D.ql = c.q_lora_rank;
+    D.kl = c.kv_lora_rank; D.IH = c.index_n_heads; D.ID = c.index_head_dim; D.topk = c.index_topk;
+    D.kpool = c.index_kpool; D.tail = c.index_kpool_always_select_tail;
+    D.E = c.n_routed_experts; D.ktop = c.num_experts_per_tok; D.inter = c.moe_intermediate_size;
+    D.dense_inter = c.intermediate_size;
+    return D;
+}
+
+// MoE weights + per-layer views into the shared scratch
+static bool alloc_moe(ApusGcudaModel *m, MoeDev &md, int E, int topk, int inter) {
+    const Dims &D = m->D;
+    md = m->moe_scr;
+    md.E = E; md.topk = topk; md.inter = inter; md.dim = D.d; md.max_r = MAXR; md.pdl = 0;
+    md.route_scale = D.route_scale; md.limit = D.limit;
+    const size_t nkd = (D.d + 127) / 128, nki = (inter + 127) / 128;
+    md.gate_w = E ? (uint16_t *)dmalloc(m, (size_t)E * D.d * 2) : nullptr;
+    md.gate_bias = E ? (float *)dmalloc(m, (size_t)E * 4) : nullptr;
+    md.gu_codes = (uint8_t *)dmalloc(m, (size_t)(E + 1) * 2 * inter * D.d, false);
+    md.gu_scales = (float *)dmalloc(m, (size_t)(E + 1) * (2 * inter / 128) * nkd * 4, false);
+    md.d_codes = (uint8_t *)dmalloc(m, (size_t)(E + 1) * D.d * inter, false);
+    md.d_scales = (float *)dmalloc(m, (size_t)(E + 1) * nkd * nki * 4, false);
+    return md.gu_codes && md.gu_scales && md.d_codes && md.d_scales && (!E || (md.gate_w && md.gate_bias));
+}
+
+static bool alloc_dsa_w(ApusGcudaModel *m, DsaW &w) {
+    const Dims &D = m->D;
+    const size_t nkd = (D.d + 127) / 128;
+    w.qkva_c = (uint8_t *)dmalloc(m, (size_t)(D.ql + D.kl) * D.d, false);
+    w.qkva_s = (float *)dmalloc(m, (size_t)((D.ql + D.kl) / 128) * nkd * 4, false);
+    w.q_a_norm = (uint16_t *)dmalloc(m, (size_t)D.ql * 2);
+    w.kv_a_norm = (uint16_t *)dmalloc(m, (size_t)D.kl * 2);
+    w.q_b_c = (uint8_t *)dmalloc(m, (size_t)D.AH * D.qd * D.ql, false);
+    w.q_b_s = (float *)dmalloc(m, (size_t)((D.AH * D.qd + 127) / 128) * ((D.ql + 127) / 128) * 4, false);
+    w.kv_b = (uint16_t *)dmalloc(m, (size_t)D.AH * (D.qd + D.vd) * D.kl * 2, false);
+    w.o_c = (uint8_t *)dmalloc(m, (size_t)D.d * D.AH * D.vd, false);
+    w.o_s = (float *)dmalloc(m, nkd * (((size_t)D.AH * D.vd + 127) / 128) * 4, false);
+    w.idx_wq_b = (uint16_t *)dmalloc(m, (size_t)D.IH * D.ID * D.ql * 2, false);
+    w.idx_kgw = (uint16_t *)dmalloc(m, (size_t)(2 * D.ID + D.IH) * D.d * 2, false);
+    w.idx_knorm_w = (uint16_t *)dmalloc(m, (size_t)D.ID * 2);
+    w.idx_knorm_b = (uint16_t *)dmalloc(m, (size_t)D.ID * 2);
+    w.idx_ape = (uint16_t *)dmalloc(m, (size_t)D.kpool * D.ID * 2);
+    return w.qkva_c && w.qkva_s && w.q_b_c && w.kv_b && w.o_c && w.idx_wq_b && w.idx_kgw && w.idx_ape;
+}
+
+// DSA caches hold SLACK rows past the sequence capacity: the MTP draft chain
+// runs up to depth-1 rows ahead of the committed position, and a step that
+// overruns the capacity (frozen by k_spec_begin) still writes its rows.
+#define SLACK (3 * MAXR)
+static bool alloc_dsa_state(ApusGcudaModel *m, DsaState &s) {
+    const Dims &D = m->D;
+    const size_t rows = (size_t)m->cap + SLACK;
+    s.cap = (int)rows;
+    s.k = (uint16_t *)dmalloc(m, (size_t)D.AH * rows * D.qd * 2);
+    s.v = (uint16_t *)dmalloc(m, (size_t)D.AH * rows * D.vd * 2);
+    s.ik = (uint16_t *)dmalloc(m, rows * D.ID * 2);
+    s.ig = (uint16_t *)dmalloc(m, rows * D.ID * 2);
+    s.pkey = (uint16_t *)dmalloc(m, (rows / D.kpool + 1) * D.ID * 2);
+    return s.k && s.v && s.ik && s.ig && s.pkey;
+}
+
+static void model_release(ApusGcudaModel *m) {
+    if (!m) return;
+    if (m->st) { cudaStreamSynchronize(m->st); cudaStreamDestroy(m->st); }
+    for (void *p : m->allocs) cudaFree(p);
+    delete m;
+}
+
+extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int has_mtp, size_t kv_cap, int depth) {
+    char err[128];
+    if (apus_gcuda_enable(err, sizeof err)) return nullptr;
+    const Dims D = dims_of(*cfg);
+    bool any_kda = false;
+    for (int l = 0; l < D.L && l < APUS_GCUDA_MAX_LAYERS; l++) any_kda |= !cfg->layer_is_dsa[l];
+    if (depth < 1 || depth > MAXR || D.L < 1 || D.L > APUS_GCUDA_MAX_LAYERS || (any_kda && D.D != 128) ||
+        D.hc < 1 || D.hc > 8 || cfg->n_shared_experts != 1 || D.kpool < 1 || D.ktop > D.E ||
+        D.d % 128 || D.d > 8192 || D.qd > 256 || D.qd % 32 || D.vd % 32 || D.IH > 32 || D.ID > 128 ||
+        D.kpool > 16 || D.ql % 128 || D.kl % 128 || D.inter % 128 || D.dense_inter % 128 || D.E > MOE_MAX_E ||
+        D.ktop > MOE_MAX_TOPK || kv_cap < 16) {
+        gcuda_set_error("gmodel: unsupported configuration");
+        return nullptr;
+    }
+    if (layers_prepare(D)) {
+        cudaGetLastError();
+        gcuda_set_error("gmodel: unsupported layer shapes");
+        return nullptr;
+    }
+    ApusGcudaModel *m = new ApusGcudaModel();
+    m->cfg = *cfg;
+    m->D = D;
+    m->has_mtp = has_mtp ? 1 : 0;
+    m->depth = depth;
+    m->cap = (int)kv_cap;
+    m->nL = D.L + m->has_mtp;
+    bool ok = cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) == cudaSuccess;
+    // shared scratch (all layers run one after another on one stream)
+    Scratch &S = m->S;
+    const int R = MAXR, d = D.d, qkv = D.qkv, ldkp = kda_ldkp(D);
+    auto A = [&](size_t n) { void *p = dmalloc(m, n); ok = ok && p; return p; };
+    S.h4 = (uint16_t *)A((size_t)R * D.hc * d * 2);
+    S.h4b = (uint16_t *)A((size_t)R * D.hc * d * 2);
+    S.x = (uint16_t *)A((size_t)R * d * 2);
+    S.sub = (uint16_t *)A((size_t)R * d * 2);
+    S.rms = (float *)A(R * 4);
+    S.mix = (float *)A((size_t)R * (2 + D.hc) * D.hc * 4);
+    S.post = (float *)A((size_t)R * D.hc * 4);
+    S.comb = (float *)A((size_t)R * D.hc * D.hc * 4);
+    S.kp = (uint16_t *)A((size_t)R * ldkp * 2);
+    S.fgo = (uint16_t *)A((size_t)2 * R * qkv * 2);
+    S.qkvc = (uint16_t *)A((size_t)R * 3 * qkv * 2);
+    S.core = (uint16_t *)A((size_t)R * qkv * 2);
+    S.qkva = (uint16_t *)A((size_t)R * (D.ql + D.kl) * 2);
+    S.qres = (uint16_t *)A((size_t)R * D.ql * 2);
+    S.kpass = (uint16_t *)A((size_t)R * D.kl * 2);
+    S.q = (uint16_t *)A((size_t)R * D.AH * D.qd * 2);
+    S.kvb = (uint16_t *)A((size_t)R * D.AH * (D.qd + D.vd) * 2);
+    S.iq = (uint16_t *)A((size_t)R * D.IH * D.ID * 2);
+    S.ikgw = (uint16_t *)A((size_t)R * (2 * D.ID + D.IH) * 2);
+    S.maxpools = (m->cap + SLACK) / D.kpool + 1;
+    S.iscore = (float *)A((size_t)R * S.maxpools * 4);
+    S.isel = (uint8_t *)A((size_t)R * S.maxpools);
+    S.attn = (uint16_t *)A((size_t)R * D.AH * D.vd * 2);
+    S.attn_sstride = m->cap + SLACK + MAXR;
+    S.attn_scores = (float *)A((size_t)D.AH * R * S.attn_sstride * 4);
+    S.yn = (uint16_t *)A((size_t)R * d * 2);
+    S.logits = (uint16_t *)A((size_t)R * D.V * 2);
+    S.amax = (unsigned long long *)A(R * 8);
+    S.ids = (int32_t *)A(R * 4);
+    S.eh = (uint16_t *)A((size_t)R * 2 * d * 2);
+    S.mx = (uint16_t *)A((size_t)R * d * 2);
+    S.mxn = (uint16_t *)A((size_t)R * d * 2);
+    S.oh = (uint16_t *)A((size_t)R * d * 2);
+    S.hprev = (uint16_t *)A((size_t)R * d * 2);
+    // split-K scratch sized for the largest split GEMV: K up to 4 ranges of
+    // 4096 over up to V rows
+    {
+        size_t pf1, nt1, pf2, nt2;
+        gemv_scratch_need(D.V, 2L * d, &pf1, &nt1);
+        gemv_scratch_need(16384, (long)D.AH * D.vd > qkv ? (long)D.AH * D.vd : qkv, &pf2, &nt2);
+        size_t pf = pf1 > pf2 ? pf1 : pf2, nt = nt1 > nt2 ? nt1 : nt2;
+        const size_t pd = (size_t)d / 16 * 4 * 128;
+        if (pf < pd) pf = pd;
+        if (nt < (size_t)d / 16) nt = d / 16;
+        m->part = (float *)A(pf * 4);
+        m->tick = (int *)A(nt * 4);
+    }
+    m->ctl = (Ctl *)A(sizeof(Ctl));
+    m->log_cap = m->cap + 2 * MAXR;
+    m->log = (int32_t *)A((size_t)m->log_cap * 4);
+    m->yn_prompt = (uint16_t *)A((size_t)(m->cap + MAXR) * d * 2);
+    m->hcarry = (uint16_t *)A((size_t)d * 2);
+    m->hmtp = (uint16_t *)A((size_t)d * 2);
+    m->mtp_rows = (uint16_t *)A((size_t)R * d * 2);
+    m->ids = (int32_t *)A(R * 4);
+    // MoE scratch shared by every sparse layer
+    {
+        MoeDev &ms = m->moe_scr;
+        const int maxi = D.inter > D.dense_inter ? D.inter : D.dense_inter;
+        const size_t P = (size_t)R * (D.ktop > 0 ? D.ktop : 1) + 1;
+        ms.logits = (float *)A((size_t)R * (D.E > 0 ? D.E : 1) * 4);
+        ms.row_expert = (int32_t *)A((size_t)R * MOE_MAX_TOPK * 4);
+        ms.row_weight = (float *)A((size_t)R * MOE_MAX_TOPK * 4);
+        ms.row_sel = (int32_t *)A((size_t)R * MOE_MAX_TOPK * 4);
+        ms.row_prob = (int32_t *)A((size_t)R * MOE_MAX_TOPK * 4);
+        ms.row_prob_shared = (int32_t *)A((size_t)R * 4);
+        ms.prob_expert = (int32_t *)A(P * 4);
+        ms.prob_count = (int32_t *)A(4);
+        ms.gu = (uint16_t *)A(P * R * 2 * (size_t)maxi * 2);
+        ms.yd = (uint16_t *)A(P * R * (size_t)d * 2);
+    }
+    // weights
+    m->embed = (uint16_t *)A((size_t)D.V * d * 2);
+    m->norm = (uint16_t *)A((size_t)d * 2);
+    m->head = (uint16_t *)A((size_t)D.V * d * 2);
+    m->L.resize(m->nL);
+    m->kda.resize(D.L);
+    m->dsa.resize(D.L);
+    const int mix = (2 + D.hc) * D.hc;
+    for (int l = 0; l < m->nL && ok; l++) {
+        LayerW &W = m->L[l];
+        const bool mtp = l >= D.L;
+        W.is_dsa = mtp ? 1 : cfg->layer_is_dsa[l];
+        W.sparse = mtp ? 1 : cfg->mlp_is_sparse[l];
+        W.input_norm = (uint16_t *)A((size_t)d * 2);
+        W.post_norm = (uint16_t *)A((size_t)d * 2);
+        if (!mtp)
+            for (int s = 0; s < 2; s++) {
+                W.hc_fn[s] = (uint16_t *)A((size_t)mix * D.hc * d * 2);
+                W.hc_base[s] = (float *)A((size_t)mix * 4);
+                W.hc_scale[s] = (float *)A(3 * 4);
+            }
+        if (!W.is_dsa) {
+            W.kda.proj = (uint16_t *)A((size_t)kda_nproj(D) * d * 2);
+            W.kda.fg_b = (uint16_t *)A((size_t)2 * qkv * D.Dr * 2);
+            W.kda.conv = (uint16_t *)A((size_t)3 * qkv * D.K * 2);
+            W.kda.A_log = (float *)A((size_t)D.H * 4);
+            W.kda.dt_bias = (float *)A((size_t)qkv * 4);
+            W.kda.o_norm = (uint16_t *)A((size_t)D.D * 2);
+            W.kda.o_w = (uint16_t *)A((size_t)d * qkv * 2);
+            m->kda[l].conv = (uint16_t *)A((size_t)NSLOT * 3 * qkv * (D.K - 1) * 2);
+            m->kda[l].rec = (float *)A((size_t)NSLOT * D.H * D.D * D.D * 4);
+        } else {
+            ok = ok && alloc_dsa_w(m, W.dsa);
+            if (!mtp) ok = ok && alloc_dsa_state(m, m->dsa[l]);
+        }
+        if (W.sparse) ok = ok && alloc_moe(m, W.moe, D.E, D.ktop, D.inter);
+        else ok = ok && alloc_moe(m, W.moe, 0, 0, D.dense_inter);
+    }
+    if (m->has_mtp) {
+        m->enorm = (uint16_t *)A((size_t)d * 2);
+        m->hnorm = (uint16_t *)A((size_t)d * 2);
+        m->eh_proj = (uint16_t *)A((size_t)d * 2 * d * 2);
+        m->shared_norm = (uint16_t *)A((size_t)d * 2);
+        ok = ok && alloc_dsa_state(m, m->mtp_dsa);
+    }
+    if (!ok) {
+        gcuda_set_error("gmodel: device allocation failed");
+        model_release(m);
+        return nullptr;
+    }
+    apus_gcuda_model_reset(m);
+    return m;
+}
+
+extern "C" void apus_gcuda_model_free(ApusGcudaModel *m) { model_release(m); }
+
+// ---- tensor name -> packed device location --------------------------------
+
+static int resolve_moe(const ApusGcudaModel *m, const MoeDev &md, const std::string &n, void **dst, size_t *want) {
+    const size_t dim = m->D.d, inter = md.inter, E = md.E;
+    const size_t nkd = (dim + 127) / 128, nki = (inter + 127) / 128;
+    if (n == "mlp.gate.weight" && E) { *dst = (void *)md.gate_w; *want = E * dim * 2; return 0; }
+    if (n == "mlp.gate.e_score_correction_bias" && E) { *dst = (void *)md.gate_bias; *want = E * 4; return 0; }
+    int e = -1;
+    char part[64] = {0}, kind[64] = {0};
+    if (E && sscanf(n.c_str(), "mlp.experts.%d.%63[a-z]_proj.%63s", &e, part, kind) == 3) {
+        if (e < 0 || e >= (int)E) return -1;
+    } else if (E && sscanf(n.c_str(), "mlp.shared_experts.%63[a-z]_proj.%63s", part, kind) == 2) {
+        e = (int)E;
+    } else if (!E && sscanf(n.c_str(), "mlp.%63[a-z]_proj.%63s", part, kind) == 2) {
+        e = 0;     // dense MLP = the lone "shared" expert
+    } else {
+        return -1;
+    }
+    const bool scale = !strcmp(kind, "weight_scale_inv");
+    if (!scale && strcmp(kind, "weight")) return -1;
+    const size_t gus = (2 * inter / 128) * nkd, ds = nkd * nki;
+    if (!strcmp(part, "gate") || !strcmp(part, "up")) {
+        const int up = !strcmp(part, "up");
+        if (scale) { *dst = (void *)(md.gu_scales + (size_t)e * gus + up * (inter / 128) * nkd); *want = (inter / 128) * nkd * 4; }
+        else { *dst = (void *)(md.gu_codes + (size_t)e * 2 * inter * dim + up * inter * dim); *want = inter * dim; }
+    } else if (!strcmp(part, "down")) {
+        if (scale) { *dst = (void *)(md.d_scales + (size_t)e * ds); *want = ds * 4; }
+        else { *dst = (void *)(md.d_codes + (size_t)e * dim * inter); *want = dim * inter; }
+    } else {
+        return -1;
+    }
+    return 0;
+}
+
+static int resolve(const ApusGcudaModel *m, const char *name, void **dst, size_t *want) {
+    const Dims &D = m->D;
+    const size_t d = D.d, V = D.V, qkv = D.qkv, Dr = D.Dr, H = D.H;
+    std::string n(name);
+    if (n == "embed_tokens.weight") { *dst = m->embed; *want = V * d * 2; return 0; }
+    if (n == "norm.weight") { *dst = m->norm; *want = d * 2; return 0; }
+    if (n == "lm_head.weight") { *dst = m->head; *want = V * d * 2; return 0; }
+    int l = -1, off = 0;
+    if (sscanf(name, "layers.%d.%n", &l, &off) != 1 || off <= 0 || l < 0 || l >= m->nL) return -1;
+    const LayerW &W = m->L[l];
+    const bool mtp = l >= D.L;
+    const std::string r = n.substr(off);
+    const int mix = (2 + D.hc) * D.hc;
+    auto is = [&](const char *s) { return r == s; };
+    if (is("input_layernorm.weight")) { *dst = (void *)W.input_norm; *want = d * 2; return 0; }
+    if (is("post_attention_layernorm.weight")) { *dst = (void *)W.post_norm; *want = d * 2; return 0; }
+    if (mtp) {
+        if (is("enorm.weight")) { *dst = m->enorm; *want = d * 2; return 0; }
+        if (is("hnorm.weight")) { *dst = m->hnorm; *want = d * 2; return 0; }
+        if (is("eh_proj.weight")) { *dst = m->eh_proj; *want = d * 2 * d * 2; return 0; }
+        if (is("shared_head.norm.weight")) { *dst = m->shared_norm; *want = d * 2; return 0; }
+    } else {
+        for (int s = 0; s < 2; s++) {
+            const std::string site = s ? "ffn" : "attn";
+            if (r == "hc_" + site + "_fn") { *dst = (void *)W.hc_fn[s]; *want = (size_t)mix * D.hc * d * 2; return 0; }
+            if (r == "hc_" + site + "_base") { *dst = (void *)W.hc_base[s]; *want = (size_t)mix * 4; return 0; }
+            if (r == "hc_" + site + "_scale") { *dst = (void *)W.hc_scale[s]; *want = 3 * 4; return 0; }
+        }
+    }
+    if (!W.is_dsa) {
+        const KdaW &k = W.kda;
+        uint16_t *proj = (uint16_t *)k.proj;
+        if (is("self_attn.q_proj.weight")) { *dst = proj; *want = qkv * d * 2; return 0; }
+        if (is("self_attn.k_proj.weight")) { *dst = proj + qkv * d; *want = qkv * d * 2; return 0; }
+        if (is("self_attn.v_proj.weight")) { *dst = proj + 2 * qkv * d; *want = qkv * d * 2; return 0; }
+        if (is("self_attn.f_a_proj.weight")) { *dst = proj + 3 * qkv * d; *want = Dr * d * 2; return 0; }
+        if (is("self_attn.g_a_proj.weight")) { *dst = proj + (3 * qkv + Dr) * d; *want = Dr * d * 2; return 0; }
+        if (is("self_attn.b_proj.weight")) { *dst = proj + (3 * qkv + 2 * Dr) * d; *want = H * d * 2; return 0; }
+        if (is("self_attn.f_b_proj.weight")) { *dst = (void *)k.fg_b; *want = qkv * Dr * 2; return 0; }
+        if (is("self_attn.g_b_proj.weight")) { *dst = (void *)(k.fg_b + qkv * Dr); *want = qkv * Dr * 2; return 0; }
+        for (int p = 0; p < 3; p++) {
+            const std::string nm = std::string("self_attn.") + "qkv"[p] + "_conv1d.weight";
+            if (r == nm) { *dst = (void *)(k.conv + (size_t)p * qkv * D.K); *want = qkv * D.K * 2; return 0; }
+        }
+        if (is("self_attn.A_log")) { *dst = (void *)k.A_log; *want = H * 4; return 0; }
+        if (is("self_attn.dt_bias")) { *dst = (void *)k.dt_bias; *want = qkv * 4; return 0; }
+        if (is("self_attn.o_norm.weight")) { *dst = (void *)k.o_norm; *want = D.D * 2; return 0; }
+        if (is("self_attn.o_proj.weight")) { *dst = (void *)k.o_w; *want = d * qkv * 2; return 0; }
+    } else {
+        const DsaW &w = W.dsa;
+        const size_t ql = D.ql, kl = D.kl, nkd = (d + 127) / 128;
+        const size_t aq = (size_t)D.AH * D.qd, av = (size_t)D.AH * D.vd;
+        if (is("self_attn.q_a_proj.weight")) { *dst = (void *)w.qkva_c; *want = ql * d; return 0; }
+        if (is("self_attn.q_a_proj.weight_scale_inv")) { *dst = (void *)w.qkva_s; *want = (ql / 128) * nkd * 4; return 0; }
+        if (is("self_attn.kv_a_proj_with_mqa.weight")) { *dst = (void *)(w.qkva_c + ql * d); *want = kl * d; return 0; }
+        if (is("self_attn.kv_a_proj_with_mqa.weight_scale_inv")) {
+            *dst = (void *)(w.qkva_s + (ql / 128) * nkd); *want = (kl / 128) * nkd * 4; return 0;
+        }
+        if (is("self_attn.q_a_layernorm.weight")) { *dst = (void *)w.q_a_norm; *want = ql * 2; return 0; }
+        if (is("self_attn.kv_a_layernorm.weight")) { *dst = (void *)w.kv_a_norm; *want = kl * 2; return 0; }
+        if (is("self_attn.q_b_proj.weight")) { *dst = (void *)w.q_b_c; *want = aq * ql; return 0; }
+        if (is("self_attn.q_b_proj.weight_scale_inv")) {
+            *dst = (void *)w.q_b_s; *want = ((aq + 127) / 128) * ((ql + 127) / 128) * 4; return 0;
+        }
+        if (is("self_attn.kv_b_proj.weight")) { *dst = (void *)w.kv_b; *want = (aq + av) * kl * 2; return 0; }
+        if (is("self_attn.o_proj.weight")) { *dst = (void *)w.o_c; *want = d * av; return 0; }
+        if (is("self_attn.o_proj.weight_scale_inv")) { *dst = (void *)w.o_s; *want = nkd * ((av + 127) / 128) * 4; return 0; }
+        if (is("self_attn.indexer.wq_b.weight")) { *dst = (void *)w.idx_wq_b; *want = (size_t)D.IH * D.ID * ql * 2; return 0; }
+        if (is("self_attn.indexer.wk.weight")) { *dst = (void *)w.idx_kgw; *want = (size_t)D.ID * d * 2; return 0; }
+        if (is("self_attn.indexer.index_kpool_compress_gate")) {
+            *dst = (void *)(w.idx_kgw + (size_t)D.ID * d); *want = (size_t)D.ID * d * 2; return 0;
+        }
+        if (is("self_attn.indexer.weights_proj.weight")) {
+            *dst = (void *)(w.idx_kgw + (size_t)2 * D.ID * d); *want = (size_t)D.IH * d * 2; return 0;
+        }
+        if (is("self_attn.indexer.k_norm.weight")) { *dst = (void *)w.idx_knorm_w; *want = D.ID * 2; return 0; }
+        if (is("self_attn.indexer.k_norm.bias")) { *dst = (void *)w.idx_knorm_b; *want = D.ID * 2; return 0; }
+        if (is("self_attn.indexer.index_kpool_compress_ape")) {
+            *dst = (void *)w.idx_ape; *want = (size_t)D.kpool * D.ID * 2; return 0;
+        }
+    }
+    return resolve_moe(m, W.moe, r, dst, want);
+}
+
+extern "C" int apus_gcuda_model_set(ApusGcudaModel *m, const char *name, const void *host, size_t bytes) {
+    void *dst;
+    size_t want;
+    if (resolve(m, name, &dst, &want)) { gcuda_set_error("gmodel: unknown tensor %s", name); return -1; }
+    if (bytes != want) { gcuda_set_error("gmodel: %s has %zu bytes, expected %zu", name, bytes, want); return -1; }
+    return gcuda_check(cudaMemcpy(dst, host, bytes, cudaMemcpyHostToDevice), "gmodel set");
+}
+
+extern "C" int apus_gcuda_model_get(ApusGcudaModel *m, const char *name, void *host, size_t bytes) {
+    void *src;
+    size_t want;
+    if (resolve(m, name, &src, &want) || bytes != want) { gcuda_set_error("gmodel: bad get %s", name); return -1; }
+    cudaStreamSynchronize(m->st);
+    return gcuda_check(cudaMemcpy(host, src, bytes, cudaMemcpyDeviceToHost), "gmodel get");
+}
+
+// ---- synthetic weights ------------------------------------------------------
+
+extern "C" int apus_gcuda_model_init_random(ApusGcudaModel *m, uint64_t seed) {
+    const Dims &D = m->D;
+    const size_t d = D.d, qkv = D.qkv;
+    uint64_t sid = 100;
+    int rc = 0;
+    cudaStream_t st = m->st;
+    auto bf16n = [&](const void *p, size_t n, float std, float mean = 0.f) {
+        rc |= fill_launch(FILL_BF16_NORMAL, (void *)p, n, seed, sid++, std, mean, st);
+    };
+    auto f32n = [&](const void *p, size_t n, float std, float mean = 0.f) {
+        rc |= fill_launch(FILL_F32_NORMAL, (void *)p, n, seed, sid++, std, mean, st);
+    };
+    auto fp8 = [&](const void *c, const void *s, size_t n, size_t ns) {  // BASELINE config-0/1 FP8 blocks
+        rc |= fill_launch(FILL_E4M3_NORMAL, (void *)c, n, seed, sid++, 64.f, 0.f, st);
+        rc |= fill_launch(FILL_F32_LOGUNIFORM, (void *)s, ns, seed, sid++, 1e-4f, 1e-2f, st);
+    };
+    auto norm = [&](const void *p, size_t n) { bf16n(p, n, 0.05f, 1.0f); };
+    bf16n(m->embed, (size_t)D.V * d, 0.02f);          // BASELINE: N(0, 0.02) embeddings and head
+    bf16n(m->head, (size_t)D.V * d, 0.02f);
+    norm(m->norm, d);
+    const int mix = (2 + D.hc) * D.hc;
+    for (int l = 0; l < m->nL; l++) {
+        LayerW &W = m->L[l];
+        const bool mtp = l >= D.L;
+        norm(W.input_norm, d);
+        norm(W.post_norm, d);
+        if (!mtp)
+            for (int s = 0; s < 2; s++) {
+                bf16n(W.hc_fn[s], (size_t)mix * D.hc * d, 1.0f / sqrtf((float)(D.hc * d)));
+                f32n(W.hc_base[s], mix, 0.25f);
+                f32n(W.hc_scale[s], 3, 0.1f, 1.0f);
+            }
+        if (!W.is_dsa) {
+            bf16n(W.kda.proj, (size_t)kda_nproj(D) * d, 1.0f / sqrtf((float)d));
+            bf16n(W.kda.fg_b, 2 * qkv * D.Dr, 1.0f / sqrtf((float)D.Dr));
+            bf16n(W.kda.conv, 3 * qkv * D.K, 0.25f);
+            f32n(W.kda.A_log, D.H, 0.5f);
+            f32n(W.kda.dt_bias, qkv, 0.5f);
+            norm(W.kda.o_norm, D.D);
+            bf16n(W.kda.o_w, d * qkv, 1.0f / sqrtf((float)qkv));
+        } else {
+            const DsaW &w = W.dsa;
+            const size_t nkd = (d + 127) / 128, aq = (size_t)D.AH * D.qd, av = (size_t)D.AH * D.vd;
+            fp8(w.qkva_c, w.qkva_s, (size_t)(D.ql + D.kl) * d, ((D.ql + D.kl) / 128) * nkd);
+            fp8(w.q_b_c, w.q_b_s, aq * D.ql, ((aq + 127) / 128) * ((D.ql + 127) / 128));
+            fp8(w.o_c, w.o_s, d * av, nkd * ((av + 127) / 128));
+            norm(w.q_a_norm, D.ql);
+            norm(w.kv_a_norm, D.kl);
+            bf16n(w.kv_b, (aq + av) * D.kl, 1.0f / sqrtf((float)D.kl));
+            bf16n(w.idx_wq_b, (size_t)D.IH * D.ID * D.ql, 1.0f / sqrtf((float)D.ql));
+            bf16n(w.idx_kgw, (size_t)(2 * D.ID + D.IH) * d, 1.0f / sqrtf((float)d));
+            norm(w.idx_knorm_w, D.ID);
+            bf16n(w.idx_knorm_b, D.ID, 0.05f);
+            bf16n(w.idx_ape, (size_t)D.kpool * D.ID, 0.05f);
+        }
+        MoeDev &md = W.moe;
+        const size_t nkd = (d + 127) / 128, nki = (md.inter + 127) / 128;
+        if (md.E) {
+            bf16n(md.gate_w, (size_t)md.E * d, 0.02f);           // N(0, 0.02), bias 0
+            rc |= fill_launch(FILL_F32_CONST, (void *)md.gate_bias, md.E, seed, sid++, 0.f, 0.f, st);
+        }
+        fp8(md.gu_codes, md.gu_scales, (size_t)(md.E + 1) * 2 * md.inter * d, (size_t)(md.E + 1) * (2 * md.inter / 128) * nkd);
+        fp8(md.d_codes, md.d_scales, (size_t)(md.E + 1) * d * md.inter, (size_t)(md.E + 1) * nkd * nki);
+    }
+    if (m->has_mtp) {
+        norm(m->enorm, d);
+        norm(m->hnorm, d);
+        bf16n(m->eh_proj, d * 2 * d, 1.0f / sqrtf((float)(2 * d)));
+        norm(m->shared_norm, d);
+    }
+    if (rc) return gcuda_check(cudaGetLastError(), "gmodel init");
+    return gcuda_check(cudaStreamSynchronize(st), "gmodel init sync");
+}
+
+extern "C" int apus_gcuda_model_reset(ApusGcudaModel *m) {
+    const Dims &D = m->D;
+    cudaStreamSynchronize(m->st);
+    for (int l = 0; l < D.L; l++) {
+        if (!m->L[l].is_dsa) {
+            cudaMemsetAsync(m->kda[l].conv, 0, (size_t)NSLOT * 3 * D.qkv * (D.K - 1) * 2, m->st);
+            cudaMemsetAsync(m->kda[l].rec, 0, (size_t)NSLOT * D.H * D.D * D.D * 4, m->st);
+        }
+    }
+    if (m->hcarry) cudaMemsetAsync(m->hcarry, 0, (size_t)D.d * 2, m->st);
+    if (m->hmtp) cudaMemsetAsync(m->hmtp, 0, (size_t)D.d * 2, m->st);
+    Ctl c{};
+    c.one = 1;
+    for (int i = 1; i < MAXR; i++) c.chain_pos[i] = i - 1;
+    c.force_on = m->force.force_on; c.force_base = m->force.force_base; c.force_n = m->force.force_n;
+    c.force_seed = m->force.force_seed; c.force_p = m->force.force_p;
+    if (gcuda_check(cudaMemcpyAsync(m->ctl, &c, sizeof c, cudaMemcpyHostToDevice, m->st), "reset")) return -1;
+    return gcuda_check(cudaStreamSynchronize(m->st), "reset sync");
+}
+
+static Ctl read_ctl(ApusGcudaModel *m) {
+    Ctl c{};
+    cudaStreamSynchronize(m->st);
+    cudaMemcpy(&c, m->ctl, sizeof c, cudaMemcpyDeviceToHost);
+    return c;
+}
+
+extern "C" size_t apus_gcuda_model_pos(const ApusGcudaModel *m) {
+    return (size_t)read_ctl((ApusGcudaModel *)m).pos;
+}
+
+// ---- forward passes -----------------------------------------------------------
+
+// lm_head over `yn` rows with the fused greedy pick into picks[R] (and the
+// BF16 logits when want_logits).
+static int lm_head(ApusGcudaModel *m, const uint16_t *yn, int R, int *picks, bool want_logits) {
+    const Dims &D = m->D;
+    k_reset_keys<<<1, 32, 0, m->st>>>(m->S.amax, R);
+    GemvDesc g{};
+    g.W = m->head; g.x = yn; g.ldx = D.d; g.R = R; g.O = D.V; g.K = D.d; g.fp8 = 0;
+    if (want_logits) { g.y = m->S.logits; g.ldy = D.V; }
+    g.amax = m->S.amax; g.part = m->part; g.ticket = m->tick;
+    if (gemv_launch(g, m->st)) return -1;
+    k_extract_picks<<<1, 32, 0, m->st>>>(m->S.amax, R, picks);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Main model over R rows at positions ctl->pos.., not committed.  yn_out
+// (device, [R][d]) receives the post-norm rows.
+static int main_forward(ApusGcudaModel *m, const int32_t *ids_dev, int R, uint16_t *yn_out, bool want_logits) {
+    const Dims &D = m->D;
+    Scratch &S = m->S;
+    cudaStream_t st = m->st;
+    if (k_embed_launch(m->embed, ids_dev, R, D.d, D.hc, S.h4, st)) return -1;
+    uint16_t *h = S.h4, *h2 = S.h4b;
+    auto stop = [&](int l, int stage) { return l == m->dbg_layer && stage == m->dbg_stage; };
+    for (int l = 0; l < D.L; l++) {
+        LayerW &W = m->L[l];
+        if (hc_pre_launch(D, W, 0, h, R, S, st)) return -1;
+        if (stop(l, 0)) return 0;
+        if (!W.is_dsa) {
+            if (kda_launch(D, W, m->kda[l], m->ctl, R, S, m->part, m->tick, st)) return -1;
+        } else {
+            if (dsa_launch(D, W.dsa, m->dsa[l], &m->ctl->pos, R, S, S.x, S.sub, m->part, m->tick, st)) return -1;
+        }
+        if (stop(l, 1)) return 0;
+        if (hc_post_launch(D, S.sub, h, R, S, h2, st)) return -1;
+        std::swap(h, h2);
+        if (stop(l, 2)) return 0;
+        if (hc_pre_launch(D, W, 1, h, R, S, st)) return -1;
+        if (stop(l, 3)) return 0;
+        if (moe_forward_launch(W.moe, S.x, D.d, R, S.sub, D.d, nullptr, st)) return -1;
+        if (stop(l, 4)) return 0;
+        if (hc_post_launch(D, S.sub, h, R, S, h2, st)) return -1;
+        std::swap(h, h2);
+    }
+    if (h != S.h4) cudaMemcpyAsync(S.h4, h, (size_t)R * D.hc * D.d * 2, cudaMemcpyDeviceToDevice, st);
+    if (head_norm_launch(D, S.h4, m->norm, R, yn_out, st)) return -1;
+    return lm_head(m, yn_out, R, m->ctl->picks, want_logits);
+}
+
+// MTP block (c/gmtp.h:471-541) over R pairs (ids, prev_h rows) whose DSA
+// cache rows start at *base_n; out_h -> S.oh, picks -> ctl->mtp_picks.
+static int mtp_forward(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t *prev_h, int R, const int *base_n,
+                       bool want_logits) {
+    const Dims &D = m->D;
+    Scratch &S = m->S;
+    cudaStream_t st = m->st;
+    const LayerW &W = m->L[D.L];
+    const int d = D.d;
+    // eh = [enorm(embed[id]) | hnorm(prev_h)]: gather the embed rows into S.mx
+    if (k_embed_launch(m->embed, ids_dev, R, d, 1, S.mx, st)) return -1;
+    if (rmsnorm_rows_launch(S.mx, d, m->enorm, d, R, D.eps, S.eh, 2L * d, st)) return -1;
+    if (rmsnorm_rows_launch(prev_h, d, m->hnorm, d, R, D.eps, S.eh + d, 2L * d, st)) return -1;
+    GemvDesc g{};
+    g.W = m->eh_proj; g.x = S.eh; g.ldx = 2L * d; g.R = R; g.O = d; g.K = 2L * d; g.fp8 = 0;
+    g.y = S.mx; g.ldy = d; g.part = m->part; g.ticket = m->tick;
+    if (gemv_launch(g, st)) return -1;
+    if (rmsnorm_rows_launch(S.mx, d, W.input_norm, d, R, D.eps, S.mxn, d, st)) return -1;
+    if (dsa_launch(D, W.dsa, m->mtp_dsa, base_n, R, S, S.mxn, S.sub, m->part, m->tick, st)) return -1;
+    if (residual_add_launch(S.mx, S.sub, (long)R * d, st)) return -1;
+    if (rmsnorm_rows_launch(S.mx, d, W.post_norm, d, R, D.eps, S.mxn, d, st)) return -1;
+    if (moe_forward_launch(W.moe, S.mxn, d, R, S.sub, d, nullptr, st)) return -1;
+    if (residual_add_launch(S.mx, S.sub, (long)R * d, st)) return -1;
+    if (rmsnorm_rows_launch(S.mx, d, m->shared_norm, d, R, D.eps, S.oh, d, st)) return -1;
+    return lm_head(m, S.oh, R, m->ctl->mtp_picks, want_logits);
+}
+
+static bool ids_ok(const ApusGcudaModel *m, const int32_t *ids, size_t n, const char *what) {
+    for (size_t i = 0; i < n; i++)
+        if (ids[i] < 0 || ids[i] >= m->D.V) {
+            gcuda_set_error("%s: token id %d outside [0, %d)", what, (int)ids[i], m->D.V);
+            return false;
+        }
+    return true;
+}
+
+static int fail_ctl(ApusGcudaModel *m, const char *what) {
+    if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(m->st) != cudaSuccess)
+        return gcuda_check(cudaGetLastError(), what);
+    gcuda_set_error("%s failed", what);
+    return -1;
+}
+
+extern "C" int apus_gcuda_decode_batch(ApusGcudaModel *m, const int32_t *ids, size_t s, uint16_t *logits,
+                                       uint16_t *h_out, uint16_t *yn_out) {
+    const Dims &D = m->D;
+    if (s < 1 || s > MAXR) { gcuda_set_error("decode_batch: %zu rows (1..%d)", s, MAXR); return -1; }
+    if (!ids_ok(m, ids, s, "decode_batch")) return -1;
+    Ctl c = read_ctl(m);
+    if ((size_t)c.pos + s > (size_t)m->cap) { gcuda_set_error("decode_batch: capacity"); return -1; }
+    cudaMemcpyAsync(m->ids, ids, s * 4, cudaMemcpyHostToDevice, m->st);
+    if (main_forward(m, m->ids, (int)s, m->S.yn, logits != nullptr)) return fail_ctl(m, "decode_batch");
+    k_commit<<<1, 32, 0, m->st>>>(m->ctl, (int)s);
+    if (logits) cudaMemcpyAsync(logits, m->S.logits, s * D.V * 2, cudaMemcpyDeviceToHost, m->st);
+    if (h_out) cudaMemcpyAsync(h_out, m->S.h4, s * D.hc * D.d * 2, cudaMemcpyDeviceToHost, m->st);
+    if (yn_out) cudaMemcpyAsync(yn_out, m->S.yn, s * D.d * 2, cudaMemcpyDeviceToHost, m->st);
+    return gcuda_check(cudaStreamSynchronize(m->st), "decode_batch");
+}
+
+extern "C" int apus_gcuda_mtp_forward(ApusGcudaModel *m, const int32_t *ids, const uint16_t *prev_h, size_t s,
+                                      uint16_t *logits, uint16_t *out_h) {
+    const Dims &D = m->D;
+    if (!m->has_mtp) { gcuda_set_error("gmtp: model has no MTP block loaded"); return -1; }
+    if (s < 1 || s > MAXR) { gcuda_set_error("mtp_forward: %zu rows", s); return -1; }
+    if (!ids_ok(m, ids, s, "mtp_forward")) return -1;
+    Ctl c = read_ctl(m);
+    if ((size_t)c.mtp_n + s > (size_t)m->cap) { gcuda_set_error("mtp_forward: capacity"); return -1; }
+    cudaMemcpyAsync(m->ids, ids, s * 4, cudaMemcpyHostToDevice, m->st);
+    cudaMemcpyAsync(m->mtp_rows, prev_h, s * D.d * 2, cudaMemcpyHostToDevice, m->st);
+    if (mtp_forward(m, m->ids, m->mtp_rows, (int)s, &m->ctl->mtp_n, logits != nullptr))
+        return fail_ctl(m, "mtp_forward");
+    k_mtp_commit<<<1, 32, 0, m->st>>>(m->ctl, (int)s);
+    if (logits) cudaMemcpyAsync(logits, m->S.logits, s * D.V * 2, cudaMemcpyDeviceToHost, m->st);
+    if (out_h) cudaMemcpyAsync(out_h, m->S.oh, s * D.d * 2, cudaMemcpyDeviceToHost, m->st);
+    return gcuda_check(cudaStreamSynchronize(m->st), "mtp_forward");
+}
+
+// ---- speculative decoding --------------------------------------------------
+
+// D-1 chained single-row MTP forwards (c/gmtp.h:677-696): draft i from the
+// previous draft and the previous step's post-shared_head.norm hidden.
+static int draft_chain(ApusGcudaModel *m) {
+    const int D = m->depth, d = m->D.d;
+    k_chain_first<<<1, 32, 0, m->st>>>(m->ctl, m->ids);              // ids[0] = drafts[0]
+    for (int i = 1; i < D; i++) {
+        if (mtp_forward(m, m->ids, m->hmtp, 1, &m->ctl->chain_pos[i], false)) return -1;
+        k_copy_row<<<(d + 255) / 256, 256, 0, m->st>>>(m->S.oh, 0, d, m->hmtp);
+        k_chain_next<<<1, 32, 0, m->st>>>(m->ctl, i, m->ids);       // drafts[i] = pick
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+extern "C" int apus_gcuda_gspec_prefill(ApusGcudaModel *m, const int32_t *ids, size_t n) {
+    const Dims &D = m->D;
+    const int d = D.d;
+    if (!m->has_mtp) { gcuda_set_error("gspec: model has no MTP block loaded"); return -1; }
+    if (n < 1 || n > (size_t)m->cap) { gcuda_set_error("gspec_prefill: %zu prompt tokens", n); return -1; }
+    if (!ids_ok(m, ids, n, "gspec_prefill")) return -1;
+    if (apus_gcuda_model_reset(m)) return -1;
+    std::vector<int32_t> h(ids, ids + n);
+    // main model over the prompt in 8-row decode batches; keep every yn row
+    for (size_t t0 = 0; t0 < n; t0 += MAXR) {
+        const int k = (int)(n - t0 < MAXR ? n - t0 : MAXR);
+        cudaMemcpyAsync(m->ids, h.data() + t0, k * 4, cudaMemcpyHostToDevice, m->st);
+        if (main_forward(m, m->ids, k, m->yn_prompt + t0 * d, false)) return fail_ctl(m, "gspec_prefill");
+        k_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
+        if (t0 + k == n) k_set_held_from_pick<<<1, 32, 0, m->st>>>(m->ctl, k - 1);
+        cudaStreamSynchronize(m->st);
+    }
+    // a one-token prompt has no true pair: drafts stay 0 (c/gmtp.h:741-757)
+    if (n < 2) return gcuda_check(cudaStreamSynchronize(m->st), "gspec_prefill");
+    // MTP true-pair replay: (h_{t-1}, tok_t) for t = 1..n-1
+    for (size_t t0 = 1; t0 < n; t0 += MAXR) {
+        const int k = (int)(n - t0 < MAXR ? n - t0 : MAXR);
+        cudaMemcpyAsync(m->ids, h.data() + t0, k * 4, cudaMemcpyHostToDevice, m->st);
+        if (mtp_forward(m, m->ids, m->yn_prompt + (t0 - 1) * d, k, &m->ctl->mtp_n, false))
+            return fail_ctl(m, "gspec_prefill replay");
+        k_mtp_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
+        if (t0 + k == n) {
+            k_copy_row<<<(d + 255) / 256, 256, 0, m->st>>>(m->S.oh, k - 1, d, m->hmtp);
+            // drafts[0] = argmax of the last replay row
+            Ctl tmp = read_ctl(m);
+            tmp.drafts[0] = tmp.mtp_picks[k - 1];
+            for (int i = 1; i < MAXR; i++) tmp.chain_pos[i] = tmp.mtp_n + i - 1;
+            cudaMemcpy(m->ctl, &tmp, sizeof tmp, cudaMemcpyHostToDevice);
+        }
+        cudaStreamSynchronize(m->st);
+    }
+    // the hnorm input carried to the next step: yn of position n-1
+    k_copy_row<<<(d + 255) / 256, 256, 0, m->st>>>(m->yn_prompt, (long)n - 1, d, m->hcarry);
+    if (draft_chain(m)) return fail_ctl(m, "gspec_prefill chain");
+    k_force<<<1, 32, 0, m->st>>>(m->ctl, m->truth, m->depth, D.V);
+    return gcuda_check(cudaStreamSynchronize(m->st), "gspec_prefill");
+}
+
+// One verify step of Dp <= depth rows (fewer only at the capacity edge,
+// c/gmtp.h:783-786); the draft chain always runs the full depth.
+static int spec_step(ApusGcudaModel *m, int Dp) {
+    const Dims &D = m->D;
+    const int d = D.d;
+    cudaStream_t st = m->st;
+    k_spec_begin<<<1, 32, 0, st>>>(m->ctl, Dp, m->cap, m->ids);
+    if (main_forward(m, m->ids, Dp, m->S.yn, false)) return -1;
+    // MTP replay of the D candidate pairs (rows past the accepted prefix are
+    // overwritten by the chain / the next replay)
+    k_replay_rows<<<(Dp * d + 255) / 256, 256, 0, st>>>(m->hcarry, m->S.yn, Dp, d, m->mtp_rows);
+    if (mtp_forward(m, m->ids, m->mtp_rows, Dp, &m->ctl->mtp_n, false)) return -1;
+    k_spec_walk<<<1, 32, 0, st>>>(m->ctl, Dp, m->log, m->log_cap);
+    k_copy_sel_row<<<(d + 255) / 256, 256, 0, st>>>(m->S.oh, m->ctl, d, m->hmtp);
+    k_copy_sel_row<<<(d + 255) / 256, 256, 0, st>>>(m->S.yn, m->ctl, d, m->hcarry);
+    if (draft_chain(m)) return -1;
+    k_force<<<1, 32, 0, st>>>(m->ctl, m->truth, m->depth, D.V);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+extern "C" int apus_gcuda_gspec_step_async(ApusGcudaModel *m) {
+    if (!m->has_mtp) { gcuda_set_error("gspec: model has no MTP block loaded"); return -1; }
+    return spec_step(m, m->depth);
+}
+
+extern "C" int apus_gcuda_gspec_step(ApusGcudaModel *m, int *out, int cap) {
+    if (!m->has_mtp || cap < m->depth + 1) return 0;
+    Ctl c = read_ctl(m);
+    const int De = m->cap - c.pos < m->depth ? m->cap - c.pos : m->depth;
+    if (c.err || De <= 0) return 0;
+    if (spec_step(m, De)) { fail_ctl(m, "gspec_step"); return 0; }
+    c = read_ctl(m);
+    for (int i = 0; i < c.n_emitted; i++) out[i] = c.emitted[i];
+    return c.n_emitted;
+}
+
+extern "C" int apus_gcuda_gspec_emitted(ApusGcudaModel *m, int32_t *out, size_t cap) {
+    Ctl c = read_ctl(m);
+    const size_t n = (size_t)c.log_n < cap ? (size_t)c.log_n : cap;
+    if (n && gcuda_check(cudaMemcpy(out, m->log, n * 4, cudaMemcpyDeviceToHost), "emitted")) return -1;
+    return c.log_n;
+}
+
+extern "C" int apus_gcuda_gspec_stats(ApusGcudaModel *m, uint64_t *o) {
+    Ctl c = read_ctl(m);
+    o[0] = (uint64_t)c.stat_emitted; o[1] = (uint64_t)c.stat_batches; o[2] = (uint64_t)c.stat_offered;
+    o[3] = (uint64_t)c.stat_accepted; o[4] = (uint64_t)c.pos; o[5] = (uint64_t)(int64_t)c.held;
+    return c.err ? -1 : 0;
+}
+
+extern "C" int apus_gcuda_gspec_force(ApusGcudaModel *m, const int32_t *truth, size_t n, size_t base, double p,
+                                      uint64_t seed) {
+    Ctl c = read_ctl(m);
+    if (!truth) {
+        c.force_on = 0;
+        m->force.force_on = 0;
+    } else {
+        if (!m->truth) m->truth = (int32_t *)dmalloc(m, (size_t)m->log_cap * 4 + (size_t)m->cap * 4);
+        if (!m->truth || n > (size_t)m->cap + m->log_cap) { gcuda_set_error("gspec_force: truth too long"); return -1; }
+        if (!ids_ok(m, truth, n, "gspec_force")) return -1;
+        cudaMemcpy(m->truth, truth, n * 4, cudaMemcpyHostToDevice);
+        c.force_on = 1; c.force_base = (int)base; c.force_n = (int)n; c.force_p = p; c.force_seed = seed;
+        m->force = c;
+    }
+    return gcuda_check(cudaMemcpy(m->ctl, &c, sizeof c, cudaMemcpyHostToDevice), "gspec_force");
+}
+
+extern "C" int apus_gcuda_greedy(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen, int32_t *out) {
+    if (n < 1 || n_gen < 1 || n + (size_t)n_gen > (size_t)m->cap) { gcuda_set_error("greedy: capacity"); return -1; }
+    if (!ids_ok(m, ids, n, "greedy")) return -1;
+    if (apus_gcuda_model_reset(m)) return -1;
+    std::vector<int32_t> h(ids, ids + n);
+    for (size_t t0 = 0; t0 < n; t0 += MAXR) {
+        const int k = (int)(n - t0 < MAXR ? n - t0 : MAXR);
+        cudaMemcpyAsync(m->ids, h.data() + t0, k * 4, cudaMemcpyHostToDevice, m->st);
+        if (main_forward(m, m->ids, k, m->S.yn, false)) return fail_ctl(m, "greedy prefill");
+        k_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
+        if (t0 + k == n) k_set_held_from_pick<<<1, 32, 0, m->st>>>(m->ctl, k - 1);
+    }
+    for (int i = 0; i < n_gen; i++) {
+        k_greedy_prep<<<1, 32, 0, m->st>>>(m->ctl, m->ids);
+        if (i + 1 < n_gen) {
+            if (main_forward(m, m->ids, 1, m->S.yn, false)) return fail_ctl(m, "greedy");
+            k_commit<<<1, 32, 0, m->st>>>(m->ctl, 1);
+        }
+        k_greedy_post<<<1, 32, 0, m->st>>>(m->ctl, m->log, m->log_cap);
+    }
+    if (gcuda_check(cudaStreamSynchronize(m->st), "greedy")) return -1;
+    return gcuda_check(cudaMemcpy(out, m->log, (size_t)n_gen * 4, cudaMemcpyDeviceToHost), "greedy out");
+}
+
+extern "C" int apus_gcuda_model_debug_stop(ApusGcudaModel *m, int layer, int stage) {
+    m->dbg_layer = layer;
+    m->dbg_stage = stage;
+    return 0;
+}
+
+extern "C" int apus_gcuda_model_debug_read(ApusGcudaModel *m, const char *name, void *host, size_t bytes) {
+    const Scratch &S = m->S;
+    const struct { const char *n; const void *p; } tab[] = {
+        {"h4", S.h4}, {"h4b", S.h4b}, {"x", S.x}, {"sub", S.sub}, {"post", S.post}, {"comb", S.comb},
+        {"kp", S.kp}, {"qkvc", S.qkvc}, {"fgo", S.fgo}, {"core", S.core}, {"qkva", S.qkva}, {"q", S.q},
+        {"kvb", S.kvb}, {"iq", S.iq}, {"ikgw", S.ikgw}, {"attn", S.attn}, {"yn", S.yn}, {"mix", S.mix},
+        {"qres", S.qres}, {"kpass", S.kpass}, {"isel", S.isel}, {"iscore", S.iscore},
+    };
+    for (const auto &e : tab)
+        if (!strcmp(e.n, name)) {
+            cudaStreamSynchronize(m->st);
+            return gcuda_check(cudaMemcpy(host, e.p, bytes, cudaMemcpyDeviceToHost), "debug_read");
+        }
+    gcuda_set_error("debug_read: unknown buffer %s", name);
+    return -1;
+}
+
+extern "C" uint64_t apus_gcuda_state_digest(ApusGcudaModel *m) {
+    const Dims &D = m->D;
+    Ctl c = read_ctl(m);
+    uint64_t h = 14695981039346656037ull;
+    auto eat = [&](const void *dev, size_t bytes) {
+        std::vector<uint8_t> b(bytes);
+        cudaMemcpy(b.data(), dev, bytes, cudaMemcpyDeviceToHost);
+        for (uint8_t x : b) { h ^= x; h *= 1099511628211ull; }
+    };
+    for (int l = 0; l < D.L; l++) {
+        if (!m->L[l].is_dsa) {
+            const size_t cs = (size_t)3 * D.qkv * (D.K - 1) * 2, rs = (size_t)D.H * D.D * D.D * 4;
+            eat((uint8_t *)m->kda[l].conv + c.kda_cur * cs, cs);
+            eat((uint8_t *)m->kda[l].rec + c.kda_cur * rs, rs);
+        } else {
+            for (int hh = 0; hh < D.AH; hh++) {
+                eat(m->dsa[l].k + ((size_t)hh * m->cap) * D.qd, (size_t)c.pos * D.qd * 2);
+                eat(m->dsa[l].v + ((size_t)hh * m->cap) * D.vd, (size_t)c.pos * D.vd * 2);
+            }
+            eat(m->dsa[l].ik, (size_t)c.pos * D.ID * 2);
+        }
+    }
+    return h;
+}
+

@@ -1,0 +1,151 @@
+// model_dev.h — device-side descriptors of the glm5_next decode stack
+// (internal).  Every pointer is device memory.  R <= MAXR token rows per call.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gmoe_dev.h"
+
+#define MAXR 8            // rows of one forward (verify depth or prefill chunk)
+#define NSLOT (MAXR + 1)  // KDA checkpoint ring: committed state + MAXR provisional
+
+// Dimensions (field meaning of ApusGmodelConfig, c/gmodel.h:88-108).
+struct Dims {
+    int d, V, L, hc;
+    float eps, hc_eps, lower_bound, route_scale, limit;
+    int sinkhorn_iters;
+    int H, D, Dr, K;                  // KDA: heads, head dim, low rank, conv width
+    int qkv;                          // H*D
+    int AH, qd, vd, ql, kl;           // DSA MLA
+    int IH, ID, topk, kpool, tail;    // Lightning indexer
+    int E, ktop, inter, dense_inter;  // MoE / dense MLP
+};
+
+// KDA projection rows (q|k|v|f_a|g_a|b) and the row stride of their
+// scratch output, padded to 16 bytes so the low-rank f_b/g_b GEMV that reads
+// f_a|g_a from it stays on the bulk-copy path.
+inline int kda_nproj(const Dims &D) { return 3 * D.qkv + 2 * D.Dr + D.H; }
+inline int kda_ldkp(const Dims &D) { return (kda_nproj(D) + 7) & ~7; }
+
+// Control block of one sequence (device).  Positions are absolute.
+struct Ctl {
+    int pos;            // tokens committed to the main model
+    int kda_cur;        // checkpoint slot holding the committed KDA state
+    int mtp_n;          // tokens committed to the MTP block's caches
+    int held;           // sampled, not yet emitted token (speculative mode)
+    int matched;        // accepted drafts of the last step
+    int drafts[MAXR];   // d1..dD
+    int batch[MAXR];    // verify batch [held, d2..dD]
+    int picks[MAXR];    // argmax of each verify row
+    int emitted[MAXR + 1];
+    int n_emitted;
+    long long stat_emitted, stat_batches, stat_offered, stat_accepted;
+    int err;            // sticky error (capacity)
+    int log_n;          // tokens in the emitted-token log
+    int chain_pos[MAXR];// MTP cache position of each draft-chain step
+    int mtp_picks[MAXR];// argmax of each MTP row
+    int one;            // constant 1 (row count of single-row launches)
+    // forced draft agreement
+    int force_on, force_base, force_n;
+    unsigned long long force_seed;
+    double force_p;
+};
+
+struct KdaW {
+    const uint16_t *proj;     // [3*qkv + 2*Dr + H][d]: q | k | v | f_a | g_a | b
+    const uint16_t *fg_b;     // [2][qkv][Dr]: f_b | g_b
+    const uint16_t *conv;     // [3*qkv][K]
+    const float *A_log;       // [H]
+    const float *dt_bias;     // [qkv]
+    const uint16_t *o_norm;   // [D]
+    const uint16_t *o_w;      // [d][qkv]
+};
+
+struct DsaW {
+    const uint8_t *qkva_c;    // FP8 [ql + kl][d]: q_a | kv_a
+    const float *qkva_s;      // [(ql+kl)/128][d/128]
+    const uint16_t *q_a_norm, *kv_a_norm;
+    const uint8_t *q_b_c;     // FP8 [AH*qd][ql]
+    const float *q_b_s;
+    const uint16_t *kv_b;     // BF16 [AH*(qd+vd)][kl]
+    const uint8_t *o_c;       // FP8 [d][AH*vd]
+    const float *o_s;
+    const uint16_t *idx_wq_b; // BF16 [IH*ID][ql]
+    const uint16_t *idx_kgw;  // BF16 [2*ID + IH][d]: wk | compress_gate | weights_proj
+    const uint16_t *idx_knorm_w, *idx_knorm_b, *idx_ape;   // [ID], [ID], [kpool][ID]
+};
+
+struct LayerW {
+    int is_dsa, sparse;
+    const uint16_t *input_norm, *post_norm;
+    const uint16_t *hc_fn[2];       // BF16 [(2+hc)*hc][hc*d]
+    const float *hc_base[2], *hc_scale[2];
+    KdaW kda;
+    DsaW dsa;
+    MoeDev moe;                     // sparse layers (and the dense MLP as expert 0)
+};
+
+struct KdaState {
+    uint16_t *conv;   // [NSLOT][3*qkv][K-1]
+    float *rec;       // [NSLOT][H][D][D]
+};
+
+struct DsaState {
+    uint16_t *k, *v;  // [AH][cap][qd], [AH][cap][vd]
+    uint16_t *ik, *ig;// [cap][ID] indexer key (LayerNorm'd) / compress gate
+    uint16_t *pkey;   // [cap/kpool][ID] pool keys (BF16)
+    int cap;
+};
+
+// Per-forward scratch (device), sized for MAXR rows.
+struct Scratch {
+    uint16_t *h4, *h4b;     // [R][hc*d] residual streams (ping-pong)
+    uint16_t *x, *sub;      // [R][d]
+    float *rms;             // [R] inverse rms of the stream
+    float *mix;             // [R][(2+hc)*hc]
+    float *post, *comb;     // [R][hc], [R][hc*hc]
+    uint16_t *kp;           // KDA projections [R][3qkv+2Dr+H]
+    uint16_t *fgo;          // [2][R][qkv]  f_b, g_b outputs
+    uint16_t *qkvc;         // [R][3qkv] post-conv
+    uint16_t *core;         // [R][qkv] gated-normed core
+    uint16_t *qkva, *qres, *kpass;  // [R][ql+kl], [R][ql], [R][kl]
+    uint16_t *q;            // [R][AH*qd]
+    uint16_t *kvb;          // [R][AH*(qd+vd)]
+    uint16_t *iq;           // [R][IH*ID]
+    uint16_t *ikgw;         // [R][2ID+IH]
+    float *iscore;          // [R][maxpools]
+    uint8_t *isel;          // [R][maxpools] pool selected
+    uint16_t *attn;         // [R][AH*vd]
+    float *attn_scores;     // [AH][R][attn_sstride] attention scores
+    int attn_sstride;       // >= cache capacity
+    uint16_t *yn;           // [R][d] post-final-norm rows
+    uint16_t *logits;       // [R][V] (optional)
+    unsigned long long *amax;   // [R]
+    int32_t *ids;           // [R] token ids of this forward
+    // MTP glue
+    uint16_t *eh;           // [R][2d]
+    uint16_t *mx, *mxn;     // [R][d]
+    uint16_t *oh;           // [R][d] post-shared_head.norm rows
+    uint16_t *hprev;        // [R][d] hnorm inputs
+    int maxpools;
+};
+
+// ---- layer kernels (layers.cu) -------------------------------------------
+// Shape checks + kernel attributes for a model of dims D (once per model).
+int layers_prepare(const Dims &D);
+// All take the row count R and the device control block (positions).
+int k_embed_launch(const uint16_t *embed, const int32_t *ids, int R, int d, int hc, uint16_t *h4,
+                   cudaStream_t st);
+int hc_pre_launch(const Dims &D, const LayerW &W, int site, const uint16_t *h4, int R, Scratch &S,
+                  cudaStream_t st);       // -> S.x (normed with input/post norm), S.post/comb
+int hc_post_launch(const Dims &D, const uint16_t *x, const uint16_t *h4, int R, const Scratch &S,
+                   uint16_t *h4out, cudaStream_t st);
+int head_norm_launch(const Dims &D, const uint16_t *h4, const uint16_t *norm_w, int R, uint16_t *yn,
+                     cudaStream_t st);
+int rmsnorm_rows_launch(const uint16_t *x, long ldx, const uint16_t *w, int n, int R, float eps,
+                        uint16_t *y, long ldy, cudaStream_t st);
+int kda_launch(const Dims &D, const LayerW &W, KdaState &KS, const Ctl *ctl, int R, Scratch &S,
+               float *part, int *tick, cudaStream_t st);            // S.x -> S.sub
+int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, int R, Scratch &S,
+               const uint16_t *x, uint16_t *out, float *part, int *tick, cudaStream_t st);
+int residual_add_launch(uint16_t *x, const uint16_t *sub, long n, cudaStream_t st);

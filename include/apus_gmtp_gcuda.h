@@ -1,0 +1,130 @@
+/*
+ * apus_gmtp_gcuda.h — the glm5_next decode stack and the MTP speculative
+ * decode step on the B200, behind the reference's engine entry points
+ * (c/gmodel.h, c/gmtp.h).
+ *
+ * The reference's ApusGmodel is opaque and filled from its safetensors
+ * container (c/gmodel.h:622-1106); here the model is filled tensor by tensor
+ * under the same checkpoint names (or from seeded synthetic weights) and is
+ * resident in HBM.  ApusGcudaModel bundles what the reference splits over
+ * ApusGmodel + ApusGmodelState + ApusGmtp + ApusGmtpState + ApusGspec
+ * (c/gmodel.h:129-320, c/gmtp.h:123-259): one sequence, one stream.
+ *
+ * Numerics: every sublayer keeps the reference's rounding points; fp32
+ * summation orders differ where a GPU reduction replaces a sequential loop,
+ * so logits match the reference within tolerance, while inside this engine a
+ * verify row is bitwise the one-token decode of the same context.  The
+ * speculative stream is therefore bitwise the engine's own greedy stream.
+ * The greedy pick is c/sample.h:76-81 on the BF16 logits (lowest index wins
+ * ties), fused into the lm_head GEMV.
+ */
+#ifndef APUS_GMTP_GCUDA_H
+#define APUS_GMTP_GCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define APUS_GCUDA_MAX_LAYERS 64
+
+/* Field names and meaning of ApusGmodelConfig (c/gmodel.h:88-108); the two
+ * per-layer pattern arrays are inline (c/gmodel.h:344-350 rule or explicit). */
+typedef struct {
+    int hidden_size, vocab_size, num_hidden_layers;
+    float rms_norm_eps;
+    int hc_mult, hc_sinkhorn_iters;
+    float hc_eps;
+    int first_k_dense_replace;
+    int intermediate_size, moe_intermediate_size;
+    int n_routed_experts, n_shared_experts, num_experts_per_tok;
+    float routed_scaling_factor;
+    int norm_topk_prob;
+    float swiglu_limit;
+    int num_attention_heads, q_lora_rank, kv_lora_rank;
+    int qk_nope_head_dim, v_head_dim;
+    int index_n_heads, index_head_dim, index_topk, index_kpool;
+    int index_kpool_always_select_tail;
+    int linear_num_heads, linear_head_dim, linear_conv_kernel_dim;
+    float linear_lower_bound;
+    int num_nextn_predict_layers;
+    int layer_is_dsa[APUS_GCUDA_MAX_LAYERS];
+    int mlp_is_sparse[APUS_GCUDA_MAX_LAYERS];
+} ApusGcudaConfig;
+
+typedef struct ApusGcudaModel ApusGcudaModel;
+
+/* Model + one sequence state with kv_cap token positions and a speculative
+ * depth (verify rows per step, 1..8; the reference's APUS_SPEC_K).  has_mtp
+ * loads the NextN block as layer num_hidden_layers (c/gmodel.h:186-209).
+ * c/gmodel.h:161-164 (open2) + :244 (state_new) + c/gmtp.h:133,145,245. */
+ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int has_mtp, size_t kv_cap, int depth);
+void apus_gcuda_model_free(ApusGcudaModel *m);
+
+/* Tensor by checkpoint name (c/gmodel.h:622-1106 names, minus the
+ * "model.language_model." prefix), host pointer, synchronous. */
+int apus_gcuda_model_set(ApusGcudaModel *m, const char *name, const void *host, size_t bytes);
+int apus_gcuda_model_get(ApusGcudaModel *m, const char *name, void *host, size_t bytes);
+/* Seeded synthetic weights generated on the device (BASELINE distributions). */
+int apus_gcuda_model_init_random(ApusGcudaModel *m, uint64_t seed);
+/* Fresh sequence: position 0, all states zero. */
+int apus_gcuda_model_reset(ApusGcudaModel *m);
+size_t apus_gcuda_model_pos(const ApusGcudaModel *m);            /* c/gmodel.h:246 */
+
+/* c/gmodel.h:311-314 apus_gmodel_decode_batch: s <= 8 tokens at the current
+ * position, committed.  logits [s,V], h_out [s,hc*dim] (last-layer stream),
+ * yn_out [s,dim] (post-final-norm rows): host arrays, each may be NULL. */
+int apus_gcuda_decode_batch(ApusGcudaModel *m, const int32_t *ids, size_t s, uint16_t *logits,
+                            uint16_t *h_out, uint16_t *yn_out);
+
+/* c/gmtp.h:169-172 apus_gmtp_forward: s <= 8 pairs (ids[t], prev_h[t]) at the
+ * MTP block's current position, committed.  logits [s,V], out_h [s,dim]. */
+int apus_gcuda_mtp_forward(ApusGcudaModel *m, const int32_t *ids, const uint16_t *prev_h, size_t s,
+                           uint16_t *logits, uint16_t *out_h);
+
+/* c/gmtp.h:253 apus_gspec_prefill (greedy): prompt in 8-token decode
+ * batches, held token, MTP true-pair replay (postnorm source, lag 1,
+ * c/gmtp.h:99-119) and the first draft chain.  0 on success. */
+int apus_gcuda_gspec_prefill(ApusGcudaModel *m, const int32_t *ids, size_t n);
+/* c/gmtp.h:259 apus_gspec_step (greedy): one verify step entirely on the
+ * device (verify forward, accept walk, KDA checkpoint select + DSA rewind,
+ * MTP replay, draft chain); appends the emitted tokens to out (cap >=
+ * depth+1) and returns their count (0 at capacity). */
+int apus_gcuda_gspec_step(ApusGcudaModel *m, int *out, int cap);
+/* The same step enqueued on the model's stream without waiting (emitted
+ * tokens go to a device-resident log); gspec_emitted synchronises and copies
+ * up to cap logged tokens, returning how many were logged since prefill. */
+int apus_gcuda_gspec_step_async(ApusGcudaModel *m);
+int apus_gcuda_gspec_emitted(ApusGcudaModel *m, int32_t *out, size_t cap);
+/* Device-resident step counters (c/apus.c:1061-1075): emitted, batches,
+ * offered, accepted, position, held. */
+int apus_gcuda_gspec_stats(ApusGcudaModel *m, uint64_t *out6);
+/* Forced draft agreement (the reference's draft_override test hook,
+ * c/gmtp.h:211-215, generalised): after each chain, draft i for position
+ * q+i becomes truth[q+i-base] with probability p (splitmix64 of seed and the
+ * position), else (truth+1) mod V.  truth == NULL switches it off. */
+int apus_gcuda_gspec_force(ApusGcudaModel *m, const int32_t *truth, size_t n, size_t base, double p,
+                           uint64_t seed);
+
+/* Non-speculative greedy decode (the reference run loop's --no-spec path,
+ * c/apus.c:1079-1143): prefill ids[n], then n_gen argmax tokens into out. */
+int apus_gcuda_greedy(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen, int32_t *out);
+
+/* Digest (FNV-1a 64) of the committed KDA states and DSA caches (the
+ * rollback check of tests/m8g/test_m8g.c:383-424). */
+uint64_t apus_gcuda_state_digest(ApusGcudaModel *m);
+
+/* Inspection hooks (no reference counterpart; the reference dumps through
+ * its APUS_DEBUG logging): stop the main forward after (layer, stage) —
+ * stage 0 mHC pre (attn), 1 attention, 2 mHC post, 3 mHC pre (ffn), 4 MLP —
+ * and read a scratch buffer by name ("x", "sub", "h4", "h4b", "kp", "core",
+ * "q", "kvb", "attn", ...).  layer -1 clears the stop. */
+int apus_gcuda_model_debug_stop(ApusGcudaModel *m, int layer, int stage);
+int apus_gcuda_model_debug_read(ApusGcudaModel *m, const char *name, void *host, size_t bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
