@@ -104,6 +104,7 @@ __global__ void k_moe_route(MoeDev m, int R, const float *logits, const int32_t 
         slot_of[E] = p;
         m.prob_expert[p++] = E;            // shared expert, always last
         *m.prob_count = p;
+        if (m.stat_problems) atomicAdd(m.stat_problems, (unsigned long long)p);
     }
     __syncthreads();
     for (int i = threadIdx.x; i < R * K; i += blockDim.x)

@@ -26,6 +26,7 @@ struct MoeDev {
     int32_t *row_prob_shared;    // [max_r] problem slot of the shared expert
     int32_t *prob_expert;        // [max_r*topk+1] expert of each problem slot
     int32_t *prob_count;         // [1]
+    unsigned long long *stat_problems;   // optional: += expert problems (incl. shared) per call
     uint16_t *gu;                // [max_r*topk+1][max_r][2*inter]
     uint16_t *yd;                // [max_r*topk+1][max_r][dim]
 };

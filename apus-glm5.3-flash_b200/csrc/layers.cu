@@ -9,6 +9,7 @@
 #include "common.cuh"
 #include "gcuda.h"
 #include "model_dev.h"
+#include "pipe.cuh"
 
 namespace apus {
 
@@ -35,9 +36,60 @@ APUS_DEV float pw_sum_shared(const float *a, int n) {
     return ret;
 }
 
-// Block-parallel version: leaves of <= 128 summed by separate threads, the
-// combine tree walked by thread 0.  Bitwise equal to pw_sum_shared.
+// Levels of the numpy recursion when it is a perfect binary tree (every
+// halving of a length > 128 is a multiple of 8: 16384, 4096, 1536, 512, ...),
+// else -1.  Then the leaves are the 2^k equal runs of n >> k elements.
+APUS_DEV int pw_perfect_levels(int n) {
+    int k = 0;
+    while ((n >> k) > 128) {
+        if ((n >> k) & 15) return -1;
+        k++;
+    }
+    return k;
+}
+
+// Block-parallel numpy pairwise sum, bitwise equal to pw_sum_shared.  A
+// perfect tree: leaves by separate threads, then the pairs of each level
+// combined left + right in parallel.  Otherwise the leaf table and the
+// combine walk run on thread 0.
 APUS_DEV float block_pw(const float *a, int n, float *leaf_buf, float *out_sh) {
+    const int lv = pw_perfect_levels(n);
+    if (lv >= 0 && lv <= 8) {
+        const int nl = 1 << lv, L = n >> lv;
+        if (L % 8 == 0 && (blockDim.x & 31) == 0) {
+            // 8 lanes per leaf: lane k runs the leaf's k-th accumulator
+            // (a[k], a[8+k], ... in order), then the fixed combine
+            // ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) by shuffles (fp32 addition
+            // is commutative, so a lane pair adds to the same bits either way)
+            const int k = threadIdx.x & 7;
+            for (int g0 = 0; g0 < nl; g0 += blockDim.x / 8) {
+                const int g = g0 + (int)threadIdx.x / 8;
+                float r = 0.f;
+                if (g < nl) {
+                    const float *lf = a + (size_t)g * L;
+                    r = lf[k];
+                    for (int i = 8; i < L; i += 8) r += lf[i + k];
+                }
+                r += __shfl_xor_sync(0xffffffffu, r, 1);
+                r += __shfl_xor_sync(0xffffffffu, r, 2);
+                r += __shfl_xor_sync(0xffffffffu, r, 4);
+                if (g < nl && k == 0) leaf_buf[g] = r;
+            }
+        } else {
+            for (int i = threadIdx.x; i < nl; i += blockDim.x) leaf_buf[i] = pw_sum_leaf(a + (size_t)i * L, L);
+        }
+        __syncthreads();
+        for (int s = 1; s < nl; s <<= 1) {
+            for (int q = threadIdx.x; q < nl / (2 * s); q += blockDim.x) {
+                const int i = 2 * s * q;
+                leaf_buf[i] = leaf_buf[i] + leaf_buf[i + s];
+            }
+            __syncthreads();
+        }
+        const float r = leaf_buf[0];
+        __syncthreads();
+        return r;
+    }
     // leaf k covers the k-th <=128 piece in left-to-right order of the recursion
     __shared__ int leaf_off[256], leaf_len[256], nleaf;
     if (threadIdx.x == 0) {
@@ -107,50 +159,48 @@ __global__ void k_embed(const uint16_t *embed, const int32_t *ids, int d, int hc
 
 // --------------------------------------------------------------------- mHC
 
-// inverse RMS of the flattened streams (c/gmhc.h:187-195): one CTA per row
-__global__ void k_hc_rms(const uint16_t *h4, int n, float eps, float *rms) {
-    extern __shared__ float sq[];
-    __shared__ float leaf[256], res;
-    const uint16_t *x = h4 + (size_t)blockIdx.x * n;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = bf16_f32(x[i]);
-        sq[i] = v * v;
-    }
-    __syncthreads();
-    const float var = block_pw(sq, n, leaf, &res) / (float)n;
-    if (threadIdx.x == 0) rms[blockIdx.x] = 1.0f / sqrtf(var + eps);
-}
-
-// mixes[r][j] = sum_i fn[j][i] * (x4[r][i] * inv[r])  (c/gmhc.h:248-258),
-// fp32, fixed per-thread strides + fixed tree: one CTA per (j, r).
-__global__ void k_hc_mix(const uint16_t *fn, const uint16_t *h4, const float *rms, int n, int nmix,
-                         float *mix) {
-    const int j = blockIdx.x, r = blockIdx.y;
-    const float inv = rms[r];
-    const uint16_t *f = fn + (size_t)j * n, *x = h4 + (size_t)r * n;
-    float acc = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) acc += bf16_f32(f[i]) * (bf16_f32(x[i]) * inv);
-    __shared__ float red[256];
-    red[threadIdx.x] = acc;
-    __syncthreads();
-    for (int s = blockDim.x / 2; s; s >>= 1) {
-        if ((int)threadIdx.x < s) red[threadIdx.x] = red[threadIdx.x] + red[threadIdx.x + s];
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) mix[(size_t)r * nmix + j] = red[0];
-}
-
-// gates + Sinkhorn (c/gmhc.h:197-265), collapse (:267-276) and the layer's
-// weighted RMSNorm (c/gdsa.h:258-274): one CTA per row.
-__global__ void k_hc_maps(const uint16_t *h4, const float *mix, const float *scale, const float *base,
-                          const uint16_t *norm_w, int d, int hc, int iters, float hc_eps, float eps,
-                          float *post_out, float *comb_out, uint16_t *x_out) {
-    extern __shared__ float ys[];           // [d] collapsed + [d] squares
-    float *sq = ys + d;
-    __shared__ float pre[8], post[8], comb[64], leaf[256], res;
-    const int r = blockIdx.x, nmix = (2 + hc) * hc;
-    const float *m = mix + (size_t)r * nmix;
-    if (threadIdx.x == 0) {
+// Gates + Sinkhorn of one row from its mixes m[(2+hc)*hc] (c/gmhc.h:197-265):
+// pre, post and comb into shared arrays and post/comb into the row's outputs.
+// One warp when hc*hc <= 32 (lane (j,k) owns comb[j][k]), else thread 0.
+APUS_DEV void hc_maps(const float *m, const float *scale, const float *base, int hc, int iters, float hc_eps,
+                      int r, float *pre, float *post, float *comb, float *post_out, float *comb_out) {
+    if (hc * hc <= 32 && threadIdx.x < 32) {
+        // one warp: lane (j, k) = (lane / hc, lane % hc) owns comb[j][k]; every
+        // sum runs in the reference's sequential order (hc < 8) via shuffles
+        const int lane = threadIdx.x, j = lane / hc, k = lane % hc;
+        const bool act = lane < hc * hc;
+        if (lane < hc) {
+            pre[lane] = sigmoid_np(m[lane] * scale[0] + base[lane]) + hc_eps;
+            post[lane] = 2.0f * sigmoid_np(m[hc + lane] * scale[1] + base[hc + lane]);
+        }
+        float c = act ? m[2 * hc + lane] * scale[2] + base[2 * hc + lane] : 0.f;
+        const int rb = act ? j * hc : 0, cb = act ? k : 0;
+        float mx = __shfl_sync(0xffffffffu, c, rb);
+        for (int q = 1; q < hc; q++) {
+            const float v = __shfl_sync(0xffffffffu, c, rb + q);
+            if (v > mx) mx = v;
+        }
+        c = expf(c - mx);
+        float sum = __shfl_sync(0xffffffffu, c, rb);
+        for (int q = 1; q < hc; q++) sum += __shfl_sync(0xffffffffu, c, rb + q);
+        c = c / sum + hc_eps;
+        for (int it = 0; it < iters; it++) {
+            if (it) {
+                float den = __shfl_sync(0xffffffffu, c, rb);
+                for (int q = 1; q < hc; q++) den += __shfl_sync(0xffffffffu, c, rb + q);
+                c /= den + hc_eps;
+            }
+            float cs = __shfl_sync(0xffffffffu, c, cb);
+            for (int q = 1; q < hc; q++) cs += __shfl_sync(0xffffffffu, c, q * hc + cb);
+            c /= cs + hc_eps;
+        }
+        if (act) {
+            comb[lane] = c;
+            comb_out[r * hc * hc + lane] = c;
+        }
+        __syncwarp();
+        if (lane < hc) post_out[r * hc + lane] = post[lane];
+    } else if (hc * hc > 32 && threadIdx.x == 0) {
         for (int j = 0; j < hc; j++) pre[j] = sigmoid_np(m[j] * scale[0] + base[j]) + hc_eps;
         for (int j = 0; j < hc; j++) post[j] = 2.0f * sigmoid_np(m[hc + j] * scale[1] + base[hc + j]);
         for (int j = 0; j < hc; j++)
@@ -182,11 +232,74 @@ __global__ void k_hc_maps(const uint16_t *h4, const float *mix, const float *sca
         for (int j = 0; j < hc; j++) post_out[r * hc + j] = post[j];
         for (int j = 0; j < hc * hc; j++) comb_out[r * hc * hc + j] = comb[j];
     }
+}
+
+// mHC pre-mix of one row, fused (c/gmhc.h:187-276 then c/gdsa.h:258-274):
+// the inverse RMS of the flattened hc*d streams, the (2+hc)*hc mixes
+// (fp32, never rounded), gates + Sinkhorn, the collapse
+// bf16(sum_j pre_j h_j) and the layer's weighted RMSNorm.  One CTA of 512
+// threads per row; dynamic smem = max(hc*d, 2*d) floats.
+__global__ void __launch_bounds__(512) k_hc_pre(const uint16_t *h4, const uint16_t *fn, const float *scale,
+                                                const float *base, const uint16_t *norm_w, int d, int hc,
+                                                int iters, float hc_eps, float eps, float *post_out,
+                                                float *comb_out, uint16_t *x_out) {
+    extern __shared__ float fl[];
+    __shared__ float mixs[80], pre[8], post[8], comb[64], leaf[256], res;
+    const int r = blockIdx.x, n = hc * d, nmix = (2 + hc) * hc;
+    const uint16_t *x = h4 + (size_t)r * n;
+    // squares -> pairwise mean (c/gmhc.h:187-195)
+    for (int i = threadIdx.x * 8; i < n; i += blockDim.x * 8) {
+        const uint4 v = *(const uint4 *)(x + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float lo = bf16lo(w[e]), hi = bf16hi(w[e]);
+            fl[i + 2 * e] = lo * lo;
+            fl[i + 2 * e + 1] = hi * hi;
+        }
+    }
     __syncthreads();
-    const uint16_t *x4 = h4 + (size_t)r * hc * d;
+    const float inv = 1.0f / sqrtf(block_pw(fl, n, leaf, &res) / (float)n + eps);
+    // flat = x * inv, then mixes[j] = sum_i fn[j][i] * flat[i]: warp per mix,
+    // lanes over 8-element chunks, fixed shuffle tree
+    for (int i = threadIdx.x * 8; i < n; i += blockDim.x * 8) {
+        const uint4 v = *(const uint4 *)(x + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            fl[i + 2 * e] = bf16lo(w[e]) * inv;
+            fl[i + 2 * e + 1] = bf16hi(w[e]) * inv;
+        }
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+    for (int j = warp; j < nmix; j += nwarp) {
+        const uint16_t *f = fn + (size_t)j * n;
+        float acc = 0.f;
+        for (int c = lane * 8; c < n; c += 256) {
+            const uint4 wv = __ldg((const uint4 *)(f + c));
+            const float4 a = *(const float4 *)(fl + c), b = *(const float4 *)(fl + c + 4);
+            acc += bf16lo(wv.x) * a.x;
+            acc += bf16hi(wv.x) * a.y;
+            acc += bf16lo(wv.y) * a.z;
+            acc += bf16hi(wv.y) * a.w;
+            acc += bf16lo(wv.z) * b.x;
+            acc += bf16hi(wv.z) * b.y;
+            acc += bf16lo(wv.w) * b.z;
+            acc += bf16hi(wv.w) * b.w;
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) mixs[j] = acc;
+    }
+    __syncthreads();
+    hc_maps(mixs, scale, base, hc, iters, hc_eps, r, pre, post, comb, post_out, comb_out);
+    __syncthreads();
+    // collapse (c/gmhc.h:267-276) + the layer norm, reusing the smem
+    float *ys = fl, *sq = fl + d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        float acc = pre[0] * bf16_f32(x4[i]);
-        for (int j = 1; j < hc; j++) acc += pre[j] * bf16_f32(x4[(size_t)j * d + i]);
+        float acc = pre[0] * bf16_f32(x[i]);
+        for (int j = 1; j < hc; j++) acc += pre[j] * bf16_f32(x[(size_t)j * d + i]);
         ys[i] = bf16_round(acc);
     }
     __syncthreads();
@@ -342,18 +455,22 @@ __global__ void __launch_bounds__(D) k_kda_rec(const uint16_t *qkvc, const uint1
 // --------------------------------------------------------------------- DSA
 
 // Append this call's rows to the caches at base+t (c/gdsa.h:612-626 for K/V,
-// :329-334 for the indexer key LayerNorm and compress gate).
+// :329-334 for the indexer key LayerNorm and compress gate).  Grid (R, AH):
+// block (t, h) copies head h's K and V rows with 16-byte moves; block (t, 0)
+// also writes the indexer rows.
 __global__ void k_dsa_append(const uint16_t *kvb, const uint16_t *ikgw, const uint16_t *knw, const uint16_t *knb,
                              const int *base_n, int AH, int qd, int vd, int ID, int IH, int cap, DsaState ds) {
-    const int t = blockIdx.x;
+    const int t = blockIdx.x, h = blockIdx.y;
     const int pos = *base_n + t;
     if (pos >= cap) return;
-    const uint16_t *row = kvb + (size_t)t * AH * (qd + vd);
-    for (int q = threadIdx.x; q < AH * (qd + vd); q += blockDim.x) {
-        const int h = q / (qd + vd), e = q % (qd + vd);
-        if (e < qd) ds.k[((size_t)h * cap + pos) * qd + e] = row[q];
-        else ds.v[((size_t)h * cap + pos) * vd + (e - qd)] = row[q];
+    const uint16_t *row = kvb + (size_t)t * AH * (qd + vd) + (size_t)h * (qd + vd);
+    uint16_t *kd = ds.k + ((size_t)h * cap + pos) * qd, *vdst = ds.v + ((size_t)h * cap + pos) * vd;
+    for (int i = threadIdx.x; i < (qd + vd) / 8; i += blockDim.x) {
+        const uint4 v = *(const uint4 *)(row + i * 8);
+        if (i < qd / 8) *(uint4 *)(kd + i * 8) = v;
+        else *(uint4 *)(vdst + (i * 8 - qd)) = v;
     }
+    if (h != 0) return;
     // LayerNorm of the indexer key (c/gdsa.h:276-305, eps 1e-6)
     __shared__ float xs[256], d2[256], leaf[256], res;
     const uint16_t *ir = ikgw + (size_t)t * (2 * ID + IH);
@@ -396,27 +513,38 @@ __global__ void k_dsa_pool(const uint16_t *ape, const int *base_n, int R, int ID
 }
 
 // Indexer scores (c/gdsa.h:376-403) for every pool visible to row t:
-// sc = sum_h w_h * relu((idx_q[h] . key[p]) * ID^-0.5), w_h = bf16(wproj x) * IH^-0.5
-__global__ void k_dsa_score(const uint16_t *iq, const uint16_t *ikgw, const int *base_n, int IH, int ID, int kp,
-                            int maxpools, DsaState ds, float *score) {
+// sc = sum_h w_h * relu((idx_q[h] . key[p]) * ID^-0.5), w_h = bf16(wproj x) * IH^-0.5.
+// 256 threads = 8 pools x 32 heads: thread (pool, h) runs the reference's
+// sequential ID-long dot, then one thread per pool sums the heads in order.
+// Grid (ceil(maxpools / 8), R); blocks past the visible pools exit.
+__global__ void __launch_bounds__(256) k_dsa_score(const uint16_t *iq, const uint16_t *ikgw, const int *base_n,
+                                                   int IH, int ID, int kp, int maxpools, DsaState ds, float *score) {
     const int t = blockIdx.y;
     const int qpos = *base_n + t;
-    const int nvalid = (qpos + 1) / kp;
+    const int nvalid = min((qpos + 1) / kp, maxpools);
+    const int p0 = blockIdx.x * 8;
+    if (p0 >= nvalid) return;
     const float idx_scale = (float)(1.0 / sqrt((double)ID)), ih_scale = (float)(1.0 / sqrt((double)IH));
-    __shared__ float qs[32 * 128 + 32];
-    for (int i = threadIdx.x; i < IH * ID; i += blockDim.x) qs[i] = bf16_f32(iq[(size_t)t * IH * ID + i]);
+    __shared__ float qs[32 * 129];          // [h][ID] with a one-float pad per head
+    __shared__ float wh[32], wsc[8][32];
+    for (int i = threadIdx.x; i < IH * ID; i += blockDim.x)
+        qs[(i / ID) * (ID + 1) + i % ID] = bf16_f32(iq[(size_t)t * IH * ID + i]);
     for (int h = threadIdx.x; h < IH; h += blockDim.x)
-        qs[IH * ID + h] = bf16_f32(ikgw[(size_t)t * (2 * ID + IH) + 2 * ID + h]) * ih_scale;
+        wh[h] = bf16_f32(ikgw[(size_t)t * (2 * ID + IH) + 2 * ID + h]) * ih_scale;
     __syncthreads();
-    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < nvalid && p < maxpools; p += gridDim.x * blockDim.x) {
+    const int pl = threadIdx.x >> 5, h = threadIdx.x & 31, p = p0 + pl;
+    if (p < nvalid && h < IH) {
         const uint16_t *key = ds.pkey + (size_t)p * ID;
+        const float *qh = qs + h * (ID + 1);
+        float dot = 0.f;
+        for (int i = 0; i < ID; i++) dot += qh[i] * bf16_f32(key[i]);
+        const float v = dot * idx_scale;
+        wsc[pl][h] = wh[h] * (v > 0.f ? v : 0.f);
+    }
+    __syncthreads();
+    if (h == 0 && p < nvalid) {
         float acc = 0.f;
-        for (int h = 0; h < IH; h++) {
-            float dot = 0.f;
-            for (int i = 0; i < ID; i++) dot += qs[h * ID + i] * bf16_f32(key[i]);
-            const float v = dot * idx_scale;
-            acc += qs[IH * ID + h] * (v > 0.f ? v : 0.f);
-        }
+        for (int hh = 0; hh < IH; hh++) acc += wsc[pl][hh];
         score[(size_t)t * maxpools + p] = acc;
     }
 }
@@ -444,52 +572,98 @@ __global__ void k_dsa_select(const float *score, const int *base_n, int kp, int 
 // head handles every row, so each K/V row is read once per call.
 //   sc = bf16(bf16(q.k) * qd^-0.5); p = bf16(softmax(sc)); o = bf16(sum p v)
 // Visibility of position j for row t: j <= base+t and (its pool is
-// selected, or j is in the row's incomplete tail pool).
+// selected, or j is in the row's incomplete tail pool).  Row t's output sums
+// p_j v_j over every j <= base+t in ascending order with p_j = 0 where j is
+// not visible, as the reference's one-token decode does over its n = base+t+1
+// cache rows; so a row's result does not depend on the other rows of the call.
+// K and V stream through shared memory in tiles of ATJ positions, double
+// buffered with cp.async; dynamic smem = dsa_attn_smem(qd, vd).
+#define ATJ 64
 __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd,
                                                   int vd, int kp, int maxpools, const uint8_t *sel, DsaState ds,
                                                   float *sbuf, int sstride, uint16_t *out) {
+    extern __shared__ __align__(16) uint8_t dsm[];
     const int h = blockIdx.x;
     const int base = *base_n;
     const int nmax = base + R;            // positions that exist after this call's append
+    const int nt = (nmax + ATJ - 1) / ATJ;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int wmax = qd > vd ? qd : vd;
+    auto tile = [&](int b) { return (uint16_t *)dsm + b * ATJ * wmax; };
+    auto ptile = [&](int b) { return (float *)(dsm + 4 * ATJ * wmax) + b * MAXR * ATJ; };
     const float scale = (float)(1.0 / sqrt((double)qd));
-    float *sc = sbuf + (size_t)h * R * sstride;       // [R][sstride] scores (global scratch)
+    float *sc = sbuf + (size_t)h * R * sstride;       // [R][sstride] scores, then probabilities
     __shared__ float qsh[MAXR][256];
+    __shared__ int tail_s[MAXR];
+    __shared__ float red[256];
     for (int i = threadIdx.x; i < R * qd; i += blockDim.x)
         qsh[i / qd][i % qd] = bf16_f32(q[(size_t)(i / qd) * AH * qd + (size_t)h * qd + i % qd]);
-    __syncthreads();
+    if (threadIdx.x < R) {
+        const int vis = base + threadIdx.x + 1;
+        tail_s[threadIdx.x] = vis - vis % kp;
+    }
     auto visible = [&](int t, int j) -> bool {
-        const int qpos = base + t;
-        if (j > qpos) return false;
-        const int vis = qpos + 1, tc = vis % kp, ts = vis - tc;
-        if (j >= ts) return true;
+        if (j > base + t) return false;
+        if (j >= tail_s[t]) return true;
         const int p = j / kp;
         return p < maxpools && sel[(size_t)t * maxpools + p];
     };
-    // scores: one warp per position, lanes split the qd dims (fixed tree)
-    for (int j = warp; j < nmax; j += nw) {
-        bool any = false;
-        for (int t = 0; t < R; t++) any |= visible(t, j);
-        if (!any) continue;
-        const uint16_t *kr = ds.k + ((size_t)h * ds.cap + j) * qd;
-        float kv[8];
-        for (int e = 0; e < qd / 32; e++) kv[e] = bf16_f32(kr[lane + 32 * e]);
-        for (int t = 0; t < R; t++) {
-            if (!visible(t, j)) continue;
-            float acc = 0.f;
-            for (int e = 0; e < qd / 32; e++) acc += qsh[t][lane + 32 * e] * kv[e];
-#pragma unroll
-            for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-            if (lane == 0) sc[(size_t)t * sstride + j] = bf16_round(bf16_round(acc) * scale);
+    // stage rows [ti*ATJ, ti*ATJ + ATJ) of a [cap][w] cache (rows past nmax
+    // clamp to the last one; they are never used) and optionally the rows'
+    // probabilities
+    auto stage = [&](const uint16_t *cache, int w, int ti, int buf, bool probs) {
+        const int j0 = ti * ATJ, vpr = w / 8;
+        for (int i = threadIdx.x; i < ATJ * vpr; i += blockDim.x) {
+            const int jj = i / vpr, c = i % vpr;
+            const int j = min(j0 + jj, nmax - 1);
+            cp_async16(tile(buf) + jj * w + c * 8, cache + ((size_t)h * ds.cap + j) * w + c * 8);
         }
-    }
+        if (probs)
+            for (int i = threadIdx.x; i < R * (ATJ / 4); i += blockDim.x) {
+                const int t = i / (ATJ / 4), c = i % (ATJ / 4);
+                cp_async16(ptile(buf) + t * ATJ + c * 4, sc + (size_t)t * sstride + j0 + c * 4);
+            }
+        cp_async_commit();
+    };
     __syncthreads();
-    // softmax per row over its visible positions (fixed-order block reductions)
-    __shared__ float red[256], mxs[MAXR], sums[MAXR];
+    // scores: one warp per position, lanes split the qd dims (fixed tree)
+    const int ne = qd / 32;
+    stage(ds.k, qd, 0, 0, false);
+    for (int ti = 0; ti < nt; ti++) {
+        if (ti + 1 < nt) stage(ds.k, qd, ti + 1, (ti + 1) & 1, false);
+        else cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        const uint16_t *kt = tile(ti & 1);
+        for (int jj = warp; jj < ATJ; jj += nw) {
+            const int j = ti * ATJ + jj;
+            if (j >= nmax) break;
+            bool any = false;
+            for (int t = 0; t < R; t++) any |= visible(t, j);
+            if (!any) continue;
+            float kv[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) kv[e] = e < ne ? bf16_f32(kt[jj * qd + lane + 32 * e]) : 0.f;
+            for (int t = 0; t < R; t++) {
+                if (!visible(t, j)) continue;
+                float acc = 0.f;
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                    if (e < ne) acc += qsh[t][lane + 32 * e] * kv[e];
+#pragma unroll
+                for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+                if (lane == 0) sc[(size_t)t * sstride + j] = bf16_round(bf16_round(acc) * scale);
+            }
+        }
+        __syncthreads();
+    }
+    // softmax per row over its visible positions (fixed-order block
+    // reductions), stored back as p = bf16(e / sum) with 0 for the rest
     for (int t = 0; t < R; t++) {
+        float *srow = sc + (size_t)t * sstride;
         float m = -3.4028234663852886e+38f;
         for (int j = threadIdx.x; j <= base + t; j += blockDim.x)
-            if (visible(t, j)) m = fmaxf(m, sc[(size_t)t * sstride + j]);
+            if (visible(t, j)) m = fmaxf(m, srow[j]);
         red[threadIdx.x] = m;
         __syncthreads();
         for (int s = blockDim.x / 2; s; s >>= 1) {
@@ -501,8 +675,8 @@ __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *
         float su = 0.f;
         for (int j = threadIdx.x; j <= base + t; j += blockDim.x)
             if (visible(t, j)) {
-                const float e = expf(sc[(size_t)t * sstride + j] - mx);
-                sc[(size_t)t * sstride + j] = e;
+                const float e = expf(srow[j] - mx);
+                srow[j] = e;
                 su += e;
             }
         red[threadIdx.x] = su;
@@ -511,19 +685,40 @@ __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *
             if ((int)threadIdx.x < s) red[threadIdx.x] = red[threadIdx.x] + red[threadIdx.x + s];
             __syncthreads();
         }
-        if (threadIdx.x == 0) { mxs[t] = mx; sums[t] = red[0]; }
+        const float sum = red[0];
+        for (int j = threadIdx.x; j <= base + t; j += blockDim.x)
+            srow[j] = visible(t, j) ? bf16_round(srow[j] / sum) : 0.f;
         __syncthreads();
     }
-    // o[t][dv] = bf16(sum_j bf16(e_j / sum) * v_j[dv]), ascending j
-    for (int dv = threadIdx.x; dv < vd; dv += blockDim.x) {
-        float acc[MAXR];
-        for (int t = 0; t < R; t++) acc[t] = 0.f;
-        for (int j = 0; j < nmax; j++) {
-            const float vj = bf16_f32(ds.v[((size_t)h * ds.cap + j) * vd + dv]);
-            for (int t = 0; t < R; t++)
-                if (visible(t, j)) acc[t] += bf16_round(sc[(size_t)t * sstride + j] / sums[t]) * vj;
+    // o[t][dv] = bf16(sum_{j <= base+t} p_j * v_j[dv]), ascending j
+    float acc[MAXR];
+#pragma unroll
+    for (int t = 0; t < MAXR; t++) acc[t] = 0.f;
+    const int dv = threadIdx.x;               // vd <= blockDim.x
+    stage(ds.v, vd, 0, 0, true);
+    for (int ti = 0; ti < nt; ti++) {
+        if (ti + 1 < nt) stage(ds.v, vd, ti + 1, (ti + 1) & 1, true);
+        else cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        const uint16_t *vt = tile(ti & 1);
+        const float *pt = ptile(ti & 1);
+        if (dv < vd) {
+            const int jn = min(ATJ, nmax - ti * ATJ);
+            for (int jj = 0; jj < jn; jj++) {
+                const int j = ti * ATJ + jj;
+                const float vj = bf16_f32(vt[jj * vd + dv]);
+#pragma unroll
+                for (int t = 0; t < MAXR; t++)
+                    if (t < R && j <= base + t) acc[t] += pt[t * ATJ + jj] * vj;
+            }
         }
-        for (int t = 0; t < R; t++) out[(size_t)t * AH * vd + (size_t)h * vd + dv] = bf16_bits(acc[t]);
+        __syncthreads();
+    }
+    if (dv < vd) {
+#pragma unroll
+        for (int t = 0; t < MAXR; t++)
+            if (t < R) out[(size_t)t * AH * vd + (size_t)h * vd + dv] = bf16_bits(acc[t]);
     }
 }
 
@@ -532,6 +727,16 @@ __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *
 using namespace apus;
 
 static int ok_launch() { return cudaGetLastError() == cudaSuccess ? 0 : -1; }
+
+static size_t hc_pre_smem(const Dims &D) {
+    const int n = D.hc * D.d > 2 * D.d ? D.hc * D.d : 2 * D.d;
+    return (size_t)n * 4;
+}
+
+static size_t dsa_attn_smem(const Dims &D) {
+    const int w = D.qd > D.vd ? D.qd : D.vd;
+    return (size_t)2 * ATJ * w * 2 + (size_t)2 * MAXR * ATJ * 4;
+}
 
 // Leaves of the numpy pairwise recursion over n (what block_pw's 256-entry
 // leaf table must hold).
@@ -545,13 +750,17 @@ int layers_prepare(const Dims &D) {
     const int rows[] = {D.hc * D.d, D.d, D.ql, D.kl, D.ID, D.D};
     for (int n : rows)
         if (n > 0 && pw_leaves(n) > 256) return -1;
-    if (D.K < 2 || D.K > 9 || D.kpool > 16 || D.qd > 256 || D.IH * D.ID > 32 * 128) return -1;
+    if (D.K < 2 || D.K > 9 || D.kpool > 16 || D.qd > 256 || D.vd > 256 || D.qd % 32 || D.vd % 8 ||
+        D.IH * D.ID > 32 * 128)
+        return -1;
+    if (cudaFuncSetAttribute(k_dsa_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsa_attn_smem(D)))
+        return -1;
     // row kernels keep one or two fp32 copies of the row in dynamic smem
     const int maxrow = D.d > D.ql ? (D.d > D.kl ? D.d : D.kl) : (D.ql > D.kl ? D.ql : D.kl);
     const size_t need_rms = (size_t)D.hc * D.d * 4, need_row = (size_t)2 * maxrow * 4;
     if (need_rms > 200 * 1024 || need_row > 200 * 1024) return -1;
-    if (cudaFuncSetAttribute(k_hc_rms, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_rms) ||
-        cudaFuncSetAttribute(k_hc_maps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
+    if (D.d % 8 || D.hc * D.hc > 64 || (2 + D.hc) * D.hc > 80 || hc_pre_smem(D) > 200 * 1024) return -1;
+    if (cudaFuncSetAttribute(k_hc_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hc_pre_smem(D)) ||
         cudaFuncSetAttribute(k_head_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
         cudaFuncSetAttribute(k_rmsnorm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row))
         return -1;
@@ -565,12 +774,9 @@ int k_embed_launch(const uint16_t *embed, const int32_t *ids, int R, int d, int 
 
 int hc_pre_launch(const Dims &D, const LayerW &W, int site, const uint16_t *h4, int R, Scratch &S,
                   cudaStream_t st) {
-    const int n = D.hc * D.d, nmix = (2 + D.hc) * D.hc;
-    k_hc_rms<<<R, 512, n * sizeof(float), st>>>(h4, n, D.eps, S.rms);
-    k_hc_mix<<<dim3(nmix, R), 256, 0, st>>>(W.hc_fn[site], h4, S.rms, n, nmix, S.mix);
-    k_hc_maps<<<R, 512, 2 * D.d * sizeof(float), st>>>(h4, S.mix, W.hc_scale[site], W.hc_base[site],
-                                                       site ? W.post_norm : W.input_norm, D.d, D.hc,
-                                                       D.sinkhorn_iters, D.hc_eps, D.eps, S.post, S.comb, S.x);
+    k_hc_pre<<<R, 512, hc_pre_smem(D), st>>>(h4, W.hc_fn[site], W.hc_scale[site], W.hc_base[site],
+                                             site ? W.post_norm : W.input_norm, D.d, D.hc, D.sinkhorn_iters,
+                                             D.hc_eps, D.eps, S.post, S.comb, S.x);
     return ok_launch();
 }
 
@@ -661,14 +867,15 @@ int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, in
     f.W = W.idx_wq_b; f.x = S.qres; f.ldx = ql; f.R = R; f.O = (long)D.IH * D.ID; f.K = ql; f.fp8 = 0;
     f.y = S.iq; f.ldy = f.O; f.part = part; f.ticket = tick;
     if (gemv_launch(f, st)) return -1;
-    k_dsa_append<<<R, 256, 0, st>>>(S.kvb, S.ikgw, W.idx_knorm_w, W.idx_knorm_b, base_n, D.AH, D.qd, D.vd, D.ID,
-                                     D.IH, DS.cap, DS);
+    k_dsa_append<<<dim3(R, D.AH), 128, 0, st>>>(S.kvb, S.ikgw, W.idx_knorm_w, W.idx_knorm_b, base_n, D.AH, D.qd,
+                                                 D.vd, D.ID, D.IH, DS.cap, DS);
     k_dsa_pool<<<R, 128, 0, st>>>(W.idx_ape, base_n, R, D.ID, D.kpool, DS.cap, DS);
-    k_dsa_score<<<dim3(8, R), 256, 0, st>>>(S.iq, S.ikgw, base_n, D.IH, D.ID, D.kpool, S.maxpools, DS, S.iscore);
+    k_dsa_score<<<dim3((S.maxpools + 7) / 8, R), 256, 0, st>>>(S.iq, S.ikgw, base_n, D.IH, D.ID, D.kpool,
+                                                                 S.maxpools, DS, S.iscore);
     k_dsa_select<<<R, 256, 0, st>>>(S.iscore, base_n, D.kpool, D.topk / D.kpool, S.maxpools, S.isel);
     if (ok_launch()) return -1;
-    k_dsa_attn<<<D.AH, 256, 0, st>>>(S.q, base_n, R, D.AH, D.qd, D.vd, D.kpool, S.maxpools, S.isel, DS,
-                                      (float *)S.attn_scores, S.attn_sstride, S.attn);
+    k_dsa_attn<<<D.AH, 256, dsa_attn_smem(D), st>>>(S.q, base_n, R, D.AH, D.qd, D.vd, D.kpool, S.maxpools,
+                                                     S.isel, DS, (float *)S.attn_scores, S.attn_sstride, S.attn);
     if (ok_launch()) return -1;
     GemvDesc o{};
     o.W = W.o_c; o.WS = W.o_s; o.nkb = ((long)D.AH * D.vd + 127) / 128; o.x = S.attn; o.ldx = (long)D.AH * D.vd;

@@ -191,6 +191,12 @@ struct ApusGcudaModel {
     std::vector<void *> allocs;
     // shared MoE scratch
     MoeDev moe_scr{};
+    unsigned long long *moe_problems = nullptr;   // device counter (expert problems run)
+    uint64_t n_main_fwd = 0, n_mtp_fwd = 0;       // forwards enqueued (host count)
+    cudaGraph_t graph = nullptr;                  // captured full-depth step
+    cudaGraphExec_t gexec = nullptr;
+    int use_graph = 0;
+    size_t graph_kernels = 0;
 };
 
 static void *dmalloc(ApusGcudaModel *m, size_t n, bool zero = true) {
@@ -270,7 +276,10 @@ static bool alloc_dsa_state(ApusGcudaModel *m, DsaState &s) {
 
 static void model_release(ApusGcudaModel *m) {
     if (!m) return;
-    if (m->st) { cudaStreamSynchronize(m->st); cudaStreamDestroy(m->st); }
+    if (m->st) cudaStreamSynchronize(m->st);
+    if (m->gexec) cudaGraphExecDestroy(m->gexec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    if (m->st) cudaStreamDestroy(m->st);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
 }
@@ -329,7 +338,9 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
     S.iscore = (float *)A((size_t)R * S.maxpools * 4);
     S.isel = (uint8_t *)A((size_t)R * S.maxpools);
     S.attn = (uint16_t *)A((size_t)R * D.AH * D.vd * 2);
-    S.attn_sstride = m->cap + SLACK + MAXR;
+    // scores row: every position a call can see, plus a full attention tile
+    // past it (the tile loader reads whole tiles), in 16-byte units
+    S.attn_sstride = (m->cap + SLACK + MAXR + 64 + 3) & ~3;
     S.attn_scores = (float *)A((size_t)D.AH * R * S.attn_sstride * 4);
     S.yn = (uint16_t *)A((size_t)R * d * 2);
     S.logits = (uint16_t *)A((size_t)R * D.V * 2);
@@ -364,6 +375,8 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
     // MoE scratch shared by every sparse layer
     {
         MoeDev &ms = m->moe_scr;
+        m->moe_problems = (unsigned long long *)A(sizeof(unsigned long long));
+        ms.stat_problems = m->moe_problems;
         const int maxi = D.inter > D.dense_inter ? D.inter : D.dense_inter;
         const size_t P = (size_t)R * (D.ktop > 0 ? D.ktop : 1) + 1;
         ms.logits = (float *)A((size_t)R * (D.E > 0 ? D.E : 1) * 4);
@@ -696,6 +709,7 @@ static int main_forward(ApusGcudaModel *m, const int32_t *ids_dev, int R, uint16
     const Dims &D = m->D;
     Scratch &S = m->S;
     cudaStream_t st = m->st;
+    m->n_main_fwd++;
     if (k_embed_launch(m->embed, ids_dev, R, D.d, D.hc, S.h4, st)) return -1;
     uint16_t *h = S.h4, *h2 = S.h4b;
     auto stop = [&](int l, int stage) { return l == m->dbg_layer && stage == m->dbg_stage; };
@@ -733,6 +747,7 @@ static int mtp_forward(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t
     cudaStream_t st = m->st;
     const LayerW &W = m->L[D.L];
     const int d = D.d;
+    m->n_mtp_fwd++;
     // eh = [enorm(embed[id]) | hnorm(prev_h)]: gather the embed rows into S.mx
     if (k_embed_launch(m->embed, ids_dev, R, d, 1, S.mx, st)) return -1;
     if (rmsnorm_rows_launch(S.mx, d, m->enorm, d, R, D.eps, S.eh, 2L * d, st)) return -1;
@@ -879,9 +894,60 @@ static int spec_step(ApusGcudaModel *m, int Dp) {
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+// The full-depth step is fixed-shape and reads all of its control state
+// from device memory, so it is captured once into a CUDA graph and replayed.
+static int graph_build(ApusGcudaModel *m) {
+    if (cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return gcuda_check(cudaGetLastError(), "graph capture begin");
+    const int rc = spec_step(m, m->depth);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(m->st, &g);
+    if (rc || e != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        gcuda_set_error("gspec: step capture failed");
+        return -1;
+    }
+    if (cudaGraphInstantiate(&m->gexec, g, 0) != cudaSuccess) {
+        cudaGraphDestroy(g);
+        return gcuda_check(cudaGetLastError(), "graph instantiate");
+    }
+    m->graph = g;
+    size_t n = 0;
+    cudaGraphGetNodes(g, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    cudaGraphGetNodes(g, nodes.data(), &n);
+    size_t k = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
+    }
+    m->graph_kernels = k;
+    return 0;
+}
+
 extern "C" int apus_gcuda_gspec_step_async(ApusGcudaModel *m) {
     if (!m->has_mtp) { gcuda_set_error("gspec: model has no MTP block loaded"); return -1; }
-    return spec_step(m, m->depth);
+    if (!m->use_graph) return spec_step(m, m->depth);
+    if (!m->gexec && graph_build(m)) return -1;
+    return gcuda_check(cudaGraphLaunch(m->gexec, m->st), "graph launch");
+}
+
+extern "C" int apus_gcuda_gspec_use_graph(ApusGcudaModel *m, int on) {
+    m->use_graph = on ? 1 : 0;
+    return 0;
+}
+
+extern "C" void *apus_gcuda_model_stream(ApusGcudaModel *m) { return (void *)m->st; }
+
+extern "C" int apus_gcuda_model_counters(ApusGcudaModel *m, uint64_t *out, size_t n) {
+    uint64_t v[5] = {0, m->n_main_fwd, m->n_mtp_fwd, (uint64_t)m->graph_kernels, (uint64_t)sizeof(Ctl)};
+    cudaStreamSynchronize(m->st);
+    unsigned long long p = 0;
+    if (gcuda_check(cudaMemcpy(&p, m->moe_problems, sizeof p, cudaMemcpyDeviceToHost), "counters")) return -1;
+    v[0] = p;
+    for (size_t i = 0; i < n && i < 5; i++) out[i] = v[i];
+    return 0;
 }
 
 extern "C" int apus_gcuda_gspec_step(ApusGcudaModel *m, int *out, int cap) {

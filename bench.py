@@ -15,6 +15,7 @@ from the reference sources) runs a bounded sample of the same workload on
 the host cores.
 """
 import argparse
+import ctypes as C
 import json
 import os
 import subprocess
@@ -404,36 +405,321 @@ def cpu_c1(h, budget_s=10.0):
                       f"to BF16 as the reference engine holds them), {dt * 1e3:.1f} ms each"}
 
 
+# --------------------------------------------------------------------------
+# config 2: the scaled glm5_next stack + MTP speculative decode (headline)
+def c2_config():
+    """4 layers at hidden 4096 (3 KDA 32x128 + DSA at layer
+    3 with the real MLA / Lightning-indexer dims), every layer the config-1
+    MoE (288 experts top-8 + shared, inter 1024), vocab 154880, one NextN
+    layer.  Other fields from the reference's config.json."""
+    return dict(hidden_size=4096, vocab_size=154880, num_hidden_layers=4, rms_norm_eps=1e-5, hc_mult=4,
+                hc_sinkhorn_iters=20, hc_eps=1e-6, first_k_dense_replace=0, intermediate_size=12288,
+                moe_intermediate_size=1024, n_routed_experts=288, n_shared_experts=1, num_experts_per_tok=8,
+                routed_scaling_factor=2.5, norm_topk_prob=1, swiglu_limit=10.0, num_attention_heads=64,
+                q_lora_rank=1536, kv_lora_rank=512, qk_nope_head_dim=256, v_head_dim=256, index_n_heads=32,
+                index_head_dim=128, index_topk=2048, index_kpool=4, index_kpool_always_select_tail=1,
+                linear_num_heads=32, linear_head_dim=128, linear_conv_kernel_dim=4, linear_lower_bound=-5.0,
+                num_nextn_predict_layers=1, layer_is_dsa=[0, 0, 0, 1], mlp_is_sparse=[1, 1, 1, 1])
+
+
+C2 = dict(prompt=512, depth=4, seed=2)   # BASELINE "depth 3" = 4 verify rows (reference APUS_SPEC_K 4)
+
+
+def c2_weights(kw, seed):
+    """Seeded synthetic weights for every tensor of tensor_specs(kw), made
+    with torch on the GPU and returned as host numpy arrays (both bench arms
+    load the same arrays).  Experts: BASELINE config 0 codes (E4M3 of
+    N(0,1)*64) with log-uniform [1e-4, 1e-2] block scales; router BF16
+    N(0, 0.02) with a zero bias; embeddings and head BF16 N(0, 0.02); the DSA
+    FP8 linears amax/448 block-scaled N(0, 1/sqrt(K)); BF16 matrices
+    N(0, 1/sqrt(K)); norms 1 + 0.05 N(0,1)."""
+    import math
+    import numpy as np
+    import torch
+    import apus_gcuda as G
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    g = torch.Generator(device=dev).manual_seed(seed)
+    out = {}
+    specs = G.tensor_specs(kw)
+    expert = lambda n: ".mlp." in n
+
+    def bf16(t):
+        return t.to(torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16)
+
+    i = 0
+    while i < len(specs):
+        name, shape, dt, kind = specs[i]
+        if kind == "e4m3":
+            sname, sshape = specs[i + 1][0], specs[i + 1][1]
+            O_, K_ = shape
+            if expert(name):
+                v = torch.clamp(torch.randn(shape, generator=g, device=dev) * 64, -448, 448)
+                codes = v.to(torch.float8_e4m3fn)
+                lo, hi = math.log(1e-4), math.log(1e-2)
+                sc = torch.exp(lo + (hi - lo) * torch.rand(sshape, generator=g, device=dev))
+            else:
+                w = torch.randn(shape, generator=g, device=dev) / math.sqrt(K_)
+                nbo, nbk = sshape
+                wp = torch.zeros((nbo * 128, nbk * 128), device=dev)
+                wp[:O_, :K_] = w
+                blk = wp.view(nbo, 128, nbk, 128)
+                amax = blk.abs().amax(dim=(1, 3)).clamp_min(2.0 ** -126)
+                sc = amax / 448.0
+                q = torch.clamp(blk / sc[:, None, :, None], -448, 448).view(nbo * 128, nbk * 128)
+                codes = q[:O_, :K_].to(torch.float8_e4m3fn)
+            out[name] = codes.view(torch.uint8).cpu().numpy()
+            out[sname] = sc.float().cpu().numpy()
+            i += 2
+            continue
+        if kind == "f32":
+            if name.endswith("e_score_correction_bias"):
+                v = torch.zeros(shape, device=dev)
+            elif name.endswith("_scale"):
+                v = 1.0 + 0.1 * torch.randn(shape, generator=g, device=dev)
+            elif name.endswith("_base"):
+                v = 0.25 * torch.randn(shape, generator=g, device=dev)
+            else:                                   # A_log, dt_bias
+                v = 0.5 * torch.randn(shape, generator=g, device=dev)
+            out[name] = v.float().cpu().numpy()
+        else:
+            if len(shape) == 1 or name.endswith("compress_ape"):
+                if name.endswith("bias") or name.endswith("compress_ape"):
+                    v = 0.05 * torch.randn(shape, generator=g, device=dev)
+                else:
+                    v = 1.0 + 0.05 * torch.randn(shape, generator=g, device=dev)
+            elif name in ("embed_tokens.weight", "lm_head.weight") or name.endswith("mlp.gate.weight"):
+                v = 0.02 * torch.randn(shape, generator=g, device=dev)
+            elif name.endswith("_conv1d.weight"):
+                v = 0.25 * torch.randn(shape, generator=g, device=dev)
+            else:
+                v = torch.randn(shape, generator=g, device=dev) / math.sqrt(shape[-1])
+            out[name] = bf16(v)
+        i += 1
+    if dev == "cuda":
+        torch.cuda.empty_cache()
+    return out
+
+
+def c2_prompt(kw, seed):
+    import numpy as np
+    return np.random.default_rng(seed).integers(0, kw["vocab_size"], C2["prompt"]).astype(np.int32)
+
+
+def c2_algo_bytes(kw, depth, n_ctx, moe_problems):
+    """Algorithmic HBM bytes of one speculative step: every weight byte the
+    step's forwards must read once (main forward over `depth` rows, the MTP
+    replay and depth-1 chain forwards), the realised MoE expert union
+    (`moe_problems` expert GEMV pairs, shared expert included, counted on the
+    device), the KDA state read + final write, the DSA K/V and pool-key rows
+    visible at context n_ctx, and the new cache rows.  Checkpoint copies and
+    L2 reuse are not counted."""
+    d, V, hc, L = kw["hidden_size"], kw["vocab_size"], kw["hc_mult"], kw["num_hidden_layers"]
+    H, D, K = kw["linear_num_heads"], kw["linear_head_dim"], kw["linear_conv_kernel_dim"]
+    qkv, mix = H * D, (2 + hc) * hc
+    AH, qd, vd = kw["num_attention_heads"], kw["qk_nope_head_dim"], kw["v_head_dim"]
+    ql, kl, IH, ID, kp = (kw["q_lora_rank"], kw["kv_lora_rank"], kw["index_n_heads"], kw["index_head_dim"],
+                          kw["index_kpool"])
+    E, inter = kw["n_routed_experts"], kw["moe_intermediate_size"]
+    cb = lambda n: (n + 127) // 128
+    fp8 = lambda O_, K_: O_ * K_ + cb(O_) * cb(K_) * 4
+    kda = (3 * qkv + 2 * D + H) * d * 2 + 2 * qkv * D * 2 + 3 * qkv * K * 2 + d * qkv * 2 + 2 * H * D * D * 4
+    dsa_w = (fp8(ql + kl, d) + fp8(AH * qd, ql) + AH * (qd + vd) * kl * 2 + fp8(d, AH * vd) + IH * ID * ql * 2
+             + (2 * ID + IH) * d * 2)
+
+    def dsa(rows, n):
+        return dsa_w + n * AH * (qd + vd) * 2 + (n // kp) * ID * 2 + rows * (AH * (qd + vd) + 2 * ID) * 2
+
+    router = E * d * 2 + E * 4
+    expert = fp8(2 * inter, d) + fp8(d, inter)
+    hcb = 2 * mix * hc * d * 2
+    main = sum(hcb + (dsa(depth, n_ctx) if kw["layer_is_dsa"][l] else kda) + router for l in range(L))
+    main += V * d * 2
+    mtp_fwd = lambda rows, n: 2 * d * d * 2 + dsa(rows, n) + router + V * d * 2
+    mtp = mtp_fwd(depth, n_ctx) + sum(mtp_fwd(1, n_ctx + i) for i in range(depth - 1))
+    n_moe_calls = L + 1 + (depth - 1)
+    return main + mtp + moe_problems * expert, n_moe_calls
+
+
+def bench_c2(args, ws, rank, W=None):
+    import numpy as np
+    import torch
+    import apus_gcuda as G
+    G.enable()
+    kw = c2_config()
+    depth = C2["depth"]
+    if W is None:
+        W = c2_weights(kw, C2["seed"])
+    prompt = c2_prompt(kw, C2["seed"])[:args.prompt or C2["prompt"]]
+    cap = len(prompt) + depth * (2 * args.steps + 2 * args.warmup) + 64
+    m = G.GModel(G.make_config(**kw), has_mtp=True, kv_cap=cap, depth=depth)
+    m.load(W)
+    m.use_graph(True)
+    m.spec_prefill(prompt)
+    st = torch.cuda.ExternalStream(m.stream())
+    for _ in range(args.warmup):
+        m.spec_step_async()
+    st.synchronize()
+    s0, _ = m.stats()
+    c0 = m.counters()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        time.sleep(0.3)
+        torch.cuda.nvtx.range_push("timed")
+        e0.record(st)
+        for _ in range(args.steps):
+            m.spec_step_async()
+        e1.record(st)
+        st.synchronize()
+        torch.cuda.nvtx.range_pop()
+    ms = e0.elapsed_time(e1)
+    s1, rc = m.stats()
+    c1 = m.counters()
+    if rc != 0:
+        raise RuntimeError("sequence ran past its capacity")
+    barrier(ws)
+    ms = max_over_ranks(ms, ws)
+    emitted = s1["emitted"] - s0["emitted"]
+    per = ms / args.steps
+    tok_s = emitted / (ms * 1e-3)
+    n_ctx = (s0["pos"] + s1["pos"]) // 2
+    probs = (c1["moe_problems"] - c0["moe_problems"]) / args.steps
+    algo, _ = c2_algo_bytes(kw, depth, n_ctx, probs)
+    hbm, _, src = peaks()
+    gbs = algo / (per * 1e-3) / 1e9
+    offered = s1["offered"] - s0["offered"]
+    accepted = s1["accepted"] - s0["accepted"]
+    out = {"metric": METRIC, "value": round(tok_s * ws, 2), "unit": "accepted tok/s (emitted tokens / s)",
+           "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16 activations, fp8e4m3/bf16 weights, f32 accumulation",
+           "data": f"synthetic random-init weights (seed {C2['seed']}), {len(prompt)} uniform random prompt ids",
+           "config": {"workload": "config2: scaled glm5_next (4 layers: 3 KDA 32x128 + 1 DSA, MoE 288 top-8 "
+                                  "inter 1024, vocab 154880) + 1 NextN MTP layer, greedy spec decode",
+                      "depth": "BASELINE depth 3 = 4 verify rows (reference APUS_SPEC_K 4)",
+                      "prompt": len(prompt), "parallelism": f"replicas x{ws}",
+                      "l2": "inputs larger than L2: each step streams ~10 GB of weights",
+                      "step": "one device-resident speculative step replayed from a CUDA graph"},
+           "spec": {"tokens_per_step": round(emitted / args.steps, 4), "offered": offered, "accepted": accepted,
+                    "acceptance": round(accepted / offered, 4) if offered else None,
+                    "context_avg": n_ctx},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": src,
+                        "algo_bytes_per_step": int(algo), "moe_expert_problems_per_step": round(probs, 2),
+                        "note": "step-level: algorithmic bytes per step / device step time"},
+           "gpu_launches": int(c1["graph_kernels"]) * args.steps,
+           "clocks": clk.summary()}
+    if args.quick:
+        m.close()
+        return out, W
+    # e2e: the reference-facing synchronous apus_gspec_step drop-in, host tokens out
+    for _ in range(min(args.warmup, 3)):
+        m.spec_step()
+    t0 = time.perf_counter()
+    n_e2e = 0
+    for _ in range(args.steps):
+        n_e2e += len(m.spec_step())
+    e2e = max_over_ranks(time.perf_counter() - t0, ws)
+    out["e2e"] = {"value": round(n_e2e / e2e * ws, 2), "unit": "accepted tok/s through apus_gcuda_gspec_step",
+                  "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 2 * int(c1["ctl_bytes"]),
+                  "note": "no per-step inputs cross to the device; the control block is read back twice"}
+    m.close()
+    return out, W
+
+
+def cpu_c2(W, budget_s=20.0, prompt_len=64, log=None):
+    """The reference's own speculative engine (oracle/_ref: apus_gspec_* over
+    apus_gmodel, compiled from the reference sources) on the host cores with
+    the same weights: prefill of the first prompt_len prompt tokens (not
+    timed), then apus_gspec_step until budget_s.  Experts are dequantized to
+    BF16 at load as the reference engine holds them (not timed)."""
+    import numpy as np
+    import oracle as O
+    if O.REF is None:
+        return None
+    kw = c2_config()
+    depth = C2["depth"]
+    cfg = O.make_config(**kw)
+    t_load = time.perf_counter()
+    R = O.REF.ref_model_new(C.byref(cfg), 1)
+    for name, arr in W.items():
+        if O.REF.ref_model_set(R, name.encode(), O.p(arr)) != 0:
+            raise KeyError(name)
+    O.REF.ref_model_finalize(R)
+    cap = prompt_len + 4096
+    st = O.REF.ref_state_new(R, cap)
+    sp = O.REF.ref_spec_new(R, st, cap, depth)
+    ids = np.ascontiguousarray(c2_prompt(kw, C2["seed"])[:prompt_len])
+    assert O.REF.ref_spec_prefill(sp, O.p(ids), len(ids)) == 0
+    t_load = time.perf_counter() - t_load
+    buf = np.zeros(depth + 1, np.int32)
+    n = tok = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or n < 1:
+        k = O.REF.ref_spec_step(sp, O.p(buf), depth + 1)
+        if k <= 0:
+            break
+        tok += k
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(tok / dt, 4), "unit": "accepted tok/s", "cores": O.REF.apus_ref_threads(),
+            "kind": "reference",
+            "sample": f"{n} apus_gspec_step calls ({tok} tokens, {dt:.1f} s) after a {prompt_len}-token prefill "
+                      f"(the bench prompt's first {prompt_len} ids; setup {t_load:.0f} s untimed)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 256 for config 2, else 200)")
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", type=int, default=0)
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--prompt", type=int, default=0, help="config 2: prompt tokens (default 512; profiling only)")
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of reference CPU decode sampled")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed kernels only (no e2e, no CPU baseline): the profiling command")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 256 if args.config == 2 else 200
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
         if rank != 0:
             return
-        cb = cpu_c0(budget_s=max(3.0, 0.05 * args.steps))
-        line = {"metric": METRIC, "impl": "reference"}
-        if cb is None:
-            line["unavailable"] = "reference CPU engine (oracle/_ref/libapus_ref.so) not built"
+        line = {"metric": METRIC, "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True}
+        if args.config == 2:
+            import oracle as O
+            if O.REF is None:
+                line["unavailable"] = "reference CPU engine (oracle/_ref/libapus_ref.so) not built"
+            else:
+                cb = cpu_c2(c2_weights(c2_config(), C2["seed"]), budget_s=args.cpu_budget)
+                line.update({"value": cb["value"], "unit": cb["unit"],
+                             "config": {"workload": "config2 on host cores (reference apus_gspec_*)"},
+                             "cpu_baseline": cb,
+                             "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
+                                     "d2h_bytes_per_step": 0}})
         else:
-            line.update({"value": cb["value"], "unit": "GB/s (FP8 GEMV algorithmic bytes, config 0)",
-                         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                         "higher_is_better": True, "config": {"workload": "config0 on host cores"},
-                         "cpu_baseline": cb,
-                         "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
-                                 "d2h_bytes_per_step": 0}})
+            cb = cpu_c0(budget_s=max(3.0, 0.05 * args.steps))
+            if cb is None:
+                line["unavailable"] = "reference CPU engine (oracle/_ref/libapus_ref.so) not built"
+            else:
+                line.update({"value": cb["value"], "unit": "GB/s (FP8 GEMV algorithmic bytes, config 0)",
+                             "config": {"workload": "config0 on host cores"}, "cpu_baseline": cb,
+                             "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
+                                     "d2h_bytes_per_step": 0}})
         print(json.dumps(line), flush=True)
         return
     ws, rank, local = dist_init()
-    if args.config == 1:
+    if args.config == 2:
+        out, W = bench_c2(args, ws, rank)
+        if rank == 0 and not args.quick and ws == 1:
+            out["cpu_baseline"] = cpu_c2(W, budget_s=args.cpu_budget)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    elif args.config == 1:
         out = bench_c1(args, ws, rank)
         h = out.pop("_moe", None)
         if rank == 0 and not args.quick and h:

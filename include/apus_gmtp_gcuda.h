@@ -116,6 +116,17 @@ int apus_gcuda_greedy(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen
  * rollback check of tests/m8g/test_m8g.c:383-424). */
 uint64_t apus_gcuda_state_digest(ApusGcudaModel *m);
 
+/* Replay the full-depth step from a CUDA graph captured on its first use
+ * (the step is fixed-shape and keeps its control state on the device). */
+int apus_gcuda_gspec_use_graph(ApusGcudaModel *m, int on);
+/* The model's CUDA stream (cudaStream_t), for timing with events. */
+void *apus_gcuda_model_stream(ApusGcudaModel *m);
+/* Counters: [0] MoE expert problems run (routed union + shared, summed over
+ * calls), [1] main-model forwards, [2] MTP forwards enqueued, [3] kernels in
+ * the captured step graph (0 before capture), [4] bytes of the control
+ * block a synchronous step reads back (twice per step). */
+int apus_gcuda_model_counters(ApusGcudaModel *m, uint64_t *out, size_t n);
+
 /* Inspection hooks (no reference counterpart; the reference dumps through
  * its APUS_DEBUG logging): stop the main forward after (layer, stage) —
  * stage 0 mHC pre (attn), 1 attention, 2 mHC post, 3 mHC pre (ffn), 4 MLP —

@@ -204,6 +204,25 @@ def test_async_steps_equal_sync(gcuda, tiny):
     assert b.emitted() == sync
 
 
+def test_graph_steps_equal_sync(gcuda, tiny):
+    """The full-depth step captured once into a CUDA graph and replayed."""
+    kw, W = tiny
+    a = gpu_model(gcuda, kw, W, depth=4)
+    a.spec_prefill(PROMPT)
+    sync = []
+    for _ in range(10):
+        sync += a.spec_step()
+    b = gpu_model(gcuda, kw, W, depth=4)
+    b.use_graph(True)
+    b.spec_prefill(PROMPT)
+    for _ in range(10):
+        b.spec_step_async()
+    assert b.emitted() == sync
+    c = b.counters()
+    assert c["graph_kernels"] > 20 and c["moe_problems"] > 0
+    assert b.digest() == a.digest()
+
+
 def test_capacity_edge(gcuda, tiny):
     """Near the capacity the verify batch shrinks to cap - q rows
     (c/gmtp.h:783-786); at the capacity a step emits nothing."""
