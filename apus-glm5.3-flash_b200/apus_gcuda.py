@@ -52,6 +52,8 @@ apus_gcuda_fp8blk_linear_dev = _fn("apus_gcuda_fp8blk_linear_dev", _i, _vp, _vp,
 apus_gcuda_bf16_gemm_dev = _fn("apus_gcuda_bf16_gemm_dev", _i, _vp, _vp, _vp, _sz, _sz, _sz, _vp)
 apus_gcuda_bf16_gemm_f32_dev = _fn("apus_gcuda_bf16_gemm_f32_dev", _i, _vp, _vp, _vp, _sz, _sz, _sz, _vp)
 apus_gcuda_bf16_gemm_argmax_dev = _fn("apus_gcuda_bf16_gemm_argmax_dev", _i, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp)
+apus_gcuda_bf16_gemm_argmax_static_dev = _fn("apus_gcuda_bf16_gemm_argmax_static_dev", _i, _vp, _vp, _vp, _vp,
+                                             _sz, _sz, _sz, _vp)
 
 _f = C.c_float
 apus_gcuda_moe_new = _fn("apus_gcuda_moe_new", _vp, _i, _i, _sz, _sz, _f, _f, _i)
