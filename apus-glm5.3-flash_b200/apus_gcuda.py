@@ -183,6 +183,11 @@ class GModel:
         arr = self.np.ascontiguousarray(arr)
         check(apus_gcuda_model_set(self.h, name.encode(), ptr(arr), arr.nbytes), f"set {name}")
 
+    def get(self, name, shape, dtype):
+        a = self.np.empty(shape, dtype)
+        check(apus_gcuda_model_get(self.h, name.encode(), ptr(a), a.nbytes), f"get {name}")
+        return a
+
     def load(self, weights):
         for k, v in weights.items():
             self.set(k, v)

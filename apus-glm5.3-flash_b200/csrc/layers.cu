@@ -276,17 +276,25 @@ __global__ void __launch_bounds__(512) k_hc_pre(const uint16_t *h4, const uint16
     for (int j = warp; j < nmix; j += nwarp) {
         const uint16_t *f = fn + (size_t)j * n;
         float acc = 0.f;
-        for (int c = lane * 8; c < n; c += 256) {
-            const uint4 wv = __ldg((const uint4 *)(f + c));
-            const float4 a = *(const float4 *)(fl + c), b = *(const float4 *)(fl + c + 4);
-            acc += bf16lo(wv.x) * a.x;
-            acc += bf16hi(wv.x) * a.y;
-            acc += bf16lo(wv.y) * a.z;
-            acc += bf16hi(wv.y) * a.w;
-            acc += bf16lo(wv.z) * b.x;
-            acc += bf16hi(wv.z) * b.y;
-            acc += bf16lo(wv.w) * b.z;
-            acc += bf16hi(wv.w) * b.w;
+        for (int c0 = lane * 8; c0 < n; c0 += 256 * 8) {
+            uint4 wv[8];                      // 8 weight loads in flight per lane
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                wv[u] = c0 + u * 256 < n ? __ldg((const uint4 *)(f + c0 + u * 256)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int c = c0 + u * 256;
+                if (c >= n) break;
+                const float4 a = *(const float4 *)(fl + c), b = *(const float4 *)(fl + c + 4);
+                acc += bf16lo(wv[u].x) * a.x;
+                acc += bf16hi(wv[u].x) * a.y;
+                acc += bf16lo(wv[u].y) * a.z;
+                acc += bf16hi(wv[u].y) * a.w;
+                acc += bf16lo(wv[u].z) * b.x;
+                acc += bf16hi(wv[u].z) * b.y;
+                acc += bf16lo(wv[u].w) * b.z;
+                acc += bf16hi(wv[u].w) * b.w;
+            }
         }
 #pragma unroll
         for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);

@@ -114,7 +114,8 @@ def max_over_ranks(v, ws):
         return v
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -407,19 +408,22 @@ def cpu_c1(h, budget_s=10.0):
 
 # --------------------------------------------------------------------------
 # config 2: the scaled glm5_next stack + MTP speculative decode (headline)
-def c2_config():
+def c2_config(small=False):
     """4 layers at hidden 4096 (3 KDA 32x128 + DSA at layer
     3 with the real MLA / Lightning-indexer dims), every layer the config-1
     MoE (288 experts top-8 + shared, inter 1024), vocab 154880, one NextN
     layer.  Other fields from the reference's config.json."""
-    return dict(hidden_size=4096, vocab_size=154880, num_hidden_layers=4, rms_norm_eps=1e-5, hc_mult=4,
-                hc_sinkhorn_iters=20, hc_eps=1e-6, first_k_dense_replace=0, intermediate_size=12288,
-                moe_intermediate_size=1024, n_routed_experts=288, n_shared_experts=1, num_experts_per_tok=8,
-                routed_scaling_factor=2.5, norm_topk_prob=1, swiglu_limit=10.0, num_attention_heads=64,
-                q_lora_rank=1536, kv_lora_rank=512, qk_nope_head_dim=256, v_head_dim=256, index_n_heads=32,
-                index_head_dim=128, index_topk=2048, index_kpool=4, index_kpool_always_select_tail=1,
-                linear_num_heads=32, linear_head_dim=128, linear_conv_kernel_dim=4, linear_lower_bound=-5.0,
-                num_nextn_predict_layers=1, layer_is_dsa=[0, 0, 0, 1], mlp_is_sparse=[1, 1, 1, 1])
+    kw = dict(hidden_size=4096, vocab_size=154880, num_hidden_layers=4, rms_norm_eps=1e-5, hc_mult=4,
+              hc_sinkhorn_iters=20, hc_eps=1e-6, first_k_dense_replace=0, intermediate_size=12288,
+              moe_intermediate_size=1024, n_routed_experts=288, n_shared_experts=1, num_experts_per_tok=8,
+              routed_scaling_factor=2.5, norm_topk_prob=1, swiglu_limit=10.0, num_attention_heads=64,
+              q_lora_rank=1536, kv_lora_rank=512, qk_nope_head_dim=256, v_head_dim=256, index_n_heads=32,
+              index_head_dim=128, index_topk=2048, index_kpool=4, index_kpool_always_select_tail=1,
+              linear_num_heads=32, linear_head_dim=128, linear_conv_kernel_dim=4, linear_lower_bound=-5.0,
+              num_nextn_predict_layers=1, layer_is_dsa=[0, 0, 0, 1], mlp_is_sparse=[1, 1, 1, 1])
+    if small:
+        kw.update(n_routed_experts=16, vocab_size=16384)
+    return kw
 
 
 C2 = dict(prompt=512, depth=4, seed=2)   # BASELINE "depth 3" = 4 verify rows (reference APUS_SPEC_K 4)
@@ -545,7 +549,7 @@ def bench_c2(args, ws, rank, W=None):
     import torch
     import apus_gcuda as G
     G.enable()
-    kw = c2_config()
+    kw = c2_config(args.small)
     depth = C2["depth"]
     if W is None:
         W = c2_weights(kw, C2["seed"])
@@ -677,6 +681,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--prompt", type=int, default=0, help="config 2: prompt tokens (default 512; profiling only)")
+    ap.add_argument("--small", action="store_true",
+                    help="config 2 layer shapes with 16 experts and a 16384 vocab (profiling captures only)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of reference CPU decode sampled")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed kernels only (no e2e, no CPU baseline): the profiling command")
