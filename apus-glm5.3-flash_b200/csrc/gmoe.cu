@@ -95,16 +95,39 @@ __global__ void k_moe_route(MoeDev m, int R, const float *logits, const int32_t 
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int p = 0;
-        for (int e = 0; e < E; e++) {
+    // work list: the flagged experts in ascending order (slot_of[e] = flagged
+    // experts before e), by a ballot + popc scan over blocks of blockDim experts
+    __shared__ int wsum[32], run;
+    if (threadIdx.x == 0) run = 0;
+    __syncthreads();
+    const int nw = blockDim.x >> 5;
+    for (int e0 = 0; e0 < E; e0 += blockDim.x) {
+        const int e = e0 + threadIdx.x;
+        const int f = e < E ? flag[e] : 0;
+        const unsigned bal = __ballot_sync(0xffffffffu, f);
+        const int ln = threadIdx.x & 31, w = threadIdx.x >> 5;
+        if (ln == 0) wsum[w] = __popc(bal);
+        __syncthreads();
+        int p = run + __popc(bal & ((1u << ln) - 1u));
+        for (int k = 0; k < w; k++) p += wsum[k];
+        if (e < E) {
             slot_of[e] = p;
-            if (flag[e]) m.prob_expert[p++] = e;
+            if (f) m.prob_expert[p] = e;
         }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int tot = 0;
+            for (int k = 0; k < nw; k++) tot += wsum[k];
+            run += tot;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const int p = run;
         slot_of[E] = p;
-        m.prob_expert[p++] = E;            // shared expert, always last
-        *m.prob_count = p;
-        if (m.stat_problems) atomicAdd(m.stat_problems, (unsigned long long)p);
+        m.prob_expert[p] = E;              // shared expert, always last
+        *m.prob_count = p + 1;
+        if (m.stat_problems) atomicAdd(m.stat_problems, (unsigned long long)(p + 1));
     }
     __syncthreads();
     for (int i = threadIdx.x; i < R * K; i += blockDim.x)

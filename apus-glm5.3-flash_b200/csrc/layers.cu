@@ -10,6 +10,7 @@
 #include "gcuda.h"
 #include "model_dev.h"
 #include "pipe.cuh"
+#include "linear.cuh"
 
 namespace apus {
 
@@ -576,36 +577,53 @@ __global__ void k_dsa_select(const float *score, const int *base_n, int kp, int 
     }
 }
 
-// Attention over the selected positions (c/gdsa.h:451-517): one CTA per
-// head handles every row, so each K/V row is read once per call.
-//   sc = bf16(bf16(q.k) * qd^-0.5); p = bf16(softmax(sc)); o = bf16(sum p v)
+// Attention over the selected positions (c/gdsa.h:451-517): one CTA (8
+// warps) per head handles every row of the call, so each K/V row is read
+// once.  sc = bf16(bf16(q.k) * qd^-0.5); p = bf16(softmax(sc)); o = bf16(sum p v).
 // Visibility of position j for row t: j <= base+t and (its pool is
-// selected, or j is in the row's incomplete tail pool).  Row t's output sums
-// p_j v_j over every j <= base+t in ascending order with p_j = 0 where j is
-// not visible, as the reference's one-token decode does over its n = base+t+1
-// cache rows; so a row's result does not depend on the other rows of the call.
-// K and V stream through shared memory in tiles of ATJ positions, double
-// buffered with cp.async; dynamic smem = dsa_attn_smem(qd, vd).
-#define ATJ 64
+// selected, or j is in the row's incomplete tail pool).  p_j = 0 for every
+// other position, so row t's output depends only on its own row (the rows
+// of one call do not interact).
+//
+// Both contractions run on the tensor cores (mma.sync m16n8k16, bf16 in,
+// f32 accumulate): scores = K_tile[128 pos][qd] . Q^T (8 query rows as the
+// n dimension), output^T = V_tile^T . P^T.  K and V stream through shared
+// memory in tiles of ATJ positions (cp.async, double buffered; 16-byte
+// chunks XOR-swizzled by row so ldmatrix is conflict-free).  The softmax is
+// one warp per row over the scores in global scratch; p is stored as BF16
+// (exact, it is BF16-rounded by definition) in pbuf.
+#define ATJ 128
+__device__ __forceinline__ uint32_t swz(int row, int chunk, int rowbytes) {
+    return (uint32_t)(row * rowbytes + ((chunk ^ (row & 7)) << 4));
+}
+
 __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd,
                                                   int vd, int kp, int maxpools, const uint8_t *sel, DsaState ds,
-                                                  float *sbuf, int sstride, uint16_t *out) {
-    extern __shared__ __align__(16) uint8_t dsm[];
+                                                  float *sbuf, uint16_t *pbuf, int sstride, uint16_t *out) {
+    extern __shared__ __align__(128) uint8_t dsm[];
     const int h = blockIdx.x;
     const int base = *base_n;
     const int nmax = base + R;            // positions that exist after this call's append
     const int nt = (nmax + ATJ - 1) / ATJ;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, q4 = lane & 3;
     const int wmax = qd > vd ? qd : vd;
-    auto tile = [&](int b) { return (uint16_t *)dsm + b * ATJ * wmax; };
-    auto ptile = [&](int b) { return (float *)(dsm + 4 * ATJ * wmax) + b * MAXR * ATJ; };
+    const int TB = ATJ * wmax * 2;                     // bytes of one K/V tile buffer
+    const int PROW = (ATJ + 8) * 2, QROW = (qd + 8) * 2;
+    uint8_t *kv0 = dsm, *pt0 = dsm + 2 * TB, *qs = pt0 + 2 * MAXR * PROW;
     const float scale = (float)(1.0 / sqrt((double)qd));
-    float *sc = sbuf + (size_t)h * R * sstride;       // [R][sstride] scores, then probabilities
-    __shared__ float qsh[MAXR][256];
+    float *sc = sbuf + (size_t)h * MAXR * sstride;     // [MAXR][sstride] scores, then e
+    uint16_t *pb = pbuf + (size_t)h * MAXR * sstride;  // [MAXR][sstride] p (BF16)
     __shared__ int tail_s[MAXR];
-    __shared__ float red[256];
-    for (int i = threadIdx.x; i < R * qd; i += blockDim.x)
-        qsh[i / qd][i % qd] = bf16_f32(q[(size_t)(i / qd) * AH * qd + (size_t)h * qd + i % qd]);
+    // Q rows (zero beyond R) and the P tiles' unused rows
+    for (int i = threadIdx.x; i < MAXR * (qd / 8); i += blockDim.x) {
+        const int t = i / (qd / 8), c = i % (qd / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t < R) v = *(const uint4 *)(q + (size_t)t * AH * qd + (size_t)h * qd + c * 8);
+        *(uint4 *)(qs + t * QROW + c * 16) = v;
+    }
+    for (int i = threadIdx.x; i < 2 * MAXR * (PROW / 16); i += blockDim.x)
+        *(uint4 *)(pt0 + i * 16) = make_uint4(0, 0, 0, 0);
     if (threadIdx.x < R) {
         const int vis = base + threadIdx.x + 1;
         tail_s[threadIdx.x] = vis - vis % kp;
@@ -616,117 +634,131 @@ __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *
         const int p = j / kp;
         return p < maxpools && sel[(size_t)t * maxpools + p];
     };
-    // stage rows [ti*ATJ, ti*ATJ + ATJ) of a [cap][w] cache (rows past nmax
-    // clamp to the last one; they are never used) and optionally the rows'
-    // probabilities
-    auto stage = [&](const uint16_t *cache, int w, int ti, int buf, bool probs) {
-        const int j0 = ti * ATJ, vpr = w / 8;
-        for (int i = threadIdx.x; i < ATJ * vpr; i += blockDim.x) {
-            const int jj = i / vpr, c = i % vpr;
+    // stage tile ti of a [cap][w] cache into buffer b (rows past nmax clamp to
+    // the last one; their p is 0 and their scores are never stored); with
+    // probs, also the rows' p for t < R
+    auto stage = [&](const uint16_t *cache, int w, int ti, int b, bool probs) {
+        const int j0 = ti * ATJ, cpr = w / 8;
+        uint8_t *dst = kv0 + b * TB;
+        for (int i = threadIdx.x; i < ATJ * cpr; i += blockDim.x) {
+            const int jj = i / cpr, c = i % cpr;
             const int j = min(j0 + jj, nmax - 1);
-            cp_async16(tile(buf) + jj * w + c * 8, cache + ((size_t)h * ds.cap + j) * w + c * 8);
+            cp_async16(dst + swz(jj, c, w * 2), cache + ((size_t)h * ds.cap + j) * w + c * 8);
         }
         if (probs)
-            for (int i = threadIdx.x; i < R * (ATJ / 4); i += blockDim.x) {
-                const int t = i / (ATJ / 4), c = i % (ATJ / 4);
-                cp_async16(ptile(buf) + t * ATJ + c * 4, sc + (size_t)t * sstride + j0 + c * 4);
+            for (int i = threadIdx.x; i < R * (ATJ / 8); i += blockDim.x) {
+                const int t = i / (ATJ / 8), c = i % (ATJ / 8);
+                cp_async16(pt0 + b * MAXR * PROW + t * PROW + c * 16, pb + (size_t)t * sstride + j0 + c * 8);
             }
         cp_async_commit();
     };
     __syncthreads();
-    // scores: one warp per position, lanes split the qd dims (fixed tree)
-    const int ne = qd / 32;
+    // ---- scores: warp w owns positions [16w, 16w+16) of each tile
+    uint32_t qb[16][2];
+    const int nks = qd / 16;
+#pragma unroll
+    for (int ks = 0; ks < 16; ks++)
+        if (ks < nks) ldsm_x2(qb[ks][0], qb[ks][1], qs + (lane & 7) * QROW + (ks * 16 + ((lane >> 3) & 1) * 8) * 2);
     stage(ds.k, qd, 0, 0, false);
     for (int ti = 0; ti < nt; ti++) {
         if (ti + 1 < nt) stage(ds.k, qd, ti + 1, (ti + 1) & 1, false);
         else cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        const uint16_t *kt = tile(ti & 1);
-        for (int jj = warp; jj < ATJ; jj += nw) {
-            const int j = ti * ATJ + jj;
-            if (j >= nmax) break;
-            bool any = false;
-            for (int t = 0; t < R; t++) any |= visible(t, j);
-            if (!any) continue;
-            float kv[8];
+        const uint8_t *kt = kv0 + (ti & 1) * TB;
+        const int r0 = warp * 16;
+        float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
 #pragma unroll
-            for (int e = 0; e < 8; e++) kv[e] = e < ne ? bf16_f32(kt[jj * qd + lane + 32 * e]) : 0.f;
-            for (int t = 0; t < R; t++) {
-                if (!visible(t, j)) continue;
-                float acc = 0.f;
-#pragma unroll
-                for (int e = 0; e < 8; e++)
-                    if (e < ne) acc += qsh[t][lane + 32 * e] * kv[e];
-#pragma unroll
-                for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-                if (lane == 0) sc[(size_t)t * sstride + j] = bf16_round(bf16_round(acc) * scale);
-            }
+        for (int ks = 0; ks < 16; ks++) {
+            if (ks >= nks) break;
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(a0, a1, a2, a3, kt + swz(r0 + (lane & 15), ks * 2 + (lane >> 4), qd * 2));
+            mma_bf16_16816(c0, c1, c2, c3, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+        }
+        // c0/c1: position r0+g, rows 2q4 / 2q4+1; c2/c3: position r0+g+8
+        const int pa = ti * ATJ + r0 + g, pbp = pa + 8, t0 = 2 * q4, t1 = t0 + 1;
+        if (pa < nmax) {
+            if (t0 < R) sc[(size_t)t0 * sstride + pa] = bf16_round(bf16_round(c0) * scale);
+            if (t1 < R) sc[(size_t)t1 * sstride + pa] = bf16_round(bf16_round(c1) * scale);
+        }
+        if (pbp < nmax) {
+            if (t0 < R) sc[(size_t)t0 * sstride + pbp] = bf16_round(bf16_round(c2) * scale);
+            if (t1 < R) sc[(size_t)t1 * sstride + pbp] = bf16_round(bf16_round(c3) * scale);
         }
         __syncthreads();
     }
-    // softmax per row over its visible positions (fixed-order block
-    // reductions), stored back as p = bf16(e / sum) with 0 for the rest
-    for (int t = 0; t < R; t++) {
+    // ---- softmax: warp t owns row t; lane 0's sums are broadcast so every
+    // lane uses the same bits
+    if (warp < R) {
+        const int t = warp, qpos = base + t;
         float *srow = sc + (size_t)t * sstride;
+        uint16_t *prow = pb + (size_t)t * sstride;
         float m = -3.4028234663852886e+38f;
-        for (int j = threadIdx.x; j <= base + t; j += blockDim.x)
+        for (int j = lane; j <= qpos; j += 32)
             if (visible(t, j)) m = fmaxf(m, srow[j]);
-        red[threadIdx.x] = m;
-        __syncthreads();
-        for (int s = blockDim.x / 2; s; s >>= 1) {
-            if ((int)threadIdx.x < s) red[threadIdx.x] = fmaxf(red[threadIdx.x], red[threadIdx.x + s]);
-            __syncthreads();
-        }
-        const float mx = red[0];
-        __syncthreads();
+#pragma unroll
+        for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
         float su = 0.f;
-        for (int j = threadIdx.x; j <= base + t; j += blockDim.x)
+        for (int j = lane; j <= qpos; j += 32)
             if (visible(t, j)) {
-                const float e = expf(srow[j] - mx);
+                const float e = expf(srow[j] - m);
                 srow[j] = e;
                 su += e;
             }
-        red[threadIdx.x] = su;
-        __syncthreads();
-        for (int s = blockDim.x / 2; s; s >>= 1) {
-            if ((int)threadIdx.x < s) red[threadIdx.x] = red[threadIdx.x] + red[threadIdx.x + s];
-            __syncthreads();
-        }
-        const float sum = red[0];
-        for (int j = threadIdx.x; j <= base + t; j += blockDim.x)
-            srow[j] = visible(t, j) ? bf16_round(srow[j] / sum) : 0.f;
-        __syncthreads();
-    }
-    // o[t][dv] = bf16(sum_{j <= base+t} p_j * v_j[dv]), ascending j
-    float acc[MAXR];
 #pragma unroll
-    for (int t = 0; t < MAXR; t++) acc[t] = 0.f;
-    const int dv = threadIdx.x;               // vd <= blockDim.x
+        for (int off = 16; off; off >>= 1) su += __shfl_xor_sync(0xffffffffu, su, off);
+        su = __shfl_sync(0xffffffffu, su, 0);
+        const int jend = nt * ATJ;
+        for (int j = lane; j < jend; j += 32)
+            prow[j] = (j <= qpos && visible(t, j)) ? bf16_bits(srow[j] / su) : (uint16_t)0;
+    }
+    __syncthreads();
+    // ---- output: warp w owns dv tiles mt = w, w+8, ... (16 dv each)
+    const int nmt = vd / 16;
+    float acc[2][4];
+#pragma unroll
+    for (int u = 0; u < 2; u++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[u][e] = 0.f;
     stage(ds.v, vd, 0, 0, true);
     for (int ti = 0; ti < nt; ti++) {
         if (ti + 1 < nt) stage(ds.v, vd, ti + 1, (ti + 1) & 1, true);
         else cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        const uint16_t *vt = tile(ti & 1);
-        const float *pt = ptile(ti & 1);
-        if (dv < vd) {
-            const int jn = min(ATJ, nmax - ti * ATJ);
-            for (int jj = 0; jj < jn; jj++) {
-                const int j = ti * ATJ + jj;
-                const float vj = bf16_f32(vt[jj * vd + dv]);
+        const uint8_t *vt = kv0 + (ti & 1) * TB, *pt = pt0 + (ti & 1) * MAXR * PROW;
 #pragma unroll
-                for (int t = 0; t < MAXR; t++)
-                    if (t < R && j <= base + t) acc[t] += pt[t * ATJ + jj] * vj;
+        for (int ks = 0; ks < ATJ / 16; ks++) {
+            uint32_t b0, b1;
+            ldsm_x2(b0, b1, pt + (lane & 7) * PROW + (ks * 16 + ((lane >> 3) & 1) * 8) * 2);
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int mt = warp + 8 * u;
+                if (mt >= nmt) break;
+                // matrices: (dv 0-7, j 0-7), (dv 8-15, j 0-7), (dv 0-7, j 8-15), (dv 8-15, j 8-15)
+                const int mi = lane >> 3;
+                const int jr = ks * 16 + (mi >> 1) * 8 + (lane & 7), ch = mt * 2 + (mi & 1);
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4_t(a0, a1, a2, a3, vt + swz(jr, ch, vd * 2));
+                mma_bf16_16816(acc[u][0], acc[u][1], acc[u][2], acc[u][3], a0, a1, a2, a3, b0, b1);
             }
         }
         __syncthreads();
     }
-    if (dv < vd) {
+    // acc: (dv = 16mt+g, rows 2q4 / 2q4+1) and (dv + 8, ...)
 #pragma unroll
-        for (int t = 0; t < MAXR; t++)
-            if (t < R) out[(size_t)t * AH * vd + (size_t)h * vd + dv] = bf16_bits(acc[t]);
+    for (int u = 0; u < 2; u++) {
+        const int mt = warp + 8 * u;
+        if (mt >= nmt) break;
+        const int dv = mt * 16 + g, t0 = 2 * q4, t1 = t0 + 1;
+        if (t0 < R) {
+            out[(size_t)t0 * AH * vd + (size_t)h * vd + dv] = bf16_bits(acc[u][0]);
+            out[(size_t)t0 * AH * vd + (size_t)h * vd + dv + 8] = bf16_bits(acc[u][2]);
+        }
+        if (t1 < R) {
+            out[(size_t)t1 * AH * vd + (size_t)h * vd + dv] = bf16_bits(acc[u][1]);
+            out[(size_t)t1 * AH * vd + (size_t)h * vd + dv + 8] = bf16_bits(acc[u][3]);
+        }
     }
 }
 
@@ -743,7 +775,7 @@ static size_t hc_pre_smem(const Dims &D) {
 
 static size_t dsa_attn_smem(const Dims &D) {
     const int w = D.qd > D.vd ? D.qd : D.vd;
-    return (size_t)2 * ATJ * w * 2 + (size_t)2 * MAXR * ATJ * 4;
+    return (size_t)2 * ATJ * w * 2 + (size_t)2 * MAXR * (ATJ + 8) * 2 + (size_t)MAXR * (D.qd + 8) * 2;
 }
 
 // Leaves of the numpy pairwise recursion over n (what block_pw's 256-entry
@@ -758,7 +790,7 @@ int layers_prepare(const Dims &D) {
     const int rows[] = {D.hc * D.d, D.d, D.ql, D.kl, D.ID, D.D};
     for (int n : rows)
         if (n > 0 && pw_leaves(n) > 256) return -1;
-    if (D.K < 2 || D.K > 9 || D.kpool > 16 || D.qd > 256 || D.vd > 256 || D.qd % 32 || D.vd % 8 ||
+    if (D.K < 2 || D.K > 9 || D.kpool > 16 || D.qd > 256 || D.vd > 256 || D.qd % 64 || D.vd % 64 ||
         D.IH * D.ID > 32 * 128)
         return -1;
     if (cudaFuncSetAttribute(k_dsa_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsa_attn_smem(D)))
@@ -883,7 +915,8 @@ int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, in
     k_dsa_select<<<R, 256, 0, st>>>(S.iscore, base_n, D.kpool, D.topk / D.kpool, S.maxpools, S.isel);
     if (ok_launch()) return -1;
     k_dsa_attn<<<D.AH, 256, dsa_attn_smem(D), st>>>(S.q, base_n, R, D.AH, D.qd, D.vd, D.kpool, S.maxpools,
-                                                     S.isel, DS, (float *)S.attn_scores, S.attn_sstride, S.attn);
+                                                     S.isel, DS, (float *)S.attn_scores, S.attn_p,
+                                                     S.attn_sstride, S.attn);
     if (ok_launch()) return -1;
     GemvDesc o{};
     o.W = W.o_c; o.WS = W.o_s; o.nkb = ((long)D.AH * D.vd + 127) / 128; o.x = S.attn; o.ldx = (long)D.AH * D.vd;

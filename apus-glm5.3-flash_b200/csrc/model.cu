@@ -340,8 +340,9 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
     S.attn = (uint16_t *)A((size_t)R * D.AH * D.vd * 2);
     // scores row: every position a call can see, plus a full attention tile
     // past it (the tile loader reads whole tiles), in 16-byte units
-    S.attn_sstride = (m->cap + SLACK + MAXR + 64 + 3) & ~3;
+    S.attn_sstride = (m->cap + SLACK + MAXR + 128 + 7) & ~7;
     S.attn_scores = (float *)A((size_t)D.AH * R * S.attn_sstride * 4);
+    S.attn_p = (uint16_t *)A((size_t)D.AH * R * S.attn_sstride * 2);
     S.yn = (uint16_t *)A((size_t)R * d * 2);
     S.logits = (uint16_t *)A((size_t)R * D.V * 2);
     S.amax = (unsigned long long *)A(R * 8);

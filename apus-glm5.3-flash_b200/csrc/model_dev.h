@@ -116,7 +116,8 @@ struct Scratch {
     float *iscore;          // [R][maxpools]
     uint8_t *isel;          // [R][maxpools] pool selected
     uint16_t *attn;         // [R][AH*vd]
-    float *attn_scores;     // [AH][R][attn_sstride] attention scores
+    float *attn_scores;     // [AH][MAXR][attn_sstride] attention scores
+    uint16_t *attn_p;       // [AH][MAXR][attn_sstride] attention probabilities (BF16)
     int attn_sstride;       // >= cache capacity
     uint16_t *yn;           // [R][d] post-final-norm rows
     uint16_t *logits;       // [R][V] (optional)
