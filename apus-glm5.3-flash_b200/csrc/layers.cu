@@ -135,15 +135,60 @@ APUS_DEV float block_pw(const float *a, int n, float *leaf_buf, float *out_sh) {
 
 // Weighted RMSNorm of one row held as fp32 in smem (c/gdsa.h:258-274):
 // var = pairwise mean of squares; t = bf16(x * (1/sqrt(var+eps))); y = bf16(w*t).
+APUS_DEV bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+// Row x[0..n) (BF16) -> fp32 in shared memory; 16-byte loads when aligned,
+// every load of a thread issued before any is used.
+APUS_DEV void load_row_f32(const uint16_t *x, int n, float *xs) {
+    if (n % 8 == 0 && al16(x)) {
+        for (int c0 = threadIdx.x; c0 < n / 8; c0 += 4 * blockDim.x) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int c = c0 + u * blockDim.x;
+                v[u] = c < n / 8 ? *(const uint4 *)(x + c * 8) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int c = c0 + u * blockDim.x;
+                if (c >= n / 8) break;
+                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    xs[c * 8 + 2 * e] = bf16lo(w[e]);
+                    xs[c * 8 + 2 * e + 1] = bf16hi(w[e]);
+                }
+            }
+        }
+    } else {
+#pragma unroll 4
+        for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = bf16_f32(x[i]);
+    }
+}
+
 APUS_DEV void rmsnorm_row_smem(float *xs, float *sq, int n, const uint16_t *w, float eps, uint16_t *y,
                                float *leaf, float *res) {
     for (int i = threadIdx.x; i < n; i += blockDim.x) sq[i] = xs[i] * xs[i];
     __syncthreads();
     const float var = block_pw(sq, n, leaf, res) / (float)n;
     const float inv = 1.0f / sqrtf(var + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float t = bf16_round(xs[i] * inv);
-        y[i] = bf16_bits(bf16_f32(w[i]) * t);
+    if (n % 8 == 0 && al16(w) && al16(y)) {
+        for (int c = threadIdx.x; c < n / 8; c += blockDim.x) {
+            const uint4 wv = *(const uint4 *)(w + c * 8);
+            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float t0 = bf16_round(xs[c * 8 + 2 * e] * inv), t1 = bf16_round(xs[c * 8 + 2 * e + 1] * inv);
+                o[e] = (uint32_t)bf16_bits(bf16lo(ww[e]) * t0) | ((uint32_t)bf16_bits(bf16hi(ww[e]) * t1) << 16);
+            }
+            *(uint4 *)(y + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const float t = bf16_round(xs[i] * inv);
+            y[i] = bf16_bits(bf16_f32(w[i]) * t);
+        }
     }
 }
 
@@ -235,81 +280,110 @@ APUS_DEV void hc_maps(const float *m, const float *scale, const float *base, int
     }
 }
 
-// mHC pre-mix of one row, fused (c/gmhc.h:187-276 then c/gdsa.h:258-274):
-// the inverse RMS of the flattened hc*d streams, the (2+hc)*hc mixes
-// (fp32, never rounded), gates + Sinkhorn, the collapse
-// bf16(sum_j pre_j h_j) and the layer's weighted RMSNorm.  One CTA of 512
-// threads per row; dynamic smem = max(hc*d, 2*d) floats.
-__global__ void __launch_bounds__(512) k_hc_pre(const uint16_t *h4, const uint16_t *fn, const float *scale,
-                                                const float *base, const uint16_t *norm_w, int d, int hc,
-                                                int iters, float hc_eps, float eps, float *post_out,
-                                                float *comb_out, uint16_t *x_out) {
-    extern __shared__ float fl[];
-    __shared__ float mixs[80], pre[8], post[8], comb[64], leaf[256], res;
-    const int r = blockIdx.x, n = hc * d, nmix = (2 + hc) * hc;
-    const uint16_t *x = h4 + (size_t)r * n;
-    // squares -> pairwise mean (c/gmhc.h:187-195)
-    for (int i = threadIdx.x * 8; i < n; i += blockDim.x * 8) {
-        const uint4 v = *(const uint4 *)(x + i);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const float lo = bf16lo(w[e]), hi = bf16hi(w[e]);
-            fl[i + 2 * e] = lo * lo;
-            fl[i + 2 * e + 1] = hi * hi;
-        }
-    }
+// mHC pre-mix (c/gmhc.h:187-276, then the layer RMSNorm c/gdsa.h:258-274),
+// in three launches so the 24-row mix matrix is read by many SMs at once:
+//   k_hc_rms  one CTA per row: inverse RMS of the flattened hc*d streams;
+//   k_hc_mix  CTA (j, chunk): partial mixes of row-chunk `chunk` of fn[j] for
+//             every row of the call (fn read once), fixed-order reductions;
+//   k_hc_pre  one CTA per row: mixes = ascending sum of the partials, gates +
+//             Sinkhorn, the collapse bf16(sum_j pre_j h_j) and the RMSNorm.
+#define HC_MIX_THREADS 128
+#define HC_MIX_CHUNK (8 * HC_MIX_THREADS)
+__global__ void __launch_bounds__(512) k_hc_rms(const uint16_t *h4, int n, float eps, float *rms) {
+    extern __shared__ float sq[];
+    __shared__ float leaf[256], res;
+    load_row_f32(h4 + (size_t)blockIdx.x * n, n, sq);
     __syncthreads();
-    const float inv = 1.0f / sqrtf(block_pw(fl, n, leaf, &res) / (float)n + eps);
-    // flat = x * inv, then mixes[j] = sum_i fn[j][i] * flat[i]: warp per mix,
-    // lanes over 8-element chunks, fixed shuffle tree
-    for (int i = threadIdx.x * 8; i < n; i += blockDim.x * 8) {
-        const uint4 v = *(const uint4 *)(x + i);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            fl[i + 2 * e] = bf16lo(w[e]) * inv;
-            fl[i + 2 * e + 1] = bf16hi(w[e]) * inv;
-        }
-    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) sq[i] = sq[i] * sq[i];
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
-    for (int j = warp; j < nmix; j += nwarp) {
-        const uint16_t *f = fn + (size_t)j * n;
+    const float var = block_pw(sq, n, leaf, &res) / (float)n;
+    if (threadIdx.x == 0) rms[blockIdx.x] = 1.0f / sqrtf(var + eps);
+}
+
+// part[r][j][chunk] = sum over the chunk of fn[j][i] * (x[r][i] * inv[r]):
+// thread sums its 8 elements in order, then a fixed warp tree and a fixed
+// order over the 4 warps.
+__global__ void __launch_bounds__(HC_MIX_THREADS) k_hc_mix(const uint16_t *fn, const uint16_t *h4, const float *rms,
+                                                         int n, int nmix, int nchunk, int R, float *part) {
+    const int j = blockIdx.x, ch = blockIdx.y;
+    const int i0 = ch * HC_MIX_CHUNK + threadIdx.x * 8;
+    const bool in = i0 < n;
+    const uint4 wv = in ? __ldg((const uint4 *)(fn + (size_t)j * n + i0)) : make_uint4(0, 0, 0, 0);
+    uint4 xv[MAXR];
+#pragma unroll
+    for (int r = 0; r < MAXR; r++)
+        xv[r] = (in && r < R) ? *(const uint4 *)(h4 + (size_t)r * n + i0) : make_uint4(0, 0, 0, 0);
+    __shared__ float red[MAXR][HC_MIX_THREADS / 32];
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int r = 0; r < MAXR; r++) {
+        if (r >= R) break;
+        const float inv = rms[r];
+        const uint32_t xx[4] = {xv[r].x, xv[r].y, xv[r].z, xv[r].w};
         float acc = 0.f;
-        for (int c0 = lane * 8; c0 < n; c0 += 256 * 8) {
-            uint4 wv[8];                      // 8 weight loads in flight per lane
 #pragma unroll
-            for (int u = 0; u < 8; u++)
-                wv[u] = c0 + u * 256 < n ? __ldg((const uint4 *)(f + c0 + u * 256)) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int c = c0 + u * 256;
-                if (c >= n) break;
-                const float4 a = *(const float4 *)(fl + c), b = *(const float4 *)(fl + c + 4);
-                acc += bf16lo(wv[u].x) * a.x;
-                acc += bf16hi(wv[u].x) * a.y;
-                acc += bf16lo(wv[u].y) * a.z;
-                acc += bf16hi(wv[u].y) * a.w;
-                acc += bf16lo(wv[u].z) * b.x;
-                acc += bf16hi(wv[u].z) * b.y;
-                acc += bf16lo(wv[u].w) * b.z;
-                acc += bf16hi(wv[u].w) * b.w;
-            }
+        for (int e = 0; e < 4; e++) {
+            acc += bf16lo(ww[e]) * (bf16lo(xx[e]) * inv);
+            acc += bf16hi(ww[e]) * (bf16hi(xx[e]) * inv);
         }
 #pragma unroll
         for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-        if (lane == 0) mixs[j] = acc;
+        if ((threadIdx.x & 31) == 0) red[r][threadIdx.x >> 5] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x < R) {
+        const int r = threadIdx.x;
+        float v = red[r][0];
+        for (int w = 1; w < HC_MIX_THREADS / 32; w++) v += red[r][w];
+        part[((size_t)r * nmix + j) * nchunk + ch] = v;
+    }
+}
+
+__global__ void __launch_bounds__(512) k_hc_pre(const uint16_t *h4, const float *part, int nchunk,
+                                                const float *scale, const float *base, const uint16_t *norm_w, int d,
+                                                int hc, int iters, float hc_eps, float eps, float *post_out,
+                                                float *comb_out, uint16_t *x_out) {
+    extern __shared__ float ys[];                     // [d] collapsed row + [d] squares
+    float *sq = ys + d;
+    __shared__ float mixs[80], pre[8], post[8], comb[64], leaf[256], res;
+    const int r = blockIdx.x, nmix = (2 + hc) * hc;
+    const uint16_t *x = h4 + (size_t)r * hc * d;
+    if ((int)threadIdx.x < nmix) {
+        // ascending sum of the chunk partials, loads issued 16 at a time
+        const float *pp = part + ((size_t)r * nmix + threadIdx.x) * nchunk;
+        float v = 0.f;
+        for (int c0 = 0; c0 < nchunk; c0 += 16) {
+            float t[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) t[u] = c0 + u < nchunk ? pp[c0 + u] : 0.f;
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                if (c0 + u < nchunk) v = (c0 + u == 0) ? t[u] : v + t[u];
+        }
+        mixs[threadIdx.x] = v;
     }
     __syncthreads();
     hc_maps(mixs, scale, base, hc, iters, hc_eps, r, pre, post, comb, post_out, comb_out);
     __syncthreads();
-    // collapse (c/gmhc.h:267-276) + the layer norm, reusing the smem
-    float *ys = fl, *sq = fl + d;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        float acc = pre[0] * bf16_f32(x[i]);
-        for (int j = 1; j < hc; j++) acc += pre[j] * bf16_f32(x[(size_t)j * d + i]);
-        ys[i] = bf16_round(acc);
+    // collapse (c/gmhc.h:267-276): 8 consecutive columns per thread, the hc
+    // stream loads issued together
+    for (int c = threadIdx.x; c < d / 8; c += blockDim.x) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (j < hc) v[j] = *(const uint4 *)(x + (size_t)j * d + c * 8);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (j >= hc) break;
+                const uint32_t word = (e >> 1) == 0 ? v[j].x : (e >> 1) == 1 ? v[j].y : (e >> 1) == 2 ? v[j].z : v[j].w;
+                const float xe = (e & 1) ? bf16hi(word) : bf16lo(word);
+                acc = j == 0 ? pre[0] * xe : acc + pre[j] * xe;
+            }
+            ys[c * 8 + e] = bf16_round(acc);
+        }
     }
     __syncthreads();
     rmsnorm_row_smem(ys, sq, d, norm_w, eps, x_out + (size_t)r * d, leaf, &res);
@@ -338,10 +412,23 @@ __global__ void k_head_norm(const uint16_t *h4, const uint16_t *w, int d, int hc
     __shared__ float leaf[256], res;
     const int r = blockIdx.x;
     const uint16_t *x4 = h4 + (size_t)r * hc * d;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        float acc = bf16_f32(x4[i]);
-        for (int j = 1; j < hc; j++) acc += bf16_f32(x4[(size_t)j * d + i]);
-        ys[i] = bf16_round(acc / (float)hc);
+    for (int c = threadIdx.x; c < d / 8; c += blockDim.x) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (j < hc) v[j] = *(const uint4 *)(x4 + (size_t)j * d + c * 8);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (j >= hc) break;
+                const uint32_t word = (e >> 1) == 0 ? v[j].x : (e >> 1) == 1 ? v[j].y : (e >> 1) == 2 ? v[j].z : v[j].w;
+                const float xe = (e & 1) ? bf16hi(word) : bf16lo(word);
+                acc = j == 0 ? xe : acc + xe;
+            }
+            ys[c * 8 + e] = bf16_round(acc / (float)hc);
+        }
     }
     __syncthreads();
     rmsnorm_row_smem(ys, sq, d, w, eps, yn + (size_t)r * d, leaf, &res);
@@ -353,7 +440,7 @@ __global__ void k_rmsnorm_rows(const uint16_t *x, long ldx, const uint16_t *w, i
     float *sq = ys + n;
     __shared__ float leaf[256], res;
     const int r = blockIdx.x;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ys[i] = bf16_f32(x[(size_t)r * ldx + i]);
+    load_row_f32(x + (size_t)r * ldx, n, ys);
     __syncthreads();
     rmsnorm_row_smem(ys, sq, n, w, eps, y + (size_t)r * ldy, leaf, &res);
 }
@@ -768,11 +855,6 @@ using namespace apus;
 
 static int ok_launch() { return cudaGetLastError() == cudaSuccess ? 0 : -1; }
 
-static size_t hc_pre_smem(const Dims &D) {
-    const int n = D.hc * D.d > 2 * D.d ? D.hc * D.d : 2 * D.d;
-    return (size_t)n * 4;
-}
-
 static size_t dsa_attn_smem(const Dims &D) {
     const int w = D.qd > D.vd ? D.qd : D.vd;
     return (size_t)2 * ATJ * w * 2 + (size_t)2 * MAXR * (ATJ + 8) * 2 + (size_t)MAXR * (D.qd + 8) * 2;
@@ -799,8 +881,9 @@ int layers_prepare(const Dims &D) {
     const int maxrow = D.d > D.ql ? (D.d > D.kl ? D.d : D.kl) : (D.ql > D.kl ? D.ql : D.kl);
     const size_t need_rms = (size_t)D.hc * D.d * 4, need_row = (size_t)2 * maxrow * 4;
     if (need_rms > 200 * 1024 || need_row > 200 * 1024) return -1;
-    if (D.d % 8 || D.hc * D.hc > 64 || (2 + D.hc) * D.hc > 80 || hc_pre_smem(D) > 200 * 1024) return -1;
-    if (cudaFuncSetAttribute(k_hc_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hc_pre_smem(D)) ||
+    if (D.d % 8 || D.hc > 8 || (2 + D.hc) * D.hc > 80 || (size_t)D.hc * D.d * 4 > 200 * 1024) return -1;
+    if (cudaFuncSetAttribute(k_hc_rms, cudaFuncAttributeMaxDynamicSharedMemorySize, D.hc * D.d * 4) ||
+        cudaFuncSetAttribute(k_hc_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
         cudaFuncSetAttribute(k_head_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
         cudaFuncSetAttribute(k_rmsnorm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row))
         return -1;
@@ -814,9 +897,12 @@ int k_embed_launch(const uint16_t *embed, const int32_t *ids, int R, int d, int 
 
 int hc_pre_launch(const Dims &D, const LayerW &W, int site, const uint16_t *h4, int R, Scratch &S,
                   cudaStream_t st) {
-    k_hc_pre<<<R, 512, hc_pre_smem(D), st>>>(h4, W.hc_fn[site], W.hc_scale[site], W.hc_base[site],
-                                             site ? W.post_norm : W.input_norm, D.d, D.hc, D.sinkhorn_iters,
-                                             D.hc_eps, D.eps, S.post, S.comb, S.x);
+    const int n = D.hc * D.d, nmix = (2 + D.hc) * D.hc, nchunk = (n + HC_MIX_CHUNK - 1) / HC_MIX_CHUNK;
+    k_hc_rms<<<R, 512, (size_t)n * 4, st>>>(h4, n, D.eps, S.rms);
+    k_hc_mix<<<dim3(nmix, nchunk), HC_MIX_THREADS, 0, st>>>(W.hc_fn[site], h4, S.rms, n, nmix, nchunk, R, S.mix);
+    k_hc_pre<<<R, 512, (size_t)2 * D.d * 4, st>>>(h4, S.mix, nchunk, W.hc_scale[site], W.hc_base[site],
+                                                  site ? W.post_norm : W.input_norm, D.d, D.hc, D.sinkhorn_iters,
+                                                  D.hc_eps, D.eps, S.post, S.comb, S.x);
     return ok_launch();
 }
 

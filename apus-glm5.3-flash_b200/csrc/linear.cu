@@ -146,6 +146,8 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
     uint64_t *empty = full + NSTAGE;
     __shared__ unsigned long long best_sh[8];
     __shared__ int abort_sh, ticket_sh;
+    __shared__ int xexp_sh[8];       // FP8: max BF16 exponent field of each staged row
+    __shared__ float xinv_sh[8];     // FP8: 2^-k, the inverse of the row's staging scale
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long rowbytes = FP8 ? d.K : 2 * d.K;
@@ -226,6 +228,10 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
         if (FP8 && it.grouped) WS += (size_t)d.gexpert[p] * d.s_estride;
         if (XS && xsrc != xsrc_staged) {   // stage x[:, k0:k0+klen]: row r at xs + r*xstride
             named_bar_sync(1, 256);          // previous item's readers are done
+            if (FP8) {
+                if (threadIdx.x < 8) xexp_sh[threadIdx.x] = 0;
+                named_bar_sync(1, 256);
+            }
             const int per_row = (int)(klen / 8), total = d.R * per_row;   // <= 8 per thread
             if (!d.x_swiglu) {
                 for (int u0 = 0; u0 < 8; u0 += 4) {    // two batches of 4 loads in flight
@@ -238,7 +244,10 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
 #pragma unroll
                     for (int u = 0; u < 4; u++) {
                         const int q = threadIdx.x + (u0 + u) * 256;
-                        if (q < total) *(uint4 *)(xs + (q / per_row) * xstride + (q % per_row) * 8) = v[u];
+                        if (q < total) {
+                            *(uint4 *)(xs + (q / per_row) * xstride + (q % per_row) * 8) = v[u];
+                            if (FP8) atomicMax(&xexp_sh[q / per_row], bf16x8_max_exp(v[u]));
+                        }
                     }
                 }
             } else {
@@ -265,18 +274,40 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
                         }
                         o[e] = (uint32_t)hh[0] | ((uint32_t)hh[1] << 16);
                     }
-                    *(uint4 *)(xs + r * xstride + cc) = make_uint4(o[0], o[1], o[2], o[3]);
+                    const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+                    *(uint4 *)(xs + r * xstride + cc) = ov;
+                    if (FP8) atomicMax(&xexp_sh[r], bf16x8_max_exp(ov));
                 }
             }
             named_bar_sync(1, 256);
+            if (FP8) {
+                // FP8 weights meet the activations in an f16 MMA: each staged
+                // row is scaled by an exact power of two 2^k that puts its
+                // largest magnitude in [2^14, 2^15), converted to f16 in place,
+                // and 2^-k is applied to the row's partial sums
+                for (int q = threadIdx.x; q < total; q += 256) {
+                    const int r = q / per_row;
+                    uint16_t *xp = xs + r * xstride + (q % per_row) * 8;
+                    const uint4 v = *(const uint4 *)xp;
+                    const float sc = __int_as_float((127 + stage_shift(xexp_sh[r])) << 23);
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const __half2 hv = __floats2half2_rn(bf16lo(w[e]) * sc, bf16hi(w[e]) * sc);
+                        o[e] = *reinterpret_cast<const uint32_t *>(&hv);
+                    }
+                    *(uint4 *)xp = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+                if (threadIdx.x < 8) xinv_sh[threadIdx.x] = __int_as_float((127 - stage_shift(xexp_sh[threadIdx.x])) << 23);
+                named_bar_sync(1, 256);
+            }
             xsrc_staged = xsrc;
         }
         const long row0 = t * TR;
-        const float *srA = nullptr, *srB = nullptr;
-        if (FP8) {   // scale rows of weight rows g and g+8
-            srA = WS + (size_t)(min(row0 + g, d.O - 1) >> 7) * d.nkb;
-            srB = WS + (size_t)(min(row0 + g + 8, d.O - 1) >> 7) * d.nkb;
-        }
+        const float *srA = nullptr;
+        if (FP8)     // the tile's 16 rows lie in one 128-row scale block
+            srA = WS + (size_t)(row0 >> 7) * d.nkb;
         float acc[4][4];
 #pragma unroll
         for (int q = 0; q < 4; q++) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
@@ -286,13 +317,12 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
             const int nst = (int)(min((long)CH, kbytes - off) / 64);
             const int s0 = nst * warp / 8, s1 = nst * (warp + 1) / 8;
             constexpr int MAXS = CH / 64 / 8 + 1;
-            float scA[MAXS], scB[MAXS];
+            float scA[MAXS];
             if (FP8) {   // scales first: their latency hides under the barrier wait
 #pragma unroll
                 for (int q = 0; q < MAXS; q++) {
                     const long kbk = (kb0 + off) / 128 + ((s0 + q) >> 1);
                     scA[q] = (s0 + q < s1) ? __ldg(srA + kbk) : 0.f;
-                    scB[q] = (s0 + q < s1) ? __ldg(srB + kbk) : 0.f;
                 }
             }
             const bool have = mbar_wait(&full[s], (uint32_t)((c / NSTAGE) & 1), &abort_sh,
@@ -308,27 +338,28 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
                 const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
                 const long ls = off / 64 + st;                  // step within the k-range
                 if (FP8) {
+                    // x is staged as scaled f16 (XS is always on for FP8)
                     uint32_t xw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                     if (xrow_ok) {
-                        uint4 xa, xb;
-                        if (XS) {
-                            const uint16_t *xp = xs + g * xstride + ls * 64 + 16 * t4;
-                            xa = lds128(xp); xb = lds128(xp + 8);
-                        } else {
-                            const uint16_t *xp = xsrc + (size_t)g * d.ldx + k0 + ls * 64 + 16 * t4;
-                            xa = ld_nc16(xp); xb = ld_nc16(xp + 8);
-                        }
+                        const uint16_t *xp = xs + g * xstride + ls * 64 + 16 * t4;
+                        const uint4 xa = lds128(xp), xb = lds128(xp + 8);
                         xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
                         xw[4] = xb.x; xw[5] = xb.y; xw[6] = xb.z; xw[7] = xb.w;
                     }
+                    // E4M3 -> f16 is exact; the 128x128 block scale (one per
+                    // step: the tile's 16 rows share a block) multiplies the
+                    // step's partial, two MMA chains per step
+                    float u[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
-                        uint32_t a0, a2, a1, a3;
-                        dequant4(wa[j], scA[q], a0, a2);
-                        dequant4(wb[j], scB[q], a1, a3);
-                        mma_bf16_16816(acc[j][0], acc[j][1], acc[j][2], acc[j][3],
-                                       a0, a1, a2, a3, xw[2 * j], xw[2 * j + 1]);
+                        const uint32_t a0 = cvt_e4m3x2_f16x2(wa[j] & 0xffffu), a2 = cvt_e4m3x2_f16x2(wa[j] >> 16);
+                        const uint32_t a1 = cvt_e4m3x2_f16x2(wb[j] & 0xffffu), a3 = cvt_e4m3x2_f16x2(wb[j] >> 16);
+                        mma_f16_16816(u[j & 1][0], u[j & 1][1], u[j & 1][2], u[j & 1][3], a0, a1, a2, a3,
+                                      xw[2 * j], xw[2 * j + 1]);
                     }
+                    const float sc = scA[q];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) acc[0][e] = acc[0][e] + (u[0][e] + u[1][e]) * sc;
                 } else {
                     uint32_t xw[4] = {0, 0, 0, 0};
                     if (xrow_ok) {
@@ -354,7 +385,7 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const int xc = 2 * t4 + (e & 1), wr = g + 8 * (e >> 1);
-            pw[xc * TR + wr] = (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+            pw[xc * TR + wr] = FP8 ? acc[0][e] * xinv_sh[xc] : (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
         }
         named_bar_sync(1, 256);
         const int tid = threadIdx.x;
@@ -536,9 +567,23 @@ int gemv_launch(const GemvDesc &d, cudaStream_t st) {
         const bool xs = (long)d.R * (klen * 2 + 16) <= gemvcfg::XMAX;
         if (d.K > gemvcfg::KX && (!d.part || !d.ticket)) return -1;
         if (d.gexpert && (d.K > gemvcfg::KX || !d.gcount || d.gmax < 1)) return -1;
+        if (d.fp8 && !xs) {
+            // FP8 needs the activations staged (as scaled f16): run the rows in
+            // groups that fit; every row's arithmetic is the same either way
+            const int r1 = (int)(gemvcfg::XMAX / (klen * 2 + 16));
+            if (r1 < 1) return -1;
+            GemvDesc a = d, b = d;
+            a.R = r1;
+            b.R = d.R - r1;
+            b.x = d.x + (size_t)r1 * d.ldx;
+            if (d.y) b.y = d.y + (size_t)r1 * d.ldy;
+            if (d.yf) b.yf = d.yf + (size_t)r1 * d.ldyf;
+            if (d.amax) b.amax = d.amax + r1;
+            return gemv_launch(a, st) || gemv_launch(b, st) ? -1 : 0;
+        }
         if (d.x_swiglu && !xs) return -1;
         int rc;
-        if (d.fp8) rc = xs ? launch_tma<true, true>(d, st) : launch_tma<true, false>(d, st);
+        if (d.fp8) rc = launch_tma<true, true>(d, st);
         else rc = xs ? launch_tma<false, true>(d, st) : launch_tma<false, false>(d, st);
         if (rc) return -1;
     } else {

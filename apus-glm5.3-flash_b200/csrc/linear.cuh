@@ -67,6 +67,26 @@ APUS_DEV void dequant4(uint32_t w, float s, uint32_t &b0, uint32_t &b1) {
     b1 = pack_bf16x2(__fmul_rn(f23.x, s), __fmul_rn(f23.y, s));
 }
 
+// Largest BF16 exponent field among 8 packed values.
+APUS_DEV int bf16x8_max_exp(uint4 v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    int m = 0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        m = max(m, (int)((w[e] >> 7) & 0xffu));
+        m = max(m, (int)((w[e] >> 23) & 0xffu));
+    }
+    return m;
+}
+
+// Staging shift k for a row whose largest BF16 exponent field is E: the
+// largest magnitude times 2^k lies in [2^14, 2^15), inside f16's range
+// (clamped so 2^k and 2^-k are normal floats).
+APUS_DEV int stage_shift(int E) {
+    const int k = 141 - E;
+    return k > 126 ? 126 : (k < -126 ? -126 : k);
+}
+
 APUS_DEV void mma_bf16_16816(float &d0, float &d1, float &d2, float &d3,
                              uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                              uint32_t b0, uint32_t b1) {

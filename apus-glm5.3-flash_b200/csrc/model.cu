@@ -320,7 +320,7 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
     S.x = (uint16_t *)A((size_t)R * d * 2);
     S.sub = (uint16_t *)A((size_t)R * d * 2);
     S.rms = (float *)A(R * 4);
-    S.mix = (float *)A((size_t)R * (2 + D.hc) * D.hc * 4);
+    S.mix = (float *)A((size_t)R * (2 + D.hc) * D.hc * ((D.hc * d + 1023) / 1024) * 4);   // mix partials
     S.post = (float *)A((size_t)R * D.hc * 4);
     S.comb = (float *)A((size_t)R * D.hc * D.hc * 4);
     S.kp = (uint16_t *)A((size_t)R * ldkp * 2);

@@ -102,7 +102,7 @@ struct Scratch {
     uint16_t *h4, *h4b;     // [R][hc*d] residual streams (ping-pong)
     uint16_t *x, *sub;      // [R][d]
     float *rms;             // [R] inverse rms of the stream
-    float *mix;             // [R][(2+hc)*hc]
+    float *mix;             // [R][(2+hc)*hc][ceil(hc*d/1024)] partial mixes
     float *post, *comb;     // [R][hc], [R][hc*hc]
     uint16_t *kp;           // KDA projections [R][3qkv+2Dr+H]
     uint16_t *fgo;          // [2][R][qkv]  f_b, g_b outputs

@@ -1,7 +1,8 @@
 """Parity of the linear leaf on the B200: FP8 block dequant (bitwise),
-FP8/BF16 decode GEMV (tolerance: rel 1e-2 and cosine >= 0.9999 per row,
-the north-star bound for GEMM logits), row-count invariance (bitwise) and
-the fused greedy pick (bitwise given the kernel's own logits)."""
+FP8/BF16 decode GEMV (tolerance per row: relative L2 error <= 1e-2 and
+cosine >= 0.9999, the north-star bound for GEMM logits, plus an elementwise
+ceiling), row-count invariance (bitwise) and the fused greedy pick (bitwise
+given the kernel's own logits)."""
 import os
 
 import numpy as np
@@ -13,19 +14,30 @@ from conftest import GOLDEN
 pytestmark = pytest.mark.gpu
 LIN = np.load(os.path.join(GOLDEN, "linear.npz"))
 
-REL_TOL = 1e-2
+REL_TOL = 1e-2        # per row: ||got - ref|| / ||ref||
 COS_TOL = 0.9999
+# Elementwise ceiling, relative to max(|ref|, rms(ref row)).  BF16 weights:
+# only the fp32 summation order differs, so 1e-2.  FP8 weights: the kernel
+# applies each 128x128 block scale to the MMA partial instead of rounding
+# every dequantized weight to BF16 (<= 2^-9 relative per weight), so an
+# output may sit one more BF16 ulp (<= 0.78 %) from the reference: 2e-2.
+# A whole MoE layer (FP8 gate/up -> BF16 SwiGLU -> FP8 down -> BF16-rounded
+# weighted adds) can compound that to a few ulps: callers pass elem=4e-2.
+ELEM_TOL = {False: 1e-2, True: 2e-2}
 
 
-def assert_close_rows(got_codes, ref_codes):
+def assert_close_rows(got_codes, ref_codes, fp8=False, elem=None):
     g = O.f32_of(got_codes).astype(np.float64)
     r = O.f32_of(ref_codes).astype(np.float64)
     for m in range(r.shape[0]):
         scale = np.sqrt(np.mean(r[m] ** 2)) + 1e-30
         err = np.abs(g[m] - r[m])
-        assert np.all(err <= REL_TOL * np.maximum(np.abs(r[m]), scale)), (m, err.max(), scale)
-        if np.linalg.norm(r[m]) > 0:
-            cos = g[m] @ r[m] / (np.linalg.norm(g[m]) * np.linalg.norm(r[m]))
+        tol = elem if elem is not None else ELEM_TOL[fp8]
+        assert np.all(err <= tol * np.maximum(np.abs(r[m]), scale)), (m, err.max(), scale)
+        nr = np.linalg.norm(r[m])
+        if nr > 0:
+            assert np.linalg.norm(g[m] - r[m]) <= REL_TOL * nr, (m, np.linalg.norm(g[m] - r[m]) / nr)
+            cos = g[m] @ r[m] / (np.linalg.norm(g[m]) * nr)
             assert cos >= COS_TOL, (m, cos)
 
 
@@ -93,7 +105,7 @@ def test_fp8_linear_golden(gcuda, i):
     y = np.zeros_like(want)
     assert gcuda.apus_gcuda_fp8blk_linear(O.p(c), O.p(s), O.p(x), O.p(y),
                                           x.shape[0], c.shape[0], c.shape[1]) == 0
-    assert_close_rows(y, want)
+    assert_close_rows(y, want, fp8=True)
 
 
 def _dev_linear(gcuda, fp8, W, S, x):
@@ -123,7 +135,7 @@ def test_fp8_gemv_vs_oracle(gcuda, shape):
     c, s = fp8_weights(rng, O_, K)
     x = O.bf16_of(rng.standard_normal((M, K)).astype(np.float32))
     got = _dev_linear(gcuda, True, c, s, x)
-    assert_close_rows(got, O.fp8_linear(c, s, x))
+    assert_close_rows(got, O.fp8_linear(c, s, x), fp8=True)
 
 
 @pytest.mark.parametrize("shape", [(4, 4096, 4096), (1, 2048, 8192), (5, 288, 4096), (2, 40, 512),
