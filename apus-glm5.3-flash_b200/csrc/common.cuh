@@ -48,6 +48,13 @@ APUS_DEV float sigmoid_np(float x) {
     return x >= 0.0f ? 1.0f / (1.0f + e) : e / (1.0f + e);
 }
 
+// Programmatic dependent launch: a kernel lets the next one in the stream
+// start early (the next one waits with pdl_wait before it reads anything
+// this kernel writes); a no-op when the next kernel was launched without the
+// programmatic-serialization attribute.
+APUS_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+APUS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Widen a packed bf16x2 word: low half is the lower k index.
 APUS_DEV float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 APUS_DEV float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }

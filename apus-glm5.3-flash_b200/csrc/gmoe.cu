@@ -34,64 +34,75 @@ APUS_DEV float pw_sum_small(const float *a, int n) {
     return pw_sum_leaf(a, n);
 }
 
-__global__ void k_moe_route(MoeDev m, int R, const float *logits, const int32_t *forced) {
+__global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float *logits, const int32_t *forced) {
+    pdl_launch_dependents();
     __shared__ float sc[MOE_MAX_R][MOE_MAX_E];
-    __shared__ float bi[MOE_MAX_R][MOE_MAX_E];
-    __shared__ int32_t sel[MOE_MAX_R][MOE_MAX_TOPK];
     __shared__ int flag[MOE_MAX_E + 1];
     __shared__ int slot_of[MOE_MAX_E + 1];
     const int E = m.E, K = m.topk;
-    for (int i = threadIdx.x; i < R * E; i += blockDim.x) {
-        const int r = i / E, e = i % E;
-        const float s = sigmoid_np(logits[(size_t)r * E + e]);
-        sc[r][e] = s;
-        bi[r][e] = s + m.gate_bias[e];
-    }
     for (int e = threadIdx.x; e <= E; e += blockDim.x) flag[e] = 0;
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp < R) {      // one warp per row: k passes of a lowest-index argmax
+    constexpr int EPL = MOE_MAX_E / 32;       // experts per lane: e = lane + 32u
+    if (warp < R) {      // one warp per row
         const int r = warp;
+        float lg[EPL], bs[EPL];
+#pragma unroll
+        for (int u = 0; u < EPL; u++) {       // every load first
+            const int e = lane + 32 * u;
+            lg[u] = e < E ? logits[(size_t)r * E + e] : 0.f;
+            bs[u] = e < E ? m.gate_bias[e] : 0.f;
+        }
+        // selection key of the biased score: larger value first, lower index
+        // on ties (the strict-greater scan of c/gmoe.h:175-189)
+        unsigned long long key[EPL];
+#pragma unroll
+        for (int u = 0; u < EPL; u++) {
+            const int e = lane + 32 * u;
+            const float s = sigmoid_np(lg[u]);
+            if (e < E) sc[r][e] = s;
+            key[u] = e < E ? argmax_key(s + bs[u], (uint32_t)e) : 0ull;
+        }
+        __syncwarp();
+        int my_sel = -1;                      // lane j < K: the j-th selection
         for (int j = 0; j < K; j++) {
-            float best = 0.f;
-            int bidx = -1;
-            for (int e = lane; e < E; e += 32) {
-                bool used = false;
-                for (int q = 0; q < j; q++) used |= (sel[r][q] == e);
-                if (used) continue;
-                const float v = bi[r][e];
-                if (bidx < 0 || v > best) { best = v; bidx = e; }
-            }
+            unsigned long long best = 0ull;
+#pragma unroll
+            for (int u = 0; u < EPL; u++) best = key[u] > best ? key[u] : best;
 #pragma unroll
             for (int off = 16; off; off >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, best, off);
-                const int oi = __shfl_xor_sync(0xffffffffu, bidx, off);
-                if (oi >= 0 && (bidx < 0 || ov > best || (ov == best && oi < bidx))) { best = ov; bidx = oi; }
+                const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+                best = o > best ? o : best;
             }
-            if (forced) bidx = forced[r * K + j];
-            if (lane == 0) sel[r][j] = bidx;
-            __syncwarp();
+            const int idx = (int)argmax_key_index(best);
+#pragma unroll
+            for (int u = 0; u < EPL; u++)     // the winner leaves the pool
+                if (lane + 32 * u == idx) key[u] = 0ull;
+            const int pick = forced ? forced[r * K + j] : idx;
+            if (lane == j) my_sel = pick;
         }
-        if (lane == 0) {
-            float w[MOE_MAX_TOPK];
-            for (int j = 0; j < K; j++) w[j] = sc[r][sel[r][j]];
-            const float sum = K ? pw_sum_small(w, K) : 0.f;
-            for (int j = 0; j < K; j++) w[j] = w[j] / (sum + 1e-20f) * m.route_scale;
-            // the combine walks the row's experts in ascending index order
-            int32_t id[MOE_MAX_TOPK];
-            for (int j = 0; j < K; j++) id[j] = sel[r][j];
-            for (int a = 1; a < K; a++)
-                for (int b = a; b > 0 && id[b - 1] > id[b]; b--) {
-                    int32_t ti = id[b]; id[b] = id[b - 1]; id[b - 1] = ti;
-                    float tw = w[b]; w[b] = w[b - 1]; w[b - 1] = tw;
-                }
-            for (int j = 0; j < K; j++) {
-                m.row_expert[r * K + j] = id[j];
-                m.row_weight[r * K + j] = w[j];
-                // unsorted selection, for inspection (c/gmoe.h:112-117 router_idx)
-                m.row_sel[r * K + j] = sel[r][j];
-                atomicExch(&flag[id[j]], 1);
-            }
+        __syncwarp();
+        // weights from the unbiased scores, normalised with the numpy
+        // pairwise sum in selection order (c/gmoe.h:191-208)
+        float w = lane < K ? sc[r][my_sel] : 0.f;
+        float wa[MOE_MAX_TOPK];
+#pragma unroll
+        for (int j = 0; j < MOE_MAX_TOPK; j++) wa[j] = __shfl_sync(0xffffffffu, w, j);
+        const float sum = K ? pw_sum_small(wa, K) : 0.f;
+        w = w / (sum + 1e-20f) * m.route_scale;
+        // ascending expert order for the combine: rank among the selections
+        int rank = 0;
+#pragma unroll
+        for (int j = 0; j < MOE_MAX_TOPK; j++) {
+            const int o = __shfl_sync(0xffffffffu, my_sel, j);
+            if (j < K && lane < K && o < my_sel) rank++;
+        }
+        if (lane < K) {
+            m.row_expert[r * K + rank] = my_sel;
+            m.row_weight[r * K + rank] = w;
+            // unsorted selection, for inspection (c/gmoe.h:112-117 router_idx)
+            m.row_sel[r * K + lane] = my_sel;
+            flag[my_sel] = 1;
         }
     }
     __syncthreads();
@@ -136,25 +147,44 @@ __global__ void k_moe_route(MoeDev m, int R, const float *logits, const int32_t 
 }
 
 // out[r][i] = bf16(y + shared), y = ascending bf16 accumulation of
-// bf16(bf16(expert) * w) (c/gmoe.h:305-336).
+// bf16(bf16(expert) * w) (c/gmoe.h:305-336).  A thread owns 8 consecutive
+// columns of one row; every expert row's 16-byte load is issued first.
 __global__ void k_moe_combine(MoeDev m, int R, uint16_t *out, long ldo) {
-    const int d = m.dim, K = m.topk;
+    pdl_launch_dependents();
+    const int d = m.dim, K = m.topk, nc = d / 8;
     const size_t pstride = (size_t)m.max_r * d;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < (long)R * d;
-         i += (long)gridDim.x * blockDim.x) {
-        const int r = (int)(i / d), c = (int)(i % d);
-        float y = 0.f;
-        for (int j = 0; j < K; j++) {
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * nc) return;
+    const int r = (int)(i / nc), c = (int)(i % nc) * 8;
+    uint4 ev[MOE_MAX_TOPK + 1];
+    float wt[MOE_MAX_TOPK];
+#pragma unroll
+    for (int j = 0; j < MOE_MAX_TOPK; j++)
+        if (j < K) {
             const int p = m.row_prob[r * K + j];
-            const float e = bf16_f32(m.yd[p * pstride + (size_t)r * d + c]);
-            const float contrib = bf16_round(e * m.row_weight[r * K + j]);
-            y = bf16_round(y + contrib);
+            ev[j] = *(const uint4 *)(m.yd + p * pstride + (size_t)r * d + c);
+            wt[j] = m.row_weight[r * K + j];
         }
-        const int ps = m.row_prob_shared[r];
-        const uint16_t shb = m.yd[ps * pstride + (size_t)r * d + c];
+    ev[MOE_MAX_TOPK] = *(const uint4 *)(m.yd + m.row_prob_shared[r] * pstride + (size_t)r * d + c);
+    const uint32_t sw[4] = {ev[MOE_MAX_TOPK].x, ev[MOE_MAX_TOPK].y, ev[MOE_MAX_TOPK].z, ev[MOE_MAX_TOPK].w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        float y = 0.f;
+#pragma unroll
+        for (int j = 0; j < MOE_MAX_TOPK; j++) {
+            if (j >= K) break;
+            const uint32_t wd = (e >> 1) == 0 ? ev[j].x : (e >> 1) == 1 ? ev[j].y : (e >> 1) == 2 ? ev[j].z : ev[j].w;
+            const float ex = (e & 1) ? bf16hi(wd) : bf16lo(wd);
+            y = bf16_round(y + bf16_round(ex * wt[j]));
+        }
+        const uint16_t shb = (uint16_t)((e & 1) ? sw[e >> 1] >> 16 : sw[e >> 1] & 0xffffu);
         // a dense MLP (no routed experts) passes its output through unchanged
-        out[(size_t)r * ldo + c] = K ? bf16_bits(y + bf16_f32(shb)) : shb;
+        const uint16_t v = K ? bf16_bits(y + bf16_f32(shb)) : shb;
+        if (e & 1) o[e >> 1] |= (uint32_t)v << 16;
+        else o[e >> 1] = v;
     }
+    *(uint4 *)(out + (size_t)r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 }  // namespace apus
@@ -202,7 +232,8 @@ int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint
     dn.pdl = m.pdl;
     if (gemv_launch(dn, st)) return -1;
     // 5. ordered combine
-    const long n = (long)R * m.dim;
-    k_moe_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(m, R, out, ldo);
+    if (m.dim % 8 || ((uintptr_t)out & 15) || (ldo % 8)) return -1;
+    const long n = (long)R * (m.dim / 8);
+    k_moe_combine<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(m, R, out, ldo);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

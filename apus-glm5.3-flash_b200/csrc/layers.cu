@@ -195,6 +195,7 @@ APUS_DEV void rmsnorm_row_smem(float *xs, float *sq, int n, const uint16_t *w, f
 // ------------------------------------------------------------------ embed
 
 __global__ void k_embed(const uint16_t *embed, const int32_t *ids, int d, int hc, uint16_t *h4) {
+    pdl_launch_dependents();
     const int r = blockIdx.y;
     const uint16_t *row = embed + (size_t)ids[r] * d;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x) {
@@ -290,6 +291,7 @@ APUS_DEV void hc_maps(const float *m, const float *scale, const float *base, int
 #define HC_MIX_THREADS 128
 #define HC_MIX_CHUNK (8 * HC_MIX_THREADS)
 __global__ void __launch_bounds__(512) k_hc_rms(const uint16_t *h4, int n, float eps, float *rms) {
+    pdl_launch_dependents();
     extern __shared__ float sq[];
     __shared__ float leaf[256], res;
     load_row_f32(h4 + (size_t)blockIdx.x * n, n, sq);
@@ -305,6 +307,7 @@ __global__ void __launch_bounds__(512) k_hc_rms(const uint16_t *h4, int n, float
 // order over the 4 warps.
 __global__ void __launch_bounds__(HC_MIX_THREADS) k_hc_mix(const uint16_t *fn, const uint16_t *h4, const float *rms,
                                                          int n, int nmix, int nchunk, int R, float *part) {
+    pdl_launch_dependents();
     const int j = blockIdx.x, ch = blockIdx.y;
     const int i0 = ch * HC_MIX_CHUNK + threadIdx.x * 8;
     const bool in = i0 < n;
@@ -343,6 +346,7 @@ __global__ void __launch_bounds__(512) k_hc_pre(const uint16_t *h4, const float 
                                                 const float *scale, const float *base, const uint16_t *norm_w, int d,
                                                 int hc, int iters, float hc_eps, float eps, float *post_out,
                                                 float *comb_out, uint16_t *x_out) {
+    pdl_launch_dependents();
     extern __shared__ float ys[];                     // [d] collapsed row + [d] squares
     float *sq = ys + d;
     __shared__ float mixs[80], pre[8], post[8], comb[64], leaf[256], res;
@@ -393,6 +397,7 @@ __global__ void __launch_bounds__(512) k_hc_pre(const uint16_t *h4, const float 
 // bf16(sum_k bf16(comb[k][j]) res[k][i]))
 __global__ void k_hc_post(const uint16_t *x, const uint16_t *h4, const float *post, const float *comb,
                           int d, int hc, uint16_t *out) {
+    pdl_launch_dependents();
     const int r = blockIdx.y;
     for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < hc * d; q += gridDim.x * blockDim.x) {
         const int j = q / d, i = q % d;
@@ -406,7 +411,10 @@ __global__ void k_hc_post(const uint16_t *x, const uint16_t *h4, const float *po
 }
 
 // HyperHead mean (c/gmhc.h:296-304) + final RMSNorm
-__global__ void k_head_norm(const uint16_t *h4, const uint16_t *w, int d, int hc, float eps, uint16_t *yn) {
+__global__ void k_head_norm(const uint16_t *h4, const uint16_t *w, int d, int hc, float eps, uint16_t *yn,
+                            unsigned long long *keys) {
+    pdl_launch_dependents();
+    if (keys && threadIdx.x == 0) keys[blockIdx.x] = 0ull;
     extern __shared__ float ys[];
     float *sq = ys + d;
     __shared__ float leaf[256], res;
@@ -436,6 +444,7 @@ __global__ void k_head_norm(const uint16_t *h4, const uint16_t *w, int d, int hc
 
 __global__ void k_rmsnorm_rows(const uint16_t *x, long ldx, const uint16_t *w, int n, float eps, uint16_t *y,
                                long ldy) {
+    pdl_launch_dependents();
     extern __shared__ float ys[];
     float *sq = ys + n;
     __shared__ float leaf[256], res;
@@ -445,7 +454,33 @@ __global__ void k_rmsnorm_rows(const uint16_t *x, long ldx, const uint16_t *w, i
     rmsnorm_row_smem(ys, sq, n, w, eps, y + (size_t)r * ldy, leaf, &res);
 }
 
+struct NormSegs { NormSeg s[2]; };
+
+__global__ void k_norm_seg(NormSegs sg, float eps, unsigned long long *keys) {
+    pdl_launch_dependents();
+    extern __shared__ float ys[];
+    __shared__ float leaf[256], res;
+    const NormSeg &g = sg.s[blockIdx.y];
+    const int r = blockIdx.x, n = g.n;
+    float *sq = ys + n;
+    if (keys && blockIdx.y == 0 && threadIdx.x == 0) keys[r] = 0ull;
+    uint16_t *xr = (uint16_t *)g.x + (size_t)(g.gather ? g.gather[r] : r) * g.ldx;
+    load_row_f32(xr, n, ys);
+    if (g.sub) {
+        load_row_f32(g.sub + (size_t)r * g.ldsub, n, sq);
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const float v = bf16_round(ys[i] + sq[i]);
+            ys[i] = v;
+            xr[i] = bf16_bits(v);
+        }
+    }
+    __syncthreads();
+    rmsnorm_row_smem(ys, sq, n, g.w, eps, g.y + (size_t)r * g.ldy, leaf, &res);
+}
+
 __global__ void k_residual_add(uint16_t *x, const uint16_t *sub, long n) {
+    pdl_launch_dependents();
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
         x[i] = bf16_bits(bf16_f32(x[i]) + bf16_f32(sub[i]));
 }
@@ -457,23 +492,40 @@ __global__ void k_residual_add(uint16_t *x, const uint16_t *sub, long n) {
 // (cur+1+t) % NSLOT; the committed slot is never written.
 __global__ void k_kda_conv(const uint16_t *kp, long ldkp, const uint16_t *conv_w, uint16_t *conv_slots,
                            const Ctl *ctl, int R, int C, int K, uint16_t *out) {
+    pdl_launch_dependents();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= C) return;
     const int cur = ctl->kda_cur;
     const size_t slot = (size_t)C * (K - 1);
-    uint16_t st[8];
-    for (int j = 0; j < K - 1; j++) st[j] = conv_slots[cur * slot + (size_t)c * (K - 1) + j];
-    const uint16_t *wc = conv_w + (size_t)c * K;
-    for (int t = 0; t < R; t++) {
-        const uint16_t xc = kp[(size_t)t * ldkp + c];
+    // every load first: weights, the committed state and each row's input
+    uint16_t st[8], wc[9], xs[MAXR];
+#pragma unroll
+    for (int j = 0; j < 9; j++)
+        if (j < K) wc[j] = conv_w[(size_t)c * K + j];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        if (j < K - 1) st[j] = conv_slots[cur * slot + (size_t)c * (K - 1) + j];
+#pragma unroll
+    for (int t = 0; t < MAXR; t++)
+        if (t < R) xs[t] = kp[(size_t)t * ldkp + c];
+#pragma unroll
+    for (int t = 0; t < MAXR; t++) {
+        if (t >= R) break;
+        const uint16_t xc = xs[t];
         float acc = 0.f;
-        for (int i = 0; i < K - 1; i++) acc += bf16_f32(wc[i]) * bf16_f32(st[i]);
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            if (i < K - 1) acc += bf16_f32(wc[i]) * bf16_f32(st[i]);
         acc += bf16_f32(wc[K - 1]) * bf16_f32(xc);
         out[(size_t)t * C + c] = bf16_bits(acc * sigmoid_np(acc));
-        for (int j = 0; j + 1 < K - 1; j++) st[j] = st[j + 1];
+#pragma unroll
+        for (int j = 0; j < 7; j++)
+            if (j + 1 < K - 1) st[j] = st[j + 1];
         st[K - 2] = xc;
         const int s = (cur + 1 + t) % NSLOT;
-        for (int j = 0; j < K - 1; j++) conv_slots[s * slot + (size_t)c * (K - 1) + j] = st[j];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (j < K - 1) conv_slots[s * slot + (size_t)c * (K - 1) + j] = st[j];
     }
 }
 
@@ -488,6 +540,7 @@ __global__ void __launch_bounds__(D) k_kda_rec(const uint16_t *qkvc, const uint1
                                                const float *dt_bias, const uint16_t *o_norm, float *rec_slots,
                                                const Ctl *ctl, int R, int H, float lower_bound, float eps,
                                                float qscale, uint16_t *core_out) {
+    pdl_launch_dependents();
     const int h = blockIdx.x, j = threadIdx.x, qkv = H * D;
     __shared__ float qf[D], kf[D], dec[D], sq[D], red[2];
     float S[D];
@@ -556,6 +609,7 @@ __global__ void __launch_bounds__(D) k_kda_rec(const uint16_t *qkvc, const uint1
 // also writes the indexer rows.
 __global__ void k_dsa_append(const uint16_t *kvb, const uint16_t *ikgw, const uint16_t *knw, const uint16_t *knb,
                              const int *base_n, int AH, int qd, int vd, int ID, int IH, int cap, DsaState ds) {
+    pdl_launch_dependents();
     const int t = blockIdx.x, h = blockIdx.y;
     const int pos = *base_n + t;
     if (pos >= cap) return;
@@ -590,6 +644,7 @@ __global__ void k_dsa_append(const uint16_t *kvb, const uint16_t *ikgw, const ui
 // average rounded to BF16.  A completed pool never changes, so it is
 // computed once when its last member is appended.
 __global__ void k_dsa_pool(const uint16_t *ape, const int *base_n, int R, int ID, int kp, int cap, DsaState ds) {
+    pdl_launch_dependents();
     const int base = *base_n;
     const int t = blockIdx.x, pos = base + t;
     if (pos >= cap || (pos % kp) != kp - 1) return;
@@ -615,6 +670,7 @@ __global__ void k_dsa_pool(const uint16_t *ape, const int *base_n, int R, int ID
 // Grid (ceil(maxpools / 8), R); blocks past the visible pools exit.
 __global__ void __launch_bounds__(256) k_dsa_score(const uint16_t *iq, const uint16_t *ikgw, const int *base_n,
                                                    int IH, int ID, int kp, int maxpools, DsaState ds, float *score) {
+    pdl_launch_dependents();
     const int t = blockIdx.y;
     const int qpos = *base_n + t;
     const int nvalid = min((qpos + 1) / kp, maxpools);
@@ -623,8 +679,27 @@ __global__ void __launch_bounds__(256) k_dsa_score(const uint16_t *iq, const uin
     const float idx_scale = (float)(1.0 / sqrt((double)ID)), ih_scale = (float)(1.0 / sqrt((double)IH));
     __shared__ float qs[32 * 129];          // [h][ID] with a one-float pad per head
     __shared__ float wh[32], wsc[8][32];
-    for (int i = threadIdx.x; i < IH * ID; i += blockDim.x)
-        qs[(i / ID) * (ID + 1) + i % ID] = bf16_f32(iq[(size_t)t * IH * ID + i]);
+    {   // stage the row's index queries: 16-byte loads, all issued first
+        const uint16_t *src = iq + (size_t)t * IH * ID;
+        const int nv = IH * ID / 8;                    // <= 512 = 2 per thread
+        uint4 v[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int c = threadIdx.x + u * blockDim.x;
+            v[u] = c < nv ? *(const uint4 *)(src + c * 8) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int c = threadIdx.x + u * blockDim.x;
+            if (c >= nv) break;
+            const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const int i = c * 8 + e;
+                qs[(i / ID) * (ID + 1) + i % ID] = (e & 1) ? bf16hi(w[e >> 1]) : bf16lo(w[e >> 1]);
+            }
+        }
+    }
     for (int h = threadIdx.x; h < IH; h += blockDim.x)
         wh[h] = bf16_f32(ikgw[(size_t)t * (2 * ID + IH) + 2 * ID + h]) * ih_scale;
     __syncthreads();
@@ -648,6 +723,7 @@ __global__ void __launch_bounds__(256) k_dsa_score(const uint16_t *iq, const uin
 // top-(topk/kpool) pools per row, stable with lower-index ties
 // (c/gdsa.h:404-429): a pool is kept iff fewer than K pools beat it.
 __global__ void k_dsa_select(const float *score, const int *base_n, int kp, int ksel, int maxpools, uint8_t *sel) {
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     const int nvalid = min((*base_n + t + 1) / kp, maxpools);
     const float *s = score + (size_t)t * maxpools;
@@ -687,6 +763,7 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk, int rowbytes) {
 __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd,
                                                   int vd, int kp, int maxpools, const uint8_t *sel, DsaState ds,
                                                   float *sbuf, uint16_t *pbuf, int sstride, uint16_t *out) {
+    pdl_launch_dependents();
     extern __shared__ __align__(128) uint8_t dsm[];
     const int h = blockIdx.x;
     const int base = *base_n;
@@ -872,7 +949,7 @@ int layers_prepare(const Dims &D) {
     const int rows[] = {D.hc * D.d, D.d, D.ql, D.kl, D.ID, D.D};
     for (int n : rows)
         if (n > 0 && pw_leaves(n) > 256) return -1;
-    if (D.K < 2 || D.K > 9 || D.kpool > 16 || D.qd > 256 || D.vd > 256 || D.qd % 64 || D.vd % 64 ||
+    if (D.K < 2 || D.K > 9 || D.kpool > 16 || D.qd > 256 || D.vd > 256 || D.qd % 64 || D.vd % 64 || D.ID % 8 ||
         D.IH * D.ID > 32 * 128)
         return -1;
     if (cudaFuncSetAttribute(k_dsa_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsa_attn_smem(D)))
@@ -885,7 +962,8 @@ int layers_prepare(const Dims &D) {
     if (cudaFuncSetAttribute(k_hc_rms, cudaFuncAttributeMaxDynamicSharedMemorySize, D.hc * D.d * 4) ||
         cudaFuncSetAttribute(k_hc_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
         cudaFuncSetAttribute(k_head_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
-        cudaFuncSetAttribute(k_rmsnorm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row))
+        cudaFuncSetAttribute(k_rmsnorm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
+        cudaFuncSetAttribute(k_norm_seg, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row))
         return -1;
     return 0;
 }
@@ -913,14 +991,26 @@ int hc_post_launch(const Dims &D, const uint16_t *x, const uint16_t *h4, int R, 
 }
 
 int head_norm_launch(const Dims &D, const uint16_t *h4, const uint16_t *norm_w, int R, uint16_t *yn,
-                     cudaStream_t st) {
-    k_head_norm<<<R, 512, 2 * D.d * sizeof(float), st>>>(h4, norm_w, D.d, D.hc, D.eps, yn);
+                     unsigned long long *keys, cudaStream_t st) {
+    k_head_norm<<<R, 512, 2 * D.d * sizeof(float), st>>>(h4, norm_w, D.d, D.hc, D.eps, yn, keys);
     return ok_launch();
 }
 
 int rmsnorm_rows_launch(const uint16_t *x, long ldx, const uint16_t *w, int n, int R, float eps, uint16_t *y,
                         long ldy, cudaStream_t st) {
     k_rmsnorm_rows<<<R, 512, 2 * n * sizeof(float), st>>>(x, ldx, w, n, eps, y, ldy);
+    return ok_launch();
+}
+
+int norm_seg_launch(const NormSeg *seg, int nseg, int R, float eps, unsigned long long *keys, cudaStream_t st) {
+    if (nseg < 1 || nseg > 2) return -1;
+    NormSegs sg{};
+    int n = 0;
+    for (int i = 0; i < nseg; i++) {
+        sg.s[i] = seg[i];
+        n = seg[i].n > n ? seg[i].n : n;
+    }
+    k_norm_seg<<<dim3(R, nseg), 512, (size_t)2 * n * sizeof(float), st>>>(sg, eps, keys);
     return ok_launch();
 }
 
@@ -946,6 +1036,7 @@ int kda_launch(const Dims &D, const LayerW &W, KdaState &KS, const Ctl *ctl, int
     GemvDesc g{};
     g.W = W.kda.proj; g.x = S.x; g.ldx = D.d; g.R = R; g.O = kda_nproj(D); g.K = D.d; g.fp8 = 0;
     g.y = S.kp; g.ldy = ldkp; g.part = part; g.ticket = tick;
+    g.pdl = 1;
     if (gemv_launch(g, st)) return -1;
     // conv + SiLU over q|k|v, tokens chained, checkpointed
     k_kda_conv<<<(3 * qkv + 127) / 128, 128, 0, st>>>(S.kp, ldkp, W.kda.conv, KS.conv, ctl, R, 3 * qkv, D.K, S.qkvc);
@@ -956,6 +1047,7 @@ int kda_launch(const Dims &D, const LayerW &W, KdaState &KS, const Ctl *ctl, int
     fg.y = S.fgo; fg.ldy = qkv;
     fg.gexpert = d_probs; fg.gcount = d_cnt; fg.gmax = 2;
     fg.w_estride = (long)qkv * D.Dr * 2; fg.x_pstride = D.Dr; fg.y_pstride = (long)MAXR * qkv;
+    fg.pdl = 1;
     if (gemv_launch(fg, st)) return -1;
     if (D.D != 128) return -1;
     k_kda_rec<128><<<D.H, 128, 0, st>>>(S.qkvc, S.kp, ldkp, 3 * qkv + 2 * D.Dr, S.fgo, (long)MAXR * qkv,
@@ -965,6 +1057,7 @@ int kda_launch(const Dims &D, const LayerW &W, KdaState &KS, const Ctl *ctl, int
     GemvDesc o{};
     o.W = W.kda.o_w; o.x = S.core; o.ldx = qkv; o.R = R; o.O = D.d; o.K = qkv; o.fp8 = 0;
     o.y = S.sub; o.ldy = D.d; o.part = part; o.ticket = tick;
+    o.pdl = 1;
     return gemv_launch(o, st);
 }
 
@@ -974,24 +1067,32 @@ int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, in
     GemvDesc a{};
     a.W = W.qkva_c; a.WS = W.qkva_s; a.nkb = (D.d + 127) / 128; a.x = x; a.ldx = D.d; a.R = R;
     a.O = ql + kl; a.K = D.d; a.fp8 = 1; a.y = S.qkva; a.ldy = ql + kl; a.part = part; a.ticket = tick;
+    a.pdl = 1;
     if (gemv_launch(a, st)) return -1;
-    if (rmsnorm_rows_launch(S.qkva, ql + kl, W.q_a_norm, ql, R, D.eps, S.qres, ql, st)) return -1;
-    if (rmsnorm_rows_launch(S.qkva + ql, ql + kl, W.kv_a_norm, kl, R, D.eps, S.kpass, kl, st)) return -1;
+    {   // q_a and kv_a norms (c/gdsa.h:555-590) in one launch
+        NormSeg sg[2] = {{S.qkva, ql + kl, nullptr, nullptr, 0, W.q_a_norm, ql, S.qres, ql},
+                         {S.qkva + ql, ql + kl, nullptr, nullptr, 0, W.kv_a_norm, kl, S.kpass, kl}};
+        if (norm_seg_launch(sg, 2, R, D.eps, nullptr, st)) return -1;
+    }
     GemvDesc b{};
     b.W = W.q_b_c; b.WS = W.q_b_s; b.nkb = (ql + 127) / 128; b.x = S.qres; b.ldx = ql; b.R = R;
     b.O = (long)D.AH * D.qd; b.K = ql; b.fp8 = 1; b.y = S.q; b.ldy = (long)D.AH * D.qd; b.part = part; b.ticket = tick;
+    b.pdl = 1;
     if (gemv_launch(b, st)) return -1;
     GemvDesc c{};
     c.W = W.kv_b; c.x = S.kpass; c.ldx = kl; c.R = R; c.O = (long)D.AH * (D.qd + D.vd); c.K = kl; c.fp8 = 0;
     c.y = S.kvb; c.ldy = c.O; c.part = part; c.ticket = tick;
+    c.pdl = 1;
     if (gemv_launch(c, st)) return -1;
     GemvDesc e{};
     e.W = W.idx_kgw; e.x = x; e.ldx = D.d; e.R = R; e.O = 2 * D.ID + D.IH; e.K = D.d; e.fp8 = 0;
     e.y = S.ikgw; e.ldy = e.O; e.part = part; e.ticket = tick;
+    e.pdl = 1;
     if (gemv_launch(e, st)) return -1;
     GemvDesc f{};
     f.W = W.idx_wq_b; f.x = S.qres; f.ldx = ql; f.R = R; f.O = (long)D.IH * D.ID; f.K = ql; f.fp8 = 0;
     f.y = S.iq; f.ldy = f.O; f.part = part; f.ticket = tick;
+    f.pdl = 1;
     if (gemv_launch(f, st)) return -1;
     k_dsa_append<<<dim3(R, D.AH), 128, 0, st>>>(S.kvb, S.ikgw, W.idx_knorm_w, W.idx_knorm_b, base_n, D.AH, D.qd,
                                                  D.vd, D.ID, D.IH, DS.cap, DS);
@@ -1007,5 +1108,6 @@ int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, in
     GemvDesc o{};
     o.W = W.o_c; o.WS = W.o_s; o.nkb = ((long)D.AH * D.vd + 127) / 128; o.x = S.attn; o.ldx = (long)D.AH * D.vd;
     o.R = R; o.O = D.d; o.K = (long)D.AH * D.vd; o.fp8 = 1; o.y = out; o.ldy = D.d; o.part = part; o.ticket = tick;
+    o.pdl = 1;
     return gemv_launch(o, st);
 }

@@ -83,8 +83,6 @@ constexpr int PART = 8 * TR;          // floats of one warp partial: [x col][w r
 
 __device__ int g_apus_kernel_err;
 
-APUS_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-APUS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Epilogue of one finished (x row m, weight row `row`) dot product; the 16
 // threads of an x row are consecutive lanes (one half-warp).

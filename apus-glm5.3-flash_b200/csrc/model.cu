@@ -35,6 +35,7 @@
 namespace apus {
 
 __global__ void k_commit(Ctl *c, int R) {
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         c->pos += R;
         c->kda_cur = (c->kda_cur + R) % NSLOT;
@@ -42,21 +43,20 @@ __global__ void k_commit(Ctl *c, int R) {
 }
 
 __global__ void k_mtp_commit(Ctl *c, int R) {
+    pdl_launch_dependents();
     if (threadIdx.x == 0) c->mtp_n += R;
 }
 
 __global__ void k_extract_picks(const unsigned long long *keys, int R, int *dst) {
+    pdl_launch_dependents();
     if ((int)threadIdx.x < R) dst[threadIdx.x] = (int)argmax_key_index(keys[threadIdx.x]);
-}
-
-__global__ void k_reset_keys(unsigned long long *keys, int R) {
-    if ((int)threadIdx.x < R) keys[threadIdx.x] = 0ull;
 }
 
 // Step start.  A step whose rows would pass the capacity freezes the
 // sequence (err) instead: the launches still run (into the slack rows past
 // the capacity) but commit nothing.
 __global__ void k_spec_begin(Ctl *c, int D, int cap, int32_t *ids) {
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         if (c->pos + D > cap) c->err = 1;
         c->batch[0] = c->held;
@@ -69,6 +69,7 @@ __global__ void k_spec_begin(Ctl *c, int D, int cap, int32_t *ids) {
 // input of position q-1, row j the draft batch[j] with yn[j-1] (lag 1,
 // postnorm source, c/gmtp.h:855-866).
 __global__ void k_replay_rows(const uint16_t *hprev_carry, const uint16_t *yn, int D, int d, uint16_t *rows) {
+    pdl_launch_dependents();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D * d; i += gridDim.x * blockDim.x) {
         const int r = i / d, e = i % d;
         rows[i] = r == 0 ? hprev_carry[e] : yn[(size_t)(r - 1) * d + e];
@@ -77,6 +78,7 @@ __global__ void k_replay_rows(const uint16_t *hprev_carry, const uint16_t *yn, i
 
 // Accept walk (c/gmtp.h:807-831) and state fixup (:833-848, :867-884).
 __global__ void k_spec_walk(Ctl *c, int D, int32_t *log, int log_cap) {
+    pdl_launch_dependents();
     if (threadIdx.x != 0) return;
     if (c->err) { c->n_emitted = 0; return; }
     int matched = 0, last = -1;
@@ -104,22 +106,26 @@ __global__ void k_spec_walk(Ctl *c, int D, int32_t *log, int log_cap) {
 }
 
 __global__ void k_copy_row(const uint16_t *src, long row, int d, uint16_t *dst) {
+    pdl_launch_dependents();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x)
         dst[i] = src[row * d + i];
 }
 
 // copy row `matched` (device-selected) of a [D][d] block
 __global__ void k_copy_sel_row(const uint16_t *src, const Ctl *c, int d, uint16_t *dst) {
+    pdl_launch_dependents();
     const int row = c->matched;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x)
         dst[i] = src[(size_t)row * d + i];
 }
 
 __global__ void k_chain_first(const Ctl *c, int32_t *ids) {
+    pdl_launch_dependents();
     if (threadIdx.x == 0) ids[0] = c->drafts[0];
 }
 
 __global__ void k_chain_next(Ctl *c, int i, int32_t *ids) {
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         c->drafts[i] = c->mtp_picks[0];
         ids[0] = c->drafts[i];
@@ -134,6 +140,7 @@ __device__ unsigned long long sm64(unsigned long long z) {
 }
 
 __global__ void k_force(Ctl *c, const int32_t *truth, int D, int V) {
+    pdl_launch_dependents();
     if (threadIdx.x != 0 || !c->force_on) return;
     for (int i = 0; i < D; i++) {
         const long pos = (long)c->pos + i - c->force_base;
@@ -145,10 +152,12 @@ __global__ void k_force(Ctl *c, const int32_t *truth, int D, int V) {
 }
 
 __global__ void k_greedy_prep(Ctl *c, int32_t *ids) {
+    pdl_launch_dependents();
     if (threadIdx.x == 0) ids[0] = c->held;
 }
 
 __global__ void k_greedy_post(Ctl *c, int32_t *log, int log_cap) {
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         if (c->log_n < log_cap) log[c->log_n] = c->held;
         c->log_n++;
@@ -157,6 +166,7 @@ __global__ void k_greedy_post(Ctl *c, int32_t *log, int log_cap) {
 }
 
 __global__ void k_set_held_from_pick(Ctl *c, int row) {
+    pdl_launch_dependents();
     if (threadIdx.x == 0) c->held = c->picks[row];
 }
 
@@ -226,7 +236,7 @@ static Dims dims_of(const ApusGcudaConfig &c) {
 static bool alloc_moe(ApusGcudaModel *m, MoeDev &md, int E, int topk, int inter) {
     const Dims &D = m->D;
     md = m->moe_scr;
-    md.E = E; md.topk = topk; md.inter = inter; md.dim = D.d; md.max_r = MAXR; md.pdl = 0;
+    md.E = E; md.topk = topk; md.inter = inter; md.dim = D.d; md.max_r = MAXR; md.pdl = 1;
     md.route_scale = D.route_scale; md.limit = D.limit;
     const size_t nkd = (D.d + 127) / 128, nki = (inter + 127) / 128;
     md.gate_w = E ? (uint16_t *)dmalloc(m, (size_t)E * D.d * 2) : nullptr;
@@ -692,13 +702,14 @@ extern "C" size_t apus_gcuda_model_pos(const ApusGcudaModel *m) {
 
 // lm_head over `yn` rows with the fused greedy pick into picks[R] (and the
 // BF16 logits when want_logits).
+// The argmax keys S.amax were zeroed by the norm that produced yn.
 static int lm_head(ApusGcudaModel *m, const uint16_t *yn, int R, int *picks, bool want_logits) {
     const Dims &D = m->D;
-    k_reset_keys<<<1, 32, 0, m->st>>>(m->S.amax, R);
     GemvDesc g{};
     g.W = m->head; g.x = yn; g.ldx = D.d; g.R = R; g.O = D.V; g.K = D.d; g.fp8 = 0;
     if (want_logits) { g.y = m->S.logits; g.ldy = D.V; }
     g.amax = m->S.amax; g.part = m->part; g.ticket = m->tick;
+    g.pdl = 1;
     if (gemv_launch(g, m->st)) return -1;
     k_extract_picks<<<1, 32, 0, m->st>>>(m->S.amax, R, picks);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
@@ -735,7 +746,7 @@ static int main_forward(ApusGcudaModel *m, const int32_t *ids_dev, int R, uint16
         std::swap(h, h2);
     }
     if (h != S.h4) cudaMemcpyAsync(S.h4, h, (size_t)R * D.hc * D.d * 2, cudaMemcpyDeviceToDevice, st);
-    if (head_norm_launch(D, S.h4, m->norm, R, yn_out, st)) return -1;
+    if (head_norm_launch(D, S.h4, m->norm, R, yn_out, S.amax, st)) return -1;
     return lm_head(m, yn_out, R, m->ctl->picks, want_logits);
 }
 
@@ -749,21 +760,28 @@ static int mtp_forward(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t
     const LayerW &W = m->L[D.L];
     const int d = D.d;
     m->n_mtp_fwd++;
-    // eh = [enorm(embed[id]) | hnorm(prev_h)]: gather the embed rows into S.mx
-    if (k_embed_launch(m->embed, ids_dev, R, d, 1, S.mx, st)) return -1;
-    if (rmsnorm_rows_launch(S.mx, d, m->enorm, d, R, D.eps, S.eh, 2L * d, st)) return -1;
-    if (rmsnorm_rows_launch(prev_h, d, m->hnorm, d, R, D.eps, S.eh + d, 2L * d, st)) return -1;
+    // eh = [enorm(embed[id]) | hnorm(prev_h)], the embed rows gathered by id
+    {
+        NormSeg sg[2] = {{m->embed, d, ids_dev, nullptr, 0, m->enorm, d, S.eh, 2L * d},
+                         {prev_h, d, nullptr, nullptr, 0, m->hnorm, d, S.eh + d, 2L * d}};
+        if (norm_seg_launch(sg, 2, R, D.eps, nullptr, st)) return -1;
+    }
     GemvDesc g{};
     g.W = m->eh_proj; g.x = S.eh; g.ldx = 2L * d; g.R = R; g.O = d; g.K = 2L * d; g.fp8 = 0;
     g.y = S.mx; g.ldy = d; g.part = m->part; g.ticket = m->tick;
+    g.pdl = 1;
     if (gemv_launch(g, st)) return -1;
     if (rmsnorm_rows_launch(S.mx, d, W.input_norm, d, R, D.eps, S.mxn, d, st)) return -1;
     if (dsa_launch(D, W.dsa, m->mtp_dsa, base_n, R, S, S.mxn, S.sub, m->part, m->tick, st)) return -1;
-    if (residual_add_launch(S.mx, S.sub, (long)R * d, st)) return -1;
-    if (rmsnorm_rows_launch(S.mx, d, W.post_norm, d, R, D.eps, S.mxn, d, st)) return -1;
+    {   // x = bf16(x + attn); post_attention_layernorm
+        NormSeg sg = {S.mx, d, nullptr, S.sub, d, W.post_norm, d, S.mxn, d};
+        if (norm_seg_launch(&sg, 1, R, D.eps, nullptr, st)) return -1;
+    }
     if (moe_forward_launch(W.moe, S.mxn, d, R, S.sub, d, nullptr, st)) return -1;
-    if (residual_add_launch(S.mx, S.sub, (long)R * d, st)) return -1;
-    if (rmsnorm_rows_launch(S.mx, d, m->shared_norm, d, R, D.eps, S.oh, d, st)) return -1;
+    {   // x = bf16(x + moe); shared_head.norm; zero the lm_head argmax keys
+        NormSeg sg = {S.mx, d, nullptr, S.sub, d, m->shared_norm, d, S.oh, d};
+        if (norm_seg_launch(&sg, 1, R, D.eps, S.amax, st)) return -1;
+    }
     return lm_head(m, S.oh, R, m->ctl->mtp_picks, want_logits);
 }
 

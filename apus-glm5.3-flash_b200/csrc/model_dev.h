@@ -142,9 +142,22 @@ int hc_pre_launch(const Dims &D, const LayerW &W, int site, const uint16_t *h4, 
 int hc_post_launch(const Dims &D, const uint16_t *x, const uint16_t *h4, int R, const Scratch &S,
                    uint16_t *h4out, cudaStream_t st);
 int head_norm_launch(const Dims &D, const uint16_t *h4, const uint16_t *norm_w, int R, uint16_t *yn,
-                     cudaStream_t st);
+                     unsigned long long *keys, cudaStream_t st);     // keys: zeroed for the lm_head argmax
 int rmsnorm_rows_launch(const uint16_t *x, long ldx, const uint16_t *w, int n, int R, float eps,
                         uint16_t *y, long ldy, cudaStream_t st);
+// One weighted RMSNorm per segment and row, up to 2 segments in one launch.
+// Row r of a segment reads x + (gather ? gather[r] : r) * ldx; with sub, the
+// row first becomes bf16(x + sub) and is written back to x (the residual add
+// of c/gmtp.h:281-284).  keys (optional): zeroed for rows 0..R-1 (the argmax
+// keys of the lm_head that follows).
+struct NormSeg {
+    const uint16_t *x; long ldx;
+    const int32_t *gather;
+    const uint16_t *sub; long ldsub;
+    const uint16_t *w; int n;
+    uint16_t *y; long ldy;
+};
+int norm_seg_launch(const NormSeg *seg, int nseg, int R, float eps, unsigned long long *keys, cudaStream_t st);
 int kda_launch(const Dims &D, const LayerW &W, KdaState &KS, const Ctl *ctl, int R, Scratch &S,
                float *part, int *tick, cudaStream_t st);            // S.x -> S.sub
 int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, int R, Scratch &S,
