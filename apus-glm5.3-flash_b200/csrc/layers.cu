@@ -11,6 +11,7 @@
 #include "model_dev.h"
 #include "pipe.cuh"
 #include "linear.cuh"
+#include <cooperative_groups.h>
 
 namespace apus {
 
@@ -740,32 +741,37 @@ __global__ void k_dsa_select(const float *score, const int *base_n, int kp, int 
     }
 }
 
-// Attention over the selected positions (c/gdsa.h:451-517): one CTA (8
-// warps) per head handles every row of the call, so each K/V row is read
-// once.  sc = bf16(bf16(q.k) * qd^-0.5); p = bf16(softmax(sc)); o = bf16(sum p v).
+// Attention over the selected positions (c/gdsa.h:451-517).
+//   sc = bf16(bf16(q.k) * qd^-0.5); p = bf16(softmax(sc)); o = bf16(sum p v)
 // Visibility of position j for row t: j <= base+t and (its pool is
 // selected, or j is in the row's incomplete tail pool).  p_j = 0 for every
 // other position, so row t's output depends only on its own row (the rows
 // of one call do not interact).
 //
-// Both contractions run on the tensor cores (mma.sync m16n8k16, bf16 in,
-// f32 accumulate): scores = K_tile[128 pos][qd] . Q^T (8 query rows as the
-// n dimension), output^T = V_tile^T . P^T.  K and V stream through shared
-// memory in tiles of ATJ positions (cp.async, double buffered; 16-byte
-// chunks XOR-swizzled by row so ldmatrix is conflict-free).  The softmax is
-// one warp per row over the scores in global scratch; p is stored as BF16
-// (exact, it is BF16-rounded by definition) in pbuf.
-#define ATJ 128
+// One cluster of ASPLIT CTAs per head; CTA z owns the ATJ-position tiles
+// z, z + ASPLIT, ... (a fixed function of the position, so a row gets the
+// same partial sums whatever rows share the call).  Both contractions run on the tensor cores (mma.sync
+// m16n8k16, bf16 in, f32 accumulate): scores = K_tile[pos][qd] . Q^T (the 8
+// query rows are the n dimension), out^T = V_tile^T . P^T.  K and V stream
+// through shared memory (cp.async, double buffered, 16-byte chunks
+// XOR-swizzled by row so ldmatrix is conflict-free).  The softmax's row max,
+// row sum and the output partials cross the cluster through distributed
+// shared memory and are combined in CTA order, so every CTA sees the same
+// bits.  p is stored as BF16 (exact: it is BF16-rounded by definition).
+#define ATJ 64
+#define ASPLIT 4
 __device__ __forceinline__ uint32_t swz(int row, int chunk, int rowbytes) {
     return (uint32_t)(row * rowbytes + ((chunk ^ (row & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd,
-                                                  int vd, int kp, int maxpools, const uint8_t *sel, DsaState ds,
-                                                  float *sbuf, uint16_t *pbuf, int sstride, uint16_t *out) {
+__global__ void __cluster_dims__(1, ASPLIT, 1) __launch_bounds__(256)
+k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd, int vd, int kp, int maxpools,
+           const uint8_t *sel, DsaState ds, float *sbuf, uint16_t *pbuf, int sstride, uint16_t *out) {
     pdl_launch_dependents();
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(128) uint8_t dsm[];
-    const int h = blockIdx.x;
+    const int h = blockIdx.x, z = (int)cluster.block_rank();
     const int base = *base_n;
     const int nmax = base + R;            // positions that exist after this call's append
     const int nt = (nmax + ATJ - 1) / ATJ;
@@ -775,11 +781,12 @@ __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *
     const int TB = ATJ * wmax * 2;                     // bytes of one K/V tile buffer
     const int PROW = (ATJ + 8) * 2, QROW = (qd + 8) * 2;
     uint8_t *kv0 = dsm, *pt0 = dsm + 2 * TB, *qs = pt0 + 2 * MAXR * PROW;
+    float *opart = (float *)(qs + MAXR * QROW);        // [MAXR][vd] this CTA's output partial
     const float scale = (float)(1.0 / sqrt((double)qd));
     float *sc = sbuf + (size_t)h * MAXR * sstride;     // [MAXR][sstride] scores, then e
     uint16_t *pb = pbuf + (size_t)h * MAXR * sstride;  // [MAXR][sstride] p (BF16)
     __shared__ int tail_s[MAXR];
-    // Q rows (zero beyond R) and the P tiles' unused rows
+    __shared__ float rmax_s[MAXR], rsum_s[MAXR];
     for (int i = threadIdx.x; i < MAXR * (qd / 8); i += blockDim.x) {
         const int t = i / (qd / 8), c = i % (qd / 8);
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -788,9 +795,11 @@ __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *
     }
     for (int i = threadIdx.x; i < 2 * MAXR * (PROW / 16); i += blockDim.x)
         *(uint4 *)(pt0 + i * 16) = make_uint4(0, 0, 0, 0);
-    if (threadIdx.x < R) {
+    if (threadIdx.x < MAXR) {
         const int vis = base + threadIdx.x + 1;
         tail_s[threadIdx.x] = vis - vis % kp;
+        rmax_s[threadIdx.x] = -3.4028234663852886e+38f;
+        rsum_s[threadIdx.x] = 0.f;
     }
     auto visible = [&](int t, int j) -> bool {
         if (j > base + t) return false;
@@ -798,9 +807,6 @@ __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *
         const int p = j / kp;
         return p < maxpools && sel[(size_t)t * maxpools + p];
     };
-    // stage tile ti of a [cap][w] cache into buffer b (rows past nmax clamp to
-    // the last one; their p is 0 and their scores are never stored); with
-    // probs, also the rows' p for t < R
     auto stage = [&](const uint16_t *cache, int w, int ti, int b, bool probs) {
         const int j0 = ti * ATJ, cpr = w / 8;
         uint8_t *dst = kv0 + b * TB;
@@ -817,80 +823,98 @@ __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *
         cp_async_commit();
     };
     __syncthreads();
-    // ---- scores: warp w owns positions [16w, 16w+16) of each tile
+    // ---- scores over this CTA's tiles: warp w owns positions [16w, 16w+16)
+    // of a tile when w < ATJ/16
     uint32_t qb[16][2];
     const int nks = qd / 16;
 #pragma unroll
     for (int ks = 0; ks < 16; ks++)
         if (ks < nks) ldsm_x2(qb[ks][0], qb[ks][1], qs + (lane & 7) * QROW + (ks * 16 + ((lane >> 3) & 1) * 8) * 2);
-    stage(ds.k, qd, 0, 0, false);
-    for (int ti = 0; ti < nt; ti++) {
-        if (ti + 1 < nt) stage(ds.k, qd, ti + 1, (ti + 1) & 1, false);
+    if (z < nt) stage(ds.k, qd, z, 0, false);
+    for (int ti = z, it = 0; ti < nt; ti += ASPLIT, it++) {
+        if (ti + ASPLIT < nt) stage(ds.k, qd, ti + ASPLIT, (it + 1) & 1, false);
         else cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        const uint8_t *kt = kv0 + (ti & 1) * TB;
-        const int r0 = warp * 16;
-        float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+        if (warp < ATJ / 16) {
+            const uint8_t *kt = kv0 + (it & 1) * TB;
+            const int r0 = warp * 16;
+            float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
 #pragma unroll
-        for (int ks = 0; ks < 16; ks++) {
-            if (ks >= nks) break;
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(a0, a1, a2, a3, kt + swz(r0 + (lane & 15), ks * 2 + (lane >> 4), qd * 2));
-            mma_bf16_16816(c0, c1, c2, c3, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
-        }
-        // c0/c1: position r0+g, rows 2q4 / 2q4+1; c2/c3: position r0+g+8
-        const int pa = ti * ATJ + r0 + g, pbp = pa + 8, t0 = 2 * q4, t1 = t0 + 1;
-        if (pa < nmax) {
-            if (t0 < R) sc[(size_t)t0 * sstride + pa] = bf16_round(bf16_round(c0) * scale);
-            if (t1 < R) sc[(size_t)t1 * sstride + pa] = bf16_round(bf16_round(c1) * scale);
-        }
-        if (pbp < nmax) {
-            if (t0 < R) sc[(size_t)t0 * sstride + pbp] = bf16_round(bf16_round(c2) * scale);
-            if (t1 < R) sc[(size_t)t1 * sstride + pbp] = bf16_round(bf16_round(c3) * scale);
+            for (int ks = 0; ks < 16; ks++) {
+                if (ks >= nks) break;
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(a0, a1, a2, a3, kt + swz(r0 + (lane & 15), ks * 2 + (lane >> 4), qd * 2));
+                mma_bf16_16816(c0, c1, c2, c3, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+            }
+            // c0/c1: position r0+g, rows 2q4 / 2q4+1; c2/c3: position r0+g+8
+            const int pa = ti * ATJ + r0 + g, pbp = pa + 8, t0 = 2 * q4, t1 = t0 + 1;
+            if (pa < nmax) {
+                if (t0 < R) sc[(size_t)t0 * sstride + pa] = bf16_round(bf16_round(c0) * scale);
+                if (t1 < R) sc[(size_t)t1 * sstride + pa] = bf16_round(bf16_round(c1) * scale);
+            }
+            if (pbp < nmax) {
+                if (t0 < R) sc[(size_t)t0 * sstride + pbp] = bf16_round(bf16_round(c2) * scale);
+                if (t1 < R) sc[(size_t)t1 * sstride + pbp] = bf16_round(bf16_round(c3) * scale);
+            }
         }
         __syncthreads();
     }
-    // ---- softmax: warp t owns row t; lane 0's sums are broadcast so every
-    // lane uses the same bits
-    if (warp < R) {
-        const int t = warp, qpos = base + t;
-        float *srow = sc + (size_t)t * sstride;
-        uint16_t *prow = pb + (size_t)t * sstride;
+    // ---- softmax (warp t owns row t over this CTA's positions), cluster-wide
+    const int t = warp;
+    const bool row = t < R;
+    const int qpos = base + t;
+    float *srow = sc + (size_t)(row ? t : 0) * sstride;
+    if (row) {
         float m = -3.4028234663852886e+38f;
-        for (int j = lane; j <= qpos; j += 32)
-            if (visible(t, j)) m = fmaxf(m, srow[j]);
+        for (int ti = z; ti < nt; ti += ASPLIT)
+            for (int j = ti * ATJ + lane; j < ti * ATJ + ATJ && j <= qpos; j += 32)
+                if (visible(t, j)) m = fmaxf(m, srow[j]);
 #pragma unroll
         for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        if (lane == 0) rmax_s[t] = m;
+    }
+    cluster.sync();
+    float mx = -3.4028234663852886e+38f;
+    if (row)
+        for (int zz = 0; zz < ASPLIT; zz++) mx = fmaxf(mx, cluster.map_shared_rank(rmax_s, zz)[t]);
+    if (row) {
         float su = 0.f;
-        for (int j = lane; j <= qpos; j += 32)
-            if (visible(t, j)) {
-                const float e = expf(srow[j] - m);
-                srow[j] = e;
-                su += e;
-            }
+        for (int ti = z; ti < nt; ti += ASPLIT)
+            for (int j = ti * ATJ + lane; j < ti * ATJ + ATJ && j <= qpos; j += 32)
+                if (visible(t, j)) {
+                    const float e = expf(srow[j] - mx);
+                    srow[j] = e;
+                    su += e;
+                }
 #pragma unroll
         for (int off = 16; off; off >>= 1) su += __shfl_xor_sync(0xffffffffu, su, off);
-        su = __shfl_sync(0xffffffffu, su, 0);
-        const int jend = nt * ATJ;
-        for (int j = lane; j < jend; j += 32)
-            prow[j] = (j <= qpos && visible(t, j)) ? bf16_bits(srow[j] / su) : (uint16_t)0;
+        if (lane == 0) rsum_s[t] = su;
+    }
+    cluster.sync();
+    if (row) {
+        float sum = cluster.map_shared_rank(rsum_s, 0)[t];
+        for (int zz = 1; zz < ASPLIT; zz++) sum += cluster.map_shared_rank(rsum_s, zz)[t];
+        uint16_t *prow = pb + (size_t)t * sstride;
+        for (int ti = z; ti < nt; ti += ASPLIT)
+            for (int j = ti * ATJ + lane; j < ti * ATJ + ATJ; j += 32)
+                prow[j] = (j <= qpos && visible(t, j)) ? bf16_bits(srow[j] / sum) : (uint16_t)0;
     }
     __syncthreads();
-    // ---- output: warp w owns dv tiles mt = w, w+8, ... (16 dv each)
+    // ---- output partial over this CTA's tiles: warp w owns dv tiles w, w+8
     const int nmt = vd / 16;
     float acc[2][4];
 #pragma unroll
     for (int u = 0; u < 2; u++)
 #pragma unroll
         for (int e = 0; e < 4; e++) acc[u][e] = 0.f;
-    stage(ds.v, vd, 0, 0, true);
-    for (int ti = 0; ti < nt; ti++) {
-        if (ti + 1 < nt) stage(ds.v, vd, ti + 1, (ti + 1) & 1, true);
+    if (z < nt) stage(ds.v, vd, z, 0, true);
+    for (int ti = z, it = 0; ti < nt; ti += ASPLIT, it++) {
+        if (ti + ASPLIT < nt) stage(ds.v, vd, ti + ASPLIT, (it + 1) & 1, true);
         else cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        const uint8_t *vt = kv0 + (ti & 1) * TB, *pt = pt0 + (ti & 1) * MAXR * PROW;
+        const uint8_t *vt = kv0 + (it & 1) * TB, *pt = pt0 + (it & 1) * MAXR * PROW;
 #pragma unroll
         for (int ks = 0; ks < ATJ / 16; ks++) {
             uint32_t b0, b1;
@@ -909,21 +933,25 @@ __global__ void __launch_bounds__(256) k_dsa_attn(const uint16_t *q, const int *
         }
         __syncthreads();
     }
-    // acc: (dv = 16mt+g, rows 2q4 / 2q4+1) and (dv + 8, ...)
+    // acc: (dv = 16mt+g, rows 2q4 / 2q4+1) and (dv + 8, ...) -> this CTA's partial
 #pragma unroll
     for (int u = 0; u < 2; u++) {
         const int mt = warp + 8 * u;
         if (mt >= nmt) break;
         const int dv = mt * 16 + g, t0 = 2 * q4, t1 = t0 + 1;
-        if (t0 < R) {
-            out[(size_t)t0 * AH * vd + (size_t)h * vd + dv] = bf16_bits(acc[u][0]);
-            out[(size_t)t0 * AH * vd + (size_t)h * vd + dv + 8] = bf16_bits(acc[u][2]);
-        }
-        if (t1 < R) {
-            out[(size_t)t1 * AH * vd + (size_t)h * vd + dv] = bf16_bits(acc[u][1]);
-            out[(size_t)t1 * AH * vd + (size_t)h * vd + dv + 8] = bf16_bits(acc[u][3]);
-        }
+        opart[t0 * vd + dv] = acc[u][0];
+        opart[t0 * vd + dv + 8] = acc[u][2];
+        opart[t1 * vd + dv] = acc[u][1];
+        opart[t1 * vd + dv + 8] = acc[u][3];
     }
+    cluster.sync();
+    if (z == 0)        // sum the partials in CTA order
+        for (int i = threadIdx.x; i < R * vd; i += blockDim.x) {
+            float o = opart[i];
+            for (int zz = 1; zz < ASPLIT; zz++) o += cluster.map_shared_rank(opart, zz)[i];
+            out[(size_t)(i / vd) * AH * vd + (size_t)h * vd + i % vd] = bf16_bits(o);
+        }
+    cluster.sync();    // keep every CTA's shared memory alive until rank 0 has read it
 }
 
 }  // namespace apus
@@ -934,7 +962,8 @@ static int ok_launch() { return cudaGetLastError() == cudaSuccess ? 0 : -1; }
 
 static size_t dsa_attn_smem(const Dims &D) {
     const int w = D.qd > D.vd ? D.qd : D.vd;
-    return (size_t)2 * ATJ * w * 2 + (size_t)2 * MAXR * (ATJ + 8) * 2 + (size_t)MAXR * (D.qd + 8) * 2;
+    return (size_t)2 * ATJ * w * 2 + (size_t)2 * MAXR * (ATJ + 8) * 2 + (size_t)MAXR * (D.qd + 8) * 2 +
+           (size_t)MAXR * D.vd * 4;
 }
 
 // Leaves of the numpy pairwise recursion over n (what block_pw's 256-entry
@@ -1101,7 +1130,7 @@ int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, in
                                                                  S.maxpools, DS, S.iscore);
     k_dsa_select<<<R, 256, 0, st>>>(S.iscore, base_n, D.kpool, D.topk / D.kpool, S.maxpools, S.isel);
     if (ok_launch()) return -1;
-    k_dsa_attn<<<D.AH, 256, dsa_attn_smem(D), st>>>(S.q, base_n, R, D.AH, D.qd, D.vd, D.kpool, S.maxpools,
+    k_dsa_attn<<<dim3(D.AH, ASPLIT), 256, dsa_attn_smem(D), st>>>(S.q, base_n, R, D.AH, D.qd, D.vd, D.kpool, S.maxpools,
                                                      S.isel, DS, (float *)S.attn_scores, S.attn_p,
                                                      S.attn_sstride, S.attn);
     if (ok_launch()) return -1;
