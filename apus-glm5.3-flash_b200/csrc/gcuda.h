@@ -31,6 +31,10 @@ struct GemvDesc {
     const int *gcount;
     int gmax;
     long w_estride, s_estride, x_pstride, y_pstride;
+    // set by gemv_launch from (O, K, fp8, grouped) alone: the K range of one
+    // work item and the weight tiles per work item
+    long kx;
+    int tpi;
     // x holds [R][2K] gate|up pairs; the staged activation is the SwiGLU
     // h = bf16(bf16(silu(min(g, lim))) * clip(u, +-lim)) (c/gmoe.h:216-224).
     int x_swiglu;

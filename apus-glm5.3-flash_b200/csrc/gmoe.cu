@@ -199,6 +199,7 @@ int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint
         GemvDesc r{};
         r.W = m.gate_w; r.x = x; r.ldx = ldx; r.R = R; r.O = m.E; r.K = m.dim; r.fp8 = 0;
         r.yf = m.logits; r.ldyf = m.E;
+        r.part = m.part; r.ticket = m.tick;
         r.pdl = m.pdl;
         if (gemv_launch(r, st)) return -1;
     }

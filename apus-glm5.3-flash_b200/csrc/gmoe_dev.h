@@ -27,6 +27,8 @@ struct MoeDev {
     int32_t *prob_expert;        // [max_r*topk+1] expert of each problem slot
     int32_t *prob_count;         // [1]
     unsigned long long *stat_problems;   // optional: += expert problems (incl. shared) per call
+    float *part;                 // split-K scratch of the router GEMV (gemv_scratch_need(E, dim))
+    int *tick;
     uint16_t *gu;                // [max_r*topk+1][max_r][2*inter]
     uint16_t *yd;                // [max_r*topk+1][max_r][dim]
 };

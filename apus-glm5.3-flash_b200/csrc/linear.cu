@@ -62,13 +62,16 @@ __global__ void k_fp8_dequant(const uint8_t *__restrict__ w, const float *__rest
 // each takes a fixed slice of the 64-byte k-steps of every chunk.  The
 // weight rows are the 16-row A operand of mma.m16n8k16 (lane (g,t) holds rows
 // g and g+8), the activation rows the 8 B columns, so one MMA covers 256
-// weights.  FP8 codes are dequantized in registers to the reference's exact
-// BF16 weight (one fp32 multiply by the block scale, RNE).  Four accumulator
-// sets shorten the MMA dependency chain; at the end of the tile the 8 warp
-// partials are summed in warp order.  With several k-ranges the partial goes
-// to scratch and the last CTA of the tile (atomic ticket) sums the ranges in
-// range order and runs the epilogue.  Row strides are padded so the 8 lanes
-// of every quarter-warp hit distinct 16-byte shared-memory bank groups.
+// weights.  BF16 weights go to a bf16 MMA with four accumulator sets; FP8
+// codes are converted exactly to f16 and meet the power-of-two-scaled f16
+// activations in an f16 MMA, the 128x128 block scale multiplying each step's
+// partial.  At the end of the tile the 8 warp partials are summed in warp
+// order.  With several k-ranges the partial goes to scratch and the last CTA
+// of the tile (atomic ticket) sums the ranges in range order and runs the
+// epilogue.  Short-output matrices use narrower k-ranges and short FP8 rows
+// carry two tiles per work item (both fixed by the matrix shape, so a row's
+// arithmetic never depends on the number of rows).  Row strides are padded
+// so the 8 lanes of every quarter-warp hit distinct 16-byte bank groups.
 namespace gemvcfg {
 constexpr int NSTAGE = 2;
 constexpr int TR = 16;                // weight rows per tile
@@ -110,7 +113,8 @@ struct GemvItems {
     int nks, ks;
     bool grouped;
     APUS_DEV void init(const GemvDesc &d, int count) {
-        ntile = (d.O + gemvcfg::TR - 1) / gemvcfg::TR;
+        // items cover tpi consecutive 16-row tiles: ntile counts items
+        ntile = ((d.O + gemvcfg::TR - 1) / gemvcfg::TR + d.tpi - 1) / d.tpi;
         grouped = d.gexpert != nullptr;
         if (grouped) {
             nks = 1;
@@ -120,7 +124,7 @@ struct GemvItems {
             end = total * (blockIdx.x + 1) / gridDim.x;
             step = 1;
         } else {
-            nks = (int)((d.K + gemvcfg::KX - 1) / gemvcfg::KX);
+            nks = (int)((d.K + d.kx - 1) / d.kx);
             ks = (int)(blockIdx.x % nks);
             first = blockIdx.x / nks;
             step = gridDim.x / nks;
@@ -140,7 +144,7 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
     uint8_t *ring = smem;
     uint16_t *xs = (uint16_t *)(smem + NSTAGE * STAGE_BYTES);
     float *part = (float *)(smem + NSTAGE * STAGE_BYTES + (XS ? XMAX : 0));
-    uint64_t *full = (uint64_t *)(part + 8 * PART);
+    uint64_t *full = (uint64_t *)(part + 8 * 2 * PART);     // [warp][tile][PART]
     uint64_t *empty = full + NSTAGE;
     __shared__ unsigned long long best_sh[8];
     __shared__ int abort_sh, ticket_sh;
@@ -168,9 +172,10 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
         if (d.weights_after_wait || d.gexpert) pdl_wait();
         GemvItems it;
         it.init(d, d.gexpert ? min(*d.gcount, d.gmax) : 1);
-        const long k0 = it.ks * KX, klen = min(KX, d.K - k0);
+        const long k0 = it.ks * d.kx, klen = min(d.kx, d.K - k0);
         const long kb0 = FP8 ? k0 : 2 * k0, kbytes = FP8 ? klen : 2 * klen;
         const int nch = (int)((kbytes + CH - 1) / CH);
+        const int tpi = d.tpi;
         long c = 0;
         bool ok = true;
         for (long i = it.first; i < it.end && ok; i += it.step) {
@@ -179,7 +184,7 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
             it.at(i, p, t);
             const uint8_t *W = (const uint8_t *)d.W;
             if (it.grouped) W += (size_t)d.gexpert[p] * d.w_estride;
-            const long row0 = t * TR;
+            const long row0 = t * TR * tpi;
             for (int ch = 0; ch < nch; ch++, c++) {
                 const int s = (int)(c % NSTAGE);
                 const long rnd = c / NSTAGE;
@@ -190,14 +195,17 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
                                               &g_apus_kernel_err, 1))
                         ok = false;
                     else
-                        mbar_arrive_expect_tx(&full[s], TR * len);
+                        mbar_arrive_expect_tx(&full[s], TR * len * tpi);
                 }
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 if (lane < TR) {
-                    const long row = min(row0 + lane, d.O - 1);
-                    bulk_g2s(ring + s * STAGE_BYTES + lane * RS, W + row * rowbytes + kb0 + off, len,
-                             &full[s]);
+                    // tile j of the item lands at byte j*len of the lane's row slot
+                    for (int j = 0; j < tpi; j++) {
+                        const long row = min(row0 + j * TR + lane, d.O - 1);
+                        bulk_g2s(ring + s * STAGE_BYTES + lane * RS + j * len, W + row * rowbytes + kb0 + off,
+                                 len, &full[s]);
+                    }
                 }
             }
         }
@@ -208,9 +216,10 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
     pdl_wait();
     GemvItems it;
     it.init(d, d.gexpert ? min(*d.gcount, d.gmax) : 1);
-    const long k0 = it.ks * KX, klen = min(KX, d.K - k0);          // elements
+    const long k0 = it.ks * d.kx, klen = min(d.kx, d.K - k0);      // elements
     const long kb0 = FP8 ? k0 : 2 * k0, kbytes = FP8 ? klen : 2 * klen;
     const int nch = (int)((kbytes + CH - 1) / CH);
+    const int tpi = d.tpi;                                          // tiles per item (1 or 2)
     const long xstride = klen + 8;                                  // elements
     const int g = lane >> 2, t4 = lane & 3;
     const bool xrow_ok = g < d.R;            // lane supplies B column g
@@ -302,7 +311,7 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
             }
             xsrc_staged = xsrc;
         }
-        const long row0 = t * TR;
+        const long row0 = t * TR * tpi;
         const float *srA = nullptr;
         if (FP8)     // the tile's 16 rows lie in one 128-row scale block
             srA = WS + (size_t)(row0 >> 7) * d.nkb;
@@ -312,14 +321,16 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
         for (int ch = 0; ch < nch; ch++, c++) {
             const int s = (int)(c % NSTAGE);
             const long off = (long)ch * CH;
-            const int nst = (int)(min((long)CH, kbytes - off) / 64);
+            const int nstt = (int)(min((long)CH, kbytes - off) / 64);   // steps of one tile
+            const int nst = nstt * tpi;
             const int s0 = nst * warp / 8, s1 = nst * (warp + 1) / 8;
             constexpr int MAXS = CH / 64 / 8 + 1;
             float scA[MAXS];
             if (FP8) {   // scales first: their latency hides under the barrier wait
 #pragma unroll
                 for (int q = 0; q < MAXS; q++) {
-                    const long kbk = (kb0 + off) / 128 + ((s0 + q) >> 1);
+                    const int sq = s0 + q;                  // step within its tile (tpi <= 2)
+                    const long kbk = (kb0 + off) / 128 + ((sq >= nstt ? sq - nstt : sq) >> 1);
                     scA[q] = (s0 + q < s1) ? __ldg(srA + kbk) : 0.f;
                 }
             }
@@ -334,7 +345,7 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
                 if (st >= e1) break;
                 const uint4 va = lds128(wA + st * 64), vb = lds128(wB + st * 64);
                 const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
-                const long ls = off / 64 + st;                  // step within the k-range
+                const long ls = off / 64 + (st >= nstt ? st - nstt : st);   // step within the k-range
                 if (FP8) {
                     // x is staged as scaled f16 (XS is always on for FP8)
                     uint32_t xw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -356,8 +367,13 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
                                       xw[2 * j], xw[2 * j + 1]);
                     }
                     const float sc = scA[q];
+                    if (st < nstt) {                            // tile 0 of the item
 #pragma unroll
-                    for (int e = 0; e < 4; e++) acc[0][e] = acc[0][e] + (u[0][e] + u[1][e]) * sc;
+                        for (int e = 0; e < 4; e++) acc[0][e] = acc[0][e] + (u[0][e] + u[1][e]) * sc;
+                    } else {                                    // tile 1
+#pragma unroll
+                        for (int e = 0; e < 4; e++) acc[1][e] = acc[1][e] + (u[0][e] + u[1][e]) * sc;
+                    }
                 } else {
                     uint32_t xw[4] = {0, 0, 0, 0};
                     if (xrow_ok) {
@@ -379,23 +395,27 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
             if (lane == 0) mbar_arrive(&empty[s]);
         }
         // D layout: c0 = (w row g, x col 2t), c1 = (g, 2t+1), c2 = (g+8, 2t), c3 = (g+8, 2t+1)
-        float *pw = part + warp * PART;
+        float *pw = part + warp * 2 * PART;
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const int xc = 2 * t4 + (e & 1), wr = g + 8 * (e >> 1);
             pw[xc * TR + wr] = FP8 ? acc[0][e] * xinv_sh[xc] : (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+            if (FP8 && tpi == 2) pw[PART + xc * TR + wr] = acc[1][e] * xinv_sh[xc];
         }
         named_bar_sync(1, 256);
         const int tid = threadIdx.x;
-        // thread tid < 128: x col m = tid/16, weight row o = tid%16
+        // thread tid < 128*tpi: tile jt = tid/128, x col m = (tid%128)/16,
+        // weight row o = tid%16 of that tile
+        const int jt = tid >> 7, te = tid & 127;
         float a = 0.f;
-        if (tid < 128) {
-            a = part[tid];
+        if (tid < 128 * tpi) {
+            a = part[jt * PART + te];
 #pragma unroll
-            for (int w = 1; w < 8; w++) a = a + part[w * PART + tid];
+            for (int w = 1; w < 8; w++) a = a + part[w * 2 * PART + jt * PART + te];
         }
         if (it.nks == 1) {
-            if (tid < 128) gemv_store(d, yout, tid >> 4, row0 + (tid & 15), a, best_sh, (tid & 15) == 0);
+            if (tid < 128 * tpi)
+                gemv_store(d, yout, te >> 4, row0 + jt * TR + (te & 15), a, best_sh, (te & 15) == 0);
         } else {
             // publish this range's partial; the last range of the tile reduces
             float *slot = d.part + ((size_t)t * it.nks + it.ks) * PART;
@@ -497,8 +517,26 @@ __global__ void k_argmax_extract(const unsigned long long *keys, int32_t *ids, i
 
 using namespace apus;
 
+// The k-range width and the 16-row tiles per work item of a GEMV, functions
+// of the matrix shape alone (so a row's summation order never depends on how
+// many rows share the launch): matrices with too few row tiles to fill the
+// GPU split K more finely; short FP8 rows put two tiles in one work item.
+static void gemv_plan(long O, long K, bool fp8, bool grouped, long *kx, int *tpi) {
+    using namespace gemvcfg;
+    const long ntile = (O + TR - 1) / TR;
+    long x = KX;
+    if (!grouped)
+        while (x > 512 && ntile * ((K + x - 1) / x) < 148) x /= 2;
+    *kx = x;
+    const long kbytes = (fp8 ? 1 : 2) * (K < x ? K : x);
+    *tpi = (fp8 && K <= x && 2 * kbytes <= CH) ? 2 : 1;
+}
+
 void gemv_scratch_need(long O, long K, size_t *part_floats, size_t *tickets) {
-    const long nks = (K + gemvcfg::KX - 1) / gemvcfg::KX;
+    long kx;
+    int tpi;
+    gemv_plan(O, K, false, false, &kx, &tpi);
+    const long nks = (K + kx - 1) / kx;
     const long ntile = (O + gemvcfg::TR - 1) / gemvcfg::TR;
     *part_floats = nks > 1 ? (size_t)(ntile * nks * gemvcfg::PART) : 0;
     *tickets = nks > 1 ? (size_t)ntile : 0;
@@ -516,7 +554,7 @@ static int g_num_sms = 0;
 
 static size_t gemv_smem(bool xs) {
     using namespace gemvcfg;
-    return NSTAGE * STAGE_BYTES + (xs ? XMAX : 0) + 8 * PART * 4 + 2 * NSTAGE * 8;
+    return NSTAGE * STAGE_BYTES + (xs ? XMAX : 0) + 8 * 2 * PART * 4 + 2 * NSTAGE * 8;
 }
 
 template <bool FP8, bool XS>
@@ -533,13 +571,13 @@ static int launch_tma(const GemvDesc &d, cudaStream_t st) {
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     }
-    const long ntile = (d.O + gemvcfg::TR - 1) / gemvcfg::TR;
+    const long ntile = ((d.O + gemvcfg::TR - 1) / gemvcfg::TR + d.tpi - 1) / d.tpi;   // work items
     long grid;
     if (d.gexpert) {
         grid = 2L * g_num_sms;
         if (grid > (long)d.gmax * ntile) grid = (long)d.gmax * ntile;
     } else {
-        const long nks = (d.K + gemvcfg::KX - 1) / gemvcfg::KX;
+        const long nks = (d.K + d.kx - 1) / d.kx;
         long per_ks = (2L * g_num_sms) / nks;                    // CTAs per k-range
         if (per_ks < 1) per_ks = 1;
         if (per_ks > ntile) per_ks = ntile;
@@ -558,12 +596,14 @@ static int launch_tma(const GemvDesc &d, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, k_gemv_tma<FP8, XS>, d) == cudaSuccess ? 0 : -1;
 }
 
-int gemv_launch(const GemvDesc &d, cudaStream_t st) {
-    if (d.R < 1 || d.R > 8 || d.O <= 0 || d.K <= 0) return -1;
+int gemv_launch(const GemvDesc &dd, cudaStream_t st) {
+    if (dd.R < 1 || dd.R > 8 || dd.O <= 0 || dd.K <= 0) return -1;
+    GemvDesc d = dd;
+    gemv_plan(d.O, d.K, d.fp8 != 0, d.gexpert != nullptr, &d.kx, &d.tpi);
     if (gemv_fast_ok(d)) {
-        const long klen = d.K < gemvcfg::KX ? d.K : gemvcfg::KX;
+        const long klen = d.K < d.kx ? d.K : d.kx;
         const bool xs = (long)d.R * (klen * 2 + 16) <= gemvcfg::XMAX;
-        if (d.K > gemvcfg::KX && (!d.part || !d.ticket)) return -1;
+        if (d.K > d.kx && (!d.part || !d.ticket)) return -1;
         if (d.gexpert && (d.K > gemvcfg::KX || !d.gcount || d.gmax < 1)) return -1;
         if (d.fp8 && !xs) {
             // FP8 needs the activations staged (as scaled f16): run the rows in

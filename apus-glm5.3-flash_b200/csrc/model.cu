@@ -388,6 +388,8 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
         MoeDev &ms = m->moe_scr;
         m->moe_problems = (unsigned long long *)A(sizeof(unsigned long long));
         ms.stat_problems = m->moe_problems;
+        ms.part = m->part;       // the router GEMV shares the model's split-K scratch
+        ms.tick = m->tick;
         const int maxi = D.inter > D.dense_inter ? D.inter : D.dense_inter;
         const size_t P = (size_t)R * (D.ktop > 0 ? D.ktop : 1) + 1;
         ms.logits = (float *)A((size_t)R * (D.E > 0 ? D.E : 1) * 4);

@@ -54,6 +54,13 @@ ApusGcudaMoe *apus_gcuda_moe_new(int E, int topk, size_t dim, size_t inter, floa
     d.d_codes = (uint8_t *)A((size_t)(E + 1) * dim * inter);
     d.d_scales = (float *)A((size_t)(E + 1) * m->nkb_d * m->nkb_i * 4);
     d.logits = (float *)A((size_t)max_rows * E * 4);
+    {   // router split-K scratch (tickets start at zero; every launch leaves them zeroed)
+        size_t pf, nt;
+        gemv_scratch_need(E, (long)dim, &pf, &nt);
+        d.part = (float *)A((pf ? pf : 1) * 4);
+        d.tick = (int *)A((nt ? nt : 1) * 4);
+        if (d.tick) cudaMemset(d.tick, 0, (nt ? nt : 1) * 4);
+    }
     d.row_expert = (int32_t *)A((size_t)max_rows * topk * 4);
     d.row_weight = (float *)A((size_t)max_rows * topk * 4);
     d.row_sel = (int32_t *)A((size_t)max_rows * topk * 4);
