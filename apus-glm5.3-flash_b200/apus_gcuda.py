@@ -132,6 +132,9 @@ def make_config(**kw):
 _cs = C.c_char_p
 apus_gcuda_model_new = _fn("apus_gcuda_model_new", _vp, _vp, _i, _sz, _i)
 apus_gcuda_model_free = _fn("apus_gcuda_model_free", None, _vp)
+apus_gcuda_model_new_ep = _fn("apus_gcuda_model_new_ep", _vp, _vp, _i, _sz, _i, _i, _i)
+apus_gcuda_model_ep_handle = _fn("apus_gcuda_model_ep_handle", _i, _vp, _vp)
+apus_gcuda_model_ep_connect = _fn("apus_gcuda_model_ep_connect", _i, _vp, _vp)
 apus_gcuda_model_set = _fn("apus_gcuda_model_set", _i, _vp, _cs, _vp, _sz)
 apus_gcuda_model_get = _fn("apus_gcuda_model_get", _i, _vp, _cs, _vp, _sz)
 apus_gcuda_model_init_random = _fn("apus_gcuda_model_init_random", _i, _vp, _u64)
@@ -154,19 +157,66 @@ apus_gcuda_model_debug_stop = _fn("apus_gcuda_model_debug_stop", _i, _vp, _i, _i
 apus_gcuda_model_debug_read = _fn("apus_gcuda_model_debug_read", _i, _vp, _cs, _vp, _sz)
 
 
+EP_HANDLE_BYTES = 64   # sizeof(cudaIpcMemHandle_t)
+
+
+def ep_handles_blob(handles, world):
+    """Concatenate the ranks' exchange handles in rank order (host side of
+    apus_gcuda_model_ep_connect)."""
+    if len(handles) != world:
+        raise GcudaError(f"ep_connect: {len(handles)} handles for {world} ranks")
+    for r, h in enumerate(handles):
+        if len(h) != EP_HANDLE_BYTES:
+            raise GcudaError(f"ep_connect: rank {r} handle has {len(h)} bytes")
+    return b"".join(bytes(h) for h in handles)
+
+
+def ep_all_gather(group=None):
+    """An all_gather(bytes) -> [bytes] over a torch.distributed group (any
+    backend): every rank's payload, in rank order."""
+    import torch.distributed as dist
+
+    def gather(payload):
+        out = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, bytes(payload), group=group)
+        return out
+    return gather
+
+
 class GModel:
     """One resident model + sequence on the current CUDA device (the
     reference's ApusGmodel/ApusGmodelState/ApusGmtp/ApusGspec bundle,
     c/gmodel.h:161-320, c/gmtp.h:123-259).  Arrays are numpy (host)."""
 
-    def __init__(self, cfg, has_mtp=True, kv_cap=1024, depth=4):
+    def __init__(self, cfg, has_mtp=True, kv_cap=1024, depth=4, rank=0, world=1):
         import numpy as np
         self.np = np
         enable()
-        self.cfg, self.depth = cfg, depth
-        self.h = apus_gcuda_model_new(C.byref(cfg), int(has_mtp), kv_cap, depth)
+        self.cfg, self.depth, self.rank, self.world = cfg, depth, rank, world
+        if world > 1:
+            self.h = apus_gcuda_model_new_ep(C.byref(cfg), int(has_mtp), kv_cap, depth, rank, world)
+        else:
+            self.h = apus_gcuda_model_new(C.byref(cfg), int(has_mtp), kv_cap, depth)
         if not self.h:
             raise GcudaError(f"model_new: {apus_gcuda_last_error().decode(errors='replace')}")
+
+    def ep_handle(self):
+        """This rank's 64-byte exchange-region handle."""
+        buf = C.create_string_buffer(EP_HANDLE_BYTES)
+        check(apus_gcuda_model_ep_handle(self.h, buf), "ep_handle")
+        return buf.raw
+
+    def ep_connect(self, handles):
+        """Open every rank's exchange region; `handles` lists the ranks'
+        64-byte handles in rank order."""
+        blob = ep_handles_blob(handles, self.world)
+        buf = C.create_string_buffer(blob, len(blob))
+        check(apus_gcuda_model_ep_connect(self.h, buf), "ep_connect")
+
+    def ep_bootstrap(self, all_gather):
+        """Exchange handles with `all_gather(bytes) -> [bytes per rank]` (for
+        example ep_all_gather over a torch.distributed group), then connect."""
+        self.ep_connect(all_gather(self.ep_handle()))
 
     def close(self):
         if self.h:
@@ -180,8 +230,14 @@ class GModel:
             pass
 
     def set(self, name, arr):
+        """Store one checkpoint tensor; returns False for another
+        expert-parallel rank's expert (nothing stored)."""
         arr = self.np.ascontiguousarray(arr)
-        check(apus_gcuda_model_set(self.h, name.encode(), ptr(arr), arr.nbytes), f"set {name}")
+        rc = apus_gcuda_model_set(self.h, name.encode(), ptr(arr), arr.nbytes)
+        if rc == 1:
+            return False
+        check(rc, f"set {name}")
+        return True
 
     def get(self, name, shape, dtype):
         a = self.np.empty(shape, dtype)
@@ -273,6 +329,25 @@ class GModel:
         check(apus_gcuda_model_counters(self.h, o, 5), "counters")
         return dict(zip(("moe_problems", "main_forwards", "mtp_forwards", "graph_kernels", "ctl_bytes"),
                         list(o)))
+
+
+def ep_owns(kw, rank, world):
+    """Predicate over checkpoint names: does expert-parallel `rank` of `world`
+    store this tensor?  Routed expert e lives on rank e // (E / world); every
+    other tensor is stored on every rank (the lm_head as a row slice).  This
+    is the split apus_gcuda_model_set applies."""
+    E = kw["n_routed_experts"]
+    if world > 1 and E % world:
+        raise GcudaError(f"{E} experts do not split over {world} ranks")
+    per = E // world if world > 1 else E
+
+    def owns(name):
+        i = name.find(".mlp.experts.")
+        if world == 1 or i < 0:
+            return True
+        e = int(name[i + len(".mlp.experts."):].split(".", 1)[0])
+        return e // per == rank
+    return owns
 
 
 def tensor_specs(kw, has_mtp=True):

@@ -189,7 +189,8 @@ const char *apus_gcuda_last_error(void) { return g_err; }
 
 int apus_gcuda_kernel_error(void) {
     cudaDeviceSynchronize();
-    return kernel_error_read_and_clear();
+    const int a = kernel_error_read_and_clear(), b = ep_error_read_and_clear();
+    return a ? a : b;
 }
 
 int apus_gcuda_register_region(const void *ptr, size_t len) {

@@ -35,6 +35,11 @@ struct GemvDesc {
     // work item and the weight tiles per work item
     long kx;
     int tpi;
+    // argmax keys carry row + row_base (a vocabulary slice's global ids)
+    long row_base;
+    // plan the k-ranges as for a matrix of plan_o rows (0: O), so a slice of a
+    // matrix sums each row in the same order as the whole matrix
+    long plan_o;
     // x holds [R][2K] gate|up pairs; the staged activation is the SwiGLU
     // h = bf16(bf16(silu(min(g, lim))) * clip(u, +-lim)) (c/gmoe.h:216-224).
     int x_swiglu;
@@ -49,6 +54,7 @@ int gemv_launch(const GemvDesc &d, cudaStream_t st);
 int fp8_dequant_launch(const uint8_t *w, const float *ws, uint16_t *out, size_t O, size_t K,
                        cudaStream_t st);
 int kernel_error_read_and_clear(void);
+int ep_error_read_and_clear(void);      // the expert-parallel barrier's timeout word
 int argmax_reset_launch(unsigned long long *keys, int n, cudaStream_t st);
 int argmax_extract_launch(const unsigned long long *keys, int32_t *ids, int n, cudaStream_t st);
 
@@ -60,4 +66,4 @@ int gcuda_check(cudaError_t e, const char *what);
 enum { FILL_BF16_NORMAL = 0, FILL_E4M3_NORMAL = 1, FILL_F32_LOGUNIFORM = 2, FILL_F32_NORMAL = 3,
        FILL_F32_CONST = 4, FILL_BF16_CONST = 5 };
 int fill_launch(int kind, void *dst, size_t n, uint64_t seed, uint64_t stream_id, float a, float b,
-                cudaStream_t st);
+                cudaStream_t st, size_t first = 0);

@@ -24,6 +24,8 @@
 
 namespace apus {
 
+__device__ int g_apus_ep_err;   // 5: an expert-parallel barrier gave up waiting
+
 // c/gmhc.h:165-185 for n <= 8 (the router weight sum, n = topk)
 APUS_DEV float pw_sum_small(const float *a, int n) {
     if (n < 8) {
@@ -112,9 +114,10 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float 
     if (threadIdx.x == 0) run = 0;
     __syncthreads();
     const int nw = blockDim.x >> 5;
+    const int lo = m.e0, hi = m.e0 + m.eloc;  // this rank's routed experts
     for (int e0 = 0; e0 < E; e0 += blockDim.x) {
         const int e = e0 + threadIdx.x;
-        const int f = e < E ? flag[e] : 0;
+        const int f = (e >= lo && e < hi) ? flag[e] : 0;
         const unsigned bal = __ballot_sync(0xffffffffu, f);
         const int ln = threadIdx.x & 31, w = threadIdx.x >> 5;
         if (ln == 0) wsum[w] = __popc(bal);
@@ -122,8 +125,8 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float 
         int p = run + __popc(bal & ((1u << ln) - 1u));
         for (int k = 0; k < w; k++) p += wsum[k];
         if (e < E) {
-            slot_of[e] = p;
-            if (f) m.prob_expert[p] = e;
+            slot_of[e] = (e >= lo && e < hi) ? p : -1;   // -1: another rank's expert
+            if (f) m.prob_expert[p] = e - lo;             // local weight slot
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -136,7 +139,7 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float 
     if (threadIdx.x == 0) {
         const int p = run;
         slot_of[E] = p;
-        m.prob_expert[p] = E;              // shared expert, always last
+        m.prob_expert[p] = m.eloc;         // shared expert (local slot eloc), always last
         *m.prob_count = p + 1;
         if (m.stat_problems) atomicAdd(m.stat_problems, (unsigned long long)(p + 1));
     }
@@ -187,9 +190,125 @@ __global__ void k_moe_combine(MoeDev m, int R, uint16_t *out, long ldo) {
     *(uint4 *)(out + (size_t)r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// Expert parallelism: every rank writes the weighted outputs of its own
+// experts, bf16(bf16(expert) * w), into its exchange region's contrib half
+// (slot j of row r in ascending expert order); after the barrier every rank
+// combines all slots from their owners' regions.
+__global__ void k_moe_contrib(MoeDev m, int R) {
+    pdl_launch_dependents();
+    const int d = m.dim, K = m.topk, nc = d / 8;
+    const size_t pstride = (size_t)m.max_r * d;
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * K * nc) return;
+    const int c = (int)(i % nc) * 8, j = (int)((i / nc) % K), r = (int)(i / nc / K);
+    const int p = m.row_prob[r * K + j];
+    if (p < 0) return;                                   // another rank's expert
+    const int half = (*m.ep.epoch + 1) & 1;              // the half the next barrier publishes
+    const uint4 ev = *(const uint4 *)(m.yd + p * pstride + (size_t)r * d + c);
+    const float w = m.row_weight[r * K + j];
+    const uint32_t ew[4] = {ev.x, ev.y, ev.z, ev.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+        o[e] = (uint32_t)bf16_bits(bf16_round(bf16lo(ew[e]) * w)) |
+               ((uint32_t)bf16_bits(bf16_round(bf16hi(ew[e]) * w)) << 16);
+    uint16_t *dst = (uint16_t *)m.ep.peer[m.ep.rank] +
+                    (((size_t)half * MOE_MAX_R + r) * MOE_MAX_TOPK + j) * d + c;
+    *(uint4 *)dst = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void k_moe_combine_ep(MoeDev m, int R, uint16_t *out, long ldo) {
+    pdl_launch_dependents();
+    const int d = m.dim, K = m.topk, nc = d / 8;
+    const size_t pstride = (size_t)m.max_r * d;
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * nc) return;
+    const int r = (int)(i / nc), c = (int)(i % nc) * 8;
+    const int half = *m.ep.epoch & 1;                    // the half the last barrier published
+    uint4 ev[MOE_MAX_TOPK];
+#pragma unroll
+    for (int j = 0; j < MOE_MAX_TOPK; j++)
+        if (j < K) {
+            const int owner = m.row_expert[r * K + j] / m.eloc;
+            const uint16_t *src = (const uint16_t *)m.ep.peer[owner] +
+                                  (((size_t)half * MOE_MAX_R + r) * MOE_MAX_TOPK + j) * d + c;
+            ev[j] = __ldcv((const uint4 *)src);          // a peer's region: fetched afresh, never cached
+        }
+    const uint4 sh = *(const uint4 *)(m.yd + m.row_prob_shared[r] * pstride + (size_t)r * d + c);
+    const uint32_t sw[4] = {sh.x, sh.y, sh.z, sh.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        float y = 0.f;
+#pragma unroll
+        for (int j = 0; j < MOE_MAX_TOPK; j++) {
+            if (j >= K) break;
+            const uint32_t wd = (e >> 1) == 0 ? ev[j].x : (e >> 1) == 1 ? ev[j].y : (e >> 1) == 2 ? ev[j].z : ev[j].w;
+            y = bf16_round(y + ((e & 1) ? bf16hi(wd) : bf16lo(wd)));
+        }
+        const uint16_t shb = (uint16_t)((e & 1) ? sw[e >> 1] >> 16 : sw[e >> 1] & 0xffffu);
+        const uint16_t v = bf16_bits(y + bf16_f32(shb));
+        if (e & 1) o[e >> 1] |= (uint32_t)v << 16;
+        else o[e >> 1] = v;
+    }
+    *(uint4 *)(out + (size_t)r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// One warp.  Lane p < world signals peer p and then waits for peer p's
+// signal; the wait is bounded (about a second of clock cycles) and records
+// an error instead of hanging.
+__global__ void k_ep_barrier(EpCtx ep, const unsigned long long *keys, int nkeys) {
+    __shared__ int e_sh;
+    const int lane = threadIdx.x;
+    if (lane == 0) {
+        e_sh = *ep.epoch + 1;
+        *ep.epoch = e_sh;
+    }
+    __syncwarp();
+    const int e = e_sh;
+    if (lane < nkeys) {    // publish this rank's keys into the half of epoch e
+        unsigned long long *kd = (unsigned long long *)(ep.peer[ep.rank] + ep.off_keys) +
+                                 (size_t)(e & 1) * MOE_MAX_R;
+        kd[lane] = keys[lane];
+        __threadfence_system();
+    }
+    __syncwarp();
+    if (lane < ep.world) {
+        int *pf = (int *)(ep.peer[lane] + ep.off_flags) + ep.rank;
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(pf), "r"(e) : "memory");
+        const int *mine = (const int *)(ep.peer[ep.rank] + ep.off_flags) + lane;
+        const long long t0 = clock64();
+        int v = 0;
+        while (true) {
+            asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+            if (v >= e) break;
+            if (clock64() - t0 > (1ll << 31)) {
+                atomicExch(&g_apus_ep_err, 5);
+                break;
+            }
+        }
+    }
+}
+
+__global__ void k_ep_picks(EpCtx ep, int R, int *picks) {
+    const int r = threadIdx.x;
+    if (r >= R) return;
+    const int half = *ep.epoch & 1;
+    unsigned long long best = 0ull;
+    for (int p = 0; p < ep.world; p++) {
+        const unsigned long long k =
+            __ldcv((const unsigned long long *)(ep.peer[p] + ep.off_keys) + (size_t)half * MOE_MAX_R + r);
+        best = k > best ? k : best;
+    }
+    picks[r] = (int)argmax_key_index(best);
+}
+
 }  // namespace apus
 
 using namespace apus;
+
+static bool ep_connected(const EpCtx &ep);
 
 int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
                        const int32_t *forced, cudaStream_t st) {
@@ -232,9 +351,49 @@ int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint
     dn.swiglu_limit = m.limit;
     dn.pdl = m.pdl;
     if (gemv_launch(dn, st)) return -1;
-    // 5. ordered combine
+    // 5. ordered combine (across ranks when the experts are split)
     if (m.dim % 8 || ((uintptr_t)out & 15) || (ldo % 8)) return -1;
     const long n = (long)R * (m.dim / 8);
-    k_moe_combine<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(m, R, out, ldo);
+    if (m.ep.world > 1 && m.E > 0) {
+        if (!ep_connected(m.ep) || m.eloc * m.ep.world != m.E) return -1;
+        const long nc = (long)R * m.topk * (m.dim / 8);
+        k_moe_contrib<<<(unsigned)((nc + 127) / 128), 128, 0, st>>>(m, R);
+        if (ep_barrier_launch(m.ep, nullptr, 0, st)) return -1;
+        k_moe_combine_ep<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(m, R, out, ldo);
+    } else {
+        k_moe_combine<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(m, R, out, ldo);
+    }
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Every rank's region must be mapped before any exchange is launched.
+static bool ep_connected(const EpCtx &ep) {
+    if (ep.world < 2 || ep.world > EP_MAX_RANKS || ep.rank < 0 || ep.rank >= ep.world || !ep.epoch) return false;
+    for (int p = 0; p < ep.world; p++)
+        if (!ep.peer[p]) return false;
+    return true;
+}
+
+int ep_barrier_launch(const EpCtx &ep, const unsigned long long *keys, int nkeys, cudaStream_t st) {
+    if (!ep_connected(ep) || nkeys > MOE_MAX_R || (nkeys > 0 && !keys)) return -1;
+    k_ep_barrier<<<1, 32, 0, st>>>(ep, keys, nkeys);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int ep_picks_launch(const EpCtx &ep, int R, int *picks, cudaStream_t st) {
+    if (!ep_connected(ep) || R < 1 || R > MOE_MAX_R) return -1;
+    k_ep_picks<<<1, 32, 0, st>>>(ep, R, picks);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int ep_error_read_and_clear(void) {
+    int v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, g_apus_ep_err, sizeof v);
+    cudaMemcpyToSymbol(g_apus_ep_err, &z, sizeof z);
+    return v;
+}
+
+size_t ep_region_bytes(int dim) {
+    const size_t contrib = (size_t)2 * MOE_MAX_R * MOE_MAX_TOPK * dim * 2;
+    return contrib + 2 * MOE_MAX_R * 8 + EP_MAX_RANKS * 4 + 256;
 }

@@ -7,9 +7,27 @@
 #define MOE_MAX_E 512
 #define MOE_MAX_TOPK 16
 
+#define EP_MAX_RANKS 8
+
+// Expert-parallel exchange context (one process per GPU).  Every rank owns one
+// exchange region, mapped into every peer through CUDA IPC:
+//   contrib [2][MOE_MAX_R][MOE_MAX_TOPK][dim] BF16  weighted expert outputs
+//   keys    [2][MOE_MAX_R] u64                      lm_head argmax keys
+//   flags   [EP_MAX_RANKS] int                      barrier epochs, written by peers
+// The [2] halves alternate with the barrier epoch's parity, so a rank never
+// overwrites a half a peer may still be reading.  world == 1: no exchange.
+struct EpCtx {
+    int rank, world;
+    uint8_t *peer[EP_MAX_RANKS];  // every rank's region (peer[rank] is this rank's)
+    int *epoch;                   // this rank's barrier counter (device)
+    long off_keys, off_flags;     // byte offsets inside a region
+};
+
 // All pointers are device memory.  Weights: see gmoe.cu for the packed layout.
 struct MoeDev {
     int E, topk, dim, inter, max_r, pdl;
+    int e0, eloc;                 // this rank's routed experts [e0, e0+eloc); local slot eloc = shared
+    EpCtx ep;
     float route_scale, limit;
     const uint16_t *gate_w;      // [E][dim] BF16 router
     const float *gate_bias;      // [E] f32 (selection-only bias)
@@ -38,3 +56,11 @@ struct MoeDev {
 // teacher-forcing hook, c/gmoe.h:145-152).
 int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
                        const int32_t *forced, cudaStream_t st);
+
+// Cross-rank barrier of the expert-parallel group: bumps the epoch, publishes
+// keys[0..nkeys) (optional) into this rank's keys half, signals every peer and
+// waits (bounded) until every peer has signalled the same epoch.
+int ep_barrier_launch(const EpCtx &ep, const unsigned long long *keys, int nkeys, cudaStream_t st);
+// picks[r] = index of the largest key over every rank's published keys half.
+int ep_picks_launch(const EpCtx &ep, int R, int *picks, cudaStream_t st);
+size_t ep_region_bytes(int dim);

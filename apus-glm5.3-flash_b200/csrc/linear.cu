@@ -97,7 +97,7 @@ APUS_DEV void gemv_store(const GemvDesc &d, uint16_t *y, int m, long row, float 
         if (d.yf) d.yf[(size_t)m * d.ldyf + row] = a;
     }
     if (d.amax) {
-        unsigned long long k = ok ? argmax_key(bf16_round(a), (uint32_t)row) : 0ull;
+        unsigned long long k = ok ? argmax_key(bf16_round(a), (uint32_t)(row + d.row_base)) : 0ull;
 #pragma unroll
         for (int off2 = 8; off2; off2 >>= 1) {
             unsigned long long o2 = __shfl_xor_sync(0xffffffffu, k, off2, 16);
@@ -501,7 +501,7 @@ __global__ void k_gemv_generic(GemvDesc d) {
         for (int r = 1; r < 8; r++) if (lane == r) v = acc[r];
         if (yout) yout[(size_t)lane * d.ldy + o] = bf16_bits(v);
         if (d.yf && !d.gexpert) d.yf[(size_t)lane * d.ldyf + o] = v;
-        if (d.amax && !d.gexpert) atomicMax(d.amax + lane, argmax_key(bf16_round(v), (uint32_t)o));
+        if (d.amax && !d.gexpert) atomicMax(d.amax + lane, argmax_key(bf16_round(v), (uint32_t)(o + d.row_base)));
     }
 }
 
@@ -599,7 +599,7 @@ static int launch_tma(const GemvDesc &d, cudaStream_t st) {
 int gemv_launch(const GemvDesc &dd, cudaStream_t st) {
     if (dd.R < 1 || dd.R > 8 || dd.O <= 0 || dd.K <= 0) return -1;
     GemvDesc d = dd;
-    gemv_plan(d.O, d.K, d.fp8 != 0, d.gexpert != nullptr, &d.kx, &d.tpi);
+    gemv_plan(d.plan_o > 0 ? d.plan_o : d.O, d.K, d.fp8 != 0, d.gexpert != nullptr, &d.kx, &d.tpi);
     if (gemv_fast_ok(d)) {
         const long klen = d.K < d.kx ? d.K : d.kx;
         const bool xs = (long)d.R * (klen * 2 + 16) <= gemvcfg::XMAX;

@@ -207,6 +207,12 @@ struct ApusGcudaModel {
     cudaGraphExec_t gexec = nullptr;
     int use_graph = 0;
     size_t graph_kernels = 0;
+    // expert / vocabulary parallelism (one process per GPU)
+    int ep_rank = 0, ep_world = 1;
+    EpCtx ep{};
+    uint8_t *ep_region = nullptr;             // this rank's exchange region
+    void *ep_opened[EP_MAX_RANKS] = {};       // peers' regions opened through IPC
+    long v0 = 0, vn = 0;                      // this rank's lm_head rows [v0, v0+vn)
 };
 
 static void *dmalloc(ApusGcudaModel *m, size_t n, bool zero = true) {
@@ -233,18 +239,25 @@ static Dims dims_of(const ApusGcudaConfig &c) {
 }
 
 // MoE weights + per-layer views into the shared scratch
+// The router is replicated; the routed experts are split evenly over the
+// expert-parallel ranks (this rank keeps [e0, e0+eloc) in local slots
+// 0..eloc-1) and the shared expert sits in local slot eloc on every rank.
 static bool alloc_moe(ApusGcudaModel *m, MoeDev &md, int E, int topk, int inter) {
     const Dims &D = m->D;
     md = m->moe_scr;
     md.E = E; md.topk = topk; md.inter = inter; md.dim = D.d; md.max_r = MAXR; md.pdl = 1;
     md.route_scale = D.route_scale; md.limit = D.limit;
+    md.eloc = E / m->ep_world;
+    md.e0 = md.eloc * m->ep_rank;
+    md.ep = m->ep;
+    const int L = md.eloc + 1;                // local expert slots
     const size_t nkd = (D.d + 127) / 128, nki = (inter + 127) / 128;
     md.gate_w = E ? (uint16_t *)dmalloc(m, (size_t)E * D.d * 2) : nullptr;
     md.gate_bias = E ? (float *)dmalloc(m, (size_t)E * 4) : nullptr;
-    md.gu_codes = (uint8_t *)dmalloc(m, (size_t)(E + 1) * 2 * inter * D.d, false);
-    md.gu_scales = (float *)dmalloc(m, (size_t)(E + 1) * (2 * inter / 128) * nkd * 4, false);
-    md.d_codes = (uint8_t *)dmalloc(m, (size_t)(E + 1) * D.d * inter, false);
-    md.d_scales = (float *)dmalloc(m, (size_t)(E + 1) * nkd * nki * 4, false);
+    md.gu_codes = (uint8_t *)dmalloc(m, (size_t)L * 2 * inter * D.d, false);
+    md.gu_scales = (float *)dmalloc(m, (size_t)L * (2 * inter / 128) * nkd * 4, false);
+    md.d_codes = (uint8_t *)dmalloc(m, (size_t)L * D.d * inter, false);
+    md.d_scales = (float *)dmalloc(m, (size_t)L * nkd * nki * 4, false);
     return md.gu_codes && md.gu_scales && md.d_codes && md.d_scales && (!E || (md.gate_w && md.gate_bias));
 }
 
@@ -290,11 +303,14 @@ static void model_release(ApusGcudaModel *m) {
     if (m->gexec) cudaGraphExecDestroy(m->gexec);
     if (m->graph) cudaGraphDestroy(m->graph);
     if (m->st) cudaStreamDestroy(m->st);
+    for (int p = 0; p < EP_MAX_RANKS; p++)
+        if (m->ep_opened[p]) cudaIpcCloseMemHandle(m->ep_opened[p]);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
 }
 
-extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int has_mtp, size_t kv_cap, int depth) {
+static ApusGcudaModel *model_create(const ApusGcudaConfig *cfg, int has_mtp, size_t kv_cap, int depth, int rank,
+                                    int world) {
     char err[128];
     if (apus_gcuda_enable(err, sizeof err)) return nullptr;
     const Dims D = dims_of(*cfg);
@@ -306,6 +322,11 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
         D.kpool > 16 || D.ql % 128 || D.kl % 128 || D.inter % 128 || D.dense_inter % 128 || D.E > MOE_MAX_E ||
         D.ktop > MOE_MAX_TOPK || kv_cap < 16) {
         gcuda_set_error("gmodel: unsupported configuration");
+        return nullptr;
+    }
+    if (world < 1 || world > EP_MAX_RANKS || rank < 0 || rank >= world ||
+        (world > 1 && (D.E % world || D.ktop > MOE_MAX_TOPK || D.V < world))) {
+        gcuda_set_error("gmodel: expert-parallel split needs experts divisible by the %d ranks", world);
         return nullptr;
     }
     if (layers_prepare(D)) {
@@ -320,6 +341,13 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
     m->depth = depth;
     m->cap = (int)kv_cap;
     m->nL = D.L + m->has_mtp;
+    m->ep_rank = rank;
+    m->ep_world = world;
+    {   // vocabulary rows of this rank's lm_head slice
+        const long per = ((long)D.V + world - 1) / world;
+        m->v0 = per * rank < D.V ? per * rank : D.V;
+        m->vn = (m->v0 + per < D.V ? m->v0 + per : D.V) - m->v0;
+    }
     bool ok = cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) == cudaSuccess;
     // shared scratch (all layers run one after another on one stream)
     Scratch &S = m->S;
@@ -376,6 +404,17 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
         m->tick = (int *)A(nt * 4);
     }
     m->ctl = (Ctl *)A(sizeof(Ctl));
+    m->ep.rank = rank;
+    m->ep.world = world;
+    if (world > 1) {   // this rank's exchange region (peers open it through IPC)
+        const size_t contrib = (size_t)2 * MOE_MAX_R * MOE_MAX_TOPK * d * 2;
+        const size_t rb = ep_region_bytes(d);
+        m->ep_region = (uint8_t *)A(rb > (2u << 20) ? rb : (2u << 20));   // its own IPC-mappable allocation
+        m->ep.peer[rank] = m->ep_region;
+        m->ep.off_keys = (long)contrib;
+        m->ep.off_flags = (long)(contrib + 2 * MOE_MAX_R * 8);
+        m->ep.epoch = (int *)A(sizeof(int));
+    }
     m->log_cap = m->cap + 2 * MAXR;
     m->log = (int32_t *)A((size_t)m->log_cap * 4);
     m->yn_prompt = (uint16_t *)A((size_t)(m->cap + MAXR) * d * 2);
@@ -406,7 +445,7 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
     // weights
     m->embed = (uint16_t *)A((size_t)D.V * d * 2);
     m->norm = (uint16_t *)A((size_t)d * 2);
-    m->head = (uint16_t *)A((size_t)D.V * d * 2);
+    m->head = (uint16_t *)A((size_t)m->vn * d * 2);
     m->L.resize(m->nL);
     m->kda.resize(D.L);
     m->dsa.resize(D.L);
@@ -457,6 +496,43 @@ extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int 
     return m;
 }
 
+extern "C" ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int has_mtp, size_t kv_cap, int depth) {
+    return model_create(cfg, has_mtp, kv_cap, depth, 0, 1);
+}
+
+extern "C" ApusGcudaModel *apus_gcuda_model_new_ep(const ApusGcudaConfig *cfg, int has_mtp, size_t kv_cap, int depth,
+                                                   int rank, int world) {
+    return model_create(cfg, has_mtp, kv_cap, depth, rank, world);
+}
+
+extern "C" int apus_gcuda_model_ep_handle(ApusGcudaModel *m, void *handle_out) {
+    if (m->ep_world < 2) { gcuda_set_error("gmodel: not an expert-parallel model"); return -1; }
+    cudaIpcMemHandle_t h;
+    if (gcuda_check(cudaIpcGetMemHandle(&h, m->ep_region), "ep handle")) return -1;
+    memcpy(handle_out, &h, sizeof h);
+    return 0;
+}
+
+// Opens every peer's exchange region and points every MoE layer and the
+// lm_head exchange at them.  A captured step graph is dropped (its launches
+// hold the old pointers).
+extern "C" int apus_gcuda_model_ep_connect(ApusGcudaModel *m, const void *handles) {
+    if (m->ep_world < 2) { gcuda_set_error("gmodel: not an expert-parallel model"); return -1; }
+    const cudaIpcMemHandle_t *h = (const cudaIpcMemHandle_t *)handles;
+    for (int p = 0; p < m->ep_world; p++) {
+        if (p == m->ep_rank || m->ep_opened[p]) continue;
+        void *ptr = nullptr;
+        if (gcuda_check(cudaIpcOpenMemHandle(&ptr, h[p], cudaIpcMemLazyEnablePeerAccess), "ep connect")) return -1;
+        m->ep_opened[p] = ptr;
+        m->ep.peer[p] = (uint8_t *)ptr;
+    }
+    m->moe_scr.ep = m->ep;
+    for (LayerW &W : m->L) W.moe.ep = m->ep;
+    if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = nullptr; }
+    if (m->graph) { cudaGraphDestroy(m->graph); m->graph = nullptr; }
+    return 0;
+}
+
 extern "C" void apus_gcuda_model_free(ApusGcudaModel *m) { model_release(m); }
 
 // ---- tensor name -> packed device location --------------------------------
@@ -470,8 +546,10 @@ static int resolve_moe(const ApusGcudaModel *m, const MoeDev &md, const std::str
     char part[64] = {0}, kind[64] = {0};
     if (E && sscanf(n.c_str(), "mlp.experts.%d.%63[a-z]_proj.%63s", &e, part, kind) == 3) {
         if (e < 0 || e >= (int)E) return -1;
+        if (e < md.e0 || e >= md.e0 + md.eloc) return 1;   // another rank's expert
+        e -= md.e0;                                       // local slot
     } else if (E && sscanf(n.c_str(), "mlp.shared_experts.%63[a-z]_proj.%63s", part, kind) == 2) {
-        e = (int)E;
+        e = md.eloc;
     } else if (!E && sscanf(n.c_str(), "mlp.%63[a-z]_proj.%63s", part, kind) == 2) {
         e = 0;     // dense MLP = the lone "shared" expert
     } else {
@@ -499,7 +577,7 @@ static int resolve(const ApusGcudaModel *m, const char *name, void **dst, size_t
     std::string n(name);
     if (n == "embed_tokens.weight") { *dst = m->embed; *want = V * d * 2; return 0; }
     if (n == "norm.weight") { *dst = m->norm; *want = d * 2; return 0; }
-    if (n == "lm_head.weight") { *dst = m->head; *want = V * d * 2; return 0; }
+    if (n == "lm_head.weight") { *dst = m->head; *want = V * d * 2; return 2; }   // vocabulary slice
     int l = -1, off = 0;
     if (sscanf(name, "layers.%d.%n", &l, &off) != 1 || off <= 0 || l < 0 || l >= m->nL) return -1;
     const LayerW &W = m->L[l];
@@ -577,19 +655,36 @@ static int resolve(const ApusGcudaModel *m, const char *name, void **dst, size_t
     return resolve_moe(m, W.moe, r, dst, want);
 }
 
+// 0 = stored; 1 = another expert-parallel rank's expert (nothing stored);
+// -1 = unknown tensor or wrong size.  The lm_head is stored as this rank's
+// vocabulary rows of the full host tensor.
 extern "C" int apus_gcuda_model_set(ApusGcudaModel *m, const char *name, const void *host, size_t bytes) {
     void *dst;
     size_t want;
-    if (resolve(m, name, &dst, &want)) { gcuda_set_error("gmodel: unknown tensor %s", name); return -1; }
+    const int rc = resolve(m, name, &dst, &want);
+    if (rc == 1) return 1;
+    if (rc < 0) { gcuda_set_error("gmodel: unknown tensor %s", name); return -1; }
     if (bytes != want) { gcuda_set_error("gmodel: %s has %zu bytes, expected %zu", name, bytes, want); return -1; }
+    if (rc == 2) {
+        const size_t row = (size_t)m->D.d * 2;
+        return gcuda_check(cudaMemcpy(dst, (const uint8_t *)host + m->v0 * row, m->vn * row, cudaMemcpyHostToDevice),
+                           "gmodel set");
+    }
     return gcuda_check(cudaMemcpy(dst, host, bytes, cudaMemcpyHostToDevice), "gmodel set");
 }
 
 extern "C" int apus_gcuda_model_get(ApusGcudaModel *m, const char *name, void *host, size_t bytes) {
     void *src;
     size_t want;
-    if (resolve(m, name, &src, &want) || bytes != want) { gcuda_set_error("gmodel: bad get %s", name); return -1; }
+    const int rc = resolve(m, name, &src, &want);
+    if (rc == 1) return 1;
+    if (rc < 0 || bytes != want) { gcuda_set_error("gmodel: bad get %s", name); return -1; }
     cudaStreamSynchronize(m->st);
+    if (rc == 2) {   // this rank's rows, at their place in the full tensor
+        const size_t row = (size_t)m->D.d * 2;
+        return gcuda_check(cudaMemcpy((uint8_t *)host + m->v0 * row, src, m->vn * row, cudaMemcpyDeviceToHost),
+                           "gmodel get");
+    }
     return gcuda_check(cudaMemcpy(host, src, bytes, cudaMemcpyDeviceToHost), "gmodel get");
 }
 
@@ -611,9 +706,22 @@ extern "C" int apus_gcuda_model_init_random(ApusGcudaModel *m, uint64_t seed) {
         rc |= fill_launch(FILL_E4M3_NORMAL, (void *)c, n, seed, sid++, 64.f, 0.f, st);
         rc |= fill_launch(FILL_F32_LOGUNIFORM, (void *)s, ns, seed, sid++, 1e-4f, 1e-2f, st);
     };
+    // Expert blocks of an MoE layer: one random stream over the (E+1) experts
+    // of the whole model; this rank draws its routed slice [e0, e0+eloc) and
+    // the shared expert E, so every rank count yields the same weights.
+    auto fp8_experts = [&](const MoeDev &md, const uint8_t *c, const float *s, size_t per, size_t per_s) {
+        const size_t E = md.E, e0 = md.e0, el = md.eloc;
+        rc |= fill_launch(FILL_E4M3_NORMAL, (void *)c, el * per, seed, sid, 64.f, 0.f, st, e0 * per);
+        rc |= fill_launch(FILL_E4M3_NORMAL, (void *)(c + el * per), per, seed, sid, 64.f, 0.f, st, E * per);
+        sid++;
+        rc |= fill_launch(FILL_F32_LOGUNIFORM, (void *)s, el * per_s, seed, sid, 1e-4f, 1e-2f, st, e0 * per_s);
+        rc |= fill_launch(FILL_F32_LOGUNIFORM, (void *)(s + el * per_s), per_s, seed, sid, 1e-4f, 1e-2f, st,
+                          E * per_s);
+        sid++;
+    };
     auto norm = [&](const void *p, size_t n) { bf16n(p, n, 0.05f, 1.0f); };
     bf16n(m->embed, (size_t)D.V * d, 0.02f);          // BASELINE: N(0, 0.02) embeddings and head
-    bf16n(m->head, (size_t)D.V * d, 0.02f);
+    rc |= fill_launch(FILL_BF16_NORMAL, m->head, (size_t)m->vn * d, seed, sid++, 0.02f, 0.f, st, (size_t)m->v0 * d);
     norm(m->norm, d);
     const int mix = (2 + D.hc) * D.hc;
     for (int l = 0; l < m->nL; l++) {
@@ -656,8 +764,8 @@ extern "C" int apus_gcuda_model_init_random(ApusGcudaModel *m, uint64_t seed) {
             bf16n(md.gate_w, (size_t)md.E * d, 0.02f);           // N(0, 0.02), bias 0
             rc |= fill_launch(FILL_F32_CONST, (void *)md.gate_bias, md.E, seed, sid++, 0.f, 0.f, st);
         }
-        fp8(md.gu_codes, md.gu_scales, (size_t)(md.E + 1) * 2 * md.inter * d, (size_t)(md.E + 1) * (2 * md.inter / 128) * nkd);
-        fp8(md.d_codes, md.d_scales, (size_t)(md.E + 1) * d * md.inter, (size_t)(md.E + 1) * nkd * nki);
+        fp8_experts(md, md.gu_codes, md.gu_scales, 2 * md.inter * d, (2 * md.inter / 128) * nkd);
+        fp8_experts(md, md.d_codes, md.d_scales, d * md.inter, nkd * nki);
     }
     if (m->has_mtp) {
         norm(m->enorm, d);
@@ -708,11 +816,20 @@ extern "C" size_t apus_gcuda_model_pos(const ApusGcudaModel *m) {
 static int lm_head(ApusGcudaModel *m, const uint16_t *yn, int R, int *picks, bool want_logits) {
     const Dims &D = m->D;
     GemvDesc g{};
-    g.W = m->head; g.x = yn; g.ldx = D.d; g.R = R; g.O = D.V; g.K = D.d; g.fp8 = 0;
-    if (want_logits) { g.y = m->S.logits; g.ldy = D.V; }
+    g.W = m->head; g.x = yn; g.ldx = D.d; g.R = R; g.O = m->vn; g.K = D.d; g.fp8 = 0;
+    g.row_base = m->v0; g.plan_o = D.V;     // a vocabulary slice sums like the whole head
+    if (want_logits) {
+        if (m->ep_world > 1) return -1;     // the logits stay split over the ranks
+        g.y = m->S.logits; g.ldy = D.V;
+    }
     g.amax = m->S.amax; g.part = m->part; g.ticket = m->tick;
     g.pdl = 1;
     if (gemv_launch(g, m->st)) return -1;
+    if (m->ep_world > 1) {
+        // the largest key over every rank's slice: publish, barrier, reduce
+        if (ep_barrier_launch(m->ep, m->S.amax, R, m->st) || ep_picks_launch(m->ep, R, picks, m->st)) return -1;
+        return 0;
+    }
     k_extract_picks<<<1, 32, 0, m->st>>>(m->S.amax, R, picks);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
@@ -808,6 +925,7 @@ extern "C" int apus_gcuda_decode_batch(ApusGcudaModel *m, const int32_t *ids, si
     const Dims &D = m->D;
     if (s < 1 || s > MAXR) { gcuda_set_error("decode_batch: %zu rows (1..%d)", s, MAXR); return -1; }
     if (!ids_ok(m, ids, s, "decode_batch")) return -1;
+    if (logits && m->ep_world > 1) { gcuda_set_error("decode_batch: logits are split over the ranks"); return -1; }
     Ctl c = read_ctl(m);
     if ((size_t)c.pos + s > (size_t)m->cap) { gcuda_set_error("decode_batch: capacity"); return -1; }
     cudaMemcpyAsync(m->ids, ids, s * 4, cudaMemcpyHostToDevice, m->st);
@@ -825,6 +943,7 @@ extern "C" int apus_gcuda_mtp_forward(ApusGcudaModel *m, const int32_t *ids, con
     if (!m->has_mtp) { gcuda_set_error("gmtp: model has no MTP block loaded"); return -1; }
     if (s < 1 || s > MAXR) { gcuda_set_error("mtp_forward: %zu rows", s); return -1; }
     if (!ids_ok(m, ids, s, "mtp_forward")) return -1;
+    if (logits && m->ep_world > 1) { gcuda_set_error("mtp_forward: logits are split over the ranks"); return -1; }
     Ctl c = read_ctl(m);
     if ((size_t)c.mtp_n + s > (size_t)m->cap) { gcuda_set_error("mtp_forward: capacity"); return -1; }
     cudaMemcpyAsync(m->ids, ids, s * 4, cudaMemcpyHostToDevice, m->st);

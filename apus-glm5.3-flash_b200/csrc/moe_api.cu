@@ -41,6 +41,7 @@ ApusGcudaMoe *apus_gcuda_moe_new(int E, int topk, size_t dim, size_t inter, floa
     ApusGcudaMoe *m = new ApusGcudaMoe();
     MoeDev &d = m->d;
     d.E = E; d.topk = topk; d.dim = (int)dim; d.inter = (int)inter; d.max_r = max_rows; d.pdl = 0;
+    d.e0 = 0; d.eloc = E;          // every expert local, no exchange (d.ep.world == 0)
     d.route_scale = route_scale; d.limit = swiglu_limit;
     m->nkb_d = (dim + 127) / 128;
     m->nkb_i = (inter + 127) / 128;

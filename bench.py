@@ -429,14 +429,15 @@ def c2_config(small=False):
 C2 = dict(prompt=512, depth=4, seed=2)   # BASELINE "depth 3" = 4 verify rows (reference APUS_SPEC_K 4)
 
 
-def c2_weights(kw, seed):
+def c2_weights(kw, seed, keep=None):
     """Seeded synthetic weights for every tensor of tensor_specs(kw), made
     with torch on the GPU and returned as host numpy arrays (both bench arms
     load the same arrays).  Experts: BASELINE config 0 codes (E4M3 of
     N(0,1)*64) with log-uniform [1e-4, 1e-2] block scales; router BF16
     N(0, 0.02) with a zero bias; embeddings and head BF16 N(0, 0.02); the DSA
     FP8 linears amax/448 block-scaled N(0, 1/sqrt(K)); BF16 matrices
-    N(0, 1/sqrt(K)); norms 1 + 0.05 N(0,1)."""
+    N(0, 1/sqrt(K)); norms 1 + 0.05 N(0,1).  keep(name): tensors to return
+    (the others are still drawn, so every rank sees the same stream)."""
     import math
     import numpy as np
     import torch
@@ -471,8 +472,9 @@ def c2_weights(kw, seed):
                 sc = amax / 448.0
                 q = torch.clamp(blk / sc[:, None, :, None], -448, 448).view(nbo * 128, nbk * 128)
                 codes = q[:O_, :K_].to(torch.float8_e4m3fn)
-            out[name] = codes.view(torch.uint8).cpu().numpy()
-            out[sname] = sc.float().cpu().numpy()
+            if keep is None or keep(name):
+                out[name] = codes.view(torch.uint8).cpu().numpy()
+                out[sname] = sc.float().cpu().numpy()
             i += 2
             continue
         if kind == "f32":
@@ -509,14 +511,15 @@ def c2_prompt(kw, seed):
     return np.random.default_rng(seed).integers(0, kw["vocab_size"], C2["prompt"]).astype(np.int32)
 
 
-def c2_algo_bytes(kw, depth, n_ctx, moe_problems):
+def c2_algo_bytes(kw, depth, n_ctx, moe_problems, world=1):
     """Algorithmic HBM bytes of one speculative step: every weight byte the
     step's forwards must read once (main forward over `depth` rows, the MTP
     replay and depth-1 chain forwards), the realised MoE expert union
     (`moe_problems` expert GEMV pairs, shared expert included, counted on the
     device), the KDA state read + final write, the DSA K/V and pool-key rows
     visible at context n_ctx, and the new cache rows.  Checkpoint copies and
-    L2 reuse are not counted."""
+    L2 reuse are not counted.  Expert-parallel ranks (world > 1) read their
+    vocabulary slice of the lm_head and count their own expert problems."""
     d, V, hc, L = kw["hidden_size"], kw["vocab_size"], kw["hc_mult"], kw["num_hidden_layers"]
     H, D, K = kw["linear_num_heads"], kw["linear_head_dim"], kw["linear_conv_kernel_dim"]
     qkv, mix = H * D, (2 + hc) * hc
@@ -537,8 +540,9 @@ def c2_algo_bytes(kw, depth, n_ctx, moe_problems):
     expert = fp8(2 * inter, d) + fp8(d, inter)
     hcb = 2 * mix * hc * d * 2
     main = sum(hcb + (dsa(depth, n_ctx) if kw["layer_is_dsa"][l] else kda) + router for l in range(L))
-    main += V * d * 2
-    mtp_fwd = lambda rows, n: 2 * d * d * 2 + dsa(rows, n) + router + V * d * 2
+    head = -(-V // world) * d * 2
+    main += head
+    mtp_fwd = lambda rows, n: 2 * d * d * 2 + dsa(rows, n) + router + head
     mtp = mtp_fwd(depth, n_ctx) + sum(mtp_fwd(1, n_ctx + i) for i in range(depth - 1))
     n_moe_calls = L + 1 + (depth - 1)
     return main + mtp + moe_problems * expert, n_moe_calls
@@ -551,11 +555,15 @@ def bench_c2(args, ws, rank, W=None):
     G.enable()
     kw = c2_config(args.small)
     depth = C2["depth"]
+    ep = ws > 1 and args.mode == "ep"
     if W is None:
-        W = c2_weights(kw, C2["seed"])
+        W = c2_weights(kw, C2["seed"], keep=G.ep_owns(kw, rank, ws) if ep else None)
     prompt = c2_prompt(kw, C2["seed"])[:args.prompt or C2["prompt"]]
     cap = len(prompt) + depth * (2 * args.steps + 2 * args.warmup) + 64
-    m = G.GModel(G.make_config(**kw), has_mtp=True, kv_cap=cap, depth=depth)
+    m = G.GModel(G.make_config(**kw), has_mtp=True, kv_cap=cap, depth=depth,
+                 rank=rank if ep else 0, world=ws if ep else 1)
+    if ep:   # one sequence over every GPU: experts and lm_head rows split
+        m.ep_bootstrap(G.ep_all_gather())
     m.load(W)
     m.use_graph(True)
     m.spec_prefill(prompt)
@@ -589,20 +597,24 @@ def bench_c2(args, ws, rank, W=None):
     tok_s = emitted / (ms * 1e-3)
     n_ctx = (s0["pos"] + s1["pos"]) // 2
     probs = (c1["moe_problems"] - c0["moe_problems"]) / args.steps
-    algo, _ = c2_algo_bytes(kw, depth, n_ctx, probs)
+    algo, _ = c2_algo_bytes(kw, depth, n_ctx, probs, ws if ep else 1)
     hbm, _, src = peaks()
     gbs = algo / (per * 1e-3) / 1e9
     offered = s1["offered"] - s0["offered"]
     accepted = s1["accepted"] - s0["accepted"]
-    out = {"metric": METRIC, "value": round(tok_s * ws, 2), "unit": "accepted tok/s (emitted tokens / s)",
+    agg = 1 if ep else ws       # EP: one sequence across the GPUs; replicas: ws sequences
+    out = {"metric": METRIC, "value": round(tok_s * agg, 2), "unit": "accepted tok/s (emitted tokens / s)",
            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 4),
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "higher_is_better": True, "scaling": "strong" if ep else "weak", "vs_baseline": None,
            "dtype": "bf16 activations, fp8e4m3/bf16 weights, f32 accumulation",
            "data": f"synthetic random-init weights (seed {C2['seed']}), {len(prompt)} uniform random prompt ids",
            "config": {"workload": "config2: scaled glm5_next (4 layers: 3 KDA 32x128 + 1 DSA, MoE 288 top-8 "
                                   "inter 1024, vocab 154880) + 1 NextN MTP layer, greedy spec decode",
                       "depth": "BASELINE depth 3 = 4 verify rows (reference APUS_SPEC_K 4)",
-                      "prompt": len(prompt), "parallelism": f"replicas x{ws}",
+                      "prompt": len(prompt),
+                      "parallelism": (f"ep{ws}: routed experts and lm_head rows split over {ws} GPUs, "
+                                      "peer-memory exchange per MoE layer and per lm_head") if ep
+                      else f"replicas x{ws}",
                       "l2": "inputs larger than L2: each step streams ~10 GB of weights",
                       "step": "one device-resident speculative step replayed from a CUDA graph"},
            "spec": {"tokens_per_step": round(emitted / args.steps, 4), "offered": offered, "accepted": accepted,
@@ -625,7 +637,7 @@ def bench_c2(args, ws, rank, W=None):
     for _ in range(args.steps):
         n_e2e += len(m.spec_step())
     e2e = max_over_ranks(time.perf_counter() - t0, ws)
-    out["e2e"] = {"value": round(n_e2e / e2e * ws, 2), "unit": "accepted tok/s through apus_gcuda_gspec_step",
+    out["e2e"] = {"value": round(n_e2e / e2e * agg, 2), "unit": "accepted tok/s through apus_gcuda_gspec_step",
                   "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 2 * int(c1["ctl_bytes"]),
                   "note": "no per-step inputs cross to the device; the control block is read back twice"}
     m.close()
@@ -684,6 +696,9 @@ def main():
     ap.add_argument("--small", action="store_true",
                     help="config 2 layer shapes with 16 experts and a 16384 vocab (profiling captures only)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of reference CPU decode sampled")
+    ap.add_argument("--mode", default="ep", choices=["ep", "replicas"],
+                    help="config 2 with several GPUs: one sequence expert-parallel over all of them (ep), "
+                         "or one independent sequence per GPU (replicas)")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed kernels only (no e2e, no CPU baseline): the profiling command")
     args = ap.parse_args()

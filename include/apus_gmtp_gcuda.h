@@ -63,6 +63,22 @@ typedef struct ApusGcudaModel ApusGcudaModel;
 ApusGcudaModel *apus_gcuda_model_new(const ApusGcudaConfig *cfg, int has_mtp, size_t kv_cap, int depth);
 void apus_gcuda_model_free(ApusGcudaModel *m);
 
+/* Expert parallelism over `world` GPUs, one process and one model per GPU.
+ * Rank r keeps routed experts [r*E/world, (r+1)*E/world), the shared expert
+ * and vocabulary rows [r*ceil(V/world), ...) of the lm_head; everything else
+ * is replicated.  Each MoE layer exchanges the weighted expert outputs and the
+ * lm_head exchanges its argmax keys through peer memory; every rank emits the
+ * same tokens as a one-GPU model.  The reference runs the whole model in one
+ * process (c/gmodel.h:161-164); this is its multi-GPU form.  Bootstrap: every
+ * rank calls _ep_handle (64 bytes out), the handles are all-gathered by the
+ * host, then every rank calls _ep_connect with the world*64 bytes in rank
+ * order.  set() returns 1 for another rank's expert tensor (nothing stored),
+ * and decode_batch / mtp_forward refuse to return logits. */
+ApusGcudaModel *apus_gcuda_model_new_ep(const ApusGcudaConfig *cfg, int has_mtp, size_t kv_cap, int depth,
+                                        int rank, int world);
+int apus_gcuda_model_ep_handle(ApusGcudaModel *m, void *handle_out /* 64 bytes */);
+int apus_gcuda_model_ep_connect(ApusGcudaModel *m, const void *handles /* world * 64 bytes */);
+
 /* Tensor by checkpoint name (c/gmodel.h:622-1106 names, minus the
  * "model.language_model." prefix), host pointer, synchronous. */
 int apus_gcuda_model_set(ApusGcudaModel *m, const char *name, const void *host, size_t bytes);
