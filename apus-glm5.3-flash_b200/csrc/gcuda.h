@@ -31,10 +31,12 @@ struct GemvDesc {
     const int *gcount;
     int gmax;
     long w_estride, s_estride, x_pstride, y_pstride;
+    int gnum;               // weight blocks in the packed arrays (grouped mode)
     // set by gemv_launch from (O, K, fp8, grouped) alone: the K range of one
     // work item and the weight tiles per work item
     long kx;
     int tpi;
+    int box_ko;             // 128-byte k-slabs per tensor copy
     // argmax keys carry row + row_base (a vocabulary slice's global ids)
     long row_base;
     // plan the k-ranges as for a matrix of plan_o rows (0: O), so a slice of a
@@ -44,6 +46,18 @@ struct GemvDesc {
     // h = bf16(bf16(silu(min(g, lim))) * clip(u, +-lim)) (c/gmoe.h:216-224).
     int x_swiglu;
     float swiglu_limit;
+    // Grouped mode, expert parallelism: row m of problem p whose selection
+    // slot j = scat_slot[p*8 + m] is >= 0 also stores bf16(y * scat_w[m*scat_k
+    // + j]) (y already rounded to BF16) at element
+    // ((half*8 + m)*scat_j + j)*scat_ld + row of scat, half = (*scat_epoch+1)&1:
+    // the weighted expert output other ranks read after the next exchange.
+    uint16_t *scat;
+    const int *scat_slot;
+    const float *scat_w;
+    const int *scat_epoch;
+    int scat_k, scat_j;
+    long scat_ld;
+    int scat_r0;            // row offset of this launch's rows (row groups)
 };
 
 bool gemv_fast_ok(const GemvDesc &d);

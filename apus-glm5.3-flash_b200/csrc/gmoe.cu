@@ -147,6 +147,15 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float 
     for (int i = threadIdx.x; i < R * K; i += blockDim.x)
         m.row_prob[i] = slot_of[m.row_expert[i]];
     if (threadIdx.x < R) m.row_prob_shared[threadIdx.x] = slot_of[E];
+    if (m.prob_slot) {   // (problem, row) -> selection slot, for the scatter epilogue
+        const int np = slot_of[E] + 1;
+        for (int i = threadIdx.x; i < np * 8; i += blockDim.x) m.prob_slot[i] = -1;
+        __syncthreads();
+        for (int i = threadIdx.x; i < R * K; i += blockDim.x) {
+            const int p = slot_of[m.row_expert[i]];
+            if (p >= 0) m.prob_slot[p * 8 + i / K] = i % K;
+        }
+    }
 }
 
 // out[r][i] = bf16(y + shared), y = ascending bf16 accumulation of
@@ -190,41 +199,65 @@ __global__ void k_moe_combine(MoeDev m, int R, uint16_t *out, long ldo) {
     *(uint4 *)(out + (size_t)r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Expert parallelism: every rank writes the weighted outputs of its own
-// experts, bf16(bf16(expert) * w), into its exchange region's contrib half
-// (slot j of row r in ascending expert order); after the barrier every rank
-// combines all slots from their owners' regions.
-__global__ void k_moe_contrib(MoeDev m, int R) {
-    pdl_launch_dependents();
-    const int d = m.dim, K = m.topk, nc = d / 8;
-    const size_t pstride = (size_t)m.max_r * d;
-    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)R * K * nc) return;
-    const int c = (int)(i % nc) * 8, j = (int)((i / nc) % K), r = (int)(i / nc / K);
-    const int p = m.row_prob[r * K + j];
-    if (p < 0) return;                                   // another rank's expert
-    const int half = (*m.ep.epoch + 1) & 1;              // the half the next barrier publishes
-    const uint4 ev = *(const uint4 *)(m.yd + p * pstride + (size_t)r * d + c);
-    const float w = m.row_weight[r * K + j];
-    const uint32_t ew[4] = {ev.x, ev.y, ev.z, ev.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int e = 0; e < 4; e++)
-        o[e] = (uint32_t)bf16_bits(bf16_round(bf16lo(ew[e]) * w)) |
-               ((uint32_t)bf16_bits(bf16_round(bf16hi(ew[e]) * w)) << 16);
-    uint16_t *dst = (uint16_t *)m.ep.peer[m.ep.rank] +
-                    (((size_t)half * MOE_MAX_R + r) * MOE_MAX_TOPK + j) * d + c;
-    *(uint4 *)dst = make_uint4(o[0], o[1], o[2], o[3]);
+// ---- expert parallelism --------------------------------------------------
+// Every rank's down GEMV scatters bf16(bf16(expert) * w) of its own experts
+// into its exchange region (half (epoch+1)&1, [row][slot j][dim], the slot
+// order of the row's ascending expert list).  One exchange kernel then
+// signals every peer, waits for every peer's signal of the same epoch and
+// sums the slots from their owners' regions in slot order, the same
+// ascending-expert BF16 accumulation as k_moe_combine.
+
+// Thread 0 of a CTA: signal (CTA 0 only) and wait for every rank's epoch-e
+// signal.  Each wait is bounded (about a second of clock cycles) and records
+// an error instead of hanging.
+APUS_DEV void ep_signal_wait(const EpCtx &ep, int e, bool signal) {
+    if (signal) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int p = 0; p < ep.world; p++) {
+            int *pf = (int *)(ep.peer[p] + ep.off_flags) + ep.rank;
+            asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(pf), "r"(e) : "memory");
+        }
+    }
+    const int *mine = (const int *)(ep.peer[ep.rank] + ep.off_flags);
+    const long long t0 = clock64();
+    for (int p = 0; p < ep.world; p++) {
+        int v = 0;
+        while (true) {
+            asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine + p) : "memory");
+            if (v >= e) break;
+            if (clock64() - t0 > (1ll << 31)) {
+                atomicExch(&g_apus_ep_err, 5);
+                return;
+            }
+        }
+    }
 }
 
-__global__ void k_moe_combine_ep(MoeDev m, int R, uint16_t *out, long ldo) {
+// Every CTA reads the epoch before it arrives; the last CTA to arrive (all
+// others have read it by then) advances it for the next exchange.
+APUS_DEV void ep_arrive(const EpCtx &ep, int e) {
+    if (atomicAdd(ep.epoch + 1, 1) == (int)gridDim.x - 1) {
+        ep.epoch[1] = 0;
+        ep.epoch[0] = e;
+    }
+}
+
+__global__ void k_moe_exchange(MoeDev m, int R, uint16_t *out, long ldo) {
+    __shared__ int e_sh;
+    if (threadIdx.x == 0) {
+        const int e = *(volatile int *)m.ep.epoch + 1;
+        e_sh = e;
+        ep_signal_wait(m.ep, e, blockIdx.x == 0);
+        ep_arrive(m.ep, e);
+    }
+    __syncthreads();
     pdl_launch_dependents();
     const int d = m.dim, K = m.topk, nc = d / 8;
     const size_t pstride = (size_t)m.max_r * d;
     const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
     if (i >= (long)R * nc) return;
     const int r = (int)(i / nc), c = (int)(i % nc) * 8;
-    const int half = *m.ep.epoch & 1;                    // the half the last barrier published
+    const int half = e_sh & 1;
     uint4 ev[MOE_MAX_TOPK];
 #pragma unroll
     for (int j = 0; j < MOE_MAX_TOPK; j++)
@@ -254,54 +287,30 @@ __global__ void k_moe_combine_ep(MoeDev m, int R, uint16_t *out, long ldo) {
     *(uint4 *)(out + (size_t)r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// One warp.  Lane p < world signals peer p and then waits for peer p's
-// signal; the wait is bounded (about a second of clock cycles) and records
-// an error instead of hanging.
-__global__ void k_ep_barrier(EpCtx ep, const unsigned long long *keys, int nkeys) {
+// One warp: publish this rank's argmax keys, signal, wait, reduce over ranks.
+__global__ void k_ep_picks(EpCtx ep, const unsigned long long *keys, int R, int *picks) {
     __shared__ int e_sh;
     const int lane = threadIdx.x;
+    if (lane == 0) e_sh = *(volatile int *)ep.epoch + 1;
+    __syncwarp();
+    const int e = e_sh, half = e & 1;
+    unsigned long long *kd = (unsigned long long *)(ep.peer[ep.rank] + ep.off_keys) + (size_t)half * MOE_MAX_R;
+    if (lane < R) kd[lane] = keys[lane];
+    __syncwarp();
     if (lane == 0) {
-        e_sh = *ep.epoch + 1;
-        *ep.epoch = e_sh;
+        ep_signal_wait(ep, e, true);
+        ep.epoch[0] = e;                                // one CTA: nobody else reads it
     }
     __syncwarp();
-    const int e = e_sh;
-    if (lane < nkeys) {    // publish this rank's keys into the half of epoch e
-        unsigned long long *kd = (unsigned long long *)(ep.peer[ep.rank] + ep.off_keys) +
-                                 (size_t)(e & 1) * MOE_MAX_R;
-        kd[lane] = keys[lane];
-        __threadfence_system();
-    }
-    __syncwarp();
-    if (lane < ep.world) {
-        int *pf = (int *)(ep.peer[lane] + ep.off_flags) + ep.rank;
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(pf), "r"(e) : "memory");
-        const int *mine = (const int *)(ep.peer[ep.rank] + ep.off_flags) + lane;
-        const long long t0 = clock64();
-        int v = 0;
-        while (true) {
-            asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
-            if (v >= e) break;
-            if (clock64() - t0 > (1ll << 31)) {
-                atomicExch(&g_apus_ep_err, 5);
-                break;
-            }
-        }
-    }
-}
-
-__global__ void k_ep_picks(EpCtx ep, int R, int *picks) {
-    const int r = threadIdx.x;
-    if (r >= R) return;
-    const int half = *ep.epoch & 1;
+    pdl_launch_dependents();
+    if (lane >= R) return;
     unsigned long long best = 0ull;
     for (int p = 0; p < ep.world; p++) {
         const unsigned long long k =
-            __ldcv((const unsigned long long *)(ep.peer[p] + ep.off_keys) + (size_t)half * MOE_MAX_R + r);
+            __ldcv((const unsigned long long *)(ep.peer[p] + ep.off_keys) + (size_t)half * MOE_MAX_R + lane);
         best = k > best ? k : best;
     }
-    picks[r] = (int)argmax_key_index(best);
+    picks[lane] = (int)argmax_key_index(best);
 }
 
 }  // namespace apus
@@ -330,7 +339,7 @@ int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint
     gu.W = m.gu_codes; gu.WS = m.gu_scales; gu.nkb = (m.dim + 127) / 128;
     gu.x = x; gu.ldx = ldx; gu.R = R; gu.O = 2L * m.inter; gu.K = m.dim; gu.fp8 = 1;
     gu.y = m.gu; gu.ldy = 2L * m.inter;
-    gu.gexpert = m.prob_expert; gu.gcount = m.prob_count; gu.gmax = R * m.topk + 1;
+    gu.gexpert = m.prob_expert; gu.gcount = m.prob_count; gu.gmax = R * m.topk + 1; gu.gnum = m.eloc + 1;
     gu.w_estride = 2L * m.inter * m.dim;
     gu.s_estride = (2L * m.inter / 128) * ((m.dim + 127) / 128);
     gu.x_pstride = 0;
@@ -342,7 +351,7 @@ int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint
     dn.W = m.d_codes; dn.WS = m.d_scales; dn.nkb = (m.inter + 127) / 128;
     dn.x = m.gu; dn.ldx = 2L * m.inter; dn.R = R; dn.O = m.dim; dn.K = m.inter; dn.fp8 = 1;
     dn.y = m.yd; dn.ldy = m.dim;
-    dn.gexpert = m.prob_expert; dn.gcount = m.prob_count; dn.gmax = R * m.topk + 1;
+    dn.gexpert = m.prob_expert; dn.gcount = m.prob_count; dn.gmax = R * m.topk + 1; dn.gnum = m.eloc + 1;
     dn.w_estride = (long)m.dim * m.inter;
     dn.s_estride = ((m.dim + 127) / 128) * ((m.inter + 127) / 128);
     dn.x_pstride = (long)m.max_r * 2 * m.inter;
@@ -350,16 +359,23 @@ int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint
     dn.x_swiglu = 1;
     dn.swiglu_limit = m.limit;
     dn.pdl = m.pdl;
+    const bool ep = m.ep.world > 1 && m.E > 0;
+    if (ep) {
+        if (!ep_connected(m.ep) || m.eloc * m.ep.world != m.E || !m.prob_slot) return -1;
+        dn.scat = (uint16_t *)m.ep.peer[m.ep.rank];
+        dn.scat_slot = m.prob_slot;
+        dn.scat_w = m.row_weight;
+        dn.scat_epoch = m.ep.epoch;
+        dn.scat_k = m.topk;
+        dn.scat_j = MOE_MAX_TOPK;
+        dn.scat_ld = m.dim;
+    }
     if (gemv_launch(dn, st)) return -1;
     // 5. ordered combine (across ranks when the experts are split)
     if (m.dim % 8 || ((uintptr_t)out & 15) || (ldo % 8)) return -1;
     const long n = (long)R * (m.dim / 8);
-    if (m.ep.world > 1 && m.E > 0) {
-        if (!ep_connected(m.ep) || m.eloc * m.ep.world != m.E) return -1;
-        const long nc = (long)R * m.topk * (m.dim / 8);
-        k_moe_contrib<<<(unsigned)((nc + 127) / 128), 128, 0, st>>>(m, R);
-        if (ep_barrier_launch(m.ep, nullptr, 0, st)) return -1;
-        k_moe_combine_ep<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(m, R, out, ldo);
+    if (ep) {
+        k_moe_exchange<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(m, R, out, ldo);
     } else {
         k_moe_combine<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(m, R, out, ldo);
     }
@@ -374,15 +390,10 @@ static bool ep_connected(const EpCtx &ep) {
     return true;
 }
 
-int ep_barrier_launch(const EpCtx &ep, const unsigned long long *keys, int nkeys, cudaStream_t st) {
-    if (!ep_connected(ep) || nkeys > MOE_MAX_R || (nkeys > 0 && !keys)) return -1;
-    k_ep_barrier<<<1, 32, 0, st>>>(ep, keys, nkeys);
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
-}
-
-int ep_picks_launch(const EpCtx &ep, int R, int *picks, cudaStream_t st) {
-    if (!ep_connected(ep) || R < 1 || R > MOE_MAX_R) return -1;
-    k_ep_picks<<<1, 32, 0, st>>>(ep, R, picks);
+int ep_picks_exchange_launch(const EpCtx &ep, const unsigned long long *keys, int R, int *picks,
+                             cudaStream_t st) {
+    if (!ep_connected(ep) || R < 1 || R > MOE_MAX_R || !keys || !picks) return -1;
+    k_ep_picks<<<1, 32, 0, st>>>(ep, keys, R, picks);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -19,7 +19,7 @@
 struct EpCtx {
     int rank, world;
     uint8_t *peer[EP_MAX_RANKS];  // every rank's region (peer[rank] is this rank's)
-    int *epoch;                   // this rank's barrier counter (device)
+    int *epoch;                   // this rank's exchange counter (device); epoch[1]: CTA arrivals
     long off_keys, off_flags;     // byte offsets inside a region
 };
 
@@ -42,6 +42,8 @@ struct MoeDev {
     int32_t *row_sel;            // [max_r][topk] selection in top-k order
     int32_t *row_prob;           // [max_r][topk] problem slot of each selection
     int32_t *row_prob_shared;    // [max_r] problem slot of the shared expert
+    int32_t *prob_slot;          // [max_r*topk+1][8] selection slot j of (problem, row), -1: none
+                                 // (expert parallelism only)
     int32_t *prob_expert;        // [max_r*topk+1] expert of each problem slot
     int32_t *prob_count;         // [1]
     unsigned long long *stat_problems;   // optional: += expert problems (incl. shared) per call
@@ -57,10 +59,10 @@ struct MoeDev {
 int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
                        const int32_t *forced, cudaStream_t st);
 
-// Cross-rank barrier of the expert-parallel group: bumps the epoch, publishes
-// keys[0..nkeys) (optional) into this rank's keys half, signals every peer and
-// waits (bounded) until every peer has signalled the same epoch.
-int ep_barrier_launch(const EpCtx &ep, const unsigned long long *keys, int nkeys, cudaStream_t st);
-// picks[r] = index of the largest key over every rank's published keys half.
-int ep_picks_launch(const EpCtx &ep, int R, int *picks, cudaStream_t st);
+// Greedy picks over a vocabulary split across the expert-parallel group: one
+// exchange publishes keys[0..R) (this rank's argmax keys), signals every
+// peer, waits (bounded) for every peer's keys of the same exchange, and
+// writes picks[r] = index of the largest key over all ranks.
+int ep_picks_exchange_launch(const EpCtx &ep, const unsigned long long *keys, int R, int *picks,
+                             cudaStream_t st);
 size_t ep_region_bytes(int dim);

@@ -1074,7 +1074,7 @@ int kda_launch(const Dims &D, const LayerW &W, KdaState &KS, const Ctl *ctl, int
     GemvDesc fg{};
     fg.W = W.kda.fg_b; fg.x = S.kp + 3 * qkv; fg.ldx = ldkp; fg.R = R; fg.O = qkv; fg.K = D.Dr; fg.fp8 = 0;
     fg.y = S.fgo; fg.ldy = qkv;
-    fg.gexpert = d_probs; fg.gcount = d_cnt; fg.gmax = 2;
+    fg.gexpert = d_probs; fg.gcount = d_cnt; fg.gmax = 2; fg.gnum = 2;
     fg.w_estride = (long)qkv * D.Dr * 2; fg.x_pstride = D.Dr; fg.y_pstride = (long)MAXR * qkv;
     fg.pdl = 1;
     if (gemv_launch(fg, st)) return -1;

@@ -2,6 +2,10 @@
 #include "linear.cuh"
 #include "pipe.cuh"
 #include "gcuda.h"
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <mutex>
+#include <unordered_map>
 
 namespace apus {
 
@@ -72,14 +76,23 @@ __global__ void k_fp8_dequant(const uint8_t *__restrict__ w, const float *__rest
 // carry two tiles per work item (both fixed by the matrix shape, so a row's
 // arithmetic never depends on the number of rows).  Row strides are padded
 // so the 8 lanes of every quarter-warp hit distinct 16-byte bank groups.
+#ifndef APUS_GEMV_NSTAGE
+#define APUS_GEMV_NSTAGE 2
+#endif
+#ifndef APUS_GEMV_CTAS
+#define APUS_GEMV_CTAS 2
+#endif
+#ifndef APUS_GEMV_CH
+#define APUS_GEMV_CH 2048
+#endif
 namespace gemvcfg {
-constexpr int NSTAGE = 2;
-constexpr int TR = 16;                // weight rows per tile
-constexpr int CH = 2048;              // bytes of one weight row per chunk
-constexpr int RS = CH + 64;           // smem row stride of the ring
-constexpr int STAGE_BYTES = TR * RS;
+constexpr int NSTAGE = APUS_GEMV_NSTAGE;      // ring depth per CTA
+constexpr int CTAS_PER_SM = APUS_GEMV_CTAS;   // CTAs per SM: one's epilogue overlaps another's stream
+constexpr int TR = 16;                        // weight rows per tile
+constexpr int CH = APUS_GEMV_CH;              // bytes of one weight row per chunk
+constexpr int STAGE_BYTES = TR * CH;         // one swizzled box (or two tiles' boxes)
 constexpr long KX = 4096;             // elements of K per work item
-constexpr int XMAX = 4 * (2 * (int)KX + 16);   // staged activations: up to 4 rows
+constexpr int XMAX = 4 * (2 * (int)KX + 32);   // staged activations: up to 4 rows
 constexpr int THREADS = 288;          // 8 consumer warps + 1 producer warp
 constexpr int PART = 8 * TR;          // floats of one warp partial: [x col][w row]
 }  // namespace gemvcfg
@@ -90,11 +103,20 @@ __device__ int g_apus_kernel_err;
 // Epilogue of one finished (x row m, weight row `row`) dot product; the 16
 // threads of an x row are consecutive lanes (one half-warp).
 APUS_DEV void gemv_store(const GemvDesc &d, uint16_t *y, int m, long row, float a,
-                         unsigned long long *best_sh, bool lead) {
+                         unsigned long long *best_sh, bool lead, int p) {
     const bool ok = (m < d.R) && (row < d.O);
     if (ok) {
         if (y) y[(size_t)m * d.ldy + row] = bf16_bits(a);
         if (d.yf) d.yf[(size_t)m * d.ldyf + row] = a;
+        if (d.scat) {
+            const int mm = m + d.scat_r0;
+            const int j = d.scat_slot[p * 8 + mm];
+            if (j >= 0) {
+                const int half = (*d.scat_epoch + 1) & 1;
+                d.scat[(((size_t)half * 8 + mm) * d.scat_j + j) * d.scat_ld + row] =
+                    bf16_bits(bf16_round(bf16_round(a) * d.scat_w[mm * d.scat_k + j]));
+            }
+        }
     }
     if (d.amax) {
         unsigned long long k = ok ? argmax_key(bf16_round(a), (uint32_t)(row + d.row_base)) : 0ull;
@@ -137,22 +159,45 @@ struct GemvItems {
     }
 };
 
-template <bool FP8, bool XS>
-__global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
+// One 3-D tensor copy per chunk: box {128 bytes of k, 16 rows, box_ko
+// 128-byte k-slabs} lands as [slab][row][128 B] with the 128-byte swizzle
+// (16-byte unit u of row r stored at unit u ^ (r & 7)), so the eight rows an
+// ldmatrix reads sit in eight distinct bank groups.
+APUS_DEV void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, int e, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(e), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Address of 16-byte unit `u` of row `r` (0..15) of slab `ko` in a tile.
+APUS_DEV const uint8_t *swz(const uint8_t *tile, int ko, int r, int u) {
+    return tile + ko * (gemvcfg::TR * 128) + r * 128 + ((u ^ (r & 7)) << 4);
+}
+
+APUS_DEV void lds64(uint32_t &lo, uint32_t &hi, const void *p) {
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(lo), "=r"(hi) : "r"(smem_u32(p)));
+}
+
+template <bool FP8>
+__global__ void __launch_bounds__(gemvcfg::THREADS, gemvcfg::CTAS_PER_SM)
+k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
     using namespace gemvcfg;
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t *ring = smem;
-    uint16_t *xs = (uint16_t *)(smem + NSTAGE * STAGE_BYTES);
-    float *part = (float *)(smem + NSTAGE * STAGE_BYTES + (XS ? XMAX : 0));
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *ring = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);   // swizzle atoms: 1 KiB
+    uint16_t *xs = (uint16_t *)(ring + NSTAGE * STAGE_BYTES);
+    float *part = (float *)((uint8_t *)xs + XMAX);
     uint64_t *full = (uint64_t *)(part + 8 * 2 * PART);     // [warp][tile][PART]
     uint64_t *empty = full + NSTAGE;
     __shared__ unsigned long long best_sh[8];
-    __shared__ int abort_sh, ticket_sh;
+    __shared__ int abort_sh;
+    __shared__ unsigned char last_sh[256];   // split K: tiles this CTA reduces
     __shared__ int xexp_sh[8];       // FP8: max BF16 exponent field of each staged row
     __shared__ float xinv_sh[8];     // FP8: 2^-k, the inverse of the row's staging scale
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long rowbytes = FP8 ? d.K : 2 * d.K;
+    const int tile_bytes = TR * d.box_ko * 128;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 8); }
@@ -164,11 +209,11 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
     // The next kernel in the stream may start its own weight stream now.
     pdl_launch_dependents();
 
-    if (warp == 8) {            // ---------------- producer
-        // Lane 0 owns the barriers; lanes 0..TR-1 each issue one row's copy, so
-        // the per-instruction issue cost of the bulk copies is paid in parallel.
+    if (warp == 8) {            // ---------------- producer (one lane)
         // Weights never depend on the previous kernel, so the stream starts
         // before the dependency wait unless the caller says otherwise.
+        if (lane != 0) return;
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
         if (d.weights_after_wait || d.gexpert) pdl_wait();
         GemvItems it;
         it.init(d, d.gexpert ? min(*d.gcount, d.gmax) : 1);
@@ -177,36 +222,21 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
         const int nch = (int)((kbytes + CH - 1) / CH);
         const int tpi = d.tpi;
         long c = 0;
-        bool ok = true;
-        for (long i = it.first; i < it.end && ok; i += it.step) {
+        for (long i = it.first; i < it.end; i += it.step) {
             int p;
             long t;
             it.at(i, p, t);
-            const uint8_t *W = (const uint8_t *)d.W;
-            if (it.grouped) W += (size_t)d.gexpert[p] * d.w_estride;
-            const long row0 = t * TR * tpi;
+            const int e = it.grouped ? d.gexpert[p] : 0;
+            const int row0 = (int)(t * TR * tpi);
             for (int ch = 0; ch < nch; ch++, c++) {
                 const int s = (int)(c % NSTAGE);
                 const long rnd = c / NSTAGE;
-                const long off = (long)ch * CH;
-                const uint32_t len = (uint32_t)min((long)CH, kbytes - off);
-                if (lane == 0) {
-                    if (rnd > 0 && !mbar_wait(&empty[s], (uint32_t)((rnd - 1) & 1), &abort_sh,
-                                              &g_apus_kernel_err, 1))
-                        ok = false;
-                    else
-                        mbar_arrive_expect_tx(&full[s], TR * len * tpi);
-                }
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) break;
-                if (lane < TR) {
-                    // tile j of the item lands at byte j*len of the lane's row slot
-                    for (int j = 0; j < tpi; j++) {
-                        const long row = min(row0 + j * TR + lane, d.O - 1);
-                        bulk_g2s(ring + s * STAGE_BYTES + lane * RS + j * len, W + row * rowbytes + kb0 + off,
-                                 len, &full[s]);
-                    }
-                }
+                if (rnd > 0 && !mbar_wait(&empty[s], (uint32_t)((rnd - 1) & 1), &abort_sh, &g_apus_kernel_err, 1))
+                    return;
+                mbar_arrive_expect_tx(&full[s], (uint32_t)(tile_bytes * tpi));
+                const int ko = (int)((kb0 + (long)ch * CH) / 128);
+                for (int j = 0; j < tpi; j++)
+                    tma_load_3d(ring + s * STAGE_BYTES + j * tile_bytes, &wmap, 0, row0 + j * TR, ko, e, &full[s]);
             }
         }
         return;
@@ -220,9 +250,15 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
     const long kb0 = FP8 ? k0 : 2 * k0, kbytes = FP8 ? klen : 2 * klen;
     const int nch = (int)((kbytes + CH - 1) / CH);
     const int tpi = d.tpi;                                          // tiles per item (1 or 2)
-    const long xstride = klen + 8;                                  // elements
+    // staged row stride: BF16 rows 16 bytes past a 128-byte multiple (the
+    // eight rows of an ldmatrix hit distinct bank groups), FP8 rows 32 bytes
+    // past (the 16 lanes of a 64-bit load phase hit distinct banks)
+    const long xstride = klen + (FP8 ? 16 : 8);                     // elements
     const int g = lane >> 2, t4 = lane & 3;
-    const bool xrow_ok = g < d.R;            // lane supplies B column g
+    const int xrow = min(FP8 ? g : (lane & 7), d.R - 1);             // x row this lane reads
+    // ldmatrix lane roles: matrix mi = lane/8 covers rows (lane&7) + 8*(mi&1)
+    // of the tile and 16-byte unit +(mi>>1)
+    const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8, lunit = lane >> 4;
     const uint16_t *xsrc_staged = nullptr;   // activations currently in smem
     long c = 0;
     for (long i = it.first; i < it.end; i += it.step) {
@@ -233,7 +269,7 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
         uint16_t *yout = d.y ? d.y + (size_t)p * d.y_pstride : nullptr;
         const float *WS = d.WS;
         if (FP8 && it.grouped) WS += (size_t)d.gexpert[p] * d.s_estride;
-        if (XS && xsrc != xsrc_staged) {   // stage x[:, k0:k0+klen]: row r at xs + r*xstride
+        if (xsrc != xsrc_staged) {           // stage x[:, k0:k0+klen]: row r at xs + r*xstride
             named_bar_sync(1, 256);          // previous item's readers are done
             if (FP8) {
                 if (threadIdx.x < 8) xexp_sh[threadIdx.x] = 0;
@@ -248,14 +284,25 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
                         const int q = threadIdx.x + (u0 + u) * 256;
                         if (q < total) v[u] = ld_nc16(xsrc + (size_t)(q / per_row) * d.ldx + k0 + (q % per_row) * 8);
                     }
+                    int mx = 0, mr = -1;
 #pragma unroll
                     for (int u = 0; u < 4; u++) {
                         const int q = threadIdx.x + (u0 + u) * 256;
                         if (q < total) {
                             *(uint4 *)(xs + (q / per_row) * xstride + (q % per_row) * 8) = v[u];
-                            if (FP8) atomicMax(&xexp_sh[q / per_row], bf16x8_max_exp(v[u]));
+                            if (FP8) {
+                                const int r = q / per_row, ex = bf16x8_max_exp(v[u]);
+                                if (r != mr) {
+                                    if (mr >= 0) atomicMax(&xexp_sh[mr], mx);
+                                    mr = r;
+                                    mx = ex;
+                                } else {
+                                    mx = max(mx, ex);
+                                }
+                            }
                         }
                     }
+                    if (FP8 && mr >= 0) atomicMax(&xexp_sh[mr], mx);
                 }
             } else {
                 // x row = [g | u] of 2*K values: h = swiglu(g, u), c/gmoe.h:216-224
@@ -321,7 +368,7 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
         for (int ch = 0; ch < nch; ch++, c++) {
             const int s = (int)(c % NSTAGE);
             const long off = (long)ch * CH;
-            const int nstt = (int)(min((long)CH, kbytes - off) / 64);   // steps of one tile
+            const int nstt = (int)(min((long)CH, kbytes - off) / 64);   // 64-byte steps of one tile
             const int nst = nstt * tpi;
             const int s0 = nst * warp / 8, s1 = nst * (warp + 1) / 8;
             constexpr int MAXS = CH / 64 / 8 + 1;
@@ -337,57 +384,54 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
             const bool have = mbar_wait(&full[s], (uint32_t)((c / NSTAGE) & 1), &abort_sh,
                                         &g_apus_kernel_err, 2);
             const int e1 = have ? s1 : s0;
-            const uint8_t *wA = ring + s * STAGE_BYTES + g * RS + 16 * t4;
-            const uint8_t *wB = wA + 8 * RS;
+            const uint8_t *stage = ring + s * STAGE_BYTES;
 #pragma unroll
             for (int q = 0; q < MAXS; q++) {
                 const int st = s0 + q;
                 if (st >= e1) break;
-                const uint4 va = lds128(wA + st * 64), vb = lds128(wB + st * 64);
-                const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
-                const long ls = off / 64 + (st >= nstt ? st - nstt : st);   // step within the k-range
+                const int jt = st >= nstt ? 1 : 0, stt = st - jt * nstt;      // tile, step within it
+                const uint8_t *tile = stage + jt * tile_bytes;
+                const int ko = stt >> 1, u0 = (stt & 1) * 4;                 // slab, first 16-byte unit
+                const long ls = off / 64 + stt;                              // step within the k-range
                 if (FP8) {
-                    // x is staged as scaled f16 (XS is always on for FP8)
-                    uint32_t xw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    if (xrow_ok) {
-                        const uint16_t *xp = xs + g * xstride + ls * 64 + 16 * t4;
-                        const uint4 xa = lds128(xp), xb = lds128(xp + 8);
-                        xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
-                        xw[4] = xb.x; xw[5] = xb.y; xw[6] = xb.z; xw[7] = xb.w;
-                    }
-                    // E4M3 -> f16 is exact; the 128x128 block scale (one per
-                    // step: the tile's 16 rows share a block) multiplies the
-                    // step's partial, two MMA chains per step
+                    // 64 codes of each row in four 16-byte units; ldmatrix
+                    // gives lane (g, t) codes 4t..4t+3 of a unit for rows g
+                    // and g+8, which become the f16 A fragment (k order
+                    // 4t, 4t+1 | 4t+2, 4t+3 in both operands)
+                    uint32_t r[2][4];
+#pragma unroll
+                    for (int pp = 0; pp < 2; pp++)
+                        ldsm_x4(r[pp][0], r[pp][1], r[pp][2], r[pp][3], swz(tile, ko, lrow, u0 + 2 * pp + lunit));
                     float u[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
-                        const uint32_t a0 = cvt_e4m3x2_f16x2(wa[j] & 0xffffu), a2 = cvt_e4m3x2_f16x2(wa[j] >> 16);
-                        const uint32_t a1 = cvt_e4m3x2_f16x2(wb[j] & 0xffffu), a3 = cvt_e4m3x2_f16x2(wb[j] >> 16);
-                        mma_f16_16816(u[j & 1][0], u[j & 1][1], u[j & 1][2], u[j & 1][3], a0, a1, a2, a3,
-                                      xw[2 * j], xw[2 * j + 1]);
+                        const uint32_t ra = r[j >> 1][(j & 1) * 2], rb = r[j >> 1][(j & 1) * 2 + 1];
+                        uint32_t b0, b1;
+                        lds64(b0, b1, xs + xrow * xstride + ls * 64 + j * 16 + 4 * t4);
+                        mma_f16_16816(u[j & 1][0], u[j & 1][1], u[j & 1][2], u[j & 1][3],
+                                      cvt_e4m3x2_f16x2(ra & 0xffffu), cvt_e4m3x2_f16x2(rb & 0xffffu),
+                                      cvt_e4m3x2_f16x2(ra >> 16), cvt_e4m3x2_f16x2(rb >> 16), b0, b1);
                     }
                     const float sc = scA[q];
-                    if (st < nstt) {                            // tile 0 of the item
+                    if (jt == 0) {
 #pragma unroll
                         for (int e = 0; e < 4; e++) acc[0][e] = acc[0][e] + (u[0][e] + u[1][e]) * sc;
-                    } else {                                    // tile 1
+                    } else {
 #pragma unroll
                         for (int e = 0; e < 4; e++) acc[1][e] = acc[1][e] + (u[0][e] + u[1][e]) * sc;
                     }
                 } else {
-                    uint32_t xw[4] = {0, 0, 0, 0};
-                    if (xrow_ok) {
-                        uint4 xa;
-                        if (XS) xa = lds128(xs + g * xstride + ls * 32 + 8 * t4);
-                        else xa = ld_nc16(xsrc + (size_t)g * d.ldx + k0 + ls * 32 + 8 * t4);
-                        xw[0] = xa.x; xw[1] = xa.y; xw[2] = xa.z; xw[3] = xa.w;
-                    }
+                    // 32 values of each row in four 16-byte units: two
+                    // k16 MMAs in the standard fragment layout
+                    uint32_t xb[4];
+                    ldsm_x4(xb[0], xb[1], xb[2], xb[3], xs + xrow * xstride + ls * 32 + (lane >> 3) * 8);
 #pragma unroll
                     for (int j = 0; j < 2; j++) {
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4(a0, a1, a2, a3, swz(tile, ko, lrow, u0 + 2 * j + lunit));
                         const int qq = (q & 1) * 2 + j;
-                        mma_bf16_16816(acc[qq][0], acc[qq][1], acc[qq][2], acc[qq][3],
-                                       wa[2 * j], wb[2 * j], wa[2 * j + 1], wb[2 * j + 1],
-                                       xw[2 * j], xw[2 * j + 1]);
+                        mma_bf16_16816(acc[qq][0], acc[qq][1], acc[qq][2], acc[qq][3], a0, a1, a2, a3,
+                                       xb[2 * j], xb[2 * j + 1]);
                     }
                 }
             }
@@ -415,27 +459,47 @@ __global__ void __launch_bounds__(gemvcfg::THREADS, 2) k_gemv_tma(GemvDesc d) {
         }
         if (it.nks == 1) {
             if (tid < 128 * tpi)
-                gemv_store(d, yout, te >> 4, row0 + jt * TR + (te & 15), a, best_sh, (te & 15) == 0);
-        } else {
-            // publish this range's partial; the last range of the tile reduces
-            float *slot = d.part + ((size_t)t * it.nks + it.ks) * PART;
-            if (tid < 128) slot[tid] = a;
-            __threadfence();
-            named_bar_sync(1, 256);
-            if (tid == 0) ticket_sh = atomicAdd(d.ticket + t, 1);
-            named_bar_sync(1, 256);
-            if (ticket_sh == it.nks - 1) {
-                __threadfence();
-                if (tid < 128) {
-                    const float *base = d.part + (size_t)t * it.nks * PART;
-                    float r = __ldcg(base + tid);
-                    for (int q = 1; q < it.nks; q++) r = r + __ldcg(base + q * PART + tid);
-                    gemv_store(d, yout, tid >> 4, row0 + (tid & 15), r, best_sh, (tid & 15) == 0);
-                }
-                if (tid == 0) d.ticket[t] = 0;     // ready for the next launch
-            }
+                gemv_store(d, yout, te >> 4, row0 + jt * TR + (te & 15), a, best_sh, (te & 15) == 0, p);
+        } else if (tid < 128) {
+            // publish this range's partial; the tiles are reduced after the stream
+            d.part[((size_t)t * it.nks + it.ks) * PART + tid] = a;
         }
         named_bar_sync(1, 256);
+    }
+    if (it.nks > 1) {
+        // Split K: the last range of each tile to arrive (atomic ticket) sums
+        // the ranges in range order and runs the epilogue.  Done once after
+        // the whole stream, so the fence and ticket round trips of all this
+        // CTA's tiles overlap instead of stalling the ring after every tile;
+        // thread j takes the CTA's j-th tile (the barrier above ordered every
+        // slot store before the fences).
+        const int tid = threadIdx.x;
+        for (long b0 = it.first; b0 < it.end; b0 += 256 * it.step) {
+            const long i = b0 + tid * it.step;
+            unsigned char last = 0;
+            if (i < it.end) {
+                __threadfence();
+                if (atomicAdd(d.ticket + i, 1) == it.nks - 1) {
+                    __threadfence();
+                    last = 1;
+                    d.ticket[i] = 0;               // ready for the next launch
+                }
+            }
+            last_sh[tid] = last;
+            named_bar_sync(1, 256);
+            for (int j = 0; j < 256; j++) {
+                const long tj = b0 + j * it.step;
+                if (tj >= it.end) break;
+                if (!last_sh[j]) continue;
+                if (tid < 128) {
+                    const float *base = d.part + (size_t)tj * it.nks * PART;
+                    float r = __ldcg(base + tid);
+                    for (int q = 1; q < it.nks; q++) r = r + __ldcg(base + q * PART + tid);
+                    gemv_store(d, d.y, tid >> 4, tj * TR + (tid & 15), r, best_sh, (tid & 15) == 0, 0);
+                }
+            }
+            named_bar_sync(1, 256);
+        }
     }
     if (d.amax && threadIdx.x < d.R && best_sh[threadIdx.x])
         atomicMax(d.amax + threadIdx.x, best_sh[threadIdx.x]);
@@ -501,6 +565,15 @@ __global__ void k_gemv_generic(GemvDesc d) {
         for (int r = 1; r < 8; r++) if (lane == r) v = acc[r];
         if (yout) yout[(size_t)lane * d.ldy + o] = bf16_bits(v);
         if (d.yf && !d.gexpert) d.yf[(size_t)lane * d.ldyf + o] = v;
+        if (d.scat && d.gexpert) {
+            const int mm = lane + d.scat_r0;
+            const int j = d.scat_slot[p * 8 + mm];
+            if (j >= 0) {
+                const int half = (*d.scat_epoch + 1) & 1;
+                d.scat[(((size_t)half * 8 + mm) * d.scat_j + j) * d.scat_ld + o] =
+                    bf16_bits(bf16_round(bf16_round(v) * d.scat_w[mm * d.scat_k + j]));
+            }
+        }
         if (d.amax && !d.gexpert) atomicMax(d.amax + lane, argmax_key(bf16_round(v), (uint32_t)(o + d.row_base)));
     }
 }
@@ -543,8 +616,8 @@ void gemv_scratch_need(long O, long K, size_t *part_floats, size_t *tickets) {
 }
 
 bool gemv_fast_ok(const GemvDesc &d) {
-    const int kstep = d.fp8 ? 64 : 32;
-    if (d.K <= 0 || d.K % kstep) return false;
+    // rows must be whole 128-byte slabs for the tensor map
+    if (d.K <= 0 || ((d.fp8 ? 1 : 2) * d.K) % 128) return false;
     if (((uintptr_t)d.W & 15) || ((uintptr_t)d.x & 15)) return false;
     if ((d.ldx * 2) % 16) return false;
     return true;
@@ -552,17 +625,82 @@ bool gemv_fast_ok(const GemvDesc &d) {
 
 static int g_num_sms = 0;
 
-static size_t gemv_smem(bool xs) {
+static size_t gemv_smem() {
     using namespace gemvcfg;
-    return NSTAGE * STAGE_BYTES + (xs ? XMAX : 0) + 8 * 2 * PART * 4 + 2 * NSTAGE * 8;
+    return 1024 + NSTAGE * STAGE_BYTES + XMAX + 8 * 2 * PART * 4 + 2 * NSTAGE * 8;
 }
 
-template <bool FP8, bool XS>
+// Tensor map of the weights as (128 bytes of k, row, 128-byte k-slab,
+// weight block) with strides (row bytes, 128, block bytes): box {128 bytes,
+// 16 rows, box_ko slabs, 1} lands as [slab][row][128 B] with the 128-byte
+// swizzle.  Encoded maps are cached by their arguments.
+struct WmapKey {
+    const void *W;
+    long O, K, gnum, estride;
+    int fp8, box_ko;
+    bool operator==(const WmapKey &o) const {
+        return W == o.W && O == o.O && K == o.K && gnum == o.gnum && estride == o.estride && fp8 == o.fp8 &&
+               box_ko == o.box_ko;
+    }
+};
+struct WmapHash {
+    size_t operator()(const WmapKey &k) const {
+        size_t h = std::hash<const void *>()(k.W);
+        for (long v : {k.O, k.K, k.gnum, k.estride, (long)k.fp8, (long)k.box_ko}) h = h * 1000003u ^ (size_t)v;
+        return h;
+    }
+};
+static std::mutex g_wmap_mu;
+static std::unordered_map<WmapKey, CUtensorMap, WmapHash> g_wmaps;
+
+// The driver's encoder, looked up through the runtime so the library has no
+// link-time dependency on libcuda (it loads on hosts without a driver).
+static PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+static int wmap_get(const GemvDesc &d, CUtensorMap *out) {
+    const long rowbytes = d.fp8 ? d.K : 2 * d.K;
+    const long gnum = d.gexpert ? d.gnum : 1;
+    const long estride = d.gexpert ? d.w_estride : d.O * rowbytes;
+    const WmapKey key{d.W, d.O, d.K, gnum, estride, d.fp8, d.box_ko};
+    std::lock_guard<std::mutex> lk(g_wmap_mu);
+    auto f = g_wmaps.find(key);
+    if (f != g_wmaps.end()) { *out = f->second; return 0; }
+    if (gnum < 1 || (estride & 15) || rowbytes % 128) return -1;
+    const cuuint64_t dims[4] = {(cuuint64_t)(d.fp8 ? 128 : 64), (cuuint64_t)d.O, (cuuint64_t)(rowbytes / 128),
+                                (cuuint64_t)gnum};
+    const cuuint64_t strides[3] = {(cuuint64_t)rowbytes, 128, (cuuint64_t)estride};
+    const cuuint32_t box[4] = {(cuuint32_t)(d.fp8 ? 128 : 64), (cuuint32_t)gemvcfg::TR, (cuuint32_t)d.box_ko, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    CUtensorMap m;
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = encode_tiled();
+    if (!enc) return -1;
+    if (enc(&m, d.fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 4,
+                               const_cast<void *>(d.W), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return -1;
+    if (g_wmaps.size() > 4096) g_wmaps.clear();
+    g_wmaps.emplace(key, m);
+    *out = m;
+    return 0;
+}
+
+template <bool FP8>
 static int launch_tma(const GemvDesc &d, cudaStream_t st) {
     static bool attr = false;
-    const size_t sm = gemv_smem(XS);
+    const size_t sm = gemv_smem();
     if (!attr) {
-        if (cudaFuncSetAttribute(k_gemv_tma<FP8, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
+        if (cudaFuncSetAttribute(k_gemv_tma<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
             != cudaSuccess) return -1;
         attr = true;
     }
@@ -571,14 +709,16 @@ static int launch_tma(const GemvDesc &d, cudaStream_t st) {
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     }
+    CUtensorMap wmap;
+    if (wmap_get(d, &wmap)) return -1;
     const long ntile = ((d.O + gemvcfg::TR - 1) / gemvcfg::TR + d.tpi - 1) / d.tpi;   // work items
     long grid;
     if (d.gexpert) {
-        grid = 2L * g_num_sms;
+        grid = (long)gemvcfg::CTAS_PER_SM * g_num_sms;
         if (grid > (long)d.gmax * ntile) grid = (long)d.gmax * ntile;
     } else {
         const long nks = (d.K + d.kx - 1) / d.kx;
-        long per_ks = (2L * g_num_sms) / nks;                    // CTAs per k-range
+        long per_ks = ((long)gemvcfg::CTAS_PER_SM * g_num_sms) / nks;   // CTAs per k-range
         if (per_ks < 1) per_ks = 1;
         if (per_ks > ntile) per_ks = ntile;
         grid = per_ks * nks;
@@ -593,7 +733,7 @@ static int launch_tma(const GemvDesc &d, cudaStream_t st) {
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = d.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_gemv_tma<FP8, XS>, d) == cudaSuccess ? 0 : -1;
+    return cudaLaunchKernelEx(&cfg, k_gemv_tma<FP8>, wmap, d) == cudaSuccess ? 0 : -1;
 }
 
 int gemv_launch(const GemvDesc &dd, cudaStream_t st) {
@@ -602,27 +742,27 @@ int gemv_launch(const GemvDesc &dd, cudaStream_t st) {
     gemv_plan(d.plan_o > 0 ? d.plan_o : d.O, d.K, d.fp8 != 0, d.gexpert != nullptr, &d.kx, &d.tpi);
     if (gemv_fast_ok(d)) {
         const long klen = d.K < d.kx ? d.K : d.kx;
-        const bool xs = (long)d.R * (klen * 2 + 16) <= gemvcfg::XMAX;
+        const long kbytes = (d.fp8 ? 1 : 2) * klen;
+        d.box_ko = (int)((kbytes < gemvcfg::CH ? kbytes : gemvcfg::CH) / 128);
+        const bool xs = (long)d.R * (klen * 2 + 32) <= gemvcfg::XMAX;
         if (d.K > d.kx && (!d.part || !d.ticket)) return -1;
-        if (d.gexpert && (d.K > gemvcfg::KX || !d.gcount || d.gmax < 1)) return -1;
-        if (d.fp8 && !xs) {
-            // FP8 needs the activations staged (as scaled f16): run the rows in
+        if (d.gexpert && (d.K > gemvcfg::KX || !d.gcount || d.gmax < 1 || d.gnum < 1)) return -1;
+        if (!xs) {
+            // the activations are staged in shared memory: run the rows in
             // groups that fit; every row's arithmetic is the same either way
-            const int r1 = (int)(gemvcfg::XMAX / (klen * 2 + 16));
+            const int r1 = (int)(gemvcfg::XMAX / (klen * 2 + 32));
             if (r1 < 1) return -1;
-            GemvDesc a = d, b = d;
+            GemvDesc a = dd, b = dd;
             a.R = r1;
             b.R = d.R - r1;
             b.x = d.x + (size_t)r1 * d.ldx;
             if (d.y) b.y = d.y + (size_t)r1 * d.ldy;
             if (d.yf) b.yf = d.yf + (size_t)r1 * d.ldyf;
             if (d.amax) b.amax = d.amax + r1;
+            b.scat_r0 = d.scat_r0 + r1;
             return gemv_launch(a, st) || gemv_launch(b, st) ? -1 : 0;
         }
-        if (d.x_swiglu && !xs) return -1;
-        int rc;
-        if (d.fp8) rc = launch_tma<true, true>(d, st);
-        else rc = xs ? launch_tma<false, true>(d, st) : launch_tma<false, false>(d, st);
+        const int rc = d.fp8 ? launch_tma<true>(d, st) : launch_tma<false>(d, st);
         if (rc) return -1;
     } else {
         if (d.R > 8) return -1;

@@ -413,7 +413,7 @@ static ApusGcudaModel *model_create(const ApusGcudaConfig *cfg, int has_mtp, siz
         m->ep.peer[rank] = m->ep_region;
         m->ep.off_keys = (long)contrib;
         m->ep.off_flags = (long)(contrib + 2 * MOE_MAX_R * 8);
-        m->ep.epoch = (int *)A(sizeof(int));
+        m->ep.epoch = (int *)A(2 * sizeof(int));     // epoch, CTA arrivals
     }
     m->log_cap = m->cap + 2 * MAXR;
     m->log = (int32_t *)A((size_t)m->log_cap * 4);
@@ -437,6 +437,7 @@ static ApusGcudaModel *model_create(const ApusGcudaConfig *cfg, int has_mtp, siz
         ms.row_sel = (int32_t *)A((size_t)R * MOE_MAX_TOPK * 4);
         ms.row_prob = (int32_t *)A((size_t)R * MOE_MAX_TOPK * 4);
         ms.row_prob_shared = (int32_t *)A((size_t)R * 4);
+        ms.prob_slot = world > 1 ? (int32_t *)A(P * 8 * 4) : nullptr;
         ms.prob_expert = (int32_t *)A(P * 4);
         ms.prob_count = (int32_t *)A(4);
         ms.gu = (uint16_t *)A(P * R * 2 * (size_t)maxi * 2);
@@ -827,7 +828,7 @@ static int lm_head(ApusGcudaModel *m, const uint16_t *yn, int R, int *picks, boo
     if (gemv_launch(g, m->st)) return -1;
     if (m->ep_world > 1) {
         // the largest key over every rank's slice: publish, barrier, reduce
-        if (ep_barrier_launch(m->ep, m->S.amax, R, m->st) || ep_picks_launch(m->ep, R, picks, m->st)) return -1;
+        if (ep_picks_exchange_launch(m->ep, m->S.amax, R, picks, m->st)) return -1;
         return 0;
     }
     k_extract_picks<<<1, 32, 0, m->st>>>(m->S.amax, R, picks);

@@ -685,6 +685,70 @@ def cpu_c2(W, budget_s=20.0, prompt_len=64, log=None):
                       f"(the bench prompt's first {prompt_len} ids; setup {t_load:.0f} s untimed)"}
 
 
+def gemv_table(only="all", rows=(4, 1), reps=50):
+    """Per-shape GEMV timings of the config-2 step's matrices (profiling aid,
+    --gemv-table): back-to-back PDL launches over rotating weight copies
+    (>= 512 MB per shape, so every launch streams from HBM), CUDA events on
+    the launching stream.  Prints one JSON line per (matrix, rows)."""
+    import numpy as np
+    import torch
+    import apus_gcuda as G
+    G.enable()
+    G.apus_gcuda_set_pdl(1)
+    kw = c2_config()
+    d, V, qkv = kw["hidden_size"], kw["vocab_size"], kw["linear_num_heads"] * kw["linear_head_dim"]
+    D, H = kw["linear_head_dim"], kw["linear_num_heads"]
+    AH, qd, vd, ql, kl = (kw["num_attention_heads"], kw["qk_nope_head_dim"], kw["v_head_dim"], kw["q_lora_rank"],
+                          kw["kv_lora_rank"])
+    IH, ID, E = kw["index_n_heads"], kw["index_head_dim"], kw["n_routed_experts"]
+    shapes = [("lm_head", V, d, "bf16"), ("kda_proj", 3 * qkv + 2 * D + H, d, "bf16"), ("kda_o", d, qkv, "bf16"),
+              ("eh_proj", d, 2 * d, "bf16"), ("router", E, d, "f32"), ("dsa_qa_kva", ql + kl, d, "fp8"),
+              ("dsa_qb", AH * qd, ql, "fp8"), ("dsa_kvb", AH * (qd + vd), kl, "bf16"),
+              ("idx_wqb", IH * ID, ql, "bf16"), ("idx_kgw", 2 * ID + IH, d, "bf16"), ("dsa_o", d, AH * vd, "fp8")]
+    st = torch.cuda.Stream()
+    sp = G.C.c_void_p(st.cuda_stream)
+    hbm, _, _ = peaks()
+    for name, O_, K_, kind in shapes:
+        if only not in ("all", name):
+            continue
+        wb = O_ * K_ * (1 if kind == "fp8" else 2)
+        nbuf = max(1, -(-(512 << 20) // wb))
+        if kind == "fp8":
+            Ws = [torch.randint(0, 120, (O_, K_), dtype=torch.uint8, device="cuda") for _ in range(nbuf)]
+            S = torch.full(((O_ + 127) // 128, (K_ + 127) // 128), 1e-3, device="cuda")
+        else:
+            Ws = [torch.randn(O_, K_, device="cuda").to(torch.bfloat16) * 0.02 for _ in range(nbuf)]
+        for R in rows:
+            x = torch.randn(R, K_, device="cuda").to(torch.bfloat16)
+            y = torch.empty(R, O_, device="cuda", dtype=torch.float32 if kind == "f32" else torch.bfloat16)
+
+            def call(i):
+                w = Ws[i % nbuf]
+                if kind == "fp8":
+                    rc = G.apus_gcuda_fp8blk_linear_dev(G.ptr(w), G.ptr(S), G.ptr(x), G.ptr(y), R, O_, K_, sp)
+                elif kind == "f32":
+                    rc = G.apus_gcuda_bf16_gemm_f32_dev(G.ptr(w), G.ptr(x), G.ptr(y), R, O_, K_, sp)
+                else:
+                    rc = G.apus_gcuda_bf16_gemm_dev(G.ptr(w), G.ptr(x), G.ptr(y), R, O_, K_, sp)
+                G.check(rc, name)
+            for i in range(5):
+                call(i)
+            st.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for i in range(reps):
+                call(i)
+            e1.record(st)
+            st.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            algo = wb + (S.numel() * 4 if kind == "fp8" else 0)
+            print(json.dumps({"matrix": name, "O": O_, "K": K_, "weights": kind, "rows": R,
+                              "us": round(us, 2), "GB/s": round(algo / us / 1e3, 1),
+                              "frac": round(algo / us / 1e3 / hbm, 3)}), flush=True)
+        del Ws
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -699,6 +763,9 @@ def main():
     ap.add_argument("--mode", default="ep", choices=["ep", "replicas"],
                     help="config 2 with several GPUs: one sequence expert-parallel over all of them (ep), "
                          "or one independent sequence per GPU (replicas)")
+    ap.add_argument("--gemv-table", nargs="?", const="all", default=None,
+                    help="per-matrix GEMV timings of the config-2 step (profiling aid, one GPU); "
+                         "optionally one matrix name")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed kernels only (no e2e, no CPU baseline): the profiling command")
     args = ap.parse_args()
@@ -734,6 +801,9 @@ def main():
         print(json.dumps(line), flush=True)
         return
     ws, rank, local = dist_init()
+    if args.gemv_table:
+        gemv_table(args.gemv_table)
+        return
     if args.config == 2:
         out, W = bench_c2(args, ws, rank)
         if rank == 0 and not args.quick and ws == 1:
