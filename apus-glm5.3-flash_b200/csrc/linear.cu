@@ -195,12 +195,15 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
     __shared__ unsigned char last_sh[256];   // split K: tiles this CTA reduces
     __shared__ int xexp_sh[8];       // FP8: max BF16 exponent field of each staged row
     __shared__ float xinv_sh[8];     // FP8: 2^-k, the inverse of the row's staging scale
+    __shared__ float scl_sh[NSTAGE][32];   // FP8: block scales of each stage's slabs, [tile][slab]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile_bytes = TR * d.box_ko * 128;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 8); }
+        // FP8 stages complete on two arrivals: the copy's expect-tx and the
+        // producer's block-scale stores
+        for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], FP8 ? 2 : 1); mbar_init(&empty[s], 8); }
         fence_barrier_init();
         abort_sh = 0;
     }
@@ -209,11 +212,14 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
     // The next kernel in the stream may start its own weight stream now.
     pdl_launch_dependents();
 
-    if (warp == 8) {            // ---------------- producer (one lane)
-        // Weights never depend on the previous kernel, so the stream starts
-        // before the dependency wait unless the caller says otherwise.
-        if (lane != 0) return;
-        asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
+    if (warp == 8) {            // ---------------- producer
+        // Lane 0 streams the weights; for FP8 the lanes also fetch each
+        // stage's block scales into shared memory, so the consumers never
+        // wait on a global load.  Weights never depend on the previous
+        // kernel, so the stream starts before the dependency wait unless the
+        // caller says otherwise.
+        if (!FP8 && lane != 0) return;
+        if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
         if (d.weights_after_wait || d.gexpert) pdl_wait();
         GemvItems it;
         it.init(d, d.gexpert ? min(*d.gcount, d.gmax) : 1);
@@ -228,15 +234,34 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
             it.at(i, p, t);
             const int e = it.grouped ? d.gexpert[p] : 0;
             const int row0 = (int)(t * TR * tpi);
+            const float *WS = FP8 ? d.WS + (size_t)e * d.s_estride + (size_t)(row0 >> 7) * d.nkb : nullptr;
             for (int ch = 0; ch < nch; ch++, c++) {
                 const int s = (int)(c % NSTAGE);
                 const long rnd = c / NSTAGE;
-                if (rnd > 0 && !mbar_wait(&empty[s], (uint32_t)((rnd - 1) & 1), &abort_sh, &g_apus_kernel_err, 1))
+                bool ok = true;
+                if (lane == 0) {
+                    if (rnd > 0 && !mbar_wait(&empty[s], (uint32_t)((rnd - 1) & 1), &abort_sh, &g_apus_kernel_err, 1))
+                        ok = false;
+                    else {
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)(tile_bytes * tpi));
+                        const int ko = (int)((kb0 + (long)ch * CH) / 128);
+                        for (int j = 0; j < tpi; j++)
+                            tma_load_3d(ring + s * STAGE_BYTES + j * tile_bytes, &wmap, 0, row0 + j * TR, ko, e,
+                                        &full[s]);
+                    }
+                }
+                if (FP8) {
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) return;
+                    // lane l: slab l%16 of tile l/16 (both tiles lie in one 128-row block)
+                    const long kbk = (kb0 + (long)ch * CH) / 128 + (lane & 15);
+                    const long nsl = (min((long)CH, kbytes - (long)ch * CH) + 127) / 128;
+                    if ((lane & 15) < nsl && (lane >> 4) < tpi) scl_sh[s][lane] = __ldg(WS + kbk);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full[s]);
+                } else if (!ok) {
                     return;
-                mbar_arrive_expect_tx(&full[s], (uint32_t)(tile_bytes * tpi));
-                const int ko = (int)((kb0 + (long)ch * CH) / 128);
-                for (int j = 0; j < tpi; j++)
-                    tma_load_3d(ring + s * STAGE_BYTES + j * tile_bytes, &wmap, 0, row0 + j * TR, ko, e, &full[s]);
+                }
             }
         }
         return;
@@ -267,8 +292,6 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
         it.at(i, p, t);
         const uint16_t *xsrc = d.x + (size_t)p * d.x_pstride;
         uint16_t *yout = d.y ? d.y + (size_t)p * d.y_pstride : nullptr;
-        const float *WS = d.WS;
-        if (FP8 && it.grouped) WS += (size_t)d.gexpert[p] * d.s_estride;
         if (xsrc != xsrc_staged) {           // stage x[:, k0:k0+klen]: row r at xs + r*xstride
             named_bar_sync(1, 256);          // previous item's readers are done
             if (FP8) {
@@ -359,9 +382,6 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
             xsrc_staged = xsrc;
         }
         const long row0 = t * TR * tpi;
-        const float *srA = nullptr;
-        if (FP8)     // the tile's 16 rows lie in one 128-row scale block
-            srA = WS + (size_t)(row0 >> 7) * d.nkb;
         float acc[4][4];
 #pragma unroll
         for (int q = 0; q < 4; q++) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
@@ -372,15 +392,6 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
             const int nst = nstt * tpi;
             const int s0 = nst * warp / 8, s1 = nst * (warp + 1) / 8;
             constexpr int MAXS = CH / 64 / 8 + 1;
-            float scA[MAXS];
-            if (FP8) {   // scales first: their latency hides under the barrier wait
-#pragma unroll
-                for (int q = 0; q < MAXS; q++) {
-                    const int sq = s0 + q;                  // step within its tile (tpi <= 2)
-                    const long kbk = (kb0 + off) / 128 + ((sq >= nstt ? sq - nstt : sq) >> 1);
-                    scA[q] = (s0 + q < s1) ? __ldg(srA + kbk) : 0.f;
-                }
-            }
             const bool have = mbar_wait(&full[s], (uint32_t)((c / NSTAGE) & 1), &abort_sh,
                                         &g_apus_kernel_err, 2);
             const int e1 = have ? s1 : s0;
@@ -412,7 +423,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
                                       cvt_e4m3x2_f16x2(ra & 0xffffu), cvt_e4m3x2_f16x2(rb & 0xffffu),
                                       cvt_e4m3x2_f16x2(ra >> 16), cvt_e4m3x2_f16x2(rb >> 16), b0, b1);
                     }
-                    const float sc = scA[q];
+                    const float sc = scl_sh[s][jt * 16 + (stt >> 1)];
                     if (jt == 0) {
 #pragma unroll
                         for (int e = 0; e < 4; e++) acc[0][e] = acc[0][e] + (u[0][e] + u[1][e]) * sc;
