@@ -32,6 +32,7 @@ apus_gcuda_enable = _fn("apus_gcuda_enable", _i, C.c_char_p, _sz)
 apus_gcuda_disable = _fn("apus_gcuda_disable", None)
 apus_gcuda_is_enabled = _fn("apus_gcuda_is_enabled", _i)
 apus_gcuda_last_error = _fn("apus_gcuda_last_error", C.c_char_p)
+apus_gcuda_clear_error = _fn("apus_gcuda_clear_error", None)
 apus_gcuda_kernel_error = _fn("apus_gcuda_kernel_error", _i)
 apus_gcuda_register_region = _fn("apus_gcuda_register_region", _i, _vp, _sz)
 apus_gcuda_unregister_region = _fn("apus_gcuda_unregister_region", None, _vp)

@@ -186,6 +186,7 @@ void apus_gcuda_disable(void) {
 int apus_gcuda_is_enabled(void) { return g_enabled ? 1 : 0; }
 
 const char *apus_gcuda_last_error(void) { return g_err; }
+void apus_gcuda_clear_error(void) { g_err[0] = 0; }
 
 int apus_gcuda_kernel_error(void) {
     cudaDeviceSynchronize();

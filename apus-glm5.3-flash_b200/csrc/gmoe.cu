@@ -371,7 +371,9 @@ int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint
         dn.scat_ld = m.dim;
     }
     if (gemv_launch(dn, st)) return -1;
-    // 5. ordered combine (across ranks when the experts are split)
+    // 5. ordered combine (across ranks when the experts are split); with
+    // out == null the caller combines (one GPU only)
+    if (!out) return (ep || cudaGetLastError() != cudaSuccess) ? -1 : 0;
     if (m.dim % 8 || ((uintptr_t)out & 15) || (ldo % 8)) return -1;
     const long n = (long)R * (m.dim / 8);
     if (ep) {
@@ -383,6 +385,13 @@ int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint
 }
 
 // Every rank's region must be mapped before any exchange is launched.
+int moe_combine_launch(const MoeDev &m, int R, uint16_t *out, long ldo, cudaStream_t st) {
+    if (m.dim % 8 || ((uintptr_t)out & 15) || (ldo % 8) || R < 1 || R > m.max_r) return -1;
+    const long n = (long)R * (m.dim / 8);
+    k_moe_combine<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(m, R, out, ldo);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 static bool ep_connected(const EpCtx &ep) {
     if (ep.world < 2 || ep.world > EP_MAX_RANKS || ep.rank < 0 || ep.rank >= ep.world || !ep.epoch) return false;
     for (int p = 0; p < ep.world; p++)

@@ -58,6 +58,10 @@ struct MoeDev {
 // teacher-forcing hook, c/gmoe.h:145-152).
 int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
                        const int32_t *forced, cudaStream_t st);
+// The ordered combine alone (what moe_forward_launch with out == null leaves
+// to the caller): out[r] = bf16 sum of the row's weighted expert outputs in
+// ascending expert order, shared expert last.
+int moe_combine_launch(const MoeDev &m, int R, uint16_t *out, long ldo, cudaStream_t st);
 
 // Greedy picks over a vocabulary split across the expert-parallel group: one
 // exchange publishes keys[0..R) (this rank's argmax keys), signals every

@@ -282,85 +282,176 @@ APUS_DEV void hc_maps(const float *m, const float *scale, const float *base, int
     }
 }
 
-// mHC pre-mix (c/gmhc.h:187-276, then the layer RMSNorm c/gdsa.h:258-274),
-// in three launches so the 24-row mix matrix is read by many SMs at once:
-//   k_hc_rms  one CTA per row: inverse RMS of the flattened hc*d streams;
-//   k_hc_mix  CTA (j, chunk): partial mixes of row-chunk `chunk` of fn[j] for
-//             every row of the call (fn read once), fixed-order reductions;
-//   k_hc_pre  one CTA per row: mixes = ascending sum of the partials, gates +
-//             Sinkhorn, the collapse bf16(sum_j pre_j h_j) and the RMSNorm.
-#define HC_MIX_THREADS 128
-#define HC_MIX_CHUNK (8 * HC_MIX_THREADS)
-__global__ void __launch_bounds__(512) k_hc_rms(const uint16_t *h4, int n, float eps, float *rms) {
+// mHC (c/gmhc.h:187-294) in two launches per sublayer boundary:
+//   k_hc_postmix  CTA per 64-column chunk, all rows: the expand of the
+//                 sublayer just finished (its output combined on the fly when
+//                 it is the MoE), then the next site's pre-mix partials over
+//                 the chunk: sum_i fn[m][i] h[i] and sum_i h[i]^2, in a fixed
+//                 order (lane-sequential, then a fixed warp tree);
+//   k_hc_pre      CTAs 0..R-1: mixes = inverse RMS * (chunk-ordered sums),
+//                 pre gates, the collapse bf16(sum_j pre_j h_j) and the layer
+//                 RMSNorm; CTAs R..2R-1: the same mixes, then post gates and
+//                 the Sinkhorn comb (needed only by the next expand), so the
+//                 Sinkhorn runs beside the collapse instead of before it.
+// The inverse RMS multiplies the summed dot products (the reference scales
+// the streams first, c/gmhc.h:241-251): equal up to fp32 rounding.
+#define HC_PM_CW 64
+__global__ void __launch_bounds__(256) k_hc_postmix(HcPostMix a) {
     pdl_launch_dependents();
-    extern __shared__ float sq[];
-    __shared__ float leaf[256], res;
-    load_row_f32(h4 + (size_t)blockIdx.x * n, n, sq);
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) sq[i] = sq[i] * sq[i];
-    __syncthreads();
-    const float var = block_pw(sq, n, leaf, &res) / (float)n;
-    if (threadIdx.x == 0) rms[blockIdx.x] = 1.0f / sqrtf(var + eps);
-}
-
-// part[r][j][chunk] = sum over the chunk of fn[j][i] * (x[r][i] * inv[r]):
-// thread sums its 8 elements in order, then a fixed warp tree and a fixed
-// order over the 4 warps.
-__global__ void __launch_bounds__(HC_MIX_THREADS) k_hc_mix(const uint16_t *fn, const uint16_t *h4, const float *rms,
-                                                         int n, int nmix, int nchunk, int R, float *part) {
-    pdl_launch_dependents();
-    const int j = blockIdx.x, ch = blockIdx.y;
-    const int i0 = ch * HC_MIX_CHUNK + threadIdx.x * 8;
-    const bool in = i0 < n;
-    const uint4 wv = in ? __ldg((const uint4 *)(fn + (size_t)j * n + i0)) : make_uint4(0, 0, 0, 0);
-    uint4 xv[MAXR];
+    __shared__ float xs[MAXR][HC_PM_CW];
+    __shared__ float hs[MAXR][8][HC_PM_CW];
+    const int c = blockIdx.x, i0 = c * HC_PM_CW, d = a.d, hc = a.hc, R = a.R;
+    const int cw = min(HC_PM_CW, d - i0);
+    const bool expand = a.h4out != nullptr;
+    if (expand) {
+        for (int q = threadIdx.x; q < R * HC_PM_CW; q += blockDim.x) {
+            const int r = q / HC_PM_CW, ii = q % HC_PM_CW;
+            if (ii >= cw) continue;
+            const int i = i0 + ii;
+            float v;
+            if (a.x) {
+                v = bf16_f32(a.x[(size_t)r * d + i]);
+            } else {   // MoE output (c/gmoe.h:226-236): ascending experts, shared expert last
+                const MoeDev &m = a.moe;
+                const int K = m.topk;
+                const size_t ps = (size_t)m.max_r * d, off = (size_t)r * d + i;
+                // every load issued before the ordered sum uses any of them
+                int pj[MOE_MAX_TOPK];
+                float wj[MOE_MAX_TOPK];
 #pragma unroll
-    for (int r = 0; r < MAXR; r++)
-        xv[r] = (in && r < R) ? *(const uint4 *)(h4 + (size_t)r * n + i0) : make_uint4(0, 0, 0, 0);
-    __shared__ float red[MAXR][HC_MIX_THREADS / 32];
-    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+                for (int j = 0; j < MOE_MAX_TOPK; j++)
+                    if (j < K) { pj[j] = m.row_prob[r * K + j]; wj[j] = m.row_weight[r * K + j]; }
+                uint16_t ev[MOE_MAX_TOPK];
 #pragma unroll
-    for (int r = 0; r < MAXR; r++) {
-        if (r >= R) break;
-        const float inv = rms[r];
-        const uint32_t xx[4] = {xv[r].x, xv[r].y, xv[r].z, xv[r].w};
-        float acc = 0.f;
+                for (int j = 0; j < MOE_MAX_TOPK; j++)
+                    if (j < K) ev[j] = m.yd[(size_t)pj[j] * ps + off];
+                const uint16_t shv = m.yd[(size_t)m.row_prob_shared[r] * ps + off];
+                float y = 0.f;
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            acc += bf16lo(ww[e]) * (bf16lo(xx[e]) * inv);
-            acc += bf16hi(ww[e]) * (bf16hi(xx[e]) * inv);
+                for (int j = 0; j < MOE_MAX_TOPK; j++)
+                    if (j < K) y = bf16_round(y + bf16_round(bf16_f32(ev[j]) * wj[j]));
+                v = K ? bf16_round(y + bf16_f32(shv)) : bf16_f32(shv);
+            }
+            xs[r][ii] = v;
+        }
+        __syncthreads();
+    }
+    // expand (c/gmhc.h:278-294): y[j][i] = bf16(bf16(bf16(post[j]) x[i]) +
+    // bf16(sum_k bf16(comb[k][j]) h[k][i])), or the input streams as they
+    // are; four elements per thread with all their loads issued first
+    const int tot = R * hc * HC_PM_CW;
+    for (int q0 = threadIdx.x; q0 < tot; q0 += 4 * blockDim.x) {
+        uint16_t hk[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int q = q0 + u * blockDim.x;
+            const int r = q / (hc * HC_PM_CW), j = (q / HC_PM_CW) % hc, ii = q % HC_PM_CW;
+            if (q >= tot || ii >= cw) continue;
+            const uint16_t *hr = a.h4 + (size_t)r * hc * d + i0 + ii;
+            if (expand) {
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (k < hc) hk[u][k] = hr[(size_t)k * d];
+            } else {
+                hk[u][0] = hr[(size_t)j * d];
+            }
         }
 #pragma unroll
-        for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-        if ((threadIdx.x & 31) == 0) red[r][threadIdx.x >> 5] = acc;
+        for (int u = 0; u < 4; u++) {
+            const int q = q0 + u * blockDim.x;
+            const int r = q / (hc * HC_PM_CW), j = (q / HC_PM_CW) % hc, ii = q % HC_PM_CW;
+            if (q >= tot || ii >= cw) continue;
+            float o;
+            if (expand) {
+                const float pb = bf16_round(a.post[r * hc + j]);
+                const float t1 = bf16_round(pb * xs[r][ii]);
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (k < hc) acc += bf16_round(a.comb[(r * hc + k) * hc + j]) * bf16_f32(hk[u][k]);
+                const uint16_t ob = bf16_bits(t1 + bf16_round(acc));
+                a.h4out[((size_t)r * hc + j) * d + i0 + ii] = ob;
+                o = bf16_f32(ob);
+            } else {
+                o = bf16_f32(hk[u][0]);
+            }
+            hs[r][j][ii] = o;
+        }
     }
+    if (!a.fn) return;
     __syncthreads();
-    if (threadIdx.x < R) {
-        const int r = threadIdx.x;
-        float v = red[r][0];
-        for (int w = 1; w < HC_MIX_THREADS / 32; w++) v += red[r][w];
-        part[((size_t)r * nmix + j) * nchunk + ch] = v;
+    // partials: warp w takes m = w, w+8, w+16, w+24 (m == nmix: the sum of
+    // squares; nmix <= 31); lane l covers elements 8l.. of every 256-element
+    // group of the chunk, its weight loads issued first
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, E = hc * cw;
+    float accr[4][MAXR];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+        for (int r = 0; r < MAXR; r++) accr[u][r] = 0.f;
+    for (int e0 = lane * 8; e0 < E; e0 += 256) {
+        const int j = e0 / cw, ii = e0 % cw;
+        uint4 fv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int m = warp + 8 * u;
+            if (m < a.nmix) fv[u] = __ldg((const uint4 *)(a.fn + (size_t)m * hc * d + (size_t)j * d + i0 + ii));
+        }
+        float hv[MAXR][8];
+#pragma unroll
+        for (int r = 0; r < MAXR; r++)
+#pragma unroll
+            for (int e = 0; e < 8; e++) hv[r][e] = r < R ? hs[r][j][ii + e] : 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int m = warp + 8 * u;
+            if (m > a.nmix) break;
+            const uint32_t fw[4] = {fv[u].x, fv[u].y, fv[u].z, fv[u].w};
+#pragma unroll
+            for (int r = 0; r < MAXR; r++) {
+                if (r >= R) break;
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const float f = m < a.nmix ? ((e & 1) ? bf16hi(fw[e >> 1]) : bf16lo(fw[e >> 1])) : hv[r][e];
+                    accr[u][r] += f * hv[r][e];
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int m = warp + 8 * u;
+        if (m > a.nmix) break;
+#pragma unroll
+        for (int r = 0; r < MAXR; r++) {
+            if (r >= R) break;
+            float v = accr[u][r];
+#pragma unroll
+            for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0) a.part[((size_t)r * a.nchunk + c) * (a.nmix + 1) + m] = v;
+        }
     }
 }
 
 __global__ void __launch_bounds__(512) k_hc_pre(const uint16_t *h4, const float *part, int nchunk,
                                                 const float *scale, const float *base, const uint16_t *norm_w, int d,
-                                                int hc, int iters, float hc_eps, float eps, float *post_out,
+                                                int hc, int iters, float hc_eps, float eps, int R, float *post_out,
                                                 float *comb_out, uint16_t *x_out) {
     pdl_launch_dependents();
     extern __shared__ float ys[];                     // [d] collapsed row + [d] squares
     float *sq = ys + d;
-    __shared__ float mixs[80], pre[8], post[8], comb[64], leaf[256], res;
-    const int r = blockIdx.x, nmix = (2 + hc) * hc;
+    __shared__ float mixs[81], pre[8], post[8], comb[64], leaf[256], res;
+    const bool maps = (int)blockIdx.x >= R;
+    const int r = maps ? blockIdx.x - R : blockIdx.x, nmix = (2 + hc) * hc;
     const uint16_t *x = h4 + (size_t)r * hc * d;
-    if ((int)threadIdx.x < nmix) {
-        // ascending sum of the chunk partials, loads issued 16 at a time
-        const float *pp = part + ((size_t)r * nmix + threadIdx.x) * nchunk;
+    if ((int)threadIdx.x <= nmix) {
+        // chunk-ordered sums of the partials, loads issued 16 at a time
+        const float *pp = part + (size_t)r * nchunk * (nmix + 1) + threadIdx.x;
         float v = 0.f;
         for (int c0 = 0; c0 < nchunk; c0 += 16) {
             float t[16];
 #pragma unroll
-            for (int u = 0; u < 16; u++) t[u] = c0 + u < nchunk ? pp[c0 + u] : 0.f;
+            for (int u = 0; u < 16; u++) t[u] = c0 + u < nchunk ? pp[(size_t)(c0 + u) * (nmix + 1)] : 0.f;
 #pragma unroll
             for (int u = 0; u < 16; u++)
                 if (c0 + u < nchunk) v = (c0 + u == 0) ? t[u] : v + t[u];
@@ -368,7 +459,17 @@ __global__ void __launch_bounds__(512) k_hc_pre(const uint16_t *h4, const float 
         mixs[threadIdx.x] = v;
     }
     __syncthreads();
-    hc_maps(mixs, scale, base, hc, iters, hc_eps, r, pre, post, comb, post_out, comb_out);
+    if ((int)threadIdx.x < nmix) {
+        const float inv = 1.0f / sqrtf(mixs[nmix] / (float)(hc * d) + eps);
+        mixs[threadIdx.x] *= inv;
+    }
+    __syncthreads();
+    if (maps) {     // post gates + Sinkhorn comb for the next expand
+        hc_maps(mixs, scale, base, hc, iters, hc_eps, r, pre, post, comb, post_out, comb_out);
+        return;
+    }
+    if ((int)threadIdx.x < hc)
+        pre[threadIdx.x] = sigmoid_np(mixs[threadIdx.x] * scale[0] + base[threadIdx.x]) + hc_eps;
     __syncthreads();
     // collapse (c/gmhc.h:267-276): 8 consecutive columns per thread, the hc
     // stream loads issued together
@@ -392,23 +493,6 @@ __global__ void __launch_bounds__(512) k_hc_pre(const uint16_t *h4, const float 
     }
     __syncthreads();
     rmsnorm_row_smem(ys, sq, d, norm_w, eps, x_out + (size_t)r * d, leaf, &res);
-}
-
-// expand (c/gmhc.h:278-294): y[j][i] = bf16(bf16(bf16(post[j]) x[i]) +
-// bf16(sum_k bf16(comb[k][j]) res[k][i]))
-__global__ void k_hc_post(const uint16_t *x, const uint16_t *h4, const float *post, const float *comb,
-                          int d, int hc, uint16_t *out) {
-    pdl_launch_dependents();
-    const int r = blockIdx.y;
-    for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < hc * d; q += gridDim.x * blockDim.x) {
-        const int j = q / d, i = q % d;
-        const float pb = bf16_round(post[r * hc + j]);
-        const float t1 = bf16_round(pb * bf16_f32(x[(size_t)r * d + i]));
-        float acc = 0.f;
-        for (int k = 0; k < hc; k++)
-            acc += bf16_round(comb[r * hc * hc + k * hc + j]) * bf16_f32(h4[((size_t)r * hc + k) * d + i]);
-        out[((size_t)r * hc + j) * d + i] = bf16_bits(t1 + bf16_round(acc));
-    }
 }
 
 // HyperHead mean (c/gmhc.h:296-304) + final RMSNorm
@@ -987,9 +1071,9 @@ int layers_prepare(const Dims &D) {
     const int maxrow = D.d > D.ql ? (D.d > D.kl ? D.d : D.kl) : (D.ql > D.kl ? D.ql : D.kl);
     const size_t need_rms = (size_t)D.hc * D.d * 4, need_row = (size_t)2 * maxrow * 4;
     if (need_rms > 200 * 1024 || need_row > 200 * 1024) return -1;
-    if (D.d % 8 || D.hc > 8 || (2 + D.hc) * D.hc > 80 || (size_t)D.hc * D.d * 4 > 200 * 1024) return -1;
-    if (cudaFuncSetAttribute(k_hc_rms, cudaFuncAttributeMaxDynamicSharedMemorySize, D.hc * D.d * 4) ||
-        cudaFuncSetAttribute(k_hc_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
+    // k_hc_postmix: one warp slot per mix and the sum of squares (<= 32)
+    if (D.d % 8 || D.hc > 8 || (2 + D.hc) * D.hc + 1 > 32 || (size_t)D.hc * D.d * 4 > 200 * 1024) return -1;
+    if (cudaFuncSetAttribute(k_hc_pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
         cudaFuncSetAttribute(k_head_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
         cudaFuncSetAttribute(k_rmsnorm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row) ||
         cudaFuncSetAttribute(k_norm_seg, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need_row))
@@ -1002,20 +1086,26 @@ int k_embed_launch(const uint16_t *embed, const int32_t *ids, int R, int d, int 
     return ok_launch();
 }
 
+int hc_nchunk(const Dims &D) { return (D.d + HC_PM_CW - 1) / HC_PM_CW; }
+
 int hc_pre_launch(const Dims &D, const LayerW &W, int site, const uint16_t *h4, int R, Scratch &S,
                   cudaStream_t st) {
-    const int n = D.hc * D.d, nmix = (2 + D.hc) * D.hc, nchunk = (n + HC_MIX_CHUNK - 1) / HC_MIX_CHUNK;
-    k_hc_rms<<<R, 512, (size_t)n * 4, st>>>(h4, n, D.eps, S.rms);
-    k_hc_mix<<<dim3(nmix, nchunk), HC_MIX_THREADS, 0, st>>>(W.hc_fn[site], h4, S.rms, n, nmix, nchunk, R, S.mix);
-    k_hc_pre<<<R, 512, (size_t)2 * D.d * 4, st>>>(h4, S.mix, nchunk, W.hc_scale[site], W.hc_base[site],
-                                                  site ? W.post_norm : W.input_norm, D.d, D.hc, D.sinkhorn_iters,
-                                                  D.hc_eps, D.eps, S.post, S.comb, S.x);
+    k_hc_pre<<<2 * R, 512, (size_t)2 * D.d * 4, st>>>(h4, S.mix, hc_nchunk(D), W.hc_scale[site], W.hc_base[site],
+                                                      site ? W.post_norm : W.input_norm, D.d, D.hc,
+                                                      D.sinkhorn_iters, D.hc_eps, D.eps, R, S.post, S.comb, S.x);
     return ok_launch();
 }
 
-int hc_post_launch(const Dims &D, const uint16_t *x, const uint16_t *h4, int R, const Scratch &S, uint16_t *h4out,
-                   cudaStream_t st) {
-    k_hc_post<<<dim3((D.hc * D.d + 255) / 256, R), 256, 0, st>>>(x, h4, S.post, S.comb, D.d, D.hc, h4out);
+int hc_postmix_launch(const Dims &D, const uint16_t *x, const MoeDev *moe, const uint16_t *h4, int R, Scratch &S,
+                      uint16_t *h4out, const uint16_t *fn_next, cudaStream_t st) {
+    if (R < 1 || R > MAXR || (h4out && !x && !moe)) return -1;
+    HcPostMix a{};
+    a.x = x;
+    if (moe) a.moe = *moe;
+    a.h4 = h4; a.post = S.post; a.comb = S.comb; a.h4out = h4out;
+    a.fn = fn_next; a.part = S.mix;
+    a.d = D.d; a.hc = D.hc; a.nmix = (2 + D.hc) * D.hc; a.R = R; a.nchunk = hc_nchunk(D);
+    k_hc_postmix<<<a.nchunk, 256, 0, st>>>(a);
     return ok_launch();
 }
 

@@ -357,8 +357,7 @@ static ApusGcudaModel *model_create(const ApusGcudaConfig *cfg, int has_mtp, siz
     S.h4b = (uint16_t *)A((size_t)R * D.hc * d * 2);
     S.x = (uint16_t *)A((size_t)R * d * 2);
     S.sub = (uint16_t *)A((size_t)R * d * 2);
-    S.rms = (float *)A(R * 4);
-    S.mix = (float *)A((size_t)R * (2 + D.hc) * D.hc * ((D.hc * d + 1023) / 1024) * 4);   // mix partials
+    S.mix = (float *)A((size_t)R * hc_nchunk(D) * ((2 + D.hc) * D.hc + 1) * 4);   // pre-mix partials
     S.post = (float *)A((size_t)R * D.hc * 4);
     S.comb = (float *)A((size_t)R * D.hc * D.hc * 4);
     S.kp = (uint16_t *)A((size_t)R * ldkp * 2);
@@ -845,6 +844,9 @@ static int main_forward(ApusGcudaModel *m, const int32_t *ids_dev, int R, uint16
     if (k_embed_launch(m->embed, ids_dev, R, D.d, D.hc, S.h4, st)) return -1;
     uint16_t *h = S.h4, *h2 = S.h4b;
     auto stop = [&](int l, int stage) { return l == m->dbg_layer && stage == m->dbg_stage; };
+    // each expand also leaves the next site's pre-mix partials in S.mix
+    if (hc_postmix_launch(D, nullptr, nullptr, h, R, S, nullptr, m->L[0].hc_fn[0], st)) return -1;
+    const bool ep = m->ep_world > 1;
     for (int l = 0; l < D.L; l++) {
         LayerW &W = m->L[l];
         if (hc_pre_launch(D, W, 0, h, R, S, st)) return -1;
@@ -855,14 +857,16 @@ static int main_forward(ApusGcudaModel *m, const int32_t *ids_dev, int R, uint16
             if (dsa_launch(D, W.dsa, m->dsa[l], &m->ctl->pos, R, S, S.x, S.sub, m->part, m->tick, st)) return -1;
         }
         if (stop(l, 1)) return 0;
-        if (hc_post_launch(D, S.sub, h, R, S, h2, st)) return -1;
+        if (hc_postmix_launch(D, S.sub, nullptr, h, R, S, h2, W.hc_fn[1], st)) return -1;
         std::swap(h, h2);
         if (stop(l, 2)) return 0;
         if (hc_pre_launch(D, W, 1, h, R, S, st)) return -1;
         if (stop(l, 3)) return 0;
-        if (moe_forward_launch(W.moe, S.x, D.d, R, S.sub, D.d, nullptr, st)) return -1;
-        if (stop(l, 4)) return 0;
-        if (hc_post_launch(D, S.sub, h, R, S, h2, st)) return -1;
+        // one GPU: the combine of the expert outputs happens inside the expand
+        if (moe_forward_launch(W.moe, S.x, D.d, R, ep ? S.sub : nullptr, D.d, nullptr, st)) return -1;
+        if (stop(l, 4)) return ep ? 0 : moe_combine_launch(W.moe, R, S.sub, D.d, st);
+        const uint16_t *fn_next = l + 1 < D.L ? m->L[l + 1].hc_fn[0] : nullptr;
+        if (hc_postmix_launch(D, ep ? S.sub : nullptr, ep ? nullptr : &W.moe, h, R, S, h2, fn_next, st)) return -1;
         std::swap(h, h2);
     }
     if (h != S.h4) cudaMemcpyAsync(S.h4, h, (size_t)R * D.hc * D.d * 2, cudaMemcpyDeviceToDevice, st);

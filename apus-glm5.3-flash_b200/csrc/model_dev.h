@@ -101,8 +101,7 @@ struct DsaState {
 struct Scratch {
     uint16_t *h4, *h4b;     // [R][hc*d] residual streams (ping-pong)
     uint16_t *x, *sub;      // [R][d]
-    float *rms;             // [R] inverse rms of the stream
-    float *mix;             // [R][(2+hc)*hc][ceil(hc*d/1024)] partial mixes
+    float *mix;             // [R][hc_nchunk][(2+hc)*hc + 1] pre-mix partials
     float *post, *comb;     // [R][hc], [R][hc*hc]
     uint16_t *kp;           // KDA projections [R][3qkv+2Dr+H]
     uint16_t *fgo;          // [2][R][qkv]  f_b, g_b outputs
@@ -137,10 +136,27 @@ int layers_prepare(const Dims &D);
 // All take the row count R and the device control block (positions).
 int k_embed_launch(const uint16_t *embed, const int32_t *ids, int R, int d, int hc, uint16_t *h4,
                    cudaStream_t st);
+// mHC of one site: the pre-mix partials in S.mix (left by hc_postmix_launch)
+// -> S.x (the collapsed row normed with the input/post norm), S.post/comb.
 int hc_pre_launch(const Dims &D, const LayerW &W, int site, const uint16_t *h4, int R, Scratch &S,
-                  cudaStream_t st);       // -> S.x (normed with input/post norm), S.post/comb
-int hc_post_launch(const Dims &D, const uint16_t *x, const uint16_t *h4, int R, const Scratch &S,
-                   uint16_t *h4out, cudaStream_t st);
+                  cudaStream_t st);
+// The expand after a sublayer (h4out != null; the sublayer output is x [R][d],
+// or, with x == null, the MoE outputs of *moe combined on the fly), then the
+// pre-mix partials of the next site's fn_next (when given) into S.mix.  With
+// h4out == null only the partials of the streams h4 are computed.
+struct HcPostMix {
+    const uint16_t *x;
+    MoeDev moe;
+    const uint16_t *h4;
+    const float *post, *comb;
+    uint16_t *h4out;
+    const uint16_t *fn;
+    float *part;                  // [R][nchunk][nmix + 1]
+    int d, hc, nmix, R, nchunk;
+};
+int hc_nchunk(const Dims &D);
+int hc_postmix_launch(const Dims &D, const uint16_t *x, const MoeDev *moe, const uint16_t *h4, int R, Scratch &S,
+                      uint16_t *h4out, const uint16_t *fn_next, cudaStream_t st);
 int head_norm_launch(const Dims &D, const uint16_t *h4, const uint16_t *norm_w, int R, uint16_t *yn,
                      unsigned long long *keys, cudaStream_t st);     // keys: zeroed for the lm_head argmax
 int rmsnorm_rows_launch(const uint16_t *x, long ldx, const uint16_t *w, int n, int R, float eps,

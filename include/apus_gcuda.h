@@ -33,8 +33,10 @@ extern "C" {
 int  apus_gcuda_enable(char *err, size_t errcap);        /* c/backend_gmetal.h:134 */
 void apus_gcuda_disable(void);                           /* c/backend_gmetal.h:136 */
 int  apus_gcuda_is_enabled(void);                        /* c/backend_gmetal.h:137 */
-/* Last error message of the calling thread ("" when none). */
+/* Last error message of the calling thread ("" when none); the message
+ * stays until the next failure or apus_gcuda_clear_error. */
 const char *apus_gcuda_last_error(void);
+void apus_gcuda_clear_error(void);
 /* Device-side error word of the pipelined kernels (0 = none; nonzero = a
  * bounded wait gave up: 1 producer, 2 consumer), read and cleared.
  * Synchronises the device. */

@@ -71,6 +71,7 @@ def test_quant_np_matches_oracle():
 def test_dequant_host_dropin_bitwise(gcuda, i):
     c, s, want = LIN[f"deq{i}_codes"], LIN[f"deq{i}_scales"], LIN[f"deq{i}_out"]
     out = np.zeros_like(want)
+    gcuda.apus_gcuda_clear_error()
     gcuda.apus_fp8blk_dequant(O.p(c), O.p(s), O.p(out), c.shape[0], c.shape[1])
     assert gcuda.apus_gcuda_last_error().decode() == ""
     assert np.array_equal(out, want)
