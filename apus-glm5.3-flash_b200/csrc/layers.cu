@@ -870,7 +870,7 @@ k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd, int vd, 
     float *sc = sbuf + (size_t)h * MAXR * sstride;     // [MAXR][sstride] scores, then e
     uint16_t *pb = pbuf + (size_t)h * MAXR * sstride;  // [MAXR][sstride] p (BF16)
     __shared__ int tail_s[MAXR];
-    __shared__ float rmax_s[MAXR], rsum_s[MAXR];
+    __shared__ float rmax_s[MAXR], rsum_s[MAXR], wmax_s[ATJ / 16][MAXR];
     for (int i = threadIdx.x; i < MAXR * (qd / 8); i += blockDim.x) {
         const int t = i / (qd / 8), c = i % (qd / 8);
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -911,6 +911,7 @@ k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd, int vd, 
     // of a tile when w < ATJ/16
     uint32_t qb[16][2];
     const int nks = qd / 16;
+    float kmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int ks = 0; ks < 16; ks++)
         if (ks < nks) ldsm_x2(qb[ks][0], qb[ks][1], qs + (lane & 7) * QROW + (ks * 16 + ((lane >> 3) & 1) * 8) * 2);
@@ -931,46 +932,64 @@ k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd, int vd, 
                 ldsm_x4(a0, a1, a2, a3, kt + swz(r0 + (lane & 15), ks * 2 + (lane >> 4), qd * 2));
                 mma_bf16_16816(c0, c1, c2, c3, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
             }
-            // c0/c1: position r0+g, rows 2q4 / 2q4+1; c2/c3: position r0+g+8
+            // c0/c1: position r0+g, rows 2q4 / 2q4+1; c2/c3: position r0+g+8.
+            // Positions a row cannot see are stored as -inf (p = 0 below);
+            // the row maxima of this CTA's positions accumulate in kmax.
             const int pa = ti * ATJ + r0 + g, pbp = pa + 8, t0 = 2 * q4, t1 = t0 + 1;
-            if (pa < nmax) {
-                if (t0 < R) sc[(size_t)t0 * sstride + pa] = bf16_round(bf16_round(c0) * scale);
-                if (t1 < R) sc[(size_t)t1 * sstride + pa] = bf16_round(bf16_round(c1) * scale);
-            }
-            if (pbp < nmax) {
-                if (t0 < R) sc[(size_t)t0 * sstride + pbp] = bf16_round(bf16_round(c2) * scale);
-                if (t1 < R) sc[(size_t)t1 * sstride + pbp] = bf16_round(bf16_round(c3) * scale);
+            const float cv[4] = {c0, c1, c2, c3};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int j = (e & 2) ? pbp : pa, t = t0 + (e & 1);
+                if (j < nmax && t < R) {
+                    const float v = visible(t, j) ? bf16_round(bf16_round(cv[e]) * scale) : -INFINITY;
+                    sc[(size_t)t * sstride + j] = v;
+                    kmax[e & 1] = fmaxf(kmax[e & 1], v);
+                }
             }
         }
         __syncthreads();
     }
-    // ---- softmax (warp t owns row t over this CTA's positions), cluster-wide
+    // row max of this CTA: lanes (g, q4) hold rows 2q4, 2q4+1 -> reduce over g
+    // and the score warps in warp order
+#pragma unroll
+    for (int u = 0; u < 2; u++)
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) kmax[u] = fmaxf(kmax[u], __shfl_xor_sync(0xffffffffu, kmax[u], off));
+    if (warp < ATJ / 16 && lane < 4) {
+        wmax_s[warp][2 * lane] = kmax[0];
+        wmax_s[warp][2 * lane + 1] = kmax[1];
+    }
+    __syncthreads();
+    // ---- softmax (warp t owns row t over this CTA's positions), cluster-wide.
+    // Position j of tile ti is lane-slot (ti, j % 32): every lane walks its
+    // slots in tile order, the eight loads of a tile issued together.
     const int t = warp;
     const bool row = t < R;
     const int qpos = base + t;
     float *srow = sc + (size_t)(row ? t : 0) * sstride;
-    if (row) {
-        float m = -3.4028234663852886e+38f;
-        for (int ti = z; ti < nt; ti += ASPLIT)
-            for (int j = ti * ATJ + lane; j < ti * ATJ + ATJ && j <= qpos; j += 32)
-                if (visible(t, j)) m = fmaxf(m, srow[j]);
-#pragma unroll
-        for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        if (lane == 0) rmax_s[t] = m;
+    if (row && lane == 0) {
+        float m = wmax_s[0][t];
+        for (int w = 1; w < ATJ / 16; w++) m = fmaxf(m, wmax_s[w][t]);
+        rmax_s[t] = m;
     }
     cluster.sync();
-    float mx = -3.4028234663852886e+38f;
+    float mx = -INFINITY;
     if (row)
         for (int zz = 0; zz < ASPLIT; zz++) mx = fmaxf(mx, cluster.map_shared_rank(rmax_s, zz)[t]);
+    constexpr int PL = ATJ / 32;                      // slots of a lane in one tile
     if (row) {
         float su = 0.f;
-        for (int ti = z; ti < nt; ti += ASPLIT)
-            for (int j = ti * ATJ + lane; j < ti * ATJ + ATJ && j <= qpos; j += 32)
-                if (visible(t, j)) {
-                    const float e = expf(srow[j] - mx);
-                    srow[j] = e;
-                    su += e;
-                }
+        for (int ti = z; ti < nt; ti += ASPLIT) {
+            float v[PL];
+#pragma unroll
+            for (int u = 0; u < PL; u++) {
+                const int j = ti * ATJ + u * 32 + lane;
+                v[u] = j <= qpos ? srow[j] : -INFINITY;
+            }
+#pragma unroll
+            for (int u = 0; u < PL; u++)
+                if (v[u] != -INFINITY) su += expf(v[u] - mx);
+        }
 #pragma unroll
         for (int off = 16; off; off >>= 1) su += __shfl_xor_sync(0xffffffffu, su, off);
         if (lane == 0) rsum_s[t] = su;
@@ -980,9 +999,17 @@ k_dsa_attn(const uint16_t *q, const int *base_n, int R, int AH, int qd, int vd, 
         float sum = cluster.map_shared_rank(rsum_s, 0)[t];
         for (int zz = 1; zz < ASPLIT; zz++) sum += cluster.map_shared_rank(rsum_s, zz)[t];
         uint16_t *prow = pb + (size_t)t * sstride;
-        for (int ti = z; ti < nt; ti += ASPLIT)
-            for (int j = ti * ATJ + lane; j < ti * ATJ + ATJ; j += 32)
-                prow[j] = (j <= qpos && visible(t, j)) ? bf16_bits(srow[j] / sum) : (uint16_t)0;
+        for (int ti = z; ti < nt; ti += ASPLIT) {
+            float v[PL];
+#pragma unroll
+            for (int u = 0; u < PL; u++) {
+                const int j = ti * ATJ + u * 32 + lane;
+                v[u] = j <= qpos && j < nmax ? srow[j] : -INFINITY;
+            }
+#pragma unroll
+            for (int u = 0; u < PL; u++)
+                prow[ti * ATJ + u * 32 + lane] = v[u] != -INFINITY ? bf16_bits(expf(v[u] - mx) / sum) : (uint16_t)0;
+        }
     }
     __syncthreads();
     // ---- output partial over this CTA's tiles: warp w owns dv tiles w, w+8
