@@ -548,6 +548,51 @@ def c2_algo_bytes(kw, depth, n_ctx, moe_problems, world=1):
     return main + mtp + moe_problems * expert, n_moe_calls
 
 
+def profile_value(fname, key):
+    """A number recorded in a committed ncu summary under profiles/ (a line
+    `key: value`), or None."""
+    path = os.path.join(ROOT, "profiles", fname)
+    try:
+        for line in open(path):
+            if line.strip().startswith(key + ":"):
+                return float(line.split(":", 1)[1].split()[0].replace(",", ""))
+    except OSError:
+        pass
+    return None
+
+
+def lm_head_gemv_time(kw, rows, world=1, reps=20):
+    """Average device time of the dominant kernel of the step, the lm_head
+    GEMV with the fused greedy pick (BF16 [vocab][hidden], `rows` rows), timed
+    with CUDA events on its stream over `reps` back-to-back launches (the
+    matrix exceeds L2, so every launch streams it from HBM).  Expert-parallel
+    ranks time their vocabulary slice."""
+    import torch
+    import apus_gcuda as G
+    V, d = -(-kw["vocab_size"] // world), kw["hidden_size"]
+    w = (torch.randn(V, d, device="cuda") * 0.02).to(torch.bfloat16)
+    x = torch.randn(rows, d, device="cuda").to(torch.bfloat16)
+    ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+    st = torch.cuda.Stream()
+    sp = G.C.c_void_p(st.cuda_stream)
+
+    def call():
+        G.check(G.apus_gcuda_bf16_gemm_argmax_dev(G.ptr(w), G.ptr(x), None, G.ptr(ids), rows, V, d, sp), "lm_head")
+    for _ in range(3):
+        call()
+    st.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        call()
+    e1.record(st)
+    st.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    del w
+    torch.cuda.empty_cache()
+    return us, V * d * 2 + rows * d * 2
+
+
 def bench_c2(args, ws, rank, W=None):
     import numpy as np
     import torch
@@ -566,6 +611,9 @@ def bench_c2(args, ws, rank, W=None):
         m.ep_bootstrap(G.ep_all_gather())
     m.load(W)
     m.use_graph(True)
+    # every rank reaches the first device-side exchange together (its waits
+    # are bounded at about a second)
+    barrier(ws)
     m.spec_prefill(prompt)
     st = torch.cuda.ExternalStream(m.stream())
     for _ in range(args.warmup):
@@ -620,12 +668,25 @@ def bench_c2(args, ws, rank, W=None):
            "spec": {"tokens_per_step": round(emitted / args.steps, 4), "offered": offered, "accepted": accepted,
                     "acceptance": round(accepted / offered, 4) if offered else None,
                     "context_avg": n_ctx},
-           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
-                        "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": src,
-                        "algo_bytes_per_step": int(algo), "moe_expert_problems_per_step": round(probs, 2),
-                        "note": "step-level: algorithmic bytes per step / device step time"},
+           "step_roofline": {"achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
+                             "algo_bytes_per_step": int(algo), "moe_expert_problems_per_step": round(probs, 2),
+                             "note": "algorithmic bytes per step / device step time"},
            "gpu_launches": int(c1["graph_kernels"]) * args.steps,
            "clocks": clk.summary()}
+    # the dominant kernel: the lm_head GEMV (5 launches per step, ~1/3 of it)
+    us, hb = lm_head_gemv_time(kw, depth, ws if ep else 1)
+    # DRAM bytes of one full-vocabulary launch from the committed ncu capture;
+    # a vocabulary slice moves its share of them
+    traffic = profile_value("lm_head_gemv_k_gemv_tma.md", "dram_bytes_per_launch")
+    if traffic is not None and ep:
+        traffic = round(traffic / ws)
+    hgbs = hb / us / 1e3
+    out["roofline"] = {"bound": "hbm", "kernel": f"k_gemv_tma<false> lm_head (BF16 {-(-kw['vocab_size'] // (ws if ep else 1))}"
+                                                  f"x{kw['hidden_size']} per rank, fused argmax)",
+                       "achieved": round(hgbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(hgbs / hbm, 4),
+                       "traffic": traffic,
+                       "algo_bytes_per_launch": hb, "avg_launch_us": round(us, 2), "peak_source": src,
+                       "launches_per_step": 5}
     if args.quick:
         m.close()
         return out, W

@@ -40,6 +40,9 @@ def run(G, kw, W, rank, world, seed_random=None):
     owns = G.ep_owns(kw, rank, world)
     stored = {k: m.set(k, v) for k, v in W.items()}
     res["stored_ok"] = all(stored[k] == owns(k) for k in W)
+    if world > 1:    # the device-side exchanges wait at most about a second
+        import torch.distributed as dist
+        dist.barrier()
     res["greedy"] = m.greedy(PROMPT, 40)
     truth = res["greedy"]
     m.reset()
