@@ -94,7 +94,13 @@ constexpr int STAGE_BYTES = TR * CH;         // one swizzled box (or two tiles' 
 constexpr long KX = 4096;             // elements of K per work item
 constexpr int XMAX = 4 * (2 * (int)KX + 32);   // staged activations: up to 4 rows
 constexpr int THREADS = 288;          // 8 consumer warps + 1 producer warp
-constexpr int PART = 8 * TR;          // floats of one warp partial: [x col][w row]
+constexpr int PART = 8 * TR;          // floats of one tile partial in scratch: [x col][w row]
+// In shared memory an x column of a warp partial is PSTR floats apart: lane
+// (g, t) writes columns 2t, 2t+1 of rows g, g+8, and with a stride of 20 the
+// 32 lanes of each store fall in 32 distinct banks (16 would put the four
+// t of one g in one bank).
+constexpr int PSTR = 20;
+constexpr int SPART = 8 * PSTR;       // floats of one warp partial in shared memory
 }  // namespace gemvcfg
 
 __device__ int g_apus_kernel_err;
@@ -188,7 +194,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
     uint8_t *ring = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);   // swizzle atoms: 1 KiB
     uint16_t *xs = (uint16_t *)(ring + NSTAGE * STAGE_BYTES);
     float *part = (float *)((uint8_t *)xs + XMAX);
-    uint64_t *full = (uint64_t *)(part + 8 * 2 * PART);     // [warp][tile][PART]
+    uint64_t *full = (uint64_t *)(part + 8 * 2 * SPART);    // [warp][tile][SPART]
     uint64_t *empty = full + NSTAGE;
     __shared__ unsigned long long best_sh[8];
     __shared__ int abort_sh;
@@ -450,12 +456,12 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
             if (lane == 0) mbar_arrive(&empty[s]);
         }
         // D layout: c0 = (w row g, x col 2t), c1 = (g, 2t+1), c2 = (g+8, 2t), c3 = (g+8, 2t+1)
-        float *pw = part + warp * 2 * PART;
+        float *pw = part + warp * 2 * SPART;
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const int xc = 2 * t4 + (e & 1), wr = g + 8 * (e >> 1);
-            pw[xc * TR + wr] = FP8 ? acc[0][e] * xinv_sh[xc] : (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
-            if (FP8 && tpi == 2) pw[PART + xc * TR + wr] = acc[1][e] * xinv_sh[xc];
+            pw[xc * PSTR + wr] = FP8 ? acc[0][e] * xinv_sh[xc] : (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+            if (FP8 && tpi == 2) pw[SPART + xc * PSTR + wr] = acc[1][e] * xinv_sh[xc];
         }
         named_bar_sync(1, 256);
         const int tid = threadIdx.x;
@@ -464,9 +470,10 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
         const int jt = tid >> 7, te = tid & 127;
         float a = 0.f;
         if (tid < 128 * tpi) {
-            a = part[jt * PART + te];
+            const int se = (te >> 4) * PSTR + (te & 15);      // (x col, w row) in a warp partial
+            a = part[jt * SPART + se];
 #pragma unroll
-            for (int w = 1; w < 8; w++) a = a + part[w * 2 * PART + jt * PART + te];
+            for (int w = 1; w < 8; w++) a = a + part[w * 2 * SPART + jt * SPART + se];
         }
         if (it.nks == 1) {
             if (tid < 128 * tpi)
@@ -638,7 +645,7 @@ static int g_num_sms = 0;
 
 static size_t gemv_smem() {
     using namespace gemvcfg;
-    return 1024 + NSTAGE * STAGE_BYTES + XMAX + 8 * 2 * PART * 4 + 2 * NSTAGE * 8;
+    return 1024 + NSTAGE * STAGE_BYTES + XMAX + 8 * 2 * SPART * 4 + 2 * NSTAGE * 8;
 }
 
 // Tensor map of the weights as (128 bytes of k, row, 128-byte k-slab,
