@@ -133,6 +133,10 @@ def make_config(**kw):
 _cs = C.c_char_p
 apus_gcuda_model_new = _fn("apus_gcuda_model_new", _vp, _vp, _i, _sz, _i)
 apus_gcuda_model_free = _fn("apus_gcuda_model_free", None, _vp)
+apus_gcuda_config_load = _fn("apus_gcuda_config_load", _i, _cs, _vp, _vp, _sz)
+apus_gcuda_container_check = _fn("apus_gcuda_container_check", _i, _cs, _vp, _i, _vp, _sz)
+apus_gcuda_container_read = _fn("apus_gcuda_container_read", C.c_long, _cs, _cs, _vp, _sz, _vp, _sz)
+apus_gcuda_model_load_container = _fn("apus_gcuda_model_load_container", _i, _vp, _cs, _vp, _sz)
 apus_gcuda_model_new_ep = _fn("apus_gcuda_model_new_ep", _vp, _vp, _i, _sz, _i, _i, _i)
 apus_gcuda_model_ep_handle = _fn("apus_gcuda_model_ep_handle", _i, _vp, _vp)
 apus_gcuda_model_ep_connect = _fn("apus_gcuda_model_ep_connect", _i, _vp, _vp)
@@ -200,6 +204,13 @@ class GModel:
             self.h = apus_gcuda_model_new(C.byref(cfg), int(has_mtp), kv_cap, depth)
         if not self.h:
             raise GcudaError(f"model_new: {apus_gcuda_last_error().decode(errors='replace')}")
+
+    def load_container(self, path):
+        """Upload every tensor this model (this rank) stores from the
+        reference's weight container directory `path`."""
+        err = C.create_string_buffer(512)
+        if apus_gcuda_model_load_container(self.h, os.fsencode(path), err, 512) != 0:
+            raise GcudaError(err.value.decode(errors="replace"))
 
     def ep_handle(self):
         """This rank's 64-byte exchange-region handle."""
@@ -349,6 +360,47 @@ def ep_owns(kw, rank, world):
         e = int(name[i + len(".mlp.experts."):].split(".", 1)[0])
         return e // per == rank
     return owns
+
+
+def config_load(path):
+    """ApusGcudaConfig from a config.json in either layout the reference
+    reads (apus_gcuda_config_load)."""
+    cfg = GcudaConfig()
+    err = C.create_string_buffer(512)
+    if apus_gcuda_config_load(os.fsencode(path), C.byref(cfg), err, 512) != 0:
+        raise GcudaError(err.value.decode(errors="replace"))
+    return cfg
+
+
+def config_dict(cfg):
+    """The fields of an ApusGcudaConfig as the keyword dict make_config takes."""
+    kw = {name: getattr(cfg, name) for name, _ in _CFG_FIELDS if name not in ("layer_is_dsa", "mlp_is_sparse")}
+    L = cfg.num_hidden_layers
+    kw["layer_is_dsa"] = [cfg.layer_is_dsa[i] for i in range(L)]
+    kw["mlp_is_sparse"] = [cfg.mlp_is_sparse[i] for i in range(L)]
+    return kw
+
+
+def container_check(path, cfg, has_mtp=True):
+    """Number of tensors the model of cfg needs, all found in the container
+    with their dtype and size; raises on the first problem."""
+    err = C.create_string_buffer(512)
+    n = apus_gcuda_container_check(os.fsencode(path), C.byref(cfg), int(has_mtp), err, 512)
+    if n < 0:
+        raise GcudaError(err.value.decode(errors="replace"))
+    return n
+
+
+def container_read(path, name):
+    """Raw bytes of one container tensor."""
+    err = C.create_string_buffer(512)
+    n = apus_gcuda_container_read(os.fsencode(path), name.encode(), None, 0, err, 512)
+    if n < 0:
+        raise GcudaError(err.value.decode(errors="replace"))
+    buf = C.create_string_buffer(max(n, 1))
+    if apus_gcuda_container_read(os.fsencode(path), name.encode(), buf, n, err, 512) != n:
+        raise GcudaError(err.value.decode(errors="replace"))
+    return buf.raw[:n]
 
 
 def tensor_specs(kw, has_mtp=True):

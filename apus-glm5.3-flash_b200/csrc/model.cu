@@ -655,6 +655,23 @@ static int resolve(const ApusGcudaModel *m, const char *name, void **dst, size_t
     return resolve_moe(m, W.moe, r, dst, want);
 }
 
+// The configuration a model was created with (the container loader's view).
+int model_config_get(const ApusGcudaModel *m, ApusGcudaConfig *cfg, int *has_mtp) {
+    if (!m) return -1;
+    *cfg = m->cfg;
+    *has_mtp = m->has_mtp;
+    return 0;
+}
+
+// 1 = this rank stores the checkpoint tensor, 0 = another expert-parallel
+// rank does, -1 = not a tensor of this model.
+int model_tensor_here(const ApusGcudaModel *m, const char *name) {
+    void *dst;
+    size_t want;
+    const int rc = resolve(m, name, &dst, &want);
+    return rc < 0 ? -1 : rc == 1 ? 0 : 1;
+}
+
 // 0 = stored; 1 = another expert-parallel rank's expert (nothing stored);
 // -1 = unknown tensor or wrong size.  The lm_head is stored as this rank's
 // vocabulary rows of the full host tensor.

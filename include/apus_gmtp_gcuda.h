@@ -79,6 +79,28 @@ ApusGcudaModel *apus_gcuda_model_new_ep(const ApusGcudaConfig *cfg, int has_mtp,
 int apus_gcuda_model_ep_handle(ApusGcudaModel *m, void *handle_out /* 64 bytes */);
 int apus_gcuda_model_ep_connect(ApusGcudaModel *m, const void *handles /* world * 64 bytes */);
 
+/* The reference's weight container (c/gmodel.h:123-137, c/st.h:25-80):
+ * config.json in either layout the reference accepts (the real
+ * "text_config" + "linear_attn_config" file or the flat fixture file;
+ * explicit layer_types / mlp_layer_types lists win over the i % 4 == 3 and
+ * first_k_dense_replace rule), and a directory with
+ * model.safetensors.index.json naming the safetensors shard of every tensor
+ * (container names: checkpoint names minus "model.language_model.").
+ * apus_gcuda_config_load fills cfg (0 / -1 + err).  apus_gcuda_container_check
+ * verifies, without a GPU, that every tensor the model of cfg needs is present
+ * with its dtype and size; it returns their count or -1.
+ * apus_gcuda_container_read copies one tensor's raw bytes to host (or, with
+ * host == NULL, only reports its size); it returns the byte count or -1.
+ * apus_gcuda_model_load_container uploads every tensor the model stores on
+ * this rank (an expert-parallel rank reads only its own experts and its
+ * lm_head rows); the shards are memory-mapped, not copied on the host. */
+int apus_gcuda_config_load(const char *path, ApusGcudaConfig *cfg, char *err, size_t errcap);
+int apus_gcuda_container_check(const char *dir, const ApusGcudaConfig *cfg, int has_mtp, char *err,
+                               size_t errcap);
+long apus_gcuda_container_read(const char *dir, const char *name, void *host, size_t cap, char *err,
+                               size_t errcap);
+int apus_gcuda_model_load_container(ApusGcudaModel *m, const char *dir, char *err, size_t errcap);
+
 /* Tensor by checkpoint name (c/gmodel.h:622-1106 names, minus the
  * "model.language_model." prefix), host pointer, synchronous. */
 int apus_gcuda_model_set(ApusGcudaModel *m, const char *name, const void *host, size_t bytes);
