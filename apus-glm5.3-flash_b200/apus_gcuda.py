@@ -55,6 +55,8 @@ apus_gcuda_bf16_gemm_f32_dev = _fn("apus_gcuda_bf16_gemm_f32_dev", _i, _vp, _vp,
 apus_gcuda_bf16_gemm_argmax_dev = _fn("apus_gcuda_bf16_gemm_argmax_dev", _i, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp)
 apus_gcuda_bf16_gemm_argmax_static_dev = _fn("apus_gcuda_bf16_gemm_argmax_static_dev", _i, _vp, _vp, _vp, _vp,
                                              _sz, _sz, _sz, _vp)
+apus_gcuda_sample_rows_dev = _fn("apus_gcuda_sample_rows_dev", _i, _vp, _sz, _sz, _sz, C.c_float, C.c_float,
+                                 _u64, _vp, _vp)
 
 _f = C.c_float
 apus_gcuda_moe_new = _fn("apus_gcuda_moe_new", _vp, _i, _i, _sz, _sz, _f, _f, _i)
@@ -154,6 +156,9 @@ apus_gcuda_gspec_emitted = _fn("apus_gcuda_gspec_emitted", _i, _vp, _vp, _sz)
 apus_gcuda_gspec_stats = _fn("apus_gcuda_gspec_stats", _i, _vp, _vp)
 apus_gcuda_gspec_force = _fn("apus_gcuda_gspec_force", _i, _vp, _vp, _sz, _sz, C.c_double, _u64)
 apus_gcuda_greedy = _fn("apus_gcuda_greedy", _i, _vp, _vp, _sz, _i, _vp)
+apus_gcuda_generate = _fn("apus_gcuda_generate", _i, _vp, _vp, _sz, _i, _vp)
+apus_gcuda_gspec_sampling = _fn("apus_gcuda_gspec_sampling", _i, _vp, C.c_float, C.c_float, _u64)
+apus_gcuda_rng_state = _fn("apus_gcuda_rng_state", _i, _vp, C.POINTER(_u64))
 apus_gcuda_state_digest = _fn("apus_gcuda_state_digest", _u64, _vp)
 apus_gcuda_gspec_use_graph = _fn("apus_gcuda_gspec_use_graph", _i, _vp, _i)
 apus_gcuda_model_stream = _fn("apus_gcuda_model_stream", _vp, _vp)
@@ -326,6 +331,23 @@ class GModel:
         out = np.empty(n_gen, np.int32)
         check(apus_gcuda_greedy(self.h, ptr(ids), len(ids), n_gen, ptr(out)), "greedy")
         return out.tolist()
+
+    def generate(self, ids, n_gen):
+        """Non-speculative decode with the sampling settings (greedy when temp <= 0)."""
+        np = self.np
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty(n_gen, np.int32)
+        check(apus_gcuda_generate(self.h, ptr(ids), len(ids), n_gen, ptr(out)), "generate")
+        return out.tolist()
+
+    def sampling(self, temp, top_p=1.0, seed=0):
+        """apus_gspec_init's temp / top_p and apus_rng_seed(seed)."""
+        check(apus_gcuda_gspec_sampling(self.h, float(temp), float(top_p), int(seed) & ((1 << 64) - 1)), "sampling")
+
+    def rng_state(self):
+        s = _u64(0)
+        check(apus_gcuda_rng_state(self.h, C.byref(s)), "rng_state")
+        return s.value
 
     def digest(self):
         return apus_gcuda_state_digest(self.h)

@@ -149,7 +149,10 @@ APUS_DEV uint32_t f32_order_key(float v) {
 }
 
 // argmax key: value major, LOWER index wins ties (c/sample.h:76-81).
+// -0 and +0 compare equal in the reference's comparisons, so both take the
+// key of +0 and the index decides.
 APUS_DEV unsigned long long argmax_key(float v, uint32_t idx) {
+    if (__float_as_uint(v) == 0x80000000u) v = 0.0f;
     return ((unsigned long long)f32_order_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
 }
 APUS_DEV uint32_t argmax_key_index(unsigned long long k) {

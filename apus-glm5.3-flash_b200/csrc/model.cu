@@ -96,6 +96,7 @@ __global__ void k_spec_walk(Ctl *c, int D, int32_t *log, int log_cap) {
     c->log_n += matched + 1;
     c->stat_emitted += matched + 1;
     c->stat_batches++;
+    if (c->temp > 0.0f) c->rng_s += (unsigned long long)(matched + 1) * 0x9E3779B97F4A7C15ull;
     c->pos += matched + 1;
     c->kda_cur = (c->kda_cur + matched + 1) % NSLOT;
     c->held = last;
@@ -165,6 +166,11 @@ __global__ void k_greedy_post(Ctl *c, int32_t *log, int log_cap) {
     }
 }
 
+// n sampled tokens consumed n splitmix64 draws (c/sample.h:173-177)
+__global__ void k_rng_advance(Ctl *c, int n) {
+    if (threadIdx.x == 0) c->rng_s += (unsigned long long)n * 0x9E3779B97F4A7C15ull;
+}
+
 __global__ void k_set_held_from_pick(Ctl *c, int row) {
     pdl_launch_dependents();
     if (threadIdx.x == 0) c->held = c->picks[row];
@@ -193,6 +199,7 @@ struct ApusGcudaModel {
     int log_cap = 0;
     int32_t *truth = nullptr;
     Ctl force{};                         // forced-draft settings (survive reset)
+    float temp = 0.0f, top_p = 1.0f;     // sampling settings (survive reset)
     int dbg_layer = -1, dbg_stage = -1;  // inspection stop inside main_forward
     uint16_t *yn_prompt = nullptr;       // [cap][d] post-norm rows of the prompt
     uint16_t *hcarry = nullptr, *hmtp = nullptr, *mtp_rows = nullptr;
@@ -805,9 +812,13 @@ extern "C" int apus_gcuda_model_reset(ApusGcudaModel *m) {
     }
     if (m->hcarry) cudaMemsetAsync(m->hcarry, 0, (size_t)D.d * 2, m->st);
     if (m->hmtp) cudaMemsetAsync(m->hmtp, 0, (size_t)D.d * 2, m->st);
+    Ctl old{};
+    cudaMemcpy(&old, m->ctl, sizeof old, cudaMemcpyDeviceToHost);
     Ctl c{};
     c.one = 1;
     for (int i = 1; i < MAXR; i++) c.chain_pos[i] = i - 1;
+    c.temp = m->temp; c.top_p = m->top_p;
+    c.rng_s = old.rng_s;                 // the caller's stream continues (an ApusRng outlives a sequence)
     c.force_on = m->force.force_on; c.force_base = m->force.force_base; c.force_n = m->force.force_n;
     c.force_seed = m->force.force_seed; c.force_p = m->force.force_p;
     if (gcuda_check(cudaMemcpyAsync(m->ctl, &c, sizeof c, cudaMemcpyHostToDevice, m->st), "reset")) return -1;
@@ -935,6 +946,20 @@ static bool ids_ok(const ApusGcudaModel *m, const int32_t *ids, size_t n, const 
     return true;
 }
 
+// held = the draw from logits row `row` of the last forward: the fused
+// argmax pick when greedy, else one sampled token (one splitmix64 draw).
+static int draw_held(ApusGcudaModel *m, int row) {
+    if (!(m->temp > 0.0f)) {
+        k_set_held_from_pick<<<1, 32, 0, m->st>>>(m->ctl, row);
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    }
+    if (sample_launch(m->S.logits + (size_t)row * m->D.V, m->D.V, m->D.V, 1, m->temp, m->top_p, &m->ctl->rng_s, 0,
+                      &m->ctl->held, m->st))
+        return -1;
+    k_rng_advance<<<1, 32, 0, m->st>>>(m->ctl, 1);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 static int fail_ctl(ApusGcudaModel *m, const char *what) {
     if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(m->st) != cudaSuccess)
         return gcuda_check(cudaGetLastError(), what);
@@ -1004,10 +1029,13 @@ extern "C" int apus_gcuda_gspec_prefill(ApusGcudaModel *m, const int32_t *ids, s
     // main model over the prompt in 8-row decode batches; keep every yn row
     for (size_t t0 = 0; t0 < n; t0 += MAXR) {
         const int k = (int)(n - t0 < MAXR ? n - t0 : MAXR);
+        const bool last = t0 + k == n;
         cudaMemcpyAsync(m->ids, h.data() + t0, k * 4, cudaMemcpyHostToDevice, m->st);
-        if (main_forward(m, m->ids, k, m->yn_prompt + t0 * d, false)) return fail_ctl(m, "gspec_prefill");
+        if (main_forward(m, m->ids, k, m->yn_prompt + t0 * d, last && m->temp > 0.0f))
+            return fail_ctl(m, "gspec_prefill");
         k_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
-        if (t0 + k == n) k_set_held_from_pick<<<1, 32, 0, m->st>>>(m->ctl, k - 1);
+        // the first held token: exactly the non-speculative first draw (c/gmtp.h:724-727)
+        if (last && draw_held(m, k - 1)) return fail_ctl(m, "gspec_prefill draw");
         cudaStreamSynchronize(m->st);
     }
     // a one-token prompt has no true pair: drafts stay 0 (c/gmtp.h:741-757)
@@ -1042,8 +1070,13 @@ static int spec_step(ApusGcudaModel *m, int Dp) {
     const Dims &D = m->D;
     const int d = D.d;
     cudaStream_t st = m->st;
+    const bool smp = m->temp > 0.0f;
     k_spec_begin<<<1, 32, 0, st>>>(m->ctl, Dp, m->cap, m->ids);
-    if (main_forward(m, m->ids, Dp, m->S.yn, false)) return -1;
+    if (main_forward(m, m->ids, Dp, m->S.yn, smp)) return -1;
+    // sampled: every verify row's own draw replaces its argmax pick; the walk
+    // consumes the draws of the rows it reaches (c/gmtp.h:800-831)
+    if (smp && sample_launch(m->S.logits, D.V, D.V, Dp, m->temp, m->top_p, &m->ctl->rng_s, 0, m->ctl->picks, st))
+        return -1;
     // MTP replay of the D candidate pairs (rows past the accepted prefix are
     // overwritten by the chain / the next replay)
     k_replay_rows<<<(Dp * d + 255) / 256, 256, 0, st>>>(m->hcarry, m->S.yn, Dp, d, m->mtp_rows);
@@ -1154,28 +1187,77 @@ extern "C" int apus_gcuda_gspec_force(ApusGcudaModel *m, const int32_t *truth, s
     return gcuda_check(cudaMemcpy(m->ctl, &c, sizeof c, cudaMemcpyHostToDevice), "gspec_force");
 }
 
-extern "C" int apus_gcuda_greedy(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen, int32_t *out) {
-    if (n < 1 || n_gen < 1 || n + (size_t)n_gen > (size_t)m->cap) { gcuda_set_error("greedy: capacity"); return -1; }
-    if (!ids_ok(m, ids, n, "greedy")) return -1;
+// Non-speculative decode: prompt in 8-row batches, then one token per
+// forward, each the draw from its own logits row (greedy pick, or a sampled
+// token when the model samples: tests/m8g/test_m8g.c:649-678).
+static int generate(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen, int32_t *out, bool smp,
+                    const char *what) {
+    if (n < 1 || n_gen < 1 || n + (size_t)n_gen > (size_t)m->cap) { gcuda_set_error("%s: capacity", what); return -1; }
+    if (!ids_ok(m, ids, n, what)) return -1;
     if (apus_gcuda_model_reset(m)) return -1;
+    const float temp = m->temp;
+    if (!smp) m->temp = 0.0f;            // draw_held picks greedily
+    int rc = 0;
     std::vector<int32_t> h(ids, ids + n);
-    for (size_t t0 = 0; t0 < n; t0 += MAXR) {
+    for (size_t t0 = 0; t0 < n && !rc; t0 += MAXR) {
         const int k = (int)(n - t0 < MAXR ? n - t0 : MAXR);
+        const bool last = t0 + k == n;
         cudaMemcpyAsync(m->ids, h.data() + t0, k * 4, cudaMemcpyHostToDevice, m->st);
-        if (main_forward(m, m->ids, k, m->S.yn, false)) return fail_ctl(m, "greedy prefill");
-        k_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
-        if (t0 + k == n) k_set_held_from_pick<<<1, 32, 0, m->st>>>(m->ctl, k - 1);
+        rc = main_forward(m, m->ids, k, m->S.yn, last && smp);
+        if (!rc) k_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
+        if (!rc && last) rc = draw_held(m, k - 1);
     }
-    for (int i = 0; i < n_gen; i++) {
+    for (int i = 0; i < n_gen && !rc; i++) {
         k_greedy_prep<<<1, 32, 0, m->st>>>(m->ctl, m->ids);
         if (i + 1 < n_gen) {
-            if (main_forward(m, m->ids, 1, m->S.yn, false)) return fail_ctl(m, "greedy");
-            k_commit<<<1, 32, 0, m->st>>>(m->ctl, 1);
+            rc = main_forward(m, m->ids, 1, m->S.yn, smp);
+            if (!rc) k_commit<<<1, 32, 0, m->st>>>(m->ctl, 1);
+            if (!rc && smp) {
+                rc = sample_launch(m->S.logits, m->D.V, m->D.V, 1, m->temp, m->top_p, &m->ctl->rng_s, 0,
+                                   m->ctl->picks, m->st);
+                if (!rc) k_rng_advance<<<1, 32, 0, m->st>>>(m->ctl, 1);
+            }
         }
-        k_greedy_post<<<1, 32, 0, m->st>>>(m->ctl, m->log, m->log_cap);
+        if (!rc) k_greedy_post<<<1, 32, 0, m->st>>>(m->ctl, m->log, m->log_cap);
     }
-    if (gcuda_check(cudaStreamSynchronize(m->st), "greedy")) return -1;
-    return gcuda_check(cudaMemcpy(out, m->log, (size_t)n_gen * 4, cudaMemcpyDeviceToHost), "greedy out");
+    m->temp = temp;
+    if (rc) return fail_ctl(m, what);
+    if (gcuda_check(cudaStreamSynchronize(m->st), what)) return -1;
+    return gcuda_check(cudaMemcpy(out, m->log, (size_t)n_gen * 4, cudaMemcpyDeviceToHost), what);
+}
+
+extern "C" int apus_gcuda_greedy(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen, int32_t *out) {
+    return generate(m, ids, n, n_gen, out, false, "greedy");
+}
+
+extern "C" int apus_gcuda_generate(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen, int32_t *out) {
+    return generate(m, ids, n, n_gen, out, m->temp > 0.0f, "generate");
+}
+
+// Sampling settings of the speculative and non-speculative decode
+// (apus_gspec_init's temp / top_p / rng, c/gmtp.h:617-629, seeded as
+// apus_rng_seed, c/sample.h:159).  A captured step graph is dropped: the
+// sampled step launches the sampler, the greedy one does not.
+extern "C" int apus_gcuda_gspec_sampling(ApusGcudaModel *m, float temp, float top_p, uint64_t seed) {
+    if (temp != temp) { gcuda_set_error("sampling: temperature is NaN"); return -1; }
+    if (temp > 0.0f && m->ep_world > 1) {
+        gcuda_set_error("sampling: the logits are split over the expert-parallel ranks (greedy only)");
+        return -1;
+    }
+    if (temp > 0.0f && sample_prepare(m->D.V)) return -1;
+    m->temp = temp;
+    m->top_p = top_p;
+    Ctl c = read_ctl(m);
+    c.temp = temp; c.top_p = top_p; c.rng_s = seed;
+    if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = nullptr; }
+    if (m->graph) { cudaGraphDestroy(m->graph); m->graph = nullptr; }
+    return gcuda_check(cudaMemcpy(m->ctl, &c, sizeof c, cudaMemcpyHostToDevice), "sampling");
+}
+
+extern "C" int apus_gcuda_rng_state(ApusGcudaModel *m, uint64_t *state) {
+    Ctl c = read_ctl(m);
+    *state = c.rng_s;
+    return gcuda_check(cudaGetLastError(), "rng state");
 }
 
 extern "C" int apus_gcuda_model_debug_stop(ApusGcudaModel *m, int layer, int stage) {

@@ -49,6 +49,10 @@ struct Ctl {
     int force_on, force_base, force_n;
     unsigned long long force_seed;
     double force_p;
+    // sampling (c/gmtp.h:208-209): temp <= 0 is greedy; rng_s is the
+    // splitmix64 state, advanced once per sampled token
+    float temp, top_p;
+    unsigned long long rng_s;
 };
 
 struct KdaW {
@@ -179,3 +183,12 @@ int kda_launch(const Dims &D, const LayerW &W, KdaState &KS, const Ctl *ctl, int
 int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, int R, Scratch &S,
                const uint16_t *x, uint16_t *out, float *part, int *tick, cudaStream_t st);
 int residual_add_launch(uint16_t *x, const uint16_t *sub, long n, cudaStream_t st);
+// Temperature / top-p draws of BF16 logits rows (c/sample.h:91-177): row r
+// takes the (r+1)-th splitmix64 draw after the state *rng_dev (or rng_val
+// when rng_dev is null) and writes its token to out[r]; temp <= 0 is the
+// lowest-index argmax.  sample_prepare sets the kernel's shared-memory limit
+// on the current device (before its first launch there, outside any stream
+// capture).
+int sample_prepare(int V);
+int sample_launch(const uint16_t *logits, long ld, int V, int rows, float temp, float top_p,
+                  const unsigned long long *rng_dev, unsigned long long rng_val, int *out, cudaStream_t st);

@@ -611,6 +611,8 @@ def bench_c2(args, ws, rank, W=None):
         m.ep_bootstrap(G.ep_all_gather())
     m.load(W)
     m.use_graph(True)
+    if args.temp > 0:
+        m.sampling(args.temp, args.top_p, args.seed)
     # every rank reaches the first device-side exchange together (its waits
     # are bounded at about a second)
     barrier(ws)
@@ -657,7 +659,9 @@ def bench_c2(args, ws, rank, W=None):
            "dtype": "bf16 activations, fp8e4m3/bf16 weights, f32 accumulation",
            "data": f"synthetic random-init weights (seed {C2['seed']}), {len(prompt)} uniform random prompt ids",
            "config": {"workload": "config2: scaled glm5_next (4 layers: 3 KDA 32x128 + 1 DSA, MoE 288 top-8 "
-                                  "inter 1024, vocab 154880) + 1 NextN MTP layer, greedy spec decode",
+                                  "inter 1024, vocab 154880) + 1 NextN MTP layer, " + (
+                                      f"sampled spec decode (temp {args.temp}, top_p {args.top_p}, seed {args.seed})"
+                                      if args.temp > 0 else "greedy spec decode"),
                       "depth": "BASELINE depth 3 = 4 verify rows (reference APUS_SPEC_K 4)",
                       "prompt": len(prompt),
                       "parallelism": (f"ep{ws}: routed experts and lm_head rows split over {ws} GPUs, "
@@ -827,6 +831,10 @@ def main():
     ap.add_argument("--gemv-table", nargs="?", const="all", default=None,
                     help="per-matrix GEMV timings of the config-2 step (profiling aid, one GPU); "
                          "optionally one matrix name")
+    ap.add_argument("--temp", type=float, default=0.0,
+                    help="config 2: sampled decode at this temperature (default 0: greedy, the headline)")
+    ap.add_argument("--top-p", type=float, default=0.95, help="config 2 sampled decode: nucleus top_p")
+    ap.add_argument("--seed", type=int, default=12345, help="config 2 sampled decode: splitmix64 seed")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed kernels only (no e2e, no CPU baseline): the profiling command")
     args = ap.parse_args()
@@ -862,12 +870,14 @@ def main():
         print(json.dumps(line), flush=True)
         return
     ws, rank, local = dist_init()
+    if args.temp > 0 and ws > 1 and args.mode == "ep":
+        raise SystemExit("sampled decode runs on one GPU per sequence (use --mode replicas)")
     if args.gemv_table:
         gemv_table(args.gemv_table)
         return
     if args.config == 2:
         out, W = bench_c2(args, ws, rank)
-        if rank == 0 and not args.quick and ws == 1:
+        if rank == 0 and not args.quick and ws == 1 and args.temp <= 0:   # the reference leg decodes greedily
             out["cpu_baseline"] = cpu_c2(W, budget_s=args.cpu_budget)
         if rank == 0:
             print(json.dumps(out), flush=True)

@@ -121,6 +121,17 @@ int apus_gcuda_bf16_gemm_argmax_dev(const uint16_t *w, const uint16_t *x, uint16
 int apus_gcuda_bf16_gemm_argmax_static_dev(const uint16_t *w, const uint16_t *x, uint16_t *y,
                                            int32_t *ids, size_t M, size_t O, size_t K,
                                            void *stream);
+/* c/sample.h:63 apus_sample over `rows` BF16 logits rows (device, row r at
+ * logits + r*ld): row r is drawn with the (r+1)-th splitmix64 uniform after
+ * rng_state, as if apus_sample were called on the rows in order with an
+ * ApusRng holding rng_state (the caller advances its state by `rows`).
+ * temp <= 0: the lowest-index argmax, no uniform.  temp > 0: softmax of
+ * logits/temp, nucleus top_p (c/sample.h:91-132), CDF draw, computed in exact
+ * integer arithmetic for the cumulative masses and a correctly rounded exp
+ * (the token is the reference's unless u * kept or top_p lies within about
+ * 1e-7 of a cumulative-mass boundary).  n <= 256000, ld >= n; ids [rows]. */
+int apus_gcuda_sample_rows_dev(const uint16_t *logits, size_t rows, size_t ld, size_t n, float temp,
+                               float top_p, uint64_t rng_state, int32_t *out, void *stream);
 
 #ifdef __cplusplus
 }

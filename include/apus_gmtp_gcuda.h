@@ -14,9 +14,10 @@
  * summation orders differ where a GPU reduction replaces a sequential loop,
  * so logits match the reference within tolerance, while inside this engine a
  * verify row is bitwise the one-token decode of the same context.  The
- * speculative stream is therefore bitwise the engine's own greedy stream.
- * The greedy pick is c/sample.h:76-81 on the BF16 logits (lowest index wins
- * ties), fused into the lm_head GEMV.
+ * speculative stream is therefore bitwise the engine's own non-speculative
+ * stream, greedy or sampled.  The greedy pick is c/sample.h:76-81 on the
+ * BF16 logits (lowest index wins ties), fused into the lm_head GEMV; the
+ * sampled draw is apus_gcuda_sample_rows_dev's (include/apus_gcuda.h).
  */
 #ifndef APUS_GMTP_GCUDA_H
 #define APUS_GMTP_GCUDA_H
@@ -122,11 +123,22 @@ int apus_gcuda_decode_batch(ApusGcudaModel *m, const int32_t *ids, size_t s, uin
 int apus_gcuda_mtp_forward(ApusGcudaModel *m, const int32_t *ids, const uint16_t *prev_h, size_t s,
                            uint16_t *logits, uint16_t *out_h);
 
-/* c/gmtp.h:253 apus_gspec_prefill (greedy): prompt in 8-token decode
- * batches, held token, MTP true-pair replay (postnorm source, lag 1,
+/* c/gmtp.h:245-248 apus_gspec_init's temp / top_p / rng (seeded as
+ * apus_rng_seed, c/sample.h:159): temp <= 0 decodes greedily (the default),
+ * temp > 0 samples every emitted token with one splitmix64 draw, in position
+ * order (c/gmtp.h:800-831); drafts stay the MTP argmax.  The stream state
+ * persists across prefills like a caller-owned ApusRng.  Expert-parallel
+ * models decode greedily only (their logits are split over the ranks).
+ * NaN temp is rejected; -1 on error. */
+int apus_gcuda_gspec_sampling(ApusGcudaModel *m, float temp, float top_p, uint64_t seed);
+/* The splitmix64 state (c/sample.h:57 ApusRng.s) after the draws so far. */
+int apus_gcuda_rng_state(ApusGcudaModel *m, uint64_t *state);
+
+/* c/gmtp.h:253 apus_gspec_prefill: prompt in 8-token decode batches, held
+ * token (greedy or sampled), MTP true-pair replay (postnorm source, lag 1,
  * c/gmtp.h:99-119) and the first draft chain.  0 on success. */
 int apus_gcuda_gspec_prefill(ApusGcudaModel *m, const int32_t *ids, size_t n);
-/* c/gmtp.h:259 apus_gspec_step (greedy): one verify step entirely on the
+/* c/gmtp.h:259 apus_gspec_step: one verify step entirely on the
  * device (verify forward, accept walk, KDA checkpoint select + DSA rewind,
  * MTP replay, draft chain); appends the emitted tokens to out (cap >=
  * depth+1) and returns their count (0 at capacity). */
@@ -149,6 +161,10 @@ int apus_gcuda_gspec_force(ApusGcudaModel *m, const int32_t *truth, size_t n, si
 /* Non-speculative greedy decode (the reference run loop's --no-spec path,
  * c/apus.c:1079-1143): prefill ids[n], then n_gen argmax tokens into out. */
 int apus_gcuda_greedy(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen, int32_t *out);
+/* The same non-speculative decode drawing each token with the model's
+ * sampling settings (tests/m8g/test_m8g.c:649-678 nonspec_run): greedy when
+ * temp <= 0, else one splitmix64 draw per token from the stream state. */
+int apus_gcuda_generate(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen, int32_t *out);
 
 /* Digest (FNV-1a 64) of the committed KDA states and DSA caches (the
  * rollback check of tests/m8g/test_m8g.c:383-424). */

@@ -143,3 +143,193 @@ int orc_argmax_bf16(const uint16_t *logits, size_t n) {
         if (orc_bf16_f32(logits[i]) > orc_bf16_f32(logits[best])) best = i;
     return (int)best;
 }
+
+/* --------------------------------------------------------------- sample */
+
+/* splitmix64 (c/sample.h:159-170) */
+uint64_t orc_rng_next(uint64_t *s) {
+    uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static float *g_sort_p;   /* qsort comparator context (single-threaded checker) */
+
+/* probability descending, exact ties by lower index (c/sample.h:97-110) */
+static int cmp_prob_desc(const void *a, const void *b) {
+    const int32_t i = *(const int32_t *)a, j = *(const int32_t *)b;
+    const float pi = g_sort_p[i], pj = g_sort_p[j];
+    if (pi > pj) return -1;
+    if (pi < pj) return 1;
+    return i < j ? -1 : (i > j ? 1 : 0);
+}
+
+/* c/sample.h:134-157 then :91-132 on the widened BF16 row: softmax of
+ * logits/temp in fp32 with a double sum, nucleus by the HF shift rule,
+ * renormalised CDF draw with u.  The sort is qsort on the same total order
+ * as the reference's shell sort, so the permutation is the same. */
+int orc_sample_logits_u(const uint16_t *logits, size_t n, float temp, float top_p, double u) {
+    if (temp <= 0.0f) return orc_argmax_bf16(logits, n);
+    float *p = (float *)malloc(n * sizeof(float));
+    int32_t *ord = (int32_t *)malloc(n * sizeof(int32_t));
+    float mx = orc_bf16_f32(logits[0]);
+    for (size_t i = 1; i < n; i++)
+        if (orc_bf16_f32(logits[i]) > mx) mx = orc_bf16_f32(logits[i]);
+    double sum = 0.0;
+    for (size_t i = 0; i < n; i++) {
+        p[i] = expf((orc_bf16_f32(logits[i]) - mx) / temp);
+        sum += p[i];
+    }
+    for (size_t i = 0; i < n; i++) p[i] = (float)(p[i] / sum);
+    for (size_t i = 0; i < n; i++) ord[i] = (int32_t)i;
+    g_sort_p = p;
+    qsort(ord, n, sizeof(int32_t), cmp_prob_desc);
+    double cum = 0.0, kept = 0.0;
+    size_t nk = 0;
+    for (size_t i = 0; i < n; i++) {
+        if (cum <= (double)top_p) {
+            cum += p[ord[i]];
+            kept = cum;
+            nk = i + 1;
+        } else {
+            break;
+        }
+    }
+    if (nk == 0) { nk = 1; kept = p[ord[0]]; }
+    int tok = ord[nk - 1];
+    double c = 0.0;
+    for (size_t i = 0; i < nk; i++) {
+        c += (double)p[ord[i]] / kept;
+        if (u < c) { tok = ord[i]; break; }
+    }
+    free(p);
+    free(ord);
+    return tok;
+}
+
+/* The same draw in the exact arithmetic the B200 sampler uses (the
+ * bitwise checker of apus-glm5.3-flash_b200/csrc/sample.cu), computed here
+ * element by element with a full sort instead of the kernel's key
+ * histogram:
+ *   p = e^z rounded to float, e^z by a Cody-Waite reduction by ln 2 and
+ *       the degree-13 Taylor polynomial in double (one rounding per op);
+ *   sum = the exact sum of p at 2^-100 resolution, rounded once to double;
+ *   q = (float)(p / sum) as the reference;
+ *   cumulative masses exact in integers of 2^-62; nucleus = through the
+ *   first sorted token whose cumulative mass exceeds floor(top_p * 2^62);
+ *   draw = the first sorted token whose cumulative mass exceeds
+ *   floor(u53 * kept / 2^53), u = u53 * 2^-53. */
+typedef unsigned __int128 orc_u128;
+
+static double orc_exp_cw(double z) {
+    static const double c[14] = {1.0, 1.0, 0x1.0p-1, 0x1.5555555555555p-3, 0x1.5555555555555p-5,
+                                 0x1.1111111111111p-7, 0x1.6c16c16c16c17p-10, 0x1.a01a01a01a01ap-13,
+                                 0x1.a01a01a01a01ap-16, 0x1.71de3a556c734p-19, 0x1.27e4fb7789f5cp-22,
+                                 0x1.ae64567f544e4p-26, 0x1.1eed8eff8d898p-29, 0x1.6124613a86d09p-33};
+    const double inv_ln2 = 0x1.71547652b82fep+0, ln2_hi = 0x1.62e42fee00000p-1, ln2_lo = 0x1.a39ef35793c76p-33;
+    const double k = rint(z * inv_ln2);
+    const double r = (z - k * ln2_hi) - k * ln2_lo;
+    double e = c[13];
+    for (int i = 12; i >= 0; i--) e = e * r + c[i];
+    const uint64_t kb = (uint64_t)((int64_t)k + 1023) << 52;
+    double s;
+    memcpy(&s, &kb, 8);
+    return e * s;
+}
+
+static float orc_smp_p(float l, float mx, float temp) {
+    const float z = (l - mx) / temp;
+    if (!(z >= -105.0f)) return 0.0f;
+    return (float)orc_exp_cw((double)z);
+}
+
+static void orc_float_parts(float v, uint64_t *M, int *E) {
+    uint32_t b;
+    memcpy(&b, &v, 4);
+    const uint32_t e = b >> 23;
+    *M = b & 0x7FFFFFu;
+    *E = -149;
+    if (e) { *M |= 0x800000u; *E = (int)e - 150; }
+}
+
+static uint64_t orc_fix62(float v) {
+    uint64_t M;
+    int E;
+    orc_float_parts(v, &M, &E);
+    const int s = E + 62;
+    return s >= 0 ? M << s : (s > -64 ? M >> -s : 0);
+}
+
+static orc_u128 orc_fix100(float v) {
+    uint64_t M;
+    int E;
+    orc_float_parts(v, &M, &E);
+    const int s = E + 100;
+    return s >= 0 ? (orc_u128)M << s : (orc_u128)(s > -64 ? M >> -s : 0);
+}
+
+static double orc_u128_scaled_rn(orc_u128 x) {
+    if (x < ((orc_u128)1 << 53)) return (double)(uint64_t)x * 0x1.0p-100;
+    int nb = 0;
+    for (orc_u128 t = x; t; t >>= 1) nb++;
+    const int sh = nb - 53;
+    orc_u128 mant = x >> sh;
+    const orc_u128 rem = x - (mant << sh), half = (orc_u128)1 << (sh - 1);
+    if (rem > half || (rem == half && (mant & 1))) mant += 1;
+    return ldexp((double)(uint64_t)mant, sh - 100);
+}
+
+static uint64_t *g_sort_f;
+static float *g_sort_q;
+
+static int cmp_q_desc(const void *a, const void *b) {
+    const int32_t i = *(const int32_t *)a, j = *(const int32_t *)b;
+    const float qi = g_sort_q[i], qj = g_sort_q[j];
+    if (qi > qj) return -1;
+    if (qi < qj) return 1;
+    return i < j ? -1 : (i > j ? 1 : 0);
+}
+
+int orc_sample_exact(const uint16_t *logits, size_t n, float temp, float top_p, uint64_t u53) {
+    if (!(temp > 0.0f)) return orc_argmax_bf16(logits, n);
+    float *q = (float *)malloc(n * sizeof(float));
+    uint64_t *f = (uint64_t *)malloc(n * sizeof(uint64_t));
+    int32_t *ord = (int32_t *)malloc(n * sizeof(int32_t));
+    float mx = orc_bf16_f32(logits[0]);
+    for (size_t i = 1; i < n; i++)
+        if (orc_bf16_f32(logits[i]) > mx) mx = orc_bf16_f32(logits[i]);
+    orc_u128 acc = 0;
+    for (size_t i = 0; i < n; i++) {
+        q[i] = orc_smp_p(orc_bf16_f32(logits[i]), mx, temp);
+        acc += orc_fix100(q[i]);
+    }
+    const double S = orc_u128_scaled_rn(acc);
+    uint64_t total = 0;
+    for (size_t i = 0; i < n; i++) {
+        q[i] = (float)((double)q[i] / S);
+        f[i] = orc_fix62(q[i]);
+        total += f[i];
+        ord[i] = (int32_t)i;
+    }
+    g_sort_q = q;
+    g_sort_f = f;
+    qsort(ord, n, sizeof(int32_t), cmp_q_desc);
+    const uint64_t TP = !(top_p >= 0.0f) ? 0 : (top_p >= 4.0f ? ~0ull : (uint64_t)((double)top_p * 0x1.0p62));
+    uint64_t kept = total, cum = 0;
+    for (size_t i = 0; i < n; i++) {
+        if (cum + f[ord[i]] > TP) { kept = cum + f[ord[i]]; break; }
+        cum += f[ord[i]];
+    }
+    const uint64_t X = (uint64_t)(((orc_u128)u53 * kept) >> 53);
+    int tok = ord[0];
+    cum = 0;
+    for (size_t i = 0; i < n; i++) {
+        cum += f[ord[i]];
+        if (cum > X) { tok = ord[i]; break; }
+    }
+    free(q);
+    free(f);
+    free(ord);
+    return tok;
+}

@@ -37,6 +37,13 @@ void orc_fp8_linear(const uint8_t *codes, const float *scales, const uint16_t *x
                     size_t M, size_t O, size_t K);
 int  orc_argmax_bf16(const uint16_t *logits, size_t n);   /* c/sample.h:76-81 on widened codes */
 
+/* ---- sampling (c/sample.h:91-177) ---- */
+uint64_t orc_rng_next(uint64_t *s);                       /* splitmix64, c/sample.h:159-166 */
+/* apus_sample_logits_u on the widened BF16 row (c/sample.h:134-157, :91-132) */
+int orc_sample_logits_u(const uint16_t *logits, size_t n, float temp, float top_p, double u);
+/* the same draw in the B200 sampler's exact arithmetic, u = u53 * 2^-53 */
+int orc_sample_exact(const uint16_t *logits, size_t n, float temp, float top_p, uint64_t u53);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,6 +40,9 @@ _decl(ORC, "orc_bf16_gemm", None, _vp, _vp, _vp, _sz, _sz, _sz)
 _decl(ORC, "orc_bf16_gemm_f32", None, _vp, _vp, _vp, _sz, _sz, _sz)
 _decl(ORC, "orc_fp8_linear", None, _vp, _vp, _vp, _vp, _sz, _sz, _sz)
 _decl(ORC, "orc_argmax_bf16", _i, _vp, _sz)
+_decl(ORC, "orc_rng_next", C.c_uint64, C.POINTER(C.c_uint64))
+_decl(ORC, "orc_sample_logits_u", _i, _vp, _sz, _f, _f, C.c_double)
+_decl(ORC, "orc_sample_exact", _i, _vp, _sz, _f, _f, C.c_uint64)
 
 if REF is not None:
     _decl(REF, "apus_fp8blk_dequant_scalar", None, _vp, _vp, _vp, _sz, _sz)
@@ -49,6 +52,8 @@ if REF is not None:
     _decl(REF, "apus_e4m3_dequant_f32", _f, C.c_uint8)
     _decl(REF, "apus_e4m3_quant_f32", C.c_uint8, _f)
     _decl(REF, "apus_ref_threads", _i)
+    _decl(REF, "apus_sample_logits_u", _i, _vp, _sz, _f, _f, C.c_double, _vp)
+    _decl(REF, "apus_sample", _i, _vp, _sz, _f, _f, _vp, _vp)
 
 
 def p(a):
@@ -220,3 +225,36 @@ class Model:
         rc = fn(self.h, st, p(ids), s, p(logits), p(h), p(yn))
         assert rc == 0
         return (logits, h, yn) if want_h else logits
+
+
+# ---- sampling (c/sample.h:91-177) ----
+
+GOLDEN = 0x9E3779B97F4A7C15
+M64 = (1 << 64) - 1
+
+
+def rng_draws(state, n):
+    """The next n splitmix64 outputs after `state` and the state after them
+    (c/sample.h:159-166)."""
+    s = C.c_uint64(state)
+    out = [ORC.orc_rng_next(C.byref(s)) for _ in range(n)]
+    return out, s.value
+
+
+def sample_logits_u(row, temp, top_p, u):
+    """c/sample.h apus_sample_logits_u on a BF16 codes row (restatement)."""
+    row = np.ascontiguousarray(row, np.uint16)
+    return ORC.orc_sample_logits_u(p(row), row.size, temp, top_p, u)
+
+
+def sample_exact(row, temp, top_p, u53):
+    """The same draw in the B200 sampler's exact arithmetic (u = u53 * 2^-53)."""
+    row = np.ascontiguousarray(row, np.uint16)
+    return ORC.orc_sample_exact(p(row), row.size, temp, top_p, u53)
+
+
+def ref_sample_logits_u(row, temp, top_p, u):
+    """The reference's own apus_sample_logits_u on the widened row (REF only)."""
+    lf = np.ascontiguousarray(f32_of(np.ascontiguousarray(row, np.uint16)))
+    scratch = np.empty(row.size * 8, np.uint8)
+    return REF.apus_sample_logits_u(p(lf), row.size, temp, top_p, u, p(scratch))
