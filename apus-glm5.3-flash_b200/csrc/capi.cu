@@ -53,6 +53,7 @@ struct Scratch {
     }
 };
 Scratch g_sw, g_ss, g_sx, g_sy, g_keys, g_part, g_tick;
+Scratch g_deq;   // BF16 copy of an FP8 matrix for the tensor-core path
 
 // Split-K scratch of the library's own GEMV launches (grow-only; the ticket
 // array is zeroed on growth and every launch leaves it zeroed).
@@ -70,6 +71,47 @@ int splitk_scratch(long O, long K, float **part, int **tick) {
     return 0;
 }
 cudaStream_t g_stream = nullptr;
+
+// y / yf / argmax keys of M rows: 64 rows or more (without the fused argmax)
+// run the tcgen05 GEMM, an FP8 matrix dequantised to BF16 first exactly as
+// c/fp8blk.h does; fewer rows run 8-row GEMV launches, each row bitwise
+// independent of the others.  Caller holds g_mu.
+int rows_locked(const void *dw, const float *dws, int fp8, const uint16_t *dx, uint16_t *dy, float *dyf,
+                unsigned long long *keys, size_t M, size_t O, size_t K, cudaStream_t st, int pdl) {
+    // (an FP8 matrix is checked through dx's alignment: its BF16 copy is a fresh allocation)
+    if (M >= 64 && !keys && gemm_tc_ok(dx, (long)K, fp8 ? (const void *)dx : dw, (long)K, (long)M, (long)O, (long)K)) {
+        const uint16_t *wb = (const uint16_t *)dw;
+        if (fp8) {
+            uint16_t *deq = (uint16_t *)g_deq.get(O * K * 2);
+            if (!deq) { gcuda_set_error("dequant scratch allocation failed"); return -1; }
+            if (fp8_dequant_launch((const uint8_t *)dw, dws, deq, O, K, st))
+                return gcuda_check(cudaGetLastError(), "dequant launch") ? -1 : -1;
+            wb = deq;
+        }
+        if (gemm_tc_launch(dx, (long)K, wb, (long)K, dy, (long)O, dyf, (long)O, (long)M, (long)O, (long)K, st))
+            return gcuda_check(cudaGetLastError(), "tensor-core GEMM launch") ? -1 : -1;
+        g_dispatch++;
+        return 0;
+    }
+    float *part;
+    int *tick;
+    if (splitk_scratch((long)O, (long)K, &part, &tick)) return -1;
+    for (size_t m0 = 0; m0 < M; m0 += 8) {
+        GemvDesc d{};
+        d.W = dw; d.WS = dws; d.nkb = (long)((K + 127) / 128);
+        d.x = dx + m0 * K; d.ldx = (long)K;
+        d.R = (int)((M - m0) < 8 ? (M - m0) : 8);
+        d.O = (long)O; d.K = (long)K; d.fp8 = fp8;
+        if (dy) { d.y = dy + m0 * O; d.ldy = (long)O; }
+        if (dyf) { d.yf = dyf + m0 * O; d.ldyf = (long)O; }
+        if (keys) d.amax = keys + m0;
+        d.part = part; d.ticket = tick;
+        d.pdl = pdl;
+        if (gemv_launch(d, st)) return gcuda_check(cudaGetLastError(), "gemv launch") ? -1 : -1;
+        g_dispatch++;
+    }
+    return 0;
+}
 
 int ensure_enabled() {
     if (g_enabled) return 0;
@@ -118,20 +160,7 @@ int linear_host(const void *w, size_t wbytes, const float *ws, size_t sbytes, in
     if (!dx || !dy) { gcuda_set_error("scratch allocation failed"); return -1; }
     if (gcuda_check(cudaMemcpyAsync(dx, x, M * K * 2, cudaMemcpyHostToDevice, g_stream), "x upload"))
         return -1;
-    float *part;
-    int *tick;
-    if (splitk_scratch((long)O, (long)K, &part, &tick)) return -1;
-    for (size_t m0 = 0; m0 < M; m0 += 8) {
-        GemvDesc d{};
-        d.W = dw; d.WS = dws; d.nkb = (long)((K + 127) / 128);
-        d.x = dx + m0 * K; d.ldx = (long)K;
-        d.R = (int)((M - m0) < 8 ? (M - m0) : 8);
-        d.O = (long)O; d.K = (long)K; d.fp8 = fp8;
-        d.part = part; d.ticket = tick;
-        d.y = dy + m0 * O; d.ldy = (long)O;
-        if (gemv_launch(d, g_stream)) { gcuda_check(cudaGetLastError(), "gemv launch"); return -1; }
-        g_dispatch++;
-    }
+    if (rows_locked(dw, dws, fp8, dx, dy, nullptr, nullptr, M, O, K, g_stream, 0)) return -1;
     if (gcuda_check(cudaMemcpyAsync(y, dy, M * O * 2, cudaMemcpyDeviceToHost, g_stream), "y download"))
         return -1;
     if (gcuda_check(cudaStreamSynchronize(g_stream), "sync")) return -1;
@@ -190,8 +219,8 @@ void apus_gcuda_clear_error(void) { g_err[0] = 0; }
 
 int apus_gcuda_kernel_error(void) {
     cudaDeviceSynchronize();
-    const int a = kernel_error_read_and_clear(), b = ep_error_read_and_clear();
-    return a ? a : b;
+    const int a = kernel_error_read_and_clear(), b = ep_error_read_and_clear(), c = tc_error_read_and_clear();
+    return a ? a : (b ? b : c);
 }
 
 int apus_gcuda_register_region(const void *ptr, size_t len) {
@@ -296,26 +325,8 @@ void apus_gcuda_set_pdl(int on) { g_pdl = on ? 1 : 0; }
 static int linear_dev(const void *w, const float *ws, int fp8, const uint16_t *x, uint16_t *y,
                       float *yf, unsigned long long *keys, size_t M, size_t O, size_t K,
                       cudaStream_t st) {
-    float *part;
-    int *tick;
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        if (splitk_scratch((long)O, (long)K, &part, &tick)) return -1;
-    }
-    for (size_t m0 = 0; m0 < M; m0 += 8) {
-        GemvDesc d{};
-        d.W = w; d.WS = ws; d.nkb = (long)((K + 127) / 128);
-        d.x = x + m0 * K; d.ldx = (long)K;
-        d.R = (int)((M - m0) < 8 ? (M - m0) : 8);
-        d.O = (long)O; d.K = (long)K; d.fp8 = fp8;
-        if (y) { d.y = y + m0 * O; d.ldy = (long)O; }
-        if (yf) { d.yf = yf + m0 * O; d.ldyf = (long)O; }
-        if (keys) d.amax = keys + m0;
-        d.part = part; d.ticket = tick;
-        d.pdl = g_pdl;
-        if (gemv_launch(d, st)) return gcuda_check(cudaGetLastError(), "gemv launch") ? -1 : -1;
-    }
-    return 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    return rows_locked(w, ws, fp8, x, y, yf, keys, M, O, K, st, g_pdl);
 }
 
 int apus_gcuda_fp8blk_linear_dev(const uint8_t *codes, const float *scales,

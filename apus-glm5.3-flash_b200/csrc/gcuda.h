@@ -68,6 +68,12 @@ int gemv_launch(const GemvDesc &d, cudaStream_t st);
 int fp8_dequant_launch(const uint8_t *w, const float *ws, uint16_t *out, size_t O, size_t K,
                        cudaStream_t st);
 int kernel_error_read_and_clear(void);
+// tcgen05 GEMM for >= 64 rows (gemm_tc.cu): y / yf [M][ld] = x [M][ldx] . W [O][ldw]^T,
+// BF16 operands, fp32 accumulation; ld multiples of 8, 16-byte aligned bases.
+bool gemm_tc_ok(const void *x, long ldx, const void *w, long ldw, long M, long O, long K);
+int gemm_tc_launch(const uint16_t *x, long ldx, const uint16_t *w, long ldw, uint16_t *y, long ldy, float *yf,
+                   long ldyf, long M, long O, long K, cudaStream_t st);
+int tc_error_read_and_clear(void);
 int ep_error_read_and_clear(void);      // the expert-parallel barrier's timeout word
 int argmax_reset_launch(unsigned long long *keys, int n, cudaStream_t st);
 int argmax_extract_launch(const unsigned long long *keys, int32_t *ids, int n, cudaStream_t st);
