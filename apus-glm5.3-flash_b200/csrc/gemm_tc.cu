@@ -4,15 +4,18 @@
 // fp32 accumulation (c/bf16.h:739-767 apus_bf16_gemm_mt's contraction; an FP8
 // matrix is first dequantised to BF16 as c/fp8blk.h:109-317 does).
 //
-// One CTA computes a 128 x 128 output tile (128 rows of x against 128 rows of
-// W), 128 threads:
+// Persistent CTAs, one per SM, each taking 128 x 256 output tiles (128 rows of
+// x against 256 rows of W) in turn; 192 threads:
 //   * warp 0 lane 0 streams 64-wide k-blocks of both operands with 2-D tensor
-//     copies (128-byte swizzle, no multicast) into a 4-stage ring;
-//   * warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 128,
-//     K 16; four per k-block), accumulating in 128 TMEM columns, and commits
-//     each stage back to the producer;
-//   * all four warps then read the accumulator (warp w owns TMEM lanes
-//     32w..32w+31, i.e. tile rows), round to BF16 (or keep fp32) and store.
+//     copies (128-byte swizzle, no multicast) into a 4-stage ring (48 KB a
+//     stage);
+//   * warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 256,
+//     K 16; four per k-block) into one of two 256-column TMEM accumulators
+//     and commits each stage back to the producer and each finished tile to
+//     the epilogue;
+//   * warps 2-5 drain the other accumulator meanwhile (warp w reads TMEM
+//     lanes 32 (w mod 4) .. +31, one tile row per lane), round to BF16 (or
+//     keep fp32) and store.
 // Every mbarrier wait is bounded (pipe.cuh): a lost copy or commit ends the
 // kernel with an error word, TMEM freed, instead of a hang.
 #include <cuda.h>
@@ -27,10 +30,11 @@ namespace apus {
 __device__ int g_tc_err;   // first failed wait's code (21 stage free, 22 stage full, 23 accumulator)
 
 namespace tc {
-constexpr int BM = 128, BN = 128, BK = 64, NST = 4, THREADS = 128;
+constexpr int BM = 128, BN = 256, BK = 64, NST = 4;
+constexpr int THREADS = 192;               // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_BYTES;
 constexpr int SMEM = NST * STAGE + 1024;   // + slack to align the ring to the 1024-byte swizzle atom
-constexpr int TMEM_COLS = BN;              // fp32 accumulator columns
+constexpr int TMEM_COLS = 2 * BN;          // two fp32 accumulators: one drains while the next fills
 // instruction descriptor: D f32 (bits 4-5 = 1), A and B BF16 (bits 7-9, 10-12
 // = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24
 constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
@@ -42,6 +46,7 @@ struct TcDesc {
     float *yf;        // [M][ldyf] fp32, or null
     long ldy, ldyf;
     int M, O, K;
+    int ntn, ntiles;  // output tiles along O, in total
 };
 
 // Shared-memory matrix descriptor of a K-major operand tile whose rows are
@@ -80,29 +85,36 @@ APUS_DEV void tc_commit(uint64_t *bar) {
                  ::"r"(smem_u32(bar)) : "memory");
 }
 
-APUS_DEV void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes (one row per lane).
+APUS_DEV void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Persistent: CTA b takes output tiles b, b + grid, ... (tile t covers rows
+// 128 * (t / ntn) and weight rows 256 * (t % ntn)).  The k-block ring and the
+// two TMEM accumulators carry their phases across tiles, so the epilogue of
+// one tile overlaps the mainloop of the next.
 __global__ void __launch_bounds__(tc::THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, TcDesc d) {
     extern __shared__ __align__(1024) uint8_t tc_dyn[];
-    __shared__ __align__(8) uint64_t full[tc::NST], empty[tc::NST], accb;
+    __shared__ __align__(8) uint64_t full[tc::NST], empty[tc::NST], tfull[2], tempty[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * tc::BN, m0 = blockIdx.y * tc::BM;
     const int nkb = (d.K + tc::BK - 1) / tc::BK;
     uint8_t *ring = tc_dyn + ((1024 - (smem_u32(tc_dyn) & 1023)) & 1023);
 
     if (tid == 0) {
         for (int s = 0; s < tc::NST; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        mbar_init(&accb, 1);
+        for (int a = 0; a < 2; a++) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 128); }
         abort_flag = 0;
         fence_barrier_init();
     }
@@ -117,64 +129,87 @@ k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUte
     const uint32_t tmem = tmem_slot;
     volatile int *ab = &abort_flag;
 
-    if (warp == 0 && lane == 0) {
-        // producer
-        for (int kb = 0; kb < nkb; kb++) {
-            const int s = kb % tc::NST;
-            if (kb >= tc::NST && !mbar_wait(&empty[s], ((kb / tc::NST) - 1) & 1, ab, &g_tc_err, 21))
-                break;
-            uint8_t *sa = ring + s * tc::STAGE;
-            mbar_arrive_expect_tx(&full[s], tc::STAGE);
-            tma_load_2d(sa, &amap, kb * tc::BK, m0, &full[s]);
-            tma_load_2d(sa + tc::A_BYTES, &bmap, kb * tc::BK, n0, &full[s]);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer
-        bool ok = true;
-        for (int kb = 0; kb < nkb && ok; kb++) {
-            const int s = kb % tc::NST;
-            if (!mbar_wait(&full[s], (kb / tc::NST) & 1, ab, &g_tc_err, 22)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t sa = smem_u32(ring + s * tc::STAGE), sb = sa + tc::A_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < tc::BK / 16; kk++)
-                tc_mma(tmem, umma_desc_sw128(sa + kk * 32), umma_desc_sw128(sb + kk * 32), (kb | kk) != 0);
-            tc_commit(&empty[s]);
-        }
-        if (ok) tc_commit(&accb);
-    }
-    __syncwarp();
-
-    // epilogue: thread (warp w, lane l) owns tile row 32w + l
-    const bool have = mbar_wait(&accb, 0, ab, &g_tc_err, 23);
-    __syncwarp();     // the TMEM loads below are warp-collective
-    tc_fence_after();
-    if (have) {
-        const int row = m0 + warp * 32 + lane;
-        const bool rok = row < d.M;
-        for (int c = 0; c < tc::BN; c += 16) {
-            uint32_t v[16];
-            tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
-            const int col = n0 + c;
-            if (!rok || col >= d.O) continue;
-            if (d.y) {
-                uint16_t *yp = d.y + (size_t)row * d.ldy + col;
-                if (col + 16 <= d.O && !(((uintptr_t)yp) & 15)) {
-                    uint32_t pk[8];
-#pragma unroll
-                    for (int j = 0; j < 8; j++)
-                        pk[j] = (uint32_t)bf16_bits(__uint_as_float(v[2 * j])) |
-                                ((uint32_t)bf16_bits(__uint_as_float(v[2 * j + 1])) << 16);
-                    ((uint4 *)yp)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    ((uint4 *)yp)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                } else {
-                    for (int j = 0; j < 16 && col + j < d.O; j++) yp[j] = bf16_bits(__uint_as_float(v[j]));
+    if (warp == 0) {
+        if (lane == 0) {   // producer
+            int g = 0;     // k-blocks issued by this CTA
+            for (int t = blockIdx.x; t < d.ntiles && !*ab; t += gridDim.x) {
+                const int m0 = (t / d.ntn) * tc::BM, n0 = (t % d.ntn) * tc::BN;
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % tc::NST;
+                    if (g >= tc::NST && !mbar_wait(&empty[s], ((g / tc::NST) - 1) & 1, ab, &g_tc_err, 21)) break;
+                    uint8_t *sa = ring + s * tc::STAGE;
+                    mbar_arrive_expect_tx(&full[s], tc::STAGE);
+                    tma_load_2d(sa, &amap, kb * tc::BK, m0, &full[s]);
+                    tma_load_2d(sa + tc::A_BYTES, &bmap, kb * tc::BK, n0, &full[s]);
                 }
             }
-            if (d.yf) {
-                float *fp = d.yf + (size_t)row * d.ldyf + col;
-                for (int j = 0; j < 16 && col + j < d.O; j++) fp[j] = __uint_as_float(v[j]);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {   // MMA issuer
+            int g = 0, i = 0;
+            for (int t = blockIdx.x; t < d.ntiles && !*ab; t += gridDim.x, i++) {
+                const int acc = i & 1;
+                if (i >= 2 && !mbar_wait(&tempty[acc], ((i >> 1) - 1) & 1, ab, &g_tc_err, 24)) break;
+                tc_fence_after();
+                const uint32_t td = tmem + (uint32_t)(acc * tc::BN);
+                bool ok = true;
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % tc::NST;
+                    if (!mbar_wait(&full[s], (g / tc::NST) & 1, ab, &g_tc_err, 22)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(ring + s * tc::STAGE), sb = sa + tc::A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < tc::BK / 16; kk++)
+                        tc_mma(td, umma_desc_sw128(sa + kk * 32), umma_desc_sw128(sb + kk * 32), (kb | kk) != 0);
+                    tc_commit(&empty[s]);
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
             }
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31, one tile row per lane
+        const int q = warp & 3;
+        int i = 0;
+        for (int t = blockIdx.x; t < d.ntiles; t += gridDim.x, i++) {
+            const int acc = i & 1;
+            const bool have = mbar_wait(&tfull[acc], (i >> 1) & 1, ab, &g_tc_err, 23);
+            if (!__all_sync(0xffffffffu, have)) break;   // warp-uniform: the TMEM loads are collective
+            tc_fence_after();
+            const int row = (t / d.ntn) * tc::BM + q * 32 + lane, nb = (t % d.ntn) * tc::BN;
+            const bool rok = row < d.M;
+            for (int c = 0; c < tc::BN; c += 32) {
+                uint32_t v[32];
+                tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * tc::BN + c), v);
+                const int col = nb + c;
+                if (!rok || col >= d.O) continue;
+                if (d.y) {
+                    uint16_t *yp = d.y + (size_t)row * d.ldy + col;
+                    if (col + 32 <= d.O && !(((uintptr_t)yp) & 15)) {
+#pragma unroll
+                        for (int h = 0; h < 4; h++) {
+                            uint32_t pk[4];
+#pragma unroll
+                            for (int j = 0; j < 4; j++)
+                                pk[j] = (uint32_t)bf16_bits(__uint_as_float(v[8 * h + 2 * j])) |
+                                        ((uint32_t)bf16_bits(__uint_as_float(v[8 * h + 2 * j + 1])) << 16);
+                            ((uint4 *)yp)[h] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col + j < d.O) yp[j] = bf16_bits(__uint_as_float(v[j]));
+                    }
+                }
+                if (d.yf) {
+                    float *fp = d.yf + (size_t)row * d.ldyf + col;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (col + j < d.O) fp[j] = __uint_as_float(v[j]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
         }
     }
     tc_fence_before();
@@ -188,8 +223,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUte
 using namespace apus;
 
 // 2-D BF16 tensor map of a row-major [rows][ld] matrix viewed as K x rows,
-// box 64 x 128 with the 128-byte swizzle (zero fill past the edges).
-static int tc_map(CUtensorMap *m, const void *base, long rows, long K, long ld) {
+// box 64 x box_rows with the 128-byte swizzle (zero fill past the edges).
+static int tc_map(CUtensorMap *m, const void *base, long rows, long K, long ld, int box_rows) {
     static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
     if (!enc) {
         void *p = nullptr;
@@ -201,7 +236,7 @@ static int tc_map(CUtensorMap *m, const void *base, long rows, long K, long ld) 
     }
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)tc::BK, (cuuint32_t)tc::BM};
+    const cuuint32_t box[2] = {(cuuint32_t)tc::BK, (cuuint32_t)box_rows};
     const cuuint32_t es[2] = {1, 1};
     return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -223,9 +258,17 @@ int gemm_tc_launch(const uint16_t *x, long ldx, const uint16_t *w, long ldw, uin
         attr = true;
     }
     CUtensorMap am, bm;
-    if (tc_map(&am, x, M, K, ldx) || tc_map(&bm, w, O, K, ldw)) return -1;
-    TcDesc d{y, yf, ldy, ldyf, (int)M, (int)O, (int)K};
-    const dim3 grid((unsigned)((O + tc::BN - 1) / tc::BN), (unsigned)((M + tc::BM - 1) / tc::BM));
+    if (tc_map(&am, x, M, K, ldx, tc::BM) || tc_map(&bm, w, O, K, ldw, tc::BN)) return -1;
+    static int nsm = 0;
+    if (!nsm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const long ntn = (O + tc::BN - 1) / tc::BN, ntm = (M + tc::BM - 1) / tc::BM;
+    if (ntn * ntm >= (1l << 31)) return -1;
+    TcDesc d{y, yf, ldy, ldyf, (int)M, (int)O, (int)K, (int)ntn, (int)(ntn * ntm)};
+    const int grid = (int)(d.ntiles < nsm ? d.ntiles : nsm);
     k_gemm_tc<<<grid, tc::THREADS, tc::SMEM, st>>>(am, bm, d);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
