@@ -30,15 +30,18 @@ namespace apus {
 __device__ int g_tc_err;   // first failed wait's code (21 stage free, 22 stage full, 23 accumulator)
 
 namespace tc {
-constexpr int BM = 128, BN = 256, BK = 64, NST = 4;
+constexpr int BM = 128, BK = 64, NST = 4;
 constexpr int THREADS = 192;               // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_BYTES;
-constexpr int SMEM = NST * STAGE + 1024;   // + slack to align the ring to the 1024-byte swizzle atom
-constexpr int TMEM_COLS = 2 * BN;          // two fp32 accumulators: one drains while the next fills
-// instruction descriptor: D f32 (bits 4-5 = 1), A and B BF16 (bits 7-9, 10-12
-// = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24
-constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
+constexpr int A_BYTES = BM * BK * 2;
+template <int BN> struct Cfg {
+    static constexpr int B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_BYTES;
+    static constexpr int SMEM = NST * STAGE + 1024;   // + slack to align the ring to the 1024-byte atom
+    static constexpr int TMEM_COLS = 2 * BN;          // two fp32 accumulators: one drains, one fills
+    // instruction descriptor: D f32 (bits 4-5 = 1), A and B BF16 (bits 7-9,
+    // 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24
+    static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                      ((uint32_t)(BM >> 4) << 24);
+};
 }  // namespace tc
 
 struct TcDesc {
@@ -46,7 +49,8 @@ struct TcDesc {
     float *yf;        // [M][ldyf] fp32, or null
     long ldy, ldyf;
     int M, O, K;
-    int ntn, ntiles;  // output tiles along O, in total
+    int ntm, ntn, ntiles;  // output tiles along M, along O, in total
+    int mfast;        // tile t: m tile t % ntm, o tile t / ntm (else m t / ntn, o t % ntn)
 };
 
 // Shared-memory matrix descriptor of a K-major operand tile whose rows are
@@ -70,11 +74,11 @@ APUS_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint6
 APUS_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 APUS_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-APUS_DEV void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+APUS_DEV void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
-        ::"r"(tmem_d), "l"(da), "l"(db), "r"(tc::IDESC), "r"(accumulate)
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -102,8 +106,10 @@ APUS_DEV void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 // 128 * (t / ntn) and weight rows 256 * (t % ntn)).  The k-block ring and the
 // two TMEM accumulators carry their phases across tiles, so the epilogue of
 // one tile overlaps the mainloop of the next.
+template <int BN>
 __global__ void __launch_bounds__(tc::THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, TcDesc d) {
+    using C = tc::Cfg<BN>;
     extern __shared__ __align__(1024) uint8_t tc_dyn[];
     __shared__ __align__(8) uint64_t full[tc::NST], empty[tc::NST], tfull[2], tempty[2];
     __shared__ uint32_t tmem_slot;
@@ -120,7 +126,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUte
     }
     if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(smem_u32(&tmem_slot)), "r"(tc::TMEM_COLS) : "memory");
+                     ::"r"(smem_u32(&tmem_slot)), "r"(C::TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
@@ -133,12 +139,13 @@ k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUte
         if (lane == 0) {   // producer
             int g = 0;     // k-blocks issued by this CTA
             for (int t = blockIdx.x; t < d.ntiles && !*ab; t += gridDim.x) {
-                const int m0 = (t / d.ntn) * tc::BM, n0 = (t % d.ntn) * tc::BN;
+                const int m0 = (d.mfast ? t % d.ntm : t / d.ntn) * tc::BM;
+                const int n0 = (d.mfast ? t / d.ntm : t % d.ntn) * BN;
                 for (int kb = 0; kb < nkb; kb++, g++) {
                     const int s = g % tc::NST;
                     if (g >= tc::NST && !mbar_wait(&empty[s], ((g / tc::NST) - 1) & 1, ab, &g_tc_err, 21)) break;
-                    uint8_t *sa = ring + s * tc::STAGE;
-                    mbar_arrive_expect_tx(&full[s], tc::STAGE);
+                    uint8_t *sa = ring + s * C::STAGE;
+                    mbar_arrive_expect_tx(&full[s], C::STAGE);
                     tma_load_2d(sa, &amap, kb * tc::BK, m0, &full[s]);
                     tma_load_2d(sa + tc::A_BYTES, &bmap, kb * tc::BK, n0, &full[s]);
                 }
@@ -151,16 +158,17 @@ k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUte
                 const int acc = i & 1;
                 if (i >= 2 && !mbar_wait(&tempty[acc], ((i >> 1) - 1) & 1, ab, &g_tc_err, 24)) break;
                 tc_fence_after();
-                const uint32_t td = tmem + (uint32_t)(acc * tc::BN);
+                const uint32_t td = tmem + (uint32_t)(acc * BN);
                 bool ok = true;
                 for (int kb = 0; kb < nkb; kb++, g++) {
                     const int s = g % tc::NST;
                     if (!mbar_wait(&full[s], (g / tc::NST) & 1, ab, &g_tc_err, 22)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(ring + s * tc::STAGE), sb = sa + tc::A_BYTES;
+                    const uint32_t sa = smem_u32(ring + s * C::STAGE), sb = sa + tc::A_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < tc::BK / 16; kk++)
-                        tc_mma(td, umma_desc_sw128(sa + kk * 32), umma_desc_sw128(sb + kk * 32), (kb | kk) != 0);
+                        tc_mma(td, umma_desc_sw128(sa + kk * 32), umma_desc_sw128(sb + kk * 32), C::IDESC,
+                               (kb | kk) != 0);
                     tc_commit(&empty[s]);
                 }
                 if (!ok) break;
@@ -176,11 +184,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUte
             const bool have = mbar_wait(&tfull[acc], (i >> 1) & 1, ab, &g_tc_err, 23);
             if (!__all_sync(0xffffffffu, have)) break;   // warp-uniform: the TMEM loads are collective
             tc_fence_after();
-            const int row = (t / d.ntn) * tc::BM + q * 32 + lane, nb = (t % d.ntn) * tc::BN;
+            const int row = (d.mfast ? t % d.ntm : t / d.ntn) * tc::BM + q * 32 + lane;
+            const int nb = (d.mfast ? t / d.ntm : t % d.ntn) * BN;
             const bool rok = row < d.M;
-            for (int c = 0; c < tc::BN; c += 32) {
+            for (int c = 0; c < BN; c += 32) {
                 uint32_t v[32];
-                tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * tc::BN + c), v);
+                tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c), v);
                 const int col = nb + c;
                 if (!rok || col >= d.O) continue;
                 if (d.y) {
@@ -215,7 +224,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUte
     tc_fence_before();
     __syncthreads();
     if (warp == 2)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tc::TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS)
                      : "memory");
 }
 
@@ -248,29 +257,48 @@ bool gemm_tc_ok(const void *x, long ldx, const void *w, long ldw, long M, long O
            ldw >= K && (ldx % 8) == 0 && (ldw % 8) == 0 && !((uintptr_t)x & 15) && !((uintptr_t)w & 15);
 }
 
-int gemm_tc_launch(const uint16_t *x, long ldx, const uint16_t *w, long ldw, uint16_t *y, long ldy, float *yf,
-                   long ldyf, long M, long O, long K, cudaStream_t st) {
-    if (!gemm_tc_ok(x, ldx, w, ldw, M, O, K)) return -1;
+template <int BN>
+static int tc_launch(const CUtensorMap &am, const uint16_t *w, long ldw, TcDesc d, int nsm, cudaStream_t st) {
     static bool attr = false;
     if (!attr) {
-        if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::Cfg<BN>::SMEM)
+            != cudaSuccess)
             return -1;
         attr = true;
     }
-    CUtensorMap am, bm;
-    if (tc_map(&am, x, M, K, ldx, tc::BM) || tc_map(&bm, w, O, K, ldw, tc::BN)) return -1;
+    CUtensorMap bm;
+    if (tc_map(&bm, w, d.O, d.K, ldw, BN)) return -1;
+    d.ntn = (d.O + BN - 1) / BN;
+    d.ntiles = d.ntm * d.ntn;
+    // the smaller operand is the one re-read across tiles: walk the m tiles
+    // first when x is the smaller, so each W tile is streamed once
+    d.mfast = d.M <= d.O;
+    const int grid = d.ntiles < nsm ? d.ntiles : nsm;
+    k_gemm_tc<BN><<<grid, tc::THREADS, tc::Cfg<BN>::SMEM, st>>>(am, bm, d);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int gemm_tc_launch(const uint16_t *x, long ldx, const uint16_t *w, long ldw, uint16_t *y, long ldy, float *yf,
+                   long ldyf, long M, long O, long K, cudaStream_t st) {
+    if (!gemm_tc_ok(x, ldx, w, ldw, M, O, K)) return -1;
     static int nsm = 0;
     if (!nsm) {
         int dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     }
-    const long ntn = (O + tc::BN - 1) / tc::BN, ntm = (M + tc::BM - 1) / tc::BM;
-    if (ntn * ntm >= (1l << 31)) return -1;
-    TcDesc d{y, yf, ldy, ldyf, (int)M, (int)O, (int)K, (int)ntn, (int)(ntn * ntm)};
-    const int grid = (int)(d.ntiles < nsm ? d.ntiles : nsm);
-    k_gemm_tc<<<grid, tc::THREADS, tc::SMEM, st>>>(am, bm, d);
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    const long ntm = (M + tc::BM - 1) / tc::BM;
+    if (ntm * ((O + 127) / 128) >= (1l << 31)) return -1;
+    CUtensorMap am;
+    if (tc_map(&am, x, M, K, ldx, tc::BM)) return -1;
+    TcDesc d{y, yf, ldy, ldyf, (int)M, (int)O, (int)K, (int)ntm, 0, 0, 0};
+    // 256-wide tiles unless 128-wide ones finish sooner over whole waves of
+    // SMs: measured, a 128-wide tile takes about 0.75 of a 256-wide one's
+    // time (half the work, but each SM's operand stream runs closer to its
+    // latency and shared-memory limits)
+    const long t256 = ntm * ((O + 255) / 256), t128 = ntm * ((O + 127) / 128);
+    const double c256 = (double)((t256 + nsm - 1) / nsm), c128 = (double)((t128 + nsm - 1) / nsm) * 0.75;
+    return c128 < c256 ? tc_launch<128>(am, w, ldw, d, nsm, st) : tc_launch<256>(am, w, ldw, d, nsm, st);
 }
 
 int tc_error_read_and_clear(void) {

@@ -750,6 +750,57 @@ def cpu_c2(W, budget_s=20.0, prompt_len=64, log=None):
                       f"(the bench prompt's first {prompt_len} ids; setup {t_load:.0f} s untimed)"}
 
 
+def tc_table(rows=(512, 2048), reps=20):
+    """Prefill-chunk linears of the config-2 model on the tcgen05 GEMM
+    (--tc-table): BF16 weights, M rows of activations, fp32 accumulation,
+    CUDA events on the launching stream over back-to-back launches, with
+    torch.matmul (cuBLAS) on the same operands beside it.  Prints one JSON
+    line per (matrix, rows)."""
+    import torch
+    import apus_gcuda as G
+    G.enable()
+    kw = c2_config()
+    d, V, qkv = kw["hidden_size"], kw["vocab_size"], kw["linear_num_heads"] * kw["linear_head_dim"]
+    D, H = kw["linear_head_dim"], kw["linear_num_heads"]
+    shapes = [("kda_proj", 3 * qkv + 2 * D + H, d), ("kda_o", d, qkv), ("eh_proj", d, 2 * d),
+              ("dsa_o", d, kw["num_attention_heads"] * kw["v_head_dim"]), ("lm_head", V, d),
+              ("square8k", 8192, 4096)]
+    st = torch.cuda.Stream()
+    sp = G.C.c_void_p(st.cuda_stream)
+    _, tf_peak, src = peaks()
+    for name, O_, K_ in shapes:
+        for M in rows:
+            w = (torch.randn(O_, K_, device="cuda") * 0.02).to(torch.bfloat16)
+            x = torch.randn(M, K_, device="cuda").to(torch.bfloat16)
+            y = torch.empty(M, O_, device="cuda", dtype=torch.bfloat16)
+            fl = 2.0 * M * O_ * K_
+            res = {}
+            for arm in ("tc", "cublas"):
+                with torch.cuda.stream(st):
+                    def run():
+                        if arm == "tc":
+                            G.check(G.apus_gcuda_bf16_gemm_dev(G.ptr(w), G.ptr(x), G.ptr(y), M, O_, K_, sp))
+                        else:
+                            torch.matmul(x, w.t(), out=y)
+                    for _ in range(3):
+                        run()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    for _ in range(reps):
+                        run()
+                    e1.record(st)
+                st.synchronize()
+                res[arm] = e0.elapsed_time(e1) * 1e3 / reps
+            print(json.dumps({"matrix": name, "M": M, "O": O_, "K": K_, "kernel": "k_gemm_tc (tcgen05, 128x256 tiles)",
+                              "us": round(res["tc"], 2), "tflops": round(fl / res["tc"] / 1e6, 1),
+                              "frac_of_peak": round(fl / res["tc"] / 1e6 / tf_peak, 3), "peak_tflops": tf_peak,
+                              "peak_source": src, "cublas_us": round(res["cublas"], 2),
+                              "cublas_tflops": round(fl / res["cublas"] / 1e6, 1),
+                              "kernel_error": G.apus_gcuda_kernel_error()}), flush=True)
+            del w, x, y
+    torch.cuda.empty_cache()
+
+
 def gemv_table(only="all", rows=(4, 1), reps=50):
     """Per-shape GEMV timings of the config-2 step's matrices (profiling aid,
     --gemv-table): back-to-back PDL launches over rotating weight copies
@@ -831,6 +882,9 @@ def main():
     ap.add_argument("--gemv-table", nargs="?", const="all", default=None,
                     help="per-matrix GEMV timings of the config-2 step (profiling aid, one GPU); "
                          "optionally one matrix name")
+    ap.add_argument("--tc-table", nargs="*", type=int, default=None,
+                    help="prefill-chunk linears on the tcgen05 GEMM vs cuBLAS (profiling aid, one GPU); "
+                         "optionally the row counts (default 512 2048)")
     ap.add_argument("--temp", type=float, default=0.0,
                     help="config 2: sampled decode at this temperature (default 0: greedy, the headline)")
     ap.add_argument("--top-p", type=float, default=0.95, help="config 2 sampled decode: nucleus top_p")
@@ -874,6 +928,9 @@ def main():
         raise SystemExit("sampled decode runs on one GPU per sequence (use --mode replicas)")
     if args.gemv_table:
         gemv_table(args.gemv_table)
+        return
+    if args.tc_table is not None:
+        tc_table(tuple(args.tc_table) or (512, 2048))
         return
     if args.config == 2:
         out, W = bench_c2(args, ws, rank)
