@@ -288,7 +288,7 @@ __global__ void k_moe_exchange(MoeDev m, int R, uint16_t *out, long ldo) {
 }
 
 // One warp: publish this rank's argmax keys, signal, wait, reduce over ranks.
-__global__ void k_ep_picks(EpCtx ep, const unsigned long long *keys, int R, int *picks) {
+__global__ void k_ep_picks(EpCtx ep, const unsigned long long *keys, int R, int *picks, int n0, int *picks2) {
     __shared__ int e_sh;
     const int lane = threadIdx.x;
     if (lane == 0) e_sh = *(volatile int *)ep.epoch + 1;
@@ -310,7 +310,8 @@ __global__ void k_ep_picks(EpCtx ep, const unsigned long long *keys, int R, int 
             __ldcv((const unsigned long long *)(ep.peer[p] + ep.off_keys) + (size_t)half * MOE_MAX_R + lane);
         best = k > best ? k : best;
     }
-    picks[lane] = (int)argmax_key_index(best);
+    if (lane < n0) picks[lane] = (int)argmax_key_index(best);
+    else picks2[lane - n0] = (int)argmax_key_index(best);
 }
 
 }  // namespace apus
@@ -400,9 +401,10 @@ static bool ep_connected(const EpCtx &ep) {
 }
 
 int ep_picks_exchange_launch(const EpCtx &ep, const unsigned long long *keys, int R, int *picks,
-                             cudaStream_t st) {
-    if (!ep_connected(ep) || R < 1 || R > MOE_MAX_R || !keys || !picks) return -1;
-    k_ep_picks<<<1, 32, 0, st>>>(ep, keys, R, picks);
+                             cudaStream_t st, int n0, int *picks2) {
+    if (n0 < 0 || n0 > R) n0 = R;
+    if (!ep_connected(ep) || R < 1 || R > MOE_MAX_R || !keys || !picks || (n0 < R && !picks2)) return -1;
+    k_ep_picks<<<1, 32, 0, st>>>(ep, keys, R, picks, n0, picks2);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -66,7 +66,8 @@ int moe_combine_launch(const MoeDev &m, int R, uint16_t *out, long ldo, cudaStre
 // Greedy picks over a vocabulary split across the expert-parallel group: one
 // exchange publishes keys[0..R) (this rank's argmax keys), signals every
 // peer, waits (bounded) for every peer's keys of the same exchange, and
-// writes picks[r] = index of the largest key over all ranks.
+// writes picks[r] = index of the largest key over all ranks (rows r >= n0,
+// when n0 >= 0, go to picks2[r - n0] instead).
 int ep_picks_exchange_launch(const EpCtx &ep, const unsigned long long *keys, int R, int *picks,
-                             cudaStream_t st);
+                             cudaStream_t st, int n0 = -1, int *picks2 = nullptr);
 size_t ep_region_bytes(int dim);

@@ -92,7 +92,8 @@ constexpr int TR = 16;                        // weight rows per tile
 constexpr int CH = APUS_GEMV_CH;              // bytes of one weight row per chunk
 constexpr int STAGE_BYTES = TR * CH;         // one swizzled box (or two tiles' boxes)
 constexpr long KX = 4096;             // elements of K per work item
-constexpr int XMAX = 4 * (2 * (int)KX + 32);   // staged activations: up to 4 rows
+constexpr int XROW = 2 * (int)KX + 32;       // staged bytes of one activation row (at most)
+constexpr int XMAX = 8 * XROW;                 // staged activations: up to 8 rows
 constexpr int THREADS = 288;          // 8 consumer warps + 1 producer warp
 constexpr int PART = 8 * TR;          // floats of one tile partial in scratch: [x col][w row]
 // In shared memory an x column of a warp partial is PSTR floats apart: lane
@@ -192,10 +193,12 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
     using namespace gemvcfg;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *ring = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);   // swizzle atoms: 1 KiB
-    uint16_t *xs = (uint16_t *)(ring + NSTAGE * STAGE_BYTES);
-    float *part = (float *)((uint8_t *)xs + XMAX);
-    uint64_t *full = (uint64_t *)(part + 8 * 2 * SPART);    // [warp][tile][SPART]
+    float *part = (float *)(ring + NSTAGE * STAGE_BYTES);   // [warp][tile][SPART]
+    uint64_t *full = (uint64_t *)(part + 8 * 2 * SPART);
     uint64_t *empty = full + NSTAGE;
+    // staged activations last: the launch sizes this part by its row count,
+    // so launches of up to 4 rows keep two CTAs on an SM
+    uint16_t *xs = (uint16_t *)((uint8_t *)full + 128);
     __shared__ unsigned long long best_sh[8];
     __shared__ int abort_sh;
     __shared__ unsigned char last_sh[256];   // split K: tiles this CTA reduces
@@ -304,9 +307,9 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
                 if (threadIdx.x < 8) xexp_sh[threadIdx.x] = 0;
                 named_bar_sync(1, 256);
             }
-            const int per_row = (int)(klen / 8), total = d.R * per_row;   // <= 8 per thread
+            const int per_row = (int)(klen / 8), total = d.R * per_row;   // <= 16 per thread
             if (!d.x_swiglu) {
-                for (int u0 = 0; u0 < 8; u0 += 4) {    // two batches of 4 loads in flight
+                for (int u0 = 0; u0 * 256 < total; u0 += 4) {    // batches of 4 loads in flight
                     uint4 v[4];
 #pragma unroll
                     for (int u = 0; u < 4; u++) {
@@ -643,9 +646,12 @@ bool gemv_fast_ok(const GemvDesc &d) {
 
 static int g_num_sms = 0;
 
-static size_t gemv_smem() {
+// Dynamic shared memory of a launch staging `rows` activation rows of klen
+// elements: ring, warp partials, barriers (in a 128-byte slot), activations.
+static size_t gemv_smem(int rows, long klen) {
     using namespace gemvcfg;
-    return 1024 + NSTAGE * STAGE_BYTES + XMAX + 8 * 2 * SPART * 4 + 2 * NSTAGE * 8;
+    static_assert(2 * NSTAGE * 8 <= 128, "barrier slot");
+    return 1024 + NSTAGE * STAGE_BYTES + 8 * 2 * SPART * 4 + 128 + (size_t)rows * (size_t)(2 * klen + 32);
 }
 
 // Tensor map of the weights as (128 bytes of k, row, 128-byte k-slab,
@@ -716,12 +722,16 @@ static int wmap_get(const GemvDesc &d, CUtensorMap *out) {
 template <bool FP8>
 static int launch_tma(const GemvDesc &d, cudaStream_t st) {
     static bool attr = false;
-    const size_t sm = gemv_smem();
+    const size_t sm = gemv_smem(d.R, d.K < d.kx ? d.K : d.kx);
     if (!attr) {
-        if (cudaFuncSetAttribute(k_gemv_tma<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
-            != cudaSuccess) return -1;
+        if (cudaFuncSetAttribute(k_gemv_tma<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)gemv_smem(8, gemvcfg::KX)) != cudaSuccess) return -1;
         attr = true;
     }
+    // CTAs an SM holds at this size (228 KiB per SM, 1 KiB reserved per CTA)
+    long per_sm = (long)(233472 / (sm + 1024));
+    if (per_sm > gemvcfg::CTAS_PER_SM) per_sm = gemvcfg::CTAS_PER_SM;
+    if (per_sm < 1) return -1;
     if (!g_num_sms) {
         int dev = 0;
         cudaGetDevice(&dev);
@@ -732,11 +742,11 @@ static int launch_tma(const GemvDesc &d, cudaStream_t st) {
     const long ntile = ((d.O + gemvcfg::TR - 1) / gemvcfg::TR + d.tpi - 1) / d.tpi;   // work items
     long grid;
     if (d.gexpert) {
-        grid = (long)gemvcfg::CTAS_PER_SM * g_num_sms;
+        grid = per_sm * g_num_sms;
         if (grid > (long)d.gmax * ntile) grid = (long)d.gmax * ntile;
     } else {
         const long nks = (d.K + d.kx - 1) / d.kx;
-        long per_ks = ((long)gemvcfg::CTAS_PER_SM * g_num_sms) / nks;   // CTAs per k-range
+        long per_ks = (per_sm * g_num_sms) / nks;   // CTAs per k-range
         if (per_ks < 1) per_ks = 1;
         if (per_ks > ntile) per_ks = ntile;
         grid = per_ks * nks;

@@ -47,9 +47,14 @@ __global__ void k_mtp_commit(Ctl *c, int R) {
     if (threadIdx.x == 0) c->mtp_n += R;
 }
 
-__global__ void k_extract_picks(const unsigned long long *keys, int R, int *dst) {
+// rows r < n0 -> dst[r], rows r >= n0 -> dst2[r - n0]
+__global__ void k_extract_picks(const unsigned long long *keys, int R, int *dst, int n0, int *dst2) {
     pdl_launch_dependents();
-    if ((int)threadIdx.x < R) dst[threadIdx.x] = (int)argmax_key_index(keys[threadIdx.x]);
+    const int r = threadIdx.x;
+    if (r >= R) return;
+    const int v = (int)argmax_key_index(keys[r]);
+    if (r < n0) dst[r] = v;
+    else dst2[r - n0] = v;
 }
 
 // Step start.  A step whose rows would pass the capacity freezes the
@@ -841,7 +846,9 @@ extern "C" size_t apus_gcuda_model_pos(const ApusGcudaModel *m) {
 // lm_head over `yn` rows with the fused greedy pick into picks[R] (and the
 // BF16 logits when want_logits).
 // The argmax keys S.amax were zeroed by the norm that produced yn.
-static int lm_head(ApusGcudaModel *m, const uint16_t *yn, int R, int *picks, bool want_logits) {
+static int lm_head(ApusGcudaModel *m, const uint16_t *yn, int R, int *picks, bool want_logits, int n0 = -1,
+                   int *picks2 = nullptr) {
+    if (n0 < 0 || n0 > R) n0 = R;
     const Dims &D = m->D;
     GemvDesc g{};
     g.W = m->head; g.x = yn; g.ldx = D.d; g.R = R; g.O = m->vn; g.K = D.d; g.fp8 = 0;
@@ -855,16 +862,17 @@ static int lm_head(ApusGcudaModel *m, const uint16_t *yn, int R, int *picks, boo
     if (gemv_launch(g, m->st)) return -1;
     if (m->ep_world > 1) {
         // the largest key over every rank's slice: publish, barrier, reduce
-        if (ep_picks_exchange_launch(m->ep, m->S.amax, R, picks, m->st)) return -1;
+        if (ep_picks_exchange_launch(m->ep, m->S.amax, R, picks, m->st, n0, picks2)) return -1;
         return 0;
     }
-    k_extract_picks<<<1, 32, 0, m->st>>>(m->S.amax, R, picks);
+    k_extract_picks<<<1, 32, 0, m->st>>>(m->S.amax, R, picks, n0, picks2);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 // Main model over R rows at positions ctl->pos.., not committed.  yn_out
 // (device, [R][d]) receives the post-norm rows.
-static int main_forward(ApusGcudaModel *m, const int32_t *ids_dev, int R, uint16_t *yn_out, bool want_logits) {
+static int main_forward(ApusGcudaModel *m, const int32_t *ids_dev, int R, uint16_t *yn_out, bool want_logits,
+                        bool head = true) {
     const Dims &D = m->D;
     Scratch &S = m->S;
     cudaStream_t st = m->st;
@@ -899,13 +907,15 @@ static int main_forward(ApusGcudaModel *m, const int32_t *ids_dev, int R, uint16
     }
     if (h != S.h4) cudaMemcpyAsync(S.h4, h, (size_t)R * D.hc * D.d * 2, cudaMemcpyDeviceToDevice, st);
     if (head_norm_launch(D, S.h4, m->norm, R, yn_out, S.amax, st)) return -1;
+    if (!head) return 0;      // the caller runs the lm_head (keys S.amax[0..R) are zeroed)
     return lm_head(m, yn_out, R, m->ctl->picks, want_logits);
 }
 
 // MTP block (c/gmtp.h:471-541) over R pairs (ids, prev_h rows) whose DSA
 // cache rows start at *base_n; out_h -> S.oh, picks -> ctl->mtp_picks.
 static int mtp_forward(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t *prev_h, int R, const int *base_n,
-                       bool want_logits) {
+                       bool want_logits, uint16_t *out_h = nullptr, unsigned long long *keys = nullptr,
+                       bool head = true) {
     const Dims &D = m->D;
     Scratch &S = m->S;
     cudaStream_t st = m->st;
@@ -930,11 +940,13 @@ static int mtp_forward(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t
         if (norm_seg_launch(&sg, 1, R, D.eps, nullptr, st)) return -1;
     }
     if (moe_forward_launch(W.moe, S.mxn, d, R, S.sub, d, nullptr, st)) return -1;
+    if (!out_h) out_h = S.oh;
     {   // x = bf16(x + moe); shared_head.norm; zero the lm_head argmax keys
-        NormSeg sg = {S.mx, d, nullptr, S.sub, d, m->shared_norm, d, S.oh, d};
-        if (norm_seg_launch(&sg, 1, R, D.eps, S.amax, st)) return -1;
+        NormSeg sg = {S.mx, d, nullptr, S.sub, d, m->shared_norm, d, out_h, d};
+        if (norm_seg_launch(&sg, 1, R, D.eps, keys ? keys : S.amax, st)) return -1;
     }
-    return lm_head(m, S.oh, R, m->ctl->mtp_picks, want_logits);
+    if (!head) return 0;      // the caller runs the lm_head
+    return lm_head(m, out_h, R, m->ctl->mtp_picks, want_logits);
 }
 
 static bool ids_ok(const ApusGcudaModel *m, const int32_t *ids, size_t n, const char *what) {
@@ -1071,18 +1083,30 @@ static int spec_step(ApusGcudaModel *m, int Dp) {
     const int d = D.d;
     cudaStream_t st = m->st;
     const bool smp = m->temp > 0.0f;
+    // The verify rows' lm_head waits for the MTP replay so that both row
+    // sets share one stream of the 1.27 GB head (the replay needs the verify
+    // rows' hidden states, not their picks): rows [0, Dp) of S.yn are the
+    // verify rows, rows [Dp, 2 Dp) the replay's shared-head outputs.
+    const bool one_head = 2 * Dp <= MAXR;
+    uint16_t *mtp_out = one_head ? m->S.yn + (size_t)Dp * d : m->S.oh;
     k_spec_begin<<<1, 32, 0, st>>>(m->ctl, Dp, m->cap, m->ids);
-    if (main_forward(m, m->ids, Dp, m->S.yn, smp)) return -1;
+    if (main_forward(m, m->ids, Dp, m->S.yn, smp, !one_head)) return -1;
+    // MTP replay of the D candidate pairs (rows past the accepted prefix are
+    // overwritten by the chain / the next replay)
+    k_replay_rows<<<(Dp * d + 255) / 256, 256, 0, st>>>(m->hcarry, m->S.yn, Dp, d, m->mtp_rows);
+    if (one_head) {
+        if (mtp_forward(m, m->ids, m->mtp_rows, Dp, &m->ctl->mtp_n, false, mtp_out, m->S.amax + Dp, false))
+            return -1;
+        if (lm_head(m, m->S.yn, 2 * Dp, m->ctl->picks, smp, Dp, m->ctl->mtp_picks)) return -1;
+    } else if (mtp_forward(m, m->ids, m->mtp_rows, Dp, &m->ctl->mtp_n, false)) {
+        return -1;
+    }
     // sampled: every verify row's own draw replaces its argmax pick; the walk
     // consumes the draws of the rows it reaches (c/gmtp.h:800-831)
     if (smp && sample_launch(m->S.logits, D.V, D.V, Dp, m->temp, m->top_p, &m->ctl->rng_s, 0, m->ctl->picks, st))
         return -1;
-    // MTP replay of the D candidate pairs (rows past the accepted prefix are
-    // overwritten by the chain / the next replay)
-    k_replay_rows<<<(Dp * d + 255) / 256, 256, 0, st>>>(m->hcarry, m->S.yn, Dp, d, m->mtp_rows);
-    if (mtp_forward(m, m->ids, m->mtp_rows, Dp, &m->ctl->mtp_n, false)) return -1;
     k_spec_walk<<<1, 32, 0, st>>>(m->ctl, Dp, m->log, m->log_cap);
-    k_copy_sel_row<<<(d + 255) / 256, 256, 0, st>>>(m->S.oh, m->ctl, d, m->hmtp);
+    k_copy_sel_row<<<(d + 255) / 256, 256, 0, st>>>(mtp_out, m->ctl, d, m->hmtp);
     k_copy_sel_row<<<(d + 255) / 256, 256, 0, st>>>(m->S.yn, m->ctl, d, m->hcarry);
     if (draft_chain(m)) return -1;
     k_force<<<1, 32, 0, st>>>(m->ctl, m->truth, m->depth, D.V);

@@ -801,7 +801,7 @@ def tc_table(rows=(512, 2048), reps=20):
     torch.cuda.empty_cache()
 
 
-def gemv_table(only="all", rows=(4, 1), reps=50):
+def gemv_table(only="all", rows=(8, 4, 1), reps=50):
     """Per-shape GEMV timings of the config-2 step's matrices (profiling aid,
     --gemv-table): back-to-back PDL launches over rotating weight copies
     (>= 512 MB per shape, so every launch streams from HBM), CUDA events on
