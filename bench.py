@@ -677,20 +677,29 @@ def bench_c2(args, ws, rank, W=None):
                              "note": "algorithmic bytes per step / device step time"},
            "gpu_launches": int(c1["graph_kernels"]) * args.steps,
            "clocks": clk.summary()}
-    # the dominant kernel: the lm_head GEMV (5 launches per step, ~1/3 of it)
-    us, hb = lm_head_gemv_time(kw, depth, ws if ep else 1)
+    # the dominant kernel: the lm_head GEMV, ~1/3 of the step.  Per step one
+    # launch over the verify rows and the MTP replay rows together (2*depth
+    # rows) and depth-1 one-row launches of the draft chain; timed in that mix
+    rows_main = 2 * depth if 2 * depth <= 8 else depth
+    n_one = depth - 1 if rows_main == 2 * depth else depth
+    us_m, hb_m = lm_head_gemv_time(kw, rows_main, ws if ep else 1)
+    us_1, hb_1 = lm_head_gemv_time(kw, 1, ws if ep else 1)
+    us, hb = us_m + n_one * us_1, hb_m + n_one * hb_1
     # DRAM bytes of one full-vocabulary launch from the committed ncu capture;
     # a vocabulary slice moves its share of them
     traffic = profile_value("lm_head_gemv_k_gemv_tma.md", "dram_bytes_per_launch")
     if traffic is not None and ep:
         traffic = round(traffic / ws)
     hgbs = hb / us / 1e3
+    nl = 1 + n_one
     out["roofline"] = {"bound": "hbm", "kernel": f"k_gemv_tma<false> lm_head (BF16 {-(-kw['vocab_size'] // (ws if ep else 1))}"
                                                   f"x{kw['hidden_size']} per rank, fused argmax)",
                        "achieved": round(hgbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(hgbs / hbm, 4),
                        "traffic": traffic,
-                       "algo_bytes_per_launch": hb, "avg_launch_us": round(us, 2), "peak_source": src,
-                       "launches_per_step": 5}
+                       "algo_bytes_per_launch": round(hb / nl), "avg_launch_us": round(us / nl, 2),
+                       "peak_source": src, "launches_per_step": nl,
+                       "launch_mix": {f"{rows_main}_rows_us": round(us_m, 2), "1_row_us": round(us_1, 2),
+                                      "1_row_launches": n_one}}
     if args.quick:
         m.close()
         return out, W
