@@ -514,7 +514,8 @@ def c2_prompt(kw, seed):
 def c2_algo_bytes(kw, depth, n_ctx, moe_problems, world=1):
     """Algorithmic HBM bytes of one speculative step: every weight byte the
     step's forwards must read once (main forward over `depth` rows, the MTP
-    replay and depth-1 chain forwards), the realised MoE expert union
+    replay and depth-1 chain forwards; the replay and the verify rows share
+    one pass over the lm_head when 2*depth <= 8), the realised MoE expert union
     (`moe_problems` expert GEMV pairs, shared expert included, counted on the
     device), the KDA state read + final write, the DSA K/V and pool-key rows
     visible at context n_ctx, and the new cache rows.  Checkpoint copies and
@@ -544,6 +545,8 @@ def c2_algo_bytes(kw, depth, n_ctx, moe_problems, world=1):
     main += head
     mtp_fwd = lambda rows, n: 2 * d * d * 2 + dsa(rows, n) + router + head
     mtp = mtp_fwd(depth, n_ctx) + sum(mtp_fwd(1, n_ctx + i) for i in range(depth - 1))
+    if 2 * depth <= 8:      # the replay rows share the verify rows' pass over the head
+        mtp -= head
     n_moe_calls = L + 1 + (depth - 1)
     return main + mtp + moe_problems * expert, n_moe_calls
 
