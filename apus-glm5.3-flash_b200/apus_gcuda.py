@@ -57,6 +57,8 @@ apus_gcuda_bf16_gemm_argmax_static_dev = _fn("apus_gcuda_bf16_gemm_argmax_static
                                              _sz, _sz, _sz, _vp)
 apus_gcuda_sample_rows_dev = _fn("apus_gcuda_sample_rows_dev", _i, _vp, _sz, _sz, _sz, C.c_float, C.c_float,
                                  _u64, _vp, _vp)
+apus_gcuda_kda_chunk_dev = _fn("apus_gcuda_kda_chunk_dev", _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz,
+                               _vp)
 
 _f = C.c_float
 apus_gcuda_moe_new = _fn("apus_gcuda_moe_new", _vp, _i, _i, _sz, _sz, _f, _f, _i)

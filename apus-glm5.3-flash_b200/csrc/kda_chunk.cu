@@ -1,0 +1,224 @@
+// kda_chunk.cu — the chunked KDA (delta-rule) prefill core on the device
+// (c/gkda.h:350-539 apus_gkda_chunk): a prompt of s tokens is processed in
+// chunks of 64 rows per head, carrying the fp32 state S [D][D] from chunk to
+// chunk, instead of stepping the recurrence token by token.
+//
+// Per head and chunk (rows past s are zero; the in-chunk cumulative gate
+// carries the last real row's value into them, as the reference):
+//   q, k l2-normalised (numpy pairwise sum of squares, sqrt, divide), q scaled
+//   by D^-1/2; gc = in-chunk cumulative sum of g (ascending);
+//   attn[i][j<i] = -sum_d (k_i beta_i)_d k_j,d e^(gc_i,d - gc_j,d); the UT
+//   transform row by row, then + I;
+//   value = attn (v beta); kcd = attn (k beta e^gc);
+//   v_new = value - kcd S; inter = (q e^gc) S;
+//   intra[i][j<=i] = sum_d q_i,d k_j,d e^(gc_i,d - gc_j,d);
+//   out = bf16(inter + intra v_new);
+//   S = S e^(gc_last) + sum_j (k_j e^(gc_last - gc_j)) v_new_j.
+// Every sum runs in the reference's order (ascending, from +0) and every
+// product keeps its operand order, so the only differences from the
+// reference are expf's last bits (CUDA's against libm's).
+//
+// Layout: CTA (h, p) owns value columns [32p, 32p + 32) of head h, for its
+// slice of v, v_new, the outputs and S; the four CTAs of a head each compute
+// the chunk's attn / intra / kcd (shared-memory-resident, rows padded by one
+// float so a warp's lanes hit distinct banks).  No CTA waits on another.
+#include "common.cuh"
+#include "gcuda.h"
+#include "../../include/apus_gcuda.h"
+
+namespace apus {
+
+constexpr int KC_C = 64, KC_D = 128, KC_SPLIT = 4, KC_DV = KC_D / KC_SPLIT, KC_T = 256;
+constexpr int KC_PD = KC_D + 1, KC_PV = KC_DV + 1, KC_PC = KC_C + 1;
+
+struct KcSmem {
+    float qp[KC_C * KC_D];       // q normalised and scaled; later q e^gc
+    float kp[KC_C * KC_PD];      // k normalised (rows padded: read down a column)
+    float gc[KC_C * KC_PD];      // in-chunk cumulative gate (padded likewise)
+    float kx[KC_C * KC_D];       // k beta e^gc, later k e^(gc_last - gc)
+    float kcd[KC_C * KC_D];      // attn (k beta e^gc)
+    float attn[KC_C * KC_PC];
+    float intra[KC_C * KC_PC];
+    float vp[KC_C * KC_PV];      // v beta (this CTA's columns)
+    float val[KC_C * KC_PV];     // UT transform row scratch, then value, then v_new
+    float S[KC_D * KC_PV];       // this CTA's columns of the state
+    float beta[KC_C];
+};
+static_assert(sizeof(KcSmem) <= 232448, "shared memory");
+
+__global__ void __launch_bounds__(KC_T) k_kda_chunk(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                                                    const float *g, const uint16_t *beta, float *S,
+                                                    uint16_t *out, int s, int H, float qscale) {
+    extern __shared__ __align__(16) unsigned char kc_dyn[];
+    KcSmem &sm = *reinterpret_cast<KcSmem *>(kc_dyn);
+    const int h = blockIdx.x / KC_SPLIT, c0 = (blockIdx.x % KC_SPLIT) * KC_DV;
+    const int tid = threadIdx.x;
+    const size_t hd = (size_t)H * KC_D;
+    float *Sh = S + (size_t)h * KC_D * KC_D;
+    for (int e = tid; e < KC_D * KC_DV; e += KC_T) {
+        const int m = e / KC_DV, c = e % KC_DV;
+        sm.S[m * KC_PV + c] = Sh[(size_t)m * KC_D + c0 + c];
+    }
+    const int nch = (s + KC_C - 1) / KC_C;
+    for (int n = 0; n < nch; n++) {
+        __syncthreads();
+        // ---- rows of the chunk (zero past s)
+        for (int e = tid; e < KC_C * KC_D; e += KC_T) {
+            const int i = e / KC_D, d = e % KC_D, t = n * KC_C + i;
+            const bool ok = t < s;
+            const size_t off = (size_t)t * hd + (size_t)h * KC_D + d;
+            sm.qp[i * KC_D + d] = ok ? bf16_f32(q[off]) : 0.0f;
+            sm.kp[i * KC_PD + d] = ok ? bf16_f32(k[off]) : 0.0f;
+            sm.gc[i * KC_PD + d] = ok ? g[off] : 0.0f;
+        }
+        if (tid < KC_C) {
+            const int t = n * KC_C + tid;
+            sm.beta[tid] = t < s ? bf16_f32(beta[(size_t)t * H + h]) : 0.0f;
+        }
+        __syncthreads();
+        for (int e = tid; e < KC_C * KC_DV; e += KC_T) {
+            const int i = e / KC_DV, c = e % KC_DV, t = n * KC_C + i;
+            const float vv = t < s ? bf16_f32(v[(size_t)t * hd + (size_t)h * KC_D + c0 + c]) : 0.0f;
+            sm.vp[i * KC_PV + c] = vv * sm.beta[i];
+        }
+        // l2 norms (c/gkda.h:263-273): thread r < 2C normalises one real row
+        if (tid < 2 * KC_C) {
+            const int i = tid % KC_C;
+            float *row = tid < KC_C ? sm.qp + i * KC_D : sm.kp + i * KC_PD;
+            if (n * KC_C + i < s) {
+                float sq[KC_D];
+#pragma unroll 8
+                for (int d = 0; d < KC_D; d++) sq[d] = row[d] * row[d];
+                const float root = __fsqrt_rn(pw_sum_leaf(sq, KC_D) + 1e-6f);
+                for (int d = 0; d < KC_D; d++) row[d] = __fdiv_rn(row[d], root);
+                if (tid < KC_C)
+                    for (int d = 0; d < KC_D; d++) row[d] = row[d] * qscale;
+            }
+        }
+        // in-chunk cumulative gate, ascending
+        if (tid < KC_D)
+            for (int i = 1; i < KC_C; i++)
+                sm.gc[i * KC_PD + tid] = sm.gc[(i - 1) * KC_PD + tid] + sm.gc[i * KC_PD + tid];
+        __syncthreads();
+        // ---- attn (strictly lower) and intra (lower with the diagonal), one decay each
+        for (int e = tid; e < KC_C * KC_C; e += KC_T) {
+            const int i = e / KC_C, j = e % KC_C;
+            float a = 0.0f, b = 0.0f;
+            if (j <= i) {
+                const float bi = sm.beta[i];
+                const float *qi = sm.qp + i * KC_D, *ki = sm.kp + i * KC_PD, *kj = sm.kp + j * KC_PD;
+                const float *gi = sm.gc + i * KC_PD, *gj = sm.gc + j * KC_PD;
+                for (int d = 0; d < KC_D; d++) {
+                    const float dec = expf(gi[d] - gj[d]);
+                    a += ((ki[d] * bi) * kj[d]) * dec;
+                    b += (qi[d] * kj[d]) * dec;
+                }
+            }
+            sm.attn[i * KC_PC + j] = j < i ? -a : 0.0f;
+            sm.intra[i * KC_PC + j] = j <= i ? b : 0.0f;
+        }
+        // k beta e^gc for kcd
+        for (int e = tid; e < KC_C * KC_D; e += KC_T) {
+            const int j = e / KC_D, d = e % KC_D;
+            sm.kx[j * KC_D + d] = (sm.kp[j * KC_PD + d] * sm.beta[j]) * expf(sm.gc[j * KC_PD + d]);
+        }
+        __syncthreads();
+        // ---- UT transform: row i += row i . attn[:i, :i], ascending i; the
+        // terms m <= j are zero products, so the sum starts at m = j + 1
+        for (int i = 1; i < KC_C; i++) {
+            if (tid < i) {
+                const int j = tid;
+                float a = 0.0f;
+                for (int m = j + 1; m < i; m++) a += sm.attn[i * KC_PC + m] * sm.attn[m * KC_PC + j];
+                sm.val[j] = a;
+            }
+            __syncthreads();
+            if (tid < i) sm.attn[i * KC_PC + tid] = sm.attn[i * KC_PC + tid] + sm.val[tid];
+            __syncthreads();
+        }
+        if (tid < KC_C) sm.attn[tid * KC_PC + tid] = sm.attn[tid * KC_PC + tid] + 1.0f;
+        __syncthreads();
+        // ---- value = attn (v beta); kcd = attn (k beta e^gc)
+        for (int e = tid; e < KC_C * KC_DV; e += KC_T) {
+            const int i = e / KC_DV, c = e % KC_DV;
+            float a = 0.0f;
+            for (int j = 0; j < KC_C; j++) a += sm.attn[i * KC_PC + j] * sm.vp[j * KC_PV + c];
+            sm.val[i * KC_PV + c] = a;
+        }
+        for (int e = tid; e < KC_C * KC_D; e += KC_T) {
+            const int i = e / KC_D, d = e % KC_D;
+            float a = 0.0f;
+            for (int j = 0; j < KC_C; j++) a += sm.attn[i * KC_PC + j] * sm.kx[j * KC_D + d];
+            sm.kcd[i * KC_D + d] = a;
+        }
+        __syncthreads();
+        // q e^gc (in place) and k e^(gc_last - gc) (over kx)
+        for (int e = tid; e < KC_C * KC_D; e += KC_T) {
+            const int i = e / KC_D, d = e % KC_D;
+            sm.qp[i * KC_D + d] = sm.qp[i * KC_D + d] * expf(sm.gc[i * KC_PD + d]);
+            sm.kx[i * KC_D + d] = sm.kp[i * KC_PD + d] * expf(sm.gc[(KC_C - 1) * KC_PD + d] - sm.gc[i * KC_PD + d]);
+        }
+        __syncthreads();
+        // ---- v_new = value - kcd S
+        for (int e = tid; e < KC_C * KC_DV; e += KC_T) {
+            const int i = e / KC_DV, c = e % KC_DV;
+            float a = 0.0f;
+            for (int d = 0; d < KC_D; d++) a += sm.kcd[i * KC_D + d] * sm.S[d * KC_PV + c];
+            sm.val[i * KC_PV + c] = sm.val[i * KC_PV + c] - a;
+        }
+        __syncthreads();
+        // ---- out = bf16(inter + intra v_new) for the real rows, inter = (q e^gc) S
+        for (int e = tid; e < KC_C * KC_DV; e += KC_T) {
+            const int i = e / KC_DV, c = e % KC_DV, t = n * KC_C + i;
+            if (t >= s) continue;
+            float b = 0.0f;
+            for (int d = 0; d < KC_D; d++) b += sm.qp[i * KC_D + d] * sm.S[d * KC_PV + c];
+            float a = 0.0f;
+            for (int j = 0; j < KC_C; j++) a += sm.intra[i * KC_PC + j] * sm.val[j * KC_PV + c];
+            out[(size_t)t * hd + (size_t)h * KC_D + c0 + c] = bf16_bits(b + a);
+        }
+        __syncthreads();     // the state update below overwrites S
+        // ---- S = S e^(gc_last) + sum_j (k_j e^(gc_last - gc_j)) v_new_j
+        for (int e = tid; e < KC_D * KC_DV; e += KC_T) {
+            const int m = e / KC_DV, c = e % KC_DV;
+            const float egl = expf(sm.gc[(KC_C - 1) * KC_PD + m]);
+            float a = 0.0f;
+            for (int j = 0; j < KC_C; j++) a += sm.kx[j * KC_D + m] * sm.val[j * KC_PV + c];
+            sm.S[m * KC_PV + c] = sm.S[m * KC_PV + c] * egl + a;
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < KC_D * KC_DV; e += KC_T) {
+        const int m = e / KC_DV, c = e % KC_DV;
+        Sh[(size_t)m * KC_D + c0 + c] = sm.S[m * KC_PV + c];
+    }
+}
+
+}  // namespace apus
+using namespace apus;
+
+int kda_chunk_launch(const uint16_t *q, const uint16_t *k, const uint16_t *v, const float *g, const uint16_t *beta,
+                     float *S, uint16_t *out, int s, int H, int D, cudaStream_t st) {
+    if (D != KC_D || H < 1 || s < 0) {
+        gcuda_set_error("kda_chunk: head dim %d (only %d), %d heads", D, KC_D, H);
+        return -1;
+    }
+    if (s == 0) return 0;
+    static bool attr = false;
+    if (!attr) {
+        if (gcuda_check(cudaFuncSetAttribute(k_kda_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sizeof(KcSmem)), "kda_chunk smem"))
+            return -1;
+        attr = true;
+    }
+    const float qscale = (float)pow((double)D, -0.5);
+    k_kda_chunk<<<H * KC_SPLIT, KC_T, sizeof(KcSmem), st>>>(q, k, v, g, beta, S, out, s, H, qscale);
+    return gcuda_check(cudaGetLastError(), "kda_chunk launch");
+}
+
+extern "C" int apus_gcuda_kda_chunk_dev(const uint16_t *q, const uint16_t *k, const uint16_t *v, const float *g,
+                                        const uint16_t *beta, float *S, uint16_t *out, size_t s, size_t H,
+                                        size_t D, void *stream) {
+    if (s > (size_t)1 << 30 || H > 4096) { gcuda_set_error("kda_chunk: %zu rows, %zu heads", s, H); return -1; }
+    return kda_chunk_launch(q, k, v, g, beta, S, out, (int)s, (int)H, (int)D, (cudaStream_t)stream);
+}

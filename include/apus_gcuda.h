@@ -132,6 +132,14 @@ int apus_gcuda_bf16_gemm_argmax_static_dev(const uint16_t *w, const uint16_t *x,
  * 1e-7 of a cumulative-mass boundary).  n <= 256000, ld >= n; ids [rows]. */
 int apus_gcuda_sample_rows_dev(const uint16_t *logits, size_t rows, size_t ld, size_t n, float temp,
                                float top_p, uint64_t rng_state, int32_t *out, void *stream);
+/* c/gkda.h:140-143 apus_gkda_chunk (the chunked KDA prefill core, chunks of
+ * 64 rows): q/k/v [s, H*D] BF16 codes (post-conv), g [s, H*D] fp32, beta
+ * [s, H] BF16 codes, S [H*D*D] fp32 in/out, out [s, H*D] BF16 codes, all
+ * device pointers.  Each head's sums run in the reference's order; results
+ * differ from it only through expf's last bits.  D must be 128. */
+int apus_gcuda_kda_chunk_dev(const uint16_t *q, const uint16_t *k, const uint16_t *v, const float *g,
+                             const uint16_t *beta, float *S, uint16_t *out, size_t s, size_t H, size_t D,
+                             void *stream);
 
 #ifdef __cplusplus
 }

@@ -54,6 +54,8 @@ if REF is not None:
     _decl(REF, "apus_ref_threads", _i)
     _decl(REF, "apus_sample_logits_u", _i, _vp, _sz, _f, _f, C.c_double, _vp)
     _decl(REF, "apus_sample", _i, _vp, _sz, _f, _f, _vp, _vp)
+    _decl(REF, "apus_gkda_chunk", None, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz)
+    _decl(REF, "apus_gkda_recurrent", None, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz)
 
 
 def p(a):
