@@ -219,6 +219,11 @@ struct ApusGcudaModel {
     cudaGraphExec_t gexec = nullptr;
     int use_graph = 0;
     size_t graph_kernels = 0;
+    // the control block as the last synchronous step read it back, valid
+    // while no other work has touched the control block since (ctl_epoch
+    // counts the calls that do)
+    Ctl ctl_cache{};
+    uint64_t ctl_epoch = 0, cache_epoch = ~0ull;
     // expert / vocabulary parallelism (one process per GPU)
     int ep_rank = 0, ep_world = 1;
     EpCtx ep{};
@@ -808,6 +813,7 @@ extern "C" int apus_gcuda_model_init_random(ApusGcudaModel *m, uint64_t seed) {
 
 extern "C" int apus_gcuda_model_reset(ApusGcudaModel *m) {
     const Dims &D = m->D;
+    m->ctl_epoch++;
     cudaStreamSynchronize(m->st);
     for (int l = 0; l < D.L; l++) {
         if (!m->L[l].is_dsa) {
@@ -877,6 +883,7 @@ static int main_forward(ApusGcudaModel *m, const int32_t *ids_dev, int R, uint16
     Scratch &S = m->S;
     cudaStream_t st = m->st;
     m->n_main_fwd++;
+    m->ctl_epoch++;
     if (k_embed_launch(m->embed, ids_dev, R, D.d, D.hc, S.h4, st)) return -1;
     uint16_t *h = S.h4, *h2 = S.h4b;
     auto stop = [&](int l, int stage) { return l == m->dbg_layer && stage == m->dbg_stage; };
@@ -922,6 +929,7 @@ static int mtp_forward(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t
     const LayerW &W = m->L[D.L];
     const int d = D.d;
     m->n_mtp_fwd++;
+    m->ctl_epoch++;
     // eh = [enorm(embed[id]) | hnorm(prev_h)], the embed rows gathered by id
     {
         NormSeg sg[2] = {{m->embed, d, ids_dev, nullptr, 0, m->enorm, d, S.eh, 2L * d},
@@ -1147,6 +1155,7 @@ static int graph_build(ApusGcudaModel *m) {
 
 extern "C" int apus_gcuda_gspec_step_async(ApusGcudaModel *m) {
     if (!m->has_mtp) { gcuda_set_error("gspec: model has no MTP block loaded"); return -1; }
+    m->ctl_epoch++;
     if (!m->use_graph) return spec_step(m, m->depth);
     if (!m->gexec && graph_build(m)) return -1;
     return gcuda_check(cudaGraphLaunch(m->gexec, m->st), "graph launch");
@@ -1169,13 +1178,21 @@ extern "C" int apus_gcuda_model_counters(ApusGcudaModel *m, uint64_t *out, size_
     return 0;
 }
 
+// One synchronous step: the capacity check uses the control block the
+// previous synchronous step read back (when nothing has touched it since),
+// a full-depth step replays the captured graph when graphs are on, and the
+// one read-back per step returns the emitted tokens.
 extern "C" int apus_gcuda_gspec_step(ApusGcudaModel *m, int *out, int cap) {
     if (!m->has_mtp || cap < m->depth + 1) return 0;
-    Ctl c = read_ctl(m);
+    Ctl c = m->cache_epoch == m->ctl_epoch ? m->ctl_cache : read_ctl(m);
     const int De = m->cap - c.pos < m->depth ? m->cap - c.pos : m->depth;
     if (c.err || De <= 0) return 0;
-    if (spec_step(m, De)) { fail_ctl(m, "gspec_step"); return 0; }
+    const int rc = (De == m->depth && m->use_graph) ? apus_gcuda_gspec_step_async(m) : spec_step(m, De);
+    m->ctl_epoch++;
+    if (rc) { fail_ctl(m, "gspec_step"); return 0; }
     c = read_ctl(m);
+    m->ctl_cache = c;
+    m->cache_epoch = m->ctl_epoch;
     for (int i = 0; i < c.n_emitted; i++) out[i] = c.emitted[i];
     return c.n_emitted;
 }
@@ -1196,6 +1213,7 @@ extern "C" int apus_gcuda_gspec_stats(ApusGcudaModel *m, uint64_t *o) {
 
 extern "C" int apus_gcuda_gspec_force(ApusGcudaModel *m, const int32_t *truth, size_t n, size_t base, double p,
                                       uint64_t seed) {
+    m->ctl_epoch++;
     Ctl c = read_ctl(m);
     if (!truth) {
         c.force_on = 0;
@@ -1269,6 +1287,7 @@ extern "C" int apus_gcuda_gspec_sampling(ApusGcudaModel *m, float temp, float to
         return -1;
     }
     if (temp > 0.0f && sample_prepare(m->D.V)) return -1;
+    m->ctl_epoch++;
     m->temp = temp;
     m->top_p = top_p;
     Ctl c = read_ctl(m);
