@@ -254,3 +254,29 @@ def test_errors(gcuda, tiny):
     bad = dict(kw, hc_mult=9)
     with pytest.raises(gcuda.GcudaError):
         gcuda.GModel(gcuda.make_config(**bad))
+
+
+def test_sync_steps_replay_graph(gcuda, tiny):
+    """With graphs on, the synchronous step replays the captured step; mixing
+    synchronous and enqueued steps (the control block read back by the
+    previous synchronous step is stale then) keeps the same stream."""
+    kw, W = tiny
+    a = gpu_model(gcuda, kw, W, depth=4)
+    a.spec_prefill(PROMPT)
+    eager = []
+    for _ in range(9):
+        eager += a.spec_step()
+    b = gpu_model(gcuda, kw, W, depth=4)
+    b.use_graph(True)
+    b.spec_prefill(PROMPT)
+    got = []
+    for i in range(9):
+        if i == 4:
+            b.spec_step_async()
+            got = b.emitted()
+        else:
+            got += b.spec_step()
+    assert got == eager
+    assert b.emitted() == eager
+    assert b.counters()["graph_kernels"] > 20
+    assert b.digest() == a.digest()
