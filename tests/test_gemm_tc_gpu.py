@@ -46,7 +46,7 @@ def run(gcuda, W, x, S=None, f32=False):
 
 
 SHAPES = [(64, 256, 512), (128, 128, 64), (200, 300, 136), (256, 1024, 128), (512, 4096, 4096),
-          (130, 2048, 8192), (1000, 96, 1024)]
+          (130, 2048, 8192), (1000, 96, 1024), (128, 4096, 4096), (96, 1536, 4096)]
 
 
 @pytest.mark.parametrize("shape", SHAPES)
@@ -94,3 +94,15 @@ def test_small_row_counts_stay_on_the_gemv(gcuda):
     got, launches = run(gcuda, w, x)
     assert launches == 8
     assert_close_rows(got, exact_bf16(w, x)[0])
+
+
+def test_repeatable(gcuda):
+    """Repeated calls are bitwise equal (a fixed tile plan and summation
+    order)."""
+    rng = np.random.default_rng(8)
+    w = O.bf16_of((rng.standard_normal((2048, 4096)) * 0.02).astype(np.float32))
+    x = O.bf16_of(rng.standard_normal((128, 4096)).astype(np.float32))
+    a, _ = run(gcuda, w, x)
+    b, _ = run(gcuda, w, x)
+    assert np.array_equal(a, b)
+    assert_close_rows(a, exact_bf16(w, x)[0])
