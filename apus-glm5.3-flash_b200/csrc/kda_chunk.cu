@@ -32,11 +32,11 @@ constexpr int KC_C = 64, KC_D = 128, KC_SPLIT = 4, KC_DV = KC_D / KC_SPLIT, KC_T
 constexpr int KC_PD = KC_D + 1, KC_PV = KC_DV + 1, KC_PC = KC_C + 1;
 
 struct KcSmem {
-    float qp[KC_C * KC_D];       // q normalised and scaled; later q e^gc
-    float kp[KC_C * KC_PD];      // k normalised (rows padded: read down a column)
-    float gc[KC_C * KC_PD];      // in-chunk cumulative gate (padded likewise)
+    float qp[KC_C * KC_PD];      // q normalised and scaled; later q e^gc (rows padded:
+    float kp[KC_C * KC_PD];      // k normalised                             read down a column)
+    float gc[KC_C * KC_PD];      // in-chunk cumulative gate
     float kx[KC_C * KC_D];       // k beta e^gc, later k e^(gc_last - gc)
-    float kcd[KC_C * KC_D];      // attn (k beta e^gc)
+    float kcd[KC_C * KC_PD];     // attn (k beta e^gc)
     float attn[KC_C * KC_PC];
     float intra[KC_C * KC_PC];
     float vp[KC_C * KC_PV];      // v beta (this CTA's columns)
@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(KC_T) k_kda_chunk(const uint16_t *q, const uin
             const int i = e / KC_D, d = e % KC_D, t = n * KC_C + i;
             const bool ok = t < s;
             const size_t off = (size_t)t * hd + (size_t)h * KC_D + d;
-            sm.qp[i * KC_D + d] = ok ? bf16_f32(q[off]) : 0.0f;
+            sm.qp[i * KC_PD + d] = ok ? bf16_f32(q[off]) : 0.0f;
             sm.kp[i * KC_PD + d] = ok ? bf16_f32(k[off]) : 0.0f;
             sm.gc[i * KC_PD + d] = ok ? g[off] : 0.0f;
         }
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(KC_T) k_kda_chunk(const uint16_t *q, const uin
         // l2 norms (c/gkda.h:263-273): thread r < 2C normalises one real row
         if (tid < 2 * KC_C) {
             const int i = tid % KC_C;
-            float *row = tid < KC_C ? sm.qp + i * KC_D : sm.kp + i * KC_PD;
+            float *row = (tid < KC_C ? sm.qp : sm.kp) + i * KC_PD;
             if (n * KC_C + i < s) {
                 float sq[KC_D];
 #pragma unroll 8
@@ -100,22 +100,28 @@ __global__ void __launch_bounds__(KC_T) k_kda_chunk(const uint16_t *q, const uin
             for (int i = 1; i < KC_C; i++)
                 sm.gc[i * KC_PD + tid] = sm.gc[(i - 1) * KC_PD + tid] + sm.gc[i * KC_PD + tid];
         __syncthreads();
-        // ---- attn (strictly lower) and intra (lower with the diagonal), one decay each
+        // ---- attn (strictly lower) and intra (lower with the diagonal), one
+        // decay each, over the 2080 lower-triangle pairs; zeros above
         for (int e = tid; e < KC_C * KC_C; e += KC_T) {
             const int i = e / KC_C, j = e % KC_C;
+            if (j > i) { sm.attn[i * KC_PC + j] = 0.0f; sm.intra[i * KC_PC + j] = 0.0f; }
+        }
+        for (int p = tid; p < KC_C * (KC_C + 1) / 2; p += KC_T) {
+            int i = (int)((sqrtf(8.0f * (float)p + 1.0f) - 1.0f) * 0.5f);
+            while (i * (i + 1) / 2 > p) i--;
+            while ((i + 1) * (i + 2) / 2 <= p) i++;
+            const int j = p - i * (i + 1) / 2;
+            const float bi = sm.beta[i];
+            const float *qi = sm.qp + i * KC_PD, *ki = sm.kp + i * KC_PD, *kj = sm.kp + j * KC_PD;
+            const float *gi = sm.gc + i * KC_PD, *gj = sm.gc + j * KC_PD;
             float a = 0.0f, b = 0.0f;
-            if (j <= i) {
-                const float bi = sm.beta[i];
-                const float *qi = sm.qp + i * KC_D, *ki = sm.kp + i * KC_PD, *kj = sm.kp + j * KC_PD;
-                const float *gi = sm.gc + i * KC_PD, *gj = sm.gc + j * KC_PD;
-                for (int d = 0; d < KC_D; d++) {
-                    const float dec = expf(gi[d] - gj[d]);
-                    a += ((ki[d] * bi) * kj[d]) * dec;
-                    b += (qi[d] * kj[d]) * dec;
-                }
+            for (int d = 0; d < KC_D; d++) {
+                const float dec = expf(gi[d] - gj[d]);
+                a += ((ki[d] * bi) * kj[d]) * dec;
+                b += (qi[d] * kj[d]) * dec;
             }
             sm.attn[i * KC_PC + j] = j < i ? -a : 0.0f;
-            sm.intra[i * KC_PC + j] = j <= i ? b : 0.0f;
+            sm.intra[i * KC_PC + j] = b;
         }
         // k beta e^gc for kcd
         for (int e = tid; e < KC_C * KC_D; e += KC_T) {
@@ -138,53 +144,124 @@ __global__ void __launch_bounds__(KC_T) k_kda_chunk(const uint16_t *q, const uin
         }
         if (tid < KC_C) sm.attn[tid * KC_PC + tid] = sm.attn[tid * KC_PC + tid] + 1.0f;
         __syncthreads();
-        // ---- value = attn (v beta); kcd = attn (k beta e^gc)
-        for (int e = tid; e < KC_C * KC_DV; e += KC_T) {
-            const int i = e / KC_DV, c = e % KC_DV;
-            float a = 0.0f;
-            for (int j = 0; j < KC_C; j++) a += sm.attn[i * KC_PC + j] * sm.vp[j * KC_PV + c];
-            sm.val[i * KC_PV + c] = a;
+        // ---- value = attn (v beta); kcd = attn (k beta e^gc).  Register
+        // tiles (each output still sums j = 0, 1, ... in order): value 2 rows
+        // x 4 columns a thread, kcd 4 rows x 8 columns (columns 16 apart)
+        {
+            const int i0 = (tid >> 3) * 2, cb = (tid & 7) * 4;
+            float a[2][4] = {};
+            for (int j = 0; j < KC_C; j++) {
+                const float x0 = sm.attn[i0 * KC_PC + j], x1 = sm.attn[(i0 + 1) * KC_PC + j];
+#pragma unroll
+                for (int w = 0; w < 4; w++) {
+                    const float vv = sm.vp[j * KC_PV + cb + w];
+                    a[0][w] += x0 * vv;
+                    a[1][w] += x1 * vv;
+                }
+            }
+#pragma unroll
+            for (int w = 0; w < 4; w++) { sm.val[i0 * KC_PV + cb + w] = a[0][w]; sm.val[(i0 + 1) * KC_PV + cb + w] = a[1][w]; }
         }
-        for (int e = tid; e < KC_C * KC_D; e += KC_T) {
-            const int i = e / KC_D, d = e % KC_D;
-            float a = 0.0f;
-            for (int j = 0; j < KC_C; j++) a += sm.attn[i * KC_PC + j] * sm.kx[j * KC_D + d];
-            sm.kcd[i * KC_D + d] = a;
+        {
+            const int i0 = (tid >> 4) * 4, db = tid & 15;
+            float a[4][8] = {};
+            for (int j = 0; j < KC_C; j++) {
+                float x[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) x[u] = sm.attn[(i0 + u) * KC_PC + j];
+#pragma unroll
+                for (int w = 0; w < 8; w++) {
+                    const float kv = sm.kx[j * KC_D + db + 16 * w];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) a[u][w] += x[u] * kv;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+#pragma unroll
+                for (int w = 0; w < 8; w++) sm.kcd[(i0 + u) * KC_PD + db + 16 * w] = a[u][w];
         }
         __syncthreads();
         // q e^gc (in place) and k e^(gc_last - gc) (over kx)
         for (int e = tid; e < KC_C * KC_D; e += KC_T) {
             const int i = e / KC_D, d = e % KC_D;
-            sm.qp[i * KC_D + d] = sm.qp[i * KC_D + d] * expf(sm.gc[i * KC_PD + d]);
+            sm.qp[i * KC_PD + d] = sm.qp[i * KC_PD + d] * expf(sm.gc[i * KC_PD + d]);
             sm.kx[i * KC_D + d] = sm.kp[i * KC_PD + d] * expf(sm.gc[(KC_C - 1) * KC_PD + d] - sm.gc[i * KC_PD + d]);
         }
         __syncthreads();
-        // ---- v_new = value - kcd S
-        for (int e = tid; e < KC_C * KC_DV; e += KC_T) {
-            const int i = e / KC_DV, c = e % KC_DV;
-            float a = 0.0f;
-            for (int d = 0; d < KC_D; d++) a += sm.kcd[i * KC_D + d] * sm.S[d * KC_PV + c];
-            sm.val[i * KC_PV + c] = sm.val[i * KC_PV + c] - a;
+        // ---- v_new = value - kcd S (2 x 4 register tiles, d in order)
+        const int i0 = (tid >> 3) * 2, cb = (tid & 7) * 4;
+        {
+            float a[2][4] = {};
+            for (int d = 0; d < KC_D; d++) {
+                const float x0 = sm.kcd[i0 * KC_PD + d], x1 = sm.kcd[(i0 + 1) * KC_PD + d];
+#pragma unroll
+                for (int w = 0; w < 4; w++) {
+                    const float sv = sm.S[d * KC_PV + cb + w];
+                    a[0][w] += x0 * sv;
+                    a[1][w] += x1 * sv;
+                }
+            }
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                sm.val[i0 * KC_PV + cb + w] = sm.val[i0 * KC_PV + cb + w] - a[0][w];
+                sm.val[(i0 + 1) * KC_PV + cb + w] = sm.val[(i0 + 1) * KC_PV + cb + w] - a[1][w];
+            }
         }
         __syncthreads();
         // ---- out = bf16(inter + intra v_new) for the real rows, inter = (q e^gc) S
-        for (int e = tid; e < KC_C * KC_DV; e += KC_T) {
-            const int i = e / KC_DV, c = e % KC_DV, t = n * KC_C + i;
-            if (t >= s) continue;
-            float b = 0.0f;
-            for (int d = 0; d < KC_D; d++) b += sm.qp[i * KC_D + d] * sm.S[d * KC_PV + c];
-            float a = 0.0f;
-            for (int j = 0; j < KC_C; j++) a += sm.intra[i * KC_PC + j] * sm.val[j * KC_PV + c];
-            out[(size_t)t * hd + (size_t)h * KC_D + c0 + c] = bf16_bits(b + a);
+        {
+            float b[2][4] = {}, a[2][4] = {};
+            for (int d = 0; d < KC_D; d++) {
+                const float x0 = sm.qp[i0 * KC_PD + d], x1 = sm.qp[(i0 + 1) * KC_PD + d];
+#pragma unroll
+                for (int w = 0; w < 4; w++) {
+                    const float sv = sm.S[d * KC_PV + cb + w];
+                    b[0][w] += x0 * sv;
+                    b[1][w] += x1 * sv;
+                }
+            }
+            for (int j = 0; j < KC_C; j++) {
+                const float x0 = sm.intra[i0 * KC_PC + j], x1 = sm.intra[(i0 + 1) * KC_PC + j];
+#pragma unroll
+                for (int w = 0; w < 4; w++) {
+                    const float vv = sm.val[j * KC_PV + cb + w];
+                    a[0][w] += x0 * vv;
+                    a[1][w] += x1 * vv;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int t = n * KC_C + i0 + u;
+                if (t < s)
+#pragma unroll
+                    for (int w = 0; w < 4; w++)
+                        out[(size_t)t * hd + (size_t)h * KC_D + c0 + cb + w] = bf16_bits(b[u][w] + a[u][w]);
+            }
         }
         __syncthreads();     // the state update below overwrites S
-        // ---- S = S e^(gc_last) + sum_j (k_j e^(gc_last - gc_j)) v_new_j
-        for (int e = tid; e < KC_D * KC_DV; e += KC_T) {
-            const int m = e / KC_DV, c = e % KC_DV;
-            const float egl = expf(sm.gc[(KC_C - 1) * KC_PD + m]);
-            float a = 0.0f;
-            for (int j = 0; j < KC_C; j++) a += sm.kx[j * KC_D + m] * sm.val[j * KC_PV + c];
-            sm.S[m * KC_PV + c] = sm.S[m * KC_PV + c] * egl + a;
+        // ---- S = S e^(gc_last) + sum_j (k_j e^(gc_last - gc_j)) v_new_j (4 x 4 tiles, j in order)
+        {
+            const int m0 = (tid >> 3) * 4;
+            float a[4][4] = {};
+            for (int j = 0; j < KC_C; j++) {
+                float kv[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) kv[u] = sm.kx[j * KC_D + m0 + u];
+#pragma unroll
+                for (int w = 0; w < 4; w++) {
+                    const float vv = sm.val[j * KC_PV + cb + w];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) a[u][w] += kv[u] * vv;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float egl = expf(sm.gc[(KC_C - 1) * KC_PD + m0 + u]);
+#pragma unroll
+                for (int w = 0; w < 4; w++)
+                    sm.S[(m0 + u) * KC_PV + cb + w] = sm.S[(m0 + u) * KC_PV + cb + w] * egl + a[u][w];
+            }
         }
     }
     __syncthreads();
