@@ -333,3 +333,112 @@ int orc_sample_exact(const uint16_t *logits, size_t n, float temp, float top_p, 
     free(ord);
     return tok;
 }
+
+/* ------------------------------------------------------------ chunked KDA */
+
+/* c/gkda.h:350-539 apus_gkda_chunk (the chunked delta rule, chunks of 64):
+ * per head, rows l2-normalised (numpy pairwise sum of squares), q scaled by
+ * D^-1/2, k and v weighted by beta; the gate summed within each chunk; the
+ * strictly-lower attn with per-dimension decay, its UT transform row by row
+ * (+ I after the whole solve); value, kcd, v_new, inter, intra, the output
+ * rows and the state update, every sum ascending from +0.  Rows past s are
+ * zero.  S [H*D*D] fp32 in/out. */
+#define ORC_KDA_C 64
+void orc_kda_chunk(const uint16_t *q, const uint16_t *k, const uint16_t *v, const float *g,
+                   const uint16_t *beta, float *S, uint16_t *out, size_t s, size_t H, size_t D) {
+    const size_t C = ORC_KDA_C, pad = (C - s % C) % C, sp = s + pad, N = sp / C, hd = H * D;
+    const float qscale = (float)pow((double)D, -0.5);
+    float *qp = calloc(sp * D, 4), *kp = calloc(sp * D, 4), *gc = calloc(sp * D, 4);
+    float *kb = calloc(sp * D, 4), *vb = calloc(sp * D, 4), *sq = malloc(D * 4);
+    float *attn = malloc(C * C * 4), *intra = malloc(C * C * 4), *value = malloc(C * D * 4);
+    float *kcd = malloc(C * D * 4), *vnew = malloc(C * D * 4), *inter = malloc(C * D * 4);
+    for (size_t h = 0; h < H; h++) {
+        memset(qp, 0, sp * D * 4); memset(kp, 0, sp * D * 4); memset(gc, 0, sp * D * 4);
+        memset(kb, 0, sp * D * 4); memset(vb, 0, sp * D * 4);
+        for (size_t t = 0; t < s; t++) {
+            float *rows[2] = {qp + t * D, kp + t * D};
+            const uint16_t *src[2] = {q + t * hd + h * D, k + t * hd + h * D};
+            for (int w = 0; w < 2; w++) {
+                for (size_t d = 0; d < D; d++) {
+                    rows[w][d] = orc_bf16_f32(src[w][d]);
+                    sq[d] = rows[w][d] * rows[w][d];
+                }
+                const float root = sqrtf(orc_pw_sum(sq, D) + 1e-6f);
+                for (size_t d = 0; d < D; d++) rows[w][d] = rows[w][d] / root;
+            }
+            const float bt = orc_bf16_f32(beta[t * H + h]);
+            for (size_t d = 0; d < D; d++) {
+                qp[t * D + d] = qp[t * D + d] * qscale;
+                gc[t * D + d] = g[t * hd + h * D + d];
+                kb[t * D + d] = kp[t * D + d] * bt;
+                vb[t * D + d] = orc_bf16_f32(v[t * hd + h * D + d]) * bt;
+            }
+        }
+        for (size_t n = 0; n < N; n++)
+            for (size_t i = 1; i < C; i++)
+                for (size_t d = 0; d < D; d++)
+                    gc[(n * C + i) * D + d] = gc[(n * C + i - 1) * D + d] + gc[(n * C + i) * D + d];
+        float *Sh = S + h * D * D;
+        for (size_t n = 0; n < N; n++) {
+            const float *qc = qp + n * C * D, *kc = kp + n * C * D, *gn = gc + n * C * D;
+            const float *kbc = kb + n * C * D, *vbc = vb + n * C * D;
+            memset(attn, 0, C * C * 4);
+            memset(intra, 0, C * C * 4);
+            for (size_t i = 0; i < C; i++)
+                for (size_t j = 0; j <= i; j++) {
+                    float a = 0.0f, b = 0.0f;
+                    for (size_t d = 0; d < D; d++) {
+                        const float dec = expf(gn[i * D + d] - gn[j * D + d]);
+                        a += (kbc[i * D + d] * kc[j * D + d]) * dec;
+                        b += (qc[i * D + d] * kc[j * D + d]) * dec;
+                    }
+                    if (j < i) attn[i * C + j] = -a;
+                    intra[i * C + j] = b;
+                }
+            for (size_t i = 1; i < C; i++)
+                for (size_t j = 0; j < i; j++) {
+                    float a = 0.0f;
+                    for (size_t m = 0; m < i; m++) a += attn[i * C + m] * attn[m * C + j];
+                    attn[i * C + j] = attn[i * C + j] + a;
+                }
+            for (size_t i = 0; i < C; i++) attn[i * C + i] = attn[i * C + i] + 1.0f;
+            for (size_t i = 0; i < C; i++)
+                for (size_t d = 0; d < D; d++) {
+                    float a = 0.0f, b = 0.0f;
+                    for (size_t j = 0; j < C; j++) {
+                        a += attn[i * C + j] * vbc[j * D + d];
+                        b += attn[i * C + j] * (kbc[j * D + d] * expf(gn[j * D + d]));
+                    }
+                    value[i * D + d] = a;
+                    kcd[i * D + d] = b;
+                }
+            for (size_t i = 0; i < C; i++)
+                for (size_t c = 0; c < D; c++) {
+                    float a = 0.0f, b = 0.0f;
+                    for (size_t d = 0; d < D; d++) {
+                        b += (qc[i * D + d] * expf(gn[i * D + d])) * Sh[d * D + c];
+                        a += kcd[i * D + d] * Sh[d * D + c];
+                    }
+                    inter[i * D + c] = b;
+                    vnew[i * D + c] = value[i * D + c] - a;
+                }
+            for (size_t i = 0; i < C && n * C + i < s; i++)
+                for (size_t c = 0; c < D; c++) {
+                    float a = 0.0f;
+                    for (size_t j = 0; j < C; j++) a += intra[i * C + j] * vnew[j * D + c];
+                    out[(n * C + i) * hd + h * D + c] = orc_bf16_bits(inter[i * D + c] + a);
+                }
+            const float *gl = gn + (C - 1) * D;
+            for (size_t m = 0; m < D; m++) {
+                const float egl = expf(gl[m]);
+                for (size_t c = 0; c < D; c++) {
+                    float a = 0.0f;
+                    for (size_t j = 0; j < C; j++) a += (kc[j * D + m] * expf(gl[m] - gn[j * D + m])) * vnew[j * D + c];
+                    Sh[m * D + c] = Sh[m * D + c] * egl + a;
+                }
+            }
+        }
+    }
+    free(qp); free(kp); free(gc); free(kb); free(vb); free(sq);
+    free(attn); free(intra); free(value); free(kcd); free(vnew); free(inter);
+}

@@ -44,6 +44,10 @@ int orc_sample_logits_u(const uint16_t *logits, size_t n, float temp, float top_
 /* the same draw in the B200 sampler's exact arithmetic, u = u53 * 2^-53 */
 int orc_sample_exact(const uint16_t *logits, size_t n, float temp, float top_p, uint64_t u53);
 
+/* ---- chunked KDA prefill core (c/gkda.h:350-539 apus_gkda_chunk) ---- */
+void orc_kda_chunk(const uint16_t *q, const uint16_t *k, const uint16_t *v, const float *g,
+                   const uint16_t *beta, float *S, uint16_t *out, size_t s, size_t H, size_t D);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,6 +43,7 @@ _decl(ORC, "orc_argmax_bf16", _i, _vp, _sz)
 _decl(ORC, "orc_rng_next", C.c_uint64, C.POINTER(C.c_uint64))
 _decl(ORC, "orc_sample_logits_u", _i, _vp, _sz, _f, _f, C.c_double)
 _decl(ORC, "orc_sample_exact", _i, _vp, _sz, _f, _f, C.c_uint64)
+_decl(ORC, "orc_kda_chunk", None, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz)
 
 if REF is not None:
     _decl(REF, "apus_fp8blk_dequant_scalar", None, _vp, _vp, _vp, _sz, _sz)

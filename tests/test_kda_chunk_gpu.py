@@ -59,13 +59,18 @@ def close(got, want, H, D=128):
             assert np.abs(a - b).max() <= 1e-2 * np.abs(b).max(), (t, h)
 
 
-@pytest.mark.skipif(O.REF is None, reason="oracle/_ref is not built")
 @pytest.mark.parametrize("s,H", [(1, 2), (64, 2), (100, 3), (300, 4)])
 def test_chunk_vs_reference(gcuda, s, H):
+    """Against the oracle's restatement (bitwise the reference's
+    apus_gkda_chunk, tests/test_oracle_kda_cpu.py) and, when oracle/_ref is
+    built, the reference's own chunked and recurrent cores."""
     rng = np.random.default_rng(s * 10 + H)
     args = inputs(rng, s, H)
     got_o, got_S = dev(gcuda, *args, s, H)
-    for fn in (O.REF.apus_gkda_chunk, O.REF.apus_gkda_recurrent):
+    fns = [O.ORC.orc_kda_chunk]
+    if O.REF is not None:
+        fns += [O.REF.apus_gkda_chunk, O.REF.apus_gkda_recurrent]
+    for fn in fns:
         want_o, want_S = ref(fn, *args, s, H)
         close(got_o, want_o, H)
         assert np.abs(got_S - want_S).max() <= 1e-3 * np.abs(want_S).max()
