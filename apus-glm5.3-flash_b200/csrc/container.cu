@@ -431,7 +431,96 @@ bool cfg_bool(const JVal *o, const char *k, int &out) {
     return false;
 }
 
+// The v2 manifest apus.index.json when the container has one (the reference
+// loader requires it, c/gmodel.h:647-660; the expert cache reads its slab
+// records, c/gcache.h:865-930): format_version 2 and model_type glm5_next;
+// every tensor_map entry naming a tensor of the safetensors index agrees with
+// that tensor's shard, absolute file offset, size and dtype; every expert
+// slab record is the six members (gate, up, down weight + scale, in the
+// manifest's member order) laid end to end at its offset in its shard.
+int check_manifest(ShardSet &set, std::string &err) {
+    std::string text, je;
+    if (!read_file(set.dir + "/apus.index.json", text)) return 0;      // a plain safetensors container
+    JVal man;
+    if (!json_parse(text.data(), text.size(), man, je) || man.t != JVal::OBJ) {
+        err = "container: apus.index.json: " + je;
+        return -1;
+    }
+    const JVal *fv = man.get("format_version"), *mt = man.get("model_type"), *ob = man.get("offset_base");
+    if (!fv || fv->t != JVal::NUM || (long)fv->n != 2 || !mt || mt->t != JVal::STR || mt->s != "glm5_next") {
+        err = "container: apus.index.json not a glm5_next v2 container";
+        return -1;
+    }
+    if (ob && (ob->t != JVal::STR || ob->s != "file")) {
+        err = "container: apus.index.json offsets are not file offsets";
+        return -1;
+    }
+    auto file_off = [&](const std::string &name, const std::string &shard, size_t *off, const StTensor **tp) {
+        const StTensor *t = set.get(name);
+        if (!t) return false;
+        auto w = set.where.find(name);
+        if (w == set.where.end() || w->second != shard) return false;
+        *off = (size_t)(t->data - (const uint8_t *)set.shards[shard]->map);
+        *tp = t;
+        return true;
+    };
+    const JVal *tm = man.get("tensor_map");
+    if (tm && tm->t == JVal::OBJ)
+        for (const auto &kv : tm->o) {
+            if (!set.where.count(kv.first)) continue;
+            const JVal *sh = kv.second.get("shard"), *off = kv.second.get("offset"), *nb = kv.second.get("nbytes"),
+                       *dt = kv.second.get("dtype");
+            size_t o = 0;
+            const StTensor *t = nullptr;
+            if (!sh || sh->t != JVal::STR || !off || off->t != JVal::NUM || !nb || nb->t != JVal::NUM ||
+                !file_off(kv.first, sh->s, &o, &t) || o != (size_t)off->n || t->nbytes != (size_t)nb->n ||
+                (dt && dt->t == JVal::STR && dt->s != t->dtype)) {
+                err = "container: apus.index.json disagrees with the shards for " + kv.first;
+                return -1;
+            }
+        }
+    std::vector<std::string> members = {"gate_proj.weight", "gate_proj.weight_scale_inv", "up_proj.weight",
+                                        "up_proj.weight_scale_inv", "down_proj.weight", "down_proj.weight_scale_inv"};
+    const JVal *mem = man.get("expert_slab_members");
+    if (mem && mem->t == JVal::ARR) {
+        members.clear();
+        for (const auto &x : mem->a)
+            if (x.t == JVal::STR) members.push_back(x.s);
+    }
+    const JVal *slabs = man.get("expert_slabs");
+    if (slabs && slabs->t == JVal::ARR)
+        for (const auto &r : slabs->a) {
+            const JVal *blk = r.get("block"), *ex = r.get("expert"), *sh = r.get("shard"), *off = r.get("offset"),
+                       *nb = r.get("nbytes");
+            if (!blk || blk->t != JVal::STR || !ex || ex->t != JVal::NUM || !sh || sh->t != JVal::STR || !off ||
+                off->t != JVal::NUM || !nb || nb->t != JVal::NUM) {
+                err = "container: apus.index.json has a bad expert slab record";
+                return -1;
+            }
+            const std::string base = blk->s + ".mlp.experts." + std::to_string((long)ex->n) + ".";
+            size_t at = (size_t)off->n, total = 0;
+            for (const std::string &m : members) {
+                size_t o = 0;
+                const StTensor *t = nullptr;
+                if (!file_off(base + m, sh->s, &o, &t) || o != at) {
+                    err = "container: expert slab " + blk->s + "/" + std::to_string((long)ex->n) +
+                          " is not its members laid end to end (" + m + ")";
+                    return -1;
+                }
+                at += t->nbytes;
+                total += t->nbytes;
+            }
+            if (total != (size_t)nb->n) {
+                err = "container: expert slab " + blk->s + "/" + std::to_string((long)ex->n) + " size " +
+                      std::to_string((size_t)nb->n) + " != its members' " + std::to_string(total);
+                return -1;
+            }
+        }
+    return 0;
+}
+
 int check_all(ShardSet &set, const ApusGcudaConfig &c, bool mtp, std::string &err) {
+    if (check_manifest(set, err)) return -1;
     int n = 0;
     for (const Need &nd : needed(c, mtp)) {
         const StTensor *t = set.get(nd.name);

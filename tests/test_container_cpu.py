@@ -113,6 +113,74 @@ def test_container_errors(G, tmp_path):
         G.container_check(str(tmp_path / "nowhere"), cfg, True)
 
 
+def _fixture_kw():
+    """The model config of the reference's M1 fixture checkpoint."""
+    m1 = os.path.join(REF, "tests", "m1")
+    sys.path.insert(0, m1)
+    try:
+        import fixtures as F
+    finally:
+        sys.path.remove(m1)
+    return dict(hidden_size=F.H, vocab_size=F.VOCAB, num_hidden_layers=F.N_LAYERS_MAIN, rms_norm_eps=1e-5,
+                hc_mult=F.HC, hc_sinkhorn_iters=20, hc_eps=1e-6, first_k_dense_replace=3,
+                intermediate_size=F.DENSE_INTER, moe_intermediate_size=F.MOE_INTER, n_routed_experts=F.N_EXPERTS,
+                n_shared_experts=1, num_experts_per_tok=2, routed_scaling_factor=2.5, norm_topk_prob=1,
+                swiglu_limit=10.0, num_attention_heads=F.N_HEADS, q_lora_rank=F.Q_LORA, kv_lora_rank=F.KV_LORA,
+                qk_nope_head_dim=F.QD, v_head_dim=F.VD, index_n_heads=F.I_HEADS, index_head_dim=F.I_DIM,
+                index_topk=8, index_kpool=F.KPOOL, index_kpool_always_select_tail=1,
+                linear_num_heads=F.LIN_HEADS, linear_head_dim=F.LIN_DIM, linear_conv_kernel_dim=F.CONV_K,
+                linear_lower_bound=-5.0, num_nextn_predict_layers=1,
+                layer_is_dsa=[int(i in F.DSA_LAYERS) for i in range(F.N_LAYERS_MAIN)],
+                mlp_is_sparse=[int(i in F.MOE_LAYERS) for i in range(F.N_LAYERS_MAIN)])
+
+
+def _converted(tmp_path):
+    """A container made by the reference converter from its own synthetic
+    checkpoint (tests/m1/fixtures.py + tools/convert.py), and the config."""
+    m1 = os.path.join(REF, "tests", "m1")
+    src, dst = tmp_path / "src", tmp_path / "dst"
+    src.mkdir()
+    code = ("import sys; sys.path.insert(0, %r); import fixtures; fixtures.make_fixture_tree(%r)" % (m1, str(src)))
+    subprocess.check_call([sys.executable, "-c", code])
+    subprocess.check_call([sys.executable, os.path.join(REF, "tools", "convert.py"), "convert", str(src), str(dst)],
+                          stdout=subprocess.DEVNULL)
+    return src, dst
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(REF, "tools", "convert.py")),
+                    reason="the reference tree is not present")
+def test_manifest_checks(G, tmp_path):
+    """The v2 manifest apus.index.json (c/gmodel.h:647-660, c/gcache.h:865-930)
+    is checked against the shards: a tampered version, tensor offset, slab
+    size or slab member order is refused with the reason."""
+    import shutil
+    _, dst = _converted(tmp_path)
+    cfg = G.make_config(**_fixture_kw())
+    assert G.container_check(str(dst), cfg, True) > 0
+    man = json.load(open(dst / "apus.index.json"))
+    name = next(iter(man["tensor_map"]))
+
+    def tampered(tag, edit):
+        d = tmp_path / tag
+        shutil.copytree(dst, d)
+        m = json.loads(json.dumps(man))
+        edit(m)
+        (d / "apus.index.json").write_text(json.dumps(m))
+        return str(d)
+
+    cases = [
+        ("v1", lambda m: m.update(format_version=1), "not a glm5_next v2 container"),
+        ("off", lambda m: m["tensor_map"][name].update(offset=m["tensor_map"][name]["offset"] + 8),
+         "disagrees with the shards for " + name.replace(".", r"\.")),
+        ("slab", lambda m: m["expert_slabs"][0].update(nbytes=m["expert_slabs"][0]["nbytes"] + 4), "size"),
+        ("order", lambda m: m.update(expert_slab_members=list(reversed(m["expert_slab_members"]))),
+         "laid end to end"),
+    ]
+    for tag, edit, msg in cases:
+        with pytest.raises(G.GcudaError, match=msg):
+            G.container_check(tampered(tag, edit), cfg, True)
+
+
 @pytest.mark.skipif(not os.path.exists(os.path.join(REF, "tools", "convert.py")),
                     reason="the reference tree is not present")
 def test_reference_converter_container(G, tmp_path):
@@ -121,29 +189,14 @@ def test_reference_converter_container(G, tmp_path):
     back through this reader with every tensor the model needs and the same
     bytes as the reference's source checkpoint."""
     m1 = os.path.join(REF, "tests", "m1")
-    src, dst = tmp_path / "src", tmp_path / "dst"
-    src.mkdir()
-    code = ("import sys; sys.path.insert(0, %r); import fixtures; fixtures.make_fixture_tree(%r)" % (m1, str(src)))
-    subprocess.check_call([sys.executable, "-c", code])
-    subprocess.check_call([sys.executable, os.path.join(REF, "tools", "convert.py"), "convert", str(src), str(dst)],
-                          stdout=subprocess.DEVNULL)
+    src, dst = _converted(tmp_path)
     sys.path.insert(0, m1)
     try:
         import fixtures as F
         import stutil
     finally:
         sys.path.remove(m1)
-    kw = dict(hidden_size=F.H, vocab_size=F.VOCAB, num_hidden_layers=F.N_LAYERS_MAIN, rms_norm_eps=1e-5,
-              hc_mult=F.HC, hc_sinkhorn_iters=20, hc_eps=1e-6, first_k_dense_replace=3,
-              intermediate_size=F.DENSE_INTER, moe_intermediate_size=F.MOE_INTER, n_routed_experts=F.N_EXPERTS,
-              n_shared_experts=1, num_experts_per_tok=2, routed_scaling_factor=2.5, norm_topk_prob=1,
-              swiglu_limit=10.0, num_attention_heads=F.N_HEADS, q_lora_rank=F.Q_LORA, kv_lora_rank=F.KV_LORA,
-              qk_nope_head_dim=F.QD, v_head_dim=F.VD, index_n_heads=F.I_HEADS, index_head_dim=F.I_DIM,
-              index_topk=8, index_kpool=F.KPOOL, index_kpool_always_select_tail=1,
-              linear_num_heads=F.LIN_HEADS, linear_head_dim=F.LIN_DIM, linear_conv_kernel_dim=F.CONV_K,
-              linear_lower_bound=-5.0, num_nextn_predict_layers=1,
-              layer_is_dsa=[int(i in F.DSA_LAYERS) for i in range(F.N_LAYERS_MAIN)],
-              mlp_is_sparse=[int(i in F.MOE_LAYERS) for i in range(F.N_LAYERS_MAIN)])
+    kw = _fixture_kw()
     cfg = G.make_config(**kw)
     n = G.container_check(str(dst), cfg, True)
     # every source tensor of the language model, by its container name
