@@ -28,3 +28,12 @@ def test_library_exports_header_symbols():
     assert len(names) > 10
     missing = [n for n in names if not hasattr(lib, n)]
     assert not missing, missing
+
+
+def test_python_mirror_binds_every_entry_point():
+    """The host mirror (apus_gcuda.py) declares every C-ABI entry point with
+    its argument types, except the hook-table filler, which only a C engine
+    can use (it fills a struct of C function pointers)."""
+    src = open(os.path.join(PKG, "apus_gcuda.py")).read()
+    unbound = [n for n in declared_functions() if f'"{n}"' not in src and n != "apus_gcuda_fill_hooks"]
+    assert not unbound, unbound
