@@ -10,6 +10,8 @@ raises.
 import ctypes as C
 import os
 
+import synth
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libapus_gcuda.so")
 
@@ -167,6 +169,7 @@ apus_gcuda_model_stream = _fn("apus_gcuda_model_stream", _vp, _vp)
 apus_gcuda_model_counters = _fn("apus_gcuda_model_counters", _i, _vp, _vp, _sz)
 apus_gcuda_model_debug_stop = _fn("apus_gcuda_model_debug_stop", _i, _vp, _i, _i)
 apus_gcuda_model_debug_read = _fn("apus_gcuda_model_debug_read", _i, _vp, _cs, _vp, _sz)
+apus_gcuda_gspec_keep_logits = _fn("apus_gcuda_gspec_keep_logits", _i, _vp, _i)
 
 
 EP_HANDLE_BYTES = 64   # sizeof(cudaIpcMemHandle_t)
@@ -360,6 +363,42 @@ class GModel:
     def stream(self):
         return apus_gcuda_model_stream(self.h)
 
+    def decode(self, ids):
+        """decode_batch without copying anything back (state only)."""
+        ids = self.np.ascontiguousarray(ids, self.np.int32)
+        check(apus_gcuda_decode_batch(self.h, ptr(ids), len(ids), None, None, None), "decode_batch")
+
+    def debug_stop(self, layer, stage):
+        """Stop the next forwards after (layer, stage); layer -1 clears it."""
+        check(apus_gcuda_model_debug_stop(self.h, int(layer), int(stage)), "debug_stop")
+
+    def debug_read(self, name, shape, dtype):
+        a = self.np.empty(shape, dtype)
+        check(apus_gcuda_model_debug_read(self.h, name.encode(), ptr(a), a.nbytes), f"debug_read {name}")
+        return a
+
+    def keep_logits(self, on=True):
+        check(apus_gcuda_gspec_keep_logits(self.h, int(on)), "keep_logits")
+
+    def kda_state(self, layer):
+        """Committed KDA state of `layer`: (conv [3*qkv][K-1] BF16, rec [H][D][D] f32)."""
+        c, np = self.cfg, self.np
+        qkv = c.linear_num_heads * c.linear_head_dim
+        conv = self.debug_read(f"kda_conv.{layer}", (3 * qkv, c.linear_conv_kernel_dim - 1), np.uint16)
+        rec = self.debug_read(f"kda_rec.{layer}", (c.linear_num_heads, c.linear_head_dim, c.linear_head_dim),
+                              np.float32)
+        return conv, rec
+
+    def dsa_state(self, layer, n):
+        """The n committed cache rows of DSA `layer` (num_hidden_layers: the MTP
+        block): k [AH][n][qd], v [AH][n][vd], ik / ig [n][ID] BF16."""
+        c, np = self.cfg, self.np
+        AH, ID = c.num_attention_heads, c.index_head_dim
+        return (self.debug_read(f"dsa_k.{layer}", (AH, n, c.qk_nope_head_dim), np.uint16),
+                self.debug_read(f"dsa_v.{layer}", (AH, n, c.v_head_dim), np.uint16),
+                self.debug_read(f"dsa_ik.{layer}", (n, ID), np.uint16),
+                self.debug_read(f"dsa_ig.{layer}", (n, ID), np.uint16))
+
     def counters(self):
         o = (C.c_uint64 * 5)()
         check(apus_gcuda_model_counters(self.h, o, 5), "counters")
@@ -368,22 +407,15 @@ class GModel:
 
 
 def ep_owns(kw, rank, world):
-    """Predicate over checkpoint names: does expert-parallel `rank` of `world`
-    store this tensor?  Routed expert e lives on rank e // (E / world); every
-    other tensor is stored on every rank (the lm_head as a row slice).  This
-    is the split apus_gcuda_model_set applies."""
-    E = kw["n_routed_experts"]
-    if world > 1 and E % world:
-        raise GcudaError(f"{E} experts do not split over {world} ranks")
-    per = E // world if world > 1 else E
+    """synth.ep_owns (the split apus_gcuda_model_set applies), raising
+    GcudaError for a split that does not divide the experts."""
+    try:
+        return synth.ep_owns(kw, rank, world)
+    except ValueError as e:
+        raise GcudaError(str(e)) from None
 
-    def owns(name):
-        i = name.find(".mlp.experts.")
-        if world == 1 or i < 0:
-            return True
-        e = int(name[i + len(".mlp.experts."):].split(".", 1)[0])
-        return e // per == rank
-    return owns
+
+tensor_specs = synth.tensor_specs
 
 
 def config_load(path):
@@ -425,96 +457,3 @@ def container_read(path, name):
     if apus_gcuda_container_read(os.fsencode(path), name.encode(), buf, n, err, 512) != n:
         raise GcudaError(err.value.decode(errors="replace"))
     return buf.raw[:n]
-
-
-def tensor_specs(kw, has_mtp=True):
-    """Every tensor GModel.set accepts for config kw: (checkpoint name, shape,
-    numpy dtype, kind).  kind: 'bf16' (uint16 codes), 'f32', 'e4m3' (uint8
-    codes) or 'scale' (F32 128x128 block scales of the preceding e4m3)."""
-    d, V, hc, L = kw["hidden_size"], kw["vocab_size"], kw["hc_mult"], kw["num_hidden_layers"]
-    H, D, K = kw["linear_num_heads"], kw["linear_head_dim"], kw["linear_conv_kernel_dim"]
-    qkv, mix = H * D, (2 + hc) * hc
-    AH, qd, vd = kw["num_attention_heads"], kw["qk_nope_head_dim"], kw["v_head_dim"]
-    ql, kl, IH, ID = kw["q_lora_rank"], kw["kv_lora_rank"], kw["index_n_heads"], kw["index_head_dim"]
-    E, inter, dense = kw["n_routed_experts"], kw["moe_intermediate_size"], kw["intermediate_size"]
-    cb = lambda n: (n + 127) // 128
-    out = []
-
-    def t(name, shape, kind):
-        dt = {"bf16": "uint16", "f32": "float32", "e4m3": "uint8", "scale": "float32"}[kind]
-        out.append((name, tuple(shape), dt, kind))
-
-    def fp8(name, O_, K_):
-        t(name + ".weight", (O_, K_), "e4m3")
-        t(name + ".weight_scale_inv", (cb(O_), cb(K_)), "scale")
-
-    def dsa(p):
-        fp8(p + "self_attn.q_a_proj", ql, d)
-        t(p + "self_attn.q_a_layernorm.weight", (ql,), "bf16")
-        fp8(p + "self_attn.q_b_proj", AH * qd, ql)
-        fp8(p + "self_attn.kv_a_proj_with_mqa", kl, d)
-        t(p + "self_attn.kv_a_layernorm.weight", (kl,), "bf16")
-        t(p + "self_attn.kv_b_proj.weight", (AH * (qd + vd), kl), "bf16")
-        fp8(p + "self_attn.o_proj", d, AH * vd)
-        t(p + "self_attn.indexer.wq_b.weight", (IH * ID, ql), "bf16")
-        t(p + "self_attn.indexer.wk.weight", (ID, d), "bf16")
-        t(p + "self_attn.indexer.k_norm.weight", (ID,), "bf16")
-        t(p + "self_attn.indexer.k_norm.bias", (ID,), "bf16")
-        t(p + "self_attn.indexer.weights_proj.weight", (IH, d), "bf16")
-        t(p + "self_attn.indexer.index_kpool_compress_ape", (kw["index_kpool"], ID), "bf16")
-        t(p + "self_attn.indexer.index_kpool_compress_gate", (ID, d), "bf16")
-
-    def moe(p):
-        t(p + "mlp.gate.weight", (E, d), "bf16")
-        t(p + "mlp.gate.e_score_correction_bias", (E,), "f32")
-        for e in range(E):
-            fp8(f"{p}mlp.experts.{e}.gate_proj", inter, d)
-            fp8(f"{p}mlp.experts.{e}.up_proj", inter, d)
-            fp8(f"{p}mlp.experts.{e}.down_proj", d, inter)
-        fp8(p + "mlp.shared_experts.gate_proj", inter, d)
-        fp8(p + "mlp.shared_experts.up_proj", inter, d)
-        fp8(p + "mlp.shared_experts.down_proj", d, inter)
-
-    t("embed_tokens.weight", (V, d), "bf16")
-    t("norm.weight", (d,), "bf16")
-    t("lm_head.weight", (V, d), "bf16")
-    for l in range(L):
-        p = f"layers.{l}."
-        t(p + "input_layernorm.weight", (d,), "bf16")
-        t(p + "post_attention_layernorm.weight", (d,), "bf16")
-        for site in ("attn", "ffn"):
-            t(p + f"hc_{site}_fn", (mix, hc * d), "bf16")
-            t(p + f"hc_{site}_base", (mix,), "f32")
-            t(p + f"hc_{site}_scale", (3,), "f32")
-        if not kw["layer_is_dsa"][l]:
-            for n in "qkv":
-                t(p + f"self_attn.{n}_proj.weight", (qkv, d), "bf16")
-                t(p + f"self_attn.{n}_conv1d.weight", (qkv, K), "bf16")
-            t(p + "self_attn.f_a_proj.weight", (D, d), "bf16")
-            t(p + "self_attn.f_b_proj.weight", (qkv, D), "bf16")
-            t(p + "self_attn.g_a_proj.weight", (D, d), "bf16")
-            t(p + "self_attn.g_b_proj.weight", (qkv, D), "bf16")
-            t(p + "self_attn.b_proj.weight", (H, d), "bf16")
-            t(p + "self_attn.A_log", (H,), "f32")
-            t(p + "self_attn.dt_bias", (qkv,), "f32")
-            t(p + "self_attn.o_norm.weight", (D,), "bf16")
-            t(p + "self_attn.o_proj.weight", (d, qkv), "bf16")
-        else:
-            dsa(p)
-        if kw["mlp_is_sparse"][l]:
-            moe(p)
-        else:
-            fp8(p + "mlp.gate_proj", dense, d)
-            fp8(p + "mlp.up_proj", dense, d)
-            fp8(p + "mlp.down_proj", d, dense)
-    if has_mtp:
-        p = f"layers.{L}."
-        t(p + "enorm.weight", (d,), "bf16")
-        t(p + "hnorm.weight", (d,), "bf16")
-        t(p + "eh_proj.weight", (d, 2 * d), "bf16")
-        t(p + "input_layernorm.weight", (d,), "bf16")
-        t(p + "post_attention_layernorm.weight", (d,), "bf16")
-        dsa(p)
-        moe(p)
-        t(p + "shared_head.norm.weight", (d,), "bf16")
-    return out

@@ -26,6 +26,34 @@ int gcuda_check(cudaError_t e, const char *what) {
 }
 
 namespace {
+std::mutex g_once_mu;
+std::map<std::pair<const void *, int>, int> g_smem_set;   // (kernel, device) -> limit set
+std::map<int, int> g_sms;                                 // device -> SM count
+}  // namespace
+
+int gcuda_smem_limit_once(const void *func, int bytes) {
+    int dev = 0;
+    if (gcuda_check(cudaGetDevice(&dev), "current device")) return -1;
+    std::lock_guard<std::mutex> lk(g_once_mu);
+    int &have = g_smem_set[{func, dev}];
+    if (have >= bytes) return 0;
+    if (gcuda_check(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                    "kernel shared-memory limit"))
+        return -1;
+    have = bytes;
+    return 0;
+}
+
+int gcuda_num_sms(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lk(g_once_mu);
+    int &n = g_sms[dev];
+    if (!n && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 0;
+    return n;
+}
+
+namespace {
 
 struct Region {
     const uint8_t *host;
@@ -356,13 +384,15 @@ int apus_gcuda_bf16_gemm_argmax_dev(const uint16_t *w, const uint16_t *x, uint16
     if (!keys) { gcuda_set_error("argmax scratch allocation failed"); return -1; }
     for (size_t m0 = 0; m0 < M; m0 += 8) {
         const int R = (int)((M - m0) < 8 ? (M - m0) : 8);
-        if (argmax_reset_launch(keys + m0, R, st)) return gcuda_check(cudaGetLastError(), "argmax reset");
+        if (argmax_reset_launch(keys + m0, R, st)) { gcuda_set_error("argmax reset launch failed"); return -1; }
     }
     if (linear_dev(w, nullptr, 0, x, y, nullptr, keys, M, O, K, st)) return -1;
     for (size_t m0 = 0; m0 < M; m0 += 8) {
         const int R = (int)((M - m0) < 8 ? (M - m0) : 8);
-        if (argmax_extract_launch(keys + m0, ids + m0, R, st))
-            return gcuda_check(cudaGetLastError(), "argmax extract");
+        if (argmax_extract_launch(keys + m0, ids + m0, R, st)) {
+            gcuda_set_error("argmax extract launch failed");
+            return -1;
+        }
     }
     return 0;
 }

@@ -81,6 +81,12 @@ int argmax_extract_launch(const unsigned long long *keys, int32_t *ids, int n, c
 // error plumbing (capi.cu)
 void gcuda_set_error(const char *fmt, ...);
 int gcuda_check(cudaError_t e, const char *what);
+// Per-device set-up shared by every launcher, thread-safe (capi.cu): raise a
+// kernel's dynamic shared-memory limit to `bytes` on the current device the
+// first time it is asked there (0 / -1), and the current device's SM count
+// (0 on error).
+int gcuda_smem_limit_once(const void *func, int bytes);
+int gcuda_num_sms(void);
 
 // seeded device-side weight fill (init.cu)
 enum { FILL_BF16_NORMAL = 0, FILL_E4M3_NORMAL = 1, FILL_F32_LOGUNIFORM = 2, FILL_F32_NORMAL = 3,

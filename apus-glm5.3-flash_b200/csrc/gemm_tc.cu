@@ -259,13 +259,7 @@ bool gemm_tc_ok(const void *x, long ldx, const void *w, long ldw, long M, long O
 
 template <int BN>
 static int tc_launch(const CUtensorMap &am, const uint16_t *w, long ldw, TcDesc d, int nsm, cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::Cfg<BN>::SMEM)
-            != cudaSuccess)
-            return -1;
-        attr = true;
-    }
+    if (gcuda_smem_limit_once((const void *)k_gemm_tc<BN>, tc::Cfg<BN>::SMEM)) return -1;
     CUtensorMap bm;
     if (tc_map(&bm, w, d.O, d.K, ldw, BN)) return -1;
     d.ntn = (d.O + BN - 1) / BN;
@@ -281,12 +275,8 @@ static int tc_launch(const CUtensorMap &am, const uint16_t *w, long ldw, TcDesc 
 int gemm_tc_launch(const uint16_t *x, long ldx, const uint16_t *w, long ldw, uint16_t *y, long ldy, float *yf,
                    long ldyf, long M, long O, long K, cudaStream_t st) {
     if (!gemm_tc_ok(x, ldx, w, ldw, M, O, K)) return -1;
-    static int nsm = 0;
-    if (!nsm) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    }
+    const int nsm = gcuda_num_sms();
+    if (nsm < 1) return -1;
     const long ntm = (M + tc::BM - 1) / tc::BM;
     if (ntm * ((O + 127) / 128) >= (1l << 31)) return -1;
     CUtensorMap am;

@@ -281,13 +281,7 @@ int kda_chunk_launch(const uint16_t *q, const uint16_t *k, const uint16_t *v, co
         return -1;
     }
     if (s == 0) return 0;
-    static bool attr = false;
-    if (!attr) {
-        if (gcuda_check(cudaFuncSetAttribute(k_kda_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)sizeof(KcSmem)), "kda_chunk smem"))
-            return -1;
-        attr = true;
-    }
+    if (gcuda_smem_limit_once((const void *)k_kda_chunk, (int)sizeof(KcSmem))) return -1;
     const float qscale = (float)pow((double)D, -0.5);
     k_kda_chunk<<<H * KC_SPLIT, KC_T, sizeof(KcSmem), st>>>(q, k, v, g, beta, S, out, s, H, qscale);
     return gcuda_check(cudaGetLastError(), "kda_chunk launch");

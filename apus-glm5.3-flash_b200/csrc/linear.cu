@@ -644,8 +644,6 @@ bool gemv_fast_ok(const GemvDesc &d) {
     return true;
 }
 
-static int g_num_sms = 0;
-
 // Dynamic shared memory of a launch staging `rows` activation rows of klen
 // elements: ring, warp partials, barriers (in a 128-byte slot), activations.
 static size_t gemv_smem(int rows, long klen) {
@@ -721,22 +719,14 @@ static int wmap_get(const GemvDesc &d, CUtensorMap *out) {
 
 template <bool FP8>
 static int launch_tma(const GemvDesc &d, cudaStream_t st) {
-    static bool attr = false;
     const size_t sm = gemv_smem(d.R, d.K < d.kx ? d.K : d.kx);
-    if (!attr) {
-        if (cudaFuncSetAttribute(k_gemv_tma<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)gemv_smem(8, gemvcfg::KX)) != cudaSuccess) return -1;
-        attr = true;
-    }
+    if (gcuda_smem_limit_once((const void *)k_gemv_tma<FP8>, (int)gemv_smem(8, gemvcfg::KX))) return -1;
     // CTAs an SM holds at this size (228 KiB per SM, 1 KiB reserved per CTA)
     long per_sm = (long)(233472 / (sm + 1024));
     if (per_sm > gemvcfg::CTAS_PER_SM) per_sm = gemvcfg::CTAS_PER_SM;
     if (per_sm < 1) return -1;
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    }
+    const int g_num_sms = gcuda_num_sms();
+    if (g_num_sms < 1) return -1;
     CUtensorMap wmap;
     if (wmap_get(d, &wmap)) return -1;
     const long ntile = ((d.O + gemvcfg::TR - 1) / gemvcfg::TR + d.tpi - 1) / d.tpi;   // work items

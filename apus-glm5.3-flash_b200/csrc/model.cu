@@ -86,6 +86,8 @@ __global__ void k_spec_walk(Ctl *c, int D, int32_t *log, int log_cap) {
     pdl_launch_dependents();
     if (threadIdx.x != 0) return;
     if (c->err) { c->n_emitted = 0; return; }
+    c->stat_d1_offered++;
+    if (c->drafts[0] == c->held) c->stat_d1_hits++;
     int matched = 0, last = -1;
     c->emitted[0] = c->held;
     for (int j = 1; j < D; j++) {
@@ -97,6 +99,7 @@ __global__ void k_spec_walk(Ctl *c, int D, int32_t *log, int log_cap) {
     if (last < 0) last = c->picks[D - 1];
     c->n_emitted = matched + 1;
     c->matched = matched;
+    if (matched < D - 1) c->stat_refeed += matched + 1;
     for (int i = 0; i <= matched && c->log_n + i < log_cap; i++) log[c->log_n + i] = c->emitted[i];
     c->log_n += matched + 1;
     c->stat_emitted += matched + 1;
@@ -147,7 +150,9 @@ __device__ unsigned long long sm64(unsigned long long z) {
 
 __global__ void k_force(Ctl *c, const int32_t *truth, int D, int V) {
     pdl_launch_dependents();
-    if (threadIdx.x != 0 || !c->force_on) return;
+    if (threadIdx.x != 0) return;
+    for (int i = 0; i < D; i++) c->raw_drafts[i] = c->drafts[i];
+    if (!c->force_on) return;
     for (int i = 0; i < D; i++) {
         const long pos = (long)c->pos + i - c->force_base;
         if (pos < 0 || pos >= c->force_n) continue;
@@ -206,6 +211,7 @@ struct ApusGcudaModel {
     Ctl force{};                         // forced-draft settings (survive reset)
     float temp = 0.0f, top_p = 1.0f;     // sampling settings (survive reset)
     int dbg_layer = -1, dbg_stage = -1;  // inspection stop inside main_forward
+    int keep_logits = 0;                 // speculative steps also write the verify rows' logits
     uint16_t *yn_prompt = nullptr;       // [cap][d] post-norm rows of the prompt
     uint16_t *hcarry = nullptr, *hmtp = nullptr, *mtp_rows = nullptr;
     int32_t *ids = nullptr;
@@ -997,7 +1003,9 @@ extern "C" int apus_gcuda_decode_batch(ApusGcudaModel *m, const int32_t *ids, si
     if ((size_t)c.pos + s > (size_t)m->cap) { gcuda_set_error("decode_batch: capacity"); return -1; }
     cudaMemcpyAsync(m->ids, ids, s * 4, cudaMemcpyHostToDevice, m->st);
     if (main_forward(m, m->ids, (int)s, m->S.yn, logits != nullptr)) return fail_ctl(m, "decode_batch");
-    k_commit<<<1, 32, 0, m->st>>>(m->ctl, (int)s);
+    // a forward stopped for inspection commits nothing (the sequence stays
+    // at its position and committed state)
+    if (m->dbg_layer < 0) k_commit<<<1, 32, 0, m->st>>>(m->ctl, (int)s);
     if (logits) cudaMemcpyAsync(logits, m->S.logits, s * D.V * 2, cudaMemcpyDeviceToHost, m->st);
     if (h_out) cudaMemcpyAsync(h_out, m->S.h4, s * D.hc * D.d * 2, cudaMemcpyDeviceToHost, m->st);
     if (yn_out) cudaMemcpyAsync(yn_out, m->S.yn, s * D.d * 2, cudaMemcpyDeviceToHost, m->st);
@@ -1097,15 +1105,16 @@ static int spec_step(ApusGcudaModel *m, int Dp) {
     // verify rows, rows [Dp, 2 Dp) the replay's shared-head outputs.
     const bool one_head = 2 * Dp <= MAXR;
     uint16_t *mtp_out = one_head ? m->S.yn + (size_t)Dp * d : m->S.oh;
+    const bool want = smp || m->keep_logits;
     k_spec_begin<<<1, 32, 0, st>>>(m->ctl, Dp, m->cap, m->ids);
-    if (main_forward(m, m->ids, Dp, m->S.yn, smp, !one_head)) return -1;
+    if (main_forward(m, m->ids, Dp, m->S.yn, want, !one_head)) return -1;
     // MTP replay of the D candidate pairs (rows past the accepted prefix are
     // overwritten by the chain / the next replay)
     k_replay_rows<<<(Dp * d + 255) / 256, 256, 0, st>>>(m->hcarry, m->S.yn, Dp, d, m->mtp_rows);
     if (one_head) {
         if (mtp_forward(m, m->ids, m->mtp_rows, Dp, &m->ctl->mtp_n, false, mtp_out, m->S.amax + Dp, false))
             return -1;
-        if (lm_head(m, m->S.yn, 2 * Dp, m->ctl->picks, smp, Dp, m->ctl->mtp_picks)) return -1;
+        if (lm_head(m, m->S.yn, 2 * Dp, m->ctl->picks, want, Dp, m->ctl->mtp_picks)) return -1;
     } else if (mtp_forward(m, m->ids, m->mtp_rows, Dp, &m->ctl->mtp_n, false)) {
         return -1;
     }
@@ -1303,19 +1312,90 @@ extern "C" int apus_gcuda_rng_state(ApusGcudaModel *m, uint64_t *state) {
     return gcuda_check(cudaGetLastError(), "rng state");
 }
 
+extern "C" int apus_gcuda_gspec_keep_logits(ApusGcudaModel *m, int on) {
+    if (on && m->ep_world > 1) { gcuda_set_error("keep_logits: the logits are split over the ranks"); return -1; }
+    m->keep_logits = on ? 1 : 0;
+    if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = nullptr; }
+    if (m->graph) { cudaGraphDestroy(m->graph); m->graph = nullptr; }
+    return 0;
+}
+
 extern "C" int apus_gcuda_model_debug_stop(ApusGcudaModel *m, int layer, int stage) {
     m->dbg_layer = layer;
     m->dbg_stage = stage;
     return 0;
 }
 
+// Committed sequence state by name, for inspection: "kda_conv.L" [3*qkv][K-1]
+// and "kda_rec.L" [H][D][D] (the committed checkpoint slot of KDA layer L),
+// "dsa_k.L" [AH][n][qd], "dsa_v.L" [AH][n][vd], "dsa_ik.L" / "dsa_ig.L"
+// [n][ID] (the n committed cache rows of DSA layer L; L = num_hidden_layers
+// names the MTP block's caches, n = its committed rows).  -2: not a state name.
+static int state_read(ApusGcudaModel *m, const char *name, void *host, size_t bytes) {
+    const Dims &D = m->D;
+    const char *dot = strchr(name, '.');
+    if (!dot) return -2;
+    const std::string kind(name, dot - name);
+    const int l = atoi(dot + 1);
+    if (kind != "kda_conv" && kind != "kda_rec" && kind != "dsa_k" && kind != "dsa_v" && kind != "dsa_ik" &&
+        kind != "dsa_ig")
+        return -2;
+    Ctl c = read_ctl(m);
+    auto need = [&](size_t n) {
+        if (bytes != n) { gcuda_set_error("debug_read %s: %zu bytes, expected %zu", name, bytes, n); return false; }
+        return true;
+    };
+    uint8_t *h = (uint8_t *)host;
+    if (kind == "kda_conv" || kind == "kda_rec") {
+        if (l < 0 || l >= D.L || m->L[l].is_dsa) { gcuda_set_error("debug_read %s: not a KDA layer", name); return -1; }
+        const size_t cs = (size_t)3 * D.qkv * (D.K - 1) * 2, rs = (size_t)D.H * D.D * D.D * 4;
+        if (kind == "kda_conv")
+            return need(cs) ? gcuda_check(cudaMemcpy(h, (uint8_t *)m->kda[l].conv + c.kda_cur * cs, cs,
+                                                     cudaMemcpyDeviceToHost), "debug_read") : -1;
+        return need(rs) ? gcuda_check(cudaMemcpy(h, (uint8_t *)m->kda[l].rec + c.kda_cur * rs, rs,
+                                                 cudaMemcpyDeviceToHost), "debug_read") : -1;
+    }
+    const bool mtp = l == D.L && m->has_mtp;
+    if (!mtp && (l < 0 || l >= D.L || !m->L[l].is_dsa)) {
+        gcuda_set_error("debug_read %s: not a DSA layer", name);
+        return -1;
+    }
+    const DsaState &ds = mtp ? m->mtp_dsa : m->dsa[l];
+    const size_t n = (size_t)(mtp ? c.mtp_n : c.pos);
+    if (kind == "dsa_k" || kind == "dsa_v") {
+        const size_t w = kind == "dsa_k" ? D.qd : D.vd;
+        const uint16_t *src = kind == "dsa_k" ? ds.k : ds.v;
+        if (!need((size_t)D.AH * n * w * 2)) return -1;
+        for (int hh = 0; hh < D.AH; hh++)
+            if (gcuda_check(cudaMemcpy(h + (size_t)hh * n * w * 2, src + (size_t)hh * ds.cap * w, n * w * 2,
+                                       cudaMemcpyDeviceToHost), "debug_read"))
+                return -1;
+        return 0;
+    }
+    if (!need(n * D.ID * 2)) return -1;
+    return gcuda_check(cudaMemcpy(h, kind == "dsa_ik" ? ds.ik : ds.ig, n * D.ID * 2, cudaMemcpyDeviceToHost),
+                       "debug_read");
+}
+
 extern "C" int apus_gcuda_model_debug_read(ApusGcudaModel *m, const char *name, void *host, size_t bytes) {
+    {
+        const int rc = state_read(m, name, host, bytes);
+        if (rc != -2) return rc;
+    }
+    if (!strcmp(name, "raw_drafts") || !strcmp(name, "drafts")) {
+        Ctl c = read_ctl(m);
+        const int *src = name[0] == 'r' ? c.raw_drafts : c.drafts;
+        if (bytes > sizeof c.drafts) { gcuda_set_error("debug_read %s: at most %zu bytes", name, sizeof c.drafts); return -1; }
+        memcpy(host, src, bytes);
+        return 0;
+    }
     const Scratch &S = m->S;
     const struct { const char *n; const void *p; } tab[] = {
         {"h4", S.h4}, {"h4b", S.h4b}, {"x", S.x}, {"sub", S.sub}, {"post", S.post}, {"comb", S.comb},
         {"kp", S.kp}, {"qkvc", S.qkvc}, {"fgo", S.fgo}, {"core", S.core}, {"qkva", S.qkva}, {"q", S.q},
         {"kvb", S.kvb}, {"iq", S.iq}, {"ikgw", S.ikgw}, {"attn", S.attn}, {"yn", S.yn}, {"mix", S.mix},
         {"qres", S.qres}, {"kpass", S.kpass}, {"isel", S.isel}, {"iscore", S.iscore},
+        {"moe_idx", m->moe_scr.row_expert}, {"moe_w", m->moe_scr.row_weight}, {"logits", S.logits},
     };
     for (const auto &e : tab)
         if (!strcmp(e.n, name)) {
@@ -1342,8 +1422,8 @@ extern "C" uint64_t apus_gcuda_state_digest(ApusGcudaModel *m) {
             eat((uint8_t *)m->kda[l].rec + c.kda_cur * rs, rs);
         } else {
             for (int hh = 0; hh < D.AH; hh++) {
-                eat(m->dsa[l].k + ((size_t)hh * m->cap) * D.qd, (size_t)c.pos * D.qd * 2);
-                eat(m->dsa[l].v + ((size_t)hh * m->cap) * D.vd, (size_t)c.pos * D.vd * 2);
+                eat(m->dsa[l].k + ((size_t)hh * m->dsa[l].cap) * D.qd, (size_t)c.pos * D.qd * 2);
+                eat(m->dsa[l].v + ((size_t)hh * m->dsa[l].cap) * D.vd, (size_t)c.pos * D.vd * 2);
             }
             eat(m->dsa[l].ik, (size_t)c.pos * D.ID * 2);
         }

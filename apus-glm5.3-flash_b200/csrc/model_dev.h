@@ -53,6 +53,13 @@ struct Ctl {
     // splitmix64 state, advanced once per sampled token
     float temp, top_p;
     unsigned long long rng_s;
+    // the MTP's own drafts of the last chain, before any forced agreement
+    int raw_drafts[MAXR];
+    // ApusGspec counters the reference keeps beside the walk's (c/gmtp.h:
+    // 786-787, 845): d1 = the first draft against the held token; refeed =
+    // the tokens its partial-reject path re-decodes (the checkpoint ring
+    // here re-decodes nothing; the count keeps the reference's meaning)
+    long long stat_d1_hits, stat_d1_offered, stat_refeed;
 };
 
 struct KdaW {

@@ -87,16 +87,18 @@ extern "C" int apus_gcuda_bf16_gemm_argmax_static_dev(const uint16_t *w, const u
         return -1;
     for (size_t m0 = 0; m0 < M; m0 += 8) {
         const int R = (int)((M - m0) < 8 ? (M - m0) : 8);
-        if (argmax_reset_launch(keys + m0, R, st)) return gcuda_check(cudaGetLastError(), "argmax reset");
+        if (argmax_reset_launch(keys + m0, R, st)) { gcuda_set_error("argmax reset launch failed"); return -1; }
         GemvDesc d{};
         d.W = w; d.x = x + m0 * K; d.ldx = (long)K; d.R = R;
         d.O = (long)O; d.K = (long)K; d.fp8 = 0;
         if (y) { d.y = y + m0 * O; d.ldy = (long)O; }
         d.amax = keys + m0;
         d.part = part; d.ticket = tick;
-        if (gemv_launch(d, st)) return gcuda_check(cudaGetLastError(), "gemv launch") ? -1 : -1;
-        if (argmax_extract_launch(keys + m0, ids + m0, R, st))
-            return gcuda_check(cudaGetLastError(), "argmax extract");
+        if (gemv_launch(d, st)) { gcuda_set_error("gemv launch failed"); return -1; }
+        if (argmax_extract_launch(keys + m0, ids + m0, R, st)) {
+            gcuda_set_error("argmax extract launch failed");
+            return -1;
+        }
     }
     return 0;
 }

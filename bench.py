@@ -27,6 +27,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "apus-glm5.3-flash_b200")
 sys.path.insert(0, PKG)
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
+from synth import c2_config, c2_weights, ep_owns  # noqa: E402  (pure Python: loads no CUDA library)
 
 METRIC = "accepted tok/s (MTP depth 3, 1 seq) at 1/2/4/8 B200; FP8 GEMV % HBM peak"
 
@@ -224,6 +225,51 @@ def bench_c0(args, ws, rank):
     return out
 
 
+def fp8_gemv_leg(reps=200, warmup=10):
+    """The metric's second half, FP8 GEMV % of HBM peak, on BASELINE config
+    0 (M=4 rows, 4096x4096 E4M3 with 128x128 block scales): back-to-back
+    launches over 16 rotating weight copies (270 MB > L2, so every launch
+    streams its weights from HBM), CUDA events on the launching stream."""
+    import numpy as np
+    import torch
+    import apus_gcuda as G
+    M, N, K = C0["M"], C0["N"], C0["K"]
+    codes, s, x = c0_inputs(0)
+    nbuf = 16
+    dW = [torch.from_numpy(codes).cuda() for _ in range(nbuf)]
+    dS = torch.from_numpy(s).cuda()
+    dx = torch.from_numpy(x.view(np.int16)).cuda()
+    dy = torch.empty((M, N), dtype=torch.int16, device="cuda")
+    st = torch.cuda.Stream()
+    sp = G.C.c_void_p(st.cuda_stream)
+    G.apus_gcuda_set_pdl(1)
+
+    def step(i):
+        G.check(G.apus_gcuda_fp8blk_linear_dev(G.ptr(dW[i % nbuf]), G.ptr(dS), G.ptr(dx), G.ptr(dy),
+                                               M, N, K, sp), "linear")
+    for i in range(warmup):
+        step(i)
+    st.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(reps):
+        step(i)
+    e1.record(st)
+    st.synchronize()
+    G.apus_gcuda_set_pdl(0)
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    hbm, _, src = peaks()
+    algo = c0_algo_bytes()
+    gbs = algo / us / 1e3
+    del dW
+    torch.cuda.empty_cache()
+    return {"workload": "config0: FP8 128x128 block-dequant GEMV, M=4, N=K=4096", "kernel": "k_gemv_tma<true>",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4), "peak_source": src, "algo_bytes_per_launch": algo,
+                         "avg_launch_us": round(us, 3), "launches": reps,
+                         "l2": "16 rotating weight copies (270 MB > L2)"}}
+
+
 _HOLD = {}
 
 
@@ -408,102 +454,13 @@ def cpu_c1(h, budget_s=10.0):
 
 # --------------------------------------------------------------------------
 # config 2: the scaled glm5_next stack + MTP speculative decode (headline)
-def c2_config(small=False):
-    """4 layers at hidden 4096 (3 KDA 32x128 + DSA at layer
-    3 with the real MLA / Lightning-indexer dims), every layer the config-1
-    MoE (288 experts top-8 + shared, inter 1024), vocab 154880, one NextN
-    layer.  Other fields from the reference's config.json."""
-    kw = dict(hidden_size=4096, vocab_size=154880, num_hidden_layers=4, rms_norm_eps=1e-5, hc_mult=4,
-              hc_sinkhorn_iters=20, hc_eps=1e-6, first_k_dense_replace=0, intermediate_size=12288,
-              moe_intermediate_size=1024, n_routed_experts=288, n_shared_experts=1, num_experts_per_tok=8,
-              routed_scaling_factor=2.5, norm_topk_prob=1, swiglu_limit=10.0, num_attention_heads=64,
-              q_lora_rank=1536, kv_lora_rank=512, qk_nope_head_dim=256, v_head_dim=256, index_n_heads=32,
-              index_head_dim=128, index_topk=2048, index_kpool=4, index_kpool_always_select_tail=1,
-              linear_num_heads=32, linear_head_dim=128, linear_conv_kernel_dim=4, linear_lower_bound=-5.0,
-              num_nextn_predict_layers=1, layer_is_dsa=[0, 0, 0, 1], mlp_is_sparse=[1, 1, 1, 1])
-    if small:
-        kw.update(n_routed_experts=16, vocab_size=16384)
-    return kw
-
-
 C2 = dict(prompt=512, depth=4, seed=2)   # BASELINE "depth 3" = 4 verify rows (reference APUS_SPEC_K 4)
 
 
-def c2_weights(kw, seed, keep=None):
-    """Seeded synthetic weights for every tensor of tensor_specs(kw), made
-    with torch on the GPU and returned as host numpy arrays (both bench arms
-    load the same arrays).  Experts: BASELINE config 0 codes (E4M3 of
-    N(0,1)*64) with log-uniform [1e-4, 1e-2] block scales; router BF16
-    N(0, 0.02) with a zero bias; embeddings and head BF16 N(0, 0.02); the DSA
-    FP8 linears amax/448 block-scaled N(0, 1/sqrt(K)); BF16 matrices
-    N(0, 1/sqrt(K)); norms 1 + 0.05 N(0,1).  keep(name): tensors to return
-    (the others are still drawn, so every rank sees the same stream)."""
-    import math
-    import numpy as np
-    import torch
-    import apus_gcuda as G
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    g = torch.Generator(device=dev).manual_seed(seed)
-    out = {}
-    specs = G.tensor_specs(kw)
-    expert = lambda n: ".mlp." in n
-
-    def bf16(t):
-        return t.to(torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16)
-
-    i = 0
-    while i < len(specs):
-        name, shape, dt, kind = specs[i]
-        if kind == "e4m3":
-            sname, sshape = specs[i + 1][0], specs[i + 1][1]
-            O_, K_ = shape
-            if expert(name):
-                v = torch.clamp(torch.randn(shape, generator=g, device=dev) * 64, -448, 448)
-                codes = v.to(torch.float8_e4m3fn)
-                lo, hi = math.log(1e-4), math.log(1e-2)
-                sc = torch.exp(lo + (hi - lo) * torch.rand(sshape, generator=g, device=dev))
-            else:
-                w = torch.randn(shape, generator=g, device=dev) / math.sqrt(K_)
-                nbo, nbk = sshape
-                wp = torch.zeros((nbo * 128, nbk * 128), device=dev)
-                wp[:O_, :K_] = w
-                blk = wp.view(nbo, 128, nbk, 128)
-                amax = blk.abs().amax(dim=(1, 3)).clamp_min(2.0 ** -126)
-                sc = amax / 448.0
-                q = torch.clamp(blk / sc[:, None, :, None], -448, 448).view(nbo * 128, nbk * 128)
-                codes = q[:O_, :K_].to(torch.float8_e4m3fn)
-            if keep is None or keep(name):
-                out[name] = codes.view(torch.uint8).cpu().numpy()
-                out[sname] = sc.float().cpu().numpy()
-            i += 2
-            continue
-        if kind == "f32":
-            if name.endswith("e_score_correction_bias"):
-                v = torch.zeros(shape, device=dev)
-            elif name.endswith("_scale"):
-                v = 1.0 + 0.1 * torch.randn(shape, generator=g, device=dev)
-            elif name.endswith("_base"):
-                v = 0.25 * torch.randn(shape, generator=g, device=dev)
-            else:                                   # A_log, dt_bias
-                v = 0.5 * torch.randn(shape, generator=g, device=dev)
-            out[name] = v.float().cpu().numpy()
-        else:
-            if len(shape) == 1 or name.endswith("compress_ape"):
-                if name.endswith("bias") or name.endswith("compress_ape"):
-                    v = 0.05 * torch.randn(shape, generator=g, device=dev)
-                else:
-                    v = 1.0 + 0.05 * torch.randn(shape, generator=g, device=dev)
-            elif name in ("embed_tokens.weight", "lm_head.weight") or name.endswith("mlp.gate.weight"):
-                v = 0.02 * torch.randn(shape, generator=g, device=dev)
-            elif name.endswith("_conv1d.weight"):
-                v = 0.25 * torch.randn(shape, generator=g, device=dev)
-            else:
-                v = torch.randn(shape, generator=g, device=dev) / math.sqrt(shape[-1])
-            out[name] = bf16(v)
-        i += 1
-    if dev == "cuda":
-        torch.cuda.empty_cache()
-    return out
+def c2_workload(temp=0.0, top_p=1.0, seed=0):
+    return ("config2: scaled glm5_next (4 layers: 3 KDA 32x128 + 1 DSA, MoE 288 top-8 inter 1024, vocab 154880)"
+            " + 1 NextN MTP layer, " + (f"sampled spec decode (temp {temp}, top_p {top_p}, seed {seed})"
+                                       if temp > 0 else "greedy spec decode"))
 
 
 def c2_prompt(kw, seed):
@@ -605,7 +562,7 @@ def bench_c2(args, ws, rank, W=None):
     depth = C2["depth"]
     ep = ws > 1 and args.mode == "ep"
     if W is None:
-        W = c2_weights(kw, C2["seed"], keep=G.ep_owns(kw, rank, ws) if ep else None)
+        W = c2_weights(kw, C2["seed"], keep=ep_owns(kw, rank, ws) if ep else None)
     prompt = c2_prompt(kw, C2["seed"])[:args.prompt or C2["prompt"]]
     cap = len(prompt) + depth * (2 * args.steps + 2 * args.warmup) + 64
     m = G.GModel(G.make_config(**kw), has_mtp=True, kv_cap=cap, depth=depth,
@@ -656,15 +613,12 @@ def bench_c2(args, ws, rank, W=None):
     offered = s1["offered"] - s0["offered"]
     accepted = s1["accepted"] - s0["accepted"]
     agg = 1 if ep else ws       # EP: one sequence across the GPUs; replicas: ws sequences
-    out = {"metric": METRIC, "value": round(tok_s * agg, 2), "unit": "accepted tok/s (emitted tokens / s)",
+    out = {"metric": METRIC, "value": round(tok_s * agg, 2), "unit": "accepted tok/s",
            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 4),
            "higher_is_better": True, "scaling": "strong" if ep else "weak", "vs_baseline": None,
            "dtype": "bf16 activations, fp8e4m3/bf16 weights, f32 accumulation",
            "data": f"synthetic random-init weights (seed {C2['seed']}), {len(prompt)} uniform random prompt ids",
-           "config": {"workload": "config2: scaled glm5_next (4 layers: 3 KDA 32x128 + 1 DSA, MoE 288 top-8 "
-                                  "inter 1024, vocab 154880) + 1 NextN MTP layer, " + (
-                                      f"sampled spec decode (temp {args.temp}, top_p {args.top_p}, seed {args.seed})"
-                                      if args.temp > 0 else "greedy spec decode"),
+           "config": {"workload": c2_workload(args.temp, args.top_p, args.seed),
                       "depth": "BASELINE depth 3 = 4 verify rows (reference APUS_SPEC_K 4)",
                       "prompt": len(prompt),
                       "parallelism": (f"ep{ws}: routed experts and lm_head rows split over {ws} GPUs, "
@@ -714,14 +668,33 @@ def bench_c2(args, ws, rank, W=None):
     for _ in range(args.steps):
         n_e2e += len(m.spec_step())
     e2e = max_over_ranks(time.perf_counter() - t0, ws)
-    out["e2e"] = {"value": round(n_e2e / e2e * agg, 2), "unit": "accepted tok/s through apus_gcuda_gspec_step",
-                  "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 2 * int(c1["ctl_bytes"]),
-                  "note": "no per-step inputs cross to the device; the control block is read back twice"}
+    out["e2e"] = {"value": round(n_e2e / e2e * agg, 2), "unit": "accepted tok/s",
+                  "path": "apus_gcuda_gspec_step per step, emitted tokens copied to the host",
+                  "h2d_bytes_per_step": 0, "d2h_bytes_per_step": int(c1["ctl_bytes"]),
+                  "note": "no per-step inputs cross to the device (the held token and drafts stay resident); "
+                          "the control block with the emitted tokens is read back once a step"}
+    # the same decode with the prompt upload and prefill inside the timed
+    # region: host prompt ids in, host tokens out (a whole request)
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    m.spec_prefill(prompt)
+    t_pf = time.perf_counter()
+    n_req = 0
+    for _ in range(args.steps):
+        n_req += len(m.spec_step())
+    t1 = time.perf_counter()
+    req = max_over_ranks(t1 - t0, ws)
+    out["e2e_request"] = {"value": round(n_req / req * agg, 2), "unit": "accepted tok/s",
+                          "path": "apus_gcuda_gspec_prefill (host prompt ids) + apus_gcuda_gspec_step x steps",
+                          "prompt": len(prompt), "prefill_ms": round((t_pf - t0) * 1e3, 2),
+                          "h2d_bytes": int(len(prompt) * 4), "d2h_bytes_per_step": int(c1["ctl_bytes"])}
     m.close()
+    out["fp8_gemv"] = fp8_gemv_leg()
     return out, W
 
 
-def cpu_c2(W, budget_s=20.0, prompt_len=64, log=None):
+def cpu_c2(W, budget_s=20.0, prompt_len=C2["prompt"], log=None):
     """The reference's own speculative engine (oracle/_ref: apus_gspec_* over
     apus_gmodel, compiled from the reference sources) on the host cores with
     the same weights: prefill of the first prompt_len prompt tokens (not
@@ -758,8 +731,8 @@ def cpu_c2(W, budget_s=20.0, prompt_len=64, log=None):
     dt = time.perf_counter() - t0
     return {"value": round(tok / dt, 4), "unit": "accepted tok/s", "cores": O.REF.apus_ref_threads(),
             "kind": "reference",
-            "sample": f"{n} apus_gspec_step calls ({tok} tokens, {dt:.1f} s) after a {prompt_len}-token prefill "
-                      f"(the bench prompt's first {prompt_len} ids; setup {t_load:.0f} s untimed)"}
+            "sample": f"{n} apus_gspec_step calls ({tok} tokens, {dt:.1f} s) after the {prompt_len}-token prompt's "
+                      f"prefill (weights, expert dequant and prefill {t_load:.0f} s, untimed)"}
 
 
 def tc_table(rows=(512, 2048), reps=20):
@@ -920,7 +893,10 @@ def main():
             else:
                 cb = cpu_c2(c2_weights(c2_config(), C2["seed"]), budget_s=args.cpu_budget)
                 line.update({"value": cb["value"], "unit": cb["unit"],
-                             "config": {"workload": "config2 on host cores (reference apus_gspec_*)"},
+                             "config": {"workload": c2_workload(),
+                                        "depth": "BASELINE depth 3 = 4 verify rows (reference APUS_SPEC_K 4)",
+                                        "prompt": C2["prompt"],
+                                        "parallelism": f"the reference's CPU engine on {cb['cores']} host threads"},
                              "cpu_baseline": cb,
                              "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                                      "d2h_bytes_per_step": 0}})
@@ -948,6 +924,8 @@ def main():
         out, W = bench_c2(args, ws, rank)
         if rank == 0 and not args.quick and ws == 1 and args.temp <= 0:   # the reference leg decodes greedily
             out["cpu_baseline"] = cpu_c2(W, budget_s=args.cpu_budget)
+            if "fp8_gemv" in out:
+                out["fp8_gemv"]["cpu_baseline"] = cpu_c0(budget_s=5.0)
         if rank == 0:
             print(json.dumps(out), flush=True)
     elif args.config == 1:

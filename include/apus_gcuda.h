@@ -112,11 +112,15 @@ int apus_gcuda_bf16_gemm_argmax_dev(const uint16_t *w, const uint16_t *x, uint16
  * file-scope device array instead of the grow-only pool, for callers that
  * may not call cudaMalloc/cudaFree (an HBM budget already handed out, or
  * streams that cannot take the implied device synchronisation).  Limits:
- * M <= 64 and O, K whose split-K scratch fits the array (K <= 4096 needs
- * none; K <= 8192 allows O up to about 65,000); larger shapes return -1 with
- * the reason in apus_gcuda_last_error().  The first call on a device sets up
- * the array's address (make it before any stream capture); calls that
- * overlap in time share the array and race.  Outputs are bitwise those of
+ * M <= 64 and O, K whose split-K scratch fits the array.  Split-K scratch
+ * is only needed when the shape splits K (a function of O and K: small O
+ * splits even a K of 2048); every K <= 4096 fits, and K = 8192 fits O up to
+ * about 65,000.  Larger shapes return -1 with the reason in
+ * apus_gcuda_last_error().  The first call on a device sets up the array's
+ * address (make it before any stream capture).  Calls that overlap in time
+ * share the array and race; serialising them is the caller's job, while the
+ * library's own per-device set-up (kernel attributes, SM count) is
+ * thread-safe.  Outputs are bitwise those of
  * apus_gcuda_bf16_gemm_argmax_dev. */
 int apus_gcuda_bf16_gemm_argmax_static_dev(const uint16_t *w, const uint16_t *x, uint16_t *y,
                                            int32_t *ids, size_t M, size_t O, size_t K,

@@ -188,6 +188,18 @@ int apus_gcuda_model_counters(ApusGcudaModel *m, uint64_t *out, size_t n);
  * "q", "kvb", "attn", ...).  layer -1 clears the stop. */
 int apus_gcuda_model_debug_stop(ApusGcudaModel *m, int layer, int stage);
 int apus_gcuda_model_debug_read(ApusGcudaModel *m, const char *name, void *host, size_t bytes);
+/* More inspection names for debug_read: "moe_idx" / "moe_w" (the last MoE
+ * call's routing, [8][16] int32 / f32, ascending experts), "logits" ([8][V]
+ * BF16 rows of the last forward that wrote logits), "drafts" / "raw_drafts"
+ * (int32, the verify drafts of the next step / the MTP chain's own drafts
+ * before forced agreement), and the committed sequence state: "kda_conv.L"
+ * [3*qkv][K-1] BF16, "kda_rec.L" [H][D][D] f32, "dsa_k.L" [AH][n][qd],
+ * "dsa_v.L" [AH][n][vd], "dsa_ik.L" / "dsa_ig.L" [n][ID] BF16 (n committed
+ * rows; L = num_hidden_layers names the MTP block).  A decode_batch stopped
+ * by debug_stop commits nothing.  gspec_keep_logits(1): every speculative
+ * step also writes its verify rows' BF16 logits (rows 0..depth-1 of
+ * "logits"), so a test can replay the accept walk on them. */
+int apus_gcuda_gspec_keep_logits(ApusGcudaModel *m, int on);
 
 #ifdef __cplusplus
 }

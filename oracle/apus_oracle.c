@@ -7,7 +7,9 @@
 #include "apus_oracle.h"
 
 #include <math.h>
+#include <pthread.h>
 #include <stdlib.h>
+#include <unistd.h>
 #include <string.h>
 
 /* ------------------------------------------------------------------ num */
@@ -99,32 +101,90 @@ float orc_pw_sum(const float *a, size_t n) {
 /* ---------------------------------------------------------- linear leaf */
 
 /* c/fp8blk.h:115-136 — one fp32 multiply, then BF16 RNE */
+/* Large loops over output rows are split over host threads: every output
+ * element is still computed by one thread in the reference's order, so the
+ * results do not depend on the thread count (ORC_THREADS, default: the
+ * online cores). */
+typedef void (*par_fn)(void *ctx, size_t i0, size_t i1);
+typedef struct { par_fn fn; void *ctx; size_t i0, i1; } ParJob;
+
+static void *par_run(void *a) {
+    ParJob *j = (ParJob *)a;
+    j->fn(j->ctx, j->i0, j->i1);
+    return NULL;
+}
+
+static int par_threads(void) {
+    static int n = 0;
+    if (!n) {
+        const char *e = getenv("ORC_THREADS");
+        n = e ? atoi(e) : (int)sysconf(_SC_NPROCESSORS_ONLN);
+        if (n < 1) n = 1;
+        if (n > 64) n = 64;
+    }
+    return n;
+}
+
+static void par_for(size_t n, size_t work, par_fn fn, void *ctx) {
+    int nt = par_threads();
+    if (work < ((size_t)1 << 22) || nt < 2 || n < 2) { fn(ctx, 0, n); return; }
+    if ((size_t)nt > n) nt = (int)n;
+    pthread_t th[64];
+    ParJob jb[64];
+    for (int t = 0; t < nt; t++) {
+        jb[t].fn = fn; jb[t].ctx = ctx;
+        jb[t].i0 = n * (size_t)t / (size_t)nt;
+        jb[t].i1 = n * (size_t)(t + 1) / (size_t)nt;
+    }
+    int started[64] = {0};
+    for (int t = 1; t < nt; t++) started[t] = pthread_create(&th[t], NULL, par_run, &jb[t]) == 0;
+    par_run(&jb[0]);
+    for (int t = 1; t < nt; t++) {
+        if (started[t]) pthread_join(th[t], NULL);
+        else par_run(&jb[t]);
+    }
+}
+
+typedef struct { const uint8_t *w; const float *ws; uint16_t *out; size_t K, nkb; } DeqCtx;
+
+static void deq_rows(void *a, size_t o0, size_t o1) {
+    DeqCtx *c = (DeqCtx *)a;
+    for (size_t o = o0; o < o1; o++)
+        for (size_t k = 0; k < c->K; k++)
+            c->out[o * c->K + k] =
+                orc_bf16_bits(orc_e4m3_f32(c->w[o * c->K + k]) * c->ws[(o / 128) * c->nkb + k / 128]);
+}
+
 void orc_fp8_dequant(const uint8_t *w, const float *ws, uint16_t *out, size_t O, size_t K) {
-    size_t nkb = (K + 127) / 128;
-    for (size_t o = 0; o < O; o++)
-        for (size_t k = 0; k < K; k++)
-            out[o * K + k] = orc_bf16_bits(orc_e4m3_f32(w[o * K + k]) * ws[(o / 128) * nkb + k / 128]);
+    DeqCtx c = {w, ws, out, K, (K + 127) / 128};
+    par_for(O, O * K, deq_rows, &c);
 }
 
 /* c/bf16.h:202-217 — fp32 accumulate from +0, strictly ascending k */
-void orc_bf16_gemm_f32(const uint16_t *w, const uint16_t *x, float *y, size_t M, size_t O, size_t K) {
-    for (size_t m = 0; m < M; m++)
-        for (size_t o = 0; o < O; o++) {
-            const uint16_t *wr = w + o * K, *xr = x + m * K;
+typedef struct { const uint16_t *w, *x; float *yf; uint16_t *y; size_t M, O, K; } GemmCtx;
+
+/* rows o0..o1 of W against every activation row; each output sums from +0
+ * in strictly ascending k */
+static void gemm_rows(void *a, size_t o0, size_t o1) {
+    GemmCtx *c = (GemmCtx *)a;
+    for (size_t m = 0; m < c->M; m++)
+        for (size_t o = o0; o < o1; o++) {
+            const uint16_t *wr = c->w + o * c->K, *xr = c->x + m * c->K;
             float acc = 0.0f;
-            for (size_t k = 0; k < K; k++) acc += orc_bf16_f32(wr[k]) * orc_bf16_f32(xr[k]);
-            y[m * O + o] = acc;
+            for (size_t k = 0; k < c->K; k++) acc += orc_bf16_f32(wr[k]) * orc_bf16_f32(xr[k]);
+            if (c->yf) c->yf[m * c->O + o] = acc;
+            else c->y[m * c->O + o] = orc_bf16_bits(acc);
         }
 }
 
+void orc_bf16_gemm_f32(const uint16_t *w, const uint16_t *x, float *y, size_t M, size_t O, size_t K) {
+    GemmCtx c = {w, x, y, NULL, M, O, K};
+    par_for(O, M * O * K, gemm_rows, &c);
+}
+
 void orc_bf16_gemm(const uint16_t *w, const uint16_t *x, uint16_t *y, size_t M, size_t O, size_t K) {
-    for (size_t m = 0; m < M; m++)
-        for (size_t o = 0; o < O; o++) {
-            const uint16_t *wr = w + o * K, *xr = x + m * K;
-            float acc = 0.0f;
-            for (size_t k = 0; k < K; k++) acc += orc_bf16_f32(wr[k]) * orc_bf16_f32(xr[k]);
-            y[m * O + o] = orc_bf16_bits(acc);
-        }
+    GemmCtx c = {w, x, NULL, y, M, O, K};
+    par_for(O, M * O * K, gemm_rows, &c);
 }
 
 /* c/gdsa.h:525-534 — dequant -> BF16 -> BF16 GEMM */

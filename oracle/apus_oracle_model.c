@@ -37,11 +37,18 @@ typedef struct {
     const uint16_t *enorm, *hnorm, *eh_proj, *shared_norm;
 } OLayer;
 
+typedef struct { const uint8_t *c; uint16_t *deq; } DeqEntry;
+
 struct OrcModel {
     OrcConfig c;
     int has_mtp;
     OLayer *L;                       /* [num_hidden_layers + has_mtp] */
     const uint16_t *embed, *norm, *head;
+    /* BF16 copies of the FP8 matrices, made on first use (the reference
+     * engine likewise holds dequantized experts, c/gmodel.h:1003-1073); the
+     * arithmetic is orc_fp8_dequant's either way */
+    DeqEntry *deq;
+    size_t ndeq, capdeq;
 };
 
 typedef struct {
@@ -65,13 +72,48 @@ struct OrcMtpState {
 /* ------------------------------------------------------------ helpers */
 
 static void *xc(size_t n) { void *p = calloc(n ? n : 1, 1); if (!p) abort(); return p; }
+static size_t kda_bytes(const OrcConfig *c, int rec);
 
 static void gemm(const uint16_t *w, const uint16_t *x, uint16_t *y, size_t M, size_t O, size_t K) {
     orc_bf16_gemm(w, x, y, M, O, K);
 }
 
-static void fp8lin(Fp8 w, const uint16_t *x, uint16_t *y, size_t M, size_t O, size_t K) {
-    orc_fp8_linear(w.c, w.s, x, y, M, O, K);
+static const uint16_t *deq_of(const OrcModel *cm, Fp8 w, size_t O, size_t K) {
+    OrcModel *m = (OrcModel *)cm;
+    size_t h = ((uintptr_t)w.c >> 4) * 0x9E3779B97F4A7C15ull;
+    if (m->capdeq) {
+        for (size_t i = h % m->capdeq;; i = (i + 1) % m->capdeq) {
+            if (!m->deq[i].c) break;
+            if (m->deq[i].c == w.c) return m->deq[i].deq;
+        }
+    }
+    if (2 * (m->ndeq + 1) > m->capdeq) {   /* grow and rehash */
+        size_t nc = m->capdeq ? 2 * m->capdeq : 256;
+        DeqEntry *nt = xc(nc * sizeof *nt);
+        for (size_t j = 0; j < m->capdeq; j++) {
+            if (!m->deq[j].c) continue;
+            size_t i = (((uintptr_t)m->deq[j].c >> 4) * 0x9E3779B97F4A7C15ull) % nc;
+            while (nt[i].c) i = (i + 1) % nc;
+            nt[i] = m->deq[j];
+        }
+        free(m->deq);
+        m->deq = nt;
+        m->capdeq = nc;
+    }
+    uint16_t *b = malloc(O * K * 2);
+    if (!b) abort();
+    orc_fp8_dequant(w.c, w.s, b, O, K);
+    size_t i = h % m->capdeq;
+    while (m->deq[i].c) i = (i + 1) % m->capdeq;
+    m->deq[i].c = w.c;
+    m->deq[i].deq = b;
+    m->ndeq++;
+    return b;
+}
+
+/* c/gdsa.h:525-534 fp8_linear: dequant -> BF16 -> BF16 GEMM */
+static void fp8lin(const OrcModel *m, Fp8 w, const uint16_t *x, uint16_t *y, size_t M, size_t O, size_t K) {
+    orc_bf16_gemm(deq_of(m, w, O, K), x, y, M, O, K);
 }
 
 /* c/gdsa.h:258-274 — weighted RMSNorm: f32 pairwise mean, bf16 round, x w */
@@ -229,11 +271,11 @@ static void router(const OrcModel *m, const OLayer *Ly, const uint16_t *x, int32
 }
 
 /* c/gmoe.h:210-227 SwiGLU expert on FP8 weights (dequant -> BF16 GEMV) */
-static void expert(Fp8 g, Fp8 u, Fp8 dn, const uint16_t *x, size_t d, size_t inter, float limit,
-                   uint16_t *out) {
+static void expert(const OrcModel *m, Fp8 g, Fp8 u, Fp8 dn, const uint16_t *x, size_t d, size_t inter,
+                   float limit, uint16_t *out) {
     uint16_t *gv = xc(inter * 2), *uv = xc(inter * 2), *h = xc(inter * 2);
-    fp8lin(g, x, gv, 1, inter, d);
-    fp8lin(u, x, uv, 1, inter, d);
+    fp8lin(m, g, x, gv, 1, inter, d);
+    fp8lin(m, u, x, uv, 1, inter, d);
     for (size_t i = 0; i < inter; i++) {
         float a = orc_bf16_f32(gv[i]), b = orc_bf16_f32(uv[i]);
         if (a > limit) a = limit;
@@ -242,7 +284,7 @@ static void expert(Fp8 g, Fp8 u, Fp8 dn, const uint16_t *x, size_t d, size_t int
         float hv = orc_bf16_round(a * orc_sigmoid(a));
         h[i] = orc_bf16_bits(orc_bf16_round(hv * b));
     }
-    fp8lin(dn, h, out, 1, d, inter);
+    fp8lin(m, dn, h, out, 1, d, inter);
     free(h); free(uv); free(gv);
 }
 
@@ -279,13 +321,13 @@ void orc_moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, 
             int slot = -1;
             for (int j = 0; j < topk; j++) if (idx[j] == e) { slot = j; break; }
             if (slot < 0) continue;
-            expert(Ly->eg[e], Ly->eu[e], Ly->ed[e], xt, d, inter, c->swiglu_limit, eo);
+            expert(m, Ly->eg[e], Ly->eu[e], Ly->ed[e], xt, d, inter, c->swiglu_limit, eo);
             for (size_t i = 0; i < d; i++) {
                 float contrib = orc_bf16_round(orc_bf16_f32(eo[i]) * wt[slot]);
                 y[i] = orc_bf16_round(y[i] + contrib);
             }
         }
-        expert(Ly->sg, Ly->su, Ly->sd, xt, d, sinter, c->swiglu_limit, sh);
+        expert(m, Ly->sg, Ly->su, Ly->sd, xt, d, sinter, c->swiglu_limit, sh);
         for (size_t i = 0; i < d; i++) out[t * d + i] = orc_bf16_bits(y[i] + orc_bf16_f32(sh[i]));
     }
     free(sh); free(eo); free(y);
@@ -411,7 +453,7 @@ static size_t dsa_width(const OrcConfig *c) {
 /* c/gdsa.h:307-449 indexer: appends this call's idx rows at st->n, rebuilds
  * every full pool, scores, selects. */
 static void indexer(const OrcModel *m, const OLayer *W, const uint16_t *x, const uint16_t *qres,
-                    size_t s, ODsa *st, int32_t *topk) {
+                    size_t s, ODsa *st, int32_t *topk, float *score_out, size_t score_ld) {
     const OrcConfig *c = &m->c;
     size_t d = (size_t)c->hidden_size, ql = (size_t)c->q_lora_rank;
     size_t IH = (size_t)c->index_n_heads, ID = (size_t)c->index_head_dim, kp = (size_t)c->index_kpool;
@@ -459,6 +501,8 @@ static void indexer(const OrcModel *m, const OLayer *W, const uint16_t *x, const
         }
         for (size_t p = 0; p < nf; p++)
             if (p * kp + (kp - 1) > q_pos) sm[p] = NEG_INF;
+        if (score_out)
+            for (size_t p = 0; p < nf && p < score_ld; p++) score_out[t * score_ld + p] = sm[p];
         size_t sk = (size_t)c->index_topk / kp;
         if (sk > nf) sk = nf;
         int32_t *row = topk + t * width;
@@ -520,7 +564,7 @@ static void attention(const OrcModel *m, const uint16_t *q, const ODsa *st, size
 
 /* c/gdsa.h:555-674 forward3: s tokens in one shot (s = 1 for decode) */
 static void dsa_forward(const OrcModel *m, const OLayer *W, const uint16_t *x, size_t s, ODsa *st,
-                        uint16_t *out) {
+                        uint16_t *out, int32_t *topk_out, float *score_out, size_t score_ld) {
     const OrcConfig *c = &m->c;
     size_t d = (size_t)c->hidden_size, H = (size_t)c->num_attention_heads, qd = (size_t)c->qk_nope_head_dim;
     size_t vd = (size_t)c->v_head_dim, ql = (size_t)c->q_lora_rank, kl = (size_t)c->kv_lora_rank;
@@ -528,10 +572,10 @@ static void dsa_forward(const OrcModel *m, const OLayer *W, const uint16_t *x, s
     uint16_t *qa = xc(s * ql * 2), *qres = xc(s * ql * 2), *q = xc(s * H * qd * 2), *kv = xc(s * kl * 2);
     uint16_t *kpass = xc(s * kl * 2), *kvb = xc(s * H * (qd + vd) * 2), *attn = xc(s * H * vd * 2);
     int32_t *topk = xc(s * width * 4);
-    fp8lin(W->q_a, x, qa, s, ql, d);
+    fp8lin(m, W->q_a, x, qa, s, ql, d);
     for (size_t t = 0; t < s; t++) orc_rmsnorm(qa + t * ql, W->q_a_norm, qres + t * ql, ql, c->rms_norm_eps);
-    fp8lin(W->q_b, qres, q, s, H * qd, ql);
-    fp8lin(W->kv_a, x, kv, s, kl, d);
+    fp8lin(m, W->q_b, qres, q, s, H * qd, ql);
+    fp8lin(m, W->kv_a, x, kv, s, kl, d);
     for (size_t t = 0; t < s; t++) orc_rmsnorm(kv + t * kl, W->kv_a_norm, kpass + t * kl, kl, c->rms_norm_eps);
     gemm(W->kv_b, kpass, kvb, s, H * (qd + vd), kl);
     for (size_t t = 0; t < s; t++)
@@ -540,19 +584,28 @@ static void dsa_forward(const OrcModel *m, const OLayer *W, const uint16_t *x, s
             memcpy(st->v + h * st->cap * vd + (base + t) * vd, kvb + t * H * (qd + vd) + h * (qd + vd) + qd,
                    vd * 2);
         }
-    indexer(m, W, x, qres, s, st, topk);
+    indexer(m, W, x, qres, s, st, topk, score_out, score_ld);
+    if (topk_out) memcpy(topk_out, topk, s * width * 4);
     st->n = base + s;
     attention(m, q, st, s, topk, attn);
-    fp8lin(W->o, attn, out, s, d, H * vd);
+    fp8lin(m, W->o, attn, out, s, d, H * vd);
     free(topk); free(attn); free(kvb); free(kpass); free(kv); free(q); free(qres); free(qa);
 }
 
 /* c/gdsa.h:682-690 decode_batch2: per-token interleave */
 void orc_dsa_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s, OrcState *st,
                     uint16_t *out) {
-    size_t d = (size_t)m->c.hidden_size;
+    orc_dsa_decode_sel(m, layer, x, s, st, out, NULL, NULL, 0);
+}
+
+size_t orc_dsa_width(const OrcModel *m) { return dsa_width(&m->c); }
+
+void orc_dsa_decode_sel(const OrcModel *m, int layer, const uint16_t *x, size_t s, OrcState *st,
+                        uint16_t *out, int32_t *topk, float *scores, size_t score_ld) {
+    size_t d = (size_t)m->c.hidden_size, width = dsa_width(&m->c);
     for (size_t t = 0; t < s; t++)
-        dsa_forward(m, &m->L[layer], x + t * d, 1, &st->dsa[layer], out + t * d);
+        dsa_forward(m, &m->L[layer], x + t * d, 1, &st->dsa[layer], out + t * d, topk ? topk + t * width : NULL,
+                    scores ? scores + t * score_ld : NULL, score_ld);
 }
 
 /* -------------------------------------------------------------- model */
@@ -575,6 +628,8 @@ void orc_model_free(OrcModel *m) {
     if (!m) return;
     int nl = m->c.num_hidden_layers + (m->has_mtp ? 1 : 0);
     for (int l = 0; l < nl; l++) { free(m->L[l].eg); free(m->L[l].eu); free(m->L[l].ed); }
+    for (size_t i = 0; i < m->capdeq; i++) free(m->deq[i].deq);
+    free(m->deq);
     free(m->L);
     free(m);
 }
@@ -703,6 +758,38 @@ void orc_state_free(OrcState *st) {
 
 size_t orc_state_pos(const OrcState *st) { return st->pos; }
 
+void orc_state_set_pos(OrcState *st, size_t pos) { st->pos = pos; }
+
+static int dsa_load(ODsa *d, const OrcConfig *c, const uint16_t *k, const uint16_t *v, const uint16_t *ik,
+                    const uint16_t *ig, size_t n) {
+    size_t H = (size_t)c->num_attention_heads, qd = (size_t)c->qk_nope_head_dim, vd = (size_t)c->v_head_dim;
+    size_t ID = (size_t)c->index_head_dim;
+    if (n > d->cap) return -1;
+    for (size_t h = 0; h < H; h++) {
+        memcpy(d->k + h * d->cap * qd, k + h * n * qd, n * qd * 2);
+        memcpy(d->v + h * d->cap * vd, v + h * n * vd, n * vd * 2);
+    }
+    memcpy(d->ik, ik, n * ID * 2);
+    memcpy(d->ig, ig, n * ID * 2);
+    d->n = n;
+    return 0;
+}
+
+int orc_state_load_kda(OrcState *st, int layer, const uint16_t *conv, const float *rec) {
+    const OrcConfig *c = &st->m->c;
+    if (layer < 0 || layer >= c->num_hidden_layers || c->layer_is_dsa[layer]) return -1;
+    memcpy(st->conv[layer], conv, kda_bytes(c, 0));
+    memcpy(st->rec[layer], rec, kda_bytes(c, 1));
+    return 0;
+}
+
+int orc_state_load_dsa(OrcState *st, int layer, const uint16_t *k, const uint16_t *v, const uint16_t *ik,
+                       const uint16_t *ig, size_t n) {
+    const OrcConfig *c = &st->m->c;
+    if (layer < 0 || layer >= c->num_hidden_layers || !c->layer_is_dsa[layer]) return -1;
+    return dsa_load(&st->dsa[layer], c, k, v, ik, ig, n);
+}
+
 /* c/gmodel.h:1439-1626 apus_gm_run with decode = 1 */
 int orc_decode_batch(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
                      uint16_t *logits, uint16_t *h_out, uint16_t *yn_out) {
@@ -727,7 +814,7 @@ int orc_decode_batch(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
             } else if (!c->mlp_is_sparse[l]) {
                 size_t inter = (size_t)c->intermediate_size;
                 for (size_t t = 0; t < s; t++)
-                    expert(m->L[l].mlp_g, m->L[l].mlp_u, m->L[l].mlp_d, x + t * d, d, inter,
+                    expert(m, m->L[l].mlp_g, m->L[l].mlp_u, m->L[l].mlp_d, x + t * d, d, inter,
                            c->swiglu_limit, sub + t * d);
             } else {
                 orc_moe_forward(m, l, x, s, sub, NULL, NULL, NULL);
@@ -758,6 +845,13 @@ OrcMtpState *orc_mtp_state_new(const OrcModel *m, size_t cap) {
     return st;
 }
 
+int orc_mtp_state_load(const OrcModel *m, OrcMtpState *mst, const uint16_t *k, const uint16_t *v,
+                       const uint16_t *ik, const uint16_t *ig, size_t n) {
+    if (dsa_load(&mst->dsa, &m->c, k, v, ik, ig, n)) return -1;
+    mst->pos = n;
+    return 0;
+}
+
 void orc_mtp_state_free(OrcMtpState *st) {
     if (!st) return;
     dsa_free(&st->dsa);
@@ -780,7 +874,7 @@ int orc_mtp_forward(OrcModel *m, OrcMtpState *mst, const int32_t *ids, const uin
     }
     gemm(W->eh_proj, eh, x, s, d, 2 * d);
     for (size_t t = 0; t < s; t++) orc_rmsnorm(x + t * d, W->input_norm, xn + t * d, d, eps);
-    dsa_forward(m, W, xn, s, &mst->dsa, sub);
+    dsa_forward(m, W, xn, s, &mst->dsa, sub, NULL, NULL, 0);
     for (size_t i = 0; i < s * d; i++) x[i] = orc_bf16_bits(orc_bf16_f32(x[i]) + orc_bf16_f32(sub[i]));
     for (size_t t = 0; t < s; t++) orc_rmsnorm(x + t * d, W->post_norm, xn + t * d, d, eps);
     orc_moe_forward(m, Lm, xn, s, sub, NULL, NULL, NULL);
@@ -801,6 +895,9 @@ struct OrcSpec {
     int depth, V, d, hc;
     OrcDraftHook hook;
     void *hook_ctx;
+    int hook_after_chain;            /* 1: the MTP chain runs, then the hook edits its drafts */
+    int32_t *raw;                    /* the chain's own drafts (before the hook) */
+    float *margin;                   /* top-1 minus top-2 of each chain row */
     uint64_t emitted, batches, refeed, offered, accepted;
     size_t q;
     int32_t held;
@@ -820,6 +917,7 @@ OrcSpec *orc_spec_new(OrcModel *m, OrcState *st, OrcMtpState *mst, int depth) {
     sp->V = c->vocab_size; sp->d = c->hidden_size; sp->hc = c->hc_mult;
     size_t D = (size_t)sp->depth, V = (size_t)sp->V, d = (size_t)sp->d, hcd = (size_t)sp->hc * d;
     sp->drafts = xc(D * 4); sp->batch = xc(D * 4);
+    sp->raw = xc(D * 4); sp->margin = xc(D * 4);
     sp->logits16 = xc(D * V * 2); sp->H = xc(D * hcd * 2); sp->Yn = xc(D * d * 2);
     sp->ph = xc(D * d * 2); sp->h_prev = xc(d * 2); sp->oh = xc(D * d * 2);
     sp->hmtp_a = xc(d * 2); sp->hmtp_b = xc(d * 2); sp->mtp_row = xc(V * 2);
@@ -840,12 +938,58 @@ void orc_spec_free(OrcSpec *sp) {
     if (!sp) return;
     for (int l = 0; l < sp->m->c.num_hidden_layers; l++) { free(sp->snap_conv[l]); free(sp->snap_rec[l]); }
     free(sp->snap_conv); free(sp->snap_rec); free(sp->snap_n);
+    free(sp->raw); free(sp->margin);
     free(sp->drafts); free(sp->batch); free(sp->logits16); free(sp->H); free(sp->Yn); free(sp->ph);
     free(sp->h_prev); free(sp->oh); free(sp->hmtp_a); free(sp->hmtp_b); free(sp->mtp_row);
     free(sp);
 }
 
-void orc_spec_set_draft_hook(OrcSpec *sp, OrcDraftHook hook, void *ctx) { sp->hook = hook; sp->hook_ctx = ctx; }
+void orc_spec_set_draft_hook(OrcSpec *sp, OrcDraftHook hook, void *ctx) {
+    sp->hook = hook;
+    sp->hook_ctx = ctx;
+    sp->hook_after_chain = 0;
+}
+
+void orc_spec_set_force_hook(OrcSpec *sp, OrcDraftHook hook, void *ctx) {
+    sp->hook = hook;
+    sp->hook_ctx = ctx;
+    sp->hook_after_chain = 1;
+}
+
+void orc_spec_raw_drafts(const OrcSpec *sp, int32_t *drafts, float *margins) {
+    memcpy(drafts, sp->raw, (size_t)sp->depth * 4);
+    if (margins) memcpy(margins, sp->margin, (size_t)sp->depth * 4);
+}
+
+/* (top-1 - top-2) / |top-1| of a BF16 logits row: how far the pick is
+ * from a tie, relative to the row's scale */
+static float top2_margin(const uint16_t *row, size_t n) {
+    float a = -INFINITY, b = -INFINITY;
+    for (size_t i = 0; i < n; i++) {
+        float v = orc_bf16_f32(row[i]);
+        if (v > a) { b = a; a = v; } else if (v > b) b = v;
+    }
+    return (a - b) / fmaxf(fabsf(a), 1e-30f);
+}
+
+/* c/gmtp.h:807-831, greedy: the accept walk over the verify rows' BF16
+ * logits (row j-1 verifies draft j); out[0] = held, then each accepted
+ * draft; the token that ends the walk (replacement or bonus) becomes the
+ * next held token.  Returns the emitted count. */
+int orc_spec_walk(const uint16_t *logits16, int De, size_t V, const int32_t *drafts, int32_t held, int32_t *out,
+                  int *matched_out, int32_t *next_held) {
+    int ne = 0, matched = 0, last = -1;
+    out[ne++] = held;
+    for (int j = 1; j < De; j++) {
+        int x = orc_argmax_bf16(logits16 + (size_t)(j - 1) * V, V);
+        if (drafts[j] == x) { matched++; out[ne++] = x; }
+        else { last = x; break; }
+    }
+    if (last < 0) last = orc_argmax_bf16(logits16 + (size_t)(De - 1) * V, V);
+    *matched_out = matched;
+    *next_held = last;
+    return ne;
+}
 
 static size_t kda_bytes(const OrcConfig *c, int rec) {
     size_t qkv = (size_t)c->linear_num_heads * (size_t)c->linear_head_dim;
@@ -883,6 +1027,7 @@ static void snap_restore(OrcSpec *sp) {
 static void chain(OrcSpec *sp) {
     size_t V = (size_t)sp->V, d = (size_t)sp->d;
     sp->drafts[0] = orc_argmax_bf16(sp->mtp_row, V);
+    sp->margin[0] = top2_margin(sp->mtp_row, V);
     uint16_t *cur = sp->hmtp_a, *nxt = sp->hmtp_b;
     for (int i = 1; i < sp->depth; i++) {
         if (orc_mtp_forward(sp->m, sp->mst, &sp->drafts[i - 1], cur, 1, sp->logits16, nxt)) {
@@ -891,9 +1036,12 @@ static void chain(OrcSpec *sp) {
         }
         memcpy(sp->mtp_row, sp->logits16, V * 2);
         sp->drafts[i] = orc_argmax_bf16(sp->mtp_row, V);
+        sp->margin[i] = top2_margin(sp->mtp_row, V);
         uint16_t *tmp = cur; cur = nxt; nxt = tmp;
     }
     if (cur != sp->hmtp_a) memcpy(sp->hmtp_a, cur, d * 2);
+    memcpy(sp->raw, sp->drafts, (size_t)sp->depth * 4);
+    if (sp->hook && sp->hook_after_chain) sp->hook(sp->hook_ctx, (int64_t)sp->q, sp->drafts, sp->depth);
 }
 
 /* Prefill in the engine's decode ordering: 8-token decode batches, then the
@@ -908,7 +1056,7 @@ int orc_spec_prefill(OrcSpec *sp, const int32_t *ids, size_t n) {
     }
     sp->held = orc_argmax_bf16(sp->mtp_row, V);
     sp->q = n;
-    if (sp->hook) {
+    if (sp->hook && !sp->hook_after_chain) {
         sp->hook(sp->hook_ctx, (int64_t)sp->q, sp->drafts, sp->depth);
     } else if (n >= 2) {
         uint16_t *l16 = xc(n * V * 2), *oh = xc(n * d * 2);
@@ -943,15 +1091,11 @@ int orc_spec_step(OrcSpec *sp, int *out, int cap) {
     for (int j = 1; j < De; j++) sp->batch[j] = sp->drafts[j];
     if (orc_decode_batch(sp->m, sp->st, sp->batch, (size_t)De, sp->logits16, sp->H, sp->Yn)) return 0;
     sp->batches++;
-    int ne = 0, matched = 0, last = -1;
-    out[ne++] = sp->held;
-    for (int j = 1; j < De; j++) {
-        int x = orc_argmax_bf16(sp->logits16 + (size_t)(j - 1) * V, V);
-        sp->offered++;
-        if (sp->drafts[j] == x) { matched++; sp->accepted++; out[ne++] = x; }
-        else { last = x; break; }
-    }
-    if (last < 0) last = orc_argmax_bf16(sp->logits16 + (size_t)(De - 1) * V, V);
+    int matched = 0;
+    int32_t last = -1;
+    int ne = orc_spec_walk(sp->logits16, De, V, sp->drafts, sp->held, out, &matched, &last);
+    sp->offered += (uint64_t)(matched < De - 1 ? matched + 1 : matched);
+    sp->accepted += (uint64_t)matched;
     sp->emitted += (uint64_t)ne;
     if (matched < De - 1) {
         snap_restore(sp);
@@ -960,7 +1104,7 @@ int orc_spec_step(OrcSpec *sp, int *out, int cap) {
     }
     sp->held = last;
     sp->q += (size_t)(matched + 1);
-    if (!sp->hook) {
+    if (!sp->hook || sp->hook_after_chain) {
         memcpy(sp->ph, sp->h_prev, d * 2);
         for (int j = 1; j <= matched; j++) memcpy(sp->ph + (size_t)j * d, sp->Yn + (size_t)(j - 1) * d, d * 2);
         sp->mst->pos = sp->mtp_snap_pos;

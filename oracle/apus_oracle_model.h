@@ -77,18 +77,44 @@ void orc_kda_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,
                     uint16_t *conv_state, float *rec_state, uint16_t *out);
 void orc_dsa_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,
                     OrcState *st, uint16_t *out);
+/* The same with the indexer's selection of every token (topk [s][width],
+ * token ids, -1 padded; width = orc_dsa_width) and its pool scores (scores
+ * [s][score_ld], -FLT_MAX for pools a token cannot see); both may be NULL. */
+size_t orc_dsa_width(const OrcModel *m);
+void orc_dsa_decode_sel(const OrcModel *m, int layer, const uint16_t *x, size_t s, OrcState *st,
+                        uint16_t *out, int32_t *topk, float *scores, size_t score_ld);
+
+/* State transplant (tests feed the oracle the engine's committed state so a
+ * sublayer is checked on identical inputs): KDA conv [3*qkv][K-1] BF16 and
+ * rec [H][D][D] f32; DSA k [H][n][qd], v [H][n][vd], ik / ig [n][ID] BF16. */
+void orc_state_set_pos(OrcState *st, size_t pos);
+int orc_state_load_kda(OrcState *st, int layer, const uint16_t *conv, const float *rec);
+int orc_state_load_dsa(OrcState *st, int layer, const uint16_t *k, const uint16_t *v, const uint16_t *ik,
+                       const uint16_t *ig, size_t n);
 
 /* MTP head (c/gmtp.h:471-541) and its DSA-cache state. */
 OrcMtpState *orc_mtp_state_new(const OrcModel *m, size_t cap);
 void orc_mtp_state_free(OrcMtpState *st);
 int orc_mtp_forward(OrcModel *m, OrcMtpState *mst, const int32_t *ids, const uint16_t *prev_h,
                     size_t s, uint16_t *logits, uint16_t *out_h);
+int orc_mtp_state_load(const OrcModel *m, OrcMtpState *mst, const uint16_t *k, const uint16_t *v,
+                       const uint16_t *ik, const uint16_t *ig, size_t n);
 
 /* Greedy speculative decode (c/gmtp.h:617-891), depth D = verify rows. */
 typedef void (*OrcDraftHook)(void *ctx, int64_t q, int32_t *drafts, int n);
 OrcSpec *orc_spec_new(OrcModel *m, OrcState *st, OrcMtpState *mst, int depth);
 void orc_spec_free(OrcSpec *sp);
 void orc_spec_set_draft_hook(OrcSpec *sp, OrcDraftHook hook, void *ctx);
+/* The B200 engine's forced agreement: the MTP chain still runs and the hook
+ * then edits its drafts (the reference's draft_override replaces the MTP). */
+void orc_spec_set_force_hook(OrcSpec *sp, OrcDraftHook hook, void *ctx);
+/* The last chain's own drafts (before any hook) and each chain row's
+ * (top-1 - top-2) / |top-1| logit margin. */
+void orc_spec_raw_drafts(const OrcSpec *sp, int32_t *drafts, float *margins);
+/* c/gmtp.h:807-831, greedy: the accept walk over De verify rows of BF16
+ * logits; out[0..ne) = held then the accepted drafts; returns ne. */
+int orc_spec_walk(const uint16_t *logits16, int De, size_t V, const int32_t *drafts, int32_t held, int32_t *out,
+                  int *matched, int32_t *next_held);
 int  orc_spec_prefill(OrcSpec *sp, const int32_t *ids, size_t n);
 int  orc_spec_step(OrcSpec *sp, int *out, int cap);
 /* stats: emitted, batches, refeed, offered, accepted, q, held */

@@ -176,6 +176,15 @@ _decl(ORC, "orc_hc_head", None, _vp, _vp, _sz, _sz)
 _decl(ORC, "orc_moe_forward", None, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp)
 _decl(ORC, "orc_kda_decode", None, _vp, _i, _vp, _sz, _vp, _vp, _vp)
 _decl(ORC, "orc_dsa_decode", None, _vp, _i, _vp, _sz, _vp, _vp)
+_decl(ORC, "orc_dsa_width", _sz, _vp)
+_decl(ORC, "orc_dsa_decode_sel", None, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp, _sz)
+_decl(ORC, "orc_state_set_pos", None, _vp, _sz)
+_decl(ORC, "orc_state_load_kda", _i, _vp, _i, _vp, _vp)
+_decl(ORC, "orc_state_load_dsa", _i, _vp, _i, _vp, _vp, _vp, _vp, _sz)
+_decl(ORC, "orc_mtp_state_load", _i, _vp, _vp, _vp, _vp, _vp, _vp, _sz)
+_decl(ORC, "orc_spec_set_force_hook", None, _vp, _vp, _vp)
+_decl(ORC, "orc_spec_raw_drafts", None, _vp, _vp, _vp)
+_decl(ORC, "orc_spec_walk", _i, _vp, _i, _sz, _vp, C.c_int32, _vp, C.POINTER(C.c_int), C.POINTER(C.c_int32))
 
 DRAFT_HOOK = C.CFUNCTYPE(None, _vp, C.c_int64, C.POINTER(C.c_int32), C.c_int)
 
@@ -228,6 +237,19 @@ class Model:
         rc = fn(self.h, st, p(ids), s, p(logits), p(h), p(yn))
         assert rc == 0
         return (logits, h, yn) if want_h else logits
+
+
+def spec_walk(logits16, drafts, held):
+    """c/gmtp.h:807-831 (greedy) on De rows of BF16 logits: (emitted,
+    matched, next held)."""
+    lg = np.ascontiguousarray(logits16, np.uint16)
+    De, V = lg.shape
+    dr = np.zeros(max(De, 1), np.int32)
+    dr[:len(drafts)] = drafts[:De]
+    out = np.zeros(De + 1, np.int32)
+    matched, nh = C.c_int(0), C.c_int32(0)
+    ne = ORC.orc_spec_walk(p(lg), De, V, p(dr), int(held), p(out), C.byref(matched), C.byref(nh))
+    return out[:ne].tolist(), matched.value, nh.value
 
 
 # ---- sampling (c/sample.h:91-177) ----

@@ -1,0 +1,172 @@
+"""The speculative step's decisions and drafts against the oracle.
+
+  * Accept walk, bitwise: the engine keeps each step's verify-row logits
+    (apus_gcuda_gspec_keep_logits); the oracle's walk (orc_spec_walk, the
+    walk of c/gmtp.h:807-831 that orc_spec_step runs, itself pinned bitwise
+    to the reference engine's apus_gspec_step) replays it on those logits
+    and the drafts the step verified.  Emitted tokens, the matched count,
+    the next held token and the new position must be equal.
+  * Drafts: the engine's MTP chain (replay of the step's candidate pairs,
+    then depth-1 chained forwards) against the oracle's speculative loop
+    (replay of the accepted prefix after the walk, then the chain,
+    c/gmtp.h:851-884 and :677-696) on the same prompt, with the same forced
+    agreement (truth with probability p, else truth+1, keyed by splitmix64
+    of the seed and the position).  The MTP's own drafts, before the
+    forcing, must be equal wherever the oracle's pick is not a near tie
+    (relative top-2 margin above MARGIN); the emitted streams must be equal
+    up to the first position where the two engines' greedy picks may
+    differ (a near tie of the oracle's logits).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+import synth
+from modelgen import gen_weights, tiny_config
+
+pytestmark = pytest.mark.gpu
+
+PROMPT = [5, 17, 300, 2, 99, 42, 7, 381, 0, 11, 13]
+MARGIN = 0.02
+M64 = (1 << 64) - 1
+
+
+def sm64(z):
+    """splitmix64's output function on z (the forced-agreement hash of
+    apus_gcuda_gspec_force)."""
+    z = (z + 0x9E3779B97F4A7C15) & M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M64
+    return z ^ (z >> 31)
+
+
+def force_rule(truth, base, p, seed, V):
+    def hook(ctx, q, drafts, n):
+        for i in range(n):
+            pos = q + i - base
+            if 0 <= pos < len(truth):
+                u = (sm64((seed ^ (q + i)) & M64) >> 11) * 2.0 ** -53
+                drafts[i] = truth[pos] if u < p else (truth[pos] + 1) % V
+    return O.DRAFT_HOOK(hook)
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    kw = tiny_config()
+    return kw, gen_weights(kw, seed=20261201)
+
+
+def walk_steps(g, depth, V, n_steps):
+    """Run n_steps engine steps with logits kept; replay each on the oracle
+    walk and compare."""
+    g.keep_logits(True)
+    for _ in range(n_steps):
+        s0, rc = g.stats()
+        assert rc == 0
+        drafts = g.debug_read("drafts", (depth,), np.int32)
+        out = g.spec_step()
+        s1, _ = g.stats()
+        logits = g.debug_read("logits", (depth, V), np.uint16)
+        emitted, matched, nh = O.spec_walk(logits, drafts.tolist(), s0["held"])
+        assert out == emitted, (out, emitted)
+        assert len(out) == matched + 1
+        assert s1["held"] == nh
+        assert s1["pos"] == s0["pos"] + matched + 1
+        assert s1["accepted"] - s0["accepted"] == matched
+    g.keep_logits(False)
+
+
+@pytest.mark.parametrize("p", [0.0, 0.5, 1.0])
+def test_walk_bitwise_on_device_logits(gcuda, tiny, p):
+    kw, W = tiny
+    depth, V = 4, kw["vocab_size"]
+    ref = gcuda.GModel(gcuda.make_config(**kw), has_mtp=True, kv_cap=256, depth=depth)
+    ref.load(W)
+    truth = ref.greedy(PROMPT, 80)
+    ref.close()
+    g = gcuda.GModel(gcuda.make_config(**kw), has_mtp=True, kv_cap=256, depth=depth)
+    g.load(W)
+    g.force(truth, base=len(PROMPT), p=p, seed=9)
+    g.spec_prefill(PROMPT)
+    walk_steps(g, depth, V, 14)
+    g.close()
+
+
+def draft_parity(gcuda, kw, W, depth, p, n_steps, cap):
+    V = kw["vocab_size"]
+    # the oracle's own greedy stream is the truth the forcing uses on both sides
+    o = O.Model(O.make_config(**kw), W, True, "orc")
+    truth = np.zeros(n_steps * depth + 8, np.int32)
+    ids = np.array(PROMPT, np.int32)
+    st0 = o.state(cap)
+    assert O.ORC.orc_greedy(o.h, st0, O.p(ids), len(ids), len(truth), O.p(truth)) == 0
+    O.ORC.orc_state_free(st0)
+    truth = truth.tolist()
+    seed = 31
+    st, mst = o.state(cap), O.ORC.orc_mtp_state_new(o.h, cap)
+    sp = O.ORC.orc_spec_new(o.h, st, mst, depth)
+    hook = force_rule(truth, len(PROMPT), p, seed, V)
+    O.ORC.orc_spec_set_force_hook(sp, hook, None)
+    g = gcuda.GModel(gcuda.make_config(**kw), has_mtp=True, kv_cap=cap, depth=depth)
+    g.load(W)
+    g.force(truth, base=len(PROMPT), p=p, seed=seed)
+    assert O.ORC.orc_spec_prefill(sp, O.p(ids), len(ids)) == 0
+    g.spec_prefill(PROMPT)
+    raw_o = np.zeros(depth, np.int32)
+    marg = np.zeros(depth, np.float32)
+    buf = (C.c_int * (depth + 1))()
+    checked = agreed = 0
+    for step in range(n_steps + 1):
+        O.ORC.orc_spec_raw_drafts(sp, O.p(raw_o), O.p(marg))
+        raw_g = g.debug_read("raw_drafts", (depth,), np.int32)
+        for i in range(depth):
+            if marg[i] > MARGIN:
+                checked += 1
+                assert raw_g[i] == raw_o[i], f"step {step} draft {i}: engine {raw_g[i]}, oracle {raw_o[i]} " \
+                                             f"(margin {marg[i]:.3g})"
+            agreed += int(raw_g[i] == raw_o[i])
+        q = g.stats()[0]["pos"]
+        assert g.debug_read("drafts", (depth,), np.int32).tolist() == \
+            O_forced(truth, len(PROMPT), p, seed, V, q, raw_g)
+        if step == n_steps:
+            break
+        ne = O.ORC.orc_spec_step(sp, buf, depth + 1)
+        out_o = list(buf[:ne])
+        out_g = g.spec_step()
+        if out_g != out_o:
+            # the two engines' greedy streams split (a near tie of the main
+            # model's logits): the drafts after it are not comparable
+            assert out_g[:len(out_o)] != out_o[:len(out_g)], "emitted counts differ on equal tokens"
+            break
+    O.ORC.orc_spec_free(sp)
+    O.ORC.orc_mtp_state_free(mst)
+    O.ORC.orc_state_free(st)
+    g.close()
+    assert checked >= 2 * depth, f"only {checked} drafts compared away from near ties"
+    return checked, agreed
+
+
+def O_forced(truth, base, p, seed, V, q, drafts):
+    """The forced drafts the engine verifies next: its own raw drafts edited
+    by the forcing rule at position q."""
+    out = [int(x) for x in drafts]
+    for i in range(len(out)):
+        pos = q + i - base
+        if 0 <= pos < len(truth):
+            u = (sm64((seed ^ (q + i)) & M64) >> 11) * 2.0 ** -53
+            out[i] = truth[pos] if u < p else (truth[pos] + 1) % V
+    return out
+
+
+@pytest.mark.parametrize("p", [0.0, 0.5])
+def test_drafts_vs_oracle_tiny(gcuda, tiny, p):
+    kw, W = tiny
+    draft_parity(gcuda, kw, W, depth=4, p=p, n_steps=16, cap=256)
+
+
+def test_drafts_vs_oracle_config2_dims(gcuda):
+    kw = synth.c2_config(small=True)
+    W = synth.c2_weights(kw, seed=20261203)
+    draft_parity(gcuda, kw, W, depth=4, p=0.5, n_steps=3, cap=128)

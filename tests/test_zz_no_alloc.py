@@ -1,10 +1,12 @@
 """apus_gcuda_bf16_gemm_argmax_static_dev: the fused BF16 GEMV + greedy pick
 whose scratch is a fixed file-scope device array (no cudaMalloc/cudaFree on
 any call).  Checked against apus_gcuda_bf16_gemm_argmax_dev on the same
-inputs, two calls in a row, within the GEMV test tolerance (elementwise
-|err| <= 1e-2 * max(|ref|, rms(ref row)), cosine >= 0.9999) and with equal
-picks; plus the size limits.  This file is collected last on purpose and
-needs nothing from the other tests."""
+inputs, two calls in a row: the same kernels run on the same split, so the
+BF16 outputs and the picks must be bitwise equal (the GEMV test tolerance,
+elementwise |err| <= 1e-2 * max(|ref|, rms(ref row)) and cosine >= 0.9999,
+is checked too, as a diagnostic that names the row when they are not); plus
+the size limits.  This file is collected last on purpose and needs nothing
+from the other tests."""
 import ctypes as C
 
 import numpy as np
@@ -55,6 +57,7 @@ def test_static_scratch_matches_pooled(gcuda, M, O, K):
         torch.cuda.synchronize()
         assert torch.cuda.mem_get_info()[0] == free0
         _close_rows(y, y_ref)
+        assert torch.equal(y, y_ref), "static-scratch outputs differ bitwise from the pooled entry point"
         assert torch.equal(ids, id_ref)
     assert gcuda.apus_gcuda_kernel_error() == 0
 
