@@ -1395,7 +1395,8 @@ extern "C" int apus_gcuda_model_debug_read(ApusGcudaModel *m, const char *name, 
         {"kp", S.kp}, {"qkvc", S.qkvc}, {"fgo", S.fgo}, {"core", S.core}, {"qkva", S.qkva}, {"q", S.q},
         {"kvb", S.kvb}, {"iq", S.iq}, {"ikgw", S.ikgw}, {"attn", S.attn}, {"yn", S.yn}, {"mix", S.mix},
         {"qres", S.qres}, {"kpass", S.kpass}, {"isel", S.isel}, {"iscore", S.iscore},
-        {"moe_idx", m->moe_scr.row_expert}, {"moe_w", m->moe_scr.row_weight}, {"logits", S.logits},
+        {"moe_idx", m->moe_scr.row_expert}, {"moe_w", m->moe_scr.row_weight}, {"moe_sel", m->moe_scr.row_sel},
+        {"logits", S.logits}, {"hmtp", m->hmtp}, {"hcarry", m->hcarry}, {"oh", S.oh},
     };
     for (const auto &e : tab)
         if (!strcmp(e.n, name)) {

@@ -805,7 +805,9 @@ def gemv_table(only="all", rows=(8, 4, 1), reps=50):
     shapes = [("lm_head", V, d, "bf16"), ("kda_proj", 3 * qkv + 2 * D + H, d, "bf16"), ("kda_o", d, qkv, "bf16"),
               ("eh_proj", d, 2 * d, "bf16"), ("router", E, d, "f32"), ("dsa_qa_kva", ql + kl, d, "fp8"),
               ("dsa_qb", AH * qd, ql, "fp8"), ("dsa_kvb", AH * (qd + vd), kl, "bf16"),
-              ("idx_wqb", IH * ID, ql, "bf16"), ("idx_kgw", 2 * ID + IH, d, "bf16"), ("dsa_o", d, AH * vd, "fp8")]
+              ("idx_wqb", IH * ID, ql, "bf16"), ("idx_kgw", 2 * ID + IH, d, "bf16"), ("dsa_o", d, AH * vd, "fp8"),
+              ("config0", C0["N"], C0["K"], "fp8"), ("expert_gu", 2 * kw["moe_intermediate_size"], d, "fp8"),
+              ("expert_down", d, kw["moe_intermediate_size"], "fp8")]
     st = torch.cuda.Stream()
     sp = G.C.c_void_p(st.cuda_stream)
     hbm, _, _ = peaks()

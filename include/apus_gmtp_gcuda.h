@@ -189,7 +189,11 @@ int apus_gcuda_model_counters(ApusGcudaModel *m, uint64_t *out, size_t n);
 int apus_gcuda_model_debug_stop(ApusGcudaModel *m, int layer, int stage);
 int apus_gcuda_model_debug_read(ApusGcudaModel *m, const char *name, void *host, size_t bytes);
 /* More inspection names for debug_read: "moe_idx" / "moe_w" (the last MoE
- * call's routing, [8][16] int32 / f32, ascending experts), "logits" ([8][V]
+ * call's routing, [rows][top-k] int32 / f32, ascending experts), "moe_sel"
+ * (the same selections in top-k order), "hmtp" / "hcarry" ([d] BF16: the
+ * MTP hidden the next chain step starts from / the hnorm input carried to
+ * the next replay), "oh" (the last MTP forward's post-shared_head.norm
+ * rows), "logits" ([8][V]
  * BF16 rows of the last forward that wrote logits), "drafts" / "raw_drafts"
  * (int32, the verify drafts of the next step / the MTP chain's own drafts
  * before forced agreement), and the committed sequence state: "kda_conv.L"

@@ -251,6 +251,10 @@ static void topk_stable(const float *row, int n, int k, int32_t *idx) {
 }
 
 /* c/gmoe.h:191-208 */
+/* the last router call's gap between the topk-th and the next biased
+ * score (how close its selection came to a tie); test inspection only */
+static float g_route_gap;
+
 static void router(const OrcModel *m, const OLayer *Ly, const uint16_t *x, int32_t *idx, float *w) {
     const OrcConfig *c = &m->c;
     int E = c->n_routed_experts, topk = c->num_experts_per_tok;
@@ -264,6 +268,15 @@ static void router(const OrcModel *m, const OLayer *Ly, const uint16_t *x, int32
         b[e] = scores[e] + Ly->gate_bias[e];
     }
     topk_stable(b, E, topk, idx);
+    {
+        float kth = b[idx[topk - 1]], next = -INFINITY;
+        for (int e = 0; e < E; e++) {
+            int used = 0;
+            for (int j = 0; j < topk; j++) if (idx[j] == e) { used = 1; break; }
+            if (!used && b[e] > next) next = b[e];
+        }
+        g_route_gap = kth - next;
+    }
     for (int j = 0; j < topk; j++) w[j] = scores[idx[j]];
     float sum = orc_pw_sum(w, (size_t)topk);
     for (int j = 0; j < topk; j++) w[j] = w[j] / (sum + 1e-20f) * c->routed_scaling_factor;
@@ -289,8 +302,16 @@ static void expert(const OrcModel *m, Fp8 g, Fp8 u, Fp8 dn, const uint16_t *x, s
 }
 
 /* c/gmoe.h:265-337 forward2 (per token, ascending expert, shared last) */
+static void moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out,
+                        int32_t *idx_out, float *w_out, const int32_t *forced, float *gap_out);
+
 void orc_moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out,
                      int32_t *idx_out, float *w_out, const int32_t *forced) {
+    moe_forward(m, layer, x, s, out, idx_out, w_out, forced, NULL);
+}
+
+static void moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out,
+                        int32_t *idx_out, float *w_out, const int32_t *forced, float *gap_out) {
     const OrcConfig *c = &m->c;
     const OLayer *Ly = &m->L[layer];
     int E = c->n_routed_experts, topk = c->num_experts_per_tok;
@@ -302,6 +323,7 @@ void orc_moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, 
     for (size_t t = 0; t < s; t++) {
         const uint16_t *xt = x + t * d;
         router(m, Ly, xt, idx, wt);
+        if (gap_out) gap_out[t] = g_route_gap;
         if (forced) {   /* c/gmoe.h:287-297: weights re-gathered at the forced indices */
             float scores_f[64];
             for (int j = 0; j < topk; j++) {
@@ -790,9 +812,15 @@ int orc_state_load_dsa(OrcState *st, int layer, const uint16_t *k, const uint16_
     return dsa_load(&st->dsa[layer], c, k, v, ik, ig, n);
 }
 
-/* c/gmodel.h:1439-1626 apus_gm_run with decode = 1 */
 int orc_decode_batch(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
                      uint16_t *logits, uint16_t *h_out, uint16_t *yn_out) {
+    return orc_decode_batch_ex(m, st, ids, s, logits, h_out, yn_out, NULL, NULL, NULL);
+}
+
+/* c/gmodel.h:1439-1626 apus_gm_run with decode = 1 */
+int orc_decode_batch_ex(OrcModel *m, OrcState *st, const int32_t *ids, size_t s, uint16_t *logits,
+                        uint16_t *h_out, uint16_t *yn_out, const int32_t *forced, int32_t *sel_out,
+                        float *gap_out) {
     const OrcConfig *c = &m->c;
     if (st->pos + s > st->cap) return -1;
     size_t d = (size_t)c->hidden_size, hc = (size_t)c->hc_mult, V = (size_t)c->vocab_size;
@@ -817,7 +845,9 @@ int orc_decode_batch(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
                     expert(m, m->L[l].mlp_g, m->L[l].mlp_u, m->L[l].mlp_d, x + t * d, d, inter,
                            c->swiglu_limit, sub + t * d);
             } else {
-                orc_moe_forward(m, l, x, s, sub, NULL, NULL, NULL);
+                const size_t lk = (size_t)l * s * (size_t)c->num_experts_per_tok;
+                moe_forward(m, l, x, s, sub, sel_out ? sel_out + lk : NULL, NULL, forced ? forced + lk : NULL,
+                            gap_out ? gap_out + (size_t)l * s : NULL);
             }
             for (size_t t = 0; t < s; t++)
                 orc_hc_post(sub + t * d, h + t * hc * d, post + t * hc, comb + t * hc * hc, h2 + t * hc * d, d, hc);

@@ -61,6 +61,15 @@ size_t orc_state_pos(const OrcState *st);
  * (BF16 codes; h_out/yn_out may be NULL). */
 int orc_decode_batch(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
                      uint16_t *logits, uint16_t *h_out, uint16_t *yn_out);
+/* The same with the MoE routing exposed (test inspection): forced
+ * [L][s][topk] replaces each sparse layer's selection (top-k order, the
+ * teacher-forcing hook of c/gmoe.h:145-152); sel_out [L][s][topk] gets the
+ * selections, gap_out [L][s] the router's biased-score gap between the
+ * topk-th selection and the best unselected expert (any may be NULL; dense
+ * layers are left untouched). */
+int orc_decode_batch_ex(OrcModel *m, OrcState *st, const int32_t *ids, size_t s, uint16_t *logits,
+                        uint16_t *h_out, uint16_t *yn_out, const int32_t *forced, int32_t *sel_out,
+                        float *gap_out);
 
 /* Sublayer entry points for unit parity (state passed explicitly). */
 void orc_rmsnorm(const uint16_t *x, const uint16_t *w, uint16_t *y, size_t n, float eps);
