@@ -36,7 +36,7 @@ pytestmark = pytest.mark.gpu
 KW = synth.c2_config(small=True)
 CAP = 2400
 COS_MIN, REL_MAX = 0.9999, 1e-2
-E2E_COS, E2E_REL = 0.9995, 3e-2
+E2E_COS, E2E_REL = 0.999, 5e-2
 # The routing may only differ where the oracle's own top-k selection is a
 # near tie: biased-score gap between the k-th selection and the next expert
 # below ROUTE_TIE (the scores are sigmoids; an x error of 1e-2 relative moves
@@ -103,18 +103,27 @@ def c2(gcuda):
     g.close()
 
 
-def transplant(g, o, pos):
-    """An oracle state holding the engine's committed state at `pos`."""
+def engine_state(g, pos):
+    """The engine's committed state at `pos`, per layer (host copies)."""
+    return [g.dsa_state(l, pos) if KW["layer_is_dsa"][l] else g.kda_state(l)
+            for l in range(KW["num_hidden_layers"])]
+
+
+def oracle_state(o, saved, pos):
+    """A fresh oracle state holding a saved engine state."""
     st = o.state(CAP)
-    for l in range(KW["num_hidden_layers"]):
+    for l, a in enumerate(saved):
         if KW["layer_is_dsa"][l]:
-            k, v, ik, ig = g.dsa_state(l, pos)
-            assert O.ORC.orc_state_load_dsa(st, l, O.p(k), O.p(v), O.p(ik), O.p(ig), pos) == 0
+            assert O.ORC.orc_state_load_dsa(st, l, *(O.p(x) for x in a), pos) == 0
         else:
-            conv, rec = g.kda_state(l)
-            assert O.ORC.orc_state_load_kda(st, l, O.p(conv), O.p(rec)) == 0
+            assert O.ORC.orc_state_load_kda(st, l, *(O.p(x) for x in a)) == 0
     O.ORC.orc_state_set_pos(st, pos)
     return st
+
+
+def transplant(g, o, pos):
+    """An oracle state holding the engine's committed state at `pos`."""
+    return oracle_state(o, engine_state(g, pos), pos)
 
 
 def stage(g, l, s, ids, reads):
@@ -253,8 +262,9 @@ def test_c2_sublayers_vs_oracle(c2):
     # head norm + lm_head included), with the engine's routing and the
     # oracle's own
     sel = gpu_routing(g, ids)
+    saved = engine_state(g, pos)
     lg, _, yg = g.decode_batch(ids, want_h=True)
-    whole_forward(rep, o, lambda: transplant(g, o, pos), ids, sel, yg, lg)
+    whole_forward(rep, o, lambda: oracle_state(o, saved, pos), ids, sel, yg, lg)
     rep.finish()
 
 
