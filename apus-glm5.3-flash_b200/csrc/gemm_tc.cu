@@ -7,7 +7,7 @@
 // Persistent CTAs, one per SM, each taking 128 x 256 output tiles (128 rows of
 // x against 256 rows of W) in turn; 192 threads:
 //   * warp 0 lane 0 streams 64-wide k-blocks of both operands with 2-D tensor
-//     copies (128-byte swizzle, no multicast) into a 4-stage ring (48 KB a
+//     copies (128-byte swizzle, every CTA loading its own tiles) into a 4-stage ring (48 KB a
 //     stage);
 //   * warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 256,
 //     K 16; four per k-block) into one of two 256-column TMEM accumulators

@@ -142,6 +142,21 @@ def c2_config(small=False):
     return kw
 
 
+def c3_config(layers=45):
+    """the full-depth glm5_next at the reference's real
+    dims (reference/config.json): 45 layers, DSA at every 4th (i % 4 == 3,
+    11 of them) and KDA elsewhere (34, 64 heads x 128), dense MLPs in the
+    first 3 layers (intermediate 12288), then MoE of 288 experts top-8 plus
+    the shared expert at inter 2048; vocab 154880; one NextN layer.
+    `layers` < 45 keeps the same per-layer dims over fewer layers (tests)."""
+    L = layers
+    kw = dict(c2_config(), num_hidden_layers=L, first_k_dense_replace=3, moe_intermediate_size=2048,
+              linear_num_heads=64)
+    kw["layer_is_dsa"] = [int(i % 4 == 3) for i in range(L)]
+    kw["mlp_is_sparse"] = [int(i >= 3) for i in range(L)]
+    return kw
+
+
 def c2_weights(kw, seed, keep=None):
     """Seeded synthetic weights for every tensor of tensor_specs(kw), made
     with torch on the GPU and returned as host numpy arrays (both bench arms

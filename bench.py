@@ -496,8 +496,14 @@ def c2_algo_bytes(kw, depth, n_ctx, moe_problems, world=1):
 
     router = E * d * 2 + E * 4
     expert = fp8(2 * inter, d) + fp8(d, inter)
+    # dense-MLP layers (the first first_k_dense_replace): one "problem" of
+    # the device counter each per main forward, at the dense width, no router
+    dense_l = [l for l in range(L) if not kw["mlp_is_sparse"][l]]
+    dn = kw["intermediate_size"]
+    dense = len(dense_l) * (fp8(2 * dn, d) + fp8(d, dn))
     hcb = 2 * mix * hc * d * 2
-    main = sum(hcb + (dsa(depth, n_ctx) if kw["layer_is_dsa"][l] else kda) + router for l in range(L))
+    main = sum(hcb + (dsa(depth, n_ctx) if kw["layer_is_dsa"][l] else kda)
+               + (router if kw["mlp_is_sparse"][l] else 0) for l in range(L)) + dense
     head = -(-V // world) * d * 2
     main += head
     mtp_fwd = lambda rows, n: 2 * d * d * 2 + dsa(rows, n) + router + head
@@ -505,7 +511,7 @@ def c2_algo_bytes(kw, depth, n_ctx, moe_problems, world=1):
     if 2 * depth <= 8:      # the replay rows share the verify rows' pass over the head
         mtp -= head
     n_moe_calls = L + 1 + (depth - 1)
-    return main + mtp + moe_problems * expert, n_moe_calls
+    return main + mtp + (moe_problems - len(dense_l)) * expert, n_moe_calls
 
 
 def profile_value(fname, key):
@@ -694,6 +700,150 @@ def bench_c2(args, ws, rank, W=None):
     return out, W
 
 
+# --------------------------------------------------------------------------
+# config 3: the full-depth model, expert-parallel over the GPUs
+C3 = dict(prompt=4096, depth=4, seed=3, sweep=(0.0, 0.5, 0.9))
+
+
+def bench_c3(args, ws, rank):
+    """the 45-layer real-dims glm5_next (~306 GiB of FP8
+    experts) split expert-parallel over the ws GPUs (routed experts and
+    lm_head rows; everything else replicated), synthetic weights generated on
+    each device for its own slice (seed 3), a 4096-token random prompt, then
+    speculative steps at depth 3 (4 verify rows) with draft agreement forced
+    at p in {0, 0.5, 0.9}: each draft is the model's own greedy token with
+    probability p, else that token + 1 (splitmix64 of the seed and the
+    position).  The headline is p = 0: every step emits one token, as with
+    random weights' own drafts.  A step is timed on the device (CUDA events
+    on the model's stream), max over ranks."""
+    import numpy as np
+    import torch
+    import apus_gcuda as G
+    from synth import c3_config
+    G.enable()
+    kw = c3_config(args.layers or 45)
+    depth = C3["depth"]
+    n_prompt = args.prompt or C3["prompt"]
+    prompt = np.random.default_rng(C3["seed"]).integers(0, kw["vocab_size"], n_prompt).astype(np.int32)
+    n_truth = depth * (args.steps + args.warmup + 4) + 16
+    cap = n_prompt + n_truth + 64
+    m = G.GModel(G.make_config(**kw), has_mtp=True, kv_cap=cap, depth=depth, rank=rank, world=ws)
+    if ws > 1:
+        m.ep_bootstrap(G.ep_all_gather())
+    t0 = time.perf_counter()
+    m.init_random(C3["seed"])
+    t_init = time.perf_counter() - t0
+    m.use_graph(True)
+    barrier(ws)
+    t0 = time.perf_counter()
+    truth = m.greedy(prompt, n_truth)       # the model's own greedy stream: the forcing's truth
+    t_truth = time.perf_counter() - t0
+    st = torch.cuda.ExternalStream(m.stream())
+    hbm, _, src = peaks()
+    runs = {}
+    clk_sum = None
+    for p in C3["sweep"]:
+        m.force(truth, base=n_prompt, p=p, seed=C3["seed"])
+        barrier(ws)
+        t0 = time.perf_counter()
+        m.spec_prefill(prompt)
+        t_pf = time.perf_counter() - t0
+        for _ in range(args.warmup):
+            m.spec_step_async()
+        st.synchronize()
+        s0, _ = m.stats()
+        c0 = m.counters()
+        barrier(ws)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+            time.sleep(0.3)
+            e0.record(st)
+            for _ in range(args.steps):
+                m.spec_step_async()
+            e1.record(st)
+            st.synchronize()
+        ms = e0.elapsed_time(e1)
+        s1, rc = m.stats()
+        c1 = m.counters()
+        if rc != 0:
+            raise RuntimeError("sequence ran past its capacity")
+        barrier(ws)
+        ms = max_over_ranks(ms, ws)
+        emitted = s1["emitted"] - s0["emitted"]
+        per = ms / args.steps
+        n_ctx = (s0["pos"] + s1["pos"]) // 2
+        probs = (c1["moe_problems"] - c0["moe_problems"]) / args.steps
+        algo, _ = c2_algo_bytes(kw, depth, n_ctx, probs, ws)
+        algo = max_over_ranks(algo, ws)      # the busiest rank bounds the step
+        gbs = algo / (per * 1e-3) / 1e9
+        runs[p] = {"tok_s": round(emitted / (ms * 1e-3), 2), "ms_per_step": round(per, 4),
+                   "tokens_per_step": round(emitted / args.steps, 4),
+                   "acceptance": round((s1["accepted"] - s0["accepted"]) / max(1, s1["offered"] - s0["offered"]), 4),
+                   "step_roofline": {"achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                     "frac": round(gbs / hbm, 4), "algo_bytes_per_step_busiest_rank": int(algo),
+                                     "moe_expert_problems_per_step": round(probs, 2)},
+                   "prefill_ms": round(t_pf * 1e3, 1), "context_avg": n_ctx}
+        if p == C3["sweep"][0]:
+            clk_sum = clk.summary()
+            graph_kernels = int(c1["graph_kernels"])
+    head = runs[C3["sweep"][0]]
+    out = {"metric": METRIC, "value": head["tok_s"], "unit": "accepted tok/s", "n_gpus": ws, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None,
+           "dtype": "bf16 activations, fp8e4m3/bf16 weights, f32 accumulation",
+           "data": f"synthetic random-init weights generated on each GPU for its slice (seed {C3['seed']}), "
+                   f"{n_prompt} uniform random prompt ids",
+           "config": {"workload": f"config3: full-depth glm5_next ({kw['num_hidden_layers']} layers: "
+                                  f"{kw['num_hidden_layers'] - sum(kw['layer_is_dsa'])} KDA 64x128 + "
+                                  f"{sum(kw['layer_is_dsa'])} DSA, 3 dense MLP + MoE 288 top-8 inter 2048, "
+                                  "vocab 154880, real config.json dims) + 1 NextN MTP layer, greedy spec decode, "
+                                  "draft agreement forced at p = 0 (headline)",
+                      "depth": "BASELINE depth 3 = 4 verify rows (reference APUS_SPEC_K 4)",
+                      "prompt": n_prompt,
+                      "parallelism": f"ep{ws}: routed experts ({kw['n_routed_experts'] // ws} per GPU) and lm_head "
+                                     f"rows split over {ws} GPUs, dense/attention/MTP replicated, peer-memory "
+                                     "exchange per MoE layer and per lm_head",
+                      "l2": "inputs larger than L2: each step streams tens of GB of weights per GPU",
+                      "step": "one device-resident speculative step replayed from a CUDA graph"},
+           "spec": {"tokens_per_step": head["tokens_per_step"], "acceptance": head["acceptance"],
+                    "context_avg": head["context_avg"]},
+           "forced_agreement": {str(p): r for p, r in runs.items()},
+           "step_roofline": head["step_roofline"],
+           "setup_s": {"init_random": round(t_init, 1), "truth_greedy": round(t_truth, 1)},
+           "gpu_launches": graph_kernels * args.steps, "clocks": clk_sum}
+    # the dominant kernel: the lm_head slice GEMV (as config 2's line)
+    us_m, hb_m = lm_head_gemv_time(kw, 2 * depth, ws)
+    us_1, hb_1 = lm_head_gemv_time(kw, 1, ws)
+    n_one = depth - 1
+    us, hb = us_m + n_one * us_1, hb_m + n_one * hb_1
+    traffic = profile_value("lm_head_gemv_k_gemv_tma.md", "dram_bytes_per_launch")
+    hgbs = hb / us / 1e3
+    out["roofline"] = {"bound": "hbm", "kernel": f"k_gemv_tma<false> lm_head (BF16 {-(-kw['vocab_size'] // ws)}"
+                                                  f"x{kw['hidden_size']} per rank, fused argmax)",
+                       "achieved": round(hgbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(hgbs / hbm, 4),
+                       "traffic": round(traffic / ws) if traffic is not None else None,
+                       "algo_bytes_per_launch": round(hb / (1 + n_one)), "avg_launch_us": round(us / (1 + n_one), 2),
+                       "peak_source": src, "launches_per_step": 1 + n_one}
+    if not args.quick:
+        # e2e: the synchronous apus_gcuda_gspec_step (host tokens out each step)
+        m.force(truth, base=n_prompt, p=C3["sweep"][0], seed=C3["seed"])
+        m.spec_prefill(prompt)
+        for _ in range(min(args.warmup, 3)):
+            m.spec_step()
+        barrier(ws)
+        t0 = time.perf_counter()
+        n_e2e = 0
+        for _ in range(args.steps):
+            n_e2e += len(m.spec_step())
+        e2e = max_over_ranks(time.perf_counter() - t0, ws)
+        out["e2e"] = {"value": round(n_e2e / e2e, 2), "unit": "accepted tok/s",
+                      "path": "apus_gcuda_gspec_step per step on every rank, emitted tokens copied to the host",
+                      "h2d_bytes_per_step": 0, "d2h_bytes_per_step": int(m.counters()["ctl_bytes"])}
+    m.close()
+    return out
+
+
 def cpu_c2(W, budget_s=20.0, prompt_len=C2["prompt"], log=None):
     """The reference's own speculative engine (oracle/_ref: apus_gspec_* over
     apus_gmodel, compiled from the reference sources) on the host cores with
@@ -858,7 +1008,9 @@ def main():
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 256 for config 2, else 200)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--config", type=int, default=None,
+                    help="BASELINE config (default: 2 on one GPU, 3 -- the full model, expert-parallel -- on several)")
+    ap.add_argument("--layers", type=int, default=0, help="config 3: layers (default 45; fewer for quick checks)")
     ap.add_argument("--prompt", type=int, default=0, help="config 2: prompt tokens (default 512; profiling only)")
     ap.add_argument("--small", action="store_true",
                     help="config 2 layer shapes with 16 experts and a 16384 vocab (profiling captures only)")
@@ -879,10 +1031,12 @@ def main():
     ap.add_argument("--quick", action="store_true",
                     help="device-timed kernels only (no e2e, no CPU baseline): the profiling command")
     args = ap.parse_args()
-    if args.steps is None:
-        args.steps = 256 if args.config == 2 else 200
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.config is None:
+        args.config = 2 if ws == 1 and args.gpus <= 1 else 3
+    if args.steps is None:
+        args.steps = {2: 256, 3: 32}.get(args.config, 200)
     if args.impl == "reference":
         if rank != 0:
             return
@@ -902,6 +1056,9 @@ def main():
                              "cpu_baseline": cb,
                              "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                                      "d2h_bytes_per_step": 0}})
+        elif args.config == 3:
+            line["unavailable"] = ("config 3 is the 306 GiB 45-layer model; the reference CPU engine holds its "
+                                   "experts dequantized in host RAM and cannot load it on this host")
         else:
             cb = cpu_c0(budget_s=max(3.0, 0.05 * args.steps))
             if cb is None:
@@ -922,7 +1079,11 @@ def main():
     if args.tc_table is not None:
         tc_table(tuple(args.tc_table) or (512, 2048))
         return
-    if args.config == 2:
+    if args.config == 3:
+        out = bench_c3(args, ws, rank)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    elif args.config == 2:
         out, W = bench_c2(args, ws, rank)
         if rank == 0 and not args.quick and ws == 1 and args.temp <= 0:   # the reference leg decodes greedily
             out["cpu_baseline"] = cpu_c2(W, budget_s=args.cpu_budget)
