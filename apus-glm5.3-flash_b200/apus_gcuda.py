@@ -170,6 +170,30 @@ apus_gcuda_model_counters = _fn("apus_gcuda_model_counters", _i, _vp, _vp, _sz)
 apus_gcuda_model_debug_stop = _fn("apus_gcuda_model_debug_stop", _i, _vp, _i, _i)
 apus_gcuda_model_debug_read = _fn("apus_gcuda_model_debug_read", _i, _vp, _cs, _vp, _sz)
 apus_gcuda_gspec_keep_logits = _fn("apus_gcuda_gspec_keep_logits", _i, _vp, _i)
+apus_gcuda_gspec_counters = _fn("apus_gcuda_gspec_counters", _i, _vp, _vp, _sz)
+
+# ---- the reference's spec-engine names (include/apus_gspec_gcuda.h) --------
+# Structs the C host declares (ApusGmtp, ApusGspec, ApusRng) are passed as
+# pointers to caller memory; a C host uses them directly (tests/c/).
+apus_rng_seed = _fn("apus_rng_seed", None, _vp, _u64)
+apus_sample_scratch_size = _fn("apus_sample_scratch_size", _sz, _sz)
+apus_gmodel_open = _fn("apus_gmodel_open", _vp, _cs, _cs, _vp, _sz)
+apus_gmodel_open2 = _fn("apus_gmodel_open2", _vp, _cs, _cs, _vp, _vp, _sz)
+apus_gmodel_close = _fn("apus_gmodel_close", None, _vp)
+apus_gmodel_config = _fn("apus_gmodel_config", _vp, _vp)
+apus_gmodel_has_mtp = _fn("apus_gmodel_has_mtp", _i, _vp)
+apus_gmodel_state_new = _fn("apus_gmodel_state_new", _vp, _vp, _sz)
+apus_gmodel_state_free = _fn("apus_gmodel_state_free", None, _vp)
+apus_gmodel_pos = _fn("apus_gmodel_pos", _sz, _vp)
+apus_gmodel_state_cap = _fn("apus_gmodel_state_cap", _sz, _vp)
+apus_gmodel_state_gcuda = _fn("apus_gmodel_state_gcuda", _vp, _vp)
+apus_gmtp_bind = _fn("apus_gmtp_bind", _i, _vp, _vp, _vp, _sz)
+apus_gmtp_state_new = _fn("apus_gmtp_state_new", _vp, _vp, _sz)
+apus_gmtp_state_free = _fn("apus_gmtp_state_free", None, _vp)
+apus_gspec_init = _fn("apus_gspec_init", None, _vp, _vp, _vp, _vp, _vp, _i, C.c_float, C.c_float, _vp, _vp)
+apus_gspec_free = _fn("apus_gspec_free", None, _vp)
+apus_gspec_prefill = _fn("apus_gspec_prefill", _i, _vp, _vp, _sz)
+apus_gspec_step = _fn("apus_gspec_step", _i, _vp, _vp, _i)
 
 
 EP_HANDLE_BYTES = 64   # sizeof(cudaIpcMemHandle_t)

@@ -88,6 +88,7 @@ __global__ void k_spec_walk(Ctl *c, int D, int32_t *log, int log_cap) {
     if (c->err) { c->n_emitted = 0; return; }
     c->stat_d1_offered++;
     if (c->drafts[0] == c->held) c->stat_d1_hits++;
+    c->stat_batch_tokens += D;
     int matched = 0, last = -1;
     c->emitted[0] = c->held;
     for (int j = 1; j < D; j++) {
@@ -1219,6 +1220,48 @@ extern "C" int apus_gcuda_gspec_stats(ApusGcudaModel *m, uint64_t *o) {
     o[3] = (uint64_t)c.stat_accepted; o[4] = (uint64_t)c.pos; o[5] = (uint64_t)(int64_t)c.held;
     return c.err ? -1 : 0;
 }
+
+// Counters for the reference's ApusGspec fields (apus_gspec_gcuda.h).
+extern "C" int apus_gcuda_gspec_counters(ApusGcudaModel *m, uint64_t *o, size_t n) {
+    Ctl c = read_ctl(m);
+    const uint64_t v[10] = {(uint64_t)c.stat_emitted, (uint64_t)c.stat_batches, (uint64_t)c.stat_offered,
+                            (uint64_t)c.stat_accepted, (uint64_t)c.pos, (uint64_t)(int64_t)c.held,
+                            (uint64_t)c.stat_d1_hits, (uint64_t)c.stat_d1_offered, (uint64_t)c.stat_refeed,
+                            (uint64_t)c.stat_batch_tokens};
+    for (size_t i = 0; i < n && i < 10; i++) o[i] = v[i];
+    return gcuda_check(cudaGetLastError(), "gspec counters");
+}
+
+// The next step's drafts d1..dD (host copy), read or replaced: the
+// reference's draft_override hook edits them between steps.
+int model_drafts_rw(ApusGcudaModel *m, int32_t *drafts, int n, int write) {
+    if (n < 0 || n > MAXR) { gcuda_set_error("drafts: %d entries (0..%d)", n, MAXR); return -1; }
+    m->ctl_epoch++;
+    Ctl c = read_ctl(m);
+    if (!write) {
+        memcpy(drafts, c.drafts, (size_t)n * 4);
+        return 0;
+    }
+    for (int i = 0; i < n; i++)
+        if (drafts[i] < 0 || drafts[i] >= m->D.V) {
+            gcuda_set_error("drafts: token id %d outside [0, %d)", drafts[i], m->D.V);
+            return -1;
+        }
+    return gcuda_check(cudaMemcpy(m->ctl->drafts, drafts, (size_t)n * 4, cudaMemcpyHostToDevice), "drafts write");
+}
+
+// Verify rows per step (1..8): the reference's depth, chosen at
+// apus_gspec_init; the captured step graph is dropped.
+int model_set_depth(ApusGcudaModel *m, int depth) {
+    if (depth < 1 || depth > MAXR) { gcuda_set_error("depth %d (1..%d)", depth, MAXR); return -1; }
+    if (depth == m->depth) return 0;
+    m->depth = depth;
+    if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = nullptr; }
+    if (m->graph) { cudaGraphDestroy(m->graph); m->graph = nullptr; }
+    return 0;
+}
+
+size_t model_cap(const ApusGcudaModel *m) { return (size_t)m->cap; }
 
 extern "C" int apus_gcuda_gspec_force(ApusGcudaModel *m, const int32_t *truth, size_t n, size_t base, double p,
                                       uint64_t seed) {

@@ -59,7 +59,7 @@ struct Ctl {
     // 786-787, 845): d1 = the first draft against the held token; refeed =
     // the tokens its partial-reject path re-decodes (the checkpoint ring
     // here re-decodes nothing; the count keeps the reference's meaning)
-    long long stat_d1_hits, stat_d1_offered, stat_refeed;
+    long long stat_d1_hits, stat_d1_offered, stat_refeed, stat_batch_tokens;
 };
 
 struct KdaW {
