@@ -196,6 +196,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
     float *part = (float *)(ring + NSTAGE * STAGE_BYTES);   // [warp][tile][SPART]
     uint64_t *full = (uint64_t *)(part + 8 * 2 * SPART);
     uint64_t *empty = full + NSTAGE;
+    uint64_t *xbar = empty + NSTAGE;   // the activations' bulk copies
     // staged activations last: the launch sizes this part by its row count,
     // so launches of up to 4 rows keep two CTAs on an SM
     uint16_t *xs = (uint16_t *)((uint8_t *)full + 128);
@@ -213,6 +214,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
         // FP8 stages complete on two arrivals: the copy's expect-tx and the
         // producer's block-scale stores
         for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], FP8 ? 2 : 1); mbar_init(&empty[s], 8); }
+        mbar_init(xbar, 1);
         fence_barrier_init();
         abort_sh = 0;
     }
@@ -294,6 +296,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
     // of the tile and 16-byte unit +(mi>>1)
     const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8, lunit = lane >> 4;
     const uint16_t *xsrc_staged = nullptr;   // activations currently in smem
+    uint32_t xph = 0;                        // phase of the activations' barrier
     long c = 0;
     for (long i = it.first; i < it.end; i += it.step) {
         int p;
@@ -309,32 +312,31 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
             }
             const int per_row = (int)(klen / 8), total = d.R * per_row;   // <= 16 per thread
             if (!d.x_swiglu) {
-                for (int u0 = 0; u0 * 256 < total; u0 += 4) {    // batches of 4 loads in flight
-                    uint4 v[4];
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int q = threadIdx.x + (u0 + u) * 256;
-                        if (q < total) v[u] = ld_nc16(xsrc + (size_t)(q / per_row) * d.ldx + k0 + (q % per_row) * 8);
-                    }
-                    int mx = 0, mr = -1;
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int q = threadIdx.x + (u0 + u) * 256;
-                        if (q < total) {
-                            *(uint4 *)(xs + (q / per_row) * xstride + (q % per_row) * 8) = v[u];
-                            if (FP8) {
-                                const int r = q / per_row, ex = bf16x8_max_exp(v[u]);
-                                if (r != mr) {
-                                    if (mr >= 0) atomicMax(&xexp_sh[mr], mx);
-                                    mr = r;
-                                    mx = ex;
-                                } else {
-                                    mx = max(mx, ex);
-                                }
-                            }
+                // one bulk copy per activation row into its padded shared
+                // row: the whole slice lands in one memory round trip
+                if (threadIdx.x == 0) {
+                    mbar_arrive_expect_tx(xbar, (uint32_t)(d.R * klen * 2));
+                    for (int r = 0; r < d.R; r++)
+                        bulk_g2s(xs + r * xstride, xsrc + (size_t)r * d.ldx + k0, (uint32_t)(klen * 2), xbar);
+                }
+                mbar_wait(xbar, xph, &abort_sh, &g_apus_kernel_err, 3);
+                xph ^= 1u;
+                if (FP8) {
+                    // largest BF16 exponent of each staged row: a warp whose
+                    // 32 units lie in one row reduces them in one step
+                    for (int q0 = 0; q0 < total; q0 += 256) {
+                        const int q = q0 + (int)threadIdx.x;
+                        const bool in = q < total;
+                        const int r = in ? q / per_row : -1;
+                        const int ex = in ? bf16x8_max_exp(*(const uint4 *)(xs + r * xstride + (q % per_row) * 8)) : 0;
+                        const int r0 = __shfl_sync(0xffffffffu, r, 0);
+                        if (__all_sync(0xffffffffu, r == r0)) {
+                            const int mx = __reduce_max_sync(0xffffffffu, ex);
+                            if (lane == 0 && r0 >= 0) atomicMax(&xexp_sh[r0], mx);
+                        } else if (in) {
+                            atomicMax(&xexp_sh[r], ex);
                         }
                     }
-                    if (FP8 && mr >= 0) atomicMax(&xexp_sh[mr], mx);
                 }
             } else {
                 // x row = [g | u] of 2*K values: h = swiglu(g, u), c/gmoe.h:216-224
@@ -648,7 +650,7 @@ bool gemv_fast_ok(const GemvDesc &d) {
 // elements: ring, warp partials, barriers (in a 128-byte slot), activations.
 static size_t gemv_smem(int rows, long klen) {
     using namespace gemvcfg;
-    static_assert(2 * NSTAGE * 8 <= 128, "barrier slot");
+    static_assert((2 * NSTAGE + 1) * 8 <= 128, "barrier slot");
     return 1024 + NSTAGE * STAGE_BYTES + 8 * 2 * SPART * 4 + 128 + (size_t)rows * (size_t)(2 * klen + 32);
 }
 
