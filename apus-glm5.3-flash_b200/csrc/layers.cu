@@ -805,23 +805,92 @@ __global__ void __launch_bounds__(256) k_dsa_score(const uint16_t *iq, const uin
     }
 }
 
+// Order key of a pool score: larger score, larger key; -0 counts as +0
+// (the reference's comparisons treat them as equal).
+APUS_DEV uint32_t score_key(float v) { return f32_order_key(__float_as_uint(v) == 0x80000000u ? 0.0f : v); }
+
 // top-(topk/kpool) pools per row, stable with lower-index ties
-// (c/gdsa.h:404-429): a pool is kept iff fewer than K pools beat it.
-__global__ void k_dsa_select(const float *score, const int *base_n, int kp, int ksel, int maxpools, uint8_t *sel) {
+// (c/gdsa.h:404-429).  One CTA per row finds the key K-th from the top with
+// a 4-pass radix select (8 bits a pass, block histogram in shared memory),
+// then keeps every pool above it and, of the pools equal to it, the lowest
+// indices until K are kept -- the set the reference's stable top-k picks, in
+// O(pools) work per row instead of O(pools^2).
+__global__ void __launch_bounds__(256) k_dsa_select(const float *score, const int *base_n, int kp, int ksel,
+                                                    int maxpools, uint8_t *sel) {
     pdl_launch_dependents();
-    const int t = blockIdx.x;
+    __shared__ int hist[256];
+    __shared__ uint32_t pre_sh;
+    __shared__ int k_sh, wsum[8];
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nvalid = min((*base_n + t + 1) / kp, maxpools);
     const float *s = score + (size_t)t * maxpools;
     uint8_t *o = sel + (size_t)t * maxpools;
     if (nvalid <= ksel) {
-        for (int p = threadIdx.x; p < nvalid; p += blockDim.x) o[p] = 1;
+        for (int p = tid; p < nvalid; p += blockDim.x) o[p] = 1;
         return;
     }
-    for (int p = threadIdx.x; p < nvalid; p += blockDim.x) {
-        const unsigned long long kpk = argmax_key(s[p], (uint32_t)p);
-        int beat = 0;
-        for (int q = 0; q < nvalid && beat < ksel; q++) beat += argmax_key(s[q], (uint32_t)q) > kpk;
-        o[p] = beat < ksel;
+    uint32_t prefix = 0, mask = 0;
+    int k = ksel;                                  // rank (from the top) still to place
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        hist[tid] = 0;
+        __syncthreads();
+        for (int p = tid; p < nvalid; p += blockDim.x) {
+            const uint32_t u = score_key(s[p]);
+            if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // lane l sums digits 255-8l .. 248-8l (descending); a scan over the
+            // lanes finds the digit where the count from the top reaches k
+            int c[8], tot = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) { c[j] = hist[255 - 8 * lane - j]; tot += c[j]; }
+            int incl = tot;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += v;
+            }
+            const int excl = incl - tot;
+            const unsigned own = __ballot_sync(0xffffffffu, excl < k && k <= incl);
+            if (lane == __ffs(own) - 1) {
+                int cum = excl;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    if (cum + c[j] >= k) {
+                        pre_sh = prefix | ((uint32_t)(255 - 8 * lane - j) << shift);
+                        k_sh = k - cum;
+                        break;
+                    }
+                    cum += c[j];
+                }
+            }
+        }
+        __syncthreads();
+        prefix = pre_sh;
+        k = k_sh;
+        mask |= 255u << shift;
+    }
+    // prefix: the K-th key; k: how many pools equal to it to keep (lowest
+    // indices first).  Thread tid owns pools [tid*chunk, (tid+1)*chunk).
+    const int chunk = (nvalid + blockDim.x - 1) / blockDim.x;
+    const int p0 = min(tid * chunk, nvalid), p1 = min(p0 + chunk, nvalid);
+    int eq = 0;
+    for (int p = p0; p < p1; p++) eq += score_key(s[p]) == prefix;
+    int incl = eq;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    int before = incl - eq;
+    for (int w = 0; w < warp; w++) before += wsum[w];
+    for (int p = p0; p < p1; p++) {
+        const uint32_t u = score_key(s[p]);
+        const bool keep = u > prefix || (u == prefix && before++ < k);
+        o[p] = keep ? 1 : 0;
     }
 }
 
