@@ -37,6 +37,11 @@ struct GemvDesc {
     long kx;
     int tpi;
     int box_ko;             // 128-byte k-slabs per tensor copy
+    // FP8 inner loop (set by the launcher): 1 = codes widened to f16 against
+    // activations rescaled by a power of two into f16 range (one cvt per two
+    // weights, a scan and a conversion pass when staging); 0 = codes widened
+    // to bf16 against the activations as they are (exact e4m3 -> f16 -> bf16)
+    int x16;
     // argmax keys carry row + row_base (a vocabulary slice's global ids)
     long row_base;
     // plan the k-ranges as for a matrix of plan_o rows (0: O), so a slice of a

@@ -209,6 +209,8 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile_bytes = TR * d.box_ko * 128;
+    // FP8 weights meet the activations in one of two MMA forms (GemvDesc::x16)
+    const bool XF16 = FP8 && d.x16;
 
     if (threadIdx.x == 0) {
         // FP8 stages complete on two arrivals: the copy's expect-tx and the
@@ -306,7 +308,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
         uint16_t *yout = d.y ? d.y + (size_t)p * d.y_pstride : nullptr;
         if (xsrc != xsrc_staged) {           // stage x[:, k0:k0+klen]: row r at xs + r*xstride
             named_bar_sync(1, 256);          // previous item's readers are done
-            if (FP8) {
+            if (XF16) {
                 if (threadIdx.x < 8) xexp_sh[threadIdx.x] = 0;
                 named_bar_sync(1, 256);
             }
@@ -321,7 +323,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
                 }
                 mbar_wait(xbar, xph, &abort_sh, &g_apus_kernel_err, 3);
                 xph ^= 1u;
-                if (FP8) {
+                if (XF16) {
                     // largest BF16 exponent of each staged row: a warp whose
                     // 32 units lie in one row reduces them in one step
                     for (int q0 = 0; q0 < total; q0 += 256) {
@@ -364,11 +366,11 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
                     }
                     const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
                     *(uint4 *)(xs + r * xstride + cc) = ov;
-                    if (FP8) atomicMax(&xexp_sh[r], bf16x8_max_exp(ov));
+                    if (XF16) atomicMax(&xexp_sh[r], bf16x8_max_exp(ov));
                 }
             }
             named_bar_sync(1, 256);
-            if (FP8) {
+            if (XF16) {
                 // FP8 weights meet the activations in an f16 MMA: each staged
                 // row is scaled by an exact power of two 2^k that puts its
                 // largest magnitude in [2^14, 2^15), converted to f16 in place,
@@ -430,9 +432,14 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
                         const uint32_t ra = r[j >> 1][(j & 1) * 2], rb = r[j >> 1][(j & 1) * 2 + 1];
                         uint32_t b0, b1;
                         lds64(b0, b1, xs + xrow * xstride + ls * 64 + j * 16 + 4 * t4);
-                        mma_f16_16816(u[j & 1][0], u[j & 1][1], u[j & 1][2], u[j & 1][3],
-                                      cvt_e4m3x2_f16x2(ra & 0xffffu), cvt_e4m3x2_f16x2(rb & 0xffffu),
-                                      cvt_e4m3x2_f16x2(ra >> 16), cvt_e4m3x2_f16x2(rb >> 16), b0, b1);
+                        if (XF16)
+                            mma_f16_16816(u[j & 1][0], u[j & 1][1], u[j & 1][2], u[j & 1][3],
+                                          cvt_e4m3x2_f16x2(ra & 0xffffu), cvt_e4m3x2_f16x2(rb & 0xffffu),
+                                          cvt_e4m3x2_f16x2(ra >> 16), cvt_e4m3x2_f16x2(rb >> 16), b0, b1);
+                        else
+                            mma_bf16_16816(u[j & 1][0], u[j & 1][1], u[j & 1][2], u[j & 1][3],
+                                           e4m3x2_bf16x2(ra & 0xffffu), e4m3x2_bf16x2(rb & 0xffffu),
+                                           e4m3x2_bf16x2(ra >> 16), e4m3x2_bf16x2(rb >> 16), b0, b1);
                     }
                     const float sc = scl_sh[s][jt * 16 + (stt >> 1)];
                     if (jt == 0) {
@@ -465,8 +472,9 @@ k_gemv_tma(const __grid_constant__ CUtensorMap wmap, GemvDesc d) {
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const int xc = 2 * t4 + (e & 1), wr = g + 8 * (e >> 1);
-            pw[xc * PSTR + wr] = FP8 ? acc[0][e] * xinv_sh[xc] : (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
-            if (FP8 && tpi == 2) pw[SPART + xc * PSTR + wr] = acc[1][e] * xinv_sh[xc];
+            pw[xc * PSTR + wr] = FP8 ? (XF16 ? acc[0][e] * xinv_sh[xc] : acc[0][e])
+                                     : (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+            if (FP8 && tpi == 2) pw[SPART + xc * PSTR + wr] = XF16 ? acc[1][e] * xinv_sh[xc] : acc[1][e];
         }
         named_bar_sync(1, 256);
         const int tid = threadIdx.x;
@@ -746,6 +754,11 @@ static int launch_tma(const GemvDesc &d, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(gemvcfg::THREADS);
+    // grouped launches stream many tiles per CTA: the cheaper f16 inner loop
+    // wins; single launches are short, where the f16 form's activation
+    // rescaling (a scan and a conversion pass) dominates
+    GemvDesc dl = d;
+    dl.x16 = FP8 && d.gexpert ? 1 : 0;
     cfg.dynamicSmemBytes = sm;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
@@ -753,7 +766,7 @@ static int launch_tma(const GemvDesc &d, cudaStream_t st) {
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = d.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_gemv_tma<FP8>, wmap, d) == cudaSuccess ? 0 : -1;
+    return cudaLaunchKernelEx(&cfg, k_gemv_tma<FP8>, wmap, dl) == cudaSuccess ? 0 : -1;
 }
 
 int gemv_launch(const GemvDesc &dd, cudaStream_t st) {

@@ -47,11 +47,21 @@ APUS_DEV uint32_t cvt_e4m3x2_f16x2(uint32_t two_codes) {
     return r;
 }
 
+// Two E4M3 codes -> bf16x2, exact: every E4M3 value (subnormals included)
+// is an f16 and a bf16, so the f16 detour rounds nothing.
+APUS_DEV uint32_t e4m3x2_bf16x2(uint32_t two_codes);
+
 // (lo, hi) fp32 -> bf16x2 with RNE; lo goes to the low half.
 APUS_DEV uint32_t pack_bf16x2(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
+}
+
+APUS_DEV uint32_t e4m3x2_bf16x2(uint32_t two_codes) {
+    const uint32_t h = cvt_e4m3x2_f16x2(two_codes);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h));
+    return pack_bf16x2(f.x, f.y);
 }
 
 // Four E4M3 codes of one 32-bit word times the block scale, each rounded to

@@ -1065,7 +1065,6 @@ extern "C" int apus_gcuda_gspec_prefill(ApusGcudaModel *m, const int32_t *ids, s
         k_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
         // the first held token: exactly the non-speculative first draw (c/gmtp.h:724-727)
         if (last && draw_held(m, k - 1)) return fail_ctl(m, "gspec_prefill draw");
-        cudaStreamSynchronize(m->st);
     }
     // a one-token prompt has no true pair: drafts stay 0 (c/gmtp.h:741-757)
     if (n < 2) return gcuda_check(cudaStreamSynchronize(m->st), "gspec_prefill");
@@ -1084,7 +1083,6 @@ extern "C" int apus_gcuda_gspec_prefill(ApusGcudaModel *m, const int32_t *ids, s
             for (int i = 1; i < MAXR; i++) tmp.chain_pos[i] = tmp.mtp_n + i - 1;
             cudaMemcpy(m->ctl, &tmp, sizeof tmp, cudaMemcpyHostToDevice);
         }
-        cudaStreamSynchronize(m->st);
     }
     // the hnorm input carried to the next step: yn of position n-1
     k_copy_row<<<(d + 255) / 256, 256, 0, m->st>>>(m->yn_prompt, (long)n - 1, d, m->hcarry);
