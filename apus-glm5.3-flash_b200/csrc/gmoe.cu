@@ -335,6 +335,32 @@ int moe_forward_launch(const MoeDev &m, const uint16_t *x, long ldx, int R, uint
     // 2. routing + work list
     k_moe_route<<<1, 256, 0, st>>>(m, R, m.logits, forced);
     if (cudaGetLastError() != cudaSuccess) return -1;
+    if (m.E == 0) {
+        // a dense MLP (the shared expert of a 0-expert layer): two single
+        // GEMVs, the down one split over K when the width passes one range
+        // (intermediate 12288 in the reference's first three layers)
+        GemvDesc gs{};
+        gs.W = m.gu_codes; gs.WS = m.gu_scales; gs.nkb = (m.dim + 127) / 128;
+        gs.x = x; gs.ldx = ldx; gs.R = R; gs.O = 2L * m.inter; gs.K = m.dim; gs.fp8 = 1;
+        gs.y = m.gu; gs.ldy = 2L * m.inter;
+        gs.part = m.part; gs.ticket = m.tick;
+        gs.pdl = m.pdl;
+        if (gemv_launch(gs, st)) return -1;
+        GemvDesc ds{};
+        ds.W = m.d_codes; ds.WS = m.d_scales; ds.nkb = (m.inter + 127) / 128;
+        ds.x = m.gu; ds.ldx = 2L * m.inter; ds.R = R; ds.O = m.dim; ds.K = m.inter; ds.fp8 = 1;
+        ds.y = m.yd; ds.ldy = m.dim;
+        ds.x_swiglu = 1;
+        ds.swiglu_limit = m.limit;
+        ds.part = m.part; ds.ticket = m.tick;
+        ds.pdl = m.pdl;
+        if (gemv_launch(ds, st)) return -1;
+        if (!out) return cudaGetLastError() != cudaSuccess ? -1 : 0;
+        if (m.dim % 8 || ((uintptr_t)out & 15) || (ldo % 8)) return -1;
+        const long n = (long)R * (m.dim / 8);
+        k_moe_combine<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(m, R, out, ldo);
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    }
     // 3. gate|up of every active expert
     GemvDesc gu{};
     gu.W = m.gu_codes; gu.WS = m.gu_scales; gu.nkb = (m.dim + 127) / 128;

@@ -310,6 +310,15 @@ void orc_moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, 
     moe_forward(m, layer, x, s, out, idx_out, w_out, forced, NULL);
 }
 
+/* c/gmodel.h dense MLP layers (the first first_k_dense_replace): the SwiGLU
+ * expert of c/gmoe.h:210-227 on the layer's mlp.{gate,up,down}_proj */
+void orc_mlp_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out) {
+    const OLayer *Ly = &m->L[layer];
+    size_t d = (size_t)m->c.hidden_size, inter = (size_t)m->c.intermediate_size;
+    for (size_t t = 0; t < s; t++)
+        expert(m, Ly->mlp_g, Ly->mlp_u, Ly->mlp_d, x + t * d, d, inter, m->c.swiglu_limit, out + t * d);
+}
+
 static void moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out,
                         int32_t *idx_out, float *w_out, const int32_t *forced, float *gap_out) {
     const OrcConfig *c = &m->c;

@@ -82,6 +82,7 @@ void orc_hc_post(const uint16_t *x, const uint16_t *res4, const float *post, con
 void orc_hc_head(const uint16_t *x4, uint16_t *y, size_t d, size_t n);
 void orc_moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out,
                      int32_t *idx_out, float *w_out, const int32_t *forced);
+void orc_mlp_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out);
 void orc_kda_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,
                     uint16_t *conv_state, float *rec_state, uint16_t *out);
 void orc_dsa_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,

@@ -177,6 +177,7 @@ _decl(ORC, "orc_moe_forward", None, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp)
 _decl(ORC, "orc_kda_decode", None, _vp, _i, _vp, _sz, _vp, _vp, _vp)
 _decl(ORC, "orc_dsa_decode", None, _vp, _i, _vp, _sz, _vp, _vp)
 _decl(ORC, "orc_dsa_width", _sz, _vp)
+_decl(ORC, "orc_mlp_forward", None, _vp, _i, _vp, _sz, _vp)
 _decl(ORC, "orc_decode_batch_ex", _i, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp)
 _decl(ORC, "orc_dsa_decode_sel", None, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp, _sz)
 _decl(ORC, "orc_state_set_pos", None, _vp, _sz)

@@ -20,6 +20,11 @@ the MoE routing of both sides the same (the oracle forced to the engine's
 selections), and the oracle's own routing may differ from the engine's only
 at a near tie of its top-k scores.
 
+The same checks run at the config-3 (full model) per-layer dims too: four
+layers of the reference's config.json shapes -- the first three dense MLPs of
+intermediate 12288, KDA at 64 heads, MoE at inter 2048 -- with the routed
+experts and the vocabulary cut as above.
+
 The long-context case decodes 2200 tokens first, so the indexer's top-2048
 (512 pools of 4) selection binds: selected pools must equal the oracle's
 except where the oracle's own scores tie within the observed score error at
@@ -34,6 +39,7 @@ import synth
 pytestmark = pytest.mark.gpu
 
 KW = synth.c2_config(small=True)
+KW3 = dict(synth.c3_config(4), n_routed_experts=16, vocab_size=16384)
 CAP = 2400
 COS_MIN, REL_MAX = 0.9999, 1e-2
 E2E_COS, E2E_REL = 0.999, 5e-2
@@ -93,27 +99,44 @@ class Report:
         assert not self.bad, "; ".join(self.bad)
 
 
+def make_case(gcuda, kw, seed):
+    W = synth.c2_weights(kw, seed=seed)
+    g = gcuda.GModel(gcuda.make_config(**kw), has_mtp=True, kv_cap=CAP, depth=4)
+    g.load(W)
+    o = O.Model(O.make_config(**kw), W, True, "orc")
+    return W, g, o
+
+
 @pytest.fixture(scope="module")
 def c2(gcuda):
-    W = synth.c2_weights(KW, seed=20261202)
-    g = gcuda.GModel(gcuda.make_config(**KW), has_mtp=True, kv_cap=CAP, depth=4)
-    g.load(W)
-    o = O.Model(O.make_config(**KW), W, True, "orc")
+    W, g, o = make_case(gcuda, KW, 20261202)
     yield W, g, o
     g.close()
 
 
-def engine_state(g, pos):
+@pytest.fixture(scope="module", params=["config2", "config3"])
+def case(request, gcuda):
+    """(kw, W, engine model, oracle model) at the config-2 or the config-3
+    per-layer dims."""
+    if request.param == "config2":
+        yield (KW,) + request.getfixturevalue("c2")
+        return
+    W, g, o = make_case(gcuda, KW3, 20261205)
+    yield KW3, W, g, o
+    g.close()
+
+
+def engine_state(g, pos, kw=KW):
     """The engine's committed state at `pos`, per layer (host copies)."""
-    return [g.dsa_state(l, pos) if KW["layer_is_dsa"][l] else g.kda_state(l)
-            for l in range(KW["num_hidden_layers"])]
+    return [g.dsa_state(l, pos) if kw["layer_is_dsa"][l] else g.kda_state(l)
+            for l in range(kw["num_hidden_layers"])]
 
 
-def oracle_state(o, saved, pos):
+def oracle_state(o, saved, pos, kw=KW):
     """A fresh oracle state holding a saved engine state."""
     st = o.state(CAP)
     for l, a in enumerate(saved):
-        if KW["layer_is_dsa"][l]:
+        if kw["layer_is_dsa"][l]:
             assert O.ORC.orc_state_load_dsa(st, l, *(O.p(x) for x in a), pos) == 0
         else:
             assert O.ORC.orc_state_load_kda(st, l, *(O.p(x) for x in a)) == 0
@@ -121,9 +144,9 @@ def oracle_state(o, saved, pos):
     return st
 
 
-def transplant(g, o, pos):
+def transplant(g, o, pos, kw=KW):
     """An oracle state holding the engine's committed state at `pos`."""
-    return oracle_state(o, engine_state(g, pos), pos)
+    return oracle_state(o, engine_state(g, pos, kw), pos, kw)
 
 
 def stage(g, l, s, ids, reads):
@@ -135,20 +158,20 @@ def stage(g, l, s, ids, reads):
         g.debug_stop(-1, 0)
 
 
-def gpu_routing(g, ids):
+def gpu_routing(g, ids, kw=KW):
     """The engine's MoE selections of a forward over ids, top-k order,
     [L][R][K] (stage-4 stops; nothing is committed)."""
-    R, K, L = len(ids), KW["num_experts_per_tok"], KW["num_hidden_layers"]
+    R, K, L = len(ids), kw["num_experts_per_tok"], kw["num_hidden_layers"]
     sel = np.zeros((L, R, K), np.int32)
     for l in range(L):
-        if KW["mlp_is_sparse"][l]:
+        if kw["mlp_is_sparse"][l]:
             sel[l] = stage(g, l, 4, ids, {"moe_sel": ((8 * 16,), np.int32)})["moe_sel"][:R * K].reshape(R, K)
     return sel
 
 
-def oracle_forward(o, st, ids, forced):
-    R, L, K = len(ids), KW["num_hidden_layers"], KW["num_experts_per_tok"]
-    V, d, hc = KW["vocab_size"], KW["hidden_size"], KW["hc_mult"]
+def oracle_forward(o, st, ids, forced, kw=KW):
+    R, L, K = len(ids), kw["num_hidden_layers"], kw["num_experts_per_tok"]
+    V, d, hc = kw["vocab_size"], kw["hidden_size"], kw["hc_mult"]
     ids = np.ascontiguousarray(ids, np.int32)
     lo, ho, yo = np.empty((R, V), np.uint16), np.empty((R, hc * d), np.uint16), np.empty((R, d), np.uint16)
     osel, gap = np.zeros((L, R, K), np.int32), np.zeros((L, R), np.float32)
@@ -158,20 +181,20 @@ def oracle_forward(o, st, ids, forced):
     return lo, yo, osel, gap
 
 
-def whole_forward(rep, o, new_state, ids, sel, yg, lg, tag=""):
+def whole_forward(rep, o, new_state, ids, sel, yg, lg, tag="", kw=KW):
     """Oracle forwards from fresh copies of the same state: forced to the
     engine's routing (within the composite bound), and free (its routing may
     differ only at a near tie; without a difference, within bound)."""
-    R, L = len(ids), KW["num_hidden_layers"]
+    R, L = len(ids), kw["num_hidden_layers"]
     st = new_state()
-    lo, yo, _, _ = oracle_forward(o, st, ids, sel)
+    lo, yo, _, _ = oracle_forward(o, st, ids, sel, kw)
     O.ORC.orc_state_free(st)
     rep.check(f"{tag}final norm rows (engine routing)", yg, yo, cos_min=E2E_COS, rel_max=E2E_REL)
     rep.check(f"{tag}logits (engine routing)", lg, lo, cos_min=E2E_COS, rel_max=E2E_REL)
     st = new_state()
-    lo, yo, osel, gap = oracle_forward(o, st, ids, None)
+    lo, yo, osel, gap = oracle_forward(o, st, ids, None, kw)
     O.ORC.orc_state_free(st)
-    diff = [(l, t) for l in range(L) if KW["mlp_is_sparse"][l] for t in range(R)
+    diff = [(l, t) for l in range(L) if kw["mlp_is_sparse"][l] for t in range(R)
             if sorted(osel[l, t].tolist()) != sorted(sel[l, t].tolist())]
     if diff:
         l0 = diff[0][0]
@@ -185,8 +208,8 @@ def whole_forward(rep, o, new_state, ids, sel, yg, lg, tag=""):
         rep.check(f"{tag}logits (own routing)", lg, lo, cos_min=E2E_COS, rel_max=E2E_REL)
 
 
-def test_c2_sublayers_vs_oracle(c2):
-    W, g, o = c2
+def test_sublayers_vs_oracle(case):
+    KW, W, g, o = case
     d, hc, R = KW["hidden_size"], KW["hc_mult"], 4
     K = KW["num_experts_per_tok"]
     rng = np.random.default_rng(5)
@@ -199,7 +222,8 @@ def test_c2_sublayers_vs_oracle(c2):
     assert g.pos() == pos
     u16, f4 = np.uint16, np.float32
     rows = lambda n: ((R, n), u16)
-    rep = Report("config-2 stage parity")
+    rep = Report(f"stage parity at {KW['num_hidden_layers']} layers of {KW['linear_num_heads']}-head KDA, "
+                 f"MoE inter {KW['moe_intermediate_size']}")
     for l in range(KW["num_hidden_layers"]):
         # stage 0: mHC pre (attention site) + input RMSNorm
         r0 = stage(g, l, 0, ids, {"h4": rows(hc * d), "x": rows(d), "post": ((R, hc), f4),
@@ -218,7 +242,7 @@ def test_c2_sublayers_vs_oracle(c2):
         rep.fact(f"L{l} stage-1 input = stage-0 output", np.array_equal(r1["x"], r0["x"]), "moved")
         out = np.empty((R, d), u16)
         if KW["layer_is_dsa"][l]:
-            st = transplant(g, o, pos)
+            st = transplant(g, o, pos, KW)
             O.ORC.orc_dsa_decode(o.h, l, O.p(r1["x"]), R, st, O.p(out))
             O.ORC.orc_state_free(st)
             name = "DSA"
@@ -247,9 +271,13 @@ def test_c2_sublayers_vs_oracle(c2):
         rep.check(f"L{l} mHC pre (ffn) x", r3["x"], x3)
         rep.check(f"L{l} mHC pre (ffn) post", r3["post"], post3, to_f=ident)
         rep.check(f"L{l} mHC pre (ffn) comb", r3["comb"], comb3, to_f=ident)
-        # stage 4: the MoE on the engine's x; routing exact
+        # stage 4: the MoE (routing exact) or the dense MLP on the engine's x
         r4 = stage(g, l, 4, ids, {"x": rows(d), "sub": rows(d), "moe_idx": ((8 * 16,), np.int32)})
         out = np.empty((R, d), u16)
+        if not KW["mlp_is_sparse"][l]:
+            O.ORC.orc_mlp_forward(o.h, l, O.p(r4["x"]), R, O.p(out))
+            rep.check(f"L{l} dense MLP (inter {KW['intermediate_size']})", r4["sub"], out)
+            continue
         idx = np.empty((R, K), np.int32)
         wts = np.empty((R, K), f4)
         O.ORC.orc_moe_forward(o.h, l, O.p(r4["x"]), R, O.p(out), O.p(idx), O.p(wts), None)
@@ -261,30 +289,30 @@ def test_c2_sublayers_vs_oracle(c2):
     # the whole forward from the transplanted state (the MoE expand and the
     # head norm + lm_head included), with the engine's routing and the
     # oracle's own
-    sel = gpu_routing(g, ids)
-    saved = engine_state(g, pos)
+    sel = gpu_routing(g, ids, KW)
+    saved = engine_state(g, pos, KW)
     lg, _, yg = g.decode_batch(ids, want_h=True)
-    whole_forward(rep, o, lambda: oracle_state(o, saved, pos), ids, sel, yg, lg)
+    whole_forward(rep, o, lambda: oracle_state(o, saved, pos, KW), ids, sel, yg, lg, kw=KW)
     rep.finish()
 
 
-def test_c2_decode_and_mtp_vs_oracle(c2):
+def test_decode_and_mtp_vs_oracle(case):
     """Fresh sequences on both sides, no transplant: a 12-token prompt in
     batches of 5, 4 and 3 rows (the oracle following the engine's routing),
     then the MTP block on the engine's true pairs and three chained MTP
     steps."""
-    W, g, o = c2
+    KW, W, g, o = case
     rng = np.random.default_rng(11)
     ids = rng.integers(0, KW["vocab_size"], 12).astype(np.int32)
     g.reset()
     st = o.state(CAP)
     yns = []
-    rep = Report("config-2 fresh decode + MTP")
+    rep = Report(f"fresh decode + MTP ({KW['linear_num_heads']}-head KDA)")
     for a, b in ((0, 5), (5, 9), (9, 12)):
         chunk = np.ascontiguousarray(ids[a:b])
-        sel = gpu_routing(g, chunk)
+        sel = gpu_routing(g, chunk, KW)
         lg, _, yg = g.decode_batch(chunk, want_h=True)
-        lo, yo, _, _ = oracle_forward(o, st, chunk, sel)
+        lo, yo, _, _ = oracle_forward(o, st, chunk, sel, KW)
         rep.check(f"yn@{a} (engine routing)", yg, yo, cos_min=E2E_COS, rel_max=E2E_REL)
         rep.check(f"logits@{a} (engine routing)", lg, lo, cos_min=E2E_COS, rel_max=E2E_REL)
         yns.append(yg)
