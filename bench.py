@@ -58,6 +58,12 @@ class ClockSampler:
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes a while to start: wait (bounded) for its first
+            # sample so that a short timed region is still covered
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.05)
+            self.lines.clear()
         except OSError:
             self.proc = None
         return self
