@@ -403,9 +403,24 @@ static void recurrent_head(float *S, const uint16_t *qh, const uint16_t *kh, con
     free(dl); free(kv); free(vf); free(kf); free(qf);
 }
 
-/* c/gkda.h:581-683 with decode = 1 (conv + recurrent chained per token) */
+/* c/gkda.h:581-683: conv chained per token, then the core: recurrent per
+ * token (decode = 1) or the chunked delta rule over the s rows (decode = 0,
+ * the prefill's apus_gkda_chunk) */
+static void kda_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *conv_state,
+                        float *rec_state, int decode, uint16_t *out);
+
 void orc_kda_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,
                     uint16_t *conv_state, float *rec_state, uint16_t *out) {
+    kda_forward(m, layer, x, s, conv_state, rec_state, 1, out);
+}
+
+void orc_kda_prefill(const OrcModel *m, int layer, const uint16_t *x, size_t s,
+                     uint16_t *conv_state, float *rec_state, uint16_t *out) {
+    kda_forward(m, layer, x, s, conv_state, rec_state, 0, out);
+}
+
+static void kda_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *conv_state,
+                        float *rec_state, int decode, uint16_t *out) {
     const OrcConfig *c = &m->c;
     const OLayer *W = &m->L[layer];
     size_t d = (size_t)c->hidden_size, H = (size_t)c->linear_num_heads, D = (size_t)c->linear_head_dim;
@@ -449,11 +464,15 @@ void orc_kda_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,
     gemm(W->b_w, x, bt, s, H, d);
     for (size_t i = 0; i < s * H; i++) beta[i] = orc_bf16_bits(orc_sigmoid(orc_bf16_f32(bt[i])));
     float qscale = (float)pow((double)D, -0.5);
-    for (size_t t = 0; t < s; t++)
-        for (size_t hh = 0; hh < H; hh++)
-            recurrent_head(rec_state + hh * D * D, mq + t * qkv + hh * D, mk + t * qkv + hh * D,
-                           mv + t * qkv + hh * D, g + t * qkv + hh * D, beta[t * H + hh],
-                           core + t * qkv + hh * D, D, qscale);
+    if (decode) {
+        for (size_t t = 0; t < s; t++)
+            for (size_t hh = 0; hh < H; hh++)
+                recurrent_head(rec_state + hh * D * D, mq + t * qkv + hh * D, mk + t * qkv + hh * D,
+                               mv + t * qkv + hh * D, g + t * qkv + hh * D, beta[t * H + hh],
+                               core + t * qkv + hh * D, D, qscale);
+    } else {
+        orc_kda_chunk(mq, mk, mv, g, beta, rec_state, core, s, H, D);
+    }
     gemm(W->g_a, x, ga, s, Dr, d);
     gemm(W->g_b, ga, gate, s, qkv, Dr);
     /* c/gkda.h:543-569 gated o_norm */
@@ -826,11 +845,37 @@ int orc_decode_batch(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
     return orc_decode_batch_ex(m, st, ids, s, logits, h_out, yn_out, NULL, NULL, NULL);
 }
 
-/* c/gmodel.h:1439-1626 apus_gm_run with decode = 1 */
+/* c/gmodel.h:1439-1626 apus_gm_run.  decode = 1: recurrent KDA, DSA one
+ * token at a time (the decode batch); decode = 0: chunked KDA, DSA over the s
+ * tokens in one call (the prefill).  logits: [s][V], or [V] of the last row
+ * only when last_only (the rows are independent, so it is the same row). */
+static int run(OrcModel *m, OrcState *st, const int32_t *ids, size_t s, int decode, uint16_t *logits,
+               int last_only, uint16_t *h_out, uint16_t *yn_out, const int32_t *forced, int32_t *sel_out,
+               float *gap_out);
+
 int orc_decode_batch_ex(OrcModel *m, OrcState *st, const int32_t *ids, size_t s, uint16_t *logits,
                         uint16_t *h_out, uint16_t *yn_out, const int32_t *forced, int32_t *sel_out,
                         float *gap_out) {
+    return run(m, st, ids, s, 1, logits, 0, h_out, yn_out, forced, sel_out, gap_out);
+}
+
+/* c/gmodel.h:1658-1666 apus_gmodel_prefill_h */
+int orc_prefill_h(OrcModel *m, OrcState *st, const int32_t *ids, size_t s, uint16_t *logits,
+                  uint16_t *h_out, uint16_t *yn_out) {
+    return run(m, st, ids, s, 0, logits, 0, h_out, yn_out, NULL, NULL, NULL);
+}
+
+/* The same prompt pass with the logits of the last row only ([V]). */
+int orc_prefill_last(OrcModel *m, OrcState *st, const int32_t *ids, size_t s, uint16_t *logits_last,
+                     uint16_t *h_out, uint16_t *yn_out) {
+    return run(m, st, ids, s, 0, logits_last, 1, h_out, yn_out, NULL, NULL, NULL);
+}
+
+static int run(OrcModel *m, OrcState *st, const int32_t *ids, size_t s, int decode, uint16_t *logits,
+               int last_only, uint16_t *h_out, uint16_t *yn_out, const int32_t *forced, int32_t *sel_out,
+               float *gap_out) {
     const OrcConfig *c = &m->c;
+    if (s < 1) return -1;
     if (st->pos + s > st->cap) return -1;
     size_t d = (size_t)c->hidden_size, hc = (size_t)c->hc_mult, V = (size_t)c->vocab_size;
     uint16_t *h = xc(s * hc * d * 2), *h2 = xc(s * hc * d * 2), *x = xc(s * d * 2), *sub = xc(s * d * 2);
@@ -846,8 +891,9 @@ int orc_decode_batch_ex(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
                             c->rms_norm_eps);
             }
             if (site == 0) {
-                if (!c->layer_is_dsa[l]) orc_kda_decode(m, l, x, s, st->conv[l], st->rec[l], sub);
-                else orc_dsa_decode(m, l, x, s, st, sub);
+                if (!c->layer_is_dsa[l]) kda_forward(m, l, x, s, st->conv[l], st->rec[l], decode, sub);
+                else if (decode) orc_dsa_decode(m, l, x, s, st, sub);
+                else dsa_forward(m, &m->L[l], x, s, &st->dsa[l], sub, NULL, NULL, 0);
             } else if (!c->mlp_is_sparse[l]) {
                 size_t inter = (size_t)c->intermediate_size;
                 for (size_t t = 0; t < s; t++)
@@ -869,7 +915,8 @@ int orc_decode_batch_ex(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
         orc_rmsnorm(yh + t * d, m->norm, yh + t * d, d, c->rms_norm_eps);
     }
     if (yn_out) memcpy(yn_out, yh, s * d * 2);
-    if (logits) gemm(m->head, yh, logits, s, V, d);
+    if (logits && last_only) gemm(m->head, yh + (s - 1) * d, logits, 1, V, d);
+    else if (logits) gemm(m->head, yh, logits, s, V, d);
     st->pos += s;
     free(comb); free(post); free(yh); free(sub); free(x); free(h2); free(h);
     return 0;
@@ -1083,16 +1130,16 @@ static void chain(OrcSpec *sp) {
     if (sp->hook && sp->hook_after_chain) sp->hook(sp->hook_ctx, (int64_t)sp->q, sp->drafts, sp->depth);
 }
 
-/* Prefill in the engine's decode ordering: 8-token decode batches, then the
- * MTP true-pair replay (lag 1, postnorm source: c/gmtp.h:99-119, 741-757). */
+/* c/gmtp.h:698-774 apus_gspec_prefill: the main model's prompt pass
+ * (apus_gmodel_prefill_h: chunked KDA, DSA over the prompt in one call), the
+ * held token from its last row, then the MTP true-pair replay over the
+ * n - 1 pairs in one call (lag 1, postnorm source: c/gmtp.h:99-119). */
 int orc_spec_prefill(OrcSpec *sp, const int32_t *ids, size_t n) {
     size_t V = (size_t)sp->V, d = (size_t)sp->d, hcd = (size_t)sp->hc * d;
-    uint16_t *h_all = xc(n * hcd * 2), *yn_all = xc(n * d * 2), *lg = xc(8 * V * 2);
-    for (size_t t0 = 0; t0 < n; t0 += 8) {
-        size_t k = n - t0 < 8 ? n - t0 : 8;
-        if (orc_decode_batch(sp->m, sp->st, ids + t0, k, lg, h_all + t0 * hcd, yn_all + t0 * d)) return -1;
-        if (t0 + k == n) memcpy(sp->mtp_row, lg + (k - 1) * V, V * 2);
-    }
+    if (n < 1) return -1;
+    uint16_t *h_all = xc(n * hcd * 2), *yn_all = xc(n * d * 2), *lg = xc(V * 2);
+    if (orc_prefill_last(sp->m, sp->st, ids, n, lg, h_all, yn_all)) { free(lg); free(yn_all); free(h_all); return -1; }
+    memcpy(sp->mtp_row, lg, V * 2);
     sp->held = orc_argmax_bf16(sp->mtp_row, V);
     sp->q = n;
     if (sp->hook && !sp->hook_after_chain) {
@@ -1171,13 +1218,10 @@ void orc_spec_stats(const OrcSpec *sp, uint64_t *o) {
 
 int orc_greedy(OrcModel *m, OrcState *st, const int32_t *ids, size_t n, int n_gen, int32_t *out) {
     size_t V = (size_t)m->c.vocab_size;
-    uint16_t *lg = xc(8 * V * 2);
-    int32_t tok = 0;
-    for (size_t t0 = 0; t0 < n; t0 += 8) {
-        size_t k = n - t0 < 8 ? n - t0 : 8;
-        if (orc_decode_batch(m, st, ids + t0, k, lg, NULL, NULL)) { free(lg); return -1; }
-        if (t0 + k == n) tok = orc_argmax_bf16(lg + (k - 1) * V, V);
-    }
+    uint16_t *lg = xc(V * 2);
+    /* the prompt through the prefill (c/apus.c:1079), then one-token decodes */
+    if (orc_prefill_last(m, st, ids, n, lg, NULL, NULL)) { free(lg); return -1; }
+    int32_t tok = orc_argmax_bf16(lg, V);
     for (int i = 0; i < n_gen; i++) {
         out[i] = tok;
         if (i + 1 == n_gen) break;

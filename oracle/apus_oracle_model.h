@@ -71,6 +71,15 @@ int orc_decode_batch_ex(OrcModel *m, OrcState *st, const int32_t *ids, size_t s,
                         uint16_t *h_out, uint16_t *yn_out, const int32_t *forced, int32_t *sel_out,
                         float *gap_out);
 
+/* apus_gmodel_prefill_h (c/gmodel.h:1658-1666): the prompt pass, s tokens
+ * in one call with CHUNKED KDA and the DSA over the s tokens at once.
+ * logits [s,V] (or NULL).  orc_prefill_last: the same with the logits of the
+ * last row only ([V]). */
+int orc_prefill_h(OrcModel *m, OrcState *st, const int32_t *ids, size_t s, uint16_t *logits,
+                  uint16_t *h_out, uint16_t *yn_out);
+int orc_prefill_last(OrcModel *m, OrcState *st, const int32_t *ids, size_t s, uint16_t *logits_last,
+                     uint16_t *h_out, uint16_t *yn_out);
+
 /* Sublayer entry points for unit parity (state passed explicitly). */
 void orc_rmsnorm(const uint16_t *x, const uint16_t *w, uint16_t *y, size_t n, float eps);
 void orc_layernorm(const uint16_t *x, const uint16_t *w, const uint16_t *b, uint16_t *y,
@@ -85,6 +94,9 @@ void orc_moe_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, 
 void orc_mlp_forward(const OrcModel *m, int layer, const uint16_t *x, size_t s, uint16_t *out);
 void orc_kda_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,
                     uint16_t *conv_state, float *rec_state, uint16_t *out);
+/* c/gkda.h:581-683 with decode = 0 (the chunked core over the s rows) */
+void orc_kda_prefill(const OrcModel *m, int layer, const uint16_t *x, size_t s,
+                     uint16_t *conv_state, float *rec_state, uint16_t *out);
 void orc_dsa_decode(const OrcModel *m, int layer, const uint16_t *x, size_t s,
                     OrcState *st, uint16_t *out);
 /* The same with the indexer's selection of every token (topk [s][width],

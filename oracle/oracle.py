@@ -186,6 +186,9 @@ _decl(ORC, "orc_state_load_dsa", _i, _vp, _i, _vp, _vp, _vp, _vp, _sz)
 _decl(ORC, "orc_mtp_state_load", _i, _vp, _vp, _vp, _vp, _vp, _vp, _sz)
 _decl(ORC, "orc_spec_set_force_hook", None, _vp, _vp, _vp)
 _decl(ORC, "orc_spec_raw_drafts", None, _vp, _vp, _vp)
+_decl(ORC, "orc_prefill_h", _i, _vp, _vp, _vp, _sz, _vp, _vp, _vp)
+_decl(ORC, "orc_prefill_last", _i, _vp, _vp, _vp, _sz, _vp, _vp, _vp)
+_decl(ORC, "orc_kda_prefill", None, _vp, _i, _vp, _sz, _vp, _vp, _vp)
 _decl(ORC, "orc_spec_walk", _i, _vp, _i, _sz, _vp, C.c_int32, _vp, C.POINTER(C.c_int), C.POINTER(C.c_int32))
 
 DRAFT_HOOK = C.CFUNCTYPE(None, _vp, C.c_int64, C.POINTER(C.c_int32), C.c_int)
@@ -197,6 +200,7 @@ if REF is not None:
     _decl(REF, "ref_state_new", _vp, _vp, _sz)
     _decl(REF, "ref_state_free", None, _vp)
     _decl(REF, "ref_decode_batch", _i, _vp, _vp, _vp, _sz, _vp, _vp, _vp)
+    _decl(REF, "ref_prefill_h", _i, _vp, _vp, _vp, _sz, _vp, _vp, _vp)
     _decl(REF, "ref_spec_new", _vp, _vp, _vp, _sz, _i)
     _decl(REF, "ref_spec_free", None, _vp)
     _decl(REF, "ref_spec_set_draft_hook", None, _vp, _vp, _vp)
@@ -239,6 +243,31 @@ class Model:
         rc = fn(self.h, st, p(ids), s, p(logits), p(h), p(yn))
         assert rc == 0
         return (logits, h, yn) if want_h else logits
+
+    def prefill(self, st, ids, want_h=False):
+        """apus_gmodel_prefill_h: the prompt pass (chunked KDA, DSA over the
+        prompt in one call); logits of every row."""
+        cfg = self.cfg
+        s = len(ids)
+        ids = np.ascontiguousarray(ids, np.int32)
+        logits = np.empty((s, cfg.vocab_size), np.uint16)
+        h = np.empty((s, cfg.hc_mult * cfg.hidden_size), np.uint16)
+        yn = np.empty((s, cfg.hidden_size), np.uint16)
+        fn = ORC.orc_prefill_h if self.kind == "orc" else REF.ref_prefill_h
+        rc = fn(self.h, st, p(ids), s, p(logits), p(h), p(yn))
+        assert rc == 0
+        return (logits, h, yn) if want_h else logits
+
+    def prefill_last(self, st, ids):
+        """The prompt pass with the last row's logits only: (logits [V], yn [s][d])."""
+        assert self.kind == "orc"
+        cfg = self.cfg
+        s = len(ids)
+        ids = np.ascontiguousarray(ids, np.int32)
+        logits = np.empty(cfg.vocab_size, np.uint16)
+        yn = np.empty((s, cfg.hidden_size), np.uint16)
+        assert ORC.orc_prefill_last(self.h, st, p(ids), s, p(logits), None, p(yn)) == 0
+        return logits, yn
 
 
 def spec_walk(logits16, drafts, held):

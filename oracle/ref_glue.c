@@ -258,11 +258,13 @@ int ref_decode_batch(RefModel *R, ApusGmodelState *st, const int32_t *ids, size_
     return apus_gmodel_decode_batch(R->m, st, ids, s, logits, NULL, h_out, yn_out);
 }
 
-/* The reference spec engine with the main-model prompt pass taken in 8-token
- * decode batches (the B200 engine's prefill ordering) instead of
- * apus_gmodel_prefill_h's chunked ordering; everything after — held token,
- * MTP true-pair replay, snapshot, chain — is apus_gspec_prefill's body
- * (c/gmtp.h:713-774, POSTNORM source, lag 1). */
+/* apus_gmodel_prefill_h (c/gmodel.h:1658-1666): the prompt pass */
+int ref_prefill_h(RefModel *R, ApusGmodelState *st, const int32_t *ids, size_t s, uint16_t *logits,
+                  uint16_t *h_out, uint16_t *yn_out) {
+    return apus_gmodel_prefill_h(R->m, st, ids, s, logits, NULL, h_out, yn_out);
+}
+
+/* The reference spec engine (c/gmtp.h:617-891), greedy, rng seeded 12345. */
 typedef struct {
     ApusGspec sp;
     ApusGmtp mt;
@@ -293,38 +295,7 @@ void ref_spec_set_draft_hook(RefSpec *S, void (*hook)(void *, int64_t, int32_t *
 }
 
 int ref_spec_prefill(RefSpec *S, const int32_t *ids, size_t n) {
-    ApusGspec *sp = &S->sp;
-    const size_t V = (size_t)sp->V, dim = (size_t)sp->dim, hcd = (size_t)sp->hc * dim;
-    uint16_t *h_all = malloc(n * hcd * 2), *yn_all = malloc(n * dim * 2), *l16 = malloc(n * V * 2);
-    for (size_t t0 = 0; t0 < n; t0 += 8) {
-        size_t k = n - t0 < 8 ? n - t0 : 8;
-        if (apus_gmodel_decode_batch(sp->m, sp->st, ids + t0, k, l16 + t0 * V, NULL,
-                                     h_all + t0 * hcd, yn_all + t0 * dim)) return -1;
-    }
-    apus_gmtp_widen(l16 + (n - 1) * V, sp->mtp_logits, V);
-    sp->held = apus_sample(sp->mtp_logits, V, sp->temp, sp->top_p, sp->rng, sp->sample_scratch);
-    sp->q = n;
-    if (sp->draft_override) {
-        sp->draft_override(sp->draft_ctx, (int64_t)sp->q, sp->drafts, sp->depth);
-    } else {
-        uint16_t *ph = malloc(n * dim * 2), *oh = malloc(n * dim * 2);
-        for (size_t t = 0; t < n; t++)
-            apus_gmtp_hnorm_input(sp->mt, h_all + t * hcd, yn_all + t * dim, ph + t * dim);
-        int rc = apus_gmtp_forward(sp->mt, sp->mst, ids + 1, ph, n - 1, l16, oh, NULL);
-        size_t last = n - 2;
-        apus_gmtp_hnorm_input(sp->mt, h_all + (n - 1) * hcd, yn_all + (n - 1) * dim, sp->h_prev);
-        if (rc == 0) {
-            apus_gmtp_widen(l16 + last * V, sp->mtp_logits, V);
-            memcpy(sp->hmtp_a, oh + last * dim, dim * 2);
-            apus_gmtp_snap_take(&sp->mtp_snap, sp->mst);
-            apus_gspec_chain(sp);
-        } else {
-            for (int i = 0; i < sp->depth; i++) sp->drafts[i] = 0;
-        }
-        free(ph); free(oh);
-    }
-    free(h_all); free(yn_all); free(l16);
-    return 0;
+    return apus_gspec_prefill(&S->sp, ids, n);
 }
 
 int ref_spec_step(RefSpec *S, int *out, int cap) { return apus_gspec_step(&S->sp, out, cap); }

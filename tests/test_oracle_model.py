@@ -37,6 +37,44 @@ def test_decode_batch_bitwise_vs_reference(tiny):
         assert np.array_equal(yo, yr)
 
 
+@needs_ref
+@pytest.mark.parametrize("n", [1, 11, 64, 150])
+def test_prefill_bitwise_vs_reference(tiny, n):
+    """apus_gmodel_prefill_h: the prompt in one call (chunked KDA over 64-row
+    chunks, the DSA over the whole prompt); logits, streams and post-norm
+    rows of every position, then one decode batch on the state it left."""
+    kw, cfg, W = tiny
+    mo, mr = O.Model(cfg, W, True, "orc"), O.Model(cfg, W, True, "ref")
+    so, sr = mo.state(256), mr.state(256)
+    ids = np.random.default_rng(n).integers(0, kw["vocab_size"], n).astype(np.int32)
+    lo, ho, yo = mo.prefill(so, ids, True)
+    lr, hr, yr = mr.prefill(sr, ids, True)
+    assert np.array_equal(lo, lr)
+    assert np.array_equal(ho, hr)
+    assert np.array_equal(yo, yr)
+    # the last row alone is the same row
+    st = mo.state(256)
+    ll, yl = mo.prefill_last(st, ids)
+    assert np.array_equal(ll, lo[-1]) and np.array_equal(yl, yo)
+    nxt = np.array([7, 3], np.int32)
+    assert np.array_equal(mo.decode_batch(so, nxt), mr.decode_batch(sr, nxt))
+
+
+def test_prefill_differs_from_decode_batches(tiny):
+    """The prompt pass is not the decode batch: the chunked KDA core sums in
+    another order, so the two orderings agree closely but not bitwise."""
+    kw, cfg, W = tiny
+    m = O.Model(cfg, W, True, "orc")
+    ids = np.random.default_rng(5).integers(0, kw["vocab_size"], 40).astype(np.int32)
+    lp = m.prefill(m.state(64), ids)
+    sd = m.state(64)
+    ld = np.concatenate([m.decode_batch(sd, ids[i:i + 8]) for i in range(0, 40, 8)])
+    a, b = O.f32_of(lp).astype(np.float64), O.f32_of(ld).astype(np.float64)
+    cos = (a * b).sum(1) / np.sqrt((a * a).sum(1) * (b * b).sum(1))
+    assert cos.min() > 0.999
+    assert not np.array_equal(lp, ld)
+
+
 def test_batch_equals_sequential_in_oracle(tiny):
     """Decode-batch interleave: R rows == R one-token decodes (c/gmodel.h:302-310)."""
     kw, cfg, W = tiny
