@@ -153,6 +153,7 @@ apus_gcuda_model_reset = _fn("apus_gcuda_model_reset", _i, _vp)
 apus_gcuda_model_pos = _fn("apus_gcuda_model_pos", _sz, _vp)
 apus_gcuda_decode_batch = _fn("apus_gcuda_decode_batch", _i, _vp, _vp, _sz, _vp, _vp, _vp)
 apus_gcuda_mtp_forward = _fn("apus_gcuda_mtp_forward", _i, _vp, _vp, _vp, _sz, _vp, _vp)
+apus_gcuda_prefill = _fn("apus_gcuda_prefill", _i, _vp, _vp, _sz, _vp, _vp)
 apus_gcuda_gspec_prefill = _fn("apus_gcuda_gspec_prefill", _i, _vp, _vp, _sz)
 apus_gcuda_gspec_step = _fn("apus_gcuda_gspec_step", _i, _vp, _vp, _i)
 apus_gcuda_gspec_step_async = _fn("apus_gcuda_gspec_step_async", _i, _vp)
@@ -312,6 +313,16 @@ class GModel:
         yn = np.empty((s, cfg.hidden_size), np.uint16)
         check(apus_gcuda_decode_batch(self.h, ptr(ids), s, ptr(logits), ptr(h), ptr(yn)), "decode_batch")
         return (logits, h, yn) if want_h else logits
+
+    def prefill(self, ids, want_logits=True):
+        """The prompt pass on a fresh sequence: (logits [n][V] or None, yn [n][d])."""
+        np, cfg = self.np, self.cfg
+        ids = np.ascontiguousarray(ids, np.int32)
+        n = len(ids)
+        logits = np.empty((n, cfg.vocab_size), np.uint16) if want_logits else None
+        yn = np.empty((n, cfg.hidden_size), np.uint16)
+        check(apus_gcuda_prefill(self.h, ptr(ids), n, ptr(logits) if want_logits else None, ptr(yn)), "prefill")
+        return logits, yn
 
     def mtp_forward(self, ids, prev_h):
         np, cfg = self.np, self.cfg

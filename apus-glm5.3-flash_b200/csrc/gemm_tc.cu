@@ -252,9 +252,18 @@ static int tc_map(CUtensorMap *m, const void *base, long rows, long K, long ld, 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS ? 0 : -1;
 }
 
-bool gemm_tc_ok(const void *x, long ldx, const void *w, long ldw, long M, long O, long K) {
-    return M >= 64 && O >= 1 && K >= 1 && M < (1l << 31) && O < (1l << 31) && K < (1l << 31) && ldx >= K &&
+// Shapes and alignments the kernel takes (16-byte aligned operand bases and
+// row strides, for the tensor maps).  Any M >= 1: the rows of the last m tile
+// past M read zeros and are not stored.
+static bool gemm_tc_shape_ok(const void *x, long ldx, const void *w, long ldw, long M, long O, long K) {
+    return M >= 1 && O >= 1 && K >= 1 && M < (1l << 31) && O < (1l << 31) && K < (1l << 31) && ldx >= K &&
            ldw >= K && (ldx % 8) == 0 && (ldw % 8) == 0 && !((uintptr_t)x & 15) && !((uintptr_t)w & 15);
+}
+
+// The linear hooks' policy: 64 rows or more go to the tensor cores, fewer
+// stay on the batch-invariant GEMV.
+bool gemm_tc_ok(const void *x, long ldx, const void *w, long ldw, long M, long O, long K) {
+    return M >= 64 && gemm_tc_shape_ok(x, ldx, w, ldw, M, O, K);
 }
 
 template <int BN>
@@ -274,7 +283,10 @@ static int tc_launch(const CUtensorMap &am, const uint16_t *w, long ldw, TcDesc 
 
 int gemm_tc_launch(const uint16_t *x, long ldx, const uint16_t *w, long ldw, uint16_t *y, long ldy, float *yf,
                    long ldyf, long M, long O, long K, cudaStream_t st) {
-    if (!gemm_tc_ok(x, ldx, w, ldw, M, O, K)) return -1;
+    if (!gemm_tc_shape_ok(x, ldx, w, ldw, M, O, K)) {
+        gcuda_set_error("gemm_tc: unsupported shape %ldx%ldx%ld (ldx %ld, ldw %ld)", M, O, K, ldx, ldw);
+        return -1;
+    }
     const int nsm = gcuda_num_sms();
     if (nsm < 1) return -1;
     const long ntm = (M + tc::BM - 1) / tc::BM;

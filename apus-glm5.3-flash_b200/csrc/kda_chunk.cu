@@ -18,12 +18,16 @@
 // product keeps its operand order, so the only differences from the
 // reference are expf's last bits (CUDA's against libm's).
 //
+// q, k and v rows may be strided (ldx elements apart: the engine's prompt
+// pass reads them from its [q | k | v] conv output); g, beta and out are dense.
+//
 // Layout: CTA (h, p) owns value columns [32p, 32p + 32) of head h, for its
 // slice of v, v_new, the outputs and S; the four CTAs of a head each compute
 // the chunk's attn / intra / kcd (shared-memory-resident, rows padded by one
 // float so a warp's lanes hit distinct banks).  No CTA waits on another.
 #include "common.cuh"
 #include "gcuda.h"
+#include "model_dev.h"
 #include "../../include/apus_gcuda.h"
 
 namespace apus {
@@ -48,7 +52,7 @@ static_assert(sizeof(KcSmem) <= 232448, "shared memory");
 
 __global__ void __launch_bounds__(KC_T) k_kda_chunk(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                                                     const float *g, const uint16_t *beta, float *S,
-                                                    uint16_t *out, int s, int H, float qscale) {
+                                                    uint16_t *out, int s, int H, float qscale, long ldx) {
     extern __shared__ __align__(16) unsigned char kc_dyn[];
     KcSmem &sm = *reinterpret_cast<KcSmem *>(kc_dyn);
     const int h = blockIdx.x / KC_SPLIT, c0 = (blockIdx.x % KC_SPLIT) * KC_DV;
@@ -66,9 +70,9 @@ __global__ void __launch_bounds__(KC_T) k_kda_chunk(const uint16_t *q, const uin
         for (int e = tid; e < KC_C * KC_D; e += KC_T) {
             const int i = e / KC_D, d = e % KC_D, t = n * KC_C + i;
             const bool ok = t < s;
-            const size_t off = (size_t)t * hd + (size_t)h * KC_D + d;
-            sm.qp[i * KC_PD + d] = ok ? bf16_f32(q[off]) : 0.0f;
-            sm.kp[i * KC_PD + d] = ok ? bf16_f32(k[off]) : 0.0f;
+            const size_t off = (size_t)t * hd + (size_t)h * KC_D + d, xo = (size_t)t * ldx + (size_t)h * KC_D + d;
+            sm.qp[i * KC_PD + d] = ok ? bf16_f32(q[xo]) : 0.0f;
+            sm.kp[i * KC_PD + d] = ok ? bf16_f32(k[xo]) : 0.0f;
             sm.gc[i * KC_PD + d] = ok ? g[off] : 0.0f;
         }
         if (tid < KC_C) {
@@ -78,7 +82,7 @@ __global__ void __launch_bounds__(KC_T) k_kda_chunk(const uint16_t *q, const uin
         __syncthreads();
         for (int e = tid; e < KC_C * KC_DV; e += KC_T) {
             const int i = e / KC_DV, c = e % KC_DV, t = n * KC_C + i;
-            const float vv = t < s ? bf16_f32(v[(size_t)t * hd + (size_t)h * KC_D + c0 + c]) : 0.0f;
+            const float vv = t < s ? bf16_f32(v[(size_t)t * ldx + (size_t)h * KC_D + c0 + c]) : 0.0f;
             sm.vp[i * KC_PV + c] = vv * sm.beta[i];
         }
         // l2 norms (c/gkda.h:263-273): thread r < 2C normalises one real row
@@ -275,7 +279,7 @@ __global__ void __launch_bounds__(KC_T) k_kda_chunk(const uint16_t *q, const uin
 using namespace apus;
 
 int kda_chunk_launch(const uint16_t *q, const uint16_t *k, const uint16_t *v, const float *g, const uint16_t *beta,
-                     float *S, uint16_t *out, int s, int H, int D, cudaStream_t st) {
+                     float *S, uint16_t *out, int s, int H, int D, cudaStream_t st, long ldx) {
     if (D != KC_D || H < 1 || s < 0) {
         gcuda_set_error("kda_chunk: head dim %d (only %d), %d heads", D, KC_D, H);
         return -1;
@@ -283,7 +287,8 @@ int kda_chunk_launch(const uint16_t *q, const uint16_t *k, const uint16_t *v, co
     if (s == 0) return 0;
     if (gcuda_smem_limit_once((const void *)k_kda_chunk, (int)sizeof(KcSmem))) return -1;
     const float qscale = (float)pow((double)D, -0.5);
-    k_kda_chunk<<<H * KC_SPLIT, KC_T, sizeof(KcSmem), st>>>(q, k, v, g, beta, S, out, s, H, qscale);
+    if (ldx <= 0) ldx = (long)H * KC_D;
+    k_kda_chunk<<<H * KC_SPLIT, KC_T, sizeof(KcSmem), st>>>(q, k, v, g, beta, S, out, s, H, qscale, ldx);
     return gcuda_check(cudaGetLastError(), "kda_chunk launch");
 }
 
@@ -291,5 +296,5 @@ extern "C" int apus_gcuda_kda_chunk_dev(const uint16_t *q, const uint16_t *k, co
                                         const uint16_t *beta, float *S, uint16_t *out, size_t s, size_t H,
                                         size_t D, void *stream) {
     if (s > (size_t)1 << 30 || H > 4096) { gcuda_set_error("kda_chunk: %zu rows, %zu heads", s, H); return -1; }
-    return kda_chunk_launch(q, k, v, g, beta, S, out, (int)s, (int)H, (int)D, (cudaStream_t)stream);
+    return kda_chunk_launch(q, k, v, g, beta, S, out, (int)s, (int)H, (int)D, (cudaStream_t)stream, 0);
 }

@@ -1234,19 +1234,10 @@ int residual_add_launch(uint16_t *x, const uint16_t *sub, long n, cudaStream_t s
     return ok_launch();
 }
 
-static const int g_two_problems[2] = {0, 1};
-
 int kda_launch(const Dims &D, const LayerW &W, KdaState &KS, const Ctl *ctl, int R, Scratch &S, float *part,
                int *tick, cudaStream_t st) {
     const int qkv = D.qkv, ldkp = kda_ldkp(D);
-    static int *d_probs = nullptr, *d_cnt = nullptr;
-    if (!d_probs) {
-        if (cudaMalloc(&d_probs, 2 * sizeof(int)) != cudaSuccess || cudaMalloc(&d_cnt, sizeof(int)) != cudaSuccess)
-            return -1;
-        const int two = 2;
-        cudaMemcpy(d_probs, g_two_problems, 2 * sizeof(int), cudaMemcpyHostToDevice);
-        cudaMemcpy(d_cnt, &two, sizeof(int), cudaMemcpyHostToDevice);
-    }
+    const int *d_probs = S.two_problems, *d_cnt = S.two_problems + 2;
     // q|k|v|f_a|g_a|b share the normed input: one GEMV
     GemvDesc g{};
     g.W = W.kda.proj; g.x = S.x; g.ldx = D.d; g.R = R; g.O = kda_nproj(D); g.K = D.d; g.fp8 = 0;
@@ -1325,4 +1316,44 @@ int dsa_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *base_n, in
     o.R = R; o.O = D.d; o.K = (long)D.AH * D.vd; o.fp8 = 1; o.y = out; o.ldy = D.d; o.part = part; o.ticket = tick;
     o.pdl = 1;
     return gemv_launch(o, st);
+}
+
+int dsa_rows_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *pos_iota, int p0, int R,
+                    const DsaRows &X, Scratch &S, uint16_t *wbuf, const uint16_t *x, uint16_t *out, cudaStream_t st) {
+    const int ql = D.ql, kl = D.kl, d = D.d;
+    const long nq = (long)D.AH * D.qd, nkv = (long)D.AH * (D.qd + D.vd), nik = 2L * D.ID + D.IH;
+    const long ni = (long)D.IH * D.ID, na = (long)D.AH * D.vd;
+    const int *base = pos_iota + p0;
+    // q_a | kv_a (FP8), then their norms
+    if (fp8_dequant_launch(W.qkva_c, W.qkva_s, wbuf, ql + kl, d, st)) return -1;
+    if (gemm_tc_launch(x, d, wbuf, d, X.qkva, ql + kl, nullptr, 0, R, ql + kl, d, st)) return -1;
+    {
+        NormSeg sg[2] = {{X.qkva, ql + kl, nullptr, nullptr, 0, W.q_a_norm, ql, X.qres, ql},
+                         {X.qkva + ql, ql + kl, nullptr, nullptr, 0, W.kv_a_norm, kl, X.kpass, kl}};
+        if (norm_seg_launch(sg, 2, R, D.eps, nullptr, st)) return -1;
+    }
+    if (fp8_dequant_launch(W.q_b_c, W.q_b_s, wbuf, nq, ql, st)) return -1;
+    if (gemm_tc_launch(X.qres, ql, wbuf, ql, X.q, nq, nullptr, 0, R, nq, ql, st)) return -1;
+    if (gemm_tc_launch(X.kpass, kl, W.kv_b, kl, X.kvb, nkv, nullptr, 0, R, nkv, kl, st)) return -1;
+    if (gemm_tc_launch(x, d, W.idx_kgw, d, X.ikgw, nik, nullptr, 0, R, nik, d, st)) return -1;
+    if (gemm_tc_launch(X.qres, ql, W.idx_wq_b, ql, X.iq, ni, nullptr, 0, R, ni, ql, st)) return -1;
+    // the chunk's cache rows, the pools they complete, every row's pool scores
+    // and selection (each row sees the pools complete at its own position)
+    k_dsa_append<<<dim3(R, D.AH), 128, 0, st>>>(X.kvb, X.ikgw, W.idx_knorm_w, W.idx_knorm_b, base, D.AH, D.qd, D.vd,
+                                                 D.ID, D.IH, DS.cap, DS);
+    k_dsa_pool<<<R, 128, 0, st>>>(W.idx_ape, base, R, D.ID, D.kpool, DS.cap, DS);
+    k_dsa_score<<<dim3((S.maxpools + 7) / 8, R), 256, 0, st>>>(X.iq, X.ikgw, base, D.IH, D.ID, D.kpool, S.maxpools, DS,
+                                                                 X.iscore);
+    k_dsa_select<<<R, 256, 0, st>>>(X.iscore, base, D.kpool, D.topk / D.kpool, S.maxpools, X.isel);
+    if (ok_launch()) return -1;
+    // attention, 8 rows a launch: rows r0.. see positions <= p0 + r0 + t
+    for (int r0 = 0; r0 < R; r0 += MAXR) {
+        const int r = R - r0 < MAXR ? R - r0 : MAXR;
+        k_dsa_attn<<<dim3(D.AH, ASPLIT), 256, dsa_attn_smem(D), st>>>(
+            X.q + (size_t)r0 * nq, base + r0, r, D.AH, D.qd, D.vd, D.kpool, S.maxpools, X.isel + (size_t)r0 * S.maxpools,
+            DS, S.attn_scores, S.attn_p, S.attn_sstride, X.attn + (size_t)r0 * na);
+        if (ok_launch()) return -1;
+    }
+    if (fp8_dequant_launch(W.o_c, W.o_s, wbuf, d, na, st)) return -1;
+    return gemm_tc_launch(X.attn, na, wbuf, na, out, d, nullptr, 0, R, d, na, st);
 }

@@ -19,6 +19,7 @@
 //   chain          D-1 single-row MTP forwards, each argmax -> next draft
 // Rollback is a checkpoint-slot select for KDA (the recurrent kernel wrote
 // the state after every row) and a position rewind for the DSA caches.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -40,6 +41,12 @@ __global__ void k_commit(Ctl *c, int R) {
         c->pos += R;
         c->kda_cur = (c->kda_cur + R) % NSLOT;
     }
+}
+
+// The prompt pass leaves each KDA layer's state in the committed slot itself:
+// only the position advances.
+__global__ void k_commit_rows(Ctl *c, int R) {
+    if (threadIdx.x == 0) c->pos += R;
 }
 
 __global__ void k_mtp_commit(Ctl *c, int R) {
@@ -237,6 +244,20 @@ struct ApusGcudaModel {
     uint8_t *ep_region = nullptr;             // this rank's exchange region
     void *ep_opened[EP_MAX_RANKS] = {};       // peers' regions opened through IPC
     long v0 = 0, vn = 0;                      // this rank's lm_head rows [v0, v0+vn)
+    // the prompt pass's row buffers (allocated by the first prompt)
+    struct Wide {
+        int W = 0;                            // rows of one prompt chunk
+        uint16_t *h4 = nullptr, *h4b = nullptr;   // [W][hc*d]
+        uint16_t *x = nullptr, *sub = nullptr;    // [W][d]
+        float *mix = nullptr, *post = nullptr, *comb = nullptr;
+        KdaRows kda{};
+        DsaRows dsa{};
+        MlpRows mlp{};
+        uint16_t *eh = nullptr, *mx = nullptr, *mxn = nullptr, *oh = nullptr;   // MTP block rows
+        uint16_t *wbuf = nullptr;             // one FP8 matrix dequantised to BF16
+        int32_t *ids = nullptr;               // [cap] prompt ids
+        int *pos = nullptr;                   // 0, 1, 2, ... (row positions)
+    } wide;
 };
 
 static void *dmalloc(ApusGcudaModel *m, size_t n, bool zero = true) {
@@ -413,6 +434,11 @@ static ApusGcudaModel *model_create(const ApusGcudaConfig *cfg, int has_mtp, siz
     S.mxn = (uint16_t *)A((size_t)R * d * 2);
     S.oh = (uint16_t *)A((size_t)R * d * 2);
     S.hprev = (uint16_t *)A((size_t)R * d * 2);
+    S.two_problems = (int *)A(3 * sizeof(int));
+    if (ok) {
+        const int tp[3] = {0, 1, 2};
+        ok = cudaMemcpy(S.two_problems, tp, sizeof tp, cudaMemcpyHostToDevice) == cudaSuccess;
+    }
     // split-K scratch sized for the largest split GEMV: K up to 4 ranges of
     // 4096 over up to V rows
     {
@@ -964,6 +990,223 @@ static int mtp_forward(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t
     return lm_head(m, out_h, R, m->ctl->mtp_picks, want_logits);
 }
 
+// ---- the prompt pass (c/gmodel.h:1658-1666 apus_gmodel_prefill_h) --------
+
+// Rows of one prompt chunk.  Every prompt row takes the same arithmetic
+// whatever the chunk size (the GEMM sums each row alike, the KDA chunks are
+// the prompt's 64-row chunks, the DSA rows attend to positions <= their own),
+// so this only trades memory for fewer weight passes.
+#define PROMPT_ROWS 256
+
+static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+static int ensure_wide(ApusGcudaModel *m) {
+    auto &X = m->wide;
+    if (X.W) return 0;
+    const Dims &D = m->D;
+    const int W = PROMPT_ROWS, d = D.d, qkv = D.qkv, ldkp = kda_ldkp(D), hc = D.hc;
+    const int mp = m->S.maxpools;
+    bool any_dense = false, any_kda = false;
+    for (int l = 0; l < D.L; l++) { any_dense |= !m->L[l].sparse; any_kda |= !m->L[l].is_dsa; }
+    // one arena for the sublayer that runs (KDA, DSA or the dense MLP)
+    const size_t kda_b = any_kda ? al256((size_t)W * ldkp * 2) + al256((size_t)W * 3 * qkv * 2) +
+                                       al256((size_t)2 * W * qkv * 2) + al256((size_t)W * qkv * 4) +
+                                       al256((size_t)W * D.H * 2) + 2 * al256((size_t)W * qkv * 2)
+                                 : 0;
+    const size_t dsa_b = al256((size_t)W * (D.ql + D.kl) * 2) + al256((size_t)W * D.ql * 2) +
+                         al256((size_t)W * D.kl * 2) + al256((size_t)W * D.AH * D.qd * 2) +
+                         al256((size_t)W * D.AH * (D.qd + D.vd) * 2) + al256((size_t)W * D.IH * D.ID * 2) +
+                         al256((size_t)W * (2 * D.ID + D.IH) * 2) + al256((size_t)W * D.AH * D.vd * 2) +
+                         al256((size_t)W * mp * 4) + al256((size_t)W * mp);
+    const size_t mlp_b = any_dense ? al256((size_t)W * 2 * D.dense_inter * 2) + al256((size_t)W * D.dense_inter * 2) : 0;
+    size_t arena_b = kda_b > dsa_b ? kda_b : dsa_b;
+    arena_b = arena_b > mlp_b ? arena_b : mlp_b;
+    size_t wb = (size_t)(D.ql + D.kl) * d;
+    wb = std::max(wb, (size_t)D.AH * D.qd * D.ql);
+    wb = std::max(wb, (size_t)d * D.AH * D.vd);
+    if (any_dense) wb = std::max(wb, (size_t)2 * D.dense_inter * d);
+    bool ok = true;
+    auto A = [&](size_t n) { void *p = dmalloc(m, n, false); ok = ok && p; return p; };
+    X.h4 = (uint16_t *)A((size_t)W * hc * d * 2);
+    X.h4b = (uint16_t *)A((size_t)W * hc * d * 2);
+    X.x = (uint16_t *)A((size_t)W * d * 2);
+    X.sub = (uint16_t *)A((size_t)W * d * 2);
+    X.mix = (float *)A((size_t)W * hc_nchunk(D) * ((2 + hc) * hc + 1) * 4);
+    X.post = (float *)A((size_t)W * hc * 4);
+    X.comb = (float *)A((size_t)W * hc * hc * 4);
+    uint8_t *arena = (uint8_t *)A(arena_b);
+    X.wbuf = (uint16_t *)A(wb * 2);
+    X.ids = (int32_t *)A((size_t)(m->cap + MAXR) * 4);
+    const int npos = m->cap + SLACK + W + MAXR;
+    X.pos = (int *)A((size_t)npos * 4);
+    if (m->has_mtp) {
+        X.eh = (uint16_t *)A((size_t)W * 2 * d * 2);
+        X.mx = (uint16_t *)A((size_t)W * d * 2);
+        X.mxn = (uint16_t *)A((size_t)W * d * 2);
+        X.oh = (uint16_t *)A((size_t)W * d * 2);
+    }
+    if (!ok) { gcuda_set_error("gmodel: prompt-pass buffers: device allocation failed"); return -1; }
+    {
+        uint8_t *p = arena;
+        auto C = [&](size_t n) { uint8_t *q = p; p += al256(n); return (void *)q; };
+        X.kda.W = W;
+        if (any_kda) {
+            X.kda.kp = (uint16_t *)C((size_t)W * ldkp * 2);
+            X.kda.qkvc = (uint16_t *)C((size_t)W * 3 * qkv * 2);
+            X.kda.fgo = (uint16_t *)C((size_t)2 * W * qkv * 2);
+            X.kda.g = (float *)C((size_t)W * qkv * 4);
+            X.kda.beta = (uint16_t *)C((size_t)W * D.H * 2);
+            X.kda.core = (uint16_t *)C((size_t)W * qkv * 2);
+            X.kda.onorm = (uint16_t *)C((size_t)W * qkv * 2);
+        }
+        p = arena;
+        X.dsa.qkva = (uint16_t *)C((size_t)W * (D.ql + D.kl) * 2);
+        X.dsa.qres = (uint16_t *)C((size_t)W * D.ql * 2);
+        X.dsa.kpass = (uint16_t *)C((size_t)W * D.kl * 2);
+        X.dsa.q = (uint16_t *)C((size_t)W * D.AH * D.qd * 2);
+        X.dsa.kvb = (uint16_t *)C((size_t)W * D.AH * (D.qd + D.vd) * 2);
+        X.dsa.iq = (uint16_t *)C((size_t)W * D.IH * D.ID * 2);
+        X.dsa.ikgw = (uint16_t *)C((size_t)W * (2 * D.ID + D.IH) * 2);
+        X.dsa.attn = (uint16_t *)C((size_t)W * D.AH * D.vd * 2);
+        X.dsa.iscore = (float *)C((size_t)W * mp * 4);
+        X.dsa.isel = (uint8_t *)C((size_t)W * mp);
+        p = arena;
+        if (any_dense) {
+            X.mlp.gu = (uint16_t *)C((size_t)W * 2 * D.dense_inter * 2);
+            X.mlp.h = (uint16_t *)C((size_t)W * D.dense_inter * 2);
+        }
+    }
+    if (iota_launch(X.pos, npos, m->st)) return gcuda_check(cudaGetLastError(), "prompt-pass positions");
+    X.W = W;
+    return 0;
+}
+
+// Scratch view of prompt rows r0.. for the per-row mHC kernels.
+static Scratch wide_view(ApusGcudaModel *m, int r0) {
+    Scratch v = m->S;
+    const auto &X = m->wide;
+    const Dims &D = m->D;
+    v.x = X.x + (size_t)r0 * D.d;
+    v.mix = X.mix + (size_t)r0 * hc_nchunk(D) * ((2 + D.hc) * D.hc + 1);
+    v.post = X.post + (size_t)r0 * D.hc;
+    v.comb = X.comb + (size_t)r0 * D.hc * D.hc;
+    return v;
+}
+
+// The main model over prompt rows ids_dev[0..R) at positions p0.. (the layer
+// loop of c/gmodel.h:1439-1626 with decode = 0): mHC maps, norms and the MoE
+// per 8-row group, the KDA / DSA / dense-MLP sublayers over all R rows.  The
+// KDA state is read from and left in checkpoint slot `slot`.  yn_out [R][d]
+// gets the post-final-norm rows.
+static int main_rows(ApusGcudaModel *m, const int32_t *ids_dev, int p0, int R, int slot, uint16_t *yn_out) {
+    const Dims &D = m->D;
+    auto &X = m->wide;
+    cudaStream_t st = m->st;
+    const size_t hcd = (size_t)D.hc * D.d;
+    const bool ep = m->ep_world > 1;
+    m->n_main_fwd++;
+    m->ctl_epoch++;
+    if (k_embed_launch(m->embed, ids_dev, R, D.d, D.hc, X.h4, st)) return -1;
+    uint16_t *h = X.h4, *h2 = X.h4b;
+    for (int r0 = 0; r0 < R; r0 += MAXR) {
+        Scratch v = wide_view(m, r0);
+        if (hc_postmix_launch(D, nullptr, nullptr, h + r0 * hcd, std::min(MAXR, R - r0), v, nullptr,
+                              m->L[0].hc_fn[0], st))
+            return -1;
+    }
+    Scratch v0 = wide_view(m, 0);
+    for (int l = 0; l < D.L; l++) {
+        LayerW &W = m->L[l];
+        if (hc_pre_launch(D, W, 0, h, R, v0, st)) return -1;
+        if (!W.is_dsa) {
+            KdaState &K = m->kda[l];
+            uint16_t *cs = K.conv + (size_t)slot * 3 * D.qkv * (D.K - 1);
+            float *rs = K.rec + (size_t)slot * D.H * D.D * D.D;
+            if (kda_rows_launch(D, W, cs, rs, R, X.kda, X.x, X.sub, st)) return -1;
+        } else if (dsa_rows_launch(D, W.dsa, m->dsa[l], X.pos, p0, R, X.dsa, m->S, X.wbuf, X.x, X.sub, st)) {
+            return -1;
+        }
+        for (int r0 = 0; r0 < R; r0 += MAXR) {
+            Scratch v = wide_view(m, r0);
+            if (hc_postmix_launch(D, X.sub + (size_t)r0 * D.d, nullptr, h + r0 * hcd, std::min(MAXR, R - r0), v,
+                                  h2 + r0 * hcd, W.hc_fn[1], st))
+                return -1;
+        }
+        std::swap(h, h2);
+        if (hc_pre_launch(D, W, 1, h, R, v0, st)) return -1;
+        const uint16_t *fn_next = l + 1 < D.L ? m->L[l + 1].hc_fn[0] : nullptr;
+        if (!W.sparse && mlp_rows_launch(W.moe, R, X.mlp, X.wbuf, X.x, X.sub, st)) return -1;
+        for (int r0 = 0; r0 < R; r0 += MAXR) {
+            const int r = std::min(MAXR, R - r0);
+            Scratch v = wide_view(m, r0);
+            uint16_t *sub = X.sub + (size_t)r0 * D.d;
+            if (W.sparse) {
+                // one GPU: the combine of the expert outputs happens inside the expand
+                if (moe_forward_launch(W.moe, X.x + (size_t)r0 * D.d, D.d, r, ep ? sub : nullptr, D.d, nullptr, st))
+                    return -1;
+                if (hc_postmix_launch(D, ep ? sub : nullptr, ep ? nullptr : &W.moe, h + r0 * hcd, r, v, h2 + r0 * hcd,
+                                      fn_next, st))
+                    return -1;
+            } else if (hc_postmix_launch(D, sub, nullptr, h + r0 * hcd, r, v, h2 + r0 * hcd, fn_next, st)) {
+                return -1;
+            }
+        }
+        std::swap(h, h2);
+    }
+    return head_norm_launch(D, h, m->norm, R, yn_out, nullptr, st);
+}
+
+// The MTP block (c/gmtp.h:471-541) over R true pairs (ids_dev[t],
+// prev_h[t]) at MTP cache positions p0..; out rows -> wide.oh.
+static int mtp_rows(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t *prev_h, int p0, int R) {
+    const Dims &D = m->D;
+    auto &X = m->wide;
+    cudaStream_t st = m->st;
+    const LayerW &W = m->L[D.L];
+    const int d = D.d;
+    m->n_mtp_fwd++;
+    m->ctl_epoch++;
+    {
+        NormSeg sg[2] = {{m->embed, d, ids_dev, nullptr, 0, m->enorm, d, X.eh, 2L * d},
+                         {prev_h, d, nullptr, nullptr, 0, m->hnorm, d, X.eh + d, 2L * d}};
+        if (norm_seg_launch(sg, 2, R, D.eps, nullptr, st)) return -1;
+    }
+    if (gemm_tc_launch(X.eh, 2L * d, m->eh_proj, 2L * d, X.mx, d, nullptr, 0, R, d, 2L * d, st)) return -1;
+    if (rmsnorm_rows_launch(X.mx, d, W.input_norm, d, R, D.eps, X.mxn, d, st)) return -1;
+    if (dsa_rows_launch(D, W.dsa, m->mtp_dsa, X.pos, p0, R, X.dsa, m->S, X.wbuf, X.mxn, X.sub, st)) return -1;
+    {   // x = bf16(x + attn); post_attention_layernorm
+        NormSeg sg = {X.mx, d, nullptr, X.sub, d, W.post_norm, d, X.mxn, d};
+        if (norm_seg_launch(&sg, 1, R, D.eps, nullptr, st)) return -1;
+    }
+    for (int r0 = 0; r0 < R; r0 += MAXR)
+        if (moe_forward_launch(W.moe, X.mxn + (size_t)r0 * d, d, std::min(MAXR, R - r0), X.sub + (size_t)r0 * d, d,
+                               nullptr, st))
+            return -1;
+    {   // x = bf16(x + moe); shared_head.norm
+        NormSeg sg = {X.mx, d, nullptr, X.sub, d, m->shared_norm, d, X.oh, d};
+        return norm_seg_launch(&sg, 1, R, D.eps, nullptr, st);
+    }
+}
+
+// The prompt ids[0..n) from a reset sequence: chunks of PROMPT_ROWS rows
+// through the main model, committed chunk by chunk, every position's
+// post-norm row kept in yn_prompt; then the lm_head of the last row (pick in
+// ctl->picks[0], its logits in S.logits row 0 when want_logits).
+static int prompt_pass(ApusGcudaModel *m, const int32_t *ids, size_t n, bool want_logits) {
+    if (ensure_wide(m)) return -1;
+    auto &X = m->wide;
+    const int d = m->D.d;
+    if (gcuda_check(cudaMemcpyAsync(X.ids, ids, n * 4, cudaMemcpyHostToDevice, m->st), "prompt upload")) return -1;
+    const int slot = read_ctl(m).kda_cur;
+    for (size_t c0 = 0; c0 < n; c0 += X.W) {
+        const int R = (int)std::min((size_t)X.W, n - c0);
+        if (main_rows(m, X.ids + c0, (int)c0, R, slot, m->yn_prompt + c0 * d)) return -1;
+        k_commit_rows<<<1, 32, 0, m->st>>>(m->ctl, R);
+    }
+    if (cudaMemsetAsync(m->S.amax, 0, sizeof(unsigned long long), m->st) != cudaSuccess) return -1;
+    return lm_head(m, m->yn_prompt + (n - 1) * d, 1, m->ctl->picks, want_logits);
+}
+
 static bool ids_ok(const ApusGcudaModel *m, const int32_t *ids, size_t n, const char *what) {
     for (size_t i = 0; i < n; i++)
         if (ids[i] < 0 || ids[i] >= m->D.V) {
@@ -1013,6 +1256,32 @@ extern "C" int apus_gcuda_decode_batch(ApusGcudaModel *m, const int32_t *ids, si
     return gcuda_check(cudaStreamSynchronize(m->st), "decode_batch");
 }
 
+extern "C" int apus_gcuda_prefill(ApusGcudaModel *m, const int32_t *ids, size_t n, uint16_t *logits,
+                                  uint16_t *yn_out) {
+    const Dims &D = m->D;
+    if (n < 1 || n > (size_t)m->cap) { gcuda_set_error("prefill: %zu prompt tokens", n); return -1; }
+    if (!ids_ok(m, ids, n, "prefill")) return -1;
+    if (logits && m->ep_world > 1) { gcuda_set_error("prefill: logits are split over the ranks"); return -1; }
+    if (apus_gcuda_model_reset(m)) return -1;
+    if (prompt_pass(m, ids, n, false)) return fail_ctl(m, "prefill");
+    if (logits) {       // every row's logits, 8 rows a launch of the head
+        for (size_t t0 = 0; t0 < n; t0 += MAXR) {
+            const int k = (int)std::min((size_t)MAXR, n - t0);
+            if (cudaMemsetAsync(m->S.amax, 0, k * sizeof(unsigned long long), m->st) != cudaSuccess ||
+                lm_head(m, m->yn_prompt + t0 * D.d, k, m->ctl->picks, true))
+                return fail_ctl(m, "prefill head");
+            if (gcuda_check(cudaMemcpyAsync(logits + t0 * D.V, m->S.logits, (size_t)k * D.V * 2,
+                                            cudaMemcpyDeviceToHost, m->st), "prefill logits"))
+                return -1;
+        }
+    }
+    if (yn_out && gcuda_check(cudaMemcpyAsync(yn_out, m->yn_prompt, n * D.d * 2, cudaMemcpyDeviceToHost, m->st),
+                              "prefill rows"))
+        return -1;
+    if (gcuda_check(cudaStreamSynchronize(m->st), "prefill")) return -1;
+    return tc_error_read_and_clear() ? (gcuda_set_error("prefill: a GEMM wait gave up"), -1) : 0;
+}
+
 extern "C" int apus_gcuda_mtp_forward(ApusGcudaModel *m, const int32_t *ids, const uint16_t *prev_h, size_t s,
                                       uint16_t *logits, uint16_t *out_h) {
     const Dims &D = m->D;
@@ -1054,41 +1323,38 @@ extern "C" int apus_gcuda_gspec_prefill(ApusGcudaModel *m, const int32_t *ids, s
     if (n < 1 || n > (size_t)m->cap) { gcuda_set_error("gspec_prefill: %zu prompt tokens", n); return -1; }
     if (!ids_ok(m, ids, n, "gspec_prefill")) return -1;
     if (apus_gcuda_model_reset(m)) return -1;
-    std::vector<int32_t> h(ids, ids + n);
-    // main model over the prompt in 8-row decode batches; keep every yn row
-    for (size_t t0 = 0; t0 < n; t0 += MAXR) {
-        const int k = (int)(n - t0 < MAXR ? n - t0 : MAXR);
-        const bool last = t0 + k == n;
-        cudaMemcpyAsync(m->ids, h.data() + t0, k * 4, cudaMemcpyHostToDevice, m->st);
-        if (main_forward(m, m->ids, k, m->yn_prompt + t0 * d, last && m->temp > 0.0f))
-            return fail_ctl(m, "gspec_prefill");
-        k_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
-        // the first held token: exactly the non-speculative first draw (c/gmtp.h:724-727)
-        if (last && draw_held(m, k - 1)) return fail_ctl(m, "gspec_prefill draw");
-    }
+    // the main model's prompt pass (c/gmtp.h:708-711); the first held token is
+    // exactly the non-speculative first draw (c/gmtp.h:724-727)
+    if (prompt_pass(m, ids, n, m->temp > 0.0f)) return fail_ctl(m, "gspec_prefill");
+    if (draw_held(m, 0)) return fail_ctl(m, "gspec_prefill draw");
     // a one-token prompt has no true pair: drafts stay 0 (c/gmtp.h:741-757)
     if (n < 2) return gcuda_check(cudaStreamSynchronize(m->st), "gspec_prefill");
-    // MTP true-pair replay: (h_{t-1}, tok_t) for t = 1..n-1
-    for (size_t t0 = 1; t0 < n; t0 += MAXR) {
-        const int k = (int)(n - t0 < MAXR ? n - t0 : MAXR);
-        cudaMemcpyAsync(m->ids, h.data() + t0, k * 4, cudaMemcpyHostToDevice, m->st);
-        if (mtp_forward(m, m->ids, m->yn_prompt + (t0 - 1) * d, k, &m->ctl->mtp_n, false))
-            return fail_ctl(m, "gspec_prefill replay");
-        k_mtp_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
-        if (t0 + k == n) {
-            k_copy_row<<<(d + 255) / 256, 256, 0, m->st>>>(m->S.oh, k - 1, d, m->hmtp);
-            // drafts[0] = argmax of the last replay row
-            Ctl tmp = read_ctl(m);
-            tmp.drafts[0] = tmp.mtp_picks[k - 1];
-            for (int i = 1; i < MAXR; i++) tmp.chain_pos[i] = tmp.mtp_n + i - 1;
-            cudaMemcpy(m->ctl, &tmp, sizeof tmp, cudaMemcpyHostToDevice);
-        }
+    // MTP true-pair replay (h_{t-1}, tok_t), t = 1..n-1, chunk by chunk
+    auto &X = m->wide;
+    int R = 0;
+    for (size_t c0 = 0; c0 + 1 < n; c0 += X.W) {
+        R = (int)std::min((size_t)X.W, n - 1 - c0);
+        if (mtp_rows(m, X.ids + 1 + c0, m->yn_prompt + c0 * d, (int)c0, R)) return fail_ctl(m, "gspec_prefill replay");
+        k_mtp_commit<<<1, 32, 0, m->st>>>(m->ctl, R);
+    }
+    // drafts[0] = argmax of the last replay row; its hidden starts the chain
+    const uint16_t *last = X.oh + (size_t)(R - 1) * d;
+    k_copy_row<<<(d + 255) / 256, 256, 0, m->st>>>(last, 0, d, m->hmtp);
+    if (cudaMemsetAsync(m->S.amax, 0, sizeof(unsigned long long), m->st) != cudaSuccess ||
+        lm_head(m, last, 1, m->ctl->mtp_picks, false))
+        return fail_ctl(m, "gspec_prefill replay head");
+    {
+        Ctl tmp = read_ctl(m);
+        tmp.drafts[0] = tmp.mtp_picks[0];
+        for (int i = 1; i < MAXR; i++) tmp.chain_pos[i] = tmp.mtp_n + i - 1;
+        if (gcuda_check(cudaMemcpy(m->ctl, &tmp, sizeof tmp, cudaMemcpyHostToDevice), "gspec_prefill ctl")) return -1;
     }
     // the hnorm input carried to the next step: yn of position n-1
     k_copy_row<<<(d + 255) / 256, 256, 0, m->st>>>(m->yn_prompt, (long)n - 1, d, m->hcarry);
     if (draft_chain(m)) return fail_ctl(m, "gspec_prefill chain");
     k_force<<<1, 32, 0, m->st>>>(m->ctl, m->truth, m->depth, D.V);
-    return gcuda_check(cudaStreamSynchronize(m->st), "gspec_prefill");
+    if (gcuda_check(cudaStreamSynchronize(m->st), "gspec_prefill")) return -1;
+    return tc_error_read_and_clear() ? (gcuda_set_error("gspec_prefill: a GEMM wait gave up"), -1) : 0;
 }
 
 // One verify step of Dp <= depth rows (fewer only at the capacity edge,
@@ -1290,15 +1556,9 @@ static int generate(ApusGcudaModel *m, const int32_t *ids, size_t n, int n_gen, 
     const float temp = m->temp;
     if (!smp) m->temp = 0.0f;            // draw_held picks greedily
     int rc = 0;
-    std::vector<int32_t> h(ids, ids + n);
-    for (size_t t0 = 0; t0 < n && !rc; t0 += MAXR) {
-        const int k = (int)(n - t0 < MAXR ? n - t0 : MAXR);
-        const bool last = t0 + k == n;
-        cudaMemcpyAsync(m->ids, h.data() + t0, k * 4, cudaMemcpyHostToDevice, m->st);
-        rc = main_forward(m, m->ids, k, m->S.yn, last && smp);
-        if (!rc) k_commit<<<1, 32, 0, m->st>>>(m->ctl, k);
-        if (!rc && last) rc = draw_held(m, k - 1);
-    }
+    // the prompt through the prefill (c/apus.c:1079), then one-token decodes
+    rc = prompt_pass(m, ids, n, smp);
+    if (!rc) rc = draw_held(m, 0);
     for (int i = 0; i < n_gen && !rc; i++) {
         k_greedy_prep<<<1, 32, 0, m->st>>>(m->ctl, m->ids);
         if (i + 1 < n_gen) {

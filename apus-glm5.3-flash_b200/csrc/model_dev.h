@@ -138,6 +138,7 @@ struct Scratch {
     uint16_t *mx, *mxn;     // [R][d]
     uint16_t *oh;           // [R][d] post-shared_head.norm rows
     uint16_t *hprev;        // [R][d] hnorm inputs
+    int *two_problems;      // {0, 1, 2}: the f_b / g_b problem list of one grouped GEMV and its count
     int maxpools;
 };
 
@@ -199,3 +200,44 @@ int residual_add_launch(uint16_t *x, const uint16_t *sub, long n, cudaStream_t s
 int sample_prepare(int V);
 int sample_launch(const uint16_t *logits, long ld, int V, int rows, float temp, float top_p,
                   const unsigned long long *rng_dev, unsigned long long rng_val, int *out, cudaStream_t st);
+
+// ---- the prompt pass (prefill.cu; dsa_rows_launch in layers.cu) -----------
+// Buffers of up to W prompt rows (device).  KDA, DSA and the dense MLP run one
+// after another, so their row buffers share one arena.
+struct KdaRows {
+    int W;
+    uint16_t *kp;           // [W][kda_ldkp]
+    uint16_t *qkvc;         // [W][3qkv] post-conv
+    uint16_t *fgo;          // [2][W][qkv] f_b, g_b outputs
+    float *g;               // [W][qkv] forget gate (log decay)
+    uint16_t *beta;         // [W][H]
+    uint16_t *core;         // [W][qkv] chunked-core output
+    uint16_t *onorm;        // [W][qkv] gated o_norm
+};
+struct DsaRows {
+    uint16_t *qkva, *qres, *kpass, *q, *kvb, *iq, *ikgw, *attn;
+    float *iscore;          // [W][maxpools]
+    uint8_t *isel;          // [W][maxpools]
+};
+struct MlpRows {
+    uint16_t *gu;           // [W][2*inter]
+    uint16_t *h;            // [W][inter]
+};
+int iota_launch(int *a, int n, cudaStream_t st);
+// The chunked KDA core (kda_chunk.cu) over s rows; q, k, v rows ldx elements
+// apart (0: dense, H*D).
+int kda_chunk_launch(const uint16_t *q, const uint16_t *k, const uint16_t *v, const float *g, const uint16_t *beta,
+                     float *S, uint16_t *out, int s, int H, int D, cudaStream_t st, long ldx);
+// The KDA sublayer over R <= X.W prompt rows x -> out, the conv window and the
+// recurrent state taken from and left in the committed slot.
+int kda_rows_launch(const Dims &D, const LayerW &W, uint16_t *conv_slot, float *rec_slot, int R, const KdaRows &X,
+                    const uint16_t *x, uint16_t *out, cudaStream_t st);
+// The DSA sublayer over R prompt rows at positions pos_iota[p0 ..] (pos_iota
+// holds 0, 1, 2, ...): the chunk's K/V and indexer rows appended, then each
+// row's indexer selection and attention over the positions <= its own.  FP8
+// matrices are dequantised into wbuf for the GEMMs; attention runs in 8-row
+// launches on S's attention scratch.
+int dsa_rows_launch(const Dims &D, const DsaW &W, DsaState &DS, const int *pos_iota, int p0, int R,
+                    const DsaRows &X, Scratch &S, uint16_t *wbuf, const uint16_t *x, uint16_t *out, cudaStream_t st);
+int mlp_rows_launch(const MoeDev &md, int R, const MlpRows &X, uint16_t *wbuf, const uint16_t *x, uint16_t *out,
+                    cudaStream_t st);

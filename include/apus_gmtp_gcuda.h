@@ -118,6 +118,15 @@ size_t apus_gcuda_model_pos(const ApusGcudaModel *m);            /* c/gmodel.h:2
 int apus_gcuda_decode_batch(ApusGcudaModel *m, const int32_t *ids, size_t s, uint16_t *logits,
                             uint16_t *h_out, uint16_t *yn_out);
 
+/* c/gmodel.h:317-320 apus_gmodel_prefill_h on a fresh sequence (reset
+ * first): the prompt ids[n] in one pass, chunked KDA and the DSA over the
+ * prompt as the reference's prefill, committed.  The prompt's rows go through
+ * each layer together (chunks of 256), the linears on the tensor-core GEMM.
+ * logits [n,V] (every row's; the rows' lm_head runs only when asked),
+ * yn_out [n,dim] (post-final-norm rows); host arrays, each may be NULL.
+ * Expert-parallel models return no logits. */
+int apus_gcuda_prefill(ApusGcudaModel *m, const int32_t *ids, size_t n, uint16_t *logits, uint16_t *yn_out);
+
 /* c/gmtp.h:169-172 apus_gmtp_forward: s <= 8 pairs (ids[t], prev_h[t]) at the
  * MTP block's current position, committed.  logits [s,V], out_h [s,dim]. */
 int apus_gcuda_mtp_forward(ApusGcudaModel *m, const int32_t *ids, const uint16_t *prev_h, size_t s,

@@ -118,12 +118,12 @@ def test_greedy_vs_oracle(gcuda, tiny):
     out = g.greedy(ids, n_gen)
     if out != ref.tolist():
         j = next(i for i in range(n_gen) if out[i] != ref[i])
-        # teacher-forced oracle logits of the step that differs: only a near tie may flip
+        # teacher-forced oracle logits of the step that differs (the prompt
+        # pass, then one-token decodes): only a near tie may flip
         st = o.state(256)
-        ctx = np.concatenate([ids, ref[:j]]).astype(np.int32)
-        lo = None
-        for a in range(0, len(ctx), 8):
-            lo = o.decode_batch(st, ctx[a:a + 8])
+        lo = o.prefill(st, ids)
+        for a in range(0, j, 8):
+            lo = o.decode_batch(st, ref[a:min(a + 8, j)].astype(np.int32))
         assert margin(lo[-1]) < 0.05 * float(np.abs(f32(lo[-1])).max()), f"greedy differs at {j}"
 
 
@@ -182,9 +182,9 @@ def test_spec_forced_partial_accept_rollback(gcuda, tiny):
     assert 0 < stats["accepted"] < stats["offered"]
     assert out == truth[:len(out)]
     dig = g.digest()
-    # plain decode of prompt + emitted tokens on a fresh sequence
-    g.reset()
-    ctx = np.array(PROMPT + out, np.int32)
+    # the prompt pass on a fresh sequence, then a plain decode of the emitted tokens
+    g.prefill(PROMPT, want_logits=False)
+    ctx = np.array(out, np.int32)
     for a in range(0, len(ctx), 8):
         g.decode_batch(ctx[a:a + 8])
     assert g.digest() == dig

@@ -164,9 +164,7 @@ def test_sampled_prefill_draw(gcuda, tiny):
     last prompt row's logits with the first uniform of the stream."""
     kw, W = tiny
     g = gpu_model(gcuda, kw, W)
-    lg = None
-    for a in range(0, len(PROMPT), 8):
-        lg = g.decode_batch(np.array(PROMPT[a:a + 8], np.int32))
+    lg, _ = g.prefill(PROMPT)
     draws, _ = O.rng_draws(777, 1)
     want = O.sample_exact(lg[-1], 0.7, 0.9, draws[0] >> 11)
     g.sampling(0.7, 0.9, 777)

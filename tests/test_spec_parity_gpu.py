@@ -15,7 +15,8 @@
     forcing, must be equal wherever the oracle's pick is not a near tie
     (relative top-2 margin above a per-dims MARGIN); the emitted streams must be equal
     up to the first position where the two engines' greedy picks may
-    differ (a near tie of the oracle's logits).
+    differ (a near tie of the oracle's logits).  Seeded extra prompts run
+    until at least depth - 1 drafts were compared away from near ties.
 """
 import ctypes as C
 
@@ -98,12 +99,14 @@ def test_walk_bitwise_on_device_logits(gcuda, tiny, p):
     g.close()
 
 
-def draft_parity(gcuda, kw, W, depth, p, n_steps, cap, margin):
+def draft_parity(gcuda, kw, W, depth, p, n_steps, cap, margin, prompt=PROMPT):
+    """Drafts compared on one prompt: (drafts compared away from a near tie,
+    drafts equal)."""
     V = kw["vocab_size"]
     # the oracle's own greedy stream is the truth the forcing uses on both sides
     o = O.Model(O.make_config(**kw), W, True, "orc")
     truth = np.zeros(n_steps * depth + 8, np.int32)
-    ids = np.array(PROMPT, np.int32)
+    ids = np.array(prompt, np.int32)
     st0 = o.state(cap)
     assert O.ORC.orc_greedy(o.h, st0, O.p(ids), len(ids), len(truth), O.p(truth)) == 0
     O.ORC.orc_state_free(st0)
@@ -111,13 +114,14 @@ def draft_parity(gcuda, kw, W, depth, p, n_steps, cap, margin):
     seed = 31
     st, mst = o.state(cap), O.ORC.orc_mtp_state_new(o.h, cap)
     sp = O.ORC.orc_spec_new(o.h, st, mst, depth)
-    hook = force_rule(truth, len(PROMPT), p, seed, V)
+    hook = force_rule(truth, len(prompt), p, seed, V)
     O.ORC.orc_spec_set_force_hook(sp, hook, None)
     g = gcuda.GModel(gcuda.make_config(**kw), has_mtp=True, kv_cap=cap, depth=depth)
     g.load(W)
-    g.force(truth, base=len(PROMPT), p=p, seed=seed)
+    g.keep_logits(True)
+    g.force(truth, base=len(prompt), p=p, seed=seed)
     assert O.ORC.orc_spec_prefill(sp, O.p(ids), len(ids)) == 0
-    g.spec_prefill(PROMPT)
+    g.spec_prefill(prompt)
     raw_o = np.zeros(depth, np.int32)
     marg = np.zeros(depth, np.float32)
     buf = (C.c_int * (depth + 1))()
@@ -139,7 +143,7 @@ def draft_parity(gcuda, kw, W, depth, p, n_steps, cap, margin):
             agreed += 1
         q = g.stats()[0]["pos"]
         assert g.debug_read("drafts", (depth,), np.int32).tolist() == \
-            O_forced(truth, len(PROMPT), p, seed, V, q, raw_g)
+            O_forced(truth, len(prompt), p, seed, V, q, raw_g)
         if step == n_steps:
             break
         ne = O.ORC.orc_spec_step(sp, buf, depth + 1)
@@ -147,15 +151,41 @@ def draft_parity(gcuda, kw, W, depth, p, n_steps, cap, margin):
         out_g = g.spec_step()
         if out_g != out_o:
             # the two engines' greedy streams split (a near tie of the main
-            # model's logits): the drafts after it are not comparable
-            assert out_g[:len(out_o)] != out_o[:len(out_g)], "emitted counts differ on equal tokens"
+            # model's logits): the drafts after it are not comparable.  Token
+            # i >= 1 of a step is draft i accepted on verify row i-1's pick, so
+            # the rows disagree at k = (first differing token) - 1, or at the
+            # last row of the shorter step when one is a prefix of the other;
+            # the engine's own pick there must be a near tie (token 0 is the
+            # previous step's last pick, checked no further)
+            diff = [i for i in range(min(len(out_g), len(out_o))) if out_g[i] != out_o[i]]
+            k = diff[0] - 1 if diff else min(len(out_g), len(out_o)) - 1
+            if k >= 0:
+                row = O.f32_of(g.debug_read("logits", (depth, V), np.uint16)[k]).astype(np.float64)
+                top = np.sort(row)
+                tie = (top[-1] - top[-2]) / max(abs(top[-1]), 1e-30)   # the oracle's top2_margin
+                assert tie <= margin, f"streams split at verify row {k} away from a near tie ({tie:.3g})"
             break
     O.ORC.orc_spec_free(sp)
     O.ORC.orc_mtp_state_free(mst)
     O.ORC.orc_state_free(st)
     g.close()
-    assert checked >= depth - 1, f"only {checked} drafts compared away from near ties"
     return checked, agreed
+
+
+def draft_parity_prompts(gcuda, kw, W, depth, p, n_steps, cap, margin, n_prompts):
+    """draft_parity over the fixed prompt and seeded random ones until at
+    least depth - 1 drafts were compared away from near ties (a run ends where
+    the two engines' greedy streams split at a near tie, which may come early)."""
+    rng = np.random.default_rng(20261208)
+    prompts = [PROMPT] + [rng.integers(0, kw["vocab_size"], 11 + 4 * i).tolist() for i in range(n_prompts - 1)]
+    checked = agreed = 0
+    for pr in prompts:
+        c, a = draft_parity(gcuda, kw, W, depth, p, n_steps, cap, margin, pr)
+        checked, agreed = checked + c, agreed + a
+        if checked >= depth - 1:
+            break
+    assert checked >= depth - 1, f"only {checked} drafts compared away from near ties"
+    print(f"{agreed} drafts equal, {checked} of them away from near ties")
 
 
 def O_forced(truth, base, p, seed, V, q, drafts):
@@ -173,10 +203,10 @@ def O_forced(truth, base, p, seed, V, q, drafts):
 @pytest.mark.parametrize("p", [0.0, 0.5])
 def test_drafts_vs_oracle_tiny(gcuda, tiny, p):
     kw, W = tiny
-    draft_parity(gcuda, kw, W, depth=4, p=p, n_steps=16, cap=256, margin=MARGIN_TINY)
+    draft_parity_prompts(gcuda, kw, W, depth=4, p=p, n_steps=16, cap=256, margin=MARGIN_TINY, n_prompts=4)
 
 
 def test_drafts_vs_oracle_config2_dims(gcuda):
     kw = synth.c2_config(small=True)
     W = synth.c2_weights(kw, seed=20261203)
-    draft_parity(gcuda, kw, W, depth=4, p=0.5, n_steps=6, cap=128, margin=MARGIN_C2)
+    draft_parity_prompts(gcuda, kw, W, depth=4, p=0.5, n_steps=6, cap=128, margin=MARGIN_C2, n_prompts=3)
