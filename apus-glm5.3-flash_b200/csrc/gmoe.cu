@@ -36,23 +36,23 @@ APUS_DEV float pw_sum_small(const float *a, int n) {
     return pw_sum_leaf(a, n);
 }
 
-__global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float *logits, const int32_t *forced) {
-    pdl_launch_dependents();
-    __shared__ float sc[MOE_MAX_R][MOE_MAX_E];
-    __shared__ int flag[MOE_MAX_E + 1];
-    __shared__ int slot_of[MOE_MAX_E + 1];
+// The selection of one row r by one warp (c/gmoe.h:168-208): sigmoid
+// (numpy-stable), +bias for selection, stable top-k with lower-index ties,
+// weights from the unbiased scores normalised with the numpy pairwise sum and
+// scaled.  Writes row_expert / row_weight (ascending experts) and row_sel (top-k
+// order) at row r; sc is the row's score scratch; flag[e] = 1 for each
+// selection when flag is given.
+APUS_DEV void route_row(const MoeDev &m, int r, const float *logits_row, const int32_t *forced_row, float *sc,
+                        int *flag) {
     const int E = m.E, K = m.topk;
-    for (int e = threadIdx.x; e <= E; e += blockDim.x) flag[e] = 0;
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31;
     constexpr int EPL = MOE_MAX_E / 32;       // experts per lane: e = lane + 32u
-    if (warp < R) {      // one warp per row
-        const int r = warp;
+    {
         float lg[EPL], bs[EPL];
 #pragma unroll
         for (int u = 0; u < EPL; u++) {       // every load first
             const int e = lane + 32 * u;
-            lg[u] = e < E ? logits[(size_t)r * E + e] : 0.f;
+            lg[u] = e < E ? logits_row[e] : 0.f;
             bs[u] = e < E ? m.gate_bias[e] : 0.f;
         }
         // selection key of the biased score: larger value first, lower index
@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float 
         for (int u = 0; u < EPL; u++) {
             const int e = lane + 32 * u;
             const float s = sigmoid_np(lg[u]);
-            if (e < E) sc[r][e] = s;
+            if (e < E) sc[e] = s;
             key[u] = e < E ? argmax_key(s + bs[u], (uint32_t)e) : 0ull;
         }
         __syncwarp();
@@ -80,13 +80,13 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float 
 #pragma unroll
             for (int u = 0; u < EPL; u++)     // the winner leaves the pool
                 if (lane + 32 * u == idx) key[u] = 0ull;
-            const int pick = forced ? forced[r * K + j] : idx;
+            const int pick = forced_row ? forced_row[j] : idx;
             if (lane == j) my_sel = pick;
         }
         __syncwarp();
         // weights from the unbiased scores, normalised with the numpy
         // pairwise sum in selection order (c/gmoe.h:191-208)
-        float w = lane < K ? sc[r][my_sel] : 0.f;
+        float w = lane < K ? sc[my_sel] : 0.f;
         float wa[MOE_MAX_TOPK];
 #pragma unroll
         for (int j = 0; j < MOE_MAX_TOPK; j++) wa[j] = __shfl_sync(0xffffffffu, w, j);
@@ -104,9 +104,22 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float 
             m.row_weight[r * K + rank] = w;
             // unsorted selection, for inspection (c/gmoe.h:112-117 router_idx)
             m.row_sel[r * K + lane] = my_sel;
-            flag[my_sel] = 1;
+            if (flag) flag[my_sel] = 1;
         }
     }
+}
+
+__global__ void __launch_bounds__(256) k_moe_route(MoeDev m, int R, const float *logits, const int32_t *forced) {
+    pdl_launch_dependents();
+    __shared__ float sc[MOE_MAX_R][MOE_MAX_E];
+    __shared__ int flag[MOE_MAX_E + 1];
+    __shared__ int slot_of[MOE_MAX_E + 1];
+    const int E = m.E, K = m.topk;
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) flag[e] = 0;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5;
+    if (warp < R)        // one warp per row
+        route_row(m, warp, logits + (size_t)warp * E, forced ? forced + warp * K : nullptr, sc[warp], flag);
     __syncthreads();
     // work list: the flagged experts in ascending order (slot_of[e] = flagged
     // experts before e), by a ballot + popc scan over blocks of blockDim experts
@@ -193,6 +206,106 @@ __global__ void k_moe_combine(MoeDev m, int R, uint16_t *out, long ldo) {
         const uint16_t shb = (uint16_t)((e & 1) ? sw[e >> 1] >> 16 : sw[e >> 1] & 0xffffu);
         // a dense MLP (no routed experts) passes its output through unchanged
         const uint16_t v = K ? bf16_bits(y + bf16_f32(shb)) : shb;
+        if (e & 1) o[e >> 1] |= (uint32_t)v << 16;
+        else o[e >> 1] = v;
+    }
+    *(uint4 *)(out + (size_t)r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ---- the prompt pass: many rows a call (one GPU) ---------------------------
+
+__global__ void __launch_bounds__(256) k_moe_route_rows(MoeDev m, MoeRows w, int R, const float *logits) {
+    __shared__ float sc[MOE_MAX_R][MOE_MAX_E];
+    const int warp = threadIdx.x >> 5, r = blockIdx.x * MOE_MAX_R + warp;
+    if (r >= R) return;        // whole warps; no block barrier follows
+    m.row_expert = w.row_expert;
+    m.row_weight = w.row_weight;
+    m.row_sel = w.row_sel;
+    route_row(m, r, logits + (size_t)r * m.E, nullptr, sc[warp], nullptr);
+}
+
+// Problem lists: expert e's rows in ascending row order, 8 a problem, experts
+// ascending; then the shared expert (local slot shared_id) over every row, 8
+// a problem.  Thread e scans the selections for its own expert.
+__global__ void __launch_bounds__(1024) k_moe_lists(MoeRows w, int R, int K, int E, int shared_id) {
+    extern __shared__ int rex[];             // [R*K]
+    __shared__ int cnt[MOE_MAX_E], pbase[MOE_MAX_E + 1];
+    const int n = R * K, tid = threadIdx.x;
+    for (int i = tid; i < n; i += blockDim.x) rex[i] = w.row_expert[i];
+    for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) atomicAdd(&cnt[rex[i]], 1);
+    __syncthreads();
+    if (tid == 0) {
+        int p = 0;
+        for (int e = 0; e < E; e++) { pbase[e] = p; p += (cnt[e] + 7) / 8; }
+        pbase[E] = p;
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += blockDim.x) {
+        const int pb = pbase[e], np = pbase[e + 1] - pb;
+        for (int q = 0; q < np; q++) {
+            w.prob_expert[pb + q] = e;
+            for (int s = 0; s < 8; s++) w.prob_rows[(pb + q) * 8 + s] = -1;
+        }
+        int c = 0;
+        for (int i = 0; i < n; i++)
+            if (rex[i] == e) {
+                const int slot = pb * 8 + c++;
+                w.prob_rows[slot] = i / K;
+                w.pair_slot[i] = slot;
+            }
+    }
+    const int p0 = pbase[E], ns = (R + 7) / 8;
+    for (int q = tid; q < ns * 8; q += blockDim.x) {
+        const int p = p0 + q / 8;
+        if (q % 8 == 0) w.prob_expert[p] = shared_id;
+        w.prob_rows[q + p0 * 8] = q < R ? q : -1;
+        if (q < R) w.shared_slot[q] = p0 * 8 + q;
+    }
+    if (tid == 0) *w.prob_count = p0 + ns;
+}
+
+// xg[slot] = x[prob_rows[slot]] (zeros for padding), one CTA per problem row.
+__global__ void k_moe_gather(const uint16_t *x, long ldx, MoeRows w, int d) {
+    const int slot = blockIdx.x;
+    if (slot / 8 >= *w.prob_count) return;
+    const int t = w.prob_rows[slot];
+    for (int c = threadIdx.x; c < d / 8; c += blockDim.x) {
+        const uint4 v = t >= 0 ? *(const uint4 *)(x + (size_t)t * ldx + c * 8) : make_uint4(0, 0, 0, 0);
+        *(uint4 *)(w.xg + (size_t)slot * d + c * 8) = v;
+    }
+}
+
+// The ordered combine of k_moe_combine over the gathered outputs.
+__global__ void k_moe_combine_rows(MoeRows w, int R, int K, int d, uint16_t *out, long ldo) {
+    const int nc = d / 8;
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * nc) return;
+    const int r = (int)(i / nc), c = (int)(i % nc) * 8;
+    uint4 ev[MOE_MAX_TOPK + 1];
+    float wt[MOE_MAX_TOPK];
+#pragma unroll
+    for (int j = 0; j < MOE_MAX_TOPK; j++)
+        if (j < K) {
+            ev[j] = *(const uint4 *)(w.yd + (size_t)w.pair_slot[r * K + j] * d + c);
+            wt[j] = w.row_weight[r * K + j];
+        }
+    ev[MOE_MAX_TOPK] = *(const uint4 *)(w.yd + (size_t)w.shared_slot[r] * d + c);
+    const uint32_t sw[4] = {ev[MOE_MAX_TOPK].x, ev[MOE_MAX_TOPK].y, ev[MOE_MAX_TOPK].z, ev[MOE_MAX_TOPK].w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        float y = 0.f;
+#pragma unroll
+        for (int j = 0; j < MOE_MAX_TOPK; j++) {
+            if (j >= K) break;
+            const uint32_t wd = (e >> 1) == 0 ? ev[j].x : (e >> 1) == 1 ? ev[j].y : (e >> 1) == 2 ? ev[j].z : ev[j].w;
+            const float ex = (e & 1) ? bf16hi(wd) : bf16lo(wd);
+            y = bf16_round(y + bf16_round(ex * wt[j]));
+        }
+        const uint16_t shb = (uint16_t)((e & 1) ? sw[e >> 1] >> 16 : sw[e >> 1] & 0xffffu);
+        const uint16_t v = bf16_bits(y + bf16_f32(shb));
         if (e & 1) o[e >> 1] |= (uint32_t)v << 16;
         else o[e >> 1] = v;
     }
@@ -444,4 +557,46 @@ int ep_error_read_and_clear(void) {
 size_t ep_region_bytes(int dim) {
     const size_t contrib = (size_t)2 * MOE_MAX_R * MOE_MAX_TOPK * dim * 2;
     return contrib + 2 * MOE_MAX_R * 8 + EP_MAX_RANKS * 4 + 256;
+}
+
+// The MoE sublayer over R prompt rows (one GPU): router logits of every row
+// on the tensor cores, each row's selection (the decode path's route_row),
+// the problem lists, the rows gathered, the grouped FP8 GEMVs of the decode
+// path over 8-row problems (so a (row, expert) output is the decode path's
+// bit for bit), the ordered combine.
+int moe_rows_launch(const MoeDev &m, const MoeRows &w, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
+                    cudaStream_t st) {
+    if (m.E < 1 || m.ep.world > 1 || R < 1 || R > w.W || m.dim % 8 || ldx % 8 || ldo % 8 || m.topk > MOE_MAX_TOPK)
+        return -1;
+    const int d = m.dim, K = m.topk;
+    if (gemm_tc_launch(x, ldx, m.gate_w, d, nullptr, 0, w.logits, m.E, R, m.E, d, st)) return -1;
+    k_moe_route_rows<<<(R + MOE_MAX_R - 1) / MOE_MAX_R, 256, 0, st>>>(m, w, R, w.logits);
+    k_moe_lists<<<1, 1024, (size_t)R * K * sizeof(int), st>>>(w, R, K, m.E, m.eloc);
+    k_moe_gather<<<w.pmax * 8, 128, 0, st>>>(x, ldx, w, d);
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    GemvDesc gu{};
+    gu.W = m.gu_codes; gu.WS = m.gu_scales; gu.nkb = (d + 127) / 128;
+    gu.x = w.xg; gu.ldx = d; gu.R = 8; gu.O = 2L * m.inter; gu.K = d; gu.fp8 = 1;
+    gu.y = w.gu; gu.ldy = 2L * m.inter;
+    gu.gexpert = w.prob_expert; gu.gcount = w.prob_count; gu.gmax = w.pmax; gu.gnum = m.eloc + 1;
+    gu.w_estride = 2L * m.inter * d;
+    gu.s_estride = (2L * m.inter / 128) * ((d + 127) / 128);
+    gu.x_pstride = 8L * d;
+    gu.y_pstride = 8L * 2 * m.inter;
+    if (gemv_launch(gu, st)) return -1;
+    GemvDesc dn{};
+    dn.W = m.d_codes; dn.WS = m.d_scales; dn.nkb = (m.inter + 127) / 128;
+    dn.x = w.gu; dn.ldx = 2L * m.inter; dn.R = 8; dn.O = d; dn.K = m.inter; dn.fp8 = 1;
+    dn.y = w.yd; dn.ldy = d;
+    dn.gexpert = w.prob_expert; dn.gcount = w.prob_count; dn.gmax = w.pmax; dn.gnum = m.eloc + 1;
+    dn.w_estride = (long)d * m.inter;
+    dn.s_estride = ((d + 127) / 128) * ((m.inter + 127) / 128);
+    dn.x_pstride = 8L * 2 * m.inter;
+    dn.y_pstride = 8L * d;
+    dn.x_swiglu = 1;
+    dn.swiglu_limit = m.limit;
+    if (gemv_launch(dn, st)) return -1;
+    const long n = (long)R * (d / 8);
+    k_moe_combine_rows<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(w, R, K, d, out, ldo);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

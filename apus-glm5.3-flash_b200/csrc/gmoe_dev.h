@@ -53,6 +53,28 @@ struct MoeDev {
     uint16_t *yd;                // [max_r*topk+1][max_r][dim]
 };
 
+// Buffers of the prompt pass's MoE over up to W rows (one GPU): every row
+// routed at once, then each active expert's rows gathered into problems of 8
+// rows, so an expert's weights stream once per 8 of its rows instead of once
+// per 8 prompt rows.  pmax = W*topk/8 + E + W/8 + 1 problems.
+struct MoeRows {
+    int W, pmax;
+    float *logits;          // [W][E] router logits (fp32)
+    int32_t *row_expert;    // [W][topk] selections, ascending
+    float *row_weight;      // [W][topk]
+    int32_t *row_sel;       // [W][topk] top-k order
+    int32_t *pair_slot;     // [W][topk] (problem*8 + row) of each selection's output
+    int32_t *shared_slot;   // [W] the shared expert's output slot of each row
+    int32_t *prob_rows;     // [pmax][8] source row of each problem row, -1: padding
+    int32_t *prob_expert;   // [pmax] local weight slot of each problem
+    int32_t *prob_count;    // [1]
+    uint16_t *xg;           // [pmax][8][dim] gathered rows
+    uint16_t *gu;           // [pmax][8][2*inter]
+    uint16_t *yd;           // [pmax][8][dim]
+};
+int moe_rows_launch(const MoeDev &m, const MoeRows &w, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
+                    cudaStream_t st);
+
 // x [R][ldx] BF16 device rows -> out [R][ldo] BF16.  forced: optional device
 // [R][topk] selections replacing the computed top-k (the reference's
 // teacher-forcing hook, c/gmoe.h:145-152).

@@ -296,8 +296,21 @@ APUS_DEV void hc_maps(const float *m, const float *scale, const float *base, int
 // The inverse RMS multiplies the summed dot products (the reference scales
 // the streams first, c/gmhc.h:241-251): equal up to fp32 rounding.
 #define HC_PM_CW 64
+// A grid with gridDim.y > 1 covers more rows, MAXR per y (the sublayer
+// output given as x rows): block y takes rows MAXR*y ...
 __global__ void __launch_bounds__(256) k_hc_postmix(HcPostMix a) {
     pdl_launch_dependents();
+    if (blockIdx.y) {
+        const size_t r0 = (size_t)blockIdx.y * MAXR;
+        if (a.x) a.x += r0 * a.d;
+        a.h4 += r0 * a.hc * a.d;
+        a.post += r0 * a.hc;
+        a.comb += r0 * a.hc * a.hc;
+        if (a.h4out) a.h4out += r0 * a.hc * a.d;
+        a.part += r0 * a.nchunk * (a.nmix + 1);
+        a.R -= (int)r0;
+    }
+    if (a.R > MAXR) a.R = MAXR;
     __shared__ float xs[MAXR][HC_PM_CW];
     __shared__ float hs[MAXR][8][HC_PM_CW];
     const int c = blockIdx.x, i0 = c * HC_PM_CW, d = a.d, hc = a.hc, R = a.R;
@@ -1202,6 +1215,18 @@ int hc_postmix_launch(const Dims &D, const uint16_t *x, const MoeDev *moe, const
     a.fn = fn_next; a.part = S.mix;
     a.d = D.d; a.hc = D.hc; a.nmix = (2 + D.hc) * D.hc; a.R = R; a.nchunk = hc_nchunk(D);
     k_hc_postmix<<<a.nchunk, 256, 0, st>>>(a);
+    return ok_launch();
+}
+
+int hc_postmix_rows_launch(const Dims &D, const uint16_t *x, const uint16_t *h4, int R, Scratch &S, uint16_t *h4out,
+                           const uint16_t *fn_next, cudaStream_t st) {
+    if (R < 1 || (h4out && !x)) return -1;
+    HcPostMix a{};
+    a.x = x;
+    a.h4 = h4; a.post = S.post; a.comb = S.comb; a.h4out = h4out;
+    a.fn = fn_next; a.part = S.mix;
+    a.d = D.d; a.hc = D.hc; a.nmix = (2 + D.hc) * D.hc; a.R = R; a.nchunk = hc_nchunk(D);
+    k_hc_postmix<<<dim3(a.nchunk, (R + MAXR - 1) / MAXR), 256, 0, st>>>(a);
     return ok_launch();
 }
 

@@ -253,6 +253,7 @@ struct ApusGcudaModel {
         KdaRows kda{};
         DsaRows dsa{};
         MlpRows mlp{};
+        MoeRows moe{};                        // one GPU: the MoE over all the chunk's rows
         uint16_t *eh = nullptr, *mx = nullptr, *mxn = nullptr, *oh = nullptr;   // MTP block rows
         uint16_t *wbuf = nullptr;             // one FP8 matrix dequantised to BF16
         int32_t *ids = nullptr;               // [cap] prompt ids
@@ -1045,6 +1046,24 @@ static int ensure_wide(ApusGcudaModel *m) {
         X.mxn = (uint16_t *)A((size_t)W * d * 2);
         X.oh = (uint16_t *)A((size_t)W * d * 2);
     }
+    if (m->ep_world == 1 && D.E > 0) {
+        MoeRows &w = X.moe;
+        const int K = D.ktop, P = W * K / 8 + D.E + W / 8 + 1;
+        w.W = W;
+        w.pmax = P;
+        w.logits = (float *)A((size_t)W * D.E * 4);
+        w.row_expert = (int32_t *)A((size_t)W * K * 4);
+        w.row_weight = (float *)A((size_t)W * K * 4);
+        w.row_sel = (int32_t *)A((size_t)W * K * 4);
+        w.pair_slot = (int32_t *)A((size_t)W * K * 4);
+        w.shared_slot = (int32_t *)A((size_t)W * 4);
+        w.prob_rows = (int32_t *)A((size_t)P * 8 * 4);
+        w.prob_expert = (int32_t *)A((size_t)P * 4);
+        w.prob_count = (int32_t *)A(4);
+        w.xg = (uint16_t *)A((size_t)P * 8 * d * 2);
+        w.gu = (uint16_t *)A((size_t)P * 8 * 2 * D.inter * 2);
+        w.yd = (uint16_t *)A((size_t)P * 8 * d * 2);
+    }
     if (!ok) { gcuda_set_error("gmodel: prompt-pass buffers: device allocation failed"); return -1; }
     {
         uint8_t *p = arena;
@@ -1094,10 +1113,11 @@ static Scratch wide_view(ApusGcudaModel *m, int r0) {
 }
 
 // The main model over prompt rows ids_dev[0..R) at positions p0.. (the layer
-// loop of c/gmodel.h:1439-1626 with decode = 0): mHC maps, norms and the MoE
-// per 8-row group, the KDA / DSA / dense-MLP sublayers over all R rows.  The
-// KDA state is read from and left in checkpoint slot `slot`.  yn_out [R][d]
-// gets the post-final-norm rows.
+// loop of c/gmodel.h:1439-1626 with decode = 0), every sublayer over all R
+// rows (the MoE gathers each expert's rows; with expert parallelism the MoE
+// and its expand go 8 rows a call, through the ranks' exchange).  The KDA
+// state is read from and left in checkpoint slot `slot`.  yn_out [R][d] gets
+// the post-final-norm rows.
 static int main_rows(ApusGcudaModel *m, const int32_t *ids_dev, int p0, int R, int slot, uint16_t *yn_out) {
     const Dims &D = m->D;
     auto &X = m->wide;
@@ -1108,13 +1128,8 @@ static int main_rows(ApusGcudaModel *m, const int32_t *ids_dev, int p0, int R, i
     m->ctl_epoch++;
     if (k_embed_launch(m->embed, ids_dev, R, D.d, D.hc, X.h4, st)) return -1;
     uint16_t *h = X.h4, *h2 = X.h4b;
-    for (int r0 = 0; r0 < R; r0 += MAXR) {
-        Scratch v = wide_view(m, r0);
-        if (hc_postmix_launch(D, nullptr, nullptr, h + r0 * hcd, std::min(MAXR, R - r0), v, nullptr,
-                              m->L[0].hc_fn[0], st))
-            return -1;
-    }
     Scratch v0 = wide_view(m, 0);
+    if (hc_postmix_rows_launch(D, nullptr, h, R, v0, nullptr, m->L[0].hc_fn[0], st)) return -1;
     for (int l = 0; l < D.L; l++) {
         LayerW &W = m->L[l];
         if (hc_pre_launch(D, W, 0, h, R, v0, st)) return -1;
@@ -1126,30 +1141,24 @@ static int main_rows(ApusGcudaModel *m, const int32_t *ids_dev, int p0, int R, i
         } else if (dsa_rows_launch(D, W.dsa, m->dsa[l], X.pos, p0, R, X.dsa, m->S, X.wbuf, X.x, X.sub, st)) {
             return -1;
         }
-        for (int r0 = 0; r0 < R; r0 += MAXR) {
-            Scratch v = wide_view(m, r0);
-            if (hc_postmix_launch(D, X.sub + (size_t)r0 * D.d, nullptr, h + r0 * hcd, std::min(MAXR, R - r0), v,
-                                  h2 + r0 * hcd, W.hc_fn[1], st))
-                return -1;
-        }
+        if (hc_postmix_rows_launch(D, X.sub, h, R, v0, h2, W.hc_fn[1], st)) return -1;
         std::swap(h, h2);
         if (hc_pre_launch(D, W, 1, h, R, v0, st)) return -1;
         const uint16_t *fn_next = l + 1 < D.L ? m->L[l + 1].hc_fn[0] : nullptr;
         if (!W.sparse && mlp_rows_launch(W.moe, R, X.mlp, X.wbuf, X.x, X.sub, st)) return -1;
+        if (!W.sparse || !ep) {
+            if (W.sparse && moe_rows_launch(W.moe, X.moe, X.x, D.d, R, X.sub, D.d, st)) return -1;
+            if (hc_postmix_rows_launch(D, X.sub, h, R, v0, h2, fn_next, st)) return -1;
+            std::swap(h, h2);
+            continue;
+        }
+        // expert parallelism: the MoE 8 rows a call, its outputs exchanged between the ranks
         for (int r0 = 0; r0 < R; r0 += MAXR) {
             const int r = std::min(MAXR, R - r0);
             Scratch v = wide_view(m, r0);
             uint16_t *sub = X.sub + (size_t)r0 * D.d;
-            if (W.sparse) {
-                // one GPU: the combine of the expert outputs happens inside the expand
-                if (moe_forward_launch(W.moe, X.x + (size_t)r0 * D.d, D.d, r, ep ? sub : nullptr, D.d, nullptr, st))
-                    return -1;
-                if (hc_postmix_launch(D, ep ? sub : nullptr, ep ? nullptr : &W.moe, h + r0 * hcd, r, v, h2 + r0 * hcd,
-                                      fn_next, st))
-                    return -1;
-            } else if (hc_postmix_launch(D, sub, nullptr, h + r0 * hcd, r, v, h2 + r0 * hcd, fn_next, st)) {
-                return -1;
-            }
+            if (moe_forward_launch(W.moe, X.x + (size_t)r0 * D.d, D.d, r, sub, D.d, nullptr, st)) return -1;
+            if (hc_postmix_launch(D, sub, nullptr, h + r0 * hcd, r, v, h2 + r0 * hcd, fn_next, st)) return -1;
         }
         std::swap(h, h2);
     }
@@ -1178,10 +1187,14 @@ static int mtp_rows(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t *p
         NormSeg sg = {X.mx, d, nullptr, X.sub, d, W.post_norm, d, X.mxn, d};
         if (norm_seg_launch(&sg, 1, R, D.eps, nullptr, st)) return -1;
     }
-    for (int r0 = 0; r0 < R; r0 += MAXR)
-        if (moe_forward_launch(W.moe, X.mxn + (size_t)r0 * d, d, std::min(MAXR, R - r0), X.sub + (size_t)r0 * d, d,
-                               nullptr, st))
-            return -1;
+    if (m->ep_world == 1) {
+        if (moe_rows_launch(W.moe, X.moe, X.mxn, d, R, X.sub, d, st)) return -1;
+    } else {
+        for (int r0 = 0; r0 < R; r0 += MAXR)
+            if (moe_forward_launch(W.moe, X.mxn + (size_t)r0 * d, d, std::min(MAXR, R - r0), X.sub + (size_t)r0 * d,
+                                   d, nullptr, st))
+                return -1;
+    }
     {   // x = bf16(x + moe); shared_head.norm
         NormSeg sg = {X.mx, d, nullptr, X.sub, d, m->shared_norm, d, X.oh, d};
         return norm_seg_launch(&sg, 1, R, D.eps, nullptr, st);

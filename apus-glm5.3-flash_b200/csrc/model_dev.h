@@ -169,6 +169,10 @@ struct HcPostMix {
 int hc_nchunk(const Dims &D);
 int hc_postmix_launch(const Dims &D, const uint16_t *x, const MoeDev *moe, const uint16_t *h4, int R, Scratch &S,
                       uint16_t *h4out, const uint16_t *fn_next, cudaStream_t st);
+// The same over R rows of any count (MAXR rows a block row), the sublayer
+// output always given as x rows.
+int hc_postmix_rows_launch(const Dims &D, const uint16_t *x, const uint16_t *h4, int R, Scratch &S, uint16_t *h4out,
+                           const uint16_t *fn_next, cudaStream_t st);
 int head_norm_launch(const Dims &D, const uint16_t *h4, const uint16_t *norm_w, int R, uint16_t *yn,
                      unsigned long long *keys, cudaStream_t st);     // keys: zeroed for the lm_head argmax
 int rmsnorm_rows_launch(const uint16_t *x, long ldx, const uint16_t *w, int n, int R, float eps,
