@@ -231,11 +231,39 @@ def bench_c0(args, ws, rank):
     return out
 
 
+def _graph_us(torch, st, body, n_calls, replays=5):
+    """Device time of one call of `body` (n_calls calls on stream st), the
+    calls captured into a CUDA graph and replayed (as the engine runs its
+    kernels: no host launch cost between them), CUDA events on st."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        body()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        g.replay()
+        e0.record(st)
+        for _ in range(replays):
+            g.replay()
+        e1.record(st)
+    st.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (replays * n_calls)
+    del g
+    return us
+
+
 def fp8_gemv_leg(reps=200, warmup=10):
-    """The metric's second half, FP8 GEMV % of HBM peak, on BASELINE config
-    0 (M=4 rows, 4096x4096 E4M3 with 128x128 block scales): back-to-back
-    launches over 16 rotating weight copies (270 MB > L2, so every launch
-    streams its weights from HBM), CUDA events on the launching stream."""
+    """The metric's second half, FP8 GEMV % of HBM peak.
+      * BASELINE config 0 (M=4 rows, 4096x4096 E4M3 with 128x128 block
+        scales): `reps` back-to-back programmatic launches over 16 rotating
+        weight copies (270 MB > L2, so every launch streams its weights from
+        HBM), captured in a CUDA graph and replayed, CUDA events on the
+        launching stream.  A 16.8 MB launch is bounded by its fixed latency
+        (launch, tensor-map fetch, first copy) as much as by the bandwidth.
+      * the shape the decode step streams most FP8 bytes through: one MoE
+        layer call of BASELINE config 1 (4 rows, 288 experts top-8 + shared,
+        inter 1024), the router and grouped expert GEMVs over the realised
+        union (~30 experts, ~400 MB), over 16 rotating input batches, graph
+        replayed; algorithmic bytes = the union's expert bytes + router."""
     import numpy as np
     import torch
     import apus_gcuda as G
@@ -256,24 +284,43 @@ def fp8_gemv_leg(reps=200, warmup=10):
     for i in range(warmup):
         step(i)
     st.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for i in range(reps):
-        step(i)
-    e1.record(st)
-    st.synchronize()
+    us = _graph_us(torch, st, lambda: [step(i) for i in range(reps)], reps)
     G.apus_gcuda_set_pdl(0)
-    us = e0.elapsed_time(e1) * 1e3 / reps
     hbm, _, src = peaks()
     algo = c0_algo_bytes()
     gbs = algo / us / 1e3
     del dW
     torch.cuda.empty_cache()
-    return {"workload": "config0: FP8 128x128 block-dequant GEMV, M=4, N=K=4096", "kernel": "k_gemv_tma<true>",
-            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(gbs / hbm, 4), "peak_source": src, "algo_bytes_per_launch": algo,
-                         "avg_launch_us": round(us, 3), "launches": reps,
-                         "l2": "16 rotating weight copies (270 MB > L2)"}}
+    out = {"workload": "config0: FP8 128x128 block-dequant GEMV, M=4, N=K=4096", "kernel": "k_gemv_tma<true>",
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(gbs / hbm, 4), "peak_source": src, "algo_bytes_per_launch": algo,
+                        "avg_launch_us": round(us, 3), "launches": reps,
+                        "timing": "graph-replayed back-to-back launches, CUDA events",
+                        "l2": "16 rotating weight copies (270 MB > L2)"}}
+    # one MoE layer (config 1): the grouped FP8 GEMVs at the step's shapes
+    R, d = C1["R"], C1["dim"]
+    h = G.apus_gcuda_moe_new(C1["E"], C1["topk"], d, C1["inter"], 2.5, 10.0, R)
+    assert h, G.apus_gcuda_last_error()
+    G.check(G.apus_gcuda_moe_init_random(h, 1), "init")
+    xs = c1_inputs(1)
+    mx = torch.from_numpy(xs.view(np.int16)).cuda()
+    my = torch.empty((R, d), dtype=torch.int16, device="cuda")
+    algo1 = []
+    for i in range(C1["nx"]):
+        G.check(G.apus_gcuda_moe_forward_dev(h, G.ptr(mx[i]), R, G.ptr(my), None, sp), "moe")
+        st.synchronize()
+        algo1.append(G.apus_gcuda_moe_last_bytes(h) + R * d * 4)
+    n1 = C1["nx"] * 4
+    us1 = _graph_us(torch, st, lambda: [G.check(G.apus_gcuda_moe_forward_dev(
+        h, G.ptr(mx[i % C1["nx"]]), R, G.ptr(my), None, sp), "moe") for i in range(n1)], n1)
+    G.apus_gcuda_moe_free(h)
+    a1 = float(np.mean(algo1))
+    out["moe_layer"] = {"workload": "config1: one MoE layer call, 4 rows, 288 experts top-8 + shared, inter 1024",
+                        "kernels": "router GEMV + k_moe_route + grouped k_gemv_tma<true> gate|up and down + combine",
+                        "achieved": round(a1 / us1 / 1e3, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(a1 / us1 / 1e3 / hbm, 4), "us_per_call": round(us1, 2),
+                        "algo_bytes_per_call": round(a1), "timing": "graph-replayed calls, CUDA events"}
+    return out
 
 
 _HOLD = {}
