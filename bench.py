@@ -1055,6 +1055,37 @@ def gemv_table(only="all", rows=(8, 4, 1), reps=50):
         torch.cuda.empty_cache()
 
 
+def prefill_table(reps=3):
+    """The prompt pass of config 2 (512 prompt tokens, the MTP replay
+    included: apus_gcuda_gspec_prefill) timed with CUDA events after one
+    untimed call, `reps` calls (profiling aid, --prefill-table).  Prints one
+    JSON line."""
+    import numpy as np
+    import torch
+    import apus_gcuda as G
+    G.enable()
+    kw = c2_config()
+    W = c2_weights(kw, C2["seed"])
+    prompt = c2_prompt(kw, C2["seed"])[:C2["prompt"]]
+    m = G.GModel(G.make_config(**kw), has_mtp=True, kv_cap=len(prompt) + 64, depth=C2["depth"])
+    m.load(W)
+    m.spec_prefill(prompt)
+    st = torch.cuda.ExternalStream(m.stream())
+    ms = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("prefill")
+        e0.record(st)
+        m.spec_prefill(prompt)
+        e1.record(st)
+        st.synchronize()
+        torch.cuda.nvtx.range_pop()
+        ms.append(e0.elapsed_time(e1))
+    m.close()
+    print(json.dumps({"workload": "config2 prompt pass: apus_gcuda_gspec_prefill, 512 tokens", "calls": reps,
+                      "ms": [round(x, 2) for x in ms], "ms_min": round(min(ms), 2)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1077,6 +1108,8 @@ def main():
     ap.add_argument("--tc-table", nargs="*", type=int, default=None,
                     help="prefill-chunk linears on the tcgen05 GEMM vs cuBLAS (profiling aid, one GPU); "
                          "optionally the row counts (default 512 2048)")
+    ap.add_argument("--prefill-table", action="store_true",
+                    help="config 2's 512-token prompt pass timed alone (profiling aid, one GPU)")
     ap.add_argument("--temp", type=float, default=0.0,
                     help="config 2: sampled decode at this temperature (default 0: greedy, the headline)")
     ap.add_argument("--top-p", type=float, default=0.95, help="config 2 sampled decode: nucleus top_p")
@@ -1131,6 +1164,9 @@ def main():
         return
     if args.tc_table is not None:
         tc_table(tuple(args.tc_table) or (512, 2048))
+        return
+    if args.prefill_table:
+        prefill_table()
         return
     if args.config == 3:
         out = bench_c3(args, ws, rank)
