@@ -323,12 +323,16 @@ __global__ void k_moe_combine_rows(MoeRows w, int R, int K, int d, uint16_t *out
 // Thread 0 of a CTA: signal (CTA 0 only) and wait for every rank's epoch-e
 // signal.  Each wait is bounded (about a second of clock cycles) and records
 // an error instead of hanging.
+// The signal is the release pattern of the PTX memory model (one fence at
+// system scope, then relaxed flag stores to every peer) and the wait its
+// acquire pattern (relaxed polls, then one fence), so the fence cost is paid
+// once per exchange rather than once per peer.
 APUS_DEV void ep_signal_wait(const EpCtx &ep, int e, bool signal) {
     if (signal) {
         asm volatile("fence.acq_rel.sys;" ::: "memory");
         for (int p = 0; p < ep.world; p++) {
             int *pf = (int *)(ep.peer[p] + ep.off_flags) + ep.rank;
-            asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(pf), "r"(e) : "memory");
+            asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(pf), "r"(e) : "memory");
         }
     }
     const int *mine = (const int *)(ep.peer[ep.rank] + ep.off_flags);
@@ -336,7 +340,7 @@ APUS_DEV void ep_signal_wait(const EpCtx &ep, int e, bool signal) {
     for (int p = 0; p < ep.world; p++) {
         int v = 0;
         while (true) {
-            asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine + p) : "memory");
+            asm volatile("ld.relaxed.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine + p) : "memory");
             if (v >= e) break;
             if (clock64() - t0 > (1ll << 31)) {
                 atomicExch(&g_apus_ep_err, 5);
@@ -344,6 +348,7 @@ APUS_DEV void ep_signal_wait(const EpCtx &ep, int e, bool signal) {
             }
         }
     }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 // Every CTA reads the epoch before it arrives; the last CTA to arrive (all
