@@ -640,7 +640,31 @@ __global__ void __launch_bounds__(D) k_kda_rec(const uint16_t *qkvc, const uint1
                                                float qscale, uint16_t *core_out) {
     pdl_launch_dependents();
     const int h = blockIdx.x, j = threadIdx.x, qkv = H * D;
-    __shared__ float qf[D], kf[D], dec[D], sq[D], red[2];
+    __shared__ float qf[D], kf[D], dec[D], sq[D], red[2], beta_sh[MAXR];
+    // every row's inputs of this thread's element j ([row][j]: q, k, v, forget
+    // and output gates), loaded before the token chain so that the chain
+    // waits on one memory round trip rather than several per token
+    __shared__ uint16_t in_sh[5][MAXR][D];
+    {
+        uint16_t r5[5][MAXR];
+#pragma unroll
+        for (int t = 0; t < MAXR; t++)
+            if (t < R) {
+                const uint16_t *q = qkvc + (size_t)t * 3 * qkv + (size_t)h * D;
+                r5[0][t] = q[j];
+                r5[1][t] = q[qkv + j];
+                r5[2][t] = q[2 * qkv + j];
+                r5[3][t] = fgo[(size_t)t * qkv + (size_t)h * D + j];
+                r5[4][t] = fgo[fg_pstride + (size_t)t * qkv + (size_t)h * D + j];
+            }
+#pragma unroll
+        for (int t = 0; t < MAXR; t++)
+            if (t < R)
+#pragma unroll
+                for (int c = 0; c < 5; c++) in_sh[c][t][j] = r5[c][t];
+    }
+    if (j < R) beta_sh[j] = bf16_round(sigmoid_np(bf16_f32(kp[(size_t)j * ldkp + beta_off + h])));
+    const float dtb = dt_bias[(size_t)h * D + j], onw = bf16_f32(o_norm[j]);
     float S[D];
     const int cur = ctl->kda_cur;
     const size_t hs = (size_t)D * D;
@@ -649,10 +673,9 @@ __global__ void __launch_bounds__(D) k_kda_rec(const uint16_t *qkvc, const uint1
     for (int i = 0; i < D; i++) S[i] = S0[(size_t)i * D + j];
     const float a = expf(A_log[h]);
     for (int t = 0; t < R; t++) {
-        const uint16_t *q = qkvc + (size_t)t * 3 * qkv + (size_t)h * D;
-        const uint16_t *k = q + qkv, *v = q + 2 * qkv;
         // l2norm q, k (c/gkda.h:263-273), pairwise sums of squares
-        const float qv = bf16_f32(q[j]), kv_ = bf16_f32(k[j]);
+        const float qv = bf16_f32(in_sh[0][t][j]), kv_ = bf16_f32(in_sh[1][t][j]), vj = bf16_f32(in_sh[2][t][j]);
+        const float fz = bf16_f32(in_sh[3][t][j]), gz = bf16_f32(in_sh[4][t][j]);
         sq[j] = qv * qv;
         __syncthreads();
         if (j == 0) red[0] = sqrtf(pw_sum_leaf(sq, D) + 1e-6f);
@@ -664,10 +687,9 @@ __global__ void __launch_bounds__(D) k_kda_rec(const uint16_t *qkvc, const uint1
         qf[j] = (qv / red[0]) * qscale;
         kf[j] = kv_ / red[1];
         // forget gate: g = lb * sigmoid(exp(A_log) * (fg + dt_bias)); decay exp(g)
-        const float z = bf16_f32(fgo[(size_t)t * qkv + (size_t)h * D + j]) + dt_bias[(size_t)h * D + j];
+        const float z = fz + dtb;
         dec[j] = expf(lower_bound * sigmoid_np(a * z));
-        const float beta = bf16_round(sigmoid_np(bf16_f32(kp[(size_t)t * ldkp + beta_off + h])));
-        const float vj = bf16_f32(v[j]);
+        const float beta = beta_sh[t];
         __syncthreads();
 #pragma unroll
         for (int i = 0; i < D; i++) S[i] = S[i] * dec[i];
@@ -692,8 +714,8 @@ __global__ void __launch_bounds__(D) k_kda_rec(const uint16_t *qkvc, const uint1
         if (j == 0) red[0] = 1.0f / sqrtf(pw_sum_leaf(sq, D) / (float)D + eps);
         __syncthreads();
         float y = core * red[0];
-        y = bf16_f32(o_norm[j]) * y;
-        y = y * sigmoid_np(bf16_f32(fgo[fg_pstride + (size_t)t * qkv + (size_t)h * D + j]));
+        y = onw * y;
+        y = y * sigmoid_np(gz);
         core_out[(size_t)t * qkv + (size_t)h * D + j] = bf16_bits(y);
         __syncthreads();
     }
