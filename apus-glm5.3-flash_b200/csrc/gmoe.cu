@@ -227,7 +227,8 @@ __global__ void __launch_bounds__(256) k_moe_route_rows(MoeDev m, MoeRows w, int
 // Problem lists: expert e's rows in ascending row order, 8 a problem, experts
 // ascending; then the shared expert (local slot shared_id) over every row, 8
 // a problem.  Thread e scans the selections for its own expert.
-__global__ void __launch_bounds__(1024) k_moe_lists(MoeRows w, int R, int K, int E, int shared_id) {
+__global__ void __launch_bounds__(1024) k_moe_lists(MoeRows w, int R, int K, int E, int e0, int eloc,
+                                                    int shared_id) {
     extern __shared__ int rex[];             // [R*K]
     __shared__ int cnt[MOE_MAX_E], pbase[MOE_MAX_E + 1];
     const int n = R * K, tid = threadIdx.x;
@@ -238,19 +239,24 @@ __global__ void __launch_bounds__(1024) k_moe_lists(MoeRows w, int R, int K, int
     __syncthreads();
     if (tid == 0) {
         int p = 0;
-        for (int e = 0; e < E; e++) { pbase[e] = p; p += (cnt[e] + 7) / 8; }
+        for (int e = 0; e < E; e++) {
+            pbase[e] = p;
+            if (e >= e0 && e < e0 + eloc) p += (cnt[e] + 7) / 8;     // this rank's experts only
+        }
         pbase[E] = p;
     }
     __syncthreads();
     for (int e = tid; e < E; e += blockDim.x) {
+        const bool mine = e >= e0 && e < e0 + eloc;
         const int pb = pbase[e], np = pbase[e + 1] - pb;
         for (int q = 0; q < np; q++) {
-            w.prob_expert[pb + q] = e;
+            w.prob_expert[pb + q] = e - e0;                        // local weight slot
             for (int s = 0; s < 8; s++) w.prob_rows[(pb + q) * 8 + s] = -1;
         }
         int c = 0;
         for (int i = 0; i < n; i++)
             if (rex[i] == e) {
+                if (!mine) { w.pair_slot[i] = -1; continue; }       // another rank's output
                 const int slot = pb * 8 + c++;
                 w.prob_rows[slot] = i / K;
                 w.pair_slot[i] = slot;
@@ -303,6 +309,81 @@ __global__ void k_moe_combine_rows(MoeRows w, int R, int K, int d, uint16_t *out
             const uint32_t wd = (e >> 1) == 0 ? ev[j].x : (e >> 1) == 1 ? ev[j].y : (e >> 1) == 2 ? ev[j].z : ev[j].w;
             const float ex = (e & 1) ? bf16hi(wd) : bf16lo(wd);
             y = bf16_round(y + bf16_round(ex * wt[j]));
+        }
+        const uint16_t shb = (uint16_t)((e & 1) ? sw[e >> 1] >> 16 : sw[e >> 1] & 0xffffu);
+        const uint16_t v = bf16_bits(y + bf16_f32(shb));
+        if (e & 1) o[e >> 1] |= (uint32_t)v << 16;
+        else o[e >> 1] = v;
+    }
+    *(uint4 *)(out + (size_t)r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Expert parallelism: this rank's weighted outputs bf16(bf16(y) * w) into its
+// region's half (epoch+1)&1 at [row][slot j] (the slot order of the row's
+// ascending expert list), one thread per (row, selection, 8 columns).
+__global__ void k_moe_scatter_rows(MoeRows w, EpCtx ep, int R, int K, int d) {
+    const int nc = d / 8;
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * K * nc) return;
+    const int pr = (int)(i / nc), c = (int)(i % nc) * 8;
+    const int slot = w.pair_slot[pr];
+    if (slot < 0) return;
+    const int r = pr / K, j = pr % K;
+    const int half = (*(volatile int *)ep.epoch + 1) & 1;
+    const float wt = w.row_weight[pr];
+    const uint4 v = *(const uint4 *)(w.yd + (size_t)slot * d + c);
+    const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const uint16_t lo = bf16_bits(bf16_round(bf16lo(in[e]) * wt)), hi = bf16_bits(bf16_round(bf16hi(in[e]) * wt));
+        o[e] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    uint16_t *dst = (uint16_t *)(ep.peer[ep.rank] + ep.off_wide) +
+                    ((((size_t)half * ep.wide_rows + r) * ep.wide_k + j) * d + c);
+    *(uint4 *)dst = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+APUS_DEV void ep_signal_wait(const EpCtx &ep, int e, bool signal);
+
+// One thread: signal every peer, wait for every peer's signal of the same
+// epoch (bounded), advance the epoch.  The combine that follows in the stream
+// reads the peers' regions.
+__global__ void k_ep_barrier(EpCtx ep) {
+    const int e = *(volatile int *)ep.epoch + 1;
+    ep_signal_wait(ep, e, true);
+    ep.epoch[0] = e;
+}
+
+// The ordered combine across ranks: per row, the slots in ascending expert
+// order from their owners' regions, y = bf16(y + contribution), then the
+// local shared expert.
+__global__ void k_moe_combine_ep_rows(MoeRows w, EpCtx ep, int R, int K, int d, int eloc, uint16_t *out, long ldo) {
+    const int nc = d / 8;
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * nc) return;
+    const int r = (int)(i / nc), c = (int)(i % nc) * 8;
+    const int half = *(volatile int *)ep.epoch & 1;
+    uint4 ev[MOE_MAX_TOPK];
+#pragma unroll
+    for (int j = 0; j < MOE_MAX_TOPK; j++)
+        if (j < K) {
+            const int owner = w.row_expert[r * K + j] / eloc;
+            const uint16_t *src = (const uint16_t *)(ep.peer[owner] + ep.off_wide) +
+                                  ((((size_t)half * ep.wide_rows + r) * ep.wide_k + j) * d + c);
+            ev[j] = __ldcv((const uint4 *)src);
+        }
+    const uint4 sh = *(const uint4 *)(w.yd + (size_t)w.shared_slot[r] * d + c);
+    const uint32_t sw[4] = {sh.x, sh.y, sh.z, sh.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        float y = 0.f;
+#pragma unroll
+        for (int j = 0; j < MOE_MAX_TOPK; j++) {
+            if (j >= K) break;
+            const uint32_t wd = (e >> 1) == 0 ? ev[j].x : (e >> 1) == 1 ? ev[j].y : (e >> 1) == 2 ? ev[j].z : ev[j].w;
+            y = bf16_round(y + ((e & 1) ? bf16hi(wd) : bf16lo(wd)));
         }
         const uint16_t shb = (uint16_t)((e & 1) ? sw[e >> 1] >> 16 : sw[e >> 1] & 0xffffu);
         const uint16_t v = bf16_bits(y + bf16_f32(shb));
@@ -559,6 +640,8 @@ int ep_error_read_and_clear(void) {
     return v;
 }
 
+size_t ep_wide_bytes(int rows, int topk, int dim) { return (size_t)2 * rows * topk * dim * 2; }
+
 size_t ep_region_bytes(int dim) {
     const size_t contrib = (size_t)2 * MOE_MAX_R * MOE_MAX_TOPK * dim * 2;
     return contrib + 2 * MOE_MAX_R * 8 + EP_MAX_RANKS * 4 + 256;
@@ -571,12 +654,14 @@ size_t ep_region_bytes(int dim) {
 // bit for bit), the ordered combine.
 int moe_rows_launch(const MoeDev &m, const MoeRows &w, const uint16_t *x, long ldx, int R, uint16_t *out, long ldo,
                     cudaStream_t st) {
-    if (m.E < 1 || m.ep.world > 1 || R < 1 || R > w.W || m.dim % 8 || ldx % 8 || ldo % 8 || m.topk > MOE_MAX_TOPK)
+    const bool ep = m.ep.world > 1;
+    if (m.E < 1 || R < 1 || R > w.W || m.dim % 8 || ldx % 8 || ldo % 8 || m.topk > MOE_MAX_TOPK) return -1;
+    if (ep && (!ep_connected(m.ep) || m.ep.wide_rows < R || m.ep.wide_k < m.topk || m.eloc * m.ep.world != m.E))
         return -1;
     const int d = m.dim, K = m.topk;
     if (gemm_tc_launch(x, ldx, m.gate_w, d, nullptr, 0, w.logits, m.E, R, m.E, d, st)) return -1;
     k_moe_route_rows<<<(R + MOE_MAX_R - 1) / MOE_MAX_R, 256, 0, st>>>(m, w, R, w.logits);
-    k_moe_lists<<<1, 1024, (size_t)R * K * sizeof(int), st>>>(w, R, K, m.E, m.eloc);
+    k_moe_lists<<<1, 1024, (size_t)R * K * sizeof(int), st>>>(w, R, K, m.E, m.e0, m.eloc, m.eloc);
     k_moe_gather<<<w.pmax * 8, 128, 0, st>>>(x, ldx, w, d);
     if (cudaGetLastError() != cudaSuccess) return -1;
     GemvDesc gu{};
@@ -602,6 +687,13 @@ int moe_rows_launch(const MoeDev &m, const MoeRows &w, const uint16_t *x, long l
     dn.swiglu_limit = m.limit;
     if (gemv_launch(dn, st)) return -1;
     const long n = (long)R * (d / 8);
+    if (ep) {
+        const long ns = (long)R * K * (d / 8);
+        k_moe_scatter_rows<<<(unsigned)((ns + 127) / 128), 128, 0, st>>>(w, m.ep, R, K, d);
+        k_ep_barrier<<<1, 1, 0, st>>>(m.ep);
+        k_moe_combine_ep_rows<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(w, m.ep, R, K, d, m.eloc, out, ldo);
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    }
     k_moe_combine_rows<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(w, R, K, d, out, ldo);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

@@ -21,6 +21,10 @@ struct EpCtx {
     uint8_t *peer[EP_MAX_RANKS];  // every rank's region (peer[rank] is this rank's)
     int *epoch;                   // this rank's exchange counter (device); epoch[1]: CTA arrivals
     long off_keys, off_flags;     // byte offsets inside a region
+    // the prompt pass's weighted expert outputs [2][wide_rows][wide_k][dim]
+    // BF16 (halves by epoch parity, as contrib), at off_wide
+    long off_wide;
+    int wide_rows, wide_k;
 };
 
 // All pointers are device memory.  Weights: see gmoe.cu for the packed layout.
@@ -53,10 +57,13 @@ struct MoeDev {
     uint16_t *yd;                // [max_r*topk+1][max_r][dim]
 };
 
-// Buffers of the prompt pass's MoE over up to W rows (one GPU): every row
-// routed at once, then each active expert's rows gathered into problems of 8
+// Buffers of the prompt pass's MoE over up to W rows: every row routed at
+// once, then each active (local) expert's rows gathered into problems of 8
 // rows, so an expert's weights stream once per 8 of its rows instead of once
-// per 8 prompt rows.  pmax = W*topk/8 + E + W/8 + 1 problems.
+// per 8 prompt rows.  pmax = W*topk/8 + E + W/8 + 1 problems.  With expert
+// parallelism each rank runs its own experts' problems (pair_slot -1 for
+// another rank's), writes the weighted outputs into its exchange region, and
+// the combine reads them from their owners after one barrier.
 struct MoeRows {
     int W, pmax;
     float *logits;          // [W][E] router logits (fp32)
@@ -93,3 +100,5 @@ int moe_combine_launch(const MoeDev &m, int R, uint16_t *out, long ldo, cudaStre
 int ep_picks_exchange_launch(const EpCtx &ep, const unsigned long long *keys, int R, int *picks,
                              cudaStream_t st, int n0 = -1, int *picks2 = nullptr);
 size_t ep_region_bytes(int dim);
+// bytes of the prompt pass's part of a region (rows x topk contributions, two halves)
+size_t ep_wide_bytes(int rows, int topk, int dim);

@@ -32,6 +32,12 @@
 #include "../../include/apus_gcuda.h"
 #include "../../include/apus_gmtp_gcuda.h"
 
+// Rows of one prompt chunk.  Every prompt row takes the same arithmetic
+// whatever the chunk size (the GEMM sums each row alike, the KDA chunks are
+// the prompt's 64-row chunks, the DSA rows attend to positions <= their own),
+// so this only trades memory for fewer weight passes.
+#define PROMPT_ROWS 256
+
 // ------------------------------------------------------------ device kernels
 namespace apus {
 
@@ -458,7 +464,12 @@ static ApusGcudaModel *model_create(const ApusGcudaConfig *cfg, int has_mtp, siz
     m->ep.world = world;
     if (world > 1) {   // this rank's exchange region (peers open it through IPC)
         const size_t contrib = (size_t)2 * MOE_MAX_R * MOE_MAX_TOPK * d * 2;
-        const size_t rb = ep_region_bytes(d);
+        const size_t rb0 = (ep_region_bytes(d) + 255) & ~(size_t)255;
+        const int wk = D.ktop > 0 ? D.ktop : 1;
+        const size_t rb = rb0 + ep_wide_bytes(PROMPT_ROWS, wk, d);   // + the prompt pass's outputs
+        m->ep.off_wide = (long)rb0;
+        m->ep.wide_rows = PROMPT_ROWS;
+        m->ep.wide_k = wk;
         m->ep_region = (uint8_t *)A(rb > (2u << 20) ? rb : (2u << 20));   // its own IPC-mappable allocation
         m->ep.peer[rank] = m->ep_region;
         m->ep.off_keys = (long)contrib;
@@ -993,11 +1004,6 @@ static int mtp_forward(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t
 
 // ---- the prompt pass (c/gmodel.h:1658-1666 apus_gmodel_prefill_h) --------
 
-// Rows of one prompt chunk.  Every prompt row takes the same arithmetic
-// whatever the chunk size (the GEMM sums each row alike, the KDA chunks are
-// the prompt's 64-row chunks, the DSA rows attend to positions <= their own),
-// so this only trades memory for fewer weight passes.
-#define PROMPT_ROWS 256
 
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 
@@ -1046,7 +1052,7 @@ static int ensure_wide(ApusGcudaModel *m) {
         X.mxn = (uint16_t *)A((size_t)W * d * 2);
         X.oh = (uint16_t *)A((size_t)W * d * 2);
     }
-    if (m->ep_world == 1 && D.E > 0) {
+    if (D.E > 0) {
         MoeRows &w = X.moe;
         const int K = D.ktop, P = W * K / 8 + D.E + W / 8 + 1;
         w.W = W;
@@ -1114,16 +1120,14 @@ static Scratch wide_view(ApusGcudaModel *m, int r0) {
 
 // The main model over prompt rows ids_dev[0..R) at positions p0.. (the layer
 // loop of c/gmodel.h:1439-1626 with decode = 0), every sublayer over all R
-// rows (the MoE gathers each expert's rows; with expert parallelism the MoE
-// and its expand go 8 rows a call, through the ranks' exchange).  The KDA
-// state is read from and left in checkpoint slot `slot`.  yn_out [R][d] gets
-// the post-final-norm rows.
+// rows (the MoE gathers each expert's rows; with expert parallelism each rank
+// runs its own experts and the outputs meet in one exchange a layer).  The
+// KDA state is read from and left in checkpoint slot `slot`.  yn_out [R][d]
+// gets the post-final-norm rows.
 static int main_rows(ApusGcudaModel *m, const int32_t *ids_dev, int p0, int R, int slot, uint16_t *yn_out) {
     const Dims &D = m->D;
     auto &X = m->wide;
     cudaStream_t st = m->st;
-    const size_t hcd = (size_t)D.hc * D.d;
-    const bool ep = m->ep_world > 1;
     m->n_main_fwd++;
     m->ctl_epoch++;
     if (k_embed_launch(m->embed, ids_dev, R, D.d, D.hc, X.h4, st)) return -1;
@@ -1146,20 +1150,8 @@ static int main_rows(ApusGcudaModel *m, const int32_t *ids_dev, int p0, int R, i
         if (hc_pre_launch(D, W, 1, h, R, v0, st)) return -1;
         const uint16_t *fn_next = l + 1 < D.L ? m->L[l + 1].hc_fn[0] : nullptr;
         if (!W.sparse && mlp_rows_launch(W.moe, R, X.mlp, X.wbuf, X.x, X.sub, st)) return -1;
-        if (!W.sparse || !ep) {
-            if (W.sparse && moe_rows_launch(W.moe, X.moe, X.x, D.d, R, X.sub, D.d, st)) return -1;
-            if (hc_postmix_rows_launch(D, X.sub, h, R, v0, h2, fn_next, st)) return -1;
-            std::swap(h, h2);
-            continue;
-        }
-        // expert parallelism: the MoE 8 rows a call, its outputs exchanged between the ranks
-        for (int r0 = 0; r0 < R; r0 += MAXR) {
-            const int r = std::min(MAXR, R - r0);
-            Scratch v = wide_view(m, r0);
-            uint16_t *sub = X.sub + (size_t)r0 * D.d;
-            if (moe_forward_launch(W.moe, X.x + (size_t)r0 * D.d, D.d, r, sub, D.d, nullptr, st)) return -1;
-            if (hc_postmix_launch(D, sub, nullptr, h + r0 * hcd, r, v, h2 + r0 * hcd, fn_next, st)) return -1;
-        }
+        if (W.sparse && moe_rows_launch(W.moe, X.moe, X.x, D.d, R, X.sub, D.d, st)) return -1;
+        if (hc_postmix_rows_launch(D, X.sub, h, R, v0, h2, fn_next, st)) return -1;
         std::swap(h, h2);
     }
     return head_norm_launch(D, h, m->norm, R, yn_out, nullptr, st);
@@ -1187,14 +1179,7 @@ static int mtp_rows(ApusGcudaModel *m, const int32_t *ids_dev, const uint16_t *p
         NormSeg sg = {X.mx, d, nullptr, X.sub, d, W.post_norm, d, X.mxn, d};
         if (norm_seg_launch(&sg, 1, R, D.eps, nullptr, st)) return -1;
     }
-    if (m->ep_world == 1) {
-        if (moe_rows_launch(W.moe, X.moe, X.mxn, d, R, X.sub, d, st)) return -1;
-    } else {
-        for (int r0 = 0; r0 < R; r0 += MAXR)
-            if (moe_forward_launch(W.moe, X.mxn + (size_t)r0 * d, d, std::min(MAXR, R - r0), X.sub + (size_t)r0 * d,
-                                   d, nullptr, st))
-                return -1;
-    }
+    if (moe_rows_launch(W.moe, X.moe, X.mxn, d, R, X.sub, d, st)) return -1;
     {   // x = bf16(x + moe); shared_head.norm
         NormSeg sg = {X.mx, d, nullptr, X.sub, d, m->shared_norm, d, X.oh, d};
         return norm_seg_launch(&sg, 1, R, D.eps, nullptr, st);
