@@ -297,6 +297,32 @@ def fp8_gemv_leg(reps=200, warmup=10):
                         "avg_launch_us": round(us, 3), "launches": reps,
                         "timing": "graph-replayed back-to-back launches, CUDA events",
                         "l2": "16 rotating weight copies (270 MB > L2)"}}
+    # the same kernel on a matrix large enough that its fixed latency is small
+    # beside the stream, K within one k-range (no split-K pass): 4 rows x
+    # 65536 x 4096 E4M3 (268 MB), 2 rotating copies
+    NO, NK = 65536, 4096
+    wl = [torch.randint(0, 120, (NO, NK), dtype=torch.uint8, device="cuda") for _ in range(2)]
+    sl = torch.full((NO // 128, NK // 128), 1e-3, device="cuda")
+    xl = torch.randn(M, NK, device="cuda").to(torch.bfloat16)
+    yl = torch.empty(M, NO, dtype=torch.bfloat16, device="cuda")
+    G.apus_gcuda_set_pdl(1)
+
+    def big(i):
+        G.check(G.apus_gcuda_fp8blk_linear_dev(G.ptr(wl[i % 2]), G.ptr(sl), G.ptr(xl), G.ptr(yl), M, NO, NK, sp),
+                "linear")
+    for i in range(4):
+        big(i)
+    st.synchronize()
+    nb = 20
+    usl = _graph_us(torch, st, lambda: [big(i) for i in range(nb)], nb)
+    G.apus_gcuda_set_pdl(0)
+    al = NO * NK + sl.numel() * 4 + M * (NK + NO) * 2
+    out["large_matrix"] = {"workload": "FP8 128x128 block-dequant GEMV, M=4, N=65536, K=4096 (268 MB)",
+                           "achieved": round(al / usl / 1e3, 1), "peak": hbm, "unit": "GB/s",
+                           "frac": round(al / usl / 1e3 / hbm, 4), "avg_launch_us": round(usl, 2),
+                           "timing": "graph-replayed back-to-back launches over 2 copies (537 MB > L2)"}
+    del wl
+    torch.cuda.empty_cache()
     # one MoE layer (config 1): the grouped FP8 GEMVs at the step's shapes
     R, d = C1["R"], C1["dim"]
     h = G.apus_gcuda_moe_new(C1["E"], C1["topk"], d, C1["inter"], 2.5, 10.0, R)
