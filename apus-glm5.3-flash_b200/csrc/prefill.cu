@@ -61,10 +61,9 @@ __global__ void k_kda_gates_rows(const uint16_t *fg, const uint16_t *kp, long ld
     const int qkv = H * D;
     const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
     if (i < (long)R * qkv) {
-        const int t = (int)(i / qkv), c = (int)(i % qkv), h = c / D;
+        const int c = (int)(i % qkv), h = c / D;
         const float z = bf16_f32(fg[i]) + dt_bias[c];
         g[i] = lb * sigmoid_np(expf(A_log[h]) * z);
-        (void)t;
     }
     if (i < (long)R * H) {
         const int t = (int)(i / H), h = (int)(i % H);
