@@ -23,6 +23,8 @@ for p in (HERE, ROOT, os.path.join(ROOT, "apus-glm5.3-flash_b200"), os.path.join
         sys.path.insert(0, p)
 
 PROMPT = [5, 17, 300, 2, 99, 42, 7, 381, 0, 11, 13]
+# a prompt over two 256-row chunks of the prompt pass (its MoE exchange runs once a chunk)
+LONG = [(i * 7919 + 13) % 1024 for i in range(300)]
 
 
 def ep_config():
@@ -33,7 +35,7 @@ def ep_config():
 
 def run(G, kw, W, rank, world, seed_random=None):
     """Every stream the comparison needs, from one model."""
-    m = G.GModel(G.make_config(**kw), has_mtp=True, kv_cap=256, depth=4, rank=rank, world=world)
+    m = G.GModel(G.make_config(**kw), has_mtp=True, kv_cap=400, depth=4, rank=rank, world=world)
     res = {}
     if world > 1:
         m.ep_bootstrap(G.ep_all_gather())
@@ -43,6 +45,12 @@ def run(G, kw, W, rank, world, seed_random=None):
     if world > 1:    # the device-side exchanges wait at most about a second
         import torch.distributed as dist
         dist.barrier()
+    res["long_greedy"] = m.greedy(LONG, 12)
+    m.reset()
+    m.spec_prefill(LONG)
+    res["long_spec"] = m.spec_step() + m.spec_step()
+    res["long_digest"] = m.digest()
+    m.reset()
     res["greedy"] = m.greedy(PROMPT, 40)
     truth = res["greedy"]
     m.reset()
