@@ -625,6 +625,29 @@ static bool ep_connected(const EpCtx &ep) {
     return true;
 }
 
+// Rank p's slice is the rows [p*per, min((p+1)*per, V)), per = ceil(V/world)
+// (the lm_head split); 8 columns a thread.
+__global__ void k_ep_logits_gather(EpCtx ep, int R, uint16_t *logits, long ldl) {
+    const int V = ep.vocab, nc = (V + 7) / 8;
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * nc) return;
+    const int r = (int)(i / nc), c0 = (int)(i % nc) * 8;
+    const int per = (V + ep.world - 1) / ep.world;
+    for (int c = c0; c < c0 + 8 && c < V; c++) {
+        const int owner = c / per;
+        const uint16_t *src = (const uint16_t *)(ep.peer[owner] + ep.off_logits) + (size_t)r * V + c;
+        logits[(size_t)r * ldl + c] = *(const volatile uint16_t *)src;
+    }
+}
+
+int ep_logits_gather_launch(const EpCtx &ep, int R, uint16_t *logits, long ldl, cudaStream_t st) {
+    if (!ep_connected(ep) || R < 1 || R > MOE_MAX_R || ep.vocab < 1) return -1;
+    const long n = (long)R * ((ep.vocab + 7) / 8);
+    k_ep_logits_gather<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ep, R, logits, ldl);
+    k_ep_barrier<<<1, 1, 0, st>>>(ep);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 int ep_picks_exchange_launch(const EpCtx &ep, const unsigned long long *keys, int R, int *picks,
                              cudaStream_t st, int n0, int *picks2) {
     if (n0 < 0 || n0 > R) n0 = R;

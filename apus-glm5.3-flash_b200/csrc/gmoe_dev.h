@@ -25,6 +25,10 @@ struct EpCtx {
     // BF16 (halves by epoch parity, as contrib), at off_wide
     long off_wide;
     int wide_rows, wide_k;
+    // lm_head logits rows [MOE_MAX_R][V] BF16 at off_logits: each rank writes
+    // its vocabulary slice's columns there, the others gather them
+    long off_logits;
+    int vocab;
 };
 
 // All pointers are device memory.  Weights: see gmoe.cu for the packed layout.
@@ -100,5 +104,11 @@ int moe_combine_launch(const MoeDev &m, int R, uint16_t *out, long ldo, cudaStre
 int ep_picks_exchange_launch(const EpCtx &ep, const unsigned long long *keys, int R, int *picks,
                              cudaStream_t st, int n0 = -1, int *picks2 = nullptr);
 size_t ep_region_bytes(int dim);
+// Every rank's vocabulary slice of logits rows [0, R) (written into the
+// regions' logits areas by each rank's lm_head) gathered into logits
+// [R][ldl] on this rank, then a barrier so that no rank writes its area
+// again before every rank has read it.  Call after the lm_head's picks
+// exchange (its barrier orders the writes before the reads).
+int ep_logits_gather_launch(const EpCtx &ep, int R, uint16_t *logits, long ldl, cudaStream_t st);
 // bytes of the prompt pass's part of a region (rows x topk contributions, two halves)
 size_t ep_wide_bytes(int rows, int topk, int dim);

@@ -466,8 +466,11 @@ static ApusGcudaModel *model_create(const ApusGcudaConfig *cfg, int has_mtp, siz
         const size_t contrib = (size_t)2 * MOE_MAX_R * MOE_MAX_TOPK * d * 2;
         const size_t rb0 = (ep_region_bytes(d) + 255) & ~(size_t)255;
         const int wk = D.ktop > 0 ? D.ktop : 1;
-        const size_t rb = rb0 + ep_wide_bytes(PROMPT_ROWS, wk, d);   // + the prompt pass's outputs
+        const size_t rbw = rb0 + ep_wide_bytes(PROMPT_ROWS, wk, d);   // + the prompt pass's outputs
+        const size_t rb = rbw + (size_t)MOE_MAX_R * D.V * 2;            // + lm_head logits rows
         m->ep.off_wide = (long)rb0;
+        m->ep.off_logits = (long)rbw;
+        m->ep.vocab = D.V;
         m->ep.wide_rows = PROMPT_ROWS;
         m->ep.wide_k = wk;
         m->ep_region = (uint8_t *)A(rb > (2u << 20) ? rb : (2u << 20));   // its own IPC-mappable allocation
@@ -905,8 +908,10 @@ static int lm_head(ApusGcudaModel *m, const uint16_t *yn, int R, int *picks, boo
     g.W = m->head; g.x = yn; g.ldx = D.d; g.R = R; g.O = m->vn; g.K = D.d; g.fp8 = 0;
     g.row_base = m->v0; g.plan_o = D.V;     // a vocabulary slice sums like the whole head
     if (want_logits) {
-        if (m->ep_world > 1) return -1;     // the logits stay split over the ranks
-        g.y = m->S.logits; g.ldy = D.V;
+        // expert parallelism: this rank's columns go into its region's logits
+        // area, gathered into S.logits on every rank after the picks exchange
+        g.y = m->ep_world > 1 ? (uint16_t *)(m->ep_region + m->ep.off_logits) + m->v0 : m->S.logits;
+        g.ldy = D.V;
     }
     g.amax = m->S.amax; g.part = m->part; g.ticket = m->tick;
     g.pdl = 1;
@@ -914,7 +919,7 @@ static int lm_head(ApusGcudaModel *m, const uint16_t *yn, int R, int *picks, boo
     if (m->ep_world > 1) {
         // the largest key over every rank's slice: publish, barrier, reduce
         if (ep_picks_exchange_launch(m->ep, m->S.amax, R, picks, m->st, n0, picks2)) return -1;
-        return 0;
+        return want_logits ? ep_logits_gather_launch(m->ep, R, m->S.logits, D.V, m->st) : 0;
     }
     k_extract_picks<<<1, 32, 0, m->st>>>(m->S.amax, R, picks, n0, picks2);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
@@ -1240,7 +1245,6 @@ extern "C" int apus_gcuda_decode_batch(ApusGcudaModel *m, const int32_t *ids, si
     const Dims &D = m->D;
     if (s < 1 || s > MAXR) { gcuda_set_error("decode_batch: %zu rows (1..%d)", s, MAXR); return -1; }
     if (!ids_ok(m, ids, s, "decode_batch")) return -1;
-    if (logits && m->ep_world > 1) { gcuda_set_error("decode_batch: logits are split over the ranks"); return -1; }
     Ctl c = read_ctl(m);
     if ((size_t)c.pos + s > (size_t)m->cap) { gcuda_set_error("decode_batch: capacity"); return -1; }
     cudaMemcpyAsync(m->ids, ids, s * 4, cudaMemcpyHostToDevice, m->st);
@@ -1259,7 +1263,6 @@ extern "C" int apus_gcuda_prefill(ApusGcudaModel *m, const int32_t *ids, size_t 
     const Dims &D = m->D;
     if (n < 1 || n > (size_t)m->cap) { gcuda_set_error("prefill: %zu prompt tokens", n); return -1; }
     if (!ids_ok(m, ids, n, "prefill")) return -1;
-    if (logits && m->ep_world > 1) { gcuda_set_error("prefill: logits are split over the ranks"); return -1; }
     if (apus_gcuda_model_reset(m)) return -1;
     if (prompt_pass(m, ids, n, false)) return fail_ctl(m, "prefill");
     if (logits) {       // every row's logits, 8 rows a launch of the head
@@ -1286,7 +1289,6 @@ extern "C" int apus_gcuda_mtp_forward(ApusGcudaModel *m, const int32_t *ids, con
     if (!m->has_mtp) { gcuda_set_error("gmtp: model has no MTP block loaded"); return -1; }
     if (s < 1 || s > MAXR) { gcuda_set_error("mtp_forward: %zu rows", s); return -1; }
     if (!ids_ok(m, ids, s, "mtp_forward")) return -1;
-    if (logits && m->ep_world > 1) { gcuda_set_error("mtp_forward: logits are split over the ranks"); return -1; }
     Ctl c = read_ctl(m);
     if ((size_t)c.mtp_n + s > (size_t)m->cap) { gcuda_set_error("mtp_forward: capacity"); return -1; }
     cudaMemcpyAsync(m->ids, ids, s * 4, cudaMemcpyHostToDevice, m->st);
@@ -1590,10 +1592,6 @@ extern "C" int apus_gcuda_generate(ApusGcudaModel *m, const int32_t *ids, size_t
 // sampled step launches the sampler, the greedy one does not.
 extern "C" int apus_gcuda_gspec_sampling(ApusGcudaModel *m, float temp, float top_p, uint64_t seed) {
     if (temp != temp) { gcuda_set_error("sampling: temperature is NaN"); return -1; }
-    if (temp > 0.0f && m->ep_world > 1) {
-        gcuda_set_error("sampling: the logits are split over the expert-parallel ranks (greedy only)");
-        return -1;
-    }
     if (temp > 0.0f && sample_prepare(m->D.V)) return -1;
     m->ctl_epoch++;
     m->temp = temp;
@@ -1612,7 +1610,6 @@ extern "C" int apus_gcuda_rng_state(ApusGcudaModel *m, uint64_t *state) {
 }
 
 extern "C" int apus_gcuda_gspec_keep_logits(ApusGcudaModel *m, int on) {
-    if (on && m->ep_world > 1) { gcuda_set_error("keep_logits: the logits are split over the ranks"); return -1; }
     m->keep_logits = on ? 1 : 0;
     if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = nullptr; }
     if (m->graph) { cudaGraphDestroy(m->graph); m->graph = nullptr; }

@@ -124,7 +124,7 @@ int apus_gcuda_decode_batch(ApusGcudaModel *m, const int32_t *ids, size_t s, uin
  * each layer together (chunks of 256), the linears on the tensor-core GEMM.
  * logits [n,V] (every row's; the rows' lm_head runs only when asked),
  * yn_out [n,dim] (post-final-norm rows); host arrays, each may be NULL.
- * Expert-parallel models return no logits. */
+ * Expert-parallel models return the logits gathered from every rank's slice. */
 int apus_gcuda_prefill(ApusGcudaModel *m, const int32_t *ids, size_t n, uint16_t *logits, uint16_t *yn_out);
 
 /* c/gmtp.h:169-172 apus_gmtp_forward: s <= 8 pairs (ids[t], prev_h[t]) at the
@@ -137,7 +137,8 @@ int apus_gcuda_mtp_forward(ApusGcudaModel *m, const int32_t *ids, const uint16_t
  * temp > 0 samples every emitted token with one splitmix64 draw, in position
  * order (c/gmtp.h:800-831); drafts stay the MTP argmax.  The stream state
  * persists across prefills like a caller-owned ApusRng.  Expert-parallel
- * models decode greedily only (their logits are split over the ranks).
+ * models sample too: each rank's vocabulary slice of the logits rows is
+ * gathered on every rank, which then draws the same tokens.
  * NaN temp is rejected; -1 on error. */
 int apus_gcuda_gspec_sampling(ApusGcudaModel *m, float temp, float top_p, uint64_t seed);
 /* The splitmix64 state (c/sample.h:57 ApusRng.s) after the draws so far. */

@@ -79,6 +79,20 @@ def run(G, kw, W, rank, world, seed_random=None):
     res["graph"] = m.emitted()
     res["graph_digest"] = m.digest()
     m.use_graph(False)
+    # sampled decode: every rank gathers the full logits rows and draws the same tokens
+    m.sampling(0.8, 0.95, 4242)
+    res["sampled_generate"] = m.generate(PROMPT, 24)
+    m.reset()
+    m.spec_prefill(PROMPT)
+    sspec = []
+    for _ in range(8):
+        sspec += m.spec_step()
+    res["sampled_spec"] = sspec
+    res["sampled_rng"] = m.rng_state()
+    m.sampling(0.0)
+    m.reset()
+    import hashlib
+    res["logits_sha"] = hashlib.sha256(m.decode_batch(PROMPT[:8]).tobytes()).hexdigest()
     if seed_random is not None:   # on-device synthetic weights, drawn per rank slice
         m.init_random(seed_random)
         res["random_greedy"] = m.greedy(PROMPT, 16)

@@ -3,8 +3,10 @@ _ep_handle / _ep_connect): one process per GPU, routed experts and lm_head
 rows split over the ranks, every MoE layer and every lm_head exchanging
 through peer memory.  The token streams (greedy, speculative, forced full
 accept, forced partial accept with rollback, CUDA-graph replay, on-device
-random weights, and a 300-token prompt whose prompt pass runs two 256-row
-chunks through the gathered MoE's exchange) and the committed-state digests
+random weights, a 300-token prompt whose prompt pass runs two 256-row
+chunks through the gathered MoE's exchange, sampled decode, speculative and
+not, on the logits rows gathered from every rank's vocabulary slice, and the
+decode batch's logits) and the committed-state digests
 must equal the one-GPU engine's bit for bit on every rank.  Needs as many
 GPUs as ranks."""
 import json
@@ -50,7 +52,8 @@ def test_ep_streams_equal_one_gpu(world, tmp_path):
     for rank, ep in enumerate(rep["ranks"]):
         assert ep["kernel_error"] == 0, f"rank {rank}: exchange error {ep['kernel_error']}"
         assert ep["stored_ok"], f"rank {rank}: set() stored the wrong expert slice"
-        for key in ("long_greedy", "long_spec", "long_digest", "greedy", "spec", "spec_digest", "forced_full",
+        for key in ("long_greedy", "long_spec", "long_digest", "sampled_generate", "sampled_spec", "sampled_rng",
+                    "logits_sha", "greedy", "spec", "spec_digest", "forced_full",
                     "forced_full_digest", "forced_half",
                     "forced_half_stats", "forced_half_digest", "graph", "graph_digest", "random_greedy"):
             assert ep[key] == one[key], f"rank {rank}: {key} differs from the one-GPU engine"
